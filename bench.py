@@ -1,0 +1,394 @@
+#!/usr/bin/env python
+"""Forward+backward frames/s of gs3d.rasterize on the BASELINE config-1 scene.
+
+Workload: 1M Gaussians, SH3, one 1920x1080
+pinhole camera per GPU, absgrad metadata, preallocated upstream image
+gradients (the reference's benchmark convention, rade/README.md:194-196).
+Seeded synthetic data with the config's distributions (no dataset).  The
+Gaussians (236 MB/step of parameters and gradients) exceed the 126 MB L2,
+so no extra L2 flush is done between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 is launched with torchrun, one rank per GPU: every rank renders its
+own camera of the shared scene (weak scaling) and the per-Gaussian gradients
+are summed with an NCCL all-reduce each step (the path's only exchange).
+`--impl reference` times the reference algorithm's CPU restatement (the
+oracle: dsl_splat's Warp code cannot run here) on the host.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "fwd+bwd frames/s, 3DGS SH3 1M Gaussians @1080p"
+UNIT = "frames/s"
+CHANNELS = 4  # RGB + the appended alpha column (gs3d/autograd.py:306-311)
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=15.0,
+                    help="seconds of CPU work for the cpu_baseline sample")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def workload(config: int, rank: int, world: int):
+    """The config scene; rank r looks from an orbit angle 2*pi*r/world."""
+    from dsl_splat_b200.scenes import look_at, make_scene
+    s = make_scene(config)
+    if world > 1 and rank > 0:
+        th = 2.0 * math.pi * rank / world
+        s.viewmats[0] = look_at(torch.tensor([8.0 * math.sin(th), 0.0, -8.0 * math.cos(th)]))
+    return s
+
+
+def describe(s, world):
+    return {
+        "workload": f"config{s.meta['config']}: gs3d.rasterize SH{s.sh_degree} "
+                    f"{s.means.shape[0]} Gaussians {s.width}x{s.height}, fwd+bwd, absgrad",
+        "n_gaussians": int(s.means.shape[0]), "width": s.width, "height": s.height,
+        "sh_degree": s.sh_degree, "views_per_gpu": 1, "global_batch": world,
+        "parallelism": f"camera-sharded dp{world}",
+        "l2": "inputs larger than L2 (236 MB of Gaussian parameters+grads per step); no flush",
+    }
+
+
+# ---- clocks ------------------------------------------------------------------
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in rows for k in range(4)
+                          if len(r) > 5 + k and r[5 + k].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+# ---- CPU baseline (the oracle) ----------------------------------------------------
+
+def cpu_band_step(s, rows: int, y0: int = 0):
+    """One fwd+bwd of the oracle on image rows [y0, y0+rows) of view 0."""
+    from oracle import oracle as O
+    import torch.nn.functional as F
+    K = s.Ks[0].numpy().copy()
+    K[1, 2] -= y0
+    qn = F.normalize(s.quats, dim=-1).numpy()
+    means = s.means.numpy()
+    r, bg = O.gs3d_view_forward(means, qn, s.scales.numpy(), s.opacities.numpy(),
+                                s.viewmats[0].numpy(), K, s.width, rows,
+                                sh_coeffs=s.sh_coeffs.numpy(), sh_degree=s.sh_degree)
+    up = np.concatenate([s.grad_image[0, y0:y0 + rows].numpy(),
+                         s.grad_alpha[0, y0:y0 + rows].numpy()], -1)
+    O.gs3d_view_backward(r, bg, means, qn, s.scales.numpy(), s.opacities.numpy(),
+                         s.viewmats[0].numpy(), K, s.width, rows, up,
+                         sh_coeffs=s.sh_coeffs.numpy(), sh_degree=s.sh_degree)
+
+
+def cpu_sample_rows(s, budget_s: float) -> int:
+    """Tile-aligned band height whose fwd+bwd takes about budget_s seconds."""
+    probe = min(128, s.height)
+    t0 = time.perf_counter()
+    cpu_band_step(s, probe)
+    dt = time.perf_counter() - t0
+    rows = int(probe * budget_s / max(dt, 1e-3)) // 16 * 16
+    return max(16, min(s.height, rows))
+
+
+def cpu_baseline(s, budget_s: float, steps: int = 1):
+    from oracle import oracle as O
+    threads = O.num_threads()
+    rows = cpu_sample_rows(s, budget_s)
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        cpu_band_step(s, rows)
+        times.append(time.perf_counter() - t0)
+    frac = rows / s.height
+    value = frac / statistics.median(times)
+    return {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"oracle (C++ restatement, OpenMP {threads} threads) fwd+bwd of image rows "
+                      f"0-{rows} of {s.height} ({frac:.3f} of a frame, all {s.means.shape[0]} "
+                      f"Gaussians projected), {steps} step(s); value = frame fraction / time"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference algorithm's CPU restatement on host cores."""
+    if rank != 0:
+        return
+    s = workload(args.config, 0, 1)
+    from oracle import oracle as O
+    threads = O.num_threads()
+    budget = max(2.0, 150.0 / max(1, args.steps + args.warmup))
+    rows = cpu_sample_rows(s, budget)
+    for _ in range(args.warmup):
+        cpu_band_step(s, rows)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_band_step(s, rows)
+        times.append(time.perf_counter() - t0)
+    frac = rows / s.height
+    value = frac * len(times) / sum(times)
+    sample = (f"oracle (C++ restatement of dsl_splat gs3d; the Warp reference needs warp-lang, "
+              f"absent) with {threads} OpenMP threads, image rows 0-{rows} of {s.height} "
+              f"({frac:.3f} frame) per step; value = frame fraction / time")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, BASELINE config distributions)", "impl": "reference",
+            "config": describe(s, 1),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- GPU arm ----------------------------------------------------------------------
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def profile_traffic(kernel: str):
+    """dram read+write bytes per launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"{kernel}_config1.md")
+    try:
+        for line in open(path):
+            if line.startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+def algorithmic_bytes(kernel: str, n: int, nv: int, m: int, pixels: int, c: int = CHANNELS):
+    """Per-launch algorithmic bytes of the blend kernels (the survey's per-view model)."""
+    if kernel == "render_forward":
+        return 4 * m + m * (24 + 4 * c) + pixels * (4 * c + 8)
+    if kernel == "render_backward":
+        return pixels * (4 * c + 8) + 4 * m + m * (24 + 4 * c) + n * (24 + 4 * c + 8)
+    raise KeyError(kernel)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
+        sys.exit(1)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=dev)
+        pg = dist
+    from dsl_splat_b200 import gs3d, stages
+    from dsl_splat_b200._native import lib
+
+    s = workload(args.config, rank, world)
+    means = s.means.to(dev).requires_grad_(True)
+    quats = s.quats.to(dev).requires_grad_(True)
+    scales = s.scales.to(dev).requires_grad_(True)
+    opac = s.opacities.to(dev).requires_grad_(True)
+    sh = s.sh_coeffs.to(dev).requires_grad_(True)
+    params = [means, quats, scales, opac, sh]
+    viewmats, Ks = s.viewmats.to(dev), s.Ks.to(dev)
+    gF, gA = s.grad_image.to(dev), s.grad_alpha.to(dev)
+    W, H = s.width, s.height
+    last = {}
+
+    def step():
+        for p in params:
+            p.grad = None
+        res = gs3d.rasterize(means, quats, scales, opac, viewmats, Ks, W, H, sh_coeffs=sh,
+                             absgrad=True)
+        torch.autograd.backward([res.features, res.alpha], [gF, gA])
+        if pg is not None:
+            for p in params:
+                pg.all_reduce(p.grad)
+        last["res"] = res
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier()
+    stages.TIMERS = {}
+    launches0 = lib.splat_launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        barrier()
+    timers, stages.TIMERS = stages.TIMERS, None
+    launches = lib.splat_launch_count() - launches0
+    elapsed = torch.tensor([start.elapsed_time(end)], device=dev, dtype=torch.float64)
+    if pg is not None:
+        pg.all_reduce(elapsed, op=pg.ReduceOp.MAX)
+    ms = float(elapsed.item())
+    value = world * args.steps / (ms / 1000.0)
+
+    # live roofline of the dominant kernel over the timed region
+    res = last["res"]
+    radii = res.meta["radii"][..., 0]
+    nv = int((radii > 0).sum())
+    m = int(res.meta["tiles_per_gauss"].sum())
+    n = int(means.shape[0])
+    durations = {k: statistics.mean(a.elapsed_time(b) for a, b in v) for k, v in timers.items()}
+    kernel = max(durations, key=durations.get)
+    per_launch = algorithmic_bytes(kernel, n, nv, m, W * H)
+    achieved = per_launch / (durations[kernel] / 1000.0) / 1e9
+    peak, peak_kind = measured_peak()
+    roofline = {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak,
+                "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                "traffic": profile_traffic(kernel),
+                "algorithmic_bytes_per_launch": per_launch,
+                "launch_ms": durations[kernel], "pairs": m, "visible": nv,
+                "kernel_ms": durations,
+                "alpha_evals_note": "blend kernels are issue-bound; see DESIGN.md"}
+
+    # end to end through the public API with host buffers each step
+    e2e = None
+    if not args.no_e2e:
+        target_host = s.target[0:1].contiguous().pin_memory()
+        view_host = s.viewmats.contiguous().pin_memory()
+        k_host = s.Ks.contiguous().pin_memory()
+        target = torch.empty_like(target_host, device=dev)
+        vm = torch.empty_like(view_host, device=dev)
+        kk = torch.empty_like(k_host, device=dev)
+
+        def e2e_step():
+            for p in params:
+                p.grad = None
+            target.copy_(target_host, non_blocking=True)
+            vm.copy_(view_host, non_blocking=True)
+            kk.copy_(k_host, non_blocking=True)
+            r = gs3d.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
+                               absgrad=True)
+            loss = (r.features - target).abs().mean()
+            loss.backward()
+            if pg is not None:
+                for p in params:
+                    pg.all_reduce(p.grad)
+            return float(loss.item())
+
+        for _ in range(2):
+            e2e_step()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        barrier()
+        et = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+        if pg is not None:
+            pg.all_reduce(et, op=pg.ReduceOp.MAX)
+        e2e = {"value": world * args.steps / (float(et.item()) / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": target_host.numel() * 4 + view_host.numel() * 4
+               + k_host.numel() * 4, "d2h_bytes_per_step": 4,
+               "path": "gs3d.rasterize + L1 loss + backward; target image, viewmat, K copied "
+                       "H2D from pinned memory and the loss read back every step"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(s, args.cpu_budget)
+
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded, BASELINE config distributions)",
+                "config": describe(s, world), "roofline": roofline, "cpu_baseline": cpu,
+                "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

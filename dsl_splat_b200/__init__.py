@@ -1,0 +1,12 @@
+"""dsl_splat_b200: a B200-native drop-in for dsl_splat's gs3d rasteriser.
+
+`dsl_splat_b200.gs3d.rasterize` and `dsl_splat_b200.gs3d.gsplat.rasterization`
+keep dsl_splat's signatures; the compute path is libsplat200.so (hand-written
+CUDA for sm_100a) reached through the C ABI in include/splat200.h.
+"""
+
+from .cameras import PinholeCamera
+from .statistics import MaskedContributionCount, WeightedContributionSum
+from . import gs3d
+
+__all__ = ["gs3d", "PinholeCamera", "MaskedContributionCount", "WeightedContributionSum"]

@@ -1,0 +1,433 @@
+// Tile binning and sorting: the B200 replacement for splatting/binning.py:
+// 116-217 (duplicate + bin_and_sort), primitives/tiling.py:39-100 (scan,
+// radix sort, identify_ranges) and Warp's array_scan / radix_sort_pairs.
+//
+// The reference emits one (tile<<32 | float_bits(depth), id) pair per
+// Gaussian-tile overlap in Gaussian order and radix-sorts the 64-bit keys
+// stably, so within a tile entries are ordered by (depth bits, Gaussian
+// index).  This file produces the identical order with less traffic:
+//
+//   1. bin_prepare: per Gaussian, depth key (culled -> 0xFFFFFFFF), packed
+//      tile rectangle, +-1 corners into a 2D difference grid over tiles and
+//      the four 8-bit digit histograms of the depth keys.
+//   2. four stable onesweep passes sort (depth bits, index) over N.
+//   3. exclusive scan of tile counts in depth order -> pair offsets, M.
+//   4. tile_counts: 2D prefix of the difference grid -> per-tile counts ->
+//      ranges (T,2) and the digit histograms of the tile ids.
+//   5. a stable onesweep pass keyed on tile bits 0-7 whose loader generates
+//      the pairs directly from the depth-ordered Gaussians (no pair buffer
+//      is written before sorting), then one pass per further 8 tile bits.
+//
+// A stable sort by tile of a sequence already ordered by (depth, index) is
+// exactly the reference order.  Every pass uses decoupled look-back with a
+// bounded spin: on expiry it records kDeviceTimeout in g_splat_device_error
+// and finishes without waiting further.
+#pragma once
+#include "splat_common.cuh"
+
+namespace splat {
+
+constexpr int kSortBlock = 256;
+constexpr int kSortItems = 16;
+constexpr int kSortTile = kSortBlock * kSortItems;  // elements per onesweep block
+constexpr int kSortWarps = kSortBlock / 32;
+constexpr int kRadix = 256;
+constexpr uint32_t kFlagAggregate = 1u << 30;
+constexpr uint32_t kFlagInclusive = 2u << 30;
+constexpr uint32_t kValueMask = (1u << 30) - 1u;
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+__device__ int g_splat_device_error;
+
+SPLAT_DEV void record_device_error(int code) { atomicCAS(&g_splat_device_error, 0, code); }
+
+// ---- phase 1: per-Gaussian preparation ---------------------------------
+__global__ void __launch_bounds__(256)
+    bin_prepare_kernel(int n, const float* __restrict__ centers, const int* __restrict__ radii,
+                       const int* __restrict__ tiles, const float* __restrict__ depths, int gx,
+                       int gy, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
+                       uint2* __restrict__ rects, int* __restrict__ diff,
+                       uint32_t* __restrict__ hist, unsigned long long* __restrict__ total) {
+  __shared__ uint32_t s_hist[4 * kRadix];
+  for (int k = threadIdx.x; k < 4 * kRadix; k += blockDim.x) s_hist[k] = 0;
+  __syncthreads();
+  const int stride = gridDim.x * blockDim.x;
+  unsigned long long pairs = 0;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int radius = radii[i];
+    uint32_t key = kCulledKey;
+    uint2 rect = make_uint2(0u, 0u);
+    if (radius > 0) {
+      key = __float_as_uint(depths[i]);
+      const float2 c = reinterpret_cast<const float2*>(centers)[i];
+      const int4 b = tile_bounds(c.x, c.y, radius, gx, gy);
+      rect = make_uint2(static_cast<uint32_t>(b.x) | (static_cast<uint32_t>(b.y) << 16),
+                        static_cast<uint32_t>(b.z) | (static_cast<uint32_t>(b.w) << 16));
+      const int row = gx + 1;
+      atomicAdd(diff + b.y * row + b.x, 1);
+      atomicAdd(diff + b.y * row + b.z, -1);
+      atomicAdd(diff + b.w * row + b.x, -1);
+      atomicAdd(diff + b.w * row + b.z, 1);
+      pairs += static_cast<unsigned long long>(max(tiles[i], 0));
+    }
+    keys[i] = key;
+    vals[i] = static_cast<uint32_t>(i);
+    rects[i] = rect;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) atomicAdd(&s_hist[p * kRadix + ((key >> (8 * p)) & 255u)], 1u);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) pairs += __shfl_xor_sync(0xffffffffu, pairs, o);
+  if ((threadIdx.x & 31) == 0 && pairs) atomicAdd(total, pairs);
+  __syncthreads();
+  for (int k = threadIdx.x; k < 4 * kRadix; k += blockDim.x)
+    if (s_hist[k]) atomicAdd(hist + k, s_hist[k]);
+}
+
+// Block-wide exclusive scan of one value per thread (blockDim.x <= 1024).
+SPLAT_DEV uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = (blockDim.x + 31) >> 5;
+  uint32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) s_warp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    uint32_t w = lane < warps ? s_warp[lane] : 0u;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    if (lane < warps) s_warp[lane] = w;
+  }
+  __syncthreads();
+  const uint32_t before = (warp > 0 ? s_warp[warp - 1] : 0u) + x - v;
+  if (total) *total = s_warp[warps - 1];
+  __syncthreads();
+  return before;
+}
+
+// Exclusive scans of `passes` 256-bin histograms (one block of 256 threads).
+__global__ void digit_offsets_kernel(const uint32_t* __restrict__ hist, int passes,
+                                     uint32_t* __restrict__ offsets) {
+  __shared__ uint32_t s_warp[32];
+  for (int p = 0; p < passes; ++p) {
+    const uint32_t v = hist[p * kRadix + threadIdx.x];
+    offsets[p * kRadix + threadIdx.x] = block_exclusive_scan(v, s_warp, nullptr);
+  }
+}
+
+// ---- generic onesweep pass ---------------------------------------------
+
+struct KeyValueLoader {
+  const uint32_t* keys;
+  const uint32_t* vals;
+  struct Shared {};
+  SPLAT_DEV void prepare(uint32_t, uint32_t, Shared&) {}
+  SPLAT_DEV void load(uint32_t idx, const Shared&, uint32_t& key, uint32_t& val) const {
+    key = keys[idx];
+    val = vals[idx];
+  }
+};
+
+// Largest j in [lo, hi) with offsets[j] <= target, given offsets[lo] <=
+// target < offsets[hi]: a block-wide 256-ary search (all threads call).
+SPLAT_DEV uint32_t block_upper_search(const uint32_t* __restrict__ offsets, uint32_t lo,
+                                      uint32_t hi, uint32_t target) {
+  while (hi - lo > 1) {
+    const uint32_t span = hi - lo;
+    const uint32_t step = (span + kSortBlock - 1) / kSortBlock;
+    const uint32_t j = lo + threadIdx.x * step;
+    const bool pred = j < hi && offsets[j] <= target;
+    const uint32_t count = static_cast<uint32_t>(__syncthreads_count(pred));
+    const uint32_t new_lo = lo + (count - 1) * step;
+    const uint32_t cand = lo + count * step;
+    hi = cand < hi ? cand : hi;
+    lo = new_lo;
+  }
+  return lo;
+}
+
+// Generates the (tile id, Gaussian id) pairs of depth-ordered Gaussians:
+// pair p belongs to the Gaussian j with offsets[j] <= p < offsets[j+1] and
+// is its (p - offsets[j])-th tile in row-major rectangle order.
+struct EmitLoader {
+  const uint32_t* offsets;  // exclusive, length nsorted + 1
+  const uint32_t* order;    // depth-ordered Gaussian ids
+  const uint2* rects;
+  uint32_t nsorted;
+  int gx;
+  struct Shared {
+    uint32_t j0;
+    uint32_t count;
+    uint32_t off[kSortTile + 1];
+  };
+  SPLAT_DEV void prepare(uint32_t base, uint32_t end, Shared& s) {
+    const uint32_t j0 = block_upper_search(offsets, 0u, nsorted, base);
+    const uint32_t j1 = block_upper_search(offsets, j0, nsorted, end - 1);
+    uint32_t cnt = j1 - j0 + 1;
+    if (cnt > static_cast<uint32_t>(kSortTile)) {  // impossible for consistent offsets
+      if (threadIdx.x == 0) record_device_error(kInconsistentInput);
+      cnt = kSortTile;
+    }
+    for (uint32_t k = threadIdx.x; k <= cnt; k += blockDim.x) s.off[k] = offsets[j0 + k];
+    if (threadIdx.x == 0) {
+      s.j0 = j0;
+      s.count = cnt;
+    }
+    __syncthreads();
+  }
+  SPLAT_DEV void load(uint32_t idx, const Shared& s, uint32_t& key, uint32_t& val) const {
+    uint32_t lo = 0, hi = s.count;  // off[lo] <= idx < off[hi]
+    while (hi - lo > 1) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (s.off[mid] <= idx) lo = mid; else hi = mid;
+    }
+    const uint32_t g = order[s.j0 + lo];
+    const uint32_t local = idx - s.off[lo];
+    const uint2 r = rects[g];
+    const uint32_t x0 = r.x & 0xFFFFu, y0 = r.x >> 16, x1 = r.y & 0xFFFFu;
+    const uint32_t w = x1 > x0 ? x1 - x0 : 1u;
+    const uint32_t dy = local / w;
+    key = (y0 + dy) * static_cast<uint32_t>(gx) + x0 + (local - dy * w);
+    val = g;
+  }
+};
+
+template <class Loader, bool WRITE_KEYS>
+__global__ void __launch_bounds__(kSortBlock)
+    onesweep_kernel(Loader ld, uint32_t n, int shift, const uint32_t* __restrict__ digit_offsets,
+                    uint32_t* __restrict__ status, uint32_t* __restrict__ counter,
+                    uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out) {
+  __shared__ uint32_t s_hist[kSortWarps][kRadix];
+  __shared__ uint32_t s_base[kRadix];
+  __shared__ uint32_t s_tile;
+  __shared__ typename Loader::Shared s_ld;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) s_tile = atomicAdd(counter, 1u);
+  for (int k = threadIdx.x; k < kSortWarps * kRadix; k += kSortBlock) (&s_hist[0][0])[k] = 0u;
+  __syncthreads();
+  const uint32_t tile = s_tile;
+  const uint32_t base = tile * kSortTile;
+  const uint32_t end = min(base + static_cast<uint32_t>(kSortTile), n);
+  ld.prepare(base, end, s_ld);
+
+  uint32_t keys[kSortItems], vals[kSortItems], rank[kSortItems];
+  const uint32_t lt = lanemask_lt();
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    const uint32_t idx = base + warp * (32 * kSortItems) + r * 32 + lane;
+    const bool valid = idx < end;
+    uint32_t key = 0u, val = 0u;
+    if (valid) ld.load(idx, s_ld, key, val);
+    const uint32_t d = valid ? ((key >> shift) & 255u) : 256u;
+    const uint32_t peers = __match_any_sync(0xffffffffu, d);
+    uint32_t before = 0u;
+    if (valid) before = s_hist[warp][d];
+    __syncwarp();
+    if (valid && (peers & lt) == 0u) s_hist[warp][d] = before + __popc(peers);
+    __syncwarp();
+    keys[r] = key;
+    vals[r] = val;
+    rank[r] = valid ? before + __popc(peers & lt) : 0xFFFFFFFFu;
+  }
+  __syncthreads();
+
+  {
+    const int d = threadIdx.x;
+    uint32_t total = 0u;
+#pragma unroll
+    for (int w = 0; w < kSortWarps; ++w) {
+      const uint32_t c = s_hist[w][d];
+      s_hist[w][d] = total;
+      total += c;
+    }
+    uint32_t excl = 0u;
+    uint32_t* mine = status + static_cast<size_t>(tile) * kRadix + d;
+    if (tile == 0) {
+      st_relaxed(mine, kFlagInclusive | total);
+    } else {
+      st_relaxed(mine, kFlagAggregate | total);
+      int64_t t = static_cast<int64_t>(tile) - 1;
+      uint32_t spins = 0;
+      while (t >= 0) {
+        const uint32_t s = ld_relaxed(status + static_cast<size_t>(t) * kRadix + d);
+        const uint32_t flag = s & ~kValueMask;
+        if (flag == 0u) {
+          if (++spins > kSpinLimit) {
+            record_device_error(kDeviceTimeout);
+            break;
+          }
+          __nanosleep(32);
+          continue;
+        }
+        excl += s & kValueMask;
+        if (flag == kFlagInclusive) break;
+        --t;
+      }
+      st_relaxed(mine, kFlagInclusive | (excl + total));
+    }
+    s_base[d] = digit_offsets[d] + excl;
+  }
+  __syncthreads();
+
+#pragma unroll
+  for (int r = 0; r < kSortItems; ++r) {
+    if (rank[r] == 0xFFFFFFFFu) continue;
+    const uint32_t d = (keys[r] >> shift) & 255u;
+    const uint32_t pos = s_base[d] + s_hist[warp][d] + rank[r];
+    if (pos >= n) {  // only reachable with inconsistent histograms
+      record_device_error(kInconsistentInput);
+      continue;
+    }
+    if (WRITE_KEYS) keys_out[pos] = keys[r];
+    vals_out[pos] = vals[r];
+  }
+}
+
+// ---- scans --------------------------------------------------------------
+// values[gather ? gather[i] : i] summed in blocks of kSortTile.
+
+SPLAT_DEV uint32_t scan_value(const int* __restrict__ values, const uint32_t* __restrict__ gather,
+                              uint32_t i) {
+  const uint32_t src = gather ? gather[i] : i;
+  const int v = values[src];
+  return v > 0 ? static_cast<uint32_t>(v) : 0u;
+}
+
+__global__ void __launch_bounds__(kSortBlock)
+    scan_block_sums_kernel(const int* __restrict__ values, const uint32_t* __restrict__ gather,
+                           uint32_t n, uint32_t* __restrict__ block_sums) {
+  __shared__ uint32_t s_warp[32];
+  const uint32_t base = blockIdx.x * kSortTile;
+  uint32_t sum = 0u;
+  for (int k = 0; k < kSortItems; ++k) {
+    const uint32_t i = base + k * kSortBlock + threadIdx.x;
+    if (i < n) sum += scan_value(values, gather, i);
+  }
+  uint32_t total;
+  block_exclusive_scan(sum, s_warp, &total);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = total;
+}
+
+// One block: exclusive scan of block_sums in place; total -> *total.
+__global__ void scan_block_prefix_kernel(uint32_t* __restrict__ block_sums, uint32_t nblocks,
+                                         uint32_t* __restrict__ total) {
+  __shared__ uint32_t s_warp[32];
+  __shared__ uint32_t s_carry;
+  if (threadIdx.x == 0) s_carry = 0u;
+  __syncthreads();
+  for (uint32_t base = 0; base < nblocks; base += blockDim.x) {
+    const uint32_t i = base + threadIdx.x;
+    const uint32_t v = i < nblocks ? block_sums[i] : 0u;
+    uint32_t chunk;
+    const uint32_t before = block_exclusive_scan(v, s_warp, &chunk);
+    if (i < nblocks) block_sums[i] = s_carry + before;
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry += chunk;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = s_carry;
+}
+
+// out[i] = exclusive (or inclusive) prefix; when exclusive, out[n] = total.
+__global__ void __launch_bounds__(kSortBlock)
+    scan_apply_kernel(const int* __restrict__ values, const uint32_t* __restrict__ gather,
+                      uint32_t n, const uint32_t* __restrict__ block_prefix, int inclusive,
+                      uint32_t* __restrict__ out) {
+  __shared__ uint32_t s_val[kSortTile];
+  __shared__ uint32_t s_warp[32];
+  const uint32_t base = blockIdx.x * kSortTile;
+  for (int k = 0; k < kSortItems; ++k) {
+    const int j = k * kSortBlock + threadIdx.x;
+    const uint32_t i = base + j;
+    s_val[j] = i < n ? scan_value(values, gather, i) : 0u;
+  }
+  __syncthreads();
+  uint32_t local[kSortItems];
+  uint32_t sum = 0u;
+#pragma unroll
+  for (int k = 0; k < kSortItems; ++k) {
+    local[k] = s_val[threadIdx.x * kSortItems + k];
+    sum += local[k];
+  }
+  uint32_t run = block_exclusive_scan(sum, s_warp, nullptr) + block_prefix[blockIdx.x];
+#pragma unroll
+  for (int k = 0; k < kSortItems; ++k) {
+    const uint32_t v = local[k];
+    s_val[threadIdx.x * kSortItems + k] = inclusive ? run + v : run;
+    run += v;
+  }
+  __syncthreads();
+  for (int k = 0; k < kSortItems; ++k) {
+    const int j = k * kSortBlock + threadIdx.x;
+    const uint32_t i = base + j;
+    if (i < n) out[i] = s_val[j];
+  }
+  if (!inclusive && blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
+    // the last element's exclusive prefix plus its value
+    const uint32_t last = n - 1;
+    if (last >= base) out[n] = s_val[last - base] + scan_value(values, gather, last);
+  }
+}
+
+// ---- tile counts, ranges and tile-id digit offsets (one block) ----------
+__global__ void __launch_bounds__(1024)
+    tile_counts_kernel(int* __restrict__ diff, int gx, int gy, int passes,
+                       int* __restrict__ ranges, uint32_t* __restrict__ digit_offsets,
+                       uint32_t* __restrict__ total) {
+  __shared__ uint32_t s_warp[32];
+  __shared__ uint32_t s_hist[3 * kRadix];
+  __shared__ uint32_t s_carry;
+  const int row = gx + 1;
+  // 2D inclusive prefix of the difference grid: rows, then columns.
+  for (int y = threadIdx.x; y <= gy; y += blockDim.x) {
+    int acc = 0;
+    for (int x = 0; x <= gx; ++x) {
+      acc += diff[y * row + x];
+      diff[y * row + x] = acc;
+    }
+  }
+  __syncthreads();
+  for (int x = threadIdx.x; x <= gx; x += blockDim.x) {
+    int acc = 0;
+    for (int y = 0; y <= gy; ++y) {
+      acc += diff[y * row + x];
+      diff[y * row + x] = acc;
+    }
+  }
+  for (int k = threadIdx.x; k < 3 * kRadix; k += blockDim.x) s_hist[k] = 0u;
+  if (threadIdx.x == 0) s_carry = 0u;
+  __syncthreads();
+  const int T = gx * gy;
+  for (int base = 0; base < T; base += blockDim.x) {
+    const int t = base + threadIdx.x;
+    uint32_t c = 0u;
+    if (t < T) c = static_cast<uint32_t>(max(diff[(t / gx) * row + (t % gx)], 0));
+    uint32_t chunk;
+    const uint32_t before = block_exclusive_scan(c, s_warp, &chunk) + s_carry;
+    if (t < T) {
+      ranges[2 * t] = c ? static_cast<int>(before) : 0;
+      ranges[2 * t + 1] = c ? static_cast<int>(before + c) : 0;
+      for (int p = 0; p < passes; ++p)
+        if (c) atomicAdd(&s_hist[p * kRadix + ((static_cast<uint32_t>(t) >> (8 * p)) & 255u)], c);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry += chunk;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = s_carry;
+  __syncthreads();
+  // exclusive scans of the tile-id digit histograms (first 256 threads)
+  for (int p = 0; p < passes; ++p) {
+    const uint32_t v = threadIdx.x < kRadix ? s_hist[p * kRadix + threadIdx.x] : 0u;
+    const uint32_t before = block_exclusive_scan(v, s_warp, nullptr);
+    if (threadIdx.x < kRadix) digit_offsets[p * kRadix + threadIdx.x] = before;
+  }
+}
+
+}  // namespace splat

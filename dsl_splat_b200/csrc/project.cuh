@@ -1,0 +1,685 @@
+// gs3d projection forward/backward, fused with SH0-3 and metadata.
+//
+// Forward restates gs3d/projection.py:37-164 (screen_covariance, project),
+// splatting/geometry.py:22-123 and primitives/sh.py:7-79 operation by
+// operation (compiled with -fmad=false; __fmaf_rn where the reference calls
+// fmaf).  Backward is the hand-derived VJP of projection_loss
+// (gs3d/projection.py:198-285) with the reference's custom adjoints for the
+// Jacobian clamp (splatting/geometry.py:42-51), the regularised inverse
+// covariance (splatting/geometry.py:61-71) and the quaternion rotation
+// (splatting/math.py:13-28), plus the SH VJP (primitives/sh.py:82-138).
+#pragma once
+#include "splat_common.cuh"
+
+namespace splat {
+
+struct ProjectParams {
+  int n;
+  const float* means;      // (n,3)
+  const float* quats;      // (n,4) normalised wxyz
+  const float* scales;     // (n,3)
+  const float* opacities;  // (n)
+  const float* view;       // 4x4 row-major world->camera
+  const float* proj;       // 4x4 full projection (camera_kernels.py:42-52)
+  const float* K;          // 3x3 intrinsics
+  int width, height;
+  float near_plane, far_plane, radius_clip;
+  float* centers;  // (n,2)  written for visible rows only
+  float* conics;   // (n,4)  (inv_a, inv_b, inv_c, opacity), visible rows only
+  int* radii;      // (n)
+  int* tiles;      // (n)
+  float* depths;   // (n)    visible rows only
+  // optional fused SH (sh == nullptr disables)
+  int sh_degree;
+  int sh_k;                // coefficients stored per Gaussian (K >= (deg+1)^2)
+  const float* sh;         // (n,K,3)
+  const float* campos;     // (3) camera centre; null => directions = means
+  float* colors;           // (n, color_stride) first 3 columns written
+  int color_stride;
+  uint8_t* active;         // (n,3) or null
+  // optional dense metadata (splatting/metadata.py:12-31), null disables
+  float* meta_means2d;     // (n,2)
+  float* meta_opacities;   // (n)
+  float* meta_conics;      // (n,3)
+};
+
+struct Mat3 {
+  float m[3][3];
+};
+
+// splatting/math.py:54-64 reference_matmul
+SPLAT_DEV Mat3 ref_matmul(const Mat3& a, const Mat3& b) {
+  Mat3 r;
+#pragma unroll
+  for (int row = 0; row < 3; ++row)
+#pragma unroll
+    for (int col = 0; col < 3; ++col)
+      r.m[row][col] = __fmaf_rn(a.m[row][2], b.m[2][col],
+                                __fmaf_rn(a.m[row][0], b.m[0][col], a.m[row][1] * b.m[1][col]));
+  return r;
+}
+
+SPLAT_DEV Mat3 transpose(const Mat3& a) {
+  Mat3 r;
+#pragma unroll
+  for (int i = 0; i < 3; ++i)
+#pragma unroll
+    for (int j = 0; j < 3; ++j) r.m[i][j] = a.m[j][i];
+  return r;
+}
+
+// splatting/math.py:67-70 point_row
+SPLAT_DEV float point_row(const float* m, int row, float p0, float p1, float p2) {
+  const float xy = __fmaf_rn(m[row * 4 + 0], p0, m[row * 4 + 1] * p1);
+  return __fmaf_rn(m[row * 4 + 2], p2, xy) + m[row * 4 + 3];
+}
+
+// primitives/math.py:33-45 glm_rotation
+SPLAT_DEV Mat3 glm_rotation(float r, float x, float y, float z) {
+  const float yy = y * y, zz = z * z;
+  const float rz = r * z, xz = x * z, rx = r * x;
+  const float d0 = yy + zz, d1 = __fmaf_rn(x, x, zz), d2 = __fmaf_rn(x, x, yy);
+  Mat3 R;
+  R.m[0][0] = 1.0f - (d0 + d0);
+  R.m[0][1] = 2.0f * __fmaf_rn(x, y, rz);
+  R.m[0][2] = 2.0f * __fmaf_rn(-r, y, xz);
+  R.m[1][0] = 2.0f * __fmaf_rn(x, y, -rz);
+  R.m[1][1] = 1.0f - (d1 + d1);
+  R.m[1][2] = 2.0f * __fmaf_rn(y, z, rx);
+  R.m[2][0] = 2.0f * __fmaf_rn(r, y, xz);
+  R.m[2][1] = 2.0f * __fmaf_rn(y, z, -rx);
+  R.m[2][2] = 1.0f - (d2 + d2);
+  return R;
+}
+
+// gs3d/projection.py:37-86 screen_covariance
+SPLAT_DEV float3 screen_covariance(float px, float py, float pz, float4 q, float3 s,
+                                   const float* view, int width, int height, float fx,
+                                   float fy) {
+  const float limx = W32(1.3) * static_cast<float>(width) / (2.0f * fx);
+  const float limy = W32(1.3) * static_cast<float>(height) / (2.0f * fy);
+  const float tx = wclamp(px / pz, -limx, limx) * pz;
+  const float ty = wclamp(py / pz, -limy, limy) * pz;
+  const float tz = pz;
+  const Mat3 R = glm_rotation(q.x, q.y, q.z, q.w);
+  const Mat3 S = {{{s.x, 0.0f, 0.0f}, {0.0f, s.y, 0.0f}, {0.0f, 0.0f, s.z}}};
+  const Mat3 M = ref_matmul(S, R);
+  const Mat3 cov = ref_matmul(transpose(M), M);
+  const Mat3 J = {{{fx / tz, 0.0f, 0.0f},
+                   {0.0f, fy / tz, 0.0f},
+                   {-(fx * tx) / (tz * tz), -(fy * ty) / (tz * tz), 0.0f}}};
+  const Mat3 cam = {{{view[0], view[4], view[8]}, {view[1], view[5], view[9]},
+                     {view[2], view[6], view[10]}}};
+  const Mat3 T = ref_matmul(cam, J);
+  const Mat3 P = ref_matmul(ref_matmul(transpose(T), transpose(cov)), T);
+  return make_float3(P.m[0][0] + W32(0.3), P.m[1][0], P.m[1][1] + W32(0.3));
+}
+
+// splatting/geometry.py:106-123 pixel_center
+SPLAT_DEV float2 pixel_center(float m0, float m1, float m2, const float* proj, int width,
+                              int height) {
+  const float c0 = point_row(proj, 0, m0, m1, m2);
+  const float c1 = point_row(proj, 1, m0, m1, m2);
+  const float c3 = point_row(proj, 3, m0, m1, m2);
+  const float inverse_w = 1.0f / (c3 + W32(1e-7));
+  const double ndc_x = static_cast<double>(c0 * inverse_w);
+  const double ndc_y = static_cast<double>(c1 * inverse_w);
+  return make_float2(
+      static_cast<float>(((ndc_x + 1.0) * static_cast<double>(width) - 1.0) * 0.5),
+      static_cast<float>(((ndc_y + 1.0) * static_cast<double>(height) - 1.0) * 0.5));
+}
+
+// primitives/sh.py:7-41 basis (Warp literals are float32-rounded doubles).
+SPLAT_DEV float sh_basis(float x, float y, float z, int k) {
+  switch (k) {
+    case 0: return W32(0.28209479177387814);
+    case 1: return -W32(0.4886025119029199) * y;
+    case 2: return W32(0.4886025119029199) * z;
+    case 3: return -W32(0.4886025119029199) * x;
+    case 4: return W32(1.0925484305920792) * x * y;
+    case 5: return -W32(1.0925484305920792) * y * z;
+    case 6: return W32(0.31539156525252005) * (2.0f * z * z - x * x - y * y);
+    case 7: return -W32(1.0925484305920792) * x * z;
+    case 8: return W32(0.5462742152960396) * (x * x - y * y);
+    case 9: return -W32(0.5900435899266435) * y * (3.0f * x * x - y * y);
+    case 10: return W32(2.890611442640554) * x * y * z;
+    case 11: return -W32(0.4570457994644658) * y * (4.0f * z * z - x * x - y * y);
+    case 12: return W32(0.3731763325901154) * z * (2.0f * z * z - 3.0f * x * x - 3.0f * y * y);
+    case 13: return -W32(0.4570457994644658) * x * (4.0f * z * z - x * x - y * y);
+    case 14: return W32(1.445305721320277) * z * (x * x - y * y);
+    default: return -W32(0.5900435899266435) * x * (x * x - 3.0f * y * y);
+  }
+}
+
+// d basis_k / d unit (what wp.grad(basis) evaluates at primitives/sh.py:127).
+SPLAT_DEV float3 sh_basis_grad(float x, float y, float z, int k) {
+  const float c1 = W32(0.4886025119029199), c4 = W32(1.0925484305920792);
+  const float c6 = W32(0.31539156525252005), c8 = W32(0.5462742152960396);
+  const float c9 = -W32(0.5900435899266435), c10 = W32(2.890611442640554);
+  const float c11 = -W32(0.4570457994644658), c12 = W32(0.3731763325901154);
+  const float c14 = W32(1.445305721320277);
+  switch (k) {
+    case 0: return make_float3(0.0f, 0.0f, 0.0f);
+    case 1: return make_float3(0.0f, -c1, 0.0f);
+    case 2: return make_float3(0.0f, 0.0f, c1);
+    case 3: return make_float3(-c1, 0.0f, 0.0f);
+    case 4: return make_float3(c4 * y, c4 * x, 0.0f);
+    case 5: return make_float3(0.0f, -c4 * z, -c4 * y);
+    case 6: return make_float3(-2.0f * c6 * x, -2.0f * c6 * y, 4.0f * c6 * z);
+    case 7: return make_float3(-c4 * z, 0.0f, -c4 * x);
+    case 8: return make_float3(2.0f * c8 * x, -2.0f * c8 * y, 0.0f);
+    case 9: return make_float3(c9 * 6.0f * x * y, c9 * (3.0f * x * x - 3.0f * y * y), 0.0f);
+    case 10: return make_float3(c10 * y * z, c10 * x * z, c10 * x * y);
+    case 11:
+      return make_float3(c11 * (-2.0f * x * y), c11 * (4.0f * z * z - x * x - 3.0f * y * y),
+                         c11 * (8.0f * y * z));
+    case 12:
+      return make_float3(c12 * (-6.0f * x * z), c12 * (-6.0f * y * z),
+                         c12 * (6.0f * z * z - 3.0f * x * x - 3.0f * y * y));
+    case 13:
+      return make_float3(c11 * (4.0f * z * z - 3.0f * x * x - y * y), c11 * (-2.0f * x * y),
+                         c11 * (8.0f * x * z));
+    case 14:
+      return make_float3(c14 * 2.0f * x * z, -c14 * 2.0f * y * z, c14 * (x * x - y * y));
+    default:
+      return make_float3(c9 * (3.0f * x * x - 3.0f * y * y), c9 * (-6.0f * x * y), 0.0f);
+  }
+}
+
+// primitives/sh.py:44-79 forward for one Gaussian (visible rows only).
+template <int DEG>
+SPLAT_DEV float3 sh_eval(const float* __restrict__ coef, float d0, float d1, float d2) {
+  float ux = 0.0f, uy = 0.0f, uz = 0.0f;
+  if (DEG > 0) {
+    const float len = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
+    const float den = wmax(len, W32(1e-12));
+    ux = d0 / den;
+    uy = d1 / den;
+    uz = d2 / den;
+  }
+  float v0 = 0.0f, v1 = 0.0f, v2 = 0.0f;
+#pragma unroll
+  for (int k = 0; k < (DEG + 1) * (DEG + 1); ++k) {
+    const float b = sh_basis(ux, uy, uz, k);
+    v0 = v0 + b * coef[3 * k + 0];
+    v1 = v1 + b * coef[3 * k + 1];
+    v2 = v2 + b * coef[3 * k + 2];
+  }
+  return make_float3(v0 + 0.5f, v1 + 0.5f, v2 + 0.5f);
+}
+
+// gs3d/projection.py:89-164 (+ primitives/sh.py:44-79, splatting/metadata.py:12-31)
+template <int DEG>
+__global__ void __launch_bounds__(256) project_forward_kernel(ProjectParams p) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= p.n) return;
+  const int gx = (p.width + 15) / 16, gy = (p.height + 15) / 16;
+  int radius_out = 0, count_out = 0;
+  float2 center = make_float2(0.0f, 0.0f);
+  float4 conic = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const float m0 = p.means[3 * i], m1 = p.means[3 * i + 1], m2 = p.means[3 * i + 2];
+  do {
+    const float t0 = point_row(p.view, 0, m0, m1, m2);
+    const float t1 = point_row(p.view, 1, m0, m1, m2);
+    const float t2 = point_row(p.view, 2, m0, m1, m2);
+    if (t2 <= p.near_plane || t2 >= p.far_plane) break;
+    const float4 q = reinterpret_cast<const float4*>(p.quats)[i];
+    const float3 s = make_float3(p.scales[3 * i], p.scales[3 * i + 1], p.scales[3 * i + 2]);
+    const float3 cov = screen_covariance(t0, t1, t2, q, s, p.view, p.width, p.height, p.K[0], p.K[4]);
+    const float a = cov.x, b = cov.y, c = cov.z;
+    const float det = a * c - b * b;
+    if (det == 0.0f) break;
+    const float mid = 0.5f * (a + c);
+    const int radius = f2i(ceilf(3.0f * sqrtf(mid + sqrtf(wmax(W32(0.1), mid * mid - det)))));
+    if (static_cast<float>(radius) <= p.radius_clip) break;
+    center = pixel_center(m0, m1, m2, p.proj, p.width, p.height);
+    const int4 bnd = tile_bounds(center.x, center.y, radius, gx, gy);
+    const int count = (bnd.z - bnd.x) * (bnd.w - bnd.y);
+    if (count == 0) break;
+    const float inverse = 1.0f / (a * c - b * b);
+    conic = make_float4(c * inverse, -b * inverse, a * inverse, p.opacities[i]);
+    reinterpret_cast<float2*>(p.centers)[i] = center;
+    reinterpret_cast<float4*>(p.conics)[i] = conic;
+    p.depths[i] = t2;
+    radius_out = radius;
+    count_out = count;
+  } while (false);
+  p.radii[i] = radius_out;
+  p.tiles[i] = count_out;
+  const bool visible = radius_out > 0;
+  if (DEG >= 0 && p.sh != nullptr) {
+    float3 v = make_float3(0.0f, 0.0f, 0.0f);
+    if (visible) {
+      float d0 = m0, d1 = m1, d2 = m2;
+      if (p.campos != nullptr) {
+        d0 = m0 - p.campos[0];
+        d1 = m1 - p.campos[1];
+        d2 = m2 - p.campos[2];
+      }
+      v = sh_eval<(DEG < 0 ? 0 : DEG)>(p.sh + static_cast<size_t>(i) * p.sh_k * 3, d0, d1, d2);
+    }
+    float* col = p.colors + static_cast<size_t>(i) * p.color_stride;
+    col[0] = wmax(v.x, 0.0f);
+    col[1] = wmax(v.y, 0.0f);
+    col[2] = wmax(v.z, 0.0f);
+    if (p.active != nullptr) {
+      p.active[3 * i + 0] = visible && v.x >= 0.0f;
+      p.active[3 * i + 1] = visible && v.y >= 0.0f;
+      p.active[3 * i + 2] = visible && v.z >= 0.0f;
+    }
+  }
+  if (p.meta_means2d != nullptr) {
+    reinterpret_cast<float2*>(p.meta_means2d)[i] = center;
+    p.meta_opacities[i] = conic.w;
+    p.meta_conics[3 * i + 0] = conic.x;
+    p.meta_conics[3 * i + 1] = conic.y;
+    p.meta_conics[3 * i + 2] = conic.z;
+  }
+}
+
+// splatting/metadata.py:12-31 _prepare (standalone stage).
+__global__ void metadata_kernel(int n, const int* __restrict__ radii,
+                                const float* __restrict__ centers,
+                                const float* __restrict__ conics, float* __restrict__ means2d,
+                                float* __restrict__ opacities, float* __restrict__ conics3) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float2 c = make_float2(0.0f, 0.0f);
+  float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (radii[i] > 0) {
+    c = reinterpret_cast<const float2*>(centers)[i];
+    q = reinterpret_cast<const float4*>(conics)[i];
+  }
+  reinterpret_cast<float2*>(means2d)[i] = c;
+  opacities[i] = q.w;
+  conics3[3 * i + 0] = q.x;
+  conics3[3 * i + 1] = q.y;
+  conics3[3 * i + 2] = q.z;
+}
+
+// primitives/sh.py:44-79 standalone SH forward (masked when radii != null).
+template <int DEG>
+__global__ void sh_forward_kernel(int n, int sh_k, const float* __restrict__ sh,
+                                  const float* __restrict__ dirs, const int* __restrict__ radii,
+                                  float* __restrict__ colors, uint8_t* __restrict__ active) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const bool visible = radii ? radii[i] > 0 : true;
+  float3 v = make_float3(0.0f, 0.0f, 0.0f);
+  if (visible)
+    v = sh_eval<DEG>(sh + static_cast<size_t>(i) * sh_k * 3, dirs[3 * i], dirs[3 * i + 1],
+                     dirs[3 * i + 2]);
+  colors[3 * i + 0] = wmax(v.x, 0.0f);
+  colors[3 * i + 1] = wmax(v.y, 0.0f);
+  colors[3 * i + 2] = wmax(v.z, 0.0f);
+  if (active) {
+    active[3 * i + 0] = visible && v.x >= 0.0f;
+    active[3 * i + 1] = visible && v.y >= 0.0f;
+    active[3 * i + 2] = visible && v.z >= 0.0f;
+  }
+}
+
+// primitives/sh.py:82-138 VJP for one Gaussian: writes the (K,3) coefficient
+// gradient (zeros past (DEG+1)^2) and returns the direction gradient.
+template <int DEG>
+SPLAT_DEV float3 sh_vjp(const float* __restrict__ coef, int sh_k, float d0, float d1, float d2,
+                        float3 cg, float* __restrict__ gcoef, bool accumulate) {
+  float ux = 0.0f, uy = 0.0f, uz = 0.0f, length = 1.0f;
+  if (DEG > 0) {
+    length = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
+    const float den = wmax(length, W32(1e-12));
+    ux = d0 / den;
+    uy = d1 / den;
+    uz = d2 / den;
+  }
+  float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+#pragma unroll
+  for (int k = 0; k < (DEG + 1) * (DEG + 1); ++k) {
+    const float b = sh_basis(ux, uy, uz, k);
+    float* o = gcoef + 3 * k;
+    if (accumulate) {
+      o[0] += b * cg.x;
+      o[1] += b * cg.y;
+      o[2] += b * cg.z;
+    } else {
+      o[0] = b * cg.x;
+      o[1] = b * cg.y;
+      o[2] = b * cg.z;
+    }
+    if (DEG > 0) {
+      const float w = coef[3 * k] * cg.x + coef[3 * k + 1] * cg.y + coef[3 * k + 2] * cg.z;
+      const float3 bg = sh_basis_grad(ux, uy, uz, k);
+      g0 += w * bg.x;
+      g1 += w * bg.y;
+      g2 += w * bg.z;
+    }
+  }
+  if (!accumulate)
+    for (int k = (DEG + 1) * (DEG + 1); k < sh_k; ++k) {
+      gcoef[3 * k] = 0.0f;
+      gcoef[3 * k + 1] = 0.0f;
+      gcoef[3 * k + 2] = 0.0f;
+    }
+  if (DEG == 0) return make_float3(0.0f, 0.0f, 0.0f);
+  const float den = wmax(length, W32(1e-12));
+  float3 dg = make_float3(g0 / den, g1 / den, g2 / den);
+  if (length >= W32(1e-12)) {
+    const float dot = (ux * g0 + uy * g1 + uz * g2) / length;
+    dg.x -= ux * dot;
+    dg.y -= uy * dot;
+    dg.z -= uz * dot;
+  }
+  return dg;
+}
+
+template <int DEG>
+__global__ void sh_backward_kernel(int n, int sh_k, const float* __restrict__ sh,
+                                   const float* __restrict__ dirs, const int* __restrict__ radii,
+                                   const uint8_t* __restrict__ active,
+                                   const float* __restrict__ upstream,
+                                   float* __restrict__ grad_sh, float* __restrict__ grad_dirs) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const bool visible = radii ? radii[i] > 0 : true;
+  float* gcoef = grad_sh + static_cast<size_t>(i) * sh_k * 3;
+  float3 dg = make_float3(0.0f, 0.0f, 0.0f);
+  if (visible) {
+    const float3 cg = make_float3(active[3 * i] ? upstream[3 * i] : 0.0f,
+                                  active[3 * i + 1] ? upstream[3 * i + 1] : 0.0f,
+                                  active[3 * i + 2] ? upstream[3 * i + 2] : 0.0f);
+    dg = sh_vjp<DEG>(sh + static_cast<size_t>(i) * sh_k * 3, sh_k, dirs[3 * i], dirs[3 * i + 1],
+                     dirs[3 * i + 2], cg, gcoef, false);
+  } else {
+    for (int k = 0; k < 3 * sh_k; ++k) gcoef[k] = 0.0f;
+  }
+  if (grad_dirs) {
+    grad_dirs[3 * i + 0] = dg.x;
+    grad_dirs[3 * i + 1] = dg.y;
+    grad_dirs[3 * i + 2] = dg.z;
+  }
+}
+
+struct ProjectBackwardParams {
+  int n;
+  const float* means;
+  const float* quats;
+  const float* scales;
+  const float* view;
+  const float* proj;
+  const float* K;
+  int width, height;
+  const int* radii;
+  const float* seed_centers;  // (n,2) dL/dcenters
+  const float* seed_conics;   // (n,4) dL/dconics (incl. opacity)
+  float* grad_means;          // (n,3) or null
+  float* grad_quats;          // (n,4) or null
+  float* grad_scales;         // (n,3) or null
+  float* grad_opacities;      // (n)   or null
+  int accumulate;             // add into grad_* instead of overwriting
+  // camera reductions (float[35]: view 16, proj 16, campos 3), null disables
+  float* cam_grads;
+  // optional fused SH backward
+  int sh_degree;
+  int sh_k;
+  const float* sh;
+  const float* campos;
+  const uint8_t* active;
+  const float* seed_colors;   // (n, color_stride)
+  int color_stride;
+  float* grad_sh;             // (n,K,3)
+};
+
+// Hand-derived VJP of gs3d/projection.py:198-210 projection_loss for one
+// visible Gaussian.  Returns grads through the out-parameters; camera
+// partials are added into cv (view, 16) and cp (proj, 16).
+SPLAT_DEV void projection_vjp(const ProjectBackwardParams& p, int i, float m0, float m1, float m2,
+                              float gm[3], float gq[4], float gs[3], float cv[16], float cp[16]) {
+  const float fx = p.K[0], fy = p.K[4];
+  const float* view = p.view;
+  const float* proj = p.proj;
+  const float4 q = reinterpret_cast<const float4*>(p.quats)[i];
+  const float s[3] = {p.scales[3 * i], p.scales[3 * i + 1], p.scales[3 * i + 2]};
+  const float2 sc = reinterpret_cast<const float2*>(p.seed_centers)[i];
+  const float4 sq = reinterpret_cast<const float4*>(p.seed_conics)[i];
+  const float m[3] = {m0, m1, m2};
+  const float t0 = point_row(view, 0, m0, m1, m2);
+  const float t1 = point_row(view, 1, m0, m1, m2);
+  const float tz = point_row(view, 2, m0, m1, m2);
+  const float limx = W32(1.3) * static_cast<float>(p.width) / (2.0f * fx);
+  const float limy = W32(1.3) * static_cast<float>(p.height) / (2.0f * fy);
+  const float xr = t0 / tz, yr = t1 / tz;
+  const float tcx = wclamp(xr, -limx, limx) * tz;
+  const float tcy = wclamp(yr, -limy, limy) * tz;
+  const Mat3 R = glm_rotation(q.x, q.y, q.z, q.w);
+  float M[3][3], Sig[3][3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) M[r][c] = s[r] * R.m[r][c];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) Sig[r][c] = M[0][r] * M[0][c] + M[1][r] * M[1][c] + M[2][r] * M[2][c];
+  const float J[3][3] = {{fx / tz, 0.0f, 0.0f},
+                         {0.0f, fy / tz, 0.0f},
+                         {-(fx * tcx) / (tz * tz), -(fy * tcy) / (tz * tz), 0.0f}};
+  const float Wc[3][3] = {{view[0], view[4], view[8]}, {view[1], view[5], view[9]},
+                          {view[2], view[6], view[10]}};
+  float Tm[3][3], A[3][3], P[3][3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) Tm[r][c] = Wc[r][0] * J[0][c] + Wc[r][1] * J[1][c] + Wc[r][2] * J[2][c];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int c = 0; c < 3; ++c)
+      A[r][c] = Tm[0][r] * Sig[c][0] + Tm[1][r] * Sig[c][1] + Tm[2][r] * Sig[c][2];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int c = 0; c < 3; ++c) P[r][c] = A[r][0] * Tm[0][c] + A[r][1] * Tm[1][c] + A[r][2] * Tm[2][c];
+  const float a = P[0][0] + W32(0.3), b = P[1][0], c = P[1][1] + W32(0.3);
+  // adj_invert_covariance (splatting/geometry.py:61-71)
+  const float det = a * c - b * b;
+  const float factor = 1.0f / (det * det + W32(0.0000001));
+  const float X = sq.x, Y = sq.y, Z = sq.z;
+  const float da = factor * (-c * c * X + b * c * Y + (det - a * c) * Z);
+  const float db = factor * (2.0f * b * c * X - (det + 2.0f * b * b) * Y + 2.0f * a * b * Z);
+  const float dc = factor * (-a * a * Z + a * b * Y + (det - a * c) * X);
+  const float dP[3][3] = {{da, 0.0f, 0.0f}, {db, dc, 0.0f}, {0.0f, 0.0f, 0.0f}};
+  float dA[3][3], dTm[3][3], dSig[3][3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      dA[r][k] = dP[r][0] * Tm[k][0] + dP[r][1] * Tm[k][1] + dP[r][2] * Tm[k][2];
+      dTm[r][k] = A[0][r] * dP[0][k] + A[1][r] * dP[1][k] + A[2][r] * dP[2][k];
+    }
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      dTm[r][k] += Sig[0][r] * dA[k][0] + Sig[1][r] * dA[k][1] + Sig[2][r] * dA[k][2];
+      dSig[r][k] = dA[0][r] * Tm[k][0] + dA[1][r] * Tm[k][1] + dA[2][r] * Tm[k][2];
+    }
+  float dWc[3][3], dJ[3][3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      dWc[r][k] = dTm[r][0] * J[k][0] + dTm[r][1] * J[k][1] + dTm[r][2] * J[k][2];
+      dJ[r][k] = Wc[0][r] * dTm[0][k] + Wc[1][r] * dTm[1][k] + Wc[2][r] * dTm[2][k];
+    }
+  float dR[3][3];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+    float dM[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      dM[k] = M[r][0] * (dSig[0][k] + dSig[k][0]) + M[r][1] * (dSig[1][k] + dSig[k][1]) +
+              M[r][2] * (dSig[2][k] + dSig[k][2]);
+    gs[r] = dM[0] * R.m[r][0] + dM[1] * R.m[r][1] + dM[2] * R.m[r][2];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) dR[r][k] = s[r] * dM[k];
+  }
+  // adj_reference_rotation (splatting/math.py:13-28)
+  {
+    const float qr = q.x, qx = q.y, qy = q.z, qz = q.w;
+    gq[0] = 2.0f * (qz * (dR[0][1] - dR[1][0]) + qy * (dR[2][0] - dR[0][2]) + qx * (dR[1][2] - dR[2][1]));
+    gq[1] = 2.0f * (qy * (dR[0][1] + dR[1][0]) + qz * (dR[0][2] + dR[2][0]) + qr * (dR[1][2] - dR[2][1])) -
+            4.0f * qx * (dR[1][1] + dR[2][2]);
+    gq[2] = 2.0f * (qx * (dR[0][1] + dR[1][0]) + qr * (dR[2][0] - dR[0][2]) + qz * (dR[1][2] + dR[2][1])) -
+            4.0f * qy * (dR[0][0] + dR[2][2]);
+    gq[3] = 2.0f * (qr * (dR[0][1] - dR[1][0]) + qx * (dR[0][2] + dR[2][0]) + qy * (dR[1][2] + dR[2][1])) -
+            4.0f * qz * (dR[0][0] + dR[1][1]);
+  }
+  const float tz2 = tz * tz, tz3 = tz2 * tz;
+  const float dtcx = dJ[2][0] * (-fx / tz2);
+  const float dtcy = dJ[2][1] * (-fy / tz2);
+  const float dtcz = dJ[0][0] * (-fx / tz2) + dJ[1][1] * (-fy / tz2) +
+                     dJ[2][0] * (2.0f * fx * tcx / tz3) + dJ[2][1] * (2.0f * fy * tcy / tz3);
+  // adj_clamp_point (splatting/geometry.py:42-51)
+  const float dt[3] = {(xr >= -limx && xr <= limx) ? dtcx : 0.0f,
+                       (yr >= -limy && yr <= limy) ? dtcy : 0.0f, dtcz};
+#pragma unroll
+  for (int j = 0; j < 3; ++j) gm[j] = view[j] * dt[0] + view[4 + j] * dt[1] + view[8 + j] * dt[2];
+#pragma unroll
+  for (int r = 0; r < 3; ++r) {
+#pragma unroll
+    for (int j = 0; j < 3; ++j) cv[r * 4 + j] += dt[r] * m[j];
+    cv[r * 4 + 3] += dt[r];
+  }
+#pragma unroll
+  for (int r = 0; r < 3; ++r)
+#pragma unroll
+    for (int k = 0; k < 3; ++k) cv[k * 4 + r] += dWc[r][k];
+  // pixel_center (splatting/geometry.py:106-123)
+  const float c0 = point_row(proj, 0, m0, m1, m2);
+  const float c1 = point_row(proj, 1, m0, m1, m2);
+  const float c3 = point_row(proj, 3, m0, m1, m2);
+  const float iw = 1.0f / (c3 + W32(1e-7));
+  const float dnx = sc.x * static_cast<float>(p.width) * 0.5f;
+  const float dny = sc.y * static_cast<float>(p.height) * 0.5f;
+  const float dc0 = dnx * iw, dc1 = dny * iw;
+  const float diw = dnx * c0 + dny * c1;
+  const float dc3 = -diw * iw * iw;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    gm[j] += proj[j] * dc0 + proj[4 + j] * dc1 + proj[12 + j] * dc3;
+    cp[0 + j] += dc0 * m[j];
+    cp[4 + j] += dc1 * m[j];
+    cp[12 + j] += dc3 * m[j];
+  }
+  cp[3] += dc0;
+  cp[7] += dc1;
+  cp[15] += dc3;
+}
+
+template <int DEG, bool CAMERA>
+__global__ void __launch_bounds__(256) project_backward_kernel(ProjectBackwardParams p) {
+  constexpr int kCam = 35;
+  float cam[kCam];
+  if (CAMERA) {
+#pragma unroll
+    for (int j = 0; j < kCam; ++j) cam[j] = 0.0f;
+  }
+  const int stride = gridDim.x * blockDim.x;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += stride) {
+    float gm[3] = {0.0f, 0.0f, 0.0f}, gq[4] = {0.0f, 0.0f, 0.0f, 0.0f}, gs[3] = {0.0f, 0.0f, 0.0f};
+    float go = 0.0f;
+    const bool visible = p.radii[i] > 0;
+    const float m0 = p.means[3 * i], m1 = p.means[3 * i + 1], m2 = p.means[3 * i + 2];
+    if (visible) {
+      float cv_local[16], cp_local[16];
+      if (CAMERA) {
+        projection_vjp(p, i, m0, m1, m2, gm, gq, gs, cam, cam + 16);
+      } else {
+        projection_vjp(p, i, m0, m1, m2, gm, gq, gs, cv_local, cp_local);
+      }
+      go = p.seed_conics[4 * i + 3];
+    }
+    if (DEG >= 0 && p.grad_sh != nullptr) {
+      float* gcoef = p.grad_sh + static_cast<size_t>(i) * p.sh_k * 3;
+      if (visible) {
+        const float* sc = p.seed_colors + static_cast<size_t>(i) * p.color_stride;
+        const float3 cg = make_float3(p.active[3 * i] ? sc[0] : 0.0f, p.active[3 * i + 1] ? sc[1] : 0.0f,
+                                      p.active[3 * i + 2] ? sc[2] : 0.0f);
+        float d0 = m0, d1 = m1, d2 = m2;
+        if (p.campos) {
+          d0 = m0 - p.campos[0];
+          d1 = m1 - p.campos[1];
+          d2 = m2 - p.campos[2];
+        }
+        const float3 dd = sh_vjp<(DEG < 0 ? 0 : DEG)>(p.sh + static_cast<size_t>(i) * p.sh_k * 3, p.sh_k,
+                                                      d0, d1, d2, cg, gcoef, p.accumulate != 0);
+        if (DEG > 0) {
+          gm[0] += dd.x;
+          gm[1] += dd.y;
+          gm[2] += dd.z;
+          if (CAMERA && p.campos) {
+            cam[32] -= dd.x;
+            cam[33] -= dd.y;
+            cam[34] -= dd.z;
+          }
+        }
+      } else if (!p.accumulate) {
+        for (int k = 0; k < 3 * p.sh_k; ++k) gcoef[k] = 0.0f;
+      }
+    }
+    if (p.accumulate) {
+      if (p.grad_means) {
+        p.grad_means[3 * i] += gm[0];
+        p.grad_means[3 * i + 1] += gm[1];
+        p.grad_means[3 * i + 2] += gm[2];
+      }
+      if (p.grad_quats) {
+        float4* o = reinterpret_cast<float4*>(p.grad_quats) + i;
+        float4 v = *o;
+        v.x += gq[0];
+        v.y += gq[1];
+        v.z += gq[2];
+        v.w += gq[3];
+        *o = v;
+      }
+      if (p.grad_scales) {
+        p.grad_scales[3 * i] += gs[0];
+        p.grad_scales[3 * i + 1] += gs[1];
+        p.grad_scales[3 * i + 2] += gs[2];
+      }
+      if (p.grad_opacities) p.grad_opacities[i] += go;
+    } else {
+      if (p.grad_means) {
+        p.grad_means[3 * i] = gm[0];
+        p.grad_means[3 * i + 1] = gm[1];
+        p.grad_means[3 * i + 2] = gm[2];
+      }
+      if (p.grad_quats) reinterpret_cast<float4*>(p.grad_quats)[i] = make_float4(gq[0], gq[1], gq[2], gq[3]);
+      if (p.grad_scales) {
+        p.grad_scales[3 * i] = gs[0];
+        p.grad_scales[3 * i + 1] = gs[1];
+        p.grad_scales[3 * i + 2] = gs[2];
+      }
+      if (p.grad_opacities) p.grad_opacities[i] = go;
+    }
+  }
+  if (CAMERA) {
+    // Warp shuffles, then warp leaders through shared memory, then one
+    // atomic per entry per block (gs3d/projection.py:269-283).
+    __shared__ float s_cam[8][kCam];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int j = 0; j < kCam; ++j) {
+      const float v = warp_sum(cam[j]);
+      if (lane == 0) s_cam[warp][j] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < kCam) {
+      float v = 0.0f;
+      for (int w = 0; w < (blockDim.x >> 5); ++w) v += s_cam[w][threadIdx.x];
+      atomicAdd(p.cam_grads + threadIdx.x, v);
+    }
+  }
+}
+
+}  // namespace splat

@@ -1,0 +1,765 @@
+// C-ABI entry points of libsplat200 (declared in include/splat200.h).
+//
+// Plain device pointers, sizes and a cudaStream_t (as void*) in; a status
+// code out (0 = success, negative = error; splat_last_error() describes the
+// latest failure of the calling thread).  All work is enqueued on the given
+// stream; nothing here allocates device memory: callers pass outputs and,
+// for binning, a workspace sized by the *_workspace_bytes queries.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "binning.cuh"
+#include "cameras.cuh"
+#include "project.cuh"
+#include "render.cuh"
+#include "splat_common.cuh"
+
+using namespace splat;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* what) {
+  g_last_error = what;
+  return status;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    g_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return kCudaError;
+  }
+  return kOk;
+}
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Every kernel launch passes its stream through counted(), so
+// splat_launch_count() reports how many kernels this library has launched.
+unsigned long long g_launches = 0;
+inline cudaStream_t counted(cudaStream_t s) {
+  __atomic_fetch_add(&g_launches, 1ULL, __ATOMIC_RELAXED);
+  return s;
+}
+inline unsigned blocks_for(long long n, int block) {
+  return static_cast<unsigned>((n + block - 1) / block);
+}
+inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+// Kernels read float2/float4 rows and issue red.global.add.v2/v4: their
+// addresses must be 8/16-byte aligned (NULL passes; it means "absent").
+inline bool aligned(const void* p, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+}
+
+int tile_passes(int tiles) { return tiles <= 256 ? 1 : (tiles <= 65536 ? 2 : 3); }
+
+// ---- binning workspace layout -------------------------------------------
+struct BinLayout {
+  size_t keys_a, vals_a, keys_b, vals_b, rects, offsets, block_sums;
+  size_t zero_begin;  // everything from here to zero_end is cleared per call
+  size_t depth_hist, diff, depth_status, counters, totals;
+  size_t zero_end;
+  size_t depth_digits, tile_digits;
+  size_t bytes;
+};
+
+BinLayout bin_layout(long long n, int width, int height) {
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+  const size_t sort_tiles = static_cast<size_t>(blocks_for(n > 0 ? n : 1, kSortTile));
+  BinLayout L{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align256(o + bytes);
+    return at;
+  };
+  L.keys_a = take(4 * n);
+  L.vals_a = take(4 * n);
+  L.keys_b = take(4 * n);
+  L.vals_b = take(4 * n);
+  L.rects = take(8 * n);
+  L.offsets = take(4 * (n + 1));
+  L.block_sums = take(4 * (sort_tiles + 1));
+  L.zero_begin = o;
+  L.depth_hist = take(4 * 4 * kRadix);
+  L.diff = take(4 * static_cast<size_t>(gx + 1) * (gy + 1));
+  L.depth_status = take(4 * 4 * sort_tiles * kRadix);
+  L.counters = take(4 * 8);
+  L.totals = take(8 * 4);
+  L.zero_end = o;
+  L.depth_digits = take(4 * 4 * kRadix);
+  L.tile_digits = take(4 * 3 * kRadix);
+  L.bytes = o;
+  return L;
+}
+
+struct PairLayout {
+  size_t keys0, vals0, keys1, vals1, status, counters, bytes;
+};
+
+PairLayout pair_layout(long long pairs, int width, int height) {
+  const int tiles = ((width + 15) / 16) * ((height + 15) / 16);
+  const int passes = tile_passes(tiles);
+  const size_t sort_tiles = static_cast<size_t>(blocks_for(pairs > 0 ? pairs : 1, kSortTile));
+  PairLayout L{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align256(o + bytes);
+    return at;
+  };
+  L.keys0 = take(4 * pairs);
+  L.vals0 = take(4 * pairs);
+  L.keys1 = take(passes > 2 ? 4 * pairs : 0);
+  L.vals1 = take(passes > 2 ? 4 * pairs : 0);
+  L.status = take(4 * passes * sort_tiles * kRadix);
+  L.counters = take(4 * 4);
+  L.bytes = o;
+  return L;
+}
+
+template <typename T>
+T* at(void* base, size_t off) {
+  return reinterpret_cast<T*>(static_cast<char*>(base) + off);
+}
+
+template <int DEG>
+void launch_project_forward(const ProjectParams& p, cudaStream_t s) {
+  project_forward_kernel<DEG><<<blocks_for(p.n, 256), 256, 0, counted(s)>>>(p);
+}
+
+int project_forward_dispatch(const ProjectParams& p, cudaStream_t s) {
+  if (p.n == 0) return kOk;
+  if (p.sh == nullptr) {
+    launch_project_forward<-1>(p, s);
+  } else {
+    switch (p.sh_degree) {
+      case 0: launch_project_forward<0>(p, s); break;
+      case 1: launch_project_forward<1>(p, s); break;
+      case 2: launch_project_forward<2>(p, s); break;
+      case 3: launch_project_forward<3>(p, s); break;
+      default: return fail(kInvalidArgument, "sh_degree must be in [0,3]");
+    }
+  }
+  return check_launch("project_forward");
+}
+
+template <int DEG, bool CAMERA>
+void launch_project_backward(const ProjectBackwardParams& p, cudaStream_t s) {
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  unsigned grid = blocks_for(p.n, 256);
+  if (CAMERA) grid = grid < static_cast<unsigned>(sms * 8) ? grid : static_cast<unsigned>(sms * 8);
+  project_backward_kernel<DEG, CAMERA><<<grid, 256, 0, counted(s)>>>(p);
+}
+
+template <bool CAMERA>
+int project_backward_deg(const ProjectBackwardParams& p, cudaStream_t s) {
+  if (p.grad_sh == nullptr) {
+    launch_project_backward<-1, CAMERA>(p, s);
+    return kOk;
+  }
+  switch (p.sh_degree) {
+    case 0: launch_project_backward<0, CAMERA>(p, s); break;
+    case 1: launch_project_backward<1, CAMERA>(p, s); break;
+    case 2: launch_project_backward<2, CAMERA>(p, s); break;
+    case 3: launch_project_backward<3, CAMERA>(p, s); break;
+    default: return fail(kInvalidArgument, "sh_degree must be in [0,3]");
+  }
+  return kOk;
+}
+
+int project_backward_dispatch(const ProjectBackwardParams& p, cudaStream_t s) {
+  if (p.n == 0) return kOk;
+  const int r = p.cam_grads ? project_backward_deg<true>(p, s) : project_backward_deg<false>(p, s);
+  if (r != kOk) return r;
+  return check_launch("project_backward");
+}
+
+template <int CHP>
+void launch_render(const RenderParams& p, bool backward, cudaStream_t s) {
+  const unsigned tiles = static_cast<unsigned>(p.gx * ((p.height + 15) / 16));
+  if (backward)
+    render_backward_kernel<CHP><<<tiles, kBlock, 0, counted(s)>>>(p);
+  else
+    render_forward_kernel<CHP><<<tiles, kBlock, 0, counted(s)>>>(p);
+}
+
+int render_dispatch(const RenderParams& p, bool backward, cudaStream_t s) {
+  if (p.channels <= 4)
+    launch_render<4>(p, backward, s);
+  else if (p.channels <= 8)
+    launch_render<8>(p, backward, s);
+  else if (p.channels <= 16)
+    launch_render<16>(p, backward, s);
+  else if (p.channels <= 32)
+    launch_render<32>(p, backward, s);
+  else
+    return fail(kInvalidArgument, "at most 32 blended channels are supported");
+  return check_launch(backward ? "render_backward" : "render_forward");
+}
+
+}  // namespace
+
+extern "C" {
+
+int splat_abi_version(void) { return 1; }
+
+unsigned long long splat_launch_count(void) { return __atomic_load_n(&g_launches, __ATOMIC_RELAXED); }
+
+const char* splat_last_error(void) { return g_last_error.c_str(); }
+
+int splat_device_error(int* code, void* stream) {
+  if (!code) return fail(kInvalidArgument, "code must not be null");
+  cudaStream_t s = as_stream(stream);
+  int value = 0;
+  if (cudaMemcpyFromSymbolAsync(&value, g_splat_device_error, sizeof(int), 0,
+                                cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return check_launch("splat_device_error");
+  const int zero = 0;
+  if (cudaMemcpyToSymbolAsync(g_splat_device_error, &zero, sizeof(int), 0,
+                              cudaMemcpyHostToDevice, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return check_launch("splat_device_error reset");
+  *code = value;
+  return kOk;
+}
+
+// ---- cameras -------------------------------------------------------------
+
+int splat_cameras_prepare(int count, const float* views, const float* Ks, int width, int height,
+                          int with_centers, float* full, float* inverse, float* centers,
+                          int* errors, void* stream) {
+  if (count < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad camera sizes");
+  if (count == 0) return kOk;
+  if (!views || !Ks || !full || !errors || (with_centers && (!inverse || !centers)))
+    return fail(kInvalidArgument, "null camera buffer");
+  cameras_prepare_kernel<<<blocks_for(count, 64), 64, 0, counted(as_stream(stream))>>>(
+      count, views, Ks, width, height, with_centers, full, inverse, centers, errors);
+  return check_launch("cameras_prepare");
+}
+
+int splat_cameras_backward(int count, const float* Ks, const float* grad_full, int width,
+                           int height, const float* inverse, const float* grad_centers,
+                           float* grad_views, void* stream) {
+  if (count < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad camera sizes");
+  if (count == 0) return kOk;
+  if (!Ks || !grad_views || (grad_centers && !inverse))
+    return fail(kInvalidArgument, "null camera buffer");
+  cameras_backward_kernel<<<blocks_for(count, 64), 64, 0, counted(as_stream(stream))>>>(
+      count, Ks, grad_full, width, height, inverse, grad_centers, grad_views);
+  return check_launch("cameras_backward");
+}
+
+// ---- projection ----------------------------------------------------------
+
+int splat_project_forward(int n, const float* means, const float* quats, const float* scales,
+                          const float* opacities, const float* view, const float* proj,
+                          const float* K, int width, int height, float near_plane,
+                          float far_plane, float radius_clip, float* centers, float* conics,
+                          int* radii, int* tiles, float* depths, void* stream) {
+  if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (!aligned(quats, 16) || !aligned(conics, 16) || !aligned(centers, 8))
+    return fail(kInvalidArgument, "quats/conics need 16-byte and centers 8-byte alignment");
+  ProjectParams p{};
+  p.n = n;
+  p.means = means;
+  p.quats = quats;
+  p.scales = scales;
+  p.opacities = opacities;
+  p.view = view;
+  p.proj = proj;
+  p.K = K;
+  p.width = width;
+  p.height = height;
+  p.near_plane = near_plane;
+  p.far_plane = far_plane;
+  p.radius_clip = radius_clip;
+  p.centers = centers;
+  p.conics = conics;
+  p.radii = radii;
+  p.tiles = tiles;
+  p.depths = depths;
+  return project_forward_dispatch(p, as_stream(stream));
+}
+
+int splat_project_forward_fused(int n, const float* means, const float* quats,
+                                const float* scales, const float* opacities, const float* view,
+                                const float* proj, const float* K, int width, int height,
+                                float near_plane, float far_plane, float radius_clip,
+                                float* centers, float* conics, int* radii, int* tiles,
+                                float* depths, int sh_degree, int sh_k, const float* sh,
+                                const float* campos, float* colors, int color_stride,
+                                unsigned char* active, float* meta_means2d,
+                                float* meta_opacities, float* meta_conics, void* stream) {
+  if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (sh && (sh_degree < 0 || sh_degree > 3 || sh_k < (sh_degree + 1) * (sh_degree + 1) ||
+             !colors || color_stride < 3))
+    return fail(kInvalidArgument, "bad SH arguments");
+  if (meta_means2d && (!meta_opacities || !meta_conics))
+    return fail(kInvalidArgument, "metadata outputs come together");
+  if (!aligned(meta_means2d, 8)) return fail(kInvalidArgument, "means2d needs 8-byte alignment");
+  ProjectParams p{};
+  p.n = n;
+  p.means = means;
+  p.quats = quats;
+  p.scales = scales;
+  p.opacities = opacities;
+  p.view = view;
+  p.proj = proj;
+  p.K = K;
+  p.width = width;
+  p.height = height;
+  p.near_plane = near_plane;
+  p.far_plane = far_plane;
+  p.radius_clip = radius_clip;
+  p.centers = centers;
+  p.conics = conics;
+  p.radii = radii;
+  p.tiles = tiles;
+  p.depths = depths;
+  p.sh_degree = sh_degree;
+  p.sh_k = sh_k;
+  p.sh = sh;
+  p.campos = campos;
+  p.colors = colors;
+  p.color_stride = color_stride;
+  p.active = active;
+  p.meta_means2d = meta_means2d;
+  p.meta_opacities = meta_opacities;
+  p.meta_conics = meta_conics;
+  return project_forward_dispatch(p, as_stream(stream));
+}
+
+int splat_metadata(int n, const int* radii, const float* centers, const float* conics,
+                   float* means2d, float* opacities, float* conics3, void* stream) {
+  if (n < 0) return fail(kInvalidArgument, "n < 0");
+  if (n == 0) return kOk;
+  if (!aligned(centers, 8) || !aligned(conics, 16) || !aligned(means2d, 8))
+    return fail(kInvalidArgument, "centers/means2d need 8-byte and conics 16-byte alignment");
+  metadata_kernel<<<blocks_for(n, 256), 256, 0, counted(as_stream(stream))>>>(n, radii, centers, conics,
+                                                                     means2d, opacities, conics3);
+  return check_launch("metadata");
+}
+
+int splat_project_backward(int n, const float* means, const float* quats, const float* scales,
+                           const float* view, const float* proj, const float* K, int width,
+                           int height, const int* radii, const float* grad_centers,
+                           const float* grad_conics, float* grad_means, float* grad_quats,
+                           float* grad_scales, float* grad_opacities, float* camera_grads,
+                           void* stream) {
+  if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (!aligned(quats, 16) || !aligned(grad_quats, 16) || !aligned(grad_conics, 16) ||
+      !aligned(grad_centers, 8))
+    return fail(kInvalidArgument, "quat/conic rows need 16-byte, center rows 8-byte alignment");
+  ProjectBackwardParams p{};
+  p.n = n;
+  p.means = means;
+  p.quats = quats;
+  p.scales = scales;
+  p.view = view;
+  p.proj = proj;
+  p.K = K;
+  p.width = width;
+  p.height = height;
+  p.radii = radii;
+  p.seed_centers = grad_centers;
+  p.seed_conics = grad_conics;
+  p.grad_means = grad_means;
+  p.grad_quats = grad_quats;
+  p.grad_scales = grad_scales;
+  p.grad_opacities = grad_opacities;
+  p.cam_grads = camera_grads;
+  return project_backward_dispatch(p, as_stream(stream));
+}
+
+int splat_project_backward_fused(int n, const float* means, const float* quats,
+                                 const float* scales, const float* view, const float* proj,
+                                 const float* K, int width, int height, const int* radii,
+                                 const float* grad_centers, const float* grad_conics,
+                                 float* grad_means, float* grad_quats, float* grad_scales,
+                                 float* grad_opacities, int accumulate, float* camera_grads,
+                                 int sh_degree, int sh_k, const float* sh, const float* campos,
+                                 const unsigned char* active, const float* grad_colors,
+                                 int color_stride, float* grad_sh, void* stream) {
+  if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (grad_sh && (!sh || !active || !grad_colors || sh_degree < 0 || sh_degree > 3 ||
+                  sh_k < (sh_degree + 1) * (sh_degree + 1)))
+    return fail(kInvalidArgument, "bad SH backward arguments");
+  if (!aligned(quats, 16) || !aligned(grad_quats, 16) || !aligned(grad_conics, 16) ||
+      !aligned(grad_centers, 8))
+    return fail(kInvalidArgument, "quat/conic rows need 16-byte, center rows 8-byte alignment");
+  ProjectBackwardParams p{};
+  p.n = n;
+  p.means = means;
+  p.quats = quats;
+  p.scales = scales;
+  p.view = view;
+  p.proj = proj;
+  p.K = K;
+  p.width = width;
+  p.height = height;
+  p.radii = radii;
+  p.seed_centers = grad_centers;
+  p.seed_conics = grad_conics;
+  p.grad_means = grad_means;
+  p.grad_quats = grad_quats;
+  p.grad_scales = grad_scales;
+  p.grad_opacities = grad_opacities;
+  p.accumulate = accumulate;
+  p.cam_grads = camera_grads;
+  p.sh_degree = sh_degree;
+  p.sh_k = sh_k;
+  p.sh = sh;
+  p.campos = campos;
+  p.active = active;
+  p.seed_colors = grad_colors;
+  p.color_stride = color_stride;
+  p.grad_sh = grad_sh;
+  return project_backward_dispatch(p, as_stream(stream));
+}
+
+// ---- spherical harmonics ---------------------------------------------------
+
+int splat_sh_forward(int n, int degree, int sh_k, const float* sh, const float* dirs,
+                     const int* radii, float* colors, unsigned char* active, void* stream) {
+  if (n < 0 || degree < 0 || degree > 3 || sh_k < (degree + 1) * (degree + 1))
+    return fail(kInvalidArgument, "bad SH arguments");
+  if (n == 0) return kOk;
+  cudaStream_t s = as_stream(stream);
+  const unsigned g = blocks_for(n, 256);
+  switch (degree) {
+    case 0: sh_forward_kernel<0><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
+    case 1: sh_forward_kernel<1><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
+    case 2: sh_forward_kernel<2><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
+    default: sh_forward_kernel<3><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
+  }
+  return check_launch("sh_forward");
+}
+
+int splat_sh_backward(int n, int degree, int sh_k, const float* sh, const float* dirs,
+                      const int* radii, const unsigned char* active, const float* upstream,
+                      float* grad_sh, float* grad_dirs, void* stream) {
+  if (n < 0 || degree < 0 || degree > 3 || sh_k < (degree + 1) * (degree + 1))
+    return fail(kInvalidArgument, "bad SH arguments");
+  if (n == 0) return kOk;
+  cudaStream_t s = as_stream(stream);
+  const unsigned g = blocks_for(n, 256);
+  switch (degree) {
+    case 0: sh_backward_kernel<0><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
+    case 1: sh_backward_kernel<1><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
+    case 2: sh_backward_kernel<2><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
+    default: sh_backward_kernel<3><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
+  }
+  return check_launch("sh_backward");
+}
+
+// ---- scan -------------------------------------------------------------------
+
+size_t splat_scan_workspace_bytes(int n) {
+  return 4 * (static_cast<size_t>(blocks_for(n > 0 ? n : 1, kSortTile)) + 2) + 256;
+}
+
+int splat_scan_counts(int n, const int* counts, int* offsets, long long* total, void* workspace,
+                      size_t workspace_bytes, void* stream) {
+  if (n < 0) return fail(kInvalidArgument, "n < 0");
+  if (workspace_bytes < splat_scan_workspace_bytes(n))
+    return fail(kWorkspaceTooSmall, "scan workspace too small");
+  cudaStream_t s = as_stream(stream);
+  uint32_t* block_sums = static_cast<uint32_t*>(workspace);
+  const unsigned nb = blocks_for(n > 0 ? n : 1, kSortTile);
+  uint32_t* tot = block_sums + nb + 1;
+  if (n == 0) {
+    if (total && cudaMemsetAsync(total, 0, sizeof(long long), s) != cudaSuccess)
+      return check_launch("scan_counts");
+    return kOk;
+  }
+  scan_block_sums_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, nullptr, n, block_sums);
+  scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, nb, tot);
+  scan_apply_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, nullptr, n, block_sums, 1,
+                                             reinterpret_cast<uint32_t*>(offsets));
+  if (total) {
+    if (cudaMemsetAsync(total, 0, sizeof(long long), s) != cudaSuccess ||
+        cudaMemcpyAsync(total, tot, sizeof(uint32_t), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return check_launch("scan_counts total");
+  }
+  return check_launch("scan_counts");
+}
+
+// ---- binning ------------------------------------------------------------------
+
+size_t splat_bin_workspace_bytes(int n, int width, int height) {
+  return bin_layout(n, width, height).bytes;
+}
+
+size_t splat_bin_pairs_workspace_bytes(long long pairs, int width, int height) {
+  return pair_layout(pairs, width, height).bytes;
+}
+
+int splat_bin_prepare(int n, const float* centers, const int* radii, const int* tiles,
+                      const float* depths, int width, int height, void* workspace,
+                      size_t workspace_bytes, int* ranges, long long* pairs, void* stream) {
+  if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad binning sizes");
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+  if (gx > 65535 || gy > 65535 || static_cast<long long>(gx) * gy >= (1LL << 24))
+    return fail(kTooLarge, "image has too many tiles");
+  if (n >= (1 << 30)) return fail(kTooLarge, "too many Gaussians");
+  const BinLayout L = bin_layout(n, width, height);
+  if (!workspace || workspace_bytes < L.bytes) return fail(kWorkspaceTooSmall, "bin workspace too small");
+  if (!ranges || !pairs) return fail(kInvalidArgument, "null ranges/pairs");
+  if (!aligned(centers, 8) || !aligned(workspace, 256))
+    return fail(kInvalidArgument, "centers need 8-byte, workspace 256-byte alignment");
+  cudaStream_t s = as_stream(stream);
+  char* ws = static_cast<char*>(workspace);
+  if (cudaMemsetAsync(ws + L.zero_begin, 0, L.zero_end - L.zero_begin, s) != cudaSuccess)
+    return check_launch("bin_prepare memset");
+  const int T = gx * gy;
+  if (n == 0) {
+    if (cudaMemsetAsync(ranges, 0, sizeof(int) * 2 * T, s) != cudaSuccess ||
+        cudaMemsetAsync(pairs, 0, sizeof(long long), s) != cudaSuccess)
+      return check_launch("bin_prepare empty");
+    return kOk;
+  }
+  uint32_t* keys_a = at<uint32_t>(ws, L.keys_a);
+  uint32_t* vals_a = at<uint32_t>(ws, L.vals_a);
+  uint32_t* keys_b = at<uint32_t>(ws, L.keys_b);
+  uint32_t* vals_b = at<uint32_t>(ws, L.vals_b);
+  uint2* rects = at<uint2>(ws, L.rects);
+  uint32_t* offsets = at<uint32_t>(ws, L.offsets);
+  uint32_t* block_sums = at<uint32_t>(ws, L.block_sums);
+  uint32_t* hist = at<uint32_t>(ws, L.depth_hist);
+  int* diff = at<int>(ws, L.diff);
+  uint32_t* status = at<uint32_t>(ws, L.depth_status);
+  uint32_t* counters = at<uint32_t>(ws, L.counters);
+  uint32_t* totals = at<uint32_t>(ws, L.totals);
+  uint32_t* depth_digits = at<uint32_t>(ws, L.depth_digits);
+  uint32_t* tile_digits = at<uint32_t>(ws, L.tile_digits);
+  const unsigned sort_tiles = blocks_for(n, kSortTile);
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const unsigned prep_grid = std::min<unsigned>(blocks_for(n, 256), static_cast<unsigned>(sms * 8));
+  unsigned long long* total64 = at<unsigned long long>(ws, L.totals + 8);
+  bin_prepare_kernel<<<prep_grid, 256, 0, counted(s)>>>(n, centers, radii, tiles, depths, gx, gy, keys_a,
+                                               vals_a, rects, diff, hist, total64);
+  digit_offsets_kernel<<<1, kRadix, 0, counted(s)>>>(hist, 4, depth_digits);
+  // four stable passes over the 32-bit depth keys: a -> b -> a -> b -> a
+  for (int pass = 0; pass < 4; ++pass) {
+    const bool even = (pass % 2) == 0;
+    KeyValueLoader ld{even ? keys_a : keys_b, even ? vals_a : vals_b};
+    onesweep_kernel<KeyValueLoader, true><<<sort_tiles, kSortBlock, 0, counted(s)>>>(
+        ld, static_cast<uint32_t>(n), 8 * pass, depth_digits + pass * kRadix,
+        status + static_cast<size_t>(pass) * sort_tiles * kRadix, counters + pass,
+        even ? keys_b : keys_a, even ? vals_b : vals_a);
+  }
+  // pair offsets in depth order: offsets[j] = sum of tiles[order[i]], i < j
+  scan_block_sums_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums);
+  scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, sort_tiles, totals + 0);
+  scan_apply_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums, 0, offsets);
+  tile_counts_kernel<<<1, 1024, 0, counted(s)>>>(diff, gx, gy, tile_passes(T), ranges, tile_digits,
+                                        totals + 1);
+  // The 64-bit total cannot wrap; splat_bin_emit refuses totals >= 2^30.
+  if (cudaMemcpyAsync(pairs, total64, sizeof(long long), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return check_launch("bin_prepare pairs");
+  return check_launch("bin_prepare");
+}
+
+int splat_bin_emit(int n, long long pairs, int width, int height, void* workspace,
+                   size_t workspace_bytes, void* pairs_workspace, size_t pairs_workspace_bytes,
+                   int* ids, void* stream) {
+  if (n < 0 || pairs < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad sizes");
+  if (pairs >= (1LL << 30)) return fail(kTooLarge, "more than 2^30 Gaussian-tile pairs");
+  if (pairs == 0) return kOk;
+  const BinLayout L = bin_layout(n, width, height);
+  const PairLayout P = pair_layout(pairs, width, height);
+  if (!workspace || workspace_bytes < L.bytes) return fail(kWorkspaceTooSmall, "bin workspace too small");
+  if (!pairs_workspace || pairs_workspace_bytes < P.bytes)
+    return fail(kWorkspaceTooSmall, "pair workspace too small");
+  if (!ids) return fail(kInvalidArgument, "null ids");
+  if (!aligned(workspace, 256) || !aligned(pairs_workspace, 256))
+    return fail(kInvalidArgument, "workspaces need 256-byte alignment");
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+  const int passes = tile_passes(gx * gy);
+  cudaStream_t s = as_stream(stream);
+  char* ws = static_cast<char*>(workspace);
+  char* pw = static_cast<char*>(pairs_workspace);
+  if (cudaMemsetAsync(pw + P.status, 0, P.bytes - P.status, s) != cudaSuccess)
+    return check_launch("bin_emit memset");
+  const uint32_t m = static_cast<uint32_t>(pairs);
+  const unsigned sort_tiles = blocks_for(pairs, kSortTile);
+  uint32_t* status = at<uint32_t>(pw, P.status);
+  uint32_t* counters = at<uint32_t>(pw, P.counters);
+  const uint32_t* tile_digits = at<uint32_t>(ws, L.tile_digits);
+  EmitLoader emit{at<uint32_t>(ws, L.offsets), at<uint32_t>(ws, L.vals_a), at<uint2>(ws, L.rects),
+                  static_cast<uint32_t>(n), gx};
+  uint32_t* k0 = at<uint32_t>(pw, P.keys0);
+  uint32_t* v0 = at<uint32_t>(pw, P.vals0);
+  uint32_t* k1 = at<uint32_t>(pw, P.keys1);
+  uint32_t* v1 = at<uint32_t>(pw, P.vals1);
+  uint32_t* out = reinterpret_cast<uint32_t*>(ids);
+  if (passes == 1) {
+    onesweep_kernel<EmitLoader, false><<<sort_tiles, kSortBlock, 0, counted(s)>>>(
+        emit, m, 0, tile_digits, status, counters, nullptr, out);
+  } else {
+    onesweep_kernel<EmitLoader, true><<<sort_tiles, kSortBlock, 0, counted(s)>>>(
+        emit, m, 0, tile_digits, status, counters, k0, v0);
+    uint32_t* src_k = k0;
+    uint32_t* src_v = v0;
+    for (int pass = 1; pass < passes; ++pass) {
+      const bool last = pass == passes - 1;
+      KeyValueLoader ld{src_k, src_v};
+      uint32_t* dst_k = (src_k == k0) ? k1 : k0;
+      uint32_t* dst_v = last ? out : ((src_v == v0) ? v1 : v0);
+      uint32_t* st = status + static_cast<size_t>(pass) * sort_tiles * kRadix;
+      if (last)
+        onesweep_kernel<KeyValueLoader, false><<<sort_tiles, kSortBlock, 0, counted(s)>>>(
+            ld, m, 8 * pass, tile_digits + pass * kRadix, st, counters + pass, nullptr, dst_v);
+      else
+        onesweep_kernel<KeyValueLoader, true><<<sort_tiles, kSortBlock, 0, counted(s)>>>(
+            ld, m, 8 * pass, tile_digits + pass * kRadix, st, counters + pass, dst_k, dst_v);
+      src_k = dst_k;
+      src_v = dst_v;
+    }
+  }
+  return check_launch("bin_emit");
+}
+
+// ---- blending -----------------------------------------------------------------
+
+int splat_render_forward_statistics(
+    int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
+    const float* centers, const float* conics, const float* feat_a, int ch_a, int stride_a,
+    const float* feat_b, int ch_b, int stride_b, int append_one, const float* background,
+    float* image, int pix_stride, int ch_stride, float* final_t, int* contributors,
+    int stat_count, int stat_sum_mask, const float* stat_pixels, int* stat_counts,
+    float* stat_sums, void* stream) {
+  if (width <= 0 || height <= 0 || ch_a < 0 || ch_b < 0 || (ch_b > 0 && !feat_b) || n < 0 ||
+      num_ids < 0 || num_ids >= (1LL << 31))
+    return fail(kInvalidArgument, "bad render sizes");
+  if (stat_count < 0 || stat_count > 30 || (stat_count > 0 && !stat_pixels))
+    return fail(kInvalidArgument, "bad statistics arguments");
+  if (!aligned(centers, 8) || !aligned(conics, 16))
+    return fail(kInvalidArgument, "centers need 8-byte and conics 16-byte alignment");
+  RenderParams p{};
+  p.width = width;
+  p.height = height;
+  p.gx = (width + 15) / 16;
+  p.ranges = ranges;
+  p.ids = ids;
+  p.num_ids = static_cast<int>(num_ids);
+  p.centers = centers;
+  p.conics = conics;
+  p.feat_a = feat_a;
+  p.ch_a = ch_a;
+  p.stride_a = stride_a;
+  p.feat_b = feat_b;
+  p.ch_b = ch_b;
+  p.stride_b = stride_b;
+  p.append_one = append_one ? 1 : 0;
+  p.channels = ch_a + ch_b + p.append_one;
+  p.background = background;
+  p.image = image;
+  p.pix_stride = pix_stride;
+  p.ch_stride = ch_stride;
+  p.final_t = final_t;
+  p.contributors = contributors;
+  p.stat_count = stat_count;
+  p.stat_sum_mask = stat_sum_mask;
+  p.n_gaussians = n;
+  p.stat_pixels = stat_pixels;
+  p.stat_counts = stat_counts;
+  p.stat_sums = stat_sums;
+  if (p.channels <= 0) return fail(kInvalidArgument, "no channels");
+  return render_dispatch(p, false, as_stream(stream));
+}
+
+int splat_render_forward(int width, int height, const int* ranges, const int* ids,
+                         long long num_ids, int n, const float* centers, const float* conics,
+                         const float* feat_a, int ch_a, int stride_a, const float* feat_b,
+                         int ch_b, int stride_b, int append_one, const float* background,
+                         float* image, int pix_stride, int ch_stride, float* final_t,
+                         int* contributors, void* stream) {
+  return splat_render_forward_statistics(width, height, ranges, ids, num_ids, n, centers, conics,
+                                         feat_a, ch_a, stride_a, feat_b, ch_b, stride_b,
+                                         append_one, background, image, pix_stride, ch_stride,
+                                         final_t, contributors, 0, 0, nullptr, nullptr, nullptr,
+                                         stream);
+}
+
+int splat_render_backward(int width, int height, const int* ranges, const int* ids,
+                          long long num_ids, int n, const float* centers, const float* conics,
+                          const float* feat_a,
+                          int ch_a, int stride_a, const float* feat_b, int ch_b, int stride_b,
+                          int append_one, const float* background, const float* final_t,
+                          const int* contributors, const float* upstream, int up_pix_stride,
+                          int up_ch_stride, float* grad_centers, float* grad_conics,
+                          float* grad_a, float* grad_b, float* abs_centers, int constant_tail,
+                          void* stream) {
+  if (width <= 0 || height <= 0 || ch_a < 0 || ch_b < 0 || (ch_b > 0 && !feat_b) || n < 0 ||
+      num_ids < 0 || num_ids >= (1LL << 31))
+    return fail(kInvalidArgument, "bad render sizes");
+  RenderParams p{};
+  p.width = width;
+  p.height = height;
+  p.gx = (width + 15) / 16;
+  p.ranges = ranges;
+  p.ids = ids;
+  p.num_ids = static_cast<int>(num_ids);
+  p.n_gaussians = n;
+  p.centers = centers;
+  p.conics = conics;
+  p.feat_a = feat_a;
+  p.ch_a = ch_a;
+  p.stride_a = stride_a;
+  p.feat_b = feat_b;
+  p.ch_b = ch_b;
+  p.stride_b = stride_b;
+  p.append_one = append_one ? 1 : 0;
+  p.channels = ch_a + ch_b + p.append_one;
+  p.background = background;
+  p.final_t = const_cast<float*>(final_t);
+  p.contributors = const_cast<int*>(contributors);
+  p.upstream = upstream;
+  p.up_pix_stride = up_pix_stride;
+  p.up_ch_stride = up_ch_stride;
+  p.grad_centers = grad_centers;
+  p.grad_conics = grad_conics;
+  p.grad_a = grad_a;
+  p.grad_b = grad_b;
+  p.abs_centers = abs_centers;
+  p.constant_tail = constant_tail;
+  if (p.channels <= 0 || constant_tail < 0 || constant_tail > p.channels)
+    return fail(kInvalidArgument, "bad channel counts");
+  if (!grad_centers || !grad_conics) return fail(kInvalidArgument, "null gradient buffers");
+  if (!aligned(centers, 8) || !aligned(conics, 16) || !aligned(grad_centers, 8) ||
+      !aligned(grad_conics, 16) || !aligned(abs_centers, 8))
+    return fail(kInvalidArgument, "center rows need 8-byte and conic rows 16-byte alignment");
+  return render_dispatch(p, true, as_stream(stream));
+}
+
+// ---- diagnostics --------------------------------------------------------------
+
+}  // extern "C"
+
+namespace {
+__global__ void expf_probe_kernel(int n, const float* __restrict__ x, float* __restrict__ ours,
+                                  float* __restrict__ cuda_exp) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  ours[i] = splat_expf(x[i]);
+  cuda_exp[i] = expf(x[i]);
+}
+}  // namespace
+
+extern "C" int splat_debug_expf(int n, const float* x, float* ours, float* cuda_exp, void* stream) {
+  if (n <= 0) return kOk;
+  expf_probe_kernel<<<blocks_for(n, 256), 256, 0, counted(as_stream(stream))>>>(n, x, ours, cuda_exp);
+  return check_launch("debug_expf");
+}

@@ -1,0 +1,115 @@
+// Shared device helpers for the sm_100a gs3d rasteriser.
+//
+// The library is compiled with -fmad=false: every a*b+c below is two IEEE
+// roundings unless the code calls __fmaf_rn, which mirrors the reference's
+// explicit fmaf / fused_multiply_add calls (dsl_splat primitives/math.py,
+// splatting/math.py) and makes integer outputs (radii, tile counts, keys)
+// reproducible by the CPU oracle bit for bit.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define SPLAT_DEV __device__ __forceinline__
+
+namespace splat {
+
+constexpr int kTile = 16;              // 16x16-pixel tiles (gs3d/render.py:57-61)
+constexpr int kBlock = 256;            // one CTA per tile, one thread per pixel
+constexpr uint32_t kCulledKey = 0xFFFFFFFFu;
+
+// Status codes returned by every C entry point (0 = success).
+enum Status : int {
+  kOk = 0,
+  kInvalidArgument = -1,
+  kCudaError = -2,
+  kDeviceTimeout = -3,
+  kTooLarge = -4,
+  kWorkspaceTooSmall = -5,
+  kInconsistentInput = -6,  // device-side guard skipped an out-of-range index
+};
+
+// A Python float literal in a Warp kernel is the double value rounded to
+// float32; W32 makes the same conversion.
+#define W32(x) static_cast<float>(x)
+
+SPLAT_DEV float wmax(float a, float b) { return a > b ? a : b; }
+SPLAT_DEV float wmin(float a, float b) { return a < b ? a : b; }
+SPLAT_DEV float wclamp(float x, float a, float b) { return wmin(wmax(a, x), b); }
+SPLAT_DEV int iclamp(int x, int a, int b) { return min(max(a, x), b); }
+
+// float -> int32, truncating, saturating, NaN -> 0 (Warp int() on CUDA).
+SPLAT_DEV int f2i(float x) { return __float2int_rz(x); }
+
+// exp(x): Cody-Waite argument reduction (x = n ln2 + r with ln2 split into
+// a 9-bit head 0.693359375 and a correction), the degree-7 Taylor series of
+// exp(r) evaluated by Horner's rule with fused multiply-adds, and scaling by
+// 2^n through the exponent field.  Each step is one IEEE float32 operation,
+// so the CPU oracle computes the same bits and both sides take the same
+// alpha-threshold decisions.  Maximum error below 1 ulp on [-80, 0].
+SPLAT_DEV float splat_expf(float x) {
+  if (!(x > -80.0f)) return 0.0f;
+  if (x > 88.0f) x = 88.0f;
+  const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
+  float r = __fmaf_rn(n, -0.693359375f, x);
+  r = __fmaf_rn(n, 2.12194440054690583e-4f, r);
+  float p = 1.98412698e-4f;
+  p = __fmaf_rn(p, r, 1.38888889e-3f);
+  p = __fmaf_rn(p, r, 8.33333377e-3f);
+  p = __fmaf_rn(p, r, 4.16666679e-2f);
+  p = __fmaf_rn(p, r, 1.66666672e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const float scale = __int_as_float((static_cast<int>(n) + 127) << 23);
+  return __fmul_rn(p, scale);
+}
+
+// splatting/geometry.py:22-30 tile_bounds: CUDA getRect truncation.
+SPLAT_DEV int4 tile_bounds(float cx, float cy, int radius, int gx, int gy) {
+  const float r = static_cast<float>(radius);
+  int4 b;
+  b.x = iclamp(f2i(__fdiv_rn(__fsub_rn(cx, r), 16.0f)), 0, gx);
+  b.y = iclamp(f2i(__fdiv_rn(__fsub_rn(cy, r), 16.0f)), 0, gy);
+  b.z = iclamp(f2i(__fdiv_rn(__fsub_rn(__fadd_rn(__fadd_rn(cx, r), 16.0f), 1.0f), 16.0f)), 0, gx);
+  b.w = iclamp(f2i(__fdiv_rn(__fsub_rn(__fadd_rn(__fadd_rn(cy, r), 16.0f), 1.0f), 16.0f)), 0, gy);
+  return b;
+}
+
+// Relaxed device-scope loads/stores for look-back status words.
+SPLAT_DEV uint32_t ld_relaxed(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+SPLAT_DEV void st_relaxed(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Vector reductions into global memory (sm_90+).
+SPLAT_DEV void red_add_v2(float* p, float a, float b) {
+  asm volatile("red.relaxed.gpu.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b)
+               : "memory");
+}
+SPLAT_DEV void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a),
+               "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+SPLAT_DEV void red_add(float* p, float a) {
+  asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
+}
+
+SPLAT_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+SPLAT_DEV uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+}  // namespace splat

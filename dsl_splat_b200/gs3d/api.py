@@ -1,0 +1,165 @@
+"""Original 3DGS entry point (gs3d/api.py:1-265) on the sm_100a kernels.
+
+Same signature, validation, batching, metadata and result type as the
+reference; the per-view work runs as: one camera launch for all views, one
+fused projection+SH+metadata launch per view, binning of all views with a
+single host read of their pair counts, and one blend launch per view.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from numbers import Integral
+from typing import Any, Sequence
+
+import torch
+from torch import Tensor
+
+from ..camera_prep import ViewConfig, prepare_cameras, prepare_cameras_with_centers
+from ..cameras import validate_camera_options
+from ..inputs import batch_item, normalize_inputs
+from ..statistics import StatisticsRequest, prepare_statistics
+from ..training import prepare_training_metadata
+from .. import stages
+from .autograd import ProjectView, RenderView
+
+TILE_MODES = ("radius", "snugbox", "accutile")
+
+
+def validate_tile_mode(mode) -> None:
+    """splatting/intersections.py:24-26."""
+    if mode not in TILE_MODES:
+        raise ValueError("tile_mode must be 'radius', 'snugbox' or 'accutile'")
+    if mode != "radius":
+        raise NotImplementedError(f"tile_mode {mode!r} is not implemented on the B200 path yet")
+
+
+@dataclass(slots=True)
+class RasterizationResult:
+    """Channel-last images and training metadata (gs3d/api.py:25-44)."""
+
+    features: Tensor
+    alpha: Tensor
+    meta: dict[str, Any]
+    statistics: dict[str, Tensor] = field(default_factory=dict)
+
+    @property
+    def radii(self) -> Tensor:
+        return self.meta["radii"]
+
+    @property
+    def means2d(self) -> Tensor:
+        return self.meta["means2d"]
+
+    @property
+    def extra_features(self) -> Tensor | None:
+        return self.meta.get("render_extra_signals")
+
+
+def _check_sh(sh_coeffs, sh_degree, features):
+    if (features is None) == (sh_coeffs is None):
+        raise ValueError("provide exactly one of features or sh_coeffs")
+    if sh_coeffs is not None:
+        if not isinstance(sh_coeffs, Tensor) or sh_coeffs.ndim < 3:
+            raise ValueError("sh_coeffs must have shape (...,N,K,3) or (...,C,N,K,3)")
+        if sh_degree is None:
+            sh_degree = min(3, math.isqrt(sh_coeffs.shape[-2]) - 1)
+    elif sh_degree is not None:
+        raise ValueError("sh_degree requires sh_coeffs")
+    if sh_degree is not None and (isinstance(sh_degree, bool) or not isinstance(sh_degree, Integral)
+                                  or sh_degree not in range(4)):
+        raise ValueError("sh_degree must be an integer in [0,3]")
+    return sh_degree
+
+
+def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, viewmats: Tensor,
+              Ks: Tensor, width: int, height: int, *, features: Tensor | None = None,
+              sh_coeffs: Tensor | None = None, sh_degree: int | None = None,
+              backgrounds: Tensor | None = None, extra_features: Tensor | None = None,
+              near_plane: float = 0.2, far_plane: float = math.inf, radius_clip: float = 0.0,
+              packed: bool = False, absgrad: bool = False,
+              statistics: Sequence[StatisticsRequest] = (),
+              tile_mode: str = "radius") -> RasterizationResult:
+    """Render original 3DGS (centre-depth order, square tile bounds).
+
+    Inputs are activated scales/opacities and wxyz quaternions (normalised
+    here).  means2d is in CUDA raster coordinates (integer pixel centres,
+    K-projected position minus 0.5), zero for culled rows.  Gradients reach
+    means, quats, scales, opacities, features/SH, extras and viewmats.
+    """
+    validate_tile_mode(tile_mode)
+    validate_camera_options(width, height, near_plane, far_plane, radius_clip)
+    sh_degree = _check_sh(sh_coeffs, sh_degree, features)
+    layout = normalize_inputs(means, quats, scales, opacities,
+                              features if sh_coeffs is None else sh_coeffs, viewmats, Ks,
+                              backgrounds, extra_features, None, sh_degree)
+    with_centers = sh_degree is not None and sh_degree > 0
+    if with_centers:
+        full, centers = prepare_cameras_with_centers(layout.viewmats, layout.Ks, width, height)
+    else:
+        full, centers = prepare_cameras(layout.viewmats, layout.Ks, width, height), None
+    config = ViewConfig(width, height, near_plane, far_plane, radius_clip, tile_mode)
+    grad_enabled = torch.is_grad_enabled()
+    frames = []
+    dense: dict[str, list[Tensor]] = {k: [] for k in ("radii", "means2d", "opacities",
+                                                      "tiles_per_gauss", "conics")}
+    for b in range(layout.batch_count):
+        bm, bq = layout.means[b], layout.quats[b]
+        bs, bo = layout.scales[b], layout.opacities[b]
+        for c in range(layout.cameras):
+            view = batch_item(batch_item(layout.viewmats, b), c)
+            proj = batch_item(batch_item(full, b), c)
+            K = batch_item(batch_item(layout.Ks, b), c)
+            campos = batch_item(batch_item(centers, b), c) if with_centers else None
+            values = layout.colors.at(b, c)
+            out = ProjectView.apply(bm, bq, bs, bo, values if sh_degree is not None else None,
+                                    view, proj, campos, K, config, sh_degree, grad_enabled)
+            ctr, con, col, radii, tiles, depths, m2d, mop, mcon = out
+            colors = col if sh_degree is not None else values
+            extras = None if layout.extras is None else layout.extras.at(b, c)
+            bg = None if layout.backgrounds is None else batch_item(batch_item(layout.backgrounds, b), c)
+            frames.append((b, c, ctr, con, colors, extras, bg,
+                           stages.ProjectedGaussians(ctr, con, radii, tiles, depths)))
+            dense["radii"].append(radii[:, None].expand(-1, 2))
+            dense["means2d"].append(m2d)
+            dense["opacities"].append(mop)
+            dense["tiles_per_gauss"].append(tiles)
+            dense["conics"].append(mcon)
+    geometry = {
+        name: (rows[0] if len(rows) == 1 else torch.stack(rows)).reshape(
+            (layout.batch_count, layout.cameras, layout.n) + tuple(rows[0].shape[1:]))
+        for name, rows in dense.items()
+    }
+    training = prepare_training_metadata(geometry, layout, packed=packed, absgrad=absgrad)
+    meta = training.values
+    meta.update(width=width, height=height, tile_size=16, tile_width=(width + 15) // 16,
+                tile_height=(height + 15) // 16, n_cameras=layout.cameras, packed=packed,
+                backend="gs3d-b200", with_eval3d=False, supports_means2d_grad=True,
+                screen_gradient_mode="projected_mean", tile_mode=tile_mode)
+    prepared_stats, statistics_outputs = (
+        prepare_statistics(statistics, batch_dims=layout.batch_dims,
+                           batch_count=layout.batch_count, cameras=layout.cameras, n=layout.n,
+                           width=width, height=height, device=layout.device)
+        if statistics else ([], {}))
+    bins = stages.bin_and_sort_many([f[7] for f in frames], width, height)
+    channels = layout.colors.channels
+    images = []
+    for i, (b, c, ctr, con, colors, extras, bg, _state) in enumerate(frames):
+        screen = None if training.screen is None else batch_item(batch_item(training.screen, b), c)
+        total = channels + (0 if extras is None else extras.shape[-1]) + 1
+        packed_bg = ctr.new_zeros(total)
+        if bg is not None:
+            packed_bg[:channels] = bg
+        image = RenderView.apply(ctr, con, colors, extras, screen, packed_bg, bins[i]["ranges"],
+                                 bins[i]["point_list"], config, training.absolute_targets[i],
+                                 prepared_stats[i] if statistics else None, grad_enabled)
+        images.append(image)
+    shape = layout.batch_dims + (layout.cameras, height, width)
+    if len(images) == 1:
+        images = images[0].reshape(shape + (images[0].shape[-1],))
+    else:
+        images = torch.stack(images).reshape(shape + (images[0].shape[-1],))
+    if layout.extras is not None:
+        meta["render_extra_signals"] = images[..., channels:-1]
+    return RasterizationResult(images[..., :channels], images[..., -1:], meta, statistics_outputs)

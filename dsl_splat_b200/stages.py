@@ -1,0 +1,378 @@
+"""Stage wrappers: allocate outputs with Torch and launch one C-ABI call.
+
+These are the swap points of the reference's L2 stage wrappers:
+gs3d/projection.py:309-428 (prepare/backward), splatting/binning.py:171-217
+(bin_and_sort), gs3d/render.py:359-463 (render/backward),
+primitives/spherical_harmonics.py:18-101, splatting/cameras.py:133-221 and
+splatting/metadata.py:34-70.  Everything runs on the caller's current CUDA
+stream; tensors must be CUDA float32/int32.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from . import _native as nv
+from ._native import check, lib, ptr
+
+
+def _stream(t: Tensor) -> int:
+    return nv.stream(t.device)
+
+
+# Optional per-stage CUDA-event timing: when TIMERS is a dict, the wrapped
+# stages record (start, end) event pairs on the launching stream under their
+# name.  bench.py uses this to time the dominant kernel live.
+TIMERS: dict[str, list] | None = None
+
+
+class _timed:
+    __slots__ = ("name", "device", "start")
+
+    def __init__(self, name: str, device: torch.device):
+        self.name, self.device = name, device
+
+    def __enter__(self):
+        if TIMERS is not None:
+            self.start = torch.cuda.Event(enable_timing=True)
+            self.start.record(torch.cuda.current_stream(self.device))
+        return self
+
+    def __exit__(self, *exc):
+        if TIMERS is not None:
+            end = torch.cuda.Event(enable_timing=True)
+            end.record(torch.cuda.current_stream(self.device))
+            TIMERS.setdefault(self.name, []).append((self.start, end))
+        return False
+
+
+def _c(t: Tensor | None) -> Tensor | None:
+    """Contiguous, with a 16-byte-aligned base (the kernels load float2/float4 rows)."""
+    if t is None:
+        return None
+    t = t.contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _far(value: float) -> float:
+    return float(value) if math.isfinite(value) else float("inf")
+
+
+@dataclass(slots=True)
+class ProjectedFootprint:
+    centers: Tensor
+    conics: Tensor
+
+
+@dataclass(slots=True)
+class ProjectedGaussians(ProjectedFootprint):
+    radii: Tensor
+    tile_counts: Tensor
+    depths: Tensor
+
+
+@dataclass(slots=True)
+class RenderedPixels:
+    features: Tensor       # (H, W, C') interleaved, or (C', H, W) planar
+    transmittance: Tensor  # (H, W)
+    contributors: Tensor   # (H, W) int32
+
+
+# ---- cameras ---------------------------------------------------------------
+
+def cameras_prepare(views: Tensor, Ks: Tensor, width: int, height: int, with_centers: bool):
+    """splatting/cameras.py:133-188: full (…,4,4), inverse (C,4,4), centers (…,3)."""
+    views_c, Ks_c = views.reshape(-1, 4, 4).contiguous(), Ks.reshape(-1, 3, 3).contiguous()
+    count = len(views_c)
+    full = torch.empty(views.shape, dtype=torch.float32, device=views.device)
+    inverse = views.new_empty((count if with_centers else 0, 4, 4))
+    centers = views.new_empty(views.shape[:-2] + (3,) if with_centers else (0, 3))
+    errors = torch.empty(count, dtype=torch.int32, device=views.device)
+    check(lib.splat_cameras_prepare(count, ptr(views_c), ptr(Ks_c), width, height, int(with_centers),
+                                    ptr(full), ptr(inverse) if with_centers else None,
+                                    ptr(centers) if with_centers else None, ptr(errors),
+                                    _stream(views)), "cameras_prepare")
+    # Only status codes cross to the host, as in the reference.
+    codes = errors.tolist()
+    if 2 in codes:
+        raise ValueError("Ks must be finite with positive fx/fy")
+    if 1 in codes:
+        raise NotImplementedError("Ks must be a zero-skew pinhole intrinsic matrix")
+    if 3 in codes:
+        raise torch.linalg.LinAlgError("viewmats must be invertible for SH directions")
+    return full, inverse, centers
+
+
+def cameras_backward(Ks: Tensor, grad_full: Tensor | None, width: int, height: int,
+                     inverse: Tensor, grad_centers: Tensor | None, views_shape) -> Tensor:
+    Ks_c = Ks.reshape(-1, 3, 3).contiguous()
+    count = len(Ks_c)
+    grad_views = torch.empty(views_shape, dtype=torch.float32, device=Ks.device)
+    gf = None if grad_full is None else grad_full.reshape(-1, 4, 4).contiguous()
+    gc = None if grad_centers is None else grad_centers.reshape(-1, 3).contiguous()
+    check(lib.splat_cameras_backward(count, ptr(Ks_c), ptr(gf), width, height,
+                                     ptr(inverse) if gc is not None else None, ptr(gc),
+                                     ptr(grad_views), _stream(Ks)), "cameras_backward")
+    return grad_views
+
+
+# ---- projection --------------------------------------------------------------
+
+def project(means, quats, scales, opacities, view, projection, intrinsics, width, height,
+            near, far, radius_clip) -> ProjectedGaussians:
+    """gs3d/projection.py:309-354 prepare."""
+    n = len(means)
+    state = ProjectedGaussians(means.new_empty((n, 2)), means.new_empty((n, 4)),
+                               torch.empty(n, dtype=torch.int32, device=means.device),
+                               torch.empty(n, dtype=torch.int32, device=means.device),
+                               means.new_empty(n))
+    if n:
+        check(lib.splat_project_forward(
+            n, ptr(_c(means)), ptr(_c(quats)), ptr(_c(scales)), ptr(_c(opacities)),
+            ptr(_c(view)), ptr(_c(projection)), ptr(_c(intrinsics)), width, height, float(near),
+            _far(far), float(radius_clip), ptr(state.centers), ptr(state.conics),
+            ptr(state.radii), ptr(state.tile_counts), ptr(state.depths), _stream(means)),
+            "project_forward")
+    return state
+
+
+@dataclass(slots=True)
+class FusedProjection:
+    state: ProjectedGaussians
+    colors: Tensor | None      # (n,3) SH colours
+    active: Tensor | None      # (n,3) uint8
+    means2d: Tensor
+    opacities: Tensor
+    conics3: Tensor
+
+
+def project_fused(means, quats, scales, opacities, view, projection, intrinsics, width, height,
+                  near, far, radius_clip, sh: Tensor | None = None, sh_degree: int = 0,
+                  campos: Tensor | None = None, need_active: bool = True) -> FusedProjection:
+    """One launch for gs3d/api.py:145-189: projection, masked SH and metadata."""
+    n = len(means)
+    dev = means.device
+    state = ProjectedGaussians(means.new_empty((n, 2)), means.new_empty((n, 4)),
+                               torch.empty(n, dtype=torch.int32, device=dev),
+                               torch.empty(n, dtype=torch.int32, device=dev), means.new_empty(n))
+    colors = means.new_empty((n, 3)) if sh is not None else None
+    active = (torch.empty((n, 3), dtype=torch.uint8, device=dev)
+              if sh is not None and need_active else None)
+    m2d, mop, mcon = means.new_empty((n, 2)), means.new_empty(n), means.new_empty((n, 3))
+    if n:
+        sh_c = _c(sh)
+        check(lib.splat_project_forward_fused(
+            n, ptr(_c(means)), ptr(_c(quats)), ptr(_c(scales)), ptr(_c(opacities)),
+            ptr(_c(view)), ptr(_c(projection)), ptr(_c(intrinsics)), width, height, float(near),
+            _far(far), float(radius_clip), ptr(state.centers), ptr(state.conics),
+            ptr(state.radii), ptr(state.tile_counts), ptr(state.depths), int(sh_degree),
+            sh_c.shape[1] if sh_c is not None else 0, ptr(sh_c), ptr(_c(campos)), ptr(colors), 3,
+            ptr(active), ptr(m2d), ptr(mop), ptr(mcon), _stream(means)), "project_forward_fused")
+    return FusedProjection(state, colors, active, m2d, mop, mcon)
+
+
+def metadata(state: ProjectedGaussians) -> dict[str, Tensor]:
+    """splatting/metadata.py:34-70 prepare_metadata."""
+    n = len(state.radii)
+    means2d = torch.empty_like(state.centers)
+    opacities = state.conics.new_empty((n,))
+    conics = state.conics.new_empty((n, 3))
+    if n:
+        check(lib.splat_metadata(n, ptr(state.radii), ptr(state.centers), ptr(state.conics),
+                                 ptr(means2d), ptr(opacities), ptr(conics),
+                                 _stream(state.radii)), "metadata")
+    return dict(radii=state.radii[:, None].expand(-1, 2), means2d=means2d, opacities=opacities,
+                tiles_per_gauss=state.tile_counts, conics=conics)
+
+
+def project_backward(means, quats, scales, opacities, view, projection, intrinsics, width,
+                     height, state: ProjectedGaussians, grad_centers, grad_conics,
+                     needs: tuple[bool, ...]):
+    """gs3d/projection.py:357-428: [means, quats, scales, opacities, view, proj] grads."""
+    if not any(needs):
+        return [None] * 6
+    tensors = [means, quats, scales, opacities]
+    grads = [torch.empty_like(t) if need else None for t, need in zip(tensors, needs[:4])]
+    n = len(means)
+    cam = means.new_zeros(32) if any(needs[4:]) else None
+    if n:
+        check(lib.splat_project_backward(
+            n, ptr(_c(means)), ptr(_c(quats)), ptr(_c(scales)), ptr(_c(view)),
+            ptr(_c(projection)), ptr(_c(intrinsics)), width, height, ptr(state.radii),
+            ptr(_c(grad_centers)), ptr(_c(grad_conics)), *[ptr(g) for g in grads], ptr(cam),
+            _stream(means)), "project_backward")
+    out = grads + [None, None]
+    if needs[4]:
+        out[4] = cam[:16].reshape(4, 4) if n else torch.zeros_like(view)
+    if needs[5]:
+        out[5] = cam[16:32].reshape(4, 4) if n else torch.zeros_like(projection)
+    return out
+
+
+# ---- spherical harmonics -----------------------------------------------------
+
+def sh_forward(coeffs: Tensor, dirs: Tensor, degree: int, radii: Tensor | None, save: bool):
+    n = len(coeffs)
+    coeffs, dirs = coeffs.contiguous(), dirs.contiguous()
+    colors = coeffs.new_empty((n, 3))
+    active = torch.empty((n if save else 0, 3), dtype=torch.uint8, device=coeffs.device)
+    if n:
+        check(lib.splat_sh_forward(n, degree, coeffs.shape[1], ptr(coeffs), ptr(dirs),
+                                   ptr(_c(radii)), ptr(colors), ptr(active) if save else None,
+                                   _stream(coeffs)), "sh_forward")
+    return colors, active
+
+
+def sh_backward(coeffs, dirs, degree, radii, active, upstream, need_dirs: bool):
+    n = len(coeffs)
+    coeffs, dirs = coeffs.contiguous(), dirs.contiguous()
+    grad_coeffs = torch.empty_like(coeffs)
+    grad_dirs = dirs.new_empty((n, 3)) if need_dirs else None
+    if radii is None:
+        radii_p = None
+    else:
+        radii_p = ptr(radii.contiguous())
+    if n:
+        check(lib.splat_sh_backward(n, degree, coeffs.shape[1], ptr(coeffs), ptr(dirs), radii_p,
+                                    ptr(active.contiguous()), ptr(upstream.contiguous()),
+                                    ptr(grad_coeffs), ptr(grad_dirs), _stream(coeffs)),
+              "sh_backward")
+    return grad_coeffs, grad_dirs
+
+
+# ---- scan / binning ----------------------------------------------------------
+
+def scan_counts(counts: Tensor) -> tuple[Tensor, int]:
+    """primitives/tiling.py:57-64: inclusive int32 offsets and the total."""
+    n = len(counts)
+    offsets = torch.empty(n, dtype=torch.int32, device=counts.device)
+    if not n:
+        return offsets, 0
+    ws = torch.empty(lib.splat_scan_workspace_bytes(n), dtype=torch.uint8, device=counts.device)
+    total = torch.zeros(1, dtype=torch.int64, device=counts.device)
+    check(lib.splat_scan_counts(n, ptr(counts.contiguous()), ptr(offsets), ptr(total), ptr(ws),
+                                ws.numel(), _stream(counts)), "scan_counts")
+    return offsets, int(total.item())
+
+
+class BinPlan:
+    """Phase 1 of binning for one view (depth sort, offsets, ranges, count)."""
+
+    def __init__(self, state: ProjectedGaussians, width: int, height: int):
+        dev = state.radii.device
+        n = len(state.radii)
+        self.n, self.width, self.height = n, width, height
+        gx, gy = (width + 15) // 16, (height + 15) // 16
+        self.ranges = torch.empty((gx * gy, 2), dtype=torch.int32, device=dev)
+        self.pairs_dev = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.workspace = torch.empty(lib.splat_bin_workspace_bytes(n, width, height),
+                                     dtype=torch.uint8, device=dev)
+        check(lib.splat_bin_prepare(
+            n, ptr(state.centers), ptr(state.radii), ptr(state.tile_counts), ptr(state.depths),
+            width, height, ptr(self.workspace), self.workspace.numel(), ptr(self.ranges),
+            ptr(self.pairs_dev), nv.stream(dev)), "bin_prepare")
+
+    def emit(self, pairs: int) -> Tensor:
+        dev = self.ranges.device
+        ids = torch.empty(pairs, dtype=torch.int32, device=dev)
+        if pairs:
+            pws = torch.empty(lib.splat_bin_pairs_workspace_bytes(pairs, self.width, self.height),
+                              dtype=torch.uint8, device=dev)
+            check(lib.splat_bin_emit(self.n, pairs, self.width, self.height, ptr(self.workspace),
+                                     self.workspace.numel(), ptr(pws), pws.numel(), ptr(ids),
+                                     nv.stream(dev)), "bin_emit")
+        self.workspace = None
+        return ids
+
+
+def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int):
+    """Bin several views with one host read of all pair counts."""
+    plans = [BinPlan(s, width, height) for s in states]
+    if not plans:
+        return []
+    counts = torch.cat([p.pairs_dev for p in plans]).tolist()
+    return [dict(point_list=p.emit(int(m)), ranges=p.ranges) for p, m in zip(plans, counts)]
+
+
+def bin_and_sort(state: ProjectedGaussians, width: int, height: int) -> dict[str, Tensor]:
+    """splatting/binning.py:171-217 (tile_mode "radius"): point_list and ranges."""
+    return bin_and_sort_many([state], width, height)[0]
+
+
+# ---- blending ----------------------------------------------------------------
+
+def _features(feat_a: Tensor, feat_b: Tensor | None):
+    a = feat_a.contiguous()
+    b = None if feat_b is None else feat_b.contiguous()
+    return a, b, a.shape[1], (0 if b is None else b.shape[1])
+
+
+def render(state: ProjectedFootprint, bins: dict, feat_a: Tensor, feat_b: Tensor | None,
+           append_one: bool, background: Tensor, width: int, height: int,
+           planar: bool = False, statistics=None) -> RenderedPixels:
+    """gs3d/render.py:359-406.  Channels: feat_a, feat_b, then a constant 1.
+
+    statistics: a PreparedStatistics (statistics.py) whose counts/sums rows
+    receive this view's accepted contributions."""
+    a, b, ca, cb = _features(feat_a, feat_b)
+    channels = ca + cb + int(append_one)
+    dev = a.device
+    if planar:
+        image = a.new_empty((channels, height, width))
+        pix_stride, ch_stride = 1, height * width
+    else:
+        image = a.new_empty((height, width, channels))
+        pix_stride, ch_stride = channels, 1
+    out = RenderedPixels(image, a.new_empty((height, width)),
+                         torch.empty((height, width), dtype=torch.int32, device=dev))
+    if statistics is None:
+        stat = (0, 0, None, None, None)
+    else:
+        mask = sum(1 << r for r, kind in enumerate(statistics.key) if kind == 1)
+        stat = (len(statistics.key), mask, ptr(statistics.pixel_values),
+                ptr(statistics.counts), ptr(statistics.sums))
+    with _timed("render_forward", dev):
+        check(lib.splat_render_forward_statistics(
+            width, height, ptr(bins["ranges"]), ptr(bins["point_list"]), len(bins["point_list"]),
+            len(state.centers), ptr(_c(state.centers)),
+            ptr(_c(state.conics)), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
+            ptr(background.contiguous()), ptr(image), pix_stride, ch_stride,
+            ptr(out.transmittance), ptr(out.contributors), *stat, nv.stream(dev)), "render_forward")
+    return out
+
+
+def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
+                    feat_b: Tensor | None, append_one: bool, background: Tensor,
+                    final_t: Tensor, contributors: Tensor, gradient: Tensor, width: int,
+                    height: int, *, planar: bool = False, absgrad: bool = False,
+                    constant_tail: int = 0, need_a: bool = True, need_b: bool = True):
+    """gs3d/render.py:409-463: grads of centers, conics, feat_a, feat_b, abs."""
+    a, b, ca, cb = _features(feat_a, feat_b)
+    channels = ca + cb + int(append_one)
+    if not 0 <= constant_tail <= channels:
+        raise ValueError("constant_tail must be within the feature channel count")
+    g = gradient.contiguous()
+    if planar:
+        pix_stride, ch_stride = 1, height * width
+    else:
+        pix_stride, ch_stride = channels, 1
+    centers = torch.zeros_like(state.centers)
+    conics = torch.zeros_like(state.conics)
+    ga = torch.zeros_like(a) if need_a else None
+    gb = torch.zeros_like(b) if (b is not None and need_b) else None
+    absolute = torch.zeros_like(state.centers) if absgrad else None
+    with _timed("render_backward", a.device):
+        check(lib.splat_render_backward(
+            width, height, ptr(bins["ranges"]), ptr(bins["point_list"]), len(bins["point_list"]),
+            len(state.centers), ptr(_c(state.centers)),
+            ptr(_c(state.conics)), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
+            ptr(background.contiguous()), ptr(final_t.contiguous()), ptr(contributors.contiguous()),
+            ptr(g), pix_stride, ch_stride, ptr(centers), ptr(conics), ptr(ga), ptr(gb),
+            ptr(absolute), constant_tail, nv.stream(a.device)), "render_backward")
+    return centers, conics, ga, gb, absolute

@@ -1,0 +1,70 @@
+"""Per-view densification metadata and auxiliary gradient targets
+(dsl_splat/training.py:1-76, runtime/gradients.py:1-16)."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+from torch import Tensor
+
+from .inputs import Inputs
+
+
+@dataclass(slots=True)
+class AbsGradientTarget:
+    """Destination of one view's |d means2d| sums (runtime/gradients.py:8-16)."""
+
+    target: Tensor
+    gaussian_ids: Tensor | None = None
+
+    @torch.no_grad()
+    def write(self, gradient: Tensor) -> None:
+        value = gradient if self.gaussian_ids is None else gradient[self.gaussian_ids]
+        self.target.copy_(value)
+
+
+@dataclass(slots=True)
+class TrainingMetadata:
+    values: dict[str, Any]
+    screen: Tensor | None
+    absolute_targets: list[AbsGradientTarget | None]
+
+
+def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packed: bool,
+                              absgrad: bool) -> TrainingMetadata:
+    """training.py:24-76: dense or packed metadata, the means2d leaf and absgrad."""
+    if packed:
+        batch_ids, camera_ids, gaussian_ids = (dense["radii"] > 0).all(-1).nonzero(as_tuple=True)
+        values = {name: v[batch_ids, camera_ids, gaussian_ids] for name, v in dense.items()}
+    else:
+        batch_ids = camera_ids = gaussian_ids = None
+        values = {name: v.reshape(layout.batch_dims + tuple(v.shape[1:]))
+                  for name, v in dense.items()}
+    values.update(batch_ids=batch_ids, camera_ids=camera_ids, gaussian_ids=gaussian_ids)
+    screen = values["means2d"].detach().requires_grad_(layout.requires_screen_grad)
+    values["means2d"] = screen
+    targets: list[AbsGradientTarget | None] = [None] * (layout.batch_count * layout.cameras)
+    if not layout.requires_screen_grad:
+        return TrainingMetadata(values, None, targets)
+    if packed:
+        dense_screen = torch.zeros_like(dense["means2d"]).index_put(
+            (batch_ids, camera_ids, gaussian_ids), screen)
+    else:
+        dense_screen = screen.reshape(layout.batch_count, layout.cameras, layout.n, 2)
+    if absgrad:
+        absolute = torch.zeros_like(screen)
+        setattr(screen, "absgrad", absolute)
+        if packed:
+            counts = ([len(screen)] if len(targets) == 1
+                      else (dense["radii"] > 0).all(-1).sum(-1).flatten().tolist())
+            begin = 0
+            for i, count in enumerate(counts):
+                end = begin + count
+                targets[i] = AbsGradientTarget(absolute[begin:end], gaussian_ids[begin:end])
+                begin = end
+        else:
+            views = absolute.reshape(layout.batch_count * layout.cameras, layout.n, 2)
+            targets = [AbsGradientTarget(v) for v in views]
+    return TrainingMetadata(values, dense_screen, targets)

@@ -1,0 +1,194 @@
+/* splat200.h -- C ABI of libsplat200, the sm_100a gs3d rasteriser.
+ *
+ * Every function takes device pointers (float32 / int32, row-major, C
+ * contiguous unless a stride argument says otherwise), plain sizes and a
+ * cudaStream_t passed as void*, enqueues its kernels on that stream and
+ * returns 0 on success or a negative status:
+ *   -1 invalid argument, -2 CUDA error, -3 a bounded device wait gave up,
+ *   -4 problem too large, -5 workspace too small.
+ * splat_last_error() describes the calling thread's latest failure.  No
+ * entry point allocates device memory; binning takes caller workspaces sized
+ * by the *_workspace_bytes queries.
+ *
+ * Each entry point names the dsl_splat function whose Warp launch it
+ * replaces (paths inside the dsl_splat project).
+ */
+#ifndef SPLAT200_H
+#define SPLAT200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+int splat_abi_version(void);
+const char* splat_last_error(void);
+
+/* Number of CUDA kernels this library has launched in the process so far. */
+unsigned long long splat_launch_count(void);
+
+/* Reads and clears the device error word set by bounded waits (synchronises
+ * the stream).  *code is 0 when no wait expired. */
+int splat_device_error(int* code, void* stream);
+
+/* splatting/cameras.py:133-188 _PrepareCameras.forward -> camera_kernels.py:11-66.
+ * views (C,4,4), Ks (C,3,3) -> full (C,4,4), inverse/centers when
+ * with_centers (C,4,4)/(C,3), errors (C) with the reference's codes
+ * 1 (skewed K), 2 (non-finite or non-positive focal), 3 (singular view). */
+int splat_cameras_prepare(int count, const float* views, const float* Ks, int width, int height,
+                          int with_centers, float* full, float* inverse, float* centers,
+                          int* errors, void* stream);
+
+/* splatting/cameras.py:190-221 _PrepareCameras.backward -> camera_kernels.py:69-106.
+ * grad_full (C,4,4) or NULL, grad_centers (C,3) or NULL -> grad_views (C,4,4). */
+int splat_cameras_backward(int count, const float* Ks, const float* grad_full, int width,
+                           int height, const float* inverse, const float* grad_centers,
+                           float* grad_views, void* stream);
+
+/* gs3d/projection.py:309-354 prepare -> project kernel :89-164 (tile_mode "radius").
+ * Outputs centers (n,2), conics (n,4), radii (n), tiles (n), depths (n);
+ * rows with radii == 0 leave centers/conics/depths unwritten, as the
+ * reference does. */
+int splat_project_forward(int n, const float* means, const float* quats, const float* scales,
+                          const float* opacities, const float* view, const float* proj,
+                          const float* K, int width, int height, float near_plane,
+                          float far_plane, float radius_clip, float* centers, float* conics,
+                          int* radii, int* tiles, float* depths, void* stream);
+
+/* gs3d/api.py:145-189 per-view preparation in one launch: the projection above,
+ * the masked SH evaluation of primitives/spherical_harmonics.py:18-59
+ * (sh.py:44-79; directions means - campos, campos NULL for SH0) writing
+ * colors[i*color_stride + 0..2] and active (n,3), and the dense metadata of
+ * splatting/metadata.py:34-70 (means2d (n,2), opacities (n), conics (n,3)).
+ * sh == NULL skips SH; meta_means2d == NULL skips metadata. */
+int splat_project_forward_fused(int n, const float* means, const float* quats,
+                                const float* scales, const float* opacities, const float* view,
+                                const float* proj, const float* K, int width, int height,
+                                float near_plane, float far_plane, float radius_clip,
+                                float* centers, float* conics, int* radii, int* tiles,
+                                float* depths, int sh_degree, int sh_k, const float* sh,
+                                const float* campos, float* colors, int color_stride,
+                                unsigned char* active, float* meta_means2d,
+                                float* meta_opacities, float* meta_conics, void* stream);
+
+/* splatting/metadata.py:34-70 prepare_metadata -> _prepare :12-31. */
+int splat_metadata(int n, const int* radii, const float* centers, const float* conics,
+                   float* means2d, float* opacities, float* conics3, void* stream);
+
+/* gs3d/projection.py:357-428 backward -> project_backward :213-285.
+ * Writes dense grads (culled rows zero; any output may be NULL).
+ * camera_grads: NULL or float[32] (view 4x4 then projection 4x4) that the
+ * call ADDS into (zero it first). */
+int splat_project_backward(int n, const float* means, const float* quats, const float* scales,
+                           const float* view, const float* proj, const float* K, int width,
+                           int height, const int* radii, const float* grad_centers,
+                           const float* grad_conics, float* grad_means, float* grad_quats,
+                           float* grad_scales, float* grad_opacities, float* camera_grads,
+                           void* stream);
+
+/* The projection backward above fused with the SH backward of
+ * primitives/spherical_harmonics.py:61-101 (sh.py:82-138): grad_colors rows
+ * (stride color_stride) give dL/dcolors, the direction gradient is added to
+ * grad_means and, negated, to camera_grads[32..34] (d campos).  accumulate
+ * != 0 adds into all per-Gaussian outputs (multi-view sums); camera_grads is
+ * NULL or float[35] (view 16, proj 16, campos 3), always added into. */
+int splat_project_backward_fused(int n, const float* means, const float* quats,
+                                 const float* scales, const float* view, const float* proj,
+                                 const float* K, int width, int height, const int* radii,
+                                 const float* grad_centers, const float* grad_conics,
+                                 float* grad_means, float* grad_quats, float* grad_scales,
+                                 float* grad_opacities, int accumulate, float* camera_grads,
+                                 int sh_degree, int sh_k, const float* sh, const float* campos,
+                                 const unsigned char* active, const float* grad_colors,
+                                 int color_stride, float* grad_sh, void* stream);
+
+/* primitives/spherical_harmonics.py:18-59 _SphericalHarmonics.forward -> sh.py:44-79.
+ * sh (n,sh_k,3), dirs (n,3), radii (n) or NULL -> colors (n,3), active (n,3) or NULL. */
+int splat_sh_forward(int n, int degree, int sh_k, const float* sh, const float* dirs,
+                     const int* radii, float* colors, unsigned char* active, void* stream);
+
+/* primitives/spherical_harmonics.py:61-101 backward -> sh.py:82-138.
+ * grad_sh (n,sh_k,3) fully written; grad_dirs (n,3) or NULL. */
+int splat_sh_backward(int n, int degree, int sh_k, const float* sh, const float* dirs,
+                      const int* radii, const unsigned char* active, const float* upstream,
+                      float* grad_sh, float* grad_dirs, void* stream);
+
+/* primitives/tiling.py:57-64 scan_counts: inclusive int32 offsets of counts
+ * (n); *total (device int64) receives the sum. */
+size_t splat_scan_workspace_bytes(int n);
+int splat_scan_counts(int n, const int* counts, int* offsets, long long* total, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* splatting/binning.py:171-217 bin_and_sort (tile_mode "radius"), split in
+ * two calls around the one host read of the pair count that the reference
+ * also makes (primitives/tiling.py:64):
+ *   splat_bin_prepare: depth-key sort, pair offsets, per-tile ranges (T,2)
+ *     (zeros for empty tiles, as identify_ranges leaves them) and the pair
+ *     count M into *pairs (device int64).
+ *   splat_bin_emit: generates and sorts the M (tile, Gaussian) pairs into
+ *     ids (M) -- the reference's point_list: per tile, Gaussians ordered by
+ *     (float bits of depth, index), identical to the stable 64-bit key sort
+ *     of primitives/tiling.py:80-86.
+ * The workspace passed to prepare must be passed unchanged to emit. */
+size_t splat_bin_workspace_bytes(int n, int width, int height);
+size_t splat_bin_pairs_workspace_bytes(long long pairs, int width, int height);
+int splat_bin_prepare(int n, const float* centers, const int* radii, const int* tiles,
+                      const float* depths, int width, int height, void* workspace,
+                      size_t workspace_bytes, int* ranges, long long* pairs, void* stream);
+int splat_bin_emit(int n, long long pairs, int width, int height, void* workspace,
+                   size_t workspace_bytes, void* pairs_workspace, size_t pairs_workspace_bytes,
+                   int* ids, void* stream);
+
+/* gs3d/render.py:359-406 render -> evaluate :41-125.  Blended channels are
+ * feat_a's ch_a columns (row stride stride_a), then feat_b's ch_b columns,
+ * then (append_one) a constant 1 -- the reference's cat([features, extras,
+ * ones]) of gs3d/autograd.py:306-311 without materialising it.
+ * background (channels).  image[pixel*pix_stride + c*ch_stride]; planar
+ * (C,H,W) is pix_stride=1, ch_stride=H*W; interleaved (H,W,C) is
+ * pix_stride=C, ch_stride=1.  ids holds num_ids entries (tile ranges are
+ * clamped to it) of Gaussian indices in [0, n).  At most 32 channels. */
+int splat_render_forward(int width, int height, const int* ranges, const int* ids,
+                         long long num_ids, int n, const float* centers, const float* conics,
+                         const float* feat_a, int ch_a, int stride_a, const float* feat_b,
+                         int ch_b, int stride_b, int append_one, const float* background,
+                         float* image, int pix_stride, int ch_stride, float* final_t,
+                         int* contributors, void* stream);
+
+/* gs3d/render.py:129-169 render with contribution statistics (statistics.py:
+ * 47-73, 393-418): as splat_render_forward, plus stat_count requests whose
+ * (stat_count, H*W) pixel maps are stat_pixels; request r is a weighted sum
+ * when bit r of stat_sum_mask is set, else a masked count.  Each accepted
+ * sample of Gaussian g with weight w = alpha*T at a pixel whose map value v
+ * is nonzero adds 1 to stat_counts[row*n + g] or v*w to stat_sums[row*n + g]
+ * (row = index among requests of its kind). */
+int splat_render_forward_statistics(
+    int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
+    const float* centers, const float* conics, const float* feat_a, int ch_a, int stride_a,
+    const float* feat_b, int ch_b, int stride_b, int append_one, const float* background,
+    float* image, int pix_stride, int ch_stride, float* final_t, int* contributors,
+    int stat_count, int stat_sum_mask, const float* stat_pixels, int* stat_counts,
+    float* stat_sums, void* stream);
+
+/* gs3d/render.py:409-463 backward -> :221-354.  Gradients are ADDED into
+ * grad_centers (n,2), grad_conics (n,4), grad_a (n,ch_a), grad_b (n,ch_b)
+ * and abs_centers (n,2) (NULL to skip a, b or abs); the last constant_tail
+ * channels receive no feature gradient. */
+int splat_render_backward(int width, int height, const int* ranges, const int* ids,
+                          long long num_ids, int n, const float* centers, const float* conics,
+                          const float* feat_a,
+                          int ch_a, int stride_a, const float* feat_b, int ch_b, int stride_b,
+                          int append_one, const float* background, const float* final_t,
+                          const int* contributors, const float* upstream, int up_pix_stride,
+                          int up_ch_stride, float* grad_centers, float* grad_conics,
+                          float* grad_a, float* grad_b, float* abs_centers, int constant_tail,
+                          void* stream);
+
+/* Diagnostic: ours[i] = the blend's exp, cuda_exp[i] = CUDA expf, for x (n). */
+int splat_debug_expf(int n, const float* x, float* ours, float* cuda_exp, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPLAT200_H */

@@ -1,0 +1,328 @@
+"""ctypes bindings for the CPU oracle (test infrastructure only).
+
+The oracle restates dsl_splat's gs3d rasteriser on the CPU (see
+splat_oracle.cpp for the per-function reference citations).  Tests,
+``__graft_entry__.smoke()`` and bench.py's CPU legs use it as the checker and
+the CPU baseline; the product package never imports it.
+
+Every function takes and returns numpy arrays (float32 / int32, C order).
+Gradient accumulators come back as float64.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "libsplat_oracle.so")
+_lib = None
+
+_f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(dtype=np.int32, flags="C_CONTIGUOUS")
+_u64p = np.ctypeslib.ndpointer(dtype=np.uint64, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
+_vp = ctypes.c_void_p
+_int = ctypes.c_int
+_flt = ctypes.c_float
+
+
+def build() -> None:
+    """Compile the oracle library in place (make, with FP contraction off)."""
+    import subprocess
+
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.oracle_expf.argtypes = [_flt]
+        L.oracle_expf.restype = _flt
+        L.oracle_cameras_prepare.argtypes = [_int, _f32p, _f32p, _int, _int, _int, _vp, _vp, _vp, _i32p]
+        L.oracle_cameras_prepare.restype = _int
+        L.oracle_cameras_backward.argtypes = [_int, _f32p, _vp, _int, _int, _vp, _vp, _f32p]
+        L.oracle_cameras_backward.restype = None
+        L.oracle_project_forward.argtypes = [
+            _int, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _int, _int,
+            _flt, _flt, _flt, _f32p, _f32p, _i32p, _i32p, _f32p]
+        L.oracle_project_forward.restype = None
+        L.oracle_sh_forward.argtypes = [_int, _int, _int, _f32p, _f32p, _vp, _f32p, _vp]
+        L.oracle_sh_forward.restype = None
+        L.oracle_sh_backward.argtypes = [_int, _int, _int, _f32p, _f32p, _vp, _u8p, _f32p, _f32p, _vp]
+        L.oracle_sh_backward.restype = None
+        L.oracle_scan_counts.argtypes = [_int, _i32p, _i32p]
+        L.oracle_scan_counts.restype = ctypes.c_longlong
+        L.oracle_bin_and_sort.argtypes = [_int, _f32p, _i32p, _f32p, _i32p, _int, _int, _u64p, _i32p, _i32p]
+        L.oracle_bin_and_sort.restype = None
+        L.oracle_render_forward.argtypes = [
+            _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i32p]
+        L.oracle_render_forward.restype = None
+        L.oracle_render_backward.argtypes = [
+            _int, _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i32p,
+            _f32p, _f64p, _f64p, _f64p, _vp]
+        L.oracle_render_backward.restype = None
+        L.oracle_project_backward.argtypes = [
+            _int, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _int, _int, _i32p, _f32p,
+            _f32p, _f32p, _f32p, _f32p, _f32p, _vp, _vp]
+        L.oracle_project_backward.restype = None
+        L.oracle_num_threads.restype = _int
+        L.oracle_set_num_threads.argtypes = [_int]
+        _lib = L
+    return _lib
+
+
+def _c(a, dtype=np.float32):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def set_threads(n: int) -> None:
+    lib().oracle_set_num_threads(int(n))
+
+
+def num_threads() -> int:
+    return int(lib().oracle_num_threads())
+
+
+def expf(x: np.ndarray) -> np.ndarray:
+    f = lib().oracle_expf
+    x = _c(x).ravel()
+    return np.array([f(float(v)) for v in x], dtype=np.float32)
+
+
+def cameras_prepare(views, Ks, width, height, with_centers):
+    views, Ks = _c(views).reshape(-1, 16), _c(Ks).reshape(-1, 9)
+    n = len(views)
+    full = np.zeros((n, 16), np.float32)
+    inverse = np.zeros((n, 16), np.float32)
+    centers = np.zeros((n, 3), np.float32)
+    errors = np.zeros(n, np.int32)
+    lib().oracle_cameras_prepare(n, views, Ks, width, height, int(with_centers),
+                                 _ptr(full), _ptr(inverse), _ptr(centers), errors)
+    return full.reshape(n, 4, 4), inverse.reshape(n, 4, 4), centers, errors
+
+
+def cameras_backward(Ks, grad_full, width, height, inverse, grad_centers):
+    Ks = _c(Ks).reshape(-1, 9)
+    n = len(Ks)
+    gf = None if grad_full is None else _c(grad_full).reshape(n, 16)
+    inv = None if inverse is None else _c(inverse).reshape(n, 16)
+    gc = None if grad_centers is None else _c(grad_centers).reshape(n, 3)
+    out = np.zeros((n, 16), np.float32)
+    lib().oracle_cameras_backward(n, Ks, _ptr(gf), width, height, _ptr(inv), _ptr(gc), out)
+    return out.reshape(n, 4, 4)
+
+
+@dataclass
+class Projected:
+    centers: np.ndarray
+    conics: np.ndarray
+    radii: np.ndarray
+    tiles: np.ndarray
+    depths: np.ndarray
+
+
+def project_forward(means, quats, scales, opacities, view, proj, K, width, height,
+                    near=0.2, far=float("inf"), radius_clip=0.0) -> Projected:
+    n = len(means)
+    out = Projected(np.zeros((n, 2), np.float32), np.zeros((n, 4), np.float32),
+                    np.zeros(n, np.int32), np.zeros(n, np.int32), np.zeros(n, np.float32))
+    lib().oracle_project_forward(
+        n, _c(means), _c(quats), _c(scales), _c(opacities), _c(view).reshape(16),
+        _c(proj).reshape(16), _c(K).reshape(9), width, height, near, far, radius_clip,
+        out.centers, out.conics, out.radii, out.tiles, out.depths)
+    return out
+
+
+def sh_forward(coeffs, dirs, degree, radii=None):
+    coeffs = _c(coeffs)
+    n, K = coeffs.shape[0], coeffs.shape[1]
+    colors = np.zeros((n, 3), np.float32)
+    active = np.zeros((n, 3), np.uint8)
+    r = None if radii is None else _c(radii, np.int32)
+    lib().oracle_sh_forward(n, degree, K, coeffs, _c(dirs), _ptr(r), colors, _ptr(active))
+    return colors, active
+
+
+def sh_backward(coeffs, dirs, degree, radii, active, upstream, need_dirs=True):
+    coeffs = _c(coeffs)
+    n, K = coeffs.shape[0], coeffs.shape[1]
+    gcoef = np.zeros_like(coeffs)
+    gdir = np.zeros((n, 3), np.float32) if need_dirs else None
+    r = None if radii is None else _c(radii, np.int32)
+    lib().oracle_sh_backward(n, degree, K, coeffs, _c(dirs), _ptr(r), _c(active, np.uint8),
+                             _c(upstream), gcoef, _ptr(gdir))
+    return gcoef, gdir
+
+
+def scan_counts(counts):
+    counts = _c(counts, np.int32)
+    offsets = np.zeros(len(counts), np.int32)
+    m = lib().oracle_scan_counts(len(counts), counts, offsets)
+    return offsets, int(m)
+
+
+def bin_and_sort(centers, radii, depths, offsets, width, height):
+    n = len(radii)
+    m = int(offsets[-1]) if n else 0
+    gx, gy = (width + 15) // 16, (height + 15) // 16
+    keys = np.zeros(m, np.uint64)
+    ids = np.zeros(m, np.int32)
+    ranges = np.zeros((gx * gy, 2), np.int32)
+    lib().oracle_bin_and_sort(n, _c(centers), _c(radii, np.int32), _c(depths),
+                              _c(offsets, np.int32), width, height, keys, ids, ranges)
+    return keys, ids, ranges
+
+
+def render_forward(width, height, ranges, ids, centers, conics, features, background):
+    features = _c(features)
+    c = features.shape[1]
+    image = np.zeros((c, height, width), np.float32)
+    final_t = np.zeros((height, width), np.float32)
+    contrib = np.zeros((height, width), np.int32)
+    lib().oracle_render_forward(width, height, c, _c(ranges, np.int32), _c(ids, np.int32),
+                                _c(centers), _c(conics), features, _c(background), image,
+                                final_t, contrib)
+    return image, final_t, contrib
+
+
+def render_backward(width, height, ranges, ids, centers, conics, features, background,
+                    final_t, contributors, upstream, absgrad=False, constant_tail=0):
+    """upstream: planar (C,H,W).  Returns float64 accumulators."""
+    features = _c(features)
+    n, c = features.shape
+    gc = np.zeros((n, 2), np.float64)
+    gq = np.zeros((n, 4), np.float64)
+    gf = np.zeros((n, c), np.float64)
+    ga = np.zeros((n, 2), np.float64) if absgrad else None
+    lib().oracle_render_backward(width, height, c, constant_tail, _c(ranges, np.int32),
+                                 _c(ids, np.int32), _c(centers), _c(conics), features,
+                                 _c(background), _c(final_t), _c(contributors, np.int32),
+                                 _c(upstream), gc, gq, gf, _ptr(ga))
+    return gc, gq, gf, ga
+
+
+def project_backward(means, quats, scales, opacities, view, proj, K, width, height, radii,
+                     seed_centers, seed_conics):
+    n = len(means)
+    gm = np.zeros((n, 3), np.float32)
+    gq = np.zeros((n, 4), np.float32)
+    gs = np.zeros((n, 3), np.float32)
+    go = np.zeros(n, np.float32)
+    gv = np.zeros(16, np.float64)
+    gp = np.zeros(16, np.float64)
+    lib().oracle_project_backward(
+        n, _c(means), _c(quats), _c(scales), _c(opacities), _c(view).reshape(16),
+        _c(proj).reshape(16), _c(K).reshape(9), width, height, _c(radii, np.int32),
+        _c(seed_centers), _c(seed_conics), gm, gq, gs, go, _ptr(gv), _ptr(gp))
+    return gm, gq, gs, go, gv.reshape(4, 4), gp.reshape(4, 4)
+
+
+# --------------------------------------------------------------------------
+# One gs3d view end to end: gs3d/api.py:47-265 + gs3d/autograd.py:19-171 for a
+# single camera, composed from the stage functions above.
+
+
+@dataclass
+class ViewResult:
+    image: np.ndarray          # (C', H, W) planar, C' = channels + extras + 1
+    final_t: np.ndarray
+    contributors: np.ndarray
+    proj: Projected
+    keys: np.ndarray
+    ids: np.ndarray
+    ranges: np.ndarray
+    features: np.ndarray       # (N, C') blended attributes
+    colors_active: np.ndarray | None
+    full: np.ndarray
+    inverse: np.ndarray
+    campos: np.ndarray | None
+
+
+def gs3d_view_forward(means, quats_n, scales, opacities, viewmat, K, width, height, *,
+                      sh_coeffs=None, sh_degree=None, features=None, extras=None,
+                      background=None, near=0.2, far=float("inf"), radius_clip=0.0):
+    """quats_n must already be normalised (the reference normalises with Torch)."""
+    with_centers = sh_coeffs is not None and sh_degree > 0
+    full, inverse, campos, errors = cameras_prepare(viewmat[None], K[None], width, height,
+                                                    with_centers)
+    if errors[0]:
+        raise ValueError(f"camera error code {errors[0]}")
+    p = project_forward(means, quats_n, scales, opacities, viewmat, full[0], K, width,
+                        height, near, far, radius_clip)
+    active = None
+    if sh_coeffs is not None:
+        dirs = (np.asarray(means, np.float32) - campos[0][None]) if with_centers else np.asarray(means, np.float32)
+        colors, active = sh_forward(sh_coeffs, dirs, sh_degree, p.radii)
+    else:
+        colors = np.asarray(features, np.float32)
+    cols = [colors]
+    if extras is not None:
+        cols.append(np.asarray(extras, np.float32))
+    cols.append(np.ones((len(means), 1), np.float32))
+    attrs = np.ascontiguousarray(np.concatenate(cols, axis=1), dtype=np.float32)
+    bg = np.zeros(attrs.shape[1], np.float32)
+    if background is not None:
+        bg[: colors.shape[1]] = background
+    offsets, m = scan_counts(p.tiles)
+    keys, ids, ranges = bin_and_sort(p.centers, p.radii, p.depths, offsets, width, height)
+    image, final_t, contrib = render_forward(width, height, ranges, ids, p.centers, p.conics,
+                                             attrs, bg)
+    return ViewResult(image, final_t, contrib, p, keys, ids, ranges, attrs, active, full[0],
+                      inverse[0], None if not with_centers else campos[0]), bg
+
+
+@dataclass
+class ViewGrads:
+    means: np.ndarray
+    quats_n: np.ndarray        # w.r.t. the normalised quaternions
+    scales: np.ndarray
+    opacities: np.ndarray
+    sh: np.ndarray | None
+    colors: np.ndarray | None  # features path
+    extras: np.ndarray | None
+    viewmat: np.ndarray
+    means2d: np.ndarray
+    absgrad: np.ndarray
+
+
+def gs3d_view_backward(r: ViewResult, bg, means, quats_n, scales, opacities, viewmat, K, width,
+                       height, upstream_hwc, *, sh_coeffs=None, sh_degree=None, n_colors=3,
+                       n_extras=0):
+    """Reverse of gs3d_view_forward: gs3d/autograd.py:91-171 + SH + camera VJPs."""
+    up = np.ascontiguousarray(np.moveaxis(np.asarray(upstream_hwc, np.float32), -1, 0))
+    gc, gq, gf, ga = render_backward(width, height, r.ranges, r.ids, r.proj.centers,
+                                     r.proj.conics, r.features, bg, r.final_t, r.contributors,
+                                     up, absgrad=True, constant_tail=1)
+    gm, gqn, gs, go, gview, gproj = project_backward(
+        means, quats_n, scales, opacities, viewmat, r.full, K, width, height, r.proj.radii,
+        gc.astype(np.float32), gq.astype(np.float32))
+    gm = gm.astype(np.float64)
+    gcolor = gf[:, :n_colors]
+    gsh = None
+    gcampos = None
+    if sh_coeffs is not None:
+        with_centers = sh_degree > 0
+        dirs = (np.asarray(means, np.float32) - r.campos[None]) if with_centers else np.asarray(means, np.float32)
+        gsh, gdir = sh_backward(sh_coeffs, dirs, sh_degree, r.proj.radii, r.colors_active,
+                                gcolor.astype(np.float32), need_dirs=with_centers)
+        if with_centers:
+            gm = gm + gdir
+            gcampos = -gdir.astype(np.float64).sum(0)
+    gv_cam = cameras_backward(K[None], gproj[None].astype(np.float32), width, height,
+                              r.inverse[None] if gcampos is not None else None,
+                              None if gcampos is None else gcampos[None].astype(np.float32))[0]
+    return ViewGrads(gm, gqn, gs, go, gsh, None if sh_coeffs is not None else gcolor,
+                     gf[:, n_colors:n_colors + n_extras] if n_extras else None,
+                     gview + gv_cam.astype(np.float64), gc, ga)

@@ -1,0 +1,189 @@
+"""gs3d.rasterize / gsplat.rasterization end to end against the oracle.
+
+The oracle composes the reference's per-view chain (gs3d/api.py:47-265,
+gs3d/autograd.py:19-171): camera preparation, projection, masked SH,
+binning, blending and their VJPs; per-view gradients are summed as Torch
+autograd does for shared parameters.  Quaternion normalisation is a Torch op
+in both (inputs.py:252), so its VJP is applied with Torch on the CPU.
+Tolerances: images max-abs 1e-5, gradients relative L2 1e-3.
+"""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import rel_l2
+from dsl_splat_b200 import gs3d
+from dsl_splat_b200.gs3d.gsplat import rasterization
+from dsl_splat_b200.scenes import make_scene
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+IMG_TOL = 1e-5
+GRAD_TOL = 1e-3
+
+
+def _run(scene, *, use_features=False, absgrad=True, background=None):
+    d = torch.device("cuda", 0)
+    p = {k: getattr(scene, k).to(d).requires_grad_(True)
+         for k in ("means", "quats", "scales", "opacities")}
+    viewmats = scene.viewmats.to(d).requires_grad_(True)
+    Ks = scene.Ks.to(d)
+    kw = {}
+    if use_features:
+        colors = scene.sh_coeffs[:, 0].to(d).contiguous().requires_grad_(True)
+        kw["features"] = colors
+    else:
+        colors = scene.sh_coeffs.to(d).requires_grad_(True)
+        kw["sh_coeffs"] = colors
+    if background is not None:
+        kw["backgrounds"] = background.to(d)
+    res = gs3d.rasterize(p["means"], p["quats"], p["scales"], p["opacities"], viewmats, Ks,
+                         scene.width, scene.height, absgrad=absgrad, **kw)
+    C = scene.viewmats.shape[0]
+    g = torch.Generator().manual_seed(11)
+    gF = torch.randn(C, scene.height, scene.width, 3, generator=g)
+    gA = torch.randn(C, scene.height, scene.width, 1, generator=g)
+    loss = (res.features * gF.to(d)).sum() + (res.alpha * gA.to(d)).sum()
+    loss.backward()
+    return res, p, viewmats, colors, gF, gA
+
+
+def _oracle(scene, gF, gA, *, use_features=False, background=None):
+    d = torch.device("cuda", 0)
+    qn_gpu = F.normalize(scene.quats.to(d), dim=-1).cpu()
+    C = scene.viewmats.shape[0]
+    means = scene.means.numpy()
+    qn = qn_gpu.numpy()
+    acc = None
+    images, per_view = [], []
+    for c in range(C):
+        kw = dict(features=scene.sh_coeffs[:, 0].numpy()) if use_features else dict(
+            sh_coeffs=scene.sh_coeffs.numpy(), sh_degree=scene.sh_degree)
+        r, bg = O.gs3d_view_forward(means, qn, scene.scales.numpy(), scene.opacities.numpy(),
+                                    scene.viewmats[c].numpy(), scene.Ks[c].numpy(), scene.width,
+                                    scene.height, background=None if background is None else
+                                    background[c].numpy(), **kw)
+        up = np.concatenate([gF[c].numpy(), gA[c].numpy()], axis=-1)
+        if use_features:
+            g = O.gs3d_view_backward(r, bg, means, qn, scene.scales.numpy(),
+                                     scene.opacities.numpy(), scene.viewmats[c].numpy(),
+                                     scene.Ks[c].numpy(), scene.width, scene.height, up)
+        else:
+            g = O.gs3d_view_backward(r, bg, means, qn, scene.scales.numpy(),
+                                     scene.opacities.numpy(), scene.viewmats[c].numpy(),
+                                     scene.Ks[c].numpy(), scene.width, scene.height, up,
+                                     sh_coeffs=scene.sh_coeffs.numpy(), sh_degree=scene.sh_degree)
+        images.append(r.image)
+        per_view.append(g)
+        vals = dict(means=g.means, quats_n=g.quats_n, scales=g.scales, opacities=g.opacities,
+                    colors=g.sh if not use_features else g.colors)
+        acc = vals if acc is None else {k: acc[k] + v for k, v in vals.items()}
+    _, vjp = torch.func.vjp(lambda q: F.normalize(q, dim=-1), scene.quats.double())
+    acc["quats"] = vjp(torch.from_numpy(np.asarray(acc["quats_n"], np.float64)))[0].numpy()
+    return images, per_view, acc
+
+
+CASES = {
+    "c0_sh0": (dict(config=0), False),
+    "c0_features": (dict(config=0), True),
+    "c1_small_sh3": (dict(config=1, n=20000, width=480, height=270), False),
+    "c2_three_views": (dict(config=2, n=30000, width=324, height=210, cameras=3), False),
+}
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_rasterize_forward_backward(case):
+    cfg, use_features = CASES[case]
+    scene = make_scene(**cfg)
+    bg = None
+    if case == "c0_features":
+        bg = torch.tensor([[0.2, 0.4, 0.6]])
+    res, p, viewmats, colors, gF, gA = _run(scene, use_features=use_features, background=bg)
+    images, per_view, acc = _oracle(scene, gF, gA, use_features=use_features, background=bg)
+    C = scene.viewmats.shape[0]
+    got = torch.cat([res.features, res.alpha], -1).detach().cpu().numpy()
+    for c in range(C):
+        assert np.abs(np.moveaxis(got[c], -1, 0) - images[c]).max() <= IMG_TOL
+    assert rel_l2(p["means"].grad.cpu(), acc["means"]) <= GRAD_TOL
+    assert rel_l2(p["quats"].grad.cpu(), acc["quats"]) <= GRAD_TOL
+    assert rel_l2(p["scales"].grad.cpu(), acc["scales"]) <= GRAD_TOL
+    assert rel_l2(p["opacities"].grad.cpu(), acc["opacities"]) <= GRAD_TOL
+    assert rel_l2(colors.grad.cpu(), acc["colors"]) <= GRAD_TOL
+    for c in range(C):
+        assert rel_l2(viewmats.grad[c].cpu(), per_view[c].viewmat) <= GRAD_TOL
+        assert rel_l2(res.means2d.grad[c].cpu(), per_view[c].means2d) <= GRAD_TOL
+        assert rel_l2(res.means2d.absgrad[c].cpu(), per_view[c].absgrad) <= GRAD_TOL
+    radii = res.radii.cpu().numpy()
+    assert radii.shape == (C, scene.means.shape[0], 2)
+
+
+def test_packed_metadata_and_gsplat_adapter():
+    scene = make_scene(0, n=2000)
+    d = torch.device("cuda", 0)
+    means = scene.means.to(d).requires_grad_(True)
+    feats, alpha, meta = rasterization(
+        means, scene.quats.to(d), scene.scales.to(d), scene.opacities.to(d),
+        scene.sh_coeffs.to(d), scene.viewmats.to(d), scene.Ks.to(d), scene.width, scene.height,
+        sh_degree=0, packed=True, absgrad=True, near_plane=0.2)
+    dense = gs3d.rasterize(means, scene.quats.to(d), scene.scales.to(d), scene.opacities.to(d),
+                           scene.viewmats.to(d), scene.Ks.to(d), scene.width, scene.height,
+                           sh_coeffs=scene.sh_coeffs.to(d), packed=False)
+    assert torch.equal(feats, dense.features)
+    vis = (dense.radii[0] > 0).all(-1)
+    assert meta["packed"] is True
+    assert len(meta["means2d"]) == int(vis.sum())
+    assert torch.equal(meta["gaussian_ids"], vis.nonzero().flatten())
+    (feats.sum() + alpha.sum()).backward()
+    assert meta["means2d"].grad is not None
+    assert meta["means2d"].absgrad.shape == meta["means2d"].shape
+
+
+def test_statistics_counts_and_sums():
+    from dsl_splat_b200 import MaskedContributionCount, WeightedContributionSum
+    scene = make_scene(0, n=3000)
+    d = torch.device("cuda", 0)
+    H, W = scene.height, scene.width
+    mask = torch.zeros(H, W, dtype=torch.bool, device=d)
+    mask[: H // 2] = True
+    weights = torch.rand(H, W, device=d)
+    res = gs3d.rasterize(scene.means.to(d), scene.quats.to(d), scene.scales.to(d),
+                         scene.opacities.to(d), scene.viewmats.to(d), scene.Ks.to(d), W, H,
+                         sh_coeffs=scene.sh_coeffs.to(d),
+                         statistics=(MaskedContributionCount("hits", mask),
+                                     WeightedContributionSum("score", weights)))
+    hits = res.statistics["hits"]
+    score = res.statistics["score"]
+    assert hits.shape == (1, 3000) and score.shape == (1, 3000)
+    # full-image weights of one reproduce sum over pixels of alpha*T per Gaussian
+    ones = torch.ones(H, W, device=d)
+    res2 = gs3d.rasterize(scene.means.to(d), scene.quats.to(d), scene.scales.to(d),
+                          scene.opacities.to(d), scene.viewmats.to(d), scene.Ks.to(d), W, H,
+                          sh_coeffs=scene.sh_coeffs.to(d),
+                          statistics=(WeightedContributionSum("w", ones),))
+    total = float(res2.statistics["w"].sum())
+    alpha_sum = float(res2.alpha.sum())
+    assert abs(total - alpha_sum) <= 1e-3 * max(1.0, alpha_sum)
+    assert int(hits.sum()) > 0 and float(score.sum()) > 0
+
+
+def test_error_paths():
+    scene = make_scene(0, n=100)
+    d = torch.device("cuda", 0)
+    args = [scene.means.to(d), scene.quats.to(d), scene.scales.to(d), scene.opacities.to(d),
+            scene.viewmats.to(d)]
+    bad_k = scene.Ks.clone()
+    bad_k[0, 0, 0] = -1.0
+    with pytest.raises(ValueError, match="positive fx/fy"):
+        gs3d.rasterize(*args, bad_k.to(d), scene.width, scene.height, sh_coeffs=scene.sh_coeffs.to(d))
+    skew = scene.Ks.clone()
+    skew[0, 0, 1] = 0.5
+    with pytest.raises(NotImplementedError, match="zero-skew"):
+        gs3d.rasterize(*args, skew.to(d), scene.width, scene.height, sh_coeffs=scene.sh_coeffs.to(d))
+    sh3 = torch.zeros(100, 16, 3, device=d)
+    singular = torch.zeros(1, 4, 4, device=d)
+    with pytest.raises(torch.linalg.LinAlgError):
+        gs3d.rasterize(args[0], args[1], args[2], args[3], singular, scene.Ks.to(d), scene.width,
+                       scene.height, sh_coeffs=sh3)

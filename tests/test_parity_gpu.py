@@ -1,0 +1,294 @@
+"""GPU parity: the sm_100a kernels (through the C ABI) against the CPU oracle.
+
+Tolerances:
+  * integer outputs -- radii, tile counts, sorted ids, ranges, keys,
+    contributor counts -- bit-exact;
+  * float forward outputs of the projection and SH (same float32 operation
+    sequence on both sides) -- bit-exact; final transmittance bit-exact;
+  * rendered colour/alpha -- max-abs <= 1e-5;
+  * gradients -- relative L2 <= 1e-3 (atomic summation order differs).
+"""
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import rel_l2
+from dsl_splat_b200 import stages
+from dsl_splat_b200.scenes import make_scene
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+IMG_TOL = 1e-5
+GRAD_TOL = 1e-3
+
+CASES = {
+    "c0": dict(config=0),
+    "c1_small": dict(config=1, n=20000, width=480, height=270),
+    "c2_view": dict(config=2, n=30000, width=324, height=210, cameras=1),
+}
+
+
+def _scene(name):
+    return make_scene(**CASES[name])
+
+
+def _dev():
+    return torch.device("cuda", 0)
+
+
+class Prepared:
+    """One view's inputs on the GPU plus the identical float32 arrays on the CPU."""
+
+    def __init__(self, scene, view=0):
+        d = _dev()
+        self.s = scene
+        self.W, self.H = scene.width, scene.height
+        self.means = scene.means.to(d)
+        self.quats = F.normalize(scene.quats.to(d), dim=-1)
+        self.scales = scene.scales.to(d)
+        self.opac = scene.opacities.to(d)
+        self.view = scene.viewmats[view].to(d).contiguous()
+        self.K = scene.Ks[view].to(d).contiguous()
+        self.sh = scene.sh_coeffs.to(d)
+        self.deg = scene.sh_degree
+        full, inv, centers = stages.cameras_prepare(self.view[None], self.K[None], self.W, self.H,
+                                                    self.deg > 0)
+        self.full, self.inv = full[0], (inv[0] if self.deg > 0 else None)
+        self.campos = centers[0] if self.deg > 0 else None
+        self.np = {k: getattr(self, k).cpu().numpy() for k in
+                   ("means", "quats", "scales", "opac", "view", "K", "sh", "full")}
+
+    def project(self):
+        return stages.project_fused(self.means, self.quats, self.scales, self.opac, self.view,
+                                    self.full, self.K, self.W, self.H, 0.2, float("inf"), 0.0,
+                                    sh=self.sh, sh_degree=self.deg, campos=self.campos)
+
+
+def _oracle_view(p: Prepared):
+    r, bg = O.gs3d_view_forward(p.np["means"], p.np["quats"], p.np["scales"], p.np["opac"],
+                                p.np["view"], p.np["K"], p.W, p.H, sh_coeffs=p.np["sh"],
+                                sh_degree=p.deg)
+    return r, bg
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_cameras_bit_exact(case):
+    p = Prepared(_scene(case))
+    full, inv, centers, err = O.cameras_prepare(p.np["view"][None], p.np["K"][None], p.W, p.H,
+                                                True)
+    g_full, g_inv, g_centers = stages.cameras_prepare(p.view[None], p.K[None], p.W, p.H, True)
+    assert err[0] == 0
+    np.testing.assert_array_equal(g_full.cpu().numpy(), full)
+    np.testing.assert_array_equal(g_inv.cpu().numpy(), inv)
+    np.testing.assert_array_equal(g_centers.cpu().numpy(), centers)
+    gf = np.random.default_rng(0).standard_normal((1, 4, 4)).astype(np.float32)
+    gc = np.random.default_rng(1).standard_normal((1, 3)).astype(np.float32)
+    ref = O.cameras_backward(p.np["K"][None], gf, p.W, p.H, inv, gc)
+    got = stages.cameras_backward(p.K[None], torch.from_numpy(gf).to(_dev()), p.W, p.H,
+                                  g_inv, torch.from_numpy(gc).to(_dev()), (1, 4, 4))
+    np.testing.assert_array_equal(got.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_projection_and_sh_bit_exact(case):
+    p = Prepared(_scene(case))
+    out = p.project()
+    r, _ = _oracle_view(p)
+    radii = out.state.radii.cpu().numpy()
+    np.testing.assert_array_equal(radii, r.proj.radii)
+    np.testing.assert_array_equal(out.state.tile_counts.cpu().numpy(), r.proj.tiles)
+    vis = radii > 0
+    assert vis.sum() > 0
+    np.testing.assert_array_equal(out.state.centers.cpu().numpy()[vis], r.proj.centers[vis])
+    np.testing.assert_array_equal(out.state.conics.cpu().numpy()[vis], r.proj.conics[vis])
+    np.testing.assert_array_equal(out.state.depths.cpu().numpy()[vis], r.proj.depths[vis])
+    np.testing.assert_array_equal(out.colors.cpu().numpy(), r.features[:, :3])
+    np.testing.assert_array_equal(out.active.cpu().numpy(), r.colors_active)
+    # dense metadata: visible rows copied, culled rows zero (metadata.py:12-31)
+    m2d = out.means2d.cpu().numpy()
+    np.testing.assert_array_equal(m2d[vis], r.proj.centers[vis])
+    assert not m2d[~vis].any()
+    np.testing.assert_array_equal(out.opacities.cpu().numpy()[vis], r.proj.conics[vis, 3])
+    meta = stages.metadata(out.state)
+    np.testing.assert_array_equal(meta["means2d"].cpu().numpy(), m2d)
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_binning_bit_exact(case):
+    p = Prepared(_scene(case))
+    out = p.project()
+    bins = stages.bin_and_sort(out.state, p.W, p.H)
+    r, _ = _oracle_view(p)
+    ranges = bins["ranges"].cpu().numpy()
+    ids = bins["point_list"].cpu().numpy()
+    np.testing.assert_array_equal(ranges, r.ranges)
+    np.testing.assert_array_equal(ids, r.ids)
+    # the 64-bit keys the reference sorts: (tile << 32) | float bits(depth)
+    depth_bits = out.state.depths.cpu().numpy().view(np.uint32).astype(np.uint64)
+    tile_of = np.repeat(np.arange(len(ranges), dtype=np.uint64), ranges[:, 1] - ranges[:, 0])
+    keys = (tile_of << np.uint64(32)) | depth_bits[ids]
+    np.testing.assert_array_equal(keys, r.keys)
+    offsets, m = stages.scan_counts(out.state.tile_counts)
+    ref_off, ref_m = O.scan_counts(r.proj.tiles)
+    assert m == ref_m == len(ids)
+    np.testing.assert_array_equal(offsets.cpu().numpy(), ref_off)
+
+
+def _render_case(case):
+    p = Prepared(_scene(case))
+    out = p.project()
+    bins = stages.bin_and_sort(out.state, p.W, p.H)
+    r, bg = _oracle_view(p)
+    return p, out, bins, r, bg
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_render_forward(case):
+    p, out, bins, r, bg = _render_case(case)
+    bg_t = torch.from_numpy(bg).to(_dev())
+    px = stages.render(out.state, bins, out.colors, None, True, bg_t, p.W, p.H)
+    np.testing.assert_array_equal(px.contributors.cpu().numpy(), r.contributors)
+    np.testing.assert_array_equal(px.transmittance.cpu().numpy(), r.final_t)
+    img = np.moveaxis(px.features.cpu().numpy(), -1, 0)
+    assert np.abs(img - r.image).max() <= IMG_TOL
+    planar = stages.render(out.state, bins, out.colors, None, True, bg_t, p.W, p.H, planar=True)
+    np.testing.assert_array_equal(planar.features.cpu().numpy(), img)
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_render_backward(case):
+    p, out, bins, r, bg = _render_case(case)
+    bg_t = torch.from_numpy(bg).to(_dev())
+    px = stages.render(out.state, bins, out.colors, None, True, bg_t, p.W, p.H)
+    up = np.random.default_rng(7).standard_normal((p.H, p.W, 4)).astype(np.float32)
+    gc, gq, ga, _, gabs = stages.render_backward(
+        out.state, bins, out.colors, None, True, bg_t, px.transmittance, px.contributors,
+        torch.from_numpy(up).to(_dev()), p.W, p.H, absgrad=True, constant_tail=1)
+    rc, rq, rf, rabs = O.render_backward(p.W, p.H, r.ranges, r.ids, r.proj.centers,
+                                         r.proj.conics, r.features, bg, r.final_t,
+                                         r.contributors, np.moveaxis(up, -1, 0).copy(),
+                                         absgrad=True, constant_tail=1)
+    assert rel_l2(gc.cpu().numpy(), rc) <= GRAD_TOL
+    assert rel_l2(gq.cpu().numpy(), rq) <= GRAD_TOL
+    assert rel_l2(ga.cpu().numpy(), rf[:, :3]) <= GRAD_TOL
+    assert rel_l2(gabs.cpu().numpy(), rabs) <= GRAD_TOL
+    assert not rf[:, 3].any()  # constant tail: no feature gradient for the ones column
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_projection_backward(case):
+    p = Prepared(_scene(case))
+    out = p.project()
+    n = len(p.means)
+    rng = np.random.default_rng(3)
+    seed_c = rng.standard_normal((n, 2)).astype(np.float32)
+    seed_q = (rng.standard_normal((n, 4)) * 1e-2).astype(np.float32)
+    d = _dev()
+    grads = stages.project_backward(p.means, p.quats, p.scales, p.opac, p.view, p.full, p.K, p.W,
+                                    p.H, out.state, torch.from_numpy(seed_c).to(d),
+                                    torch.from_numpy(seed_q).to(d), (True,) * 6)
+    ref = O.project_backward(p.np["means"], p.np["quats"], p.np["scales"], p.np["opac"],
+                             p.np["view"], p.np["full"], p.np["K"], p.W, p.H,
+                             out.state.radii.cpu().numpy(), seed_c, seed_q)
+    for got, want in zip(grads, ref):
+        assert rel_l2(got.cpu().numpy(), want) <= GRAD_TOL
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_sh_standalone(case):
+    p = Prepared(_scene(case))
+    out = p.project()
+    dirs = p.means - (p.campos if p.campos is not None else 0.0)
+    colors, active = stages.sh_forward(p.sh, dirs, p.deg, out.state.radii, True)
+    np.testing.assert_array_equal(colors.cpu().numpy(), out.colors.cpu().numpy())
+    up = torch.randn(len(p.means), 3, device=_dev())
+    gsh, gdir = stages.sh_backward(p.sh, dirs, p.deg, out.state.radii, active, up, True)
+    rsh, rdir = O.sh_backward(p.np["sh"], dirs.cpu().numpy(), p.deg,
+                              out.state.radii.cpu().numpy(), active.cpu().numpy(),
+                              up.cpu().numpy(), need_dirs=True)
+    assert rel_l2(gsh.cpu().numpy(), rsh) <= GRAD_TOL
+    if p.deg > 0:
+        assert rel_l2(gdir.cpu().numpy(), rdir) <= GRAD_TOL
+
+
+def test_expf_matches_oracle_and_cuda():
+    x = np.concatenate([np.linspace(-80.0, 0.0, 200001, dtype=np.float32),
+                        np.float32(-np.logspace(-8, 1.9, 5001))]).astype(np.float32)
+    d = _dev()
+    xt = torch.from_numpy(x).to(d)
+    ours = torch.empty_like(xt)
+    cuda = torch.empty_like(xt)
+    from dsl_splat_b200._native import check, lib, stream
+    check(lib.splat_debug_expf(len(x), xt.data_ptr(), ours.data_ptr(), cuda.data_ptr(),
+                               stream(d)), "debug_expf")
+    ours, cuda = ours.cpu().numpy(), cuda.cpu().numpy()
+    np.testing.assert_array_equal(ours, O.expf(x))
+    ulp = np.abs(ours.view(np.int32).astype(np.int64) - cuda.view(np.int32).astype(np.int64))
+    assert ulp.max() <= 3, ulp.max()
+
+
+def test_empty_and_culled_scenes():
+    d = _dev()
+    s = make_scene(0, n=64)
+    means = s.means.clone()
+    means[:, 2] = -5.0  # all behind the camera
+    W, H = s.width, s.height
+    view, K = s.viewmats[0].to(d), s.Ks[0].to(d)
+    full, _, _ = stages.cameras_prepare(view[None], K[None], W, H, False)
+    st = stages.project(means.to(d), F.normalize(s.quats.to(d), dim=-1), s.scales.to(d),
+                        s.opacities.to(d), view, full[0], K, W, H, 0.2, float("inf"), 0.0)
+    assert int(st.radii.abs().sum()) == 0
+    bins = stages.bin_and_sort(st, W, H)
+    assert len(bins["point_list"]) == 0
+    assert int(bins["ranges"].abs().sum()) == 0
+    colors = torch.rand(64, 3, device=d)
+    bg = torch.tensor([0.1, 0.2, 0.3, 0.0], device=d)
+    px = stages.render(st, bins, colors, None, True, bg, W, H)
+    assert torch.all(px.transmittance == 1)
+    assert torch.allclose(px.features[..., :3], bg[:3].expand(H, W, 3))
+    e = stages.project(means[:0].to(d), s.quats[:0].to(d), s.scales[:0].to(d),
+                       s.opacities[:0].to(d), view, full[0], K, W, H, 0.2, float("inf"), 0.0)
+    assert len(stages.bin_and_sort(e, W, H)["point_list"]) == 0
+
+
+@pytest.mark.parametrize("width,height", [(1, 1), (17, 5), (4200, 4100)])
+def test_tile_pass_counts(width, height):
+    """1, 2 and 3 tile-id radix passes (T<=256, <=65536, >65536) vs the oracle."""
+    s = make_scene(0, n=3000, width=width, height=height)
+    d = _dev()
+    s.Ks[0] = torch.tensor([[width * 1.0, 0, width / 2], [0, width * 1.0, height / 2], [0, 0, 1]])
+    view, K = s.viewmats[0].to(d), s.Ks[0].to(d)
+    full, _, _ = stages.cameras_prepare(view[None], K[None], width, height, False)
+    q = F.normalize(s.quats.to(d), dim=-1)
+    st = stages.project(s.means.to(d), q, s.scales.to(d), s.opacities.to(d), view, full[0], K,
+                        width, height, 0.2, float("inf"), 0.0)
+    bins = stages.bin_and_sort(st, width, height)
+    ref_p = O.project_forward(s.means.numpy(), q.cpu().numpy(), s.scales.numpy(),
+                              s.opacities.numpy(), view.cpu().numpy(), full[0].cpu().numpy(),
+                              K.cpu().numpy(), width, height)
+    off, _ = O.scan_counts(ref_p.tiles)
+    _, ids, ranges = O.bin_and_sort(ref_p.centers, ref_p.radii, ref_p.depths, off, width, height)
+    np.testing.assert_array_equal(bins["ranges"].cpu().numpy(), ranges)
+    np.testing.assert_array_equal(bins["point_list"].cpu().numpy(), ids)
+
+
+def test_huge_footprint_and_out_of_view():
+    """A Gaussian covering every tile, plus Gaussians outside the image."""
+    d = _dev()
+    s = make_scene(0, n=500)
+    s.scales[0] = torch.tensor([2.0, 2.0, 2.0])
+    s.means[0] = torch.tensor([0.0, 0.0, 3.0])
+    s.means[1:50, 0] += 50.0  # far to the side
+    p_scene = s
+    p = Prepared(p_scene)
+    out = p.project()
+    bins = stages.bin_and_sort(out.state, p.W, p.H)
+    r, bg = _oracle_view(p)
+    np.testing.assert_array_equal(bins["point_list"].cpu().numpy(), r.ids)
+    assert int(out.state.tile_counts[0]) == ((p.W + 15) // 16) * ((p.H + 15) // 16)
+    px = stages.render(out.state, bins, out.colors, None, True, torch.from_numpy(bg).to(d), p.W,
+                       p.H)
+    np.testing.assert_array_equal(px.contributors.cpu().numpy(), r.contributors)
