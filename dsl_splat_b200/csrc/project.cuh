@@ -269,11 +269,13 @@ __global__ void __launch_bounds__(256) project_forward_kernel(ProjectParams p) {
     }
   }
   if (p.meta_means2d != nullptr) {
-    reinterpret_cast<float2*>(p.meta_means2d)[i] = center;
-    p.meta_opacities[i] = conic.w;
-    p.meta_conics[3 * i + 0] = conic.x;
-    p.meta_conics[3 * i + 1] = conic.y;
-    p.meta_conics[3 * i + 2] = conic.z;
+    // culled rows (including those culled after the centre was computed)
+    // are zero, as splatting/metadata.py:28-32 writes them
+    reinterpret_cast<float2*>(p.meta_means2d)[i] = visible ? center : make_float2(0.0f, 0.0f);
+    p.meta_opacities[i] = visible ? conic.w : 0.0f;
+    p.meta_conics[3 * i + 0] = visible ? conic.x : 0.0f;
+    p.meta_conics[3 * i + 1] = visible ? conic.y : 0.0f;
+    p.meta_conics[3 * i + 2] = visible ? conic.z : 0.0f;
   }
 }
 

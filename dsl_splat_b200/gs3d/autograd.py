@@ -77,13 +77,13 @@ class ProjectView(torch.autograd.Function):
         else:
             gcol = None
         if n:
+            pin = stages.Args()
             check(lib.splat_project_backward_fused(
-                n, ptr(means), ptr(quats), ptr(scales), ptr(view.contiguous()),
-                ptr(full.contiguous()), ptr(intrinsics.contiguous()), cfg.width, cfg.height,
-                ptr(radii), ptr(g_centers), ptr(g_conics), ptr(gm), ptr(gq), ptr(gs), ptr(go), 0,
-                ptr(cam), ctx.sh_degree, 0 if sh is None else sh.shape[1], ptr(sh), ptr(campos),
-                ptr(active), ptr(gcol), 3, ptr(gsh), stream(means.device)),
-                "project_backward_fused")
+                n, pin(means), pin(quats), pin(scales), pin(view), pin(full), pin(intrinsics),
+                cfg.width, cfg.height, pin(radii), pin(g_centers), pin(g_conics), ptr(gm),
+                ptr(gq), ptr(gs), ptr(go), 0, ptr(cam), ctx.sh_degree,
+                0 if sh is None else sh.shape[1], pin(sh), pin(campos), pin(active), pin(gcol), 3,
+                ptr(gsh), stream(means.device)), "project_backward_fused")
         gview = cam[:16].reshape(4, 4) if needs[5] else None
         gfull = cam[16:32].reshape(4, 4) if needs[6] else None
         gcampos = cam[32:35].clone() if needs[7] else None

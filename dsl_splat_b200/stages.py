@@ -60,6 +60,28 @@ def _c(t: Tensor | None) -> Tensor | None:
     return t
 
 
+class Args:
+    """Converts tensors to device addresses for one C call and keeps every
+    converted tensor referenced until the call has been enqueued.
+
+    A copy made only to pass its address (a contiguous or aligned clone)
+    would otherwise be freed at once, and the caching allocator could hand
+    its block to the next argument's copy before the kernel reads it.
+    """
+
+    __slots__ = ("keep",)
+
+    def __init__(self):
+        self.keep: list[Tensor] = []
+
+    def __call__(self, t: Tensor | None) -> int | None:
+        if t is None:
+            return None
+        t = _c(t)
+        self.keep.append(t)
+        return t.data_ptr()
+
+
 def _far(value: float) -> float:
     return float(value) if math.isfinite(value) else float("inf")
 
@@ -127,6 +149,7 @@ def cameras_backward(Ks: Tensor, grad_full: Tensor | None, width: int, height: i
 def project(means, quats, scales, opacities, view, projection, intrinsics, width, height,
             near, far, radius_clip) -> ProjectedGaussians:
     """gs3d/projection.py:309-354 prepare."""
+    pin = Args()
     n = len(means)
     state = ProjectedGaussians(means.new_empty((n, 2)), means.new_empty((n, 4)),
                                torch.empty(n, dtype=torch.int32, device=means.device),
@@ -134,8 +157,8 @@ def project(means, quats, scales, opacities, view, projection, intrinsics, width
                                means.new_empty(n))
     if n:
         check(lib.splat_project_forward(
-            n, ptr(_c(means)), ptr(_c(quats)), ptr(_c(scales)), ptr(_c(opacities)),
-            ptr(_c(view)), ptr(_c(projection)), ptr(_c(intrinsics)), width, height, float(near),
+            n, pin(means), pin(quats), pin(scales), pin(opacities),
+            pin(view), pin(projection), pin(intrinsics), width, height, float(near),
             _far(far), float(radius_clip), ptr(state.centers), ptr(state.conics),
             ptr(state.radii), ptr(state.tile_counts), ptr(state.depths), _stream(means)),
             "project_forward")
@@ -156,6 +179,7 @@ def project_fused(means, quats, scales, opacities, view, projection, intrinsics,
                   near, far, radius_clip, sh: Tensor | None = None, sh_degree: int = 0,
                   campos: Tensor | None = None, need_active: bool = True) -> FusedProjection:
     """One launch for gs3d/api.py:145-189: projection, masked SH and metadata."""
+    pin = Args()
     n = len(means)
     dev = means.device
     state = ProjectedGaussians(means.new_empty((n, 2)), means.new_empty((n, 4)),
@@ -168,11 +192,11 @@ def project_fused(means, quats, scales, opacities, view, projection, intrinsics,
     if n:
         sh_c = _c(sh)
         check(lib.splat_project_forward_fused(
-            n, ptr(_c(means)), ptr(_c(quats)), ptr(_c(scales)), ptr(_c(opacities)),
-            ptr(_c(view)), ptr(_c(projection)), ptr(_c(intrinsics)), width, height, float(near),
+            n, pin(means), pin(quats), pin(scales), pin(opacities),
+            pin(view), pin(projection), pin(intrinsics), width, height, float(near),
             _far(far), float(radius_clip), ptr(state.centers), ptr(state.conics),
             ptr(state.radii), ptr(state.tile_counts), ptr(state.depths), int(sh_degree),
-            sh_c.shape[1] if sh_c is not None else 0, ptr(sh_c), ptr(_c(campos)), ptr(colors), 3,
+            sh_c.shape[1] if sh_c is not None else 0, ptr(sh_c), pin(campos), ptr(colors), 3,
             ptr(active), ptr(m2d), ptr(mop), ptr(mcon), _stream(means)), "project_forward_fused")
     return FusedProjection(state, colors, active, m2d, mop, mcon)
 
@@ -195,6 +219,7 @@ def project_backward(means, quats, scales, opacities, view, projection, intrinsi
                      height, state: ProjectedGaussians, grad_centers, grad_conics,
                      needs: tuple[bool, ...]):
     """gs3d/projection.py:357-428: [means, quats, scales, opacities, view, proj] grads."""
+    pin = Args()
     if not any(needs):
         return [None] * 6
     tensors = [means, quats, scales, opacities]
@@ -203,9 +228,9 @@ def project_backward(means, quats, scales, opacities, view, projection, intrinsi
     cam = means.new_zeros(32) if any(needs[4:]) else None
     if n:
         check(lib.splat_project_backward(
-            n, ptr(_c(means)), ptr(_c(quats)), ptr(_c(scales)), ptr(_c(view)),
-            ptr(_c(projection)), ptr(_c(intrinsics)), width, height, ptr(state.radii),
-            ptr(_c(grad_centers)), ptr(_c(grad_conics)), *[ptr(g) for g in grads], ptr(cam),
+            n, pin(means), pin(quats), pin(scales), pin(view),
+            pin(projection), pin(intrinsics), width, height, ptr(state.radii),
+            pin(grad_centers), pin(grad_conics), *[ptr(g) for g in grads], ptr(cam),
             _stream(means)), "project_backward")
     out = grads + [None, None]
     if needs[4]:
@@ -218,18 +243,20 @@ def project_backward(means, quats, scales, opacities, view, projection, intrinsi
 # ---- spherical harmonics -----------------------------------------------------
 
 def sh_forward(coeffs: Tensor, dirs: Tensor, degree: int, radii: Tensor | None, save: bool):
+    pin = Args()
     n = len(coeffs)
     coeffs, dirs = coeffs.contiguous(), dirs.contiguous()
     colors = coeffs.new_empty((n, 3))
     active = torch.empty((n if save else 0, 3), dtype=torch.uint8, device=coeffs.device)
     if n:
         check(lib.splat_sh_forward(n, degree, coeffs.shape[1], ptr(coeffs), ptr(dirs),
-                                   ptr(_c(radii)), ptr(colors), ptr(active) if save else None,
+                                   pin(radii), ptr(colors), ptr(active) if save else None,
                                    _stream(coeffs)), "sh_forward")
     return colors, active
 
 
 def sh_backward(coeffs, dirs, degree, radii, active, upstream, need_dirs: bool):
+    pin = Args()
     n = len(coeffs)
     coeffs, dirs = coeffs.contiguous(), dirs.contiguous()
     grad_coeffs = torch.empty_like(coeffs)
@@ -237,10 +264,10 @@ def sh_backward(coeffs, dirs, degree, radii, active, upstream, need_dirs: bool):
     if radii is None:
         radii_p = None
     else:
-        radii_p = ptr(radii.contiguous())
+        radii_p = pin(radii)
     if n:
         check(lib.splat_sh_backward(n, degree, coeffs.shape[1], ptr(coeffs), ptr(dirs), radii_p,
-                                    ptr(active.contiguous()), ptr(upstream.contiguous()),
+                                    pin(active), pin(upstream),
                                     ptr(grad_coeffs), ptr(grad_dirs), _stream(coeffs)),
               "sh_backward")
     return grad_coeffs, grad_dirs
@@ -250,13 +277,14 @@ def sh_backward(coeffs, dirs, degree, radii, active, upstream, need_dirs: bool):
 
 def scan_counts(counts: Tensor) -> tuple[Tensor, int]:
     """primitives/tiling.py:57-64: inclusive int32 offsets and the total."""
+    pin = Args()
     n = len(counts)
     offsets = torch.empty(n, dtype=torch.int32, device=counts.device)
     if not n:
         return offsets, 0
     ws = torch.empty(lib.splat_scan_workspace_bytes(n), dtype=torch.uint8, device=counts.device)
     total = torch.zeros(1, dtype=torch.int64, device=counts.device)
-    check(lib.splat_scan_counts(n, ptr(counts.contiguous()), ptr(offsets), ptr(total), ptr(ws),
+    check(lib.splat_scan_counts(n, pin(counts), ptr(offsets), ptr(total), ptr(ws),
                                 ws.numel(), _stream(counts)), "scan_counts")
     return offsets, int(total.item())
 
@@ -273,8 +301,9 @@ class BinPlan:
         self.pairs_dev = torch.zeros(1, dtype=torch.int64, device=dev)
         self.workspace = torch.empty(lib.splat_bin_workspace_bytes(n, width, height),
                                      dtype=torch.uint8, device=dev)
+        pin = Args()
         check(lib.splat_bin_prepare(
-            n, ptr(state.centers), ptr(state.radii), ptr(state.tile_counts), ptr(state.depths),
+            n, pin(state.centers), pin(state.radii), pin(state.tile_counts), pin(state.depths),
             width, height, ptr(self.workspace), self.workspace.numel(), ptr(self.ranges),
             ptr(self.pairs_dev), nv.stream(dev)), "bin_prepare")
 
@@ -320,6 +349,7 @@ def render(state: ProjectedFootprint, bins: dict, feat_a: Tensor, feat_b: Tensor
 
     statistics: a PreparedStatistics (statistics.py) whose counts/sums rows
     receive this view's accepted contributions."""
+    pin = Args()
     a, b, ca, cb = _features(feat_a, feat_b)
     channels = ca + cb + int(append_one)
     dev = a.device
@@ -340,9 +370,9 @@ def render(state: ProjectedFootprint, bins: dict, feat_a: Tensor, feat_b: Tensor
     with _timed("render_forward", dev):
         check(lib.splat_render_forward_statistics(
             width, height, ptr(bins["ranges"]), ptr(bins["point_list"]), len(bins["point_list"]),
-            len(state.centers), ptr(_c(state.centers)),
-            ptr(_c(state.conics)), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
-            ptr(background.contiguous()), ptr(image), pix_stride, ch_stride,
+            len(state.centers), pin(state.centers),
+            pin(state.conics), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
+            pin(background), ptr(image), pix_stride, ch_stride,
             ptr(out.transmittance), ptr(out.contributors), *stat, nv.stream(dev)), "render_forward")
     return out
 
@@ -353,6 +383,7 @@ def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
                     height: int, *, planar: bool = False, absgrad: bool = False,
                     constant_tail: int = 0, need_a: bool = True, need_b: bool = True):
     """gs3d/render.py:409-463: grads of centers, conics, feat_a, feat_b, abs."""
+    pin = Args()
     a, b, ca, cb = _features(feat_a, feat_b)
     channels = ca + cb + int(append_one)
     if not 0 <= constant_tail <= channels:
@@ -370,9 +401,9 @@ def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
     with _timed("render_backward", a.device):
         check(lib.splat_render_backward(
             width, height, ptr(bins["ranges"]), ptr(bins["point_list"]), len(bins["point_list"]),
-            len(state.centers), ptr(_c(state.centers)),
-            ptr(_c(state.conics)), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
-            ptr(background.contiguous()), ptr(final_t.contiguous()), ptr(contributors.contiguous()),
+            len(state.centers), pin(state.centers),
+            pin(state.conics), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
+            pin(background), pin(final_t), pin(contributors),
             ptr(g), pix_stride, ch_stride, ptr(centers), ptr(conics), ptr(ga), ptr(gb),
             ptr(absolute), constant_tail, nv.stream(a.device)), "render_backward")
     return centers, conics, ga, gb, absolute
