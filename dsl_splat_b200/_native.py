@@ -44,6 +44,7 @@ SIGNATURES: dict[str, tuple] = {
     "splat_sh_backward": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "splat_scan_workspace_bytes": (_Z, [_I]),
     "splat_scan_counts": (_I, [_I, _P, _P, _P, _P, _Z, _P]),
+    "splat_scan_counts_static": (_I, [_I, _P, _P, _P, _P]),
     "splat_bin_workspace_bytes": (_Z, [_I, _I, _I]),
     "splat_bin_pairs_workspace_bytes": (_Z, [_L, _I, _I]),
     "splat_bin_prepare": (_I, [_I, _P, _P, _P, _P, _I, _I, _P, _Z, _P, _P, _P]),

@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "binning.cuh"
@@ -492,6 +493,82 @@ int splat_scan_counts(int n, const int* counts, int* offsets, long long* total, 
       return check_launch("scan_counts total");
   }
   return check_launch("scan_counts");
+}
+
+}  // extern "C"
+
+// ---- scan without caller scratch ------------------------------------------------
+// Some callers cannot hand this library any device memory at call time: a
+// host whose device memory is all owned by its own pool, a render loop that
+// cannot afford cudaMalloc's implicit synchronisation, or a plugin running
+// where its framework forbids new allocations.  splat_scan_counts_static
+// serves them: the scan's block sums live in this file-scope array instead of
+// a caller workspace.  Every GPU that loads the library holds the array
+// (64 KiB) until the process exits.  It bounds n to kStaticScanBlocks blocks
+// of kSortTile counts.
+namespace {
+constexpr unsigned kStaticScanBlocks = 16384;
+constexpr long long kStaticScanMaxCount =
+    static_cast<long long>(kStaticScanBlocks) * kSortTile;  // 67,108,864
+static __device__ __align__(256) uint32_t g_static_scan_scratch[kStaticScanBlocks + 2];
+
+// Device address of g_static_scan_scratch per device ordinal.  The host-side
+// symbol is only a stand-in; the address comes from cudaGetSymbolAddress,
+// called once per device with that device current.
+std::mutex g_static_scan_mutex;
+void* g_static_scan_address[256] = {};
+
+int static_scan_scratch(uint32_t** out) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 256)
+    return check_launch("static scan: cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_static_scan_mutex);
+  if (g_static_scan_address[device] == nullptr) {
+    void* address = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&address, g_static_scan_scratch);
+    if (e != cudaSuccess || address == nullptr) {
+      g_last_error = std::string("static scan: cudaGetSymbolAddress: ") + cudaGetErrorString(e);
+      cudaGetLastError();
+      return kCudaError;
+    }
+    g_static_scan_address[device] = address;
+  }
+  *out = static_cast<uint32_t*>(g_static_scan_address[device]);
+  return kOk;
+}
+}  // namespace
+
+extern "C" {
+
+int splat_scan_counts_static(int n, const int* counts, int* offsets, long long* total,
+                             void* stream) {
+  if (n < 0) return fail(kInvalidArgument, "n < 0");
+  if (n > kStaticScanMaxCount)
+    return fail(kTooLarge, "splat_scan_counts_static handles at most 67108864 counts "
+                           "(16384 blocks of 4096); use splat_scan_counts with a workspace");
+  uint32_t* block_sums = nullptr;
+  const int r = static_scan_scratch(&block_sums);
+  if (r != kOk) return r;
+  cudaStream_t s = as_stream(stream);
+  if (n == 0) {
+    if (total && cudaMemsetAsync(total, 0, sizeof(long long), s) != cudaSuccess)
+      return check_launch("scan_counts_static");
+    return kOk;
+  }
+  // Each call overwrites every block sum and the total it reads, so nothing
+  // left by an earlier call needs clearing.
+  const unsigned nb = blocks_for(n, kSortTile);
+  uint32_t* tot = block_sums + kStaticScanBlocks + 1;
+  scan_block_sums_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, nullptr, n, block_sums);
+  scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, nb, tot);
+  scan_apply_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, nullptr, n, block_sums, 1,
+                                                       reinterpret_cast<uint32_t*>(offsets));
+  if (total) {
+    if (cudaMemsetAsync(total, 0, sizeof(long long), s) != cudaSuccess ||
+        cudaMemcpyAsync(total, tot, sizeof(uint32_t), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+      return check_launch("scan_counts_static total");
+  }
+  return check_launch("scan_counts_static");
 }
 
 // ---- binning ------------------------------------------------------------------

@@ -120,6 +120,24 @@ size_t splat_scan_workspace_bytes(int n);
 int splat_scan_counts(int n, const int* counts, int* offsets, long long* total, void* workspace,
                       size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference.  splat_scan_counts without any caller
+ * scratch, for callers that cannot hand the library device memory at call
+ * time (all device memory owned by the host's own pool, a render loop that
+ * cannot afford cudaMalloc's implicit synchronisation, a plugin whose
+ * framework forbids new allocations).  The scan's block sums live in a
+ * file-scope __device__ array of 64 KiB that every GPU loading the library
+ * holds until the process exits, so n is limited to 67108864 (16384 blocks
+ * of 4096 counts); larger n returns -4 without launching.  Allocates
+ * nothing: no cudaMalloc, no cudaFree.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  All calls share
+ * the array, so calls that overlap on the GPU (different streams, or
+ * different host threads without ordering) race; serialise them on one
+ * stream.  Each call rewrites the scratch it reads, so nothing needs
+ * clearing between calls.  Results are identical to splat_scan_counts. */
+int splat_scan_counts_static(int n, const int* counts, int* offsets, long long* total,
+                             void* stream);
+
 /* splatting/binning.py:171-217 bin_and_sort (tile_mode "radius"), split in
  * two calls around the one host read of the pair count that the reference
  * also makes (primitives/tiling.py:64):
