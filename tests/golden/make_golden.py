@@ -1,0 +1,260 @@
+"""Generate golden vectors from dsl_splat's own gs3d kernels (test infrastructure).
+
+Runs in a container that has the reference checkout (default
+/root/reference, or argv[1]); the committed .npz files are what the tests
+read, so nothing at test time needs the reference.  warp-lang is absent, so
+the reference modules are imported with warp_shim registered as `warp` (see
+that module for exactly what is emulated and the one substitution, exp).
+
+Kernels executed (reference file:line):
+  splatting/camera_kernels.py:11-66   prepare_kernel
+  splatting/camera_kernels.py:69-106  backward_kernel
+  gs3d/projection.py:89-164           project (tile_mode "radius")
+  primitives/sh.py:44-79, 82-138      SH forward / backward kernels
+  splatting/metadata.py:12-31         _prepare
+  splatting/binning.py:116-137        duplicate
+  primitives/tiling.py:39-54          identify_ranges
+  gs3d/render.py:36-208               render (forward blend, 256-thread blocks)
+  gs3d/render.py:211-356              backward (reverse blend, 256-thread blocks)
+Warp library calls restated: array_scan (inclusive cumsum) and
+radix_sort_pairs (a stable sort of the 64-bit keys).
+
+Usage: python tests/golden/make_golden.py [/path/to/reference]
+"""
+
+from __future__ import annotations
+
+import importlib
+import os
+import sys
+import time
+import types
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, HERE)
+sys.path.insert(0, ROOT)
+
+import warp_shim as ws  # noqa: E402
+
+
+def load_reference(ref_root: str):
+    sys.modules["warp"] = ws.make_module()
+    pkg_root = os.path.join(ref_root, "dsl_splat")
+    # Stub the packages so their __init__ files (which import the AAA stack)
+    # are not executed; submodules load from the checkout.
+    for pkg in ("dsl_splat", "dsl_splat.gs3d", "dsl_splat.splatting", "dsl_splat.primitives",
+                "dsl_splat.runtime"):
+        mod = types.ModuleType(pkg)
+        parts = pkg.split(".")[1:]
+        mod.__path__ = [os.path.join(pkg_root, *parts)]
+        sys.modules[pkg] = mod
+    from oracle import oracle as O
+    ws.set_exp(lambda x: np.float32(O.lib().oracle_expf(float(x))))
+    names = {
+        "cam": "dsl_splat.splatting.camera_kernels",
+        "proj": "dsl_splat.gs3d.projection",
+        "sh": "dsl_splat.primitives.sh",
+        "meta": "dsl_splat.splatting.metadata",
+        "bin": "dsl_splat.splatting.binning",
+        "tiling": "dsl_splat.primitives.tiling",
+        "render": "dsl_splat.gs3d.render",
+    }
+    return {k: importlib.import_module(v) for k, v in names.items()}
+
+
+def A(data, dtype=None):
+    return ws.Array(data, dtype)
+
+
+def golden_case(ref, name, scene: dict, seed: int):
+    W, H = scene["width"], scene["height"]
+    gx, gy = (W + 15) // 16, (H + 15) // 16
+    T = gx * gy
+    deg = scene["sh_degree"]
+    means = scene["means"].astype(np.float32)
+    n = len(means)
+    quats_raw = scene["quats"].astype(np.float32)
+    quats = F.normalize(torch.from_numpy(quats_raw), dim=-1).numpy()  # inputs.py:252
+    scales = scene["scales"].astype(np.float32)
+    opac = scene["opacities"].astype(np.float32)
+    sh = scene["sh"].astype(np.float32)
+    view = scene["viewmat"].astype(np.float32)
+    K = scene["K"].astype(np.float32)
+    wp = sys.modules["warp"]
+    out: dict = dict(width=W, height=H, sh_degree=deg, means=means, quats=quats, scales=scales,
+                     opacities=opac, sh=sh, viewmat=view, K=K)
+    t0 = time.time()
+
+    # camera_kernels.py:11-66 (with centres: SH degree > 0 needs them)
+    full = np.zeros((1, 4, 4), np.float32)
+    inverse = np.zeros((1, 4, 4), np.float32)
+    centers_cam = np.zeros((1, 3), np.float32)
+    errors = np.zeros(1, np.int32)
+    ws.launch(ref["cam"].prepare_kernel, 1,
+              [A(view[None].copy()), A(K[None].copy()), W, H, 1, A(full), A(inverse),
+               A(centers_cam), A(errors)])
+    assert errors[0] == 0
+    out.update(full=full[0], inverse=inverse[0], campos=centers_cam[0])
+
+    # gs3d/projection.py:89-164
+    centers = np.zeros((n, 2), np.float32)
+    conics = np.zeros((n, 4), np.float32)
+    radii = np.zeros(n, np.int32)
+    tiles = np.zeros(n, np.int32)
+    depths = np.zeros(n, np.float32)
+    ws.launch(ref["proj"].project, n,
+              [A(means, wp.vec3), A(quats, wp.vec4), A(scales, wp.vec3), A(opac), A(view.copy()),
+               A(full[0].copy()), A(K.copy()), W, H, np.float32(0.2), np.float32(np.inf),
+               np.float32(0.0), A(centers, wp.vec2), A(conics, wp.vec4), A(radii), A(tiles),
+               A(depths)])
+    out.update(centers=centers, conics=conics, radii=radii, tiles=tiles, depths=depths)
+
+    # primitives/sh.py:44-79 masked forward with saved clamp mask; directions
+    # are the Torch difference means - camera centre (gs3d/api.py:158-168)
+    dirs = (torch.from_numpy(means) - torch.from_numpy(centers_cam[0])).numpy()
+    colors = np.zeros((n, 3), np.float32)
+    active = np.zeros((n, 3), np.bool_)
+    ws.launch(ref["sh"].forward_kernel(deg, True, True), n,
+              [A(sh), A(dirs), A(radii), A(colors, wp.vec3), A(active)])
+    out.update(dirs=dirs, colors=colors, active=active)
+
+    # splatting/metadata.py:12-31
+    m2d = np.zeros((n, 2), np.float32)
+    mop = np.zeros(n, np.float32)
+    mcon = np.zeros((n, 3), np.float32)
+    ws.launch(ref["meta"]._prepare, n, [A(radii), A(centers, wp.vec2), A(conics, wp.vec4),
+                                         A(m2d, wp.vec2), A(mop), A(mcon, wp.vec3)])
+    out.update(meta_means2d=m2d, meta_opacities=mop, meta_conics=mcon)
+
+    # primitives/tiling.py:57-64 (Warp array_scan, inclusive) and
+    # splatting/binning.py:116-137 duplicate
+    offsets = np.cumsum(tiles, dtype=np.int64).astype(np.int32)
+    m = int(offsets[-1]) if n else 0
+    keys = np.zeros(2 * m, np.uint64)
+    ids = np.zeros(2 * m, np.int32)
+    ws.launch(ref["bin"].duplicate, n, [A(centers, wp.vec2), A(radii), A(depths), A(offsets),
+                                         gx, gy, A(keys), A(ids)])
+    # primitives/tiling.py:80-86 (Warp radix_sort_pairs: a stable LSD sort)
+    order = np.argsort(keys[:m], kind="stable")
+    keys_sorted = keys[:m][order]
+    ids_sorted = ids[:m][order]
+    ranges = np.zeros((T, 2), np.int32)
+    ws.launch(ref["tiling"].identify_ranges, m, [A(keys_sorted), A(ranges)])
+    out.update(offsets=offsets, keys=keys_sorted, ids=ids_sorted, ranges=ranges)
+
+    # gs3d/autograd.py:306-315: features = cat(colours, ones); black background
+    feats = np.concatenate([colors, np.ones((n, 1), np.float32)], axis=1)
+    C = feats.shape[1]
+    bg = np.zeros(C, np.float32)
+    Feature = wp.types.vector(C, np.float32)
+    image = np.zeros(C * H * W, np.float32)
+    final_t = np.zeros(H * W, np.float32)
+    contrib = np.zeros(H * W, np.int32)
+    ws.launch(ref["render"]._make_forward(C, ()), 256 * T,
+              [W, H, A(ranges), A(ids_sorted), A(centers, wp.vec2), A(conics, wp.vec4),
+               A(feats, Feature), A(bg), A(image), A(final_t), A(contrib)], block=256)
+    out.update(features=feats, background=bg, image=image.reshape(C, H, W),
+               final_t=final_t.reshape(H, W), contributors=contrib.reshape(H, W))
+
+    # gs3d/render.py:211-356 backward, absgrad, constant alpha tail
+    rng = np.random.default_rng(seed)
+    upstream = rng.standard_normal((C, H, W)).astype(np.float32)
+    g_centers = np.zeros((n, 2), np.float32)
+    g_conics = np.zeros((n, 4), np.float32)
+    g_feats = np.zeros((n, C), np.float32)
+    g_abs = np.zeros((n, 2), np.float32)
+    ws.launch(ref["render"]._make_backward(C, True, 1), 256 * T,
+              [W, H, A(ranges), A(ids_sorted), A(centers, wp.vec2), A(conics, wp.vec4),
+               A(feats, Feature), A(bg), A(final_t), A(contrib), A(upstream.ravel().copy()),
+               A(g_centers), A(g_conics), A(g_feats), A(g_abs)], block=256)
+    out.update(upstream=upstream, grad_centers=g_centers, grad_conics=g_conics,
+               grad_features=g_feats, grad_abs=g_abs)
+
+    # primitives/sh.py:82-138 backward with the blended colour gradient
+    g_sh = np.zeros_like(sh)
+    g_dirs = np.zeros((n, 3), np.float32)
+    up_colors = g_feats[:, :3].copy()
+    ws.launch(ref["sh"].backward_kernel(deg, True, True, deg > 0), n,
+              [A(sh), A(dirs), A(radii), A(active), A(up_colors), A(g_sh), A(g_dirs, wp.vec3)])
+    out.update(sh_upstream=up_colors, grad_sh=g_sh, grad_dirs=g_dirs)
+
+    # splatting/camera_kernels.py:69-106 pose VJP through full and the centre
+    gfull = rng.standard_normal((1, 4, 4)).astype(np.float32)
+    gcam = rng.standard_normal((1, 3)).astype(np.float32)
+    gviews = np.zeros((1, 4, 4), np.float32)
+    ws.launch(ref["cam"].backward_kernel, 1,
+              [A(K[None].copy()), A(gfull), W, H, A(inverse), A(gcam), 1, 1, A(gviews)])
+    out.update(cam_grad_full=gfull[0], cam_grad_centers=gcam[0], cam_grad_views=gviews[0])
+    print(f"{name}: n={n} visible={int((radii > 0).sum())} pairs={m} tiles={T} "
+          f"in {time.time() - t0:.1f}s", flush=True)
+    return out
+
+
+def scenes():
+    """Small seeded scenes with the benchmark configs' distributions."""
+    from dsl_splat_b200.scenes import intrinsics, look_at
+    g = torch.Generator().manual_seed(2024)
+    out = {}
+    # config-0 shapes: box in front of an identity camera, SH0
+    n = 160
+    xy = torch.rand(n, 2, generator=g) * 2 - 1
+    z = torch.rand(n, 1, generator=g) * 4 + 2
+    out["c0_sh0"] = dict(
+        width=48, height=40, sh_degree=0, means=torch.cat([xy, z], 1).numpy(),
+        scales=torch.exp(torch.randn(n, 3, generator=g) * 0.5 - 3.0).numpy(),
+        quats=torch.randn(n, 4, generator=g).numpy(),
+        opacities=torch.sigmoid(torch.randn(n, generator=g)).numpy(),
+        sh=torch.rand(n, 1, 3, generator=g).numpy(),
+        viewmat=torch.eye(4).numpy(), K=intrinsics(48.0, 48.0, 24.0, 20.0).numpy())
+    # config-1 shapes: clustered ball, SH3, camera at distance 8, rotated view
+    n = 220
+    centres = (torch.rand(8, 3, generator=g) * 2 - 1) * 3
+    means = centres[torch.randint(0, 8, (n,), generator=g)] + 0.5 * torch.randn(n, 3, generator=g)
+    sh = torch.empty(n, 16, 3)
+    sh[:, 0] = torch.rand(n, 3, generator=g)
+    sh[:, 1:] = torch.randn(n, 15, 3, generator=g) * 0.1
+    out["c1_sh3"] = dict(
+        width=56, height=40, sh_degree=3, means=means.numpy(),
+        scales=torch.exp(torch.randn(n, 3, generator=g) * 0.7 - 2.0).numpy(),
+        quats=torch.randn(n, 4, generator=g).numpy(),
+        opacities=torch.sigmoid(torch.randn(n, generator=g)).numpy(),
+        sh=sh.numpy(),
+        viewmat=look_at(torch.tensor([2.0, -1.0, -8.0])).numpy(),
+        K=intrinsics(60.0, 60.0, 28.0, 20.0).numpy())
+    # dense overlap (early termination), Gaussians behind the camera, off
+    # screen and one covering every tile; SH1, off-centre principal point
+    n = 420
+    means = (torch.rand(n, 3, generator=g) * 2 - 1) * torch.tensor([1.5, 1.2, 1.0])
+    means[:, 2] += 4.0
+    means[:20, 2] = -1.0 - torch.rand(20, generator=g)        # behind the camera
+    means[20:40, 0] += 12.0                                    # far off screen
+    means[40] = torch.tensor([0.0, 0.0, 3.0])
+    scales = torch.exp(torch.randn(n, 3, generator=g) * 0.4 - 2.3)
+    scales[40] = torch.tensor([1.5, 1.5, 1.5])                 # spans every tile
+    opac = torch.sigmoid(torch.randn(n, generator=g) + 2.0)
+    sh = torch.empty(n, 4, 3)
+    sh[:, 0] = torch.rand(n, 3, generator=g)
+    sh[:, 1:] = torch.randn(n, 3, 3, generator=g) * 0.2
+    out["dense_sh1"] = dict(
+        width=64, height=48, sh_degree=1, means=means.numpy(), scales=scales.numpy(),
+        quats=torch.randn(n, 4, generator=g).numpy(), opacities=opac.numpy(), sh=sh.numpy(),
+        viewmat=look_at(torch.tensor([0.5, -0.3, -1.0]), torch.tensor([0.0, 0.0, 4.0])).numpy(),
+        K=intrinsics(56.0, 52.0, 30.5, 25.0).numpy())
+    return out
+
+
+def main():
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = load_reference(ref_root)
+    for i, (name, scene) in enumerate(scenes().items()):
+        data = golden_case(ref, name, scene, seed=100 + i)
+        np.savez_compressed(os.path.join(HERE, f"gs3d_{name}.npz"), **data)
+
+
+if __name__ == "__main__":
+    main()
