@@ -28,7 +28,6 @@ import subprocess
 import sys
 import tempfile
 import time
-from datetime import timedelta
 
 import numpy as np
 import torch
@@ -44,7 +43,7 @@ CHANNELS = 4  # RGB + the appended alpha column (gs3d/autograd.py:306-311)
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", type=int, default=1)
@@ -90,17 +89,24 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, device: torch.device):
+        # nvidia-smi numbers GPUs physically; address ours by UUID instead of
+        # the CUDA ordinal, which CUDA_VISIBLE_DEVICES may remap.
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:  # noqa: BLE001
+            self.ident = str(device.index)
         self.proc = None
         self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--id={self.ident}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)  # let the first sample land inside the timed region
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
@@ -254,13 +260,12 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     pg = None
+    from dsl_splat_b200 import gs3d, sharding, stages
+    from dsl_splat_b200._native import lib
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
-                                device_id=dev)
+        sharding.init_process_group("nccl", timeout_s=180.0, device=dev)
         pg = dist
-    from dsl_splat_b200 import gs3d, stages
-    from dsl_splat_b200._native import lib
 
     s = workload(args.config, rank, world)
     means = s.means.to(dev).requires_grad_(True)
@@ -281,8 +286,7 @@ def main():
                              absgrad=True)
         torch.autograd.backward([res.features, res.alpha], [gF, gA])
         if pg is not None:
-            for p in params:
-                pg.all_reduce(p.grad)
+            sharding.allreduce_parameter_grads(params)
         last["res"] = res
 
     def barrier():
@@ -296,7 +300,7 @@ def main():
     stages.TIMERS = {}
     launches0 = lib.splat_launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         barrier()
         start.record()
         for _ in range(args.steps):
@@ -351,8 +355,7 @@ def main():
             loss = (r.features - target).abs().mean()
             loss.backward()
             if pg is not None:
-                for p in params:
-                    pg.all_reduce(p.grad)
+                sharding.allreduce_parameter_grads(params)
             return float(loss.item())
 
         for _ in range(2):

@@ -1,0 +1,65 @@
+"""Camera-sharded data parallelism for multi-view gs3d training.
+
+dsl_splat renders the views of a batch one after another and lets autograd
+sum their per-Gaussian gradients (gs3d/api.py:132-189, 229-255).  Across
+GPUs the same sum is an all-reduce: every rank holds the full Gaussian set,
+renders the cameras {k : k mod world == rank}, runs its backward (which
+already sums its local views), and the ranks all-reduce the per-Gaussian
+gradients (means 3 + quats 4 + scales 3 + opacities 1 + SH 48 floats per
+Gaussian).  That all-reduce is the path's only exchange; images, means2d
+gradients and pose gradients stay on the rank that rendered them.
+
+Works with any torch.distributed backend (NCCL over NVLink on the GPUs,
+gloo for the CPU tests).
+"""
+
+from __future__ import annotations
+
+from datetime import timedelta
+from typing import Sequence
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+
+def local_cameras(cameras: int, rank: int, world: int) -> list[int]:
+    """Camera indices rank renders: k mod world == rank (round robin)."""
+    if not 0 <= rank < world:
+        raise ValueError("rank must be in [0, world)")
+    return list(range(rank, cameras, world))
+
+
+def shard_views(viewmats: Tensor, Ks: Tensor, rank: int, world: int) -> tuple[Tensor, Tensor, list[int]]:
+    """The (C_local,4,4) poses and (C_local,3,3) intrinsics of this rank."""
+    idx = local_cameras(viewmats.shape[-3], rank, world)
+    sel = torch.tensor(idx, dtype=torch.long, device=viewmats.device)
+    return viewmats.index_select(-3, sel), Ks.index_select(-3, sel), idx
+
+
+def allreduce_gradients(grads: Sequence[Tensor | None], group=None) -> None:
+    """Sum gradients over all ranks in place (async launches, then wait).
+
+    Ranks must pass the same sequence (None entries are skipped on every rank
+    alike, so the collectives line up).
+    """
+    handles = [dist.all_reduce(g, op=dist.ReduceOp.SUM, group=group, async_op=True)
+               for g in grads if g is not None]
+    for h in handles:
+        h.wait()
+
+
+def allreduce_parameter_grads(params: Sequence[Tensor], group=None) -> None:
+    """all-reduce p.grad for every parameter that has one (same on all ranks)."""
+    allreduce_gradients([p.grad for p in params], group=group)
+
+
+def init_process_group(backend: str, timeout_s: float = 120.0, device: torch.device | None = None):
+    """Process group from the torchrun environment with a short timeout, so a
+    rank that stops joining collectives ends the others' next collective with
+    an error instead of a hang."""
+    kw = {"timeout": timedelta(seconds=timeout_s)}
+    if device is not None and device.type == "cuda":
+        kw["device_id"] = device
+    dist.init_process_group(backend, **kw)
+    return dist.group.WORLD

@@ -1,0 +1,122 @@
+"""Camera sharding on CPU ranks (gloo, world size 2).
+
+Each rank renders its cameras with the oracle (the CPU checker; the GPU path
+is exercised by bench.py --gpus N), sums its view gradients, and the ranks
+all-reduce with dsl_splat_b200.sharding.  The result must equal the sum over
+all views computed in one process (gs3d/api.py's sequential loop), within
+1e-6 relative L2 (float64 sums).  A second test makes one rank leave before
+the all-reduce: the other must get an error from the process group's
+timeout, not hang.
+"""
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import ROOT, rel_l2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _view_grads(scene, c):
+    import torch.nn.functional as F
+    from oracle import oracle as O
+    qn = F.normalize(scene.quats, dim=-1).numpy()
+    r, bg = O.gs3d_view_forward(scene.means.numpy(), qn, scene.scales.numpy(),
+                                scene.opacities.numpy(), scene.viewmats[c].numpy(),
+                                scene.Ks[c].numpy(), scene.width, scene.height,
+                                sh_coeffs=scene.sh_coeffs.numpy(), sh_degree=scene.sh_degree)
+    up = np.concatenate([scene.grad_image[c].numpy(), scene.grad_alpha[c].numpy()], -1)
+    g = O.gs3d_view_backward(r, bg, scene.means.numpy(), qn, scene.scales.numpy(),
+                             scene.opacities.numpy(), scene.viewmats[c].numpy(),
+                             scene.Ks[c].numpy(), scene.width, scene.height, up,
+                             sh_coeffs=scene.sh_coeffs.numpy(), sh_degree=scene.sh_degree)
+    return [torch.from_numpy(np.asarray(x, np.float64)) for x in
+            (g.means, g.quats_n, g.scales, g.opacities, g.sh)]
+
+
+def _scene():
+    from dsl_splat_b200.scenes import make_scene
+    return make_scene(2, n=3000, width=96, height=64, cameras=4)
+
+
+def _worker(rank, world, port, outdir, mode):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    from dsl_splat_b200 import sharding
+    sharding.init_process_group("gloo", timeout_s=15.0)
+    scene = _scene()
+    if mode == "leave" and rank == 1:
+        return  # leaves between steps, before joining the all-reduce
+    idx = sharding.local_cameras(scene.viewmats.shape[0], rank, world)
+    total = None
+    for c in idx:
+        g = _view_grads(scene, c)
+        total = g if total is None else [a + b for a, b in zip(total, g)]
+    status = "ok"
+    try:
+        sharding.allreduce_gradients(total)
+    except Exception as e:  # noqa: BLE001 - the failure is the point
+        status = f"error: {type(e).__name__}"
+    torch.save({"grads": total, "idx": idx, "status": status},
+               os.path.join(outdir, f"rank{rank}.pt"))
+    if mode != "leave":
+        dist.destroy_process_group()
+
+
+def _run(world, mode, tmp_path):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path), mode))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish")
+    return [torch.load(os.path.join(tmp_path, f"rank{r}.pt")) if
+            os.path.exists(os.path.join(tmp_path, f"rank{r}.pt")) else None for r in range(world)]
+
+
+def test_local_cameras_round_robin():
+    from dsl_splat_b200.sharding import local_cameras
+    assert local_cameras(8, 0, 2) == [0, 2, 4, 6]
+    assert local_cameras(8, 3, 4) == [3, 7]
+    assert sorted(sum((local_cameras(7, r, 3) for r in range(3)), [])) == list(range(7))
+    with pytest.raises(ValueError):
+        local_cameras(4, 2, 2)
+
+
+def test_two_rank_allreduce_equals_sequential_sum(tmp_path):
+    results = _run(2, "sum", tmp_path)
+    scene = _scene()
+    want = None
+    for c in range(scene.viewmats.shape[0]):
+        g = _view_grads(scene, c)
+        want = g if want is None else [a + b for a, b in zip(want, g)]
+    assert results[0]["idx"] == [0, 2] and results[1]["idx"] == [1, 3]
+    for res in results:
+        assert res["status"] == "ok"
+        for got, ref in zip(res["grads"], want):
+            assert rel_l2(got.numpy(), ref.numpy()) <= 1e-6
+
+
+def test_rank_that_leaves_is_detected_by_timeout(tmp_path):
+    results = _run(2, "leave", tmp_path)
+    assert results[1] is None
+    assert results[0]["status"].startswith("error")
