@@ -37,7 +37,7 @@ SIGNATURES: dict[str, tuple] = {
     "splat_metadata": (_I, [_I, _P, _P, _P, _P, _P, _P, _P]),
     "splat_project_backward": (_I, [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                     _P, _P, _P, _P]),
-    "splat_project_backward_fused": (_I, [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P,
+    "splat_project_backward_fused": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P,
                                           _P, _P, _P, _P, _I, _P, _I, _I, _P, _P, _P, _P,
                                           _I, _P, _P]),
     "splat_sh_forward": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P]),

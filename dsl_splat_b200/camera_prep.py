@@ -27,8 +27,9 @@ class ViewConfig:
 class _PrepareCameras(torch.autograd.Function):
     @staticmethod
     def forward(ctx: Any, views: Tensor, Ks: Tensor, width: int, height: int, grad_enabled: bool,
-                with_centers: bool):
-        full, inverse, centers = stages.cameras_prepare(views, Ks, width, height, with_centers)
+                with_centers: bool, status_sink: list | None = None):
+        full, inverse, centers = stages.cameras_prepare(views, Ks, width, height, with_centers,
+                                                        status_sink)
         if grad_enabled and ctx.needs_input_grad[0]:
             ctx.save_for_backward(Ks, inverse)
             ctx.width, ctx.height = width, height
@@ -42,27 +43,32 @@ class _PrepareCameras(torch.autograd.Function):
     @once_differentiable
     def backward(ctx: Any, grad_full: Tensor | None, grad_centers: Tensor | None):
         if grad_full is None and grad_centers is None:
-            return (None,) * 6
+            return (None,) * 7
         Ks, inverse = ctx.saved_tensors
         grad_views = stages.cameras_backward(Ks, grad_full, ctx.width, ctx.height, inverse,
                                              grad_centers, ctx.views_shape)
-        return grad_views, None, None, None, None, None
+        return grad_views, None, None, None, None, None, None
 
 
-def _prepare(views, Ks, width, height, with_centers):
+def _prepare(views, Ks, width, height, with_centers, status_sink=None):
     if torch.is_grad_enabled() and Ks.requires_grad:
         raise NotImplementedError("intrinsics gradients are not supported")
-    return _PrepareCameras.apply(views, Ks, width, height, torch.is_grad_enabled(), with_centers)
+    return _PrepareCameras.apply(views, Ks, width, height, torch.is_grad_enabled(), with_centers,
+                                 status_sink)
 
 
-def prepare_cameras(views: Tensor, Ks: Tensor, width: int, height: int) -> Tensor:
-    """Image-plane projection rows full = P V for every camera."""
-    return _prepare(views, Ks, width, height, False)[0]
+def prepare_cameras(views: Tensor, Ks: Tensor, width: int, height: int,
+                    status_sink: list | None = None) -> Tensor:
+    """Image-plane projection rows full = P V for every camera.
+
+    status_sink defers the status read-back (see stages.cameras_prepare)."""
+    return _prepare(views, Ks, width, height, False, status_sink)[0]
 
 
-def prepare_cameras_with_centers(views: Tensor, Ks: Tensor, width: int, height: int):
+def prepare_cameras_with_centers(views: Tensor, Ks: Tensor, width: int, height: int,
+                                 status_sink: list | None = None):
     """Projection rows and camera centres (for SH directions), one launch."""
-    return _prepare(views, Ks, width, height, True)
+    return _prepare(views, Ks, width, height, True, status_sink)
 
 
 def prepare_camera(camera: PinholeCamera, radius_clip: float):

@@ -53,28 +53,41 @@ __global__ void __launch_bounds__(256)
   __syncthreads();
   const int stride = gridDim.x * blockDim.x;
   unsigned long long pairs = 0;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const int radius = radii[i];
+  const uint32_t lt = lanemask_lt();
+  // Every lane of a warp runs the same number of iterations (lanes past n
+  // are predicated off) so the warp-aggregated histogram updates can use
+  // full-warp collectives: depth keys share few top-byte values, and 32
+  // lanes incrementing one shared counter would serialise.
+  const int n_round = (n + 31) & ~31;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_round; i += stride) {
+    const bool valid = i < n;
+    const int radius = valid ? radii[i] : 0;
     uint32_t key = kCulledKey;
-    uint2 rect = make_uint2(0u, 0u);
-    if (radius > 0) {
-      key = __float_as_uint(depths[i]);
-      const float2 c = reinterpret_cast<const float2*>(centers)[i];
-      const int4 b = tile_bounds(c.x, c.y, radius, gx, gy);
-      rect = make_uint2(static_cast<uint32_t>(b.x) | (static_cast<uint32_t>(b.y) << 16),
-                        static_cast<uint32_t>(b.z) | (static_cast<uint32_t>(b.w) << 16));
-      const int row = gx + 1;
-      atomicAdd(diff + b.y * row + b.x, 1);
-      atomicAdd(diff + b.y * row + b.z, -1);
-      atomicAdd(diff + b.w * row + b.x, -1);
-      atomicAdd(diff + b.w * row + b.z, 1);
-      pairs += static_cast<unsigned long long>(max(tiles[i], 0));
+    if (valid) {
+      uint2 rect = make_uint2(0u, 0u);
+      if (radius > 0) {
+        key = __float_as_uint(depths[i]);
+        const float2 c = reinterpret_cast<const float2*>(centers)[i];
+        const int4 b = tile_bounds(c.x, c.y, radius, gx, gy);
+        rect = make_uint2(static_cast<uint32_t>(b.x) | (static_cast<uint32_t>(b.y) << 16),
+                          static_cast<uint32_t>(b.z) | (static_cast<uint32_t>(b.w) << 16));
+        const int row = gx + 1;
+        atomicAdd(diff + b.y * row + b.x, 1);
+        atomicAdd(diff + b.y * row + b.z, -1);
+        atomicAdd(diff + b.w * row + b.x, -1);
+        atomicAdd(diff + b.w * row + b.z, 1);
+        pairs += static_cast<unsigned long long>(max(tiles[i], 0));
+      }
+      keys[i] = key;
+      vals[i] = static_cast<uint32_t>(i);
+      rects[i] = rect;
     }
-    keys[i] = key;
-    vals[i] = static_cast<uint32_t>(i);
-    rects[i] = rect;
 #pragma unroll
-    for (int p = 0; p < 4; ++p) atomicAdd(&s_hist[p * kRadix + ((key >> (8 * p)) & 255u)], 1u);
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t d = valid ? ((key >> (8 * p)) & 255u) : 256u;
+      const uint32_t peers = __match_any_sync(0xffffffffu, d);
+      if (valid && (peers & lt) == 0u) atomicAdd(&s_hist[p * kRadix + d], __popc(peers));
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) pairs += __shfl_xor_sync(0xffffffffu, pairs, o);

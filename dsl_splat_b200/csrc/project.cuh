@@ -208,10 +208,90 @@ SPLAT_DEV float3 sh_eval(const float* __restrict__ coef, float d0, float d1, flo
   return make_float3(v0 + 0.5f, v1 + 0.5f, v2 + 0.5f);
 }
 
+// SH rows are staged per warp through shared memory: each of the warp's 32
+// Gaussians owns a row of kShCols floats there (stride kShCols + 1, so lanes
+// reading their own rows hit distinct banks), and global rows move with
+// consecutive lanes on consecutive addresses.
+constexpr int kProjectBlock = 128;
+constexpr int kProjectWarps = kProjectBlock / 32;
+
+template <int DEG>
+struct ShTile {
+  static constexpr int kCols = DEG >= 0 ? 3 * (DEG + 1) * (DEG + 1) : 1;
+  static constexpr int kStride = kCols + 1;
+};
+
+// rows [base, base+32) of a (n, row_stride) array, first kCols columns.
+template <int DEG>
+SPLAT_DEV void warp_load_sh(const float* __restrict__ src, int row_stride, int base, int n,
+                            float* tile) {
+  constexpr int C = ShTile<DEG>::kCols, S = ShTile<DEG>::kStride;
+  const int lane = threadIdx.x & 31;
+  const int rows = min(32, n - base);
+  if (row_stride == C && rows == 32) {
+    // The warp's rows are one contiguous block of 32*C floats: lane-strided
+    // independent loads, unrolled so many are in flight at once.
+    const float* g = src + static_cast<size_t>(base) * C;
+#pragma unroll 12
+    for (int k = 0; k < C; ++k) {
+      const int e = k * 32 + lane;
+      const int r = e / C;
+      tile[r * S + (e - r * C)] = g[e];
+    }
+  } else {
+    for (int r = 0; r < rows; ++r) {
+      const float* row = src + static_cast<size_t>(base + r) * row_stride;
+      for (int t = lane; t < C; t += 32) tile[r * S + t] = row[t];
+    }
+  }
+  __syncwarp();
+}
+
+// Writes (accumulate: adds) the warp's rows: kCols columns from the tile and
+// zeros for the remaining columns [kCols, row_stride) of each row.
+template <int DEG>
+SPLAT_DEV void warp_store_sh(float* __restrict__ dst, int row_stride, int base, int n,
+                             const float* tile, bool accumulate) {
+  constexpr int C = ShTile<DEG>::kCols, S = ShTile<DEG>::kStride;
+  const int lane = threadIdx.x & 31;
+  __syncwarp();
+  const int rows = min(32, n - base);
+  if (row_stride == C && rows == 32) {
+    float* g = dst + static_cast<size_t>(base) * C;
+#pragma unroll 12
+    for (int k = 0; k < C; ++k) {
+      const int e = k * 32 + lane;
+      const int r = e / C;
+      const float v = tile[r * S + (e - r * C)];
+      if (accumulate)
+        g[e] += v;
+      else
+        g[e] = v;
+    }
+    return;
+  }
+  for (int r = 0; r < rows; ++r) {
+    float* row = dst + static_cast<size_t>(base + r) * row_stride;
+    for (int t = lane; t < row_stride; t += 32) {
+      const float v = t < C ? tile[r * S + t] : 0.0f;
+      if (accumulate)
+        row[t] += v;
+      else
+        row[t] = v;
+    }
+  }
+}
+
 // gs3d/projection.py:89-164 (+ primitives/sh.py:44-79, splatting/metadata.py:12-31)
 template <int DEG>
-__global__ void __launch_bounds__(256) project_forward_kernel(ProjectParams p) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(kProjectBlock) project_forward_kernel(ProjectParams p) {
+  __shared__ float s_sh[kProjectWarps][32 * ShTile<DEG>::kStride];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = (blockIdx.x * kProjectWarps + warp) * 32;
+  if (base >= p.n) return;  // uniform per warp
+  float* tile = s_sh[warp];
+  if (DEG >= 0 && p.sh != nullptr) warp_load_sh<DEG>(p.sh, p.sh_k * 3, base, p.n, tile);
+  const int i = base + lane;
   if (i >= p.n) return;
   const int gx = (p.width + 15) / 16, gy = (p.height + 15) / 16;
   int radius_out = 0, count_out = 0;
@@ -256,7 +336,7 @@ __global__ void __launch_bounds__(256) project_forward_kernel(ProjectParams p) {
         d1 = m1 - p.campos[1];
         d2 = m2 - p.campos[2];
       }
-      v = sh_eval<(DEG < 0 ? 0 : DEG)>(p.sh + static_cast<size_t>(i) * p.sh_k * 3, d0, d1, d2);
+      v = sh_eval<(DEG < 0 ? 0 : DEG)>(tile + lane * ShTile<DEG>::kStride, d0, d1, d2);
     }
     float* col = p.colors + static_cast<size_t>(i) * p.color_stride;
     col[0] = wmax(v.x, 0.0f);
@@ -374,6 +454,45 @@ SPLAT_DEV float3 sh_vjp(const float* __restrict__ coef, int sh_k, float d0, floa
   return dg;
 }
 
+// sh_vjp on a staged row: reads coefficient triple k from `row`, then
+// overwrites it with the coefficient gradient (primitives/sh.py:116-120).
+template <int DEG>
+SPLAT_DEV float3 sh_vjp_row(float* row, float d0, float d1, float d2, float3 cg) {
+  float ux = 0.0f, uy = 0.0f, uz = 0.0f, length = 1.0f;
+  if (DEG > 0) {
+    length = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
+    const float den = wmax(length, W32(1e-12));
+    ux = d0 / den;
+    uy = d1 / den;
+    uz = d2 / den;
+  }
+  float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+#pragma unroll
+  for (int k = 0; k < (DEG + 1) * (DEG + 1); ++k) {
+    const float b = sh_basis(ux, uy, uz, k);
+    if (DEG > 0) {
+      const float w = row[3 * k] * cg.x + row[3 * k + 1] * cg.y + row[3 * k + 2] * cg.z;
+      const float3 bg = sh_basis_grad(ux, uy, uz, k);
+      g0 += w * bg.x;
+      g1 += w * bg.y;
+      g2 += w * bg.z;
+    }
+    row[3 * k] = b * cg.x;
+    row[3 * k + 1] = b * cg.y;
+    row[3 * k + 2] = b * cg.z;
+  }
+  if (DEG == 0) return make_float3(0.0f, 0.0f, 0.0f);
+  const float den = wmax(length, W32(1e-12));
+  float3 dg = make_float3(g0 / den, g1 / den, g2 / den);
+  if (length >= W32(1e-12)) {
+    const float dot = (ux * g0 + uy * g1 + uz * g2) / length;
+    dg.x -= ux * dot;
+    dg.y -= uy * dot;
+    dg.z -= uz * dot;
+  }
+  return dg;
+}
+
 template <int DEG>
 __global__ void sh_backward_kernel(int n, int sh_k, const float* __restrict__ sh,
                                    const float* __restrict__ dirs, const int* __restrict__ radii,
@@ -415,6 +534,9 @@ struct ProjectBackwardParams {
   const float* seed_conics;   // (n,4) dL/dconics (incl. opacity)
   float* grad_means;          // (n,3) or null
   float* grad_quats;          // (n,4) or null
+  // When set, quats are F.normalize(quats_raw) and grad_quats receives the
+  // gradient w.r.t. quats_raw (the normalisation's VJP applied in-kernel).
+  const float* quats_raw;     // (n,4) or null
   float* grad_scales;         // (n,3) or null
   float* grad_opacities;      // (n)   or null
   int accumulate;             // add into grad_* instead of overwriting
@@ -579,97 +701,126 @@ SPLAT_DEV void projection_vjp(const ProjectBackwardParams& p, int i, float m0, f
 }
 
 template <int DEG, bool CAMERA>
-__global__ void __launch_bounds__(256) project_backward_kernel(ProjectBackwardParams p) {
+__global__ void __launch_bounds__(kProjectBlock) project_backward_kernel(ProjectBackwardParams p) {
   constexpr int kCam = 35;
+  constexpr int S = ShTile<DEG>::kStride;
+  __shared__ float s_sh[kProjectWarps][32 * S];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float* tile = s_sh[warp];
+  float* my_row = tile + lane * S;
+  const bool sh_grads = DEG >= 0 && p.grad_sh != nullptr;
   float cam[kCam];
   if (CAMERA) {
 #pragma unroll
     for (int j = 0; j < kCam; ++j) cam[j] = 0.0f;
   }
-  const int stride = gridDim.x * blockDim.x;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += stride) {
-    float gm[3] = {0.0f, 0.0f, 0.0f}, gq[4] = {0.0f, 0.0f, 0.0f, 0.0f}, gs[3] = {0.0f, 0.0f, 0.0f};
-    float go = 0.0f;
-    const bool visible = p.radii[i] > 0;
-    const float m0 = p.means[3 * i], m1 = p.means[3 * i + 1], m2 = p.means[3 * i + 2];
-    if (visible) {
-      float cv_local[16], cp_local[16];
-      if (CAMERA) {
-        projection_vjp(p, i, m0, m1, m2, gm, gq, gs, cam, cam + 16);
-      } else {
-        projection_vjp(p, i, m0, m1, m2, gm, gq, gs, cv_local, cp_local);
-      }
-      go = p.seed_conics[4 * i + 3];
-    }
-    if (DEG >= 0 && p.grad_sh != nullptr) {
-      float* gcoef = p.grad_sh + static_cast<size_t>(i) * p.sh_k * 3;
+  // Warp-uniform loop over chunks of 32 Gaussians (the SH rows of a chunk
+  // are staged in shared memory).
+  const int warps = gridDim.x * kProjectWarps;
+  for (int base = (blockIdx.x * kProjectWarps + warp) * 32; base < p.n; base += warps * 32) {
+    if (sh_grads) warp_load_sh<DEG>(p.sh, p.sh_k * 3, base, p.n, tile);
+    const int i = base + lane;
+    if (i < p.n) {
+      float gm[3] = {0.0f, 0.0f, 0.0f}, gq[4] = {0.0f, 0.0f, 0.0f, 0.0f}, gs[3] = {0.0f, 0.0f, 0.0f};
+      float go = 0.0f;
+      const bool visible = p.radii[i] > 0;
+      const float m0 = p.means[3 * i], m1 = p.means[3 * i + 1], m2 = p.means[3 * i + 2];
       if (visible) {
-        const float* sc = p.seed_colors + static_cast<size_t>(i) * p.color_stride;
-        const float3 cg = make_float3(p.active[3 * i] ? sc[0] : 0.0f, p.active[3 * i + 1] ? sc[1] : 0.0f,
-                                      p.active[3 * i + 2] ? sc[2] : 0.0f);
-        float d0 = m0, d1 = m1, d2 = m2;
-        if (p.campos) {
-          d0 = m0 - p.campos[0];
-          d1 = m1 - p.campos[1];
-          d2 = m2 - p.campos[2];
+        float cv_local[16], cp_local[16];
+        if (CAMERA) {
+          projection_vjp(p, i, m0, m1, m2, gm, gq, gs, cam, cam + 16);
+        } else {
+          projection_vjp(p, i, m0, m1, m2, gm, gq, gs, cv_local, cp_local);
         }
-        const float3 dd = sh_vjp<(DEG < 0 ? 0 : DEG)>(p.sh + static_cast<size_t>(i) * p.sh_k * 3, p.sh_k,
-                                                      d0, d1, d2, cg, gcoef, p.accumulate != 0);
-        if (DEG > 0) {
-          gm[0] += dd.x;
-          gm[1] += dd.y;
-          gm[2] += dd.z;
-          if (CAMERA && p.campos) {
-            cam[32] -= dd.x;
-            cam[33] -= dd.y;
-            cam[34] -= dd.z;
+        go = p.seed_conics[4 * i + 3];
+        if (p.quats_raw) {
+          // VJP of F.normalize(x) = x / max(|x|, 1e-12) (inputs.py:252):
+          // (g - n (n . g)) / |x|, or g / 1e-12 where the norm is clamped.
+          const float4 x = reinterpret_cast<const float4*>(p.quats_raw)[i];
+          const float norm = sqrtf(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+          if (norm > W32(1e-12)) {
+            const float4 n = reinterpret_cast<const float4*>(p.quats)[i];
+            const float d = n.x * gq[0] + n.y * gq[1] + n.z * gq[2] + n.w * gq[3];
+            gq[0] = (gq[0] - n.x * d) / norm;
+            gq[1] = (gq[1] - n.y * d) / norm;
+            gq[2] = (gq[2] - n.z * d) / norm;
+            gq[3] = (gq[3] - n.w * d) / norm;
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) gq[k] = gq[k] / W32(1e-12);
           }
         }
-      } else if (!p.accumulate) {
-        for (int k = 0; k < 3 * p.sh_k; ++k) gcoef[k] = 0.0f;
+      }
+      if (sh_grads) {
+        if (visible) {
+          const float* sc = p.seed_colors + static_cast<size_t>(i) * p.color_stride;
+          const float3 cg = make_float3(p.active[3 * i] ? sc[0] : 0.0f,
+                                        p.active[3 * i + 1] ? sc[1] : 0.0f,
+                                        p.active[3 * i + 2] ? sc[2] : 0.0f);
+          float d0 = m0, d1 = m1, d2 = m2;
+          if (p.campos) {
+            d0 = m0 - p.campos[0];
+            d1 = m1 - p.campos[1];
+            d2 = m2 - p.campos[2];
+          }
+          const float3 dd = sh_vjp_row<(DEG < 0 ? 0 : DEG)>(my_row, d0, d1, d2, cg);
+          if (DEG > 0) {
+            gm[0] += dd.x;
+            gm[1] += dd.y;
+            gm[2] += dd.z;
+            if (CAMERA && p.campos) {
+              cam[32] -= dd.x;
+              cam[33] -= dd.y;
+              cam[34] -= dd.z;
+            }
+          }
+        } else {
+          for (int k = 0; k < ShTile<DEG>::kCols; ++k) my_row[k] = 0.0f;
+        }
+      }
+      if (p.accumulate) {
+        if (p.grad_means) {
+          p.grad_means[3 * i] += gm[0];
+          p.grad_means[3 * i + 1] += gm[1];
+          p.grad_means[3 * i + 2] += gm[2];
+        }
+        if (p.grad_quats) {
+          float4* o = reinterpret_cast<float4*>(p.grad_quats) + i;
+          float4 v = *o;
+          v.x += gq[0];
+          v.y += gq[1];
+          v.z += gq[2];
+          v.w += gq[3];
+          *o = v;
+        }
+        if (p.grad_scales) {
+          p.grad_scales[3 * i] += gs[0];
+          p.grad_scales[3 * i + 1] += gs[1];
+          p.grad_scales[3 * i + 2] += gs[2];
+        }
+        if (p.grad_opacities) p.grad_opacities[i] += go;
+      } else {
+        if (p.grad_means) {
+          p.grad_means[3 * i] = gm[0];
+          p.grad_means[3 * i + 1] = gm[1];
+          p.grad_means[3 * i + 2] = gm[2];
+        }
+        if (p.grad_quats) reinterpret_cast<float4*>(p.grad_quats)[i] = make_float4(gq[0], gq[1], gq[2], gq[3]);
+        if (p.grad_scales) {
+          p.grad_scales[3 * i] = gs[0];
+          p.grad_scales[3 * i + 1] = gs[1];
+          p.grad_scales[3 * i + 2] = gs[2];
+        }
+        if (p.grad_opacities) p.grad_opacities[i] = go;
       }
     }
-    if (p.accumulate) {
-      if (p.grad_means) {
-        p.grad_means[3 * i] += gm[0];
-        p.grad_means[3 * i + 1] += gm[1];
-        p.grad_means[3 * i + 2] += gm[2];
-      }
-      if (p.grad_quats) {
-        float4* o = reinterpret_cast<float4*>(p.grad_quats) + i;
-        float4 v = *o;
-        v.x += gq[0];
-        v.y += gq[1];
-        v.z += gq[2];
-        v.w += gq[3];
-        *o = v;
-      }
-      if (p.grad_scales) {
-        p.grad_scales[3 * i] += gs[0];
-        p.grad_scales[3 * i + 1] += gs[1];
-        p.grad_scales[3 * i + 2] += gs[2];
-      }
-      if (p.grad_opacities) p.grad_opacities[i] += go;
-    } else {
-      if (p.grad_means) {
-        p.grad_means[3 * i] = gm[0];
-        p.grad_means[3 * i + 1] = gm[1];
-        p.grad_means[3 * i + 2] = gm[2];
-      }
-      if (p.grad_quats) reinterpret_cast<float4*>(p.grad_quats)[i] = make_float4(gq[0], gq[1], gq[2], gq[3]);
-      if (p.grad_scales) {
-        p.grad_scales[3 * i] = gs[0];
-        p.grad_scales[3 * i + 1] = gs[1];
-        p.grad_scales[3 * i + 2] = gs[2];
-      }
-      if (p.grad_opacities) p.grad_opacities[i] = go;
-    }
+    if (sh_grads) warp_store_sh<DEG>(p.grad_sh, p.sh_k * 3, base, p.n, tile, p.accumulate != 0);
+    __syncwarp();
   }
   if (CAMERA) {
     // Warp shuffles, then warp leaders through shared memory, then one
     // atomic per entry per block (gs3d/projection.py:269-283).
-    __shared__ float s_cam[8][kCam];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    __shared__ float s_cam[kProjectWarps][kCam];
 #pragma unroll
     for (int j = 0; j < kCam; ++j) {
       const float v = warp_sum(cam[j]);

@@ -131,7 +131,7 @@ T* at(void* base, size_t off) {
 
 template <int DEG>
 void launch_project_forward(const ProjectParams& p, cudaStream_t s) {
-  project_forward_kernel<DEG><<<blocks_for(p.n, 256), 256, 0, counted(s)>>>(p);
+  project_forward_kernel<DEG><<<blocks_for(p.n, kProjectBlock), kProjectBlock, 0, counted(s)>>>(p);
 }
 
 int project_forward_dispatch(const ProjectParams& p, cudaStream_t s) {
@@ -156,9 +156,11 @@ void launch_project_backward(const ProjectBackwardParams& p, cudaStream_t s) {
   int dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  unsigned grid = blocks_for(p.n, 256);
-  if (CAMERA) grid = grid < static_cast<unsigned>(sms * 8) ? grid : static_cast<unsigned>(sms * 8);
-  project_backward_kernel<DEG, CAMERA><<<grid, 256, 0, counted(s)>>>(p);
+  unsigned grid = blocks_for(p.n, kProjectBlock);
+  // With camera gradients each block ends in one atomic per camera entry:
+  // cap the grid (warps then loop over several chunks of 32 Gaussians).
+  if (CAMERA) grid = std::min(grid, static_cast<unsigned>(sms * 16));
+  project_backward_kernel<DEG, CAMERA><<<grid, kProjectBlock, 0, counted(s)>>>(p);
 }
 
 template <bool CAMERA>
@@ -383,7 +385,8 @@ int splat_project_backward(int n, const float* means, const float* quats, const 
 }
 
 int splat_project_backward_fused(int n, const float* means, const float* quats,
-                                 const float* scales, const float* view, const float* proj,
+                                 const float* quats_raw, const float* scales,
+                                 const float* view, const float* proj,
                                  const float* K, int width, int height, const int* radii,
                                  const float* grad_centers, const float* grad_conics,
                                  float* grad_means, float* grad_quats, float* grad_scales,
@@ -395,7 +398,8 @@ int splat_project_backward_fused(int n, const float* means, const float* quats,
   if (grad_sh && (!sh || !active || !grad_colors || sh_degree < 0 || sh_degree > 3 ||
                   sh_k < (sh_degree + 1) * (sh_degree + 1)))
     return fail(kInvalidArgument, "bad SH backward arguments");
-  if (!aligned(quats, 16) || !aligned(grad_quats, 16) || !aligned(grad_conics, 16) ||
+  if (!aligned(quats, 16) || !aligned(quats_raw, 16) || !aligned(grad_quats, 16) ||
+      !aligned(grad_conics, 16) ||
       !aligned(grad_centers, 8))
     return fail(kInvalidArgument, "quat/conic rows need 16-byte, center rows 8-byte alignment");
   ProjectBackwardParams p{};
@@ -425,6 +429,7 @@ int splat_project_backward_fused(int n, const float* means, const float* quats,
   p.seed_colors = grad_colors;
   p.color_stride = color_stride;
   p.grad_sh = grad_sh;
+  p.quats_raw = quats_raw;
   return project_backward_dispatch(p, as_stream(stream));
 }
 

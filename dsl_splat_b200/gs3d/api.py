@@ -14,6 +14,7 @@ from numbers import Integral
 from typing import Any, Sequence
 
 import torch
+import torch.nn.functional as F
 from torch import Tensor
 
 from ..camera_prep import ViewConfig, prepare_cameras, prepare_cameras_with_centers
@@ -91,14 +92,22 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
     validate_tile_mode(tile_mode)
     validate_camera_options(width, height, near_plane, far_plane, radius_clip)
     sh_degree = _check_sh(sh_coeffs, sh_degree, features)
+    # Quaternions are normalised per batch below (the same Torch op as
+    # inputs.py:252) outside autograd; ProjectView applies its VJP in-kernel.
     layout = normalize_inputs(means, quats, scales, opacities,
                               features if sh_coeffs is None else sh_coeffs, viewmats, Ks,
-                              backgrounds, extra_features, None, sh_degree)
+                              backgrounds, extra_features, None, sh_degree,
+                              normalize_quats=False)
     with_centers = sh_degree is not None and sh_degree > 0
+    # Camera status codes are read in the same host synchronisation as the
+    # pair counts below (one read per call instead of two).
+    camera_status: list = []
     if with_centers:
-        full, centers = prepare_cameras_with_centers(layout.viewmats, layout.Ks, width, height)
+        full, centers = prepare_cameras_with_centers(layout.viewmats, layout.Ks, width, height,
+                                                     camera_status)
     else:
-        full, centers = prepare_cameras(layout.viewmats, layout.Ks, width, height), None
+        full = prepare_cameras(layout.viewmats, layout.Ks, width, height, camera_status)
+        centers = None
     config = ViewConfig(width, height, near_plane, far_plane, radius_clip, tile_mode)
     grad_enabled = torch.is_grad_enabled()
     frames = []
@@ -107,14 +116,17 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
     for b in range(layout.batch_count):
         bm, bq = layout.means[b], layout.quats[b]
         bs, bo = layout.scales[b], layout.opacities[b]
+        with torch.no_grad():
+            bqn = F.normalize(bq, dim=-1)
         for c in range(layout.cameras):
             view = batch_item(batch_item(layout.viewmats, b), c)
             proj = batch_item(batch_item(full, b), c)
             K = batch_item(batch_item(layout.Ks, b), c)
             campos = batch_item(batch_item(centers, b), c) if with_centers else None
             values = layout.colors.at(b, c)
-            out = ProjectView.apply(bm, bq, bs, bo, values if sh_degree is not None else None,
-                                    view, proj, campos, K, config, sh_degree, grad_enabled)
+            out = ProjectView.apply(bm, bq, bqn, bs, bo,
+                                    values if sh_degree is not None else None, view, proj,
+                                    campos, K, config, sh_degree, grad_enabled)
             ctr, con, col, radii, tiles, depths, m2d, mop, mcon = out
             colors = col if sh_degree is not None else values
             extras = None if layout.extras is None else layout.extras.at(b, c)
@@ -142,7 +154,7 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
                            batch_count=layout.batch_count, cameras=layout.cameras, n=layout.n,
                            width=width, height=height, device=layout.device)
         if statistics else ([], {}))
-    bins = stages.bin_and_sort_many([f[7] for f in frames], width, height)
+    bins = stages.bin_and_sort_many([f[7] for f in frames], width, height, camera_status)
     channels = layout.colors.channels
     images = []
     for i, (b, c, ctr, con, colors, extras, bg, _state) in enumerate(frames):

@@ -23,13 +23,20 @@ from ..training import AbsGradientTarget
 
 
 class ProjectView(torch.autograd.Function):
-    """Projection + masked SH + metadata for one view (gs3d/api.py:145-189)."""
+    """Projection + masked SH + metadata for one view (gs3d/api.py:145-189).
+
+    quats_raw is the caller's quaternion tensor and quats its F.normalize
+    (computed by the caller without autograd, inputs.py:252); the backward
+    kernel applies the normalisation's VJP, so the gradient reaches
+    quats_raw without Torch's elementwise backward kernels."""
 
     @staticmethod
-    def forward(ctx: Any, means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor,
-                sh: Tensor | None, view: Tensor, full: Tensor, campos: Tensor | None,
-                intrinsics: Tensor, config: ViewConfig, sh_degree: int, grad_enabled: bool):
+    def forward(ctx: Any, means: Tensor, quats_raw: Tensor, quats: Tensor, scales: Tensor,
+                opacities: Tensor, sh: Tensor | None, view: Tensor, full: Tensor,
+                campos: Tensor | None, intrinsics: Tensor, config: ViewConfig, sh_degree: int,
+                grad_enabled: bool):
         means, quats, scales = means.contiguous(), quats.contiguous(), scales.contiguous()
+        quats_raw = quats_raw.contiguous()
         out = stages.project_fused(
             means, quats, scales, opacities.contiguous(), view.contiguous(), full.contiguous(),
             intrinsics.contiguous(), config.width, config.height, config.near, config.far,
@@ -38,9 +45,9 @@ class ProjectView(torch.autograd.Function):
             need_active=grad_enabled)
         st = out.state
         colors = out.colors if out.colors is not None else means.new_empty((0, 3))
-        if grad_enabled and any(ctx.needs_input_grad[:8]):
-            ctx.save_for_backward(means, quats, scales, view, full, intrinsics, st.radii,
-                                  None if sh is None else sh.contiguous(),
+        if grad_enabled and any(ctx.needs_input_grad[:9]):
+            ctx.save_for_backward(means, quats, quats_raw, scales, view, full, intrinsics,
+                                  st.radii, None if sh is None else sh.contiguous(),
                                   None if campos is None else campos.contiguous(), out.active)
             ctx.config, ctx.sh_degree = config, sh_degree or 0
         ctx.mark_non_differentiable(st.radii, st.tile_counts, st.depths, out.means2d,
@@ -55,8 +62,11 @@ class ProjectView(torch.autograd.Function):
     @once_differentiable
     def backward(ctx: Any, g_centers, g_conics, g_colors, *unused):
         if g_centers is None and g_conics is None and g_colors is None:
-            return (None,) * 12
-        means, quats, scales, view, full, intrinsics, radii, sh, campos, active = ctx.saved_tensors
+            return (None,) * 13
+        (means, quats, quats_raw, scales, view, full, intrinsics, radii, sh, campos,
+         active) = ctx.saved_tensors
+        # inputs: 0 means, 1 quats_raw, 2 quats (no grad), 3 scales, 4 opacities,
+        # 5 sh, 6 view, 7 full, 8 campos
         needs = ctx.needs_input_grad
         n = len(means)
         cfg = ctx.config
@@ -64,12 +74,12 @@ class ProjectView(torch.autograd.Function):
         g_conics = torch.zeros((n, 4), device=means.device) if g_conics is None else g_conics.contiguous()
         gm = torch.empty_like(means) if needs[0] else None
         gq = torch.empty_like(quats) if needs[1] else None
-        gs = torch.empty_like(scales) if needs[2] else None
-        go = means.new_empty(n) if needs[3] else None
+        gs = torch.empty_like(scales) if needs[3] else None
+        go = means.new_empty(n) if needs[4] else None
         gsh = None
-        if sh is not None and (needs[4] or (needs[0] and ctx.sh_degree > 0) or needs[7]):
+        if sh is not None and (needs[5] or (needs[0] and ctx.sh_degree > 0) or needs[8]):
             gsh = torch.empty_like(sh)
-        want_cam = needs[5] or needs[6] or needs[7]
+        want_cam = needs[6] or needs[7] or needs[8]
         cam = means.new_zeros(35) if want_cam else None
         if gsh is not None:
             gcol = (torch.zeros((n, 3), device=means.device) if g_colors is None
@@ -79,16 +89,16 @@ class ProjectView(torch.autograd.Function):
         if n:
             pin = stages.Args()
             check(lib.splat_project_backward_fused(
-                n, pin(means), pin(quats), pin(scales), pin(view), pin(full), pin(intrinsics),
-                cfg.width, cfg.height, pin(radii), pin(g_centers), pin(g_conics), ptr(gm),
-                ptr(gq), ptr(gs), ptr(go), 0, ptr(cam), ctx.sh_degree,
+                n, pin(means), pin(quats), pin(quats_raw), pin(scales), pin(view), pin(full),
+                pin(intrinsics), cfg.width, cfg.height, pin(radii), pin(g_centers),
+                pin(g_conics), ptr(gm), ptr(gq), ptr(gs), ptr(go), 0, ptr(cam), ctx.sh_degree,
                 0 if sh is None else sh.shape[1], pin(sh), pin(campos), pin(active), pin(gcol), 3,
                 ptr(gsh), stream(means.device)), "project_backward_fused")
-        gview = cam[:16].reshape(4, 4) if needs[5] else None
-        gfull = cam[16:32].reshape(4, 4) if needs[6] else None
-        gcampos = cam[32:35].clone() if needs[7] else None
-        return (gm, gq, gs, go, gsh if needs[4] else None, gview, gfull, gcampos, None, None,
-                None, None)
+        gview = cam[:16].reshape(4, 4) if needs[6] else None
+        gfull = cam[16:32].reshape(4, 4) if needs[7] else None
+        gcampos = cam[32:35].clone() if needs[8] else None
+        return (gm, gq, None, gs, go, gsh if needs[5] else None, gview, gfull, gcampos, None,
+                None, None, None)
 
 
 class RenderView(torch.autograd.Function):

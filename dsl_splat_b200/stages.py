@@ -108,8 +108,24 @@ class RenderedPixels:
 
 # ---- cameras ---------------------------------------------------------------
 
-def cameras_prepare(views: Tensor, Ks: Tensor, width: int, height: int, with_centers: bool):
-    """splatting/cameras.py:133-188: full (…,4,4), inverse (C,4,4), centers (…,3)."""
+def raise_camera_errors(codes) -> None:
+    """splatting/cameras.py:170-180: the reference's exceptions for status codes."""
+    if 2 in codes:
+        raise ValueError("Ks must be finite with positive fx/fy")
+    if 1 in codes:
+        raise NotImplementedError("Ks must be a zero-skew pinhole intrinsic matrix")
+    if 3 in codes:
+        raise torch.linalg.LinAlgError("viewmats must be invertible for SH directions")
+
+
+def cameras_prepare(views: Tensor, Ks: Tensor, width: int, height: int, with_centers: bool,
+                    status_sink: list | None = None):
+    """splatting/cameras.py:133-188: full (…,4,4), inverse (C,4,4), centers (…,3).
+
+    Only status codes cross to the host, as in the reference.  With a
+    status_sink the (C,) int32 codes are appended to it instead of being read
+    now, so the caller can fold that read into its next host synchronisation
+    (bin_and_sort_many does) and raise the same exceptions there."""
     views_c, Ks_c = views.reshape(-1, 4, 4).contiguous(), Ks.reshape(-1, 3, 3).contiguous()
     count = len(views_c)
     full = torch.empty(views.shape, dtype=torch.float32, device=views.device)
@@ -120,14 +136,10 @@ def cameras_prepare(views: Tensor, Ks: Tensor, width: int, height: int, with_cen
                                     ptr(full), ptr(inverse) if with_centers else None,
                                     ptr(centers) if with_centers else None, ptr(errors),
                                     _stream(views)), "cameras_prepare")
-    # Only status codes cross to the host, as in the reference.
-    codes = errors.tolist()
-    if 2 in codes:
-        raise ValueError("Ks must be finite with positive fx/fy")
-    if 1 in codes:
-        raise NotImplementedError("Ks must be a zero-skew pinhole intrinsic matrix")
-    if 3 in codes:
-        raise torch.linalg.LinAlgError("viewmats must be invertible for SH directions")
+    if status_sink is not None:
+        status_sink.append(errors)
+    else:
+        raise_camera_errors(errors.tolist())
     return full, inverse, centers
 
 
@@ -320,12 +332,25 @@ class BinPlan:
         return ids
 
 
-def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int):
-    """Bin several views with one host read of all pair counts."""
+def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
+                      camera_status: list | None = None):
+    """Bin several views with one host read of all pair counts.
+
+    camera_status: deferred camera status tensors (cameras_prepare's
+    status_sink); they are read in the same synchronisation and their errors
+    raised before any pair is emitted."""
     plans = [BinPlan(s, width, height) for s in states]
-    if not plans:
+    parts = [p.pairs_dev for p in plans]
+    ncodes = 0
+    if camera_status:
+        codes_dev = torch.cat([c.to(torch.int64) for c in camera_status])
+        ncodes = len(codes_dev)
+        parts = [codes_dev] + parts
+    if not parts:
         return []
-    counts = torch.cat([p.pairs_dev for p in plans]).tolist()
+    values = torch.cat(parts).tolist()
+    raise_camera_errors(values[:ncodes])
+    counts = values[ncodes:]
     return [dict(point_list=p.emit(int(m)), ranges=p.ranges) for p, m in zip(plans, counts)]
 
 

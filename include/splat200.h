@@ -92,9 +92,13 @@ int splat_project_backward(int n, const float* means, const float* quats, const 
  * (stride color_stride) give dL/dcolors, the direction gradient is added to
  * grad_means and, negated, to camera_grads[32..34] (d campos).  accumulate
  * != 0 adds into all per-Gaussian outputs (multi-view sums); camera_grads is
- * NULL or float[35] (view 16, proj 16, campos 3), always added into. */
+ * NULL or float[35] (view 16, proj 16, campos 3), always added into.
+ * quats_raw: NULL, or the unnormalised quaternions whose F.normalize gave
+ * quats (inputs.py:252); grad_quats then receives the gradient w.r.t.
+ * quats_raw (the normalisation's VJP is applied in the kernel). */
 int splat_project_backward_fused(int n, const float* means, const float* quats,
-                                 const float* scales, const float* view, const float* proj,
+                                 const float* quats_raw, const float* scales,
+                                 const float* view, const float* proj,
                                  const float* K, int width, int height, const int* radii,
                                  const float* grad_centers, const float* grad_conics,
                                  float* grad_means, float* grad_quats, float* grad_scales,
