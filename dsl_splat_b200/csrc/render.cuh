@@ -9,9 +9,10 @@
 //
 // Two exact shortcuts keep the blend off samples that cannot contribute:
 //  * power below a per-Gaussian cutoff (alpha < 0.951/255 there) skips exp;
-//  * a warp skips a staged Gaussian whose cutoff ellipse, padded by one
-//    pixel, misses the warp's 8x4 pixels -- one uniform test per warp
-//    instead of 32 sample evaluations.
+//  * a warp skips a staged Gaussian whose cutoff ellipse misses the warp's
+//    8x4 pixel centres (padded box test, then the exact ellipse-rectangle
+//    test of footprint.cuh) -- one test per (warp, Gaussian), evaluated 32
+//    Gaussians at a time, instead of 32 sample evaluations.
 // Neither changes any decision: a skipped sample's alpha is below 1/255.
 //
 // Backward replays each pixel from its last contributor.  Per-sample
@@ -19,6 +20,7 @@
 // 16 values in 16 shuffles -- after which 16 lanes each hold one total and
 // issue one red.global.add.f32 together.
 #pragma once
+#include "footprint.cuh"
 #include "splat_common.cuh"
 
 namespace splat {
@@ -84,14 +86,31 @@ struct RenderShared {
   float4 geom[kBlock];     // centre x, centre y, padded half extents of the cutoff ellipse
   float4 conic[kBlock];    // inv_a, inv_b, inv_c, opacity
   float cut[kBlock];       // power below which alpha < 1/255 for certain
-  float feat[CHP][kBlock];
+  float4 bound[kBlock];    // EllipseBound ra, rc, level (w unused)
+  float4 feat[kBlock][CHP / 4];  // channels of one slot, read with vector loads
 };
 
+// All CHP channels of staged slot j (padding channels are zero).
+template <int CHP>
+SPLAT_DEV void load_features(const RenderShared<CHP>& s, int j, float (&f)[CHP]) {
+#pragma unroll
+  for (int c4 = 0; c4 < CHP / 4; ++c4) {
+    const float4 v = s.feat[j][c4];
+    f[4 * c4] = v.x;
+    f[4 * c4 + 1] = v.y;
+    f[4 * c4 + 2] = v.z;
+    f[4 * c4 + 3] = v.w;
+  }
+}
+
 // Skipping samples with power < cut never changes a decision: alpha would
-// be below 0.951/255 there (exp error < 1 ulp, log error < 1 ulp).
+// be below 0.951/255 there (exp error < 1 ulp, log error < 1 ulp), and at
+// power <= -80 splat_expf is 0 (alpha 0 or NaN, rejected either way).  So
+// every evaluated sample has power in [cut, 0] with cut > -80, where
+// splat_expf_core gives the same bits as splat_expf.
 SPLAT_DEV float power_cutoff(float opacity) {
   if (!(opacity > 0.0f)) return 1.0f;  // alpha == 0: skip every sample
-  return __logf(1.0f / (255.0f * opacity)) - 0.05f;
+  return fmaxf(__logf(1.0f / (255.0f * opacity)) - 0.05f, -79.99999f);
 }
 
 // Half extents of {power >= cut} = {a dx^2 + 2 b dx dy + c dy^2 <= -2 cut},
@@ -118,8 +137,9 @@ SPLAT_DEV void stage_gaussian(const RenderParams& p, RenderShared<CHP>& s, int s
     s.geom[slot] = make_float4(0.0f, 0.0f, -1e30f, -1e30f);
     s.conic[slot] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     s.cut[slot] = 1.0f;
+    s.bound[slot] = make_float4(0.0f, 0.0f, -1.0f, 0.0f);
 #pragma unroll
-    for (int c = 0; c < CHP; ++c) s.feat[c][slot] = 0.0f;
+    for (int c4 = 0; c4 < CHP / 4; ++c4) s.feat[slot][c4] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     return;
   }
   s.id[slot] = g;
@@ -130,18 +150,23 @@ SPLAT_DEV void stage_gaussian(const RenderParams& p, RenderShared<CHP>& s, int s
   s.geom[slot] = make_float4(xy.x, xy.y, ext.x, ext.y);
   s.conic[slot] = q;
   s.cut[slot] = cut;
+  const EllipseBound e = ellipse_bound(q.x, q.y, q.z, cut);
+  s.bound[slot] = make_float4(e.ra, e.rc, e.level, 0.0f);
   const float* a = p.feat_a + static_cast<size_t>(g) * p.stride_a;
+  float v[CHP];
 #pragma unroll
   for (int c = 0; c < CHP; ++c) {
-    float v = 0.0f;
+    v[c] = 0.0f;
     if (c < p.ch_a)
-      v = a[c];
+      v[c] = a[c];
     else if (c < p.ch_a + p.ch_b)
-      v = p.feat_b[static_cast<size_t>(g) * p.stride_b + (c - p.ch_a)];
+      v[c] = p.feat_b[static_cast<size_t>(g) * p.stride_b + (c - p.ch_a)];
     else if (c < p.channels)
-      v = 1.0f;
-    s.feat[c][slot] = v;
+      v[c] = 1.0f;
   }
+#pragma unroll
+  for (int c4 = 0; c4 < CHP / 4; ++c4)
+    s.feat[slot][c4] = make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
 }
 
 // The reference's sample exponent, operation for operation (no contraction):
@@ -150,42 +175,60 @@ SPLAT_DEV float sample_power(float4 q, float dx, float dy) {
   return (-0.5f * (q.x * dx * dx + q.z * dy * dy)) - q.y * dx * dy;
 }
 
-// Pixel of thread t in tile `tile`: warp w covers the 8x4 block at
-// ((w % 2) * 8, (w / 2) * 4) of the 16x16 tile.
+// Pixels of a lane: warp w owns the 8 x 4*PX block at ((w % 2) * 8,
+// (w / 2) * 4 * PX) of the 16x16 tile, and lane l the PX pixels
+// (l % 8, l / 8 + 4 i), i < PX.  The forward uses PX = 1 (eight warps per
+// tile); the 4-channel backward PX = 2 (four warps, two pixels per lane).
+template <int PX>
 struct PixelSlot {
-  int x, y;
-  float wcx, wcy;  // centre of the warp's 8x4 block
+  int x, y;        // first pixel of the lane (the others are y + 4 i)
+  float wcx, wcy;  // centre of the warp's block
+  float wx0, wy0;  // its first pixel centre
 };
 
-SPLAT_DEV PixelSlot pixel_slot(int tile, int gx) {
+template <int PX>
+SPLAT_DEV PixelSlot<PX> pixel_slot(int tile, int gx) {
   const int t = threadIdx.x, warp = t >> 5, wl = t & 31;
   const int wx0 = (tile % gx) * kTile + (warp & 1) * 8;
-  const int wy0 = (tile / gx) * kTile + (warp >> 1) * 4;
-  PixelSlot s;
+  const int wy0 = (tile / gx) * kTile + (warp >> 1) * 4 * PX;
+  PixelSlot<PX> s;
   s.x = wx0 + (wl & 7);
   s.y = wy0 + (wl >> 3);
   s.wcx = static_cast<float>(wx0) + 3.5f;
-  s.wcy = static_cast<float>(wy0) + 1.5f;
+  s.wcy = static_cast<float>(wy0) + 0.5f * (4 * PX - 1);
+  s.wx0 = static_cast<float>(wx0);
+  s.wy0 = static_cast<float>(wy0);
   return s;
 }
 
-// True when the staged Gaussian cannot reach any pixel of this warp.
-SPLAT_DEV bool misses_warp(float4 geom, const PixelSlot& ps) {
-  return fabsf(geom.x - ps.wcx) > geom.z + 3.5f || fabsf(geom.y - ps.wcy) > geom.w + 1.5f;
+// True when staged slot j cannot reach any pixel of this warp: its padded
+// cutoff box misses the warp's block, or (exact test) the minimum of its
+// quadratic form over the block's pixel centres exceeds the cutoff level.
+template <int CHP, int PX>
+SPLAT_DEV bool misses_warp(const RenderShared<CHP>& s, int j, const PixelSlot<PX>& ps) {
+  constexpr float kHalfH = 0.5f * (4 * PX - 1);
+  const float4 geom = s.geom[j];
+  if (fabsf(geom.x - ps.wcx) > geom.z + 3.5f || fabsf(geom.y - ps.wcy) > geom.w + kHalfH)
+    return true;
+  const float4 q = s.conic[j];
+  const float4 b = s.bound[j];
+  const EllipseBound e{b.x, b.y, b.z};
+  const float u0 = ps.wx0 - geom.x, v0 = ps.wy0 - geom.y;
+  return rectangle_min_form(q.x, q.y, q.z, e, u0, u0 + 7.0f, v0, v0 + 2.0f * kHalfH) > e.level;
 }
 
 // Ordered list of the staged slots in [j0, count) that can reach this warp's
 // pixels, built with ballots (8 candidates per lane for a full batch).
 // Returns its length; the list lives in `list` (per warp).
-template <int CHP>
-SPLAT_DEV int warp_candidates(const RenderShared<CHP>& s, const PixelSlot& ps, int j0, int count,
-                              uint8_t* list) {
+template <int CHP, int PX>
+SPLAT_DEV int warp_candidates(const RenderShared<CHP>& s, const PixelSlot<PX>& ps, int j0,
+                              int count, uint8_t* list) {
   const int wl = threadIdx.x & 31;
   const uint32_t lt = lanemask_lt();
   int n = 0;
   for (int base = j0; base < count; base += 32) {
     const int j = base + wl;
-    const bool keep = j < count && !misses_warp(s.geom[j], ps);
+    const bool keep = j < count && !misses_warp(s, j, ps);
     const uint32_t b = __ballot_sync(0xffffffffu, keep);
     if (keep) list[n + __popc(b & lt)] = static_cast<uint8_t>(j);
     n += __popc(b);
@@ -196,11 +239,12 @@ SPLAT_DEV int warp_candidates(const RenderShared<CHP>& s, const PixelSlot& ps, i
 
 template <int CHP>
 __global__ void __launch_bounds__(kBlock) render_forward_kernel(RenderParams p) {
-  __shared__ RenderShared<CHP> s;
+  extern __shared__ float4 s_dynamic[];  // the staged batch (sizeof(RenderShared<CHP>) bytes)
+  RenderShared<CHP>& s = *reinterpret_cast<RenderShared<CHP>*>(s_dynamic);
   __shared__ uint8_t s_list[kBlock / 32][kBlock];
   uint8_t* list = s_list[threadIdx.x >> 5];
   const int tile = blockIdx.x;
-  const PixelSlot ps = pixel_slot(tile, p.gx);
+  const PixelSlot<1> ps = pixel_slot<1>(tile, p.gx);
   const int x = ps.x, y = ps.y;
   const bool inside = x < p.width && y < p.height;
   const float fx = static_cast<float>(x), fy = static_cast<float>(y);
@@ -227,17 +271,19 @@ __global__ void __launch_bounds__(kBlock) render_forward_kernel(RenderParams p) 
       const float dx = gm.x - fx, dy = gm.y - fy;
       const float power = sample_power(q, dx, dy);
       if (power > 0.0f || power < s.cut[j]) continue;
-      const float alpha = wmin(W32(0.99), q.w * splat_expf(power));
+      const float alpha = wmin(W32(0.99), q.w * splat_expf_core(power));
       if (!(alpha >= threshold)) continue;
       const float next_t = T * (1.0f - alpha);
-      if (next_t < W32(0.0001)) {
+      if (next_t < W32(0.0001)) {  // ends the pixel without being blended
         done = true;
         break;
       }
       const float w = alpha * T;
+      float f[CHP];
+      load_features(s, j, f);
+      // padding channels are staged as zero: accumulating them is harmless
 #pragma unroll
-      for (int c = 0; c < CHP; ++c)
-        if (c < p.channels) color[c] = __fmaf_rn(s.feat[c][j], w, color[c]);
+      for (int c = 0; c < CHP; ++c) color[c] = __fmaf_rn(f[c], w, color[c]);
       if (p.stat_count) observe(p, s.id[j], y * p.width + x, w);
       T = next_t;
       last_contributor = begin - first + j + 1;
@@ -292,70 +338,197 @@ SPLAT_DEV int butterfly_index(int lane) {
   return ((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
 }
 
-// Destination of gradient value k of Gaussian g: 0-1 centre, 2-5 conic
-// (incl. opacity), 6-7 |centre| sums, 8+c feature channel c.
-SPLAT_DEV float* gradient_slot(const RenderParams& p, int g, int k, int grad_channels) {
-  if (k < 2) return p.grad_centers + 2 * static_cast<size_t>(g) + k;
-  if (k < 6) return p.grad_conics + 4 * static_cast<size_t>(g) + (k - 2);
-  if (k < 8) return p.abs_centers ? p.abs_centers + 2 * static_cast<size_t>(g) + (k - 6) : nullptr;
-  const int c = k - 8;
-  if (c >= grad_channels) return nullptr;
-  if (c < p.ch_a) return p.grad_a ? p.grad_a + static_cast<size_t>(g) * p.ch_a + c : nullptr;
-  if (c < p.ch_a + p.ch_b)
-    return p.grad_b ? p.grad_b + static_cast<size_t>(g) * p.ch_b + (c - p.ch_a) : nullptr;
-  return nullptr;
+// The same reduction for 12 values (6 + 3 + 2 + 1 + 1 shuffles): pairs
+// (i, i+6), then (i, i+3), then (i, i+2) with a zero fourth value, then
+// (0, 1).  Returns in every lane the warp total of value
+// butterfly12_index(lane); lanes whose index is 12 hold the padding.
+SPLAT_DEV float butterfly12(float (&v)[12], int lane) {
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    const bool up = lane & 16;
+    const float send = up ? v[i] : v[i + 6];
+    const float keep = up ? v[i + 6] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const bool up = lane & 8;
+    const float send = up ? v[i] : v[i + 3];
+    const float keep = up ? v[i + 3] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const bool up = lane & 4;
+    const float send0 = up ? v[0] : v[2];
+    const float keep0 = up ? v[2] : v[0];
+    const float send1 = up ? v[1] : 0.0f;
+    const float keep1 = up ? 0.0f : v[1];
+    v[0] = keep0 + __shfl_xor_sync(0xffffffffu, send0, 4);
+    v[1] = keep1 + __shfl_xor_sync(0xffffffffu, send1, 4);
+  }
+  {
+    const bool up = lane & 2;
+    const float send = up ? v[0] : v[1];
+    const float keep = up ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  return v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
 }
 
-template <int CHP>
-__global__ void __launch_bounds__(kBlock) render_backward_kernel(RenderParams p) {
-  constexpr int kValues = 8 + CHP;
-  constexpr int kGroups = (kValues + 15) / 16;
-  __shared__ RenderShared<CHP> s;
-  __shared__ uint8_t s_list[kBlock / 32][kBlock];
+SPLAT_DEV int butterfly12_index(int lane) {
+  const int sub = ((lane >> 2) & 1) * 2 + ((lane >> 1) & 1);
+  return sub == 3 ? 12 : ((lane >> 4) & 1) * 6 + ((lane >> 3) & 1) * 3 + sub;
+}
+
+// Destination row of gradient value k: 0-1 centre, 2-5 conic (incl.
+// opacity), 6-7 |centre| sums, 8+c feature channel c.  The value of Gaussian
+// g goes to base + g * stride; base is null where value k has no output.
+struct GradientSlot {
+  float* base;
+  int stride;
+};
+
+SPLAT_DEV GradientSlot gradient_slot(const RenderParams& p, int k, int grad_channels) {
+  if (k < 2) return {p.grad_centers + k, 2};
+  if (k < 6) return {p.grad_conics + (k - 2), 4};
+  if (k < 8) return {p.abs_centers ? p.abs_centers + (k - 6) : nullptr, 2};
+  const int c = k - 8;
+  if (c >= grad_channels) return {nullptr, 0};
+  if (c < p.ch_a) return {p.grad_a ? p.grad_a + c : nullptr, p.ch_a};
+  if (c < p.ch_a + p.ch_b) return {p.grad_b ? p.grad_b + (c - p.ch_a) : nullptr, p.ch_b};
+  return {nullptr, 0};
+}
+
+// Reciprocal for the transmittance replay (relative error below 2^-22; the
+// backward is compared by relative L2, not bit for bit).
+SPLAT_DEV float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Gradient contributions of one accepted sample of one pixel, added to
+// val (0-1 centre, 2-5 conic incl. opacity, 6-7 |centre|, 8+c features).
+// T is the transmittance behind the sample on entry and in front of it on
+// return; acc the blended colour behind it, which takes the sample in.
+template <int CHP, int NV>
+SPLAT_DEV void accumulate_sample(float (&val)[NV], float4 q, const float (&f)[CHP], float G,
+                                 float alpha, float dx, float dy, float& T, float bg_term,
+                                 const float (&grad)[CHP], float (&acc)[CHP]) {
+  const float inv_one_minus = rcp_approx(1.0f - alpha);
+  T = T * inv_one_minus;
+  // dL/dalpha = T * sum_c (colour_c - acc_c) dL/dC_c + bg_term / (1 - alpha),
+  // then acc += alpha * (colour - acc)
+  float grad_alpha = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CHP; ++c) {
+    const float d = f[c] - acc[c];
+    grad_alpha = __fmaf_rn(d, grad[c], grad_alpha);
+    acc[c] = __fmaf_rn(alpha, d, acc[c]);
+  }
+  const float w_feat = alpha * T;
+#pragma unroll
+  for (int c = 0; c < CHP && 8 + c < NV; ++c) val[8 + c] = __fmaf_rn(w_feat, grad[c], val[8 + c]);
+  grad_alpha = __fmaf_rn(grad_alpha, T, bg_term * inv_one_minus);
+  const float gv = q.w * grad_alpha;
+  const float gdx = G * dx, gdy = G * dy;
+  const float half_gv = -0.5f * gv;
+  const float g0 = -gv * __fmaf_rn(gdy, q.y, gdx * q.x);
+  const float g1 = -gv * __fmaf_rn(gdx, q.y, gdy * q.z);
+  val[0] += g0;
+  val[1] += g1;
+  val[2] = __fmaf_rn(gdx * dx, half_gv, val[2]);
+  val[3] = __fmaf_rn(-gdx * dy, gv, val[3]);
+  val[4] = __fmaf_rn(gdy * dy, half_gv, val[4]);
+  val[5] = __fmaf_rn(G, grad_alpha, val[5]);
+  val[6] += fabsf(g0);
+  val[7] += fabsf(g1);
+}
+
+// Reverse replay with PX pixels per lane (kBlock / PX threads per tile).
+// Four channels (RGB + the constant alpha channel) reduce 12 values with
+// butterfly12; wider layouts reduce groups of 16 with butterfly16.
+template <int CHP, int PX>
+__global__ void __launch_bounds__(kBlock / PX) render_backward_kernel(RenderParams p) {
+  constexpr int kThreads = kBlock / PX;
+  constexpr bool kTwelve = CHP == 4;
+  constexpr int kGroups = kTwelve ? 1 : (8 + CHP + 15) / 16;
+  constexpr int kSlots = kTwelve ? 12 : 16 * kGroups;
+  extern __shared__ float4 s_dynamic[];  // the staged batch (sizeof(RenderShared<CHP>) bytes)
+  RenderShared<CHP>& s = *reinterpret_cast<RenderShared<CHP>*>(s_dynamic);
+  __shared__ uint8_t s_list[kThreads / 32][kBlock];
   __shared__ int s_max_last;
+  // destination of the value that lane l holds after the reduction of group
+  // grp (the same for every warp); null for odd lanes and unused values
+  __shared__ GradientSlot s_dst[kGroups][32];
   uint8_t* list = s_list[threadIdx.x >> 5];
   const int tile = blockIdx.x;
   const int wl = threadIdx.x & 31;
-  const PixelSlot ps = pixel_slot(tile, p.gx);
-  const int x = ps.x, y = ps.y;
-  const bool inside = x < p.width && y < p.height;
-  const float fx = static_cast<float>(x), fy = static_cast<float>(y);
+  const PixelSlot<PX> ps = pixel_slot<PX>(tile, p.gx);
   const int first = max(p.ranges[2 * tile], 0);
   const int last = min(p.ranges[2 * tile + 1], p.num_ids);
   const float threshold = 1.0f / 255.0f;
-  const int pixel = y * p.width + x;
-  float T = 0.0f, final_T = 0.0f, bg_grad = 0.0f, last_alpha = 0.0f;
-  int last_contributor = 0;
-  float grad[CHP], acc[CHP], last_color[CHP];
+  const float fx = static_cast<float>(ps.x);
+  // Per-pixel replay state: T is the transmittance in front of the current
+  // sample, acc the blended colour of the accepted samples behind it, and
+  // bg_term = -T_final * sum_c background_c * dL/dC_c.
+  float fy[PX], T[PX], bg_term[PX];
+  bool inside[PX];
+  int last_contributor[PX];
+  float grad[PX][CHP], acc[PX][CHP];
+  int lane_last = 0;
 #pragma unroll
-  for (int c = 0; c < CHP; ++c) {
-    grad[c] = 0.0f;
-    acc[c] = 0.0f;
-    last_color[c] = 0.0f;
-  }
-  if (inside) {
-    final_T = p.final_t[pixel];
-    T = final_T;
-    last_contributor = p.contributors[pixel];
-    const float* up = p.upstream + static_cast<size_t>(pixel) * p.up_pix_stride;
+  for (int i = 0; i < PX; ++i) {
+    const int y = ps.y + 4 * i;
+    fy[i] = static_cast<float>(y);
+    inside[i] = ps.x < p.width && y < p.height;
+    T[i] = 0.0f;
+    bg_term[i] = 0.0f;
+    last_contributor[i] = 0;
 #pragma unroll
-    for (int c = 0; c < CHP; ++c)
-      if (c < p.channels) {
-        grad[c] = up[c * p.up_ch_stride];
-        bg_grad += p.background[c] * grad[c];
-      }
+    for (int c = 0; c < CHP; ++c) {
+      grad[i][c] = 0.0f;
+      acc[i][c] = 0.0f;
+    }
+    if (inside[i]) {
+      const int pixel = y * p.width + ps.x;
+      const float final_T = p.final_t[pixel];
+      T[i] = final_T;
+      last_contributor[i] = p.contributors[pixel];
+      const float* up = p.upstream + static_cast<size_t>(pixel) * p.up_pix_stride;
+      float bg_grad = 0.0f;
+#pragma unroll
+      for (int c = 0; c < CHP; ++c)
+        if (c < p.channels) {
+          grad[i][c] = up[c * p.up_ch_stride];
+          bg_grad += p.background[c] * grad[i][c];
+        }
+      bg_term[i] = -final_T * bg_grad;
+    }
+    lane_last = max(lane_last, last_contributor[i]);
   }
   if (threadIdx.x == 0) s_max_last = 0;
+  if (threadIdx.x < 32 * kGroups) {
+    // even lane l holds the warp total of value grp * 16 + butterfly_index(l)
+    // (butterfly12_index(l) for 12 values); odd lanes write nothing
+    const int grp = threadIdx.x >> 5;
+    const int k = kTwelve ? butterfly12_index(wl) : grp * 16 + butterfly_index(wl);
+    GradientSlot d = k < 8 + CHP ? gradient_slot(p, k, p.channels - p.constant_tail)
+                                 : GradientSlot{nullptr, 0};
+    if (wl & 1) d.base = nullptr;
+    s_dst[grp][wl] = d;
+  }
   __syncthreads();
-  const int warp_last = __reduce_max_sync(0xffffffffu, last_contributor);
+  const int warp_last = __reduce_max_sync(0xffffffffu, lane_last);
   if (wl == 0 && warp_last > 0) atomicMax(&s_max_last, warp_last);
   __syncthreads();
   const int stop = min(first + s_max_last, last);  // later positions contribute nowhere
-  const int grad_channels = p.channels - p.constant_tail;
   for (int end = stop; end > first; end -= kBlock) {
     __syncthreads();
-    const int idx = end - 1 - static_cast<int>(threadIdx.x);
-    if (idx >= first) stage_gaussian<CHP>(p, s, threadIdx.x, p.ids[idx]);
+    for (int slot = threadIdx.x; slot < kBlock; slot += kThreads) {
+      const int idx = end - 1 - slot;
+      if (idx >= first) stage_gaussian<CHP>(p, s, slot, p.ids[idx]);
+    }
     __syncthreads();
     const int count = min(kBlock, end - first);
     // only positions below warp_last (position = end - 1 - j - first) can
@@ -367,60 +540,48 @@ __global__ void __launch_bounds__(kBlock) render_backward_kernel(RenderParams p)
       const float4 gm = s.geom[j];
       const int position = end - 1 - j - first;  // contributor index - 1
       const float4 q = s.conic[j];
-      const float dx = gm.x - fx, dy = gm.y - fy;
-      bool accept = false;
-      float G = 0.0f, alpha = 0.0f;
-      if (inside && position < last_contributor) {
-        const float power = sample_power(q, dx, dy);
-        if (power <= 0.0f && power >= s.cut[j]) {
-          G = splat_expf(power);
-          alpha = wmin(W32(0.99), q.w * G);
-          accept = alpha >= threshold;
-        }
+      const float cut = s.cut[j];
+      const float dx = gm.x - fx;
+      // evaluated by every lane; only in-range lanes use the result
+      float dy[PX], G[PX], alpha[PX];
+      bool accept[PX];
+      bool any = false;
+#pragma unroll
+      for (int i = 0; i < PX; ++i) {
+        dy[i] = gm.y - fy[i];
+        const float power = sample_power(q, dx, dy[i]);
+        const bool in_range =
+            inside[i] && position < last_contributor[i] && power <= 0.0f && power >= cut;
+        G[i] = splat_expf_core(power);
+        alpha[i] = wmin(W32(0.99), q.w * G[i]);
+        accept[i] = in_range && alpha[i] >= threshold;
+        any = any || accept[i];
       }
-      if (!__any_sync(0xffffffffu, accept)) continue;
-      float val[kGroups * 16];
+      if (!__any_sync(0xffffffffu, any)) continue;
+      float f[CHP];
+      load_features(s, j, f);
+      float val[kSlots];
 #pragma unroll
-      for (int v = 0; v < kGroups * 16; ++v) val[v] = 0.0f;
-      if (accept) {
-        const float inv_one_minus = __frcp_rn(1.0f - alpha);
-        T = T * inv_one_minus;
-        float grad_alpha = 0.0f;
+      for (int v = 0; v < kSlots; ++v) val[v] = 0.0f;
 #pragma unroll
-        for (int c = 0; c < CHP; ++c)
-          if (c < p.channels) {
-            const float col = s.feat[c][j];
-            acc[c] = last_alpha * last_color[c] + (1.0f - last_alpha) * acc[c];
-            last_color[c] = col;
-            grad_alpha += (col - acc[c]) * grad[c];
-          }
-        const float w_feat = alpha * T;
+      for (int i = 0; i < PX; ++i)
+        if (accept[i])
+          accumulate_sample(val, q, f, G[i], alpha[i], dx, dy[i], T[i], bg_term[i], grad[i],
+                            acc[i]);
+      const size_t g = static_cast<size_t>(s.id[j]);
+      if constexpr (kTwelve) {
+        const float total = butterfly12(val, wl);
+        const GradientSlot d = s_dst[0][wl];
+        if (d.base) red_add(d.base + g * d.stride, total);
+      } else {
 #pragma unroll
-        for (int c = 0; c < CHP; ++c) val[8 + c] = c < grad_channels ? w_feat * grad[c] : 0.0f;
-        grad_alpha = grad_alpha * T + (-final_T * inv_one_minus) * bg_grad;
-        last_alpha = alpha;
-        const float gv = q.w * grad_alpha;
-        const float gdx = G * dx, gdy = G * dy;
-        val[0] = gv * (-gdx * q.x - gdy * q.y);
-        val[1] = gv * (-gdy * q.z - gdx * q.y);
-        val[2] = -0.5f * gdx * dx * gv;
-        val[3] = -gdx * dy * gv;
-        val[4] = -0.5f * gdy * dy * gv;
-        val[5] = G * grad_alpha;
-        val[6] = fabsf(val[0]);
-        val[7] = fabsf(val[1]);
-      }
-      const int g = s.id[j];
-      const int k_lane = butterfly_index(wl);
+        for (int grp = 0; grp < kGroups; ++grp) {
+          float v16[16];
 #pragma unroll
-      for (int grp = 0; grp < kGroups; ++grp) {
-        float v16[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v16[k] = val[grp * 16 + k];
-        const float total = butterfly16(v16, wl);
-        if ((wl & 1) == 0) {
-          float* dst = gradient_slot(p, g, grp * 16 + k_lane, grad_channels);
-          if (dst) red_add(dst, total);
+          for (int v = 0; v < 16; ++v) v16[v] = val[grp * 16 + v];
+          const float total = butterfly16(v16, wl);
+          const GradientSlot d = s_dst[grp][wl];
+          if (d.base) red_add(d.base + g * d.stride, total);
         }
       }
     }

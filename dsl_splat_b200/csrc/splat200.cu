@@ -189,10 +189,22 @@ int project_backward_dispatch(const ProjectBackwardParams& p, cudaStream_t s) {
 template <int CHP>
 void launch_render(const RenderParams& p, bool backward, cudaStream_t s) {
   const unsigned tiles = static_cast<unsigned>(p.gx * ((p.height + 15) / 16));
-  if (backward)
-    render_backward_kernel<CHP><<<tiles, kBlock, 0, counted(s)>>>(p);
-  else
-    render_forward_kernel<CHP><<<tiles, kBlock, 0, counted(s)>>>(p);
+  // The staged batch lives in dynamic shared memory; the 32-channel variant
+  // needs more than the default 48 KB (opt-in, per device, cheap to repeat).
+  const size_t smem = sizeof(RenderShared<CHP>);
+  if (backward) {
+    // four channels: two pixels per lane (128 threads per tile)
+    constexpr int px = CHP == 4 ? 2 : 1;
+    if (smem > 32 * 1024)
+      cudaFuncSetAttribute(render_backward_kernel<CHP, px>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    render_backward_kernel<CHP, px><<<tiles, kBlock / px, smem, counted(s)>>>(p);
+  } else {
+    if (smem > 32 * 1024)
+      cudaFuncSetAttribute(render_forward_kernel<CHP>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    render_forward_kernel<CHP><<<tiles, kBlock, smem, counted(s)>>>(p);
+  }
 }
 
 int render_dispatch(const RenderParams& p, bool backward, cudaStream_t s) {

@@ -47,9 +47,17 @@ SPLAT_DEV int f2i(float x) { return __float2int_rz(x); }
 // 2^n through the exponent field.  Each step is one IEEE float32 operation,
 // so the CPU oracle computes the same bits and both sides take the same
 // alpha-threshold decisions.  Maximum error below 1 ulp on [-80, 0].
+SPLAT_DEV float splat_expf_core(float x);
+
 SPLAT_DEV float splat_expf(float x) {
   if (!(x > -80.0f)) return 0.0f;
   if (x > 88.0f) x = 88.0f;
+  return splat_expf_core(x);
+}
+
+// splat_expf for arguments already known to lie in (-80, 88]: the same bits
+// without the range guards.
+SPLAT_DEV float splat_expf_core(float x) {
   const float n = rintf(__fmul_rn(x, 1.44269504088896341f));
   float r = __fmaf_rn(n, -0.693359375f, x);
   r = __fmaf_rn(n, 2.12194440054690583e-4f, r);
