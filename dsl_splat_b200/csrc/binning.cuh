@@ -42,6 +42,8 @@ __device__ int g_splat_device_error;
 SPLAT_DEV void record_device_error(int code) { atomicCAS(&g_splat_device_error, 0, code); }
 
 // ---- phase 1: per-Gaussian preparation ---------------------------------
+// diff == nullptr selects the chunked path (no difference grid; the pair
+// total is the sum of rectangle areas).
 __global__ void __launch_bounds__(256)
     bin_prepare_kernel(int n, const float* __restrict__ centers, const int* __restrict__ radii,
                        const int* __restrict__ tiles, const float* __restrict__ depths, int gx,
@@ -71,12 +73,17 @@ __global__ void __launch_bounds__(256)
         const int4 b = tile_bounds(c.x, c.y, radius, gx, gy);
         rect = make_uint2(static_cast<uint32_t>(b.x) | (static_cast<uint32_t>(b.y) << 16),
                           static_cast<uint32_t>(b.z) | (static_cast<uint32_t>(b.w) << 16));
-        const int row = gx + 1;
-        atomicAdd(diff + b.y * row + b.x, 1);
-        atomicAdd(diff + b.y * row + b.z, -1);
-        atomicAdd(diff + b.w * row + b.x, -1);
-        atomicAdd(diff + b.w * row + b.z, 1);
-        pairs += static_cast<unsigned long long>(max(tiles[i], 0));
+        if (diff) {  // onesweep path: per-tile counts from a global difference grid
+          const int row = gx + 1;
+          atomicAdd(diff + b.y * row + b.x, 1);
+          atomicAdd(diff + b.y * row + b.z, -1);
+          atomicAdd(diff + b.w * row + b.x, -1);
+          atomicAdd(diff + b.w * row + b.z, 1);
+          pairs += static_cast<unsigned long long>(max(tiles[i], 0));
+        } else {  // chunked path: pairs are the rectangle areas it scatters
+          pairs += static_cast<unsigned long long>(max(b.z - b.x, 0)) *
+                   static_cast<unsigned long long>(max(b.w - b.y, 0));
+        }
       }
       keys[i] = key;
       vals[i] = static_cast<uint32_t>(i);
@@ -306,21 +313,21 @@ __global__ void __launch_bounds__(kSortBlock)
 // values[gather ? gather[i] : i] summed in blocks of kSortTile.
 
 SPLAT_DEV uint32_t scan_value(const int* __restrict__ values, const uint32_t* __restrict__ gather,
-                              uint32_t i) {
+                              uint32_t i, uint32_t bias) {
   const uint32_t src = gather ? gather[i] : i;
   const int v = values[src];
-  return v > 0 ? static_cast<uint32_t>(v) : 0u;
+  return (v > 0 ? static_cast<uint32_t>(v) : 0u) + bias;
 }
 
 __global__ void __launch_bounds__(kSortBlock)
     scan_block_sums_kernel(const int* __restrict__ values, const uint32_t* __restrict__ gather,
-                           uint32_t n, uint32_t* __restrict__ block_sums) {
+                           uint32_t n, uint32_t* __restrict__ block_sums, uint32_t bias = 0u) {
   __shared__ uint32_t s_warp[32];
   const uint32_t base = blockIdx.x * kSortTile;
   uint32_t sum = 0u;
   for (int k = 0; k < kSortItems; ++k) {
     const uint32_t i = base + k * kSortBlock + threadIdx.x;
-    if (i < n) sum += scan_value(values, gather, i);
+    if (i < n) sum += scan_value(values, gather, i, bias);
   }
   uint32_t total;
   block_exclusive_scan(sum, s_warp, &total);
@@ -351,14 +358,14 @@ __global__ void scan_block_prefix_kernel(uint32_t* __restrict__ block_sums, uint
 __global__ void __launch_bounds__(kSortBlock)
     scan_apply_kernel(const int* __restrict__ values, const uint32_t* __restrict__ gather,
                       uint32_t n, const uint32_t* __restrict__ block_prefix, int inclusive,
-                      uint32_t* __restrict__ out) {
+                      uint32_t* __restrict__ out, uint32_t bias = 0u) {
   __shared__ uint32_t s_val[kSortTile];
   __shared__ uint32_t s_warp[32];
   const uint32_t base = blockIdx.x * kSortTile;
   for (int k = 0; k < kSortItems; ++k) {
     const int j = k * kSortBlock + threadIdx.x;
     const uint32_t i = base + j;
-    s_val[j] = i < n ? scan_value(values, gather, i) : 0u;
+    s_val[j] = i < n ? scan_value(values, gather, i, bias) : 0u;
   }
   __syncthreads();
   uint32_t local[kSortItems];
@@ -384,7 +391,323 @@ __global__ void __launch_bounds__(kSortBlock)
   if (!inclusive && blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) {
     // the last element's exclusive prefix plus its value
     const uint32_t last = n - 1;
-    if (last >= base) out[n] = s_val[last - base] + scan_value(values, gather, last);
+    if (last >= base) out[n] = s_val[last - base] + scan_value(values, gather, last, bias);
+  }
+}
+
+// ---- chunked stable scatter ----------------------------------------------
+// The depth-ordered Gaussians are cut into K chunks of about equal work
+// (tiles + kChunkGaussianCost per Gaussian, from a prefix scan in depth
+// order).  cnt[k][t] = pairs of chunk k in tile t; an exclusive prefix over
+// k plus the tile's range start gives every chunk its first write position
+// per tile, so all chunks scatter independently.  Inside a chunk, waves of
+// 32 Gaussians are placed in order: a Gaussian's rank within tile t is the
+// number of earlier wave members whose rectangle covers t, read from
+// per-column and per-row 32-bit coverage masks.  The result is the depth
+// order within every tile, i.e. the reference's stable sort of 64-bit keys.
+
+constexpr uint32_t kChunkGaussianCost = 8;  // per-Gaussian wave overhead, in pairs
+
+SPLAT_DEV void unpack_rect(uint2 r, uint32_t& x0, uint32_t& y0, uint32_t& x1, uint32_t& y1) {
+  x0 = r.x & 0xFFFFu;
+  y0 = r.x >> 16;
+  x1 = r.y & 0xFFFFu;
+  y1 = r.y >> 16;
+}
+
+SPLAT_DEV uint32_t rect_area(uint2 r) {
+  uint32_t x0, y0, x1, y1;
+  unpack_rect(r, x0, y0, x1, y1);
+  return (x1 > x0 && y1 > y0) ? (x1 - x0) * (y1 - y0) : 0u;
+}
+
+// bounds[k] = first depth position whose work prefix reaches k/K of the
+// total (work[] exclusive, work[n] = total; strictly increasing).
+__global__ void chunk_bounds_kernel(const uint32_t* __restrict__ work, uint32_t n, unsigned chunks,
+                                    uint32_t* __restrict__ bounds) {
+  const unsigned k = blockIdx.x * blockDim.x + threadIdx.x;
+  if (k > chunks) return;
+  const uint64_t total = work[n];
+  const uint64_t target = total * k / chunks;
+  uint32_t lo = 0, hi = n;  // first i in [0, n] with work[i] >= target
+  while (lo < hi) {
+    const uint32_t mid = lo + ((hi - lo) >> 1);
+    if (work[mid] < target) lo = mid + 1; else hi = mid;
+  }
+  bounds[k] = k == chunks ? n : lo;
+}
+
+// cnt[k * T + t] for chunk k = blockIdx.x, from a difference grid of the
+// chunk's rectangles in shared memory ((gx+1)*(gy+1) ints); also gathers
+// the rectangles into depth order for the scatter.
+__global__ void __launch_bounds__(256)
+    chunk_counts_kernel(const uint32_t* __restrict__ order, const uint32_t* __restrict__ bounds,
+                        const uint2* __restrict__ rects, int gx, int gy,
+                        uint2* __restrict__ sorted_rects, uint32_t* __restrict__ cnt) {
+  extern __shared__ int s_diff[];
+  const int row = gx + 1, cells = row * (gy + 1);
+  for (int c = threadIdx.x; c < cells; c += blockDim.x) s_diff[c] = 0;
+  __syncthreads();
+  const uint32_t begin = bounds[blockIdx.x], end = bounds[blockIdx.x + 1];
+  for (uint32_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
+    const uint2 r = rects[order[i]];
+    sorted_rects[i] = r;
+    uint32_t x0, y0, x1, y1;
+    unpack_rect(r, x0, y0, x1, y1);
+    if (x1 > x0 && y1 > y0) {
+      atomicAdd(s_diff + y0 * row + x0, 1);
+      atomicAdd(s_diff + y0 * row + x1, -1);
+      atomicAdd(s_diff + y1 * row + x0, -1);
+      atomicAdd(s_diff + y1 * row + x1, 1);
+    }
+  }
+  __syncthreads();
+  for (int y = threadIdx.x; y <= gy; y += blockDim.x) {
+    int acc = 0;
+    for (int x = 0; x <= gx; ++x) acc = (s_diff[y * row + x] += acc);
+  }
+  __syncthreads();
+  for (int x = threadIdx.x; x <= gx; x += blockDim.x) {
+    int acc = 0;
+    for (int y = 0; y <= gy; ++y) acc = (s_diff[y * row + x] += acc);
+  }
+  __syncthreads();
+  const int T = gx * gy;
+  uint32_t* out = cnt + static_cast<size_t>(blockIdx.x) * T;
+  for (int t = threadIdx.x; t < T; t += blockDim.x)
+    out[t] = static_cast<uint32_t>(s_diff[(t / gx) * row + (t % gx)]);
+}
+
+// In place: cnt[k][t] -> sum of cnt[k'][t] over k' < k; totals[t] = the sum
+// over all chunks.  Block: 32 tiles x 8 chunk segments (one warp each).
+__global__ void __launch_bounds__(256)
+    chunk_prefix_kernel(uint32_t* __restrict__ cnt, int chunks, int T,
+                        uint32_t* __restrict__ totals) {
+  __shared__ uint32_t s_seg[8][32];
+  const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
+  const int t = blockIdx.x * 32 + lane;
+  const int per = (chunks + 7) / 8;
+  const int k0 = min(seg * per, chunks), k1 = min(k0 + per, chunks);
+  uint32_t sum = 0u;
+  if (t < T)
+    for (int k = k0; k < k1; ++k) sum += cnt[static_cast<size_t>(k) * T + t];
+  s_seg[seg][lane] = sum;
+  __syncthreads();
+  uint32_t run = 0u;
+  for (int q = 0; q < seg; ++q) run += s_seg[q][lane];
+  if (t < T) {
+    for (int k = k0; k < k1; ++k) {
+      uint32_t* c = cnt + static_cast<size_t>(k) * T + t;
+      const uint32_t v = *c;
+      *c = run;
+      run += v;
+    }
+    if (seg == 7) totals[t] = run;
+  }
+}
+
+// One block: ranges from per-tile totals (empty tiles get [0, 0), as
+// identify_ranges leaves them), the first position of every tile, and the
+// pair total.
+__global__ void __launch_bounds__(1024)
+    tile_ranges_kernel(const uint32_t* __restrict__ totals, int T, int* __restrict__ ranges,
+                       uint32_t* __restrict__ starts, uint32_t* __restrict__ total) {
+  constexpr int kPer = 8;
+  __shared__ uint32_t s_warp[32];
+  __shared__ uint32_t s_carry;
+  if (threadIdx.x == 0) s_carry = 0u;
+  __syncthreads();
+  for (int base = 0; base < T; base += 1024 * kPer) {
+    uint32_t v[kPer];
+    uint32_t sum = 0u;
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int t = base + threadIdx.x * kPer + r;
+      v[r] = t < T ? totals[t] : 0u;
+      sum += v[r];
+    }
+    uint32_t chunk_total;
+    uint32_t run = block_exclusive_scan(sum, s_warp, &chunk_total) + s_carry;
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int t = base + threadIdx.x * kPer + r;
+      if (t < T) {
+        ranges[2 * t] = v[r] ? static_cast<int>(run) : 0;
+        ranges[2 * t + 1] = v[r] ? static_cast<int>(run + v[r]) : 0;
+        starts[t] = run;
+      }
+      run += v[r];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry += chunk_total;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total = s_carry;
+}
+
+// Wave metadata (double-buffered): member ids, rectangles, exclusive pair
+// prefix (pref[32] = pairs of the wave) and 1/width.
+struct ScatterWave {
+  uint32_t g[32];
+  uint2 rect[32];
+  uint32_t pref[33];
+  float inv_w[32];
+};
+
+// Warp 0 publishes a wave's metadata from one member per lane.
+SPLAT_DEV void publish_wave(ScatterWave& w, int lane, uint32_t g, uint2 r) {
+  const uint32_t area = rect_area(r);
+  uint32_t incl = area;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  w.g[lane] = g;
+  w.rect[lane] = r;
+  w.pref[lane + 1] = incl;
+  if (lane == 0) w.pref[0] = 0u;
+  const uint32_t width = (r.y & 0xFFFFu) - (r.x & 0xFFFFu);
+  w.inv_w[lane] = area ? 1.0f / static_cast<float>(width) : 0.0f;
+}
+
+// Pair p of a wave: its member (largest j with pref[j] <= p), the tile it
+// covers (row-major order inside the member's rectangle) and the coverage
+// mask of that tile.
+struct WavePair {
+  int member;
+  uint32_t tile, cover;
+};
+
+SPLAT_DEV WavePair wave_pair(const ScatterWave& w, uint32_t p, int gx, const uint32_t* col,
+                             const uint32_t* rowm) {
+  int j = 0;
+#pragma unroll
+  for (int step = 16; step > 0; step >>= 1)
+    if (w.pref[j + step] <= p) j += step;
+  uint32_t x0, y0, x1, y1;
+  unpack_rect(w.rect[j], x0, y0, x1, y1);
+  const uint32_t width = x1 - x0, local = p - w.pref[j];
+  // local < 2^24: the float quotient is within one of the integer one
+  uint32_t q = static_cast<uint32_t>(static_cast<float>(local) * w.inv_w[j]);
+  if (q * width > local)
+    --q;
+  else if ((q + 1) * width <= local)
+    ++q;
+  const uint32_t tx = x0 + (local - q * width), ty = y0 + q;
+  WavePair r;
+  r.member = j;
+  r.tile = ty * static_cast<uint32_t>(gx) + tx;
+  r.cover = col[tx] & rowm[ty];
+  return r;
+}
+
+// Scatter of chunk k = blockIdx.x (256 threads).  Dynamic shared memory:
+// next[T] write positions, then two buffers of gx column masks and gy row
+// masks (the buffer of the next wave is cleared while this one is read).
+__global__ void __launch_bounds__(256)
+    tile_scatter_kernel(const uint32_t* __restrict__ order, const uint32_t* __restrict__ bounds,
+                        const uint2* __restrict__ sorted_rects, int gx, int gy,
+                        const uint32_t* __restrict__ prefix, const uint32_t* __restrict__ starts,
+                        uint32_t m, uint32_t* __restrict__ ids) {
+  constexpr int kKept = 4;  // pairs per thread whose tile update stays in registers
+  extern __shared__ uint32_t s_dyn[];
+  __shared__ ScatterWave s_wave[2];
+  const int T = gx * gy;
+  uint32_t* s_next = s_dyn;
+  uint32_t* s_masks = s_dyn + T;  // [2][gx + gy]
+  const int mask_words = gx + gy;
+  const uint32_t* base = prefix + static_cast<size_t>(blockIdx.x) * T;
+  for (int t = threadIdx.x; t < T; t += blockDim.x) s_next[t] = starts[t] + base[t];
+  for (int c = threadIdx.x; c < 2 * mask_words; c += blockDim.x) s_masks[c] = 0u;
+  const uint32_t begin = bounds[blockIdx.x], end = bounds[blockIdx.x + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // warp 0 loads members two waves ahead and publishes one wave ahead
+  uint32_t ahead_g = 0u;
+  uint2 ahead_r = make_uint2(0u, 0u);
+  if (warp == 0) {
+    uint32_t g = 0u;
+    uint2 r = make_uint2(0u, 0u);
+    if (begin + lane < end) {
+      g = order[begin + lane];
+      r = sorted_rects[begin + lane];
+    }
+    publish_wave(s_wave[0], lane, g, r);
+    if (begin + 32 + lane < end) {
+      ahead_g = order[begin + 32 + lane];
+      ahead_r = sorted_rects[begin + 32 + lane];
+    }
+  }
+  __syncthreads();
+  int buf = 0;
+  for (uint32_t w0 = begin; w0 < end; w0 += 32, buf ^= 1) {
+    const ScatterWave& wave = s_wave[buf];
+    uint32_t* col = s_masks + buf * mask_words;
+    uint32_t* rowm = col + gx;
+    {  // coverage masks: thread (member j, slot) sets every 4th column or row
+      const int j = threadIdx.x & 31, slot = threadIdx.x >> 5;
+      uint32_t x0, y0, x1, y1;
+      unpack_rect(wave.rect[j], x0, y0, x1, y1);
+      if (x1 > x0 && y1 > y0) {
+        const uint32_t bit = 1u << j;
+        if (slot < 4) {
+          for (uint32_t x = x0 + slot; x < x1; x += 4) atomicOr(col + x, bit);
+        } else {
+          for (uint32_t y = y0 + (slot - 4); y < y1; y += 4) atomicOr(rowm + y, bit);
+        }
+      }
+    }
+    __syncthreads();
+    const uint32_t P = wave.pref[32];
+    uint32_t kept_tile[kKept], kept_add[kKept];
+#pragma unroll
+    for (int it = 0; it < kKept; ++it) {
+      kept_add[it] = 0u;
+      kept_tile[it] = 0u;
+      const uint32_t p = threadIdx.x + it * blockDim.x;
+      if (p < P) {
+        const WavePair q = wave_pair(wave, p, gx, col, rowm);
+        const uint32_t below = q.cover & ((1u << q.member) - 1u);
+        const uint32_t pos = s_next[q.tile] + __popc(below);
+        if (pos < m)
+          ids[pos] = wave.g[q.member];
+        else
+          record_device_error(kInconsistentInput);
+        kept_tile[it] = q.tile;
+        kept_add[it] = below == 0u ? __popc(q.cover) : 0u;  // first covering member
+      }
+    }
+    for (uint32_t p = threadIdx.x + kKept * blockDim.x; p < P; p += blockDim.x) {
+      const WavePair q = wave_pair(wave, p, gx, col, rowm);
+      const uint32_t pos = s_next[q.tile] + __popc(q.cover & ((1u << q.member) - 1u));
+      if (pos < m)
+        ids[pos] = wave.g[q.member];
+      else
+        record_device_error(kInconsistentInput);
+    }
+    __syncthreads();
+    // advance each covered tile by the wave's count (its first covering
+    // member does it), clear the other mask buffer, publish the next wave
+#pragma unroll
+    for (int it = 0; it < kKept; ++it)
+      if (kept_add[it]) s_next[kept_tile[it]] += kept_add[it];
+    for (uint32_t p = threadIdx.x + kKept * blockDim.x; p < P; p += blockDim.x) {
+      const WavePair q = wave_pair(wave, p, gx, col, rowm);
+      if ((q.cover & ((1u << q.member) - 1u)) == 0u) s_next[q.tile] += __popc(q.cover);
+    }
+    uint32_t* other = s_masks + (buf ^ 1) * mask_words;
+    for (int c = threadIdx.x; c < mask_words; c += blockDim.x) other[c] = 0u;
+    if (warp == 0) {
+      publish_wave(s_wave[buf ^ 1], lane, ahead_g, ahead_r);
+      const uint32_t i = w0 + 64 + lane;
+      ahead_g = 0u;
+      ahead_r = make_uint2(0u, 0u);
+      if (i < end) {
+        ahead_g = order[i];
+        ahead_r = sorted_rects[i];
+      }
+    }
+    __syncthreads();
   }
 }
 

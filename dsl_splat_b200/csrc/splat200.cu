@@ -60,18 +60,54 @@ inline bool aligned(const void* p, uintptr_t a) {
 int tile_passes(int tiles) { return tiles <= 256 ? 1 : (tiles <= 65536 ? 2 : 3); }
 
 // ---- binning workspace layout -------------------------------------------
+// The chunked scatter (binning.cuh) keeps one uint32 per tile in shared
+// memory per CTA; images whose tile grid does not fit use the onesweep path.
+constexpr size_t kChunkSmemLimit = 200 * 1024;
+constexpr size_t kChunkMatrixLimit = size_t(256) << 20;  // chunk-by-tile counts
+
+struct ChunkPlan {
+  bool use = false;
+  uint32_t chunk = 0;      // Gaussians per chunk
+  unsigned chunks = 0;     // K
+  size_t smem_counts = 0;  // chunk_counts_kernel dynamic shared memory
+  size_t smem_scatter = 0;
+};
+
+ChunkPlan chunk_plan(long long n, int gx, int gy) {
+  ChunkPlan c;
+  const size_t T = static_cast<size_t>(gx) * gy;
+  c.smem_counts = 4 * static_cast<size_t>(gx + 1) * (gy + 1);
+  c.smem_scatter = 4 * (T + 2 * static_cast<size_t>(gx + gy));
+  if (c.smem_counts > kChunkSmemLimit || c.smem_scatter > kChunkSmemLimit) return c;
+  // the uint32 work prefix (tiles + kChunkGaussianCost per Gaussian) must not wrap
+  if (n > (1LL << 27)) return c;
+  c.use = true;
+  // about 2048 Gaussians per chunk on average (chunks are cut by work, not
+  // by count), fewer chunks when the chunk-by-tile matrix would grow large
+  size_t chunk = 2048;
+  const size_t nn = static_cast<size_t>(n > 0 ? n : 1);
+  if (nn * T * 4 / chunk > kChunkMatrixLimit)
+    chunk = ((nn * T * 4 + kChunkMatrixLimit - 1) / kChunkMatrixLimit + 31) / 32 * 32;
+  c.chunk = static_cast<uint32_t>(chunk);
+  c.chunks = static_cast<unsigned>((nn + chunk - 1) / chunk);
+  return c;
+}
+
 struct BinLayout {
   size_t keys_a, vals_a, keys_b, vals_b, rects, offsets, block_sums;
   size_t zero_begin;  // everything from here to zero_end is cleared per call
   size_t depth_hist, diff, depth_status, counters, totals;
   size_t zero_end;
   size_t depth_digits, tile_digits;
+  size_t chunk_counts, tile_totals, tile_starts, chunk_bounds, sorted_rects;  // chunked path
   size_t bytes;
 };
 
 BinLayout bin_layout(long long n, int width, int height) {
   const int gx = (width + 15) / 16, gy = (height + 15) / 16;
   const size_t sort_tiles = static_cast<size_t>(blocks_for(n > 0 ? n : 1, kSortTile));
+  const ChunkPlan plan = chunk_plan(n, gx, gy);
+  const size_t T = static_cast<size_t>(gx) * gy;
   BinLayout L{};
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -84,17 +120,22 @@ BinLayout bin_layout(long long n, int width, int height) {
   L.keys_b = take(4 * n);
   L.vals_b = take(4 * n);
   L.rects = take(8 * n);
-  L.offsets = take(4 * (n + 1));
+  L.offsets = take(4 * (n + 1));  // pair offsets, or the work prefix of the chunked path
   L.block_sums = take(4 * (sort_tiles + 1));
   L.zero_begin = o;
   L.depth_hist = take(4 * 4 * kRadix);
-  L.diff = take(4 * static_cast<size_t>(gx + 1) * (gy + 1));
+  L.diff = take(plan.use ? 0 : 4 * static_cast<size_t>(gx + 1) * (gy + 1));
   L.depth_status = take(4 * 4 * sort_tiles * kRadix);
   L.counters = take(4 * 8);
   L.totals = take(8 * 4);
   L.zero_end = o;
   L.depth_digits = take(4 * 4 * kRadix);
-  L.tile_digits = take(4 * 3 * kRadix);
+  L.tile_digits = take(plan.use ? 0 : 4 * 3 * kRadix);
+  L.chunk_counts = take(plan.use ? 4 * static_cast<size_t>(plan.chunks) * T : 0);
+  L.tile_totals = take(plan.use ? 4 * T : 0);
+  L.tile_starts = take(plan.use ? 4 * T : 0);
+  L.chunk_bounds = take(plan.use ? 4 * (static_cast<size_t>(plan.chunks) + 1) : 0);
+  L.sorted_rects = take(plan.use ? 8 * n : 0);
   L.bytes = o;
   return L;
 }
@@ -104,10 +145,12 @@ struct PairLayout {
 };
 
 PairLayout pair_layout(long long pairs, int width, int height) {
-  const int tiles = ((width + 15) / 16) * ((height + 15) / 16);
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+  const int tiles = gx * gy;
   const int passes = tile_passes(tiles);
   const size_t sort_tiles = static_cast<size_t>(blocks_for(pairs > 0 ? pairs : 1, kSortTile));
   PairLayout L{};
+  if (chunk_plan(1, gx, gy).use) return L;  // the chunked scatter needs no pair workspace
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t at = o;
@@ -637,6 +680,8 @@ int splat_bin_prepare(int n, const float* centers, const int* radii, const int* 
   uint32_t* depth_digits = at<uint32_t>(ws, L.depth_digits);
   uint32_t* tile_digits = at<uint32_t>(ws, L.tile_digits);
   const unsigned sort_tiles = blocks_for(n, kSortTile);
+  const ChunkPlan plan = chunk_plan(n, gx, gy);
+  if (plan.use) diff = nullptr;
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned prep_grid = std::min<unsigned>(blocks_for(n, 256), static_cast<unsigned>(sms * 8));
@@ -653,12 +698,38 @@ int splat_bin_prepare(int n, const float* centers, const int* radii, const int* 
         status + static_cast<size_t>(pass) * sort_tiles * kRadix, counters + pass,
         even ? keys_b : keys_a, even ? vals_b : vals_a);
   }
-  // pair offsets in depth order: offsets[j] = sum of tiles[order[i]], i < j
-  scan_block_sums_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums);
-  scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, sort_tiles, totals + 0);
-  scan_apply_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums, 0, offsets);
-  tile_counts_kernel<<<1, 1024, 0, counted(s)>>>(diff, gx, gy, tile_passes(T), ranges, tile_digits,
-                                        totals + 1);
+  if (plan.use) {
+    // per-(chunk, tile) pair counts of the depth-ordered Gaussians, their
+    // prefix over chunks, and the tile ranges
+    uint32_t* cnt = at<uint32_t>(ws, L.chunk_counts);
+    uint32_t* tile_totals = at<uint32_t>(ws, L.tile_totals);
+    uint32_t* bounds = at<uint32_t>(ws, L.chunk_bounds);
+    // work prefix in depth order (tiles + a per-Gaussian cost) -> chunk bounds
+    scan_block_sums_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums,
+                                                                      kChunkGaussianCost);
+    scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, sort_tiles, totals + 0);
+    scan_apply_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums, 0,
+                                                                 offsets, kChunkGaussianCost);
+    chunk_bounds_kernel<<<blocks_for(plan.chunks + 1, 256), 256, 0, counted(s)>>>(
+        offsets, static_cast<uint32_t>(n), plan.chunks, bounds);
+    if (plan.smem_counts > 48 * 1024)
+      cudaFuncSetAttribute(chunk_counts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(plan.smem_counts));
+    chunk_counts_kernel<<<plan.chunks, 256, plan.smem_counts, counted(s)>>>(
+        vals_a, bounds, rects, gx, gy, at<uint2>(ws, L.sorted_rects), cnt);
+    chunk_prefix_kernel<<<blocks_for(T, 32), 256, 0, counted(s)>>>(cnt, plan.chunks, T,
+                                                                     tile_totals);
+    tile_ranges_kernel<<<1, 1024, 0, counted(s)>>>(tile_totals, T, ranges,
+                                                   at<uint32_t>(ws, L.tile_starts), totals + 1);
+  } else {
+    // pair offsets in depth order: offsets[j] = sum of tiles[order[i]], i < j
+    scan_block_sums_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums);
+    scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, sort_tiles, totals + 0);
+    scan_apply_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums, 0,
+                                                                 offsets);
+    tile_counts_kernel<<<1, 1024, 0, counted(s)>>>(diff, gx, gy, tile_passes(T), ranges,
+                                                   tile_digits, totals + 1);
+  }
   // The 64-bit total cannot wrap; splat_bin_emit refuses totals >= 2^30.
   if (cudaMemcpyAsync(pairs, total64, sizeof(long long), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return check_launch("bin_prepare pairs");
@@ -674,7 +745,7 @@ int splat_bin_emit(int n, long long pairs, int width, int height, void* workspac
   const BinLayout L = bin_layout(n, width, height);
   const PairLayout P = pair_layout(pairs, width, height);
   if (!workspace || workspace_bytes < L.bytes) return fail(kWorkspaceTooSmall, "bin workspace too small");
-  if (!pairs_workspace || pairs_workspace_bytes < P.bytes)
+  if (P.bytes > 0 && (!pairs_workspace || pairs_workspace_bytes < P.bytes))
     return fail(kWorkspaceTooSmall, "pair workspace too small");
   if (!ids) return fail(kInvalidArgument, "null ids");
   if (!aligned(workspace, 256) || !aligned(pairs_workspace, 256))
@@ -683,6 +754,18 @@ int splat_bin_emit(int n, long long pairs, int width, int height, void* workspac
   const int passes = tile_passes(gx * gy);
   cudaStream_t s = as_stream(stream);
   char* ws = static_cast<char*>(workspace);
+  const ChunkPlan plan = chunk_plan(n, gx, gy);
+  if (plan.use) {
+    if (plan.smem_scatter > 48 * 1024)
+      cudaFuncSetAttribute(tile_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(plan.smem_scatter));
+    tile_scatter_kernel<<<plan.chunks, 256, plan.smem_scatter, counted(s)>>>(
+        at<uint32_t>(ws, L.vals_a), at<uint32_t>(ws, L.chunk_bounds),
+        at<uint2>(ws, L.sorted_rects), gx, gy, at<uint32_t>(ws, L.chunk_counts),
+        at<uint32_t>(ws, L.tile_starts), static_cast<uint32_t>(pairs),
+        reinterpret_cast<uint32_t*>(ids));
+    return check_launch("bin_emit");
+  }
   char* pw = static_cast<char*>(pairs_workspace);
   if (cudaMemsetAsync(pw + P.status, 0, P.bytes - P.status, s) != cudaSuccess)
     return check_launch("bin_emit memset");

@@ -47,7 +47,10 @@ def test_workspace_queries_without_gpu():
     small = lib.splat_bin_workspace_bytes(10, 256, 256)
     big = lib.splat_bin_workspace_bytes(1_000_000, 1920, 1080)
     assert 0 < small < big
-    assert lib.splat_bin_pairs_workspace_bytes(8_800_000, 1920, 1080) >= 8 * 8_800_000
+    # tile grids that fit the chunked scatter need no pair workspace; the
+    # onesweep fallback (65,536 tiles here) sorts 8-byte pairs
+    assert lib.splat_bin_pairs_workspace_bytes(8_800_000, 1920, 1080) == 0
+    assert lib.splat_bin_pairs_workspace_bytes(8_800_000, 4096, 4096) >= 8 * 8_800_000
     assert lib.splat_scan_workspace_bytes(1_000_000) > 0
 
 

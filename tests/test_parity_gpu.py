@@ -258,9 +258,12 @@ def test_empty_and_culled_scenes():
     assert len(stages.bin_and_sort(e, W, H)["point_list"]) == 0
 
 
-@pytest.mark.parametrize("width,height", [(1, 1), (17, 5), (4200, 4100)])
+@pytest.mark.parametrize("width,height", [(1, 1), (17, 5), (3000, 2000), (4096, 4096),
+                                          (4200, 4100)])
 def test_tile_pass_counts(width, height):
-    """1, 2 and 3 tile-id radix passes (T<=256, <=65536, >65536) vs the oracle."""
+    """Both binning paths vs the oracle: the chunked scatter (tile grids whose
+    per-tile arrays fit in shared memory, incl. one above the 48 KB default)
+    and the onesweep fallback with 2 and 3 tile-id passes (T <= 65536, > 65536)."""
     s = make_scene(0, n=3000, width=width, height=height)
     d = _dev()
     s.Ks[0] = torch.tensor([[width * 1.0, 0, width / 2], [0, width * 1.0, height / 2], [0, 0, 1]])
