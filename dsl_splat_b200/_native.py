@@ -31,7 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "splat_cameras_backward": (_I, [_I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "splat_project_forward": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,
                                    _P, _P, _P, _P, _P, _P]),
-    "splat_project_forward_fused": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,
+    "splat_project_forward_fused": (_I, [_I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,
                                          _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _P,
                                          _P, _P, _P, _P]),
     "splat_metadata": (_I, [_I, _P, _P, _P, _P, _P, _P, _P]),
@@ -50,12 +50,13 @@ SIGNATURES: dict[str, tuple] = {
     "splat_bin_prepare": (_I, [_I, _P, _P, _P, _P, _I, _I, _P, _Z, _P, _P, _P]),
     "splat_bin_emit": (_I, [_I, _L, _I, _I, _P, _Z, _P, _Z, _P, _P]),
     "splat_render_forward": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P, _I, _I, _I,
-                                  _P, _P, _I, _I, _P, _P, _P]),
+                                  _P, _P, _I, _I, _P, _P, _P, _P]),
     "splat_render_forward_statistics": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P,
-                                             _I, _I, _I, _P, _P, _I, _I, _P, _P, _I, _I, _P,
-                                             _P, _P, _P]),
+                                             _I, _I, _I, _P, _P, _I, _I, _P, _P, _P, _I, _I,
+                                             _P, _P, _P, _P]),
     "splat_render_backward": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P, _I, _I, _I,
-                                   _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P, _I, _P]),
+                                   _P, _P, _P, _P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _I,
+                                   _P]),
     "splat_debug_expf": (_I, [_I, _P, _P, _P, _P]),
 }
 
@@ -64,7 +65,7 @@ def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
             f"libsplat200.so not found at {LIB_PATH}; build it with "
-            "`python -m dsl_splat_b200.build` (nvcc, sm_100a)")
+            "`python dsl_splat_b200/build.py` (nvcc, sm_100a)")
     lib = ctypes.CDLL(LIB_PATH)
     for name, (restype, argtypes) in SIGNATURES.items():
         fn = getattr(lib, name)  # AttributeError -> missing symbol: fail loudly

@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kSortBlock)
 // per tile, so all chunks scatter independently.  Inside a chunk, waves of
 // 32 Gaussians are placed in order: a Gaussian's rank within tile t is the
 // number of earlier wave members whose rectangle covers t, read from
-// per-column and per-row 32-bit coverage masks.  The result is the depth
+// per-column and per-row 64-bit coverage masks (waves of 64 Gaussians).  The result is the depth
 // order within every tile, i.e. the reference's stable sort of 64-bit keys.
 
 constexpr uint32_t kChunkGaussianCost = 8;  // per-Gaussian wave overhead, in pairs
@@ -479,14 +479,15 @@ __global__ void __launch_bounds__(256)
 }
 
 // In place: cnt[k][t] -> sum of cnt[k'][t] over k' < k; totals[t] = the sum
-// over all chunks.  Block: 32 tiles x 8 chunk segments (one warp each).
-__global__ void __launch_bounds__(256)
+// over all chunks.  Block: 32 tiles x 32 chunk segments (one warp each).
+__global__ void __launch_bounds__(1024)
     chunk_prefix_kernel(uint32_t* __restrict__ cnt, int chunks, int T,
                         uint32_t* __restrict__ totals) {
-  __shared__ uint32_t s_seg[8][32];
+  constexpr int kSegments = 32;
+  __shared__ uint32_t s_seg[kSegments][32];
   const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
   const int t = blockIdx.x * 32 + lane;
-  const int per = (chunks + 7) / 8;
+  const int per = (chunks + kSegments - 1) / kSegments;
   const int k0 = min(seg * per, chunks), k1 = min(k0 + per, chunks);
   uint32_t sum = 0u;
   if (t < T)
@@ -502,7 +503,7 @@ __global__ void __launch_bounds__(256)
       *c = run;
       run += v;
     }
-    if (seg == 7) totals[t] = run;
+    if (seg == kSegments - 1) totals[t] = run;
   }
 }
 
@@ -546,29 +547,62 @@ __global__ void __launch_bounds__(1024)
 }
 
 // Wave metadata (double-buffered): member ids, rectangles, exclusive pair
-// prefix (pref[32] = pairs of the wave) and 1/width.
+// prefix (pref[kWave] = pairs of the wave) and 1/width.
+constexpr int kWave = 64;
+
 struct ScatterWave {
-  uint32_t g[32];
-  uint2 rect[32];
-  uint32_t pref[33];
-  float inv_w[32];
+  uint32_t g[kWave];
+  uint2 rect[kWave];
+  uint32_t pref[kWave + 1];
+  uint32_t lines[kWave + 1];  // exclusive prefix of width + height (mask tasks)
+  float inv_w[kWave];
 };
 
-// Warp 0 publishes a wave's metadata from one member per lane.
-SPLAT_DEV void publish_wave(ScatterWave& w, int lane, uint32_t g, uint2 r) {
-  const uint32_t area = rect_area(r);
-  uint32_t incl = area;
+SPLAT_DEV float inverse_width(uint2 r) {
+  const uint32_t width = (r.y & 0xFFFFu) - (r.x & 0xFFFFu);
+  return rect_area(r) ? 1.0f / static_cast<float>(width) : 0.0f;
+}
+
+// Warp 0 publishes a wave's metadata; lane l holds members l and 32 + l.
+SPLAT_DEV uint32_t rect_lines(uint2 r) {
+  uint32_t x0, y0, x1, y1;
+  unpack_rect(r, x0, y0, x1, y1);
+  return (x1 > x0 && y1 > y0) ? (x1 - x0) + (y1 - y0) : 0u;
+}
+
+SPLAT_DEV void publish_wave(ScatterWave& w, int lane, uint32_t g0, uint2 r0, uint32_t g1,
+                            uint2 r1) {
+  uint32_t a = rect_area(r0), b = rect_area(r1);
+  uint32_t la = rect_lines(r0), lb = rect_lines(r1);
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
+    const uint32_t ya = __shfl_up_sync(0xffffffffu, a, o);
+    const uint32_t yb = __shfl_up_sync(0xffffffffu, b, o);
+    const uint32_t yla = __shfl_up_sync(0xffffffffu, la, o);
+    const uint32_t ylb = __shfl_up_sync(0xffffffffu, lb, o);
+    if (lane >= o) {
+      a += ya;
+      b += yb;
+      la += yla;
+      lb += ylb;
+    }
   }
-  w.g[lane] = g;
-  w.rect[lane] = r;
-  w.pref[lane + 1] = incl;
-  if (lane == 0) w.pref[0] = 0u;
-  const uint32_t width = (r.y & 0xFFFFu) - (r.x & 0xFFFFu);
-  w.inv_w[lane] = area ? 1.0f / static_cast<float>(width) : 0.0f;
+  b += __shfl_sync(0xffffffffu, a, 31);
+  lb += __shfl_sync(0xffffffffu, la, 31);
+  w.g[lane] = g0;
+  w.g[32 + lane] = g1;
+  w.rect[lane] = r0;
+  w.rect[32 + lane] = r1;
+  w.pref[lane + 1] = a;
+  w.pref[33 + lane] = b;
+  w.lines[lane + 1] = la;
+  w.lines[33 + lane] = lb;
+  if (lane == 0) {
+    w.pref[0] = 0u;
+    w.lines[0] = 0u;
+  }
+  w.inv_w[lane] = inverse_width(r0);
+  w.inv_w[32 + lane] = inverse_width(r1);
 }
 
 // Pair p of a wave: its member (largest j with pref[j] <= p), the tile it
@@ -576,14 +610,15 @@ SPLAT_DEV void publish_wave(ScatterWave& w, int lane, uint32_t g, uint2 r) {
 // mask of that tile.
 struct WavePair {
   int member;
-  uint32_t tile, cover;
+  uint32_t tile;
+  unsigned long long cover;
 };
 
-SPLAT_DEV WavePair wave_pair(const ScatterWave& w, uint32_t p, int gx, const uint32_t* col,
-                             const uint32_t* rowm) {
+SPLAT_DEV WavePair wave_pair(const ScatterWave& w, uint32_t p, int gx,
+                             const unsigned long long* col, const unsigned long long* rowm) {
   int j = 0;
 #pragma unroll
-  for (int step = 16; step > 0; step >>= 1)
+  for (int step = kWave / 2; step > 0; step >>= 1)
     if (w.pref[j + step] <= p) j += step;
   uint32_t x0, y0, x1, y1;
   unpack_rect(w.rect[j], x0, y0, x1, y1);
@@ -602,63 +637,72 @@ SPLAT_DEV WavePair wave_pair(const ScatterWave& w, uint32_t p, int gx, const uin
   return r;
 }
 
+SPLAT_DEV unsigned long long members_below(int j) { return (1ull << j) - 1ull; }
+
 // Scatter of chunk k = blockIdx.x (256 threads).  Dynamic shared memory:
 // next[T] write positions, then two buffers of gx column masks and gy row
-// masks (the buffer of the next wave is cleared while this one is read).
+// masks (64-bit; the buffer of the next wave is cleared while this one is
+// read).
 __global__ void __launch_bounds__(256)
     tile_scatter_kernel(const uint32_t* __restrict__ order, const uint32_t* __restrict__ bounds,
                         const uint2* __restrict__ sorted_rects, int gx, int gy,
                         const uint32_t* __restrict__ prefix, const uint32_t* __restrict__ starts,
                         uint32_t m, uint32_t* __restrict__ ids) {
   constexpr int kKept = 4;  // pairs per thread whose tile update stays in registers
-  extern __shared__ uint32_t s_dyn[];
+  extern __shared__ __align__(16) uint32_t s_dyn[];
   __shared__ ScatterWave s_wave[2];
   const int T = gx * gy;
-  uint32_t* s_next = s_dyn;
-  uint32_t* s_masks = s_dyn + T;  // [2][gx + gy]
   const int mask_words = gx + gy;
+  unsigned long long* s_masks = reinterpret_cast<unsigned long long*>(s_dyn);  // [2][gx + gy]
+  uint32_t* s_next = s_dyn + 4 * mask_words;                                    // [T]
   const uint32_t* base = prefix + static_cast<size_t>(blockIdx.x) * T;
+#pragma unroll 4
   for (int t = threadIdx.x; t < T; t += blockDim.x) s_next[t] = starts[t] + base[t];
-  for (int c = threadIdx.x; c < 2 * mask_words; c += blockDim.x) s_masks[c] = 0u;
+  for (int c = threadIdx.x; c < 2 * mask_words; c += blockDim.x) s_masks[c] = 0ull;
   const uint32_t begin = bounds[blockIdx.x], end = bounds[blockIdx.x + 1];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   // warp 0 loads members two waves ahead and publishes one wave ahead
-  uint32_t ahead_g = 0u;
-  uint2 ahead_r = make_uint2(0u, 0u);
+  uint32_t ahead_g0 = 0u, ahead_g1 = 0u;
+  uint2 ahead_r0 = make_uint2(0u, 0u), ahead_r1 = make_uint2(0u, 0u);
+  auto load = [&](uint32_t i, uint32_t& g, uint2& r) {
+    g = 0u;
+    r = make_uint2(0u, 0u);
+    if (i < end) {
+      g = order[i];
+      r = sorted_rects[i];
+    }
+  };
   if (warp == 0) {
-    uint32_t g = 0u;
-    uint2 r = make_uint2(0u, 0u);
-    if (begin + lane < end) {
-      g = order[begin + lane];
-      r = sorted_rects[begin + lane];
-    }
-    publish_wave(s_wave[0], lane, g, r);
-    if (begin + 32 + lane < end) {
-      ahead_g = order[begin + 32 + lane];
-      ahead_r = sorted_rects[begin + 32 + lane];
-    }
+    uint32_t g0, g1;
+    uint2 r0, r1;
+    load(begin + lane, g0, r0);
+    load(begin + 32 + lane, g1, r1);
+    publish_wave(s_wave[0], lane, g0, r0, g1, r1);
+    load(begin + kWave + lane, ahead_g0, ahead_r0);
+    load(begin + kWave + 32 + lane, ahead_g1, ahead_r1);
   }
   __syncthreads();
   int buf = 0;
-  for (uint32_t w0 = begin; w0 < end; w0 += 32, buf ^= 1) {
+  for (uint32_t w0 = begin; w0 < end; w0 += kWave, buf ^= 1) {
     const ScatterWave& wave = s_wave[buf];
-    uint32_t* col = s_masks + buf * mask_words;
-    uint32_t* rowm = col + gx;
-    {  // coverage masks: thread (member j, slot) sets every 4th column or row
-      const int j = threadIdx.x & 31, slot = threadIdx.x >> 5;
+    unsigned long long* col = s_masks + buf * mask_words;
+    unsigned long long* rowm = col + gx;
+    // coverage masks: task q is column or row (q - lines[j]) of member j;
+    // each sets bit j with a 32-bit atomic on the half of the 64-bit word
+    // that holds it
+    for (uint32_t q = threadIdx.x; q < wave.lines[kWave]; q += blockDim.x) {
+      int j = 0;
+#pragma unroll
+      for (int step = kWave / 2; step > 0; step >>= 1)
+        if (wave.lines[j + step] <= q) j += step;
       uint32_t x0, y0, x1, y1;
       unpack_rect(wave.rect[j], x0, y0, x1, y1);
-      if (x1 > x0 && y1 > y0) {
-        const uint32_t bit = 1u << j;
-        if (slot < 4) {
-          for (uint32_t x = x0 + slot; x < x1; x += 4) atomicOr(col + x, bit);
-        } else {
-          for (uint32_t y = y0 + (slot - 4); y < y1; y += 4) atomicOr(rowm + y, bit);
-        }
-      }
+      const uint32_t local = q - wave.lines[j];
+      unsigned long long* word = local < x1 - x0 ? col + x0 + local : rowm + y0 + (local - (x1 - x0));
+      atomicOr(reinterpret_cast<uint32_t*>(word) + (j >> 5), 1u << (j & 31));
     }
     __syncthreads();
-    const uint32_t P = wave.pref[32];
+    const uint32_t P = wave.pref[kWave];
     uint32_t kept_tile[kKept], kept_add[kKept];
 #pragma unroll
     for (int it = 0; it < kKept; ++it) {
@@ -667,19 +711,19 @@ __global__ void __launch_bounds__(256)
       const uint32_t p = threadIdx.x + it * blockDim.x;
       if (p < P) {
         const WavePair q = wave_pair(wave, p, gx, col, rowm);
-        const uint32_t below = q.cover & ((1u << q.member) - 1u);
-        const uint32_t pos = s_next[q.tile] + __popc(below);
+        const unsigned long long below = q.cover & members_below(q.member);
+        const uint32_t pos = s_next[q.tile] + __popcll(below);
         if (pos < m)
           ids[pos] = wave.g[q.member];
         else
           record_device_error(kInconsistentInput);
         kept_tile[it] = q.tile;
-        kept_add[it] = below == 0u ? __popc(q.cover) : 0u;  // first covering member
+        kept_add[it] = below == 0ull ? __popcll(q.cover) : 0u;  // first covering member
       }
     }
     for (uint32_t p = threadIdx.x + kKept * blockDim.x; p < P; p += blockDim.x) {
       const WavePair q = wave_pair(wave, p, gx, col, rowm);
-      const uint32_t pos = s_next[q.tile] + __popc(q.cover & ((1u << q.member) - 1u));
+      const uint32_t pos = s_next[q.tile] + __popcll(q.cover & members_below(q.member));
       if (pos < m)
         ids[pos] = wave.g[q.member];
       else
@@ -693,19 +737,14 @@ __global__ void __launch_bounds__(256)
       if (kept_add[it]) s_next[kept_tile[it]] += kept_add[it];
     for (uint32_t p = threadIdx.x + kKept * blockDim.x; p < P; p += blockDim.x) {
       const WavePair q = wave_pair(wave, p, gx, col, rowm);
-      if ((q.cover & ((1u << q.member) - 1u)) == 0u) s_next[q.tile] += __popc(q.cover);
+      if ((q.cover & members_below(q.member)) == 0ull) s_next[q.tile] += __popcll(q.cover);
     }
-    uint32_t* other = s_masks + (buf ^ 1) * mask_words;
-    for (int c = threadIdx.x; c < mask_words; c += blockDim.x) other[c] = 0u;
+    unsigned long long* other = s_masks + (buf ^ 1) * mask_words;
+    for (int c = threadIdx.x; c < mask_words; c += blockDim.x) other[c] = 0ull;
     if (warp == 0) {
-      publish_wave(s_wave[buf ^ 1], lane, ahead_g, ahead_r);
-      const uint32_t i = w0 + 64 + lane;
-      ahead_g = 0u;
-      ahead_r = make_uint2(0u, 0u);
-      if (i < end) {
-        ahead_g = order[i];
-        ahead_r = sorted_rects[i];
-      }
+      publish_wave(s_wave[buf ^ 1], lane, ahead_g0, ahead_r0, ahead_g1, ahead_r1);
+      load(w0 + 2 * kWave + lane, ahead_g0, ahead_r0);
+      load(w0 + 2 * kWave + 32 + lane, ahead_g1, ahead_r1);
     }
     __syncthreads();
   }

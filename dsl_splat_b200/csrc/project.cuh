@@ -16,7 +16,8 @@ namespace splat {
 struct ProjectParams {
   int n;
   const float* means;      // (n,3)
-  const float* quats;      // (n,4) normalised wxyz
+  const float* quats;      // (n,4) normalised wxyz, or raw when normalize_quats
+  int normalize_quats;     // normalise in-kernel exactly as Torch's F.normalize does on CUDA
   const float* scales;     // (n,3)
   const float* opacities;  // (n)
   const float* view;       // 4x4 row-major world->camera
@@ -303,7 +304,8 @@ __global__ void __launch_bounds__(kProjectBlock) project_forward_kernel(ProjectP
     const float t1 = point_row(p.view, 1, m0, m1, m2);
     const float t2 = point_row(p.view, 2, m0, m1, m2);
     if (t2 <= p.near_plane || t2 >= p.far_plane) break;
-    const float4 q = reinterpret_cast<const float4*>(p.quats)[i];
+    float4 q = reinterpret_cast<const float4*>(p.quats)[i];
+    if (p.normalize_quats) q = torch_normalize4(q);
     const float3 s = make_float3(p.scales[3 * i], p.scales[3 * i + 1], p.scales[3 * i + 2]);
     const float3 cov = screen_covariance(t0, t1, t2, q, s, p.view, p.width, p.height, p.K[0], p.K[4]);
     const float a = cov.x, b = cov.y, c = cov.z;
@@ -534,8 +536,9 @@ struct ProjectBackwardParams {
   const float* seed_conics;   // (n,4) dL/dconics (incl. opacity)
   float* grad_means;          // (n,3) or null
   float* grad_quats;          // (n,4) or null
-  // When set, quats are F.normalize(quats_raw) and grad_quats receives the
-  // gradient w.r.t. quats_raw (the normalisation's VJP applied in-kernel).
+  // When set, grad_quats receives the gradient w.r.t. quats_raw (the
+  // normalisation's VJP applied in-kernel); quats may then be null, and the
+  // normalised quaternions are recomputed from quats_raw.
   const float* quats_raw;     // (n,4) or null
   float* grad_scales;         // (n,3) or null
   float* grad_opacities;      // (n)   or null
@@ -553,6 +556,12 @@ struct ProjectBackwardParams {
   float* grad_sh;             // (n,K,3)
 };
 
+// Normalised quaternion of Gaussian i: given, or recomputed from quats_raw.
+SPLAT_DEV float4 normalized_quat(const ProjectBackwardParams& p, int i) {
+  if (p.quats) return reinterpret_cast<const float4*>(p.quats)[i];
+  return torch_normalize4(reinterpret_cast<const float4*>(p.quats_raw)[i]);
+}
+
 // Hand-derived VJP of gs3d/projection.py:198-210 projection_loss for one
 // visible Gaussian.  Returns grads through the out-parameters; camera
 // partials are added into cv (view, 16) and cp (proj, 16).
@@ -561,7 +570,7 @@ SPLAT_DEV void projection_vjp(const ProjectBackwardParams& p, int i, float m0, f
   const float fx = p.K[0], fy = p.K[4];
   const float* view = p.view;
   const float* proj = p.proj;
-  const float4 q = reinterpret_cast<const float4*>(p.quats)[i];
+  const float4 q = normalized_quat(p, i);
   const float s[3] = {p.scales[3 * i], p.scales[3 * i + 1], p.scales[3 * i + 2]};
   const float2 sc = reinterpret_cast<const float2*>(p.seed_centers)[i];
   const float4 sq = reinterpret_cast<const float4*>(p.seed_conics)[i];
@@ -737,9 +746,9 @@ __global__ void __launch_bounds__(kProjectBlock) project_backward_kernel(Project
           // VJP of F.normalize(x) = x / max(|x|, 1e-12) (inputs.py:252):
           // (g - n (n . g)) / |x|, or g / 1e-12 where the norm is clamped.
           const float4 x = reinterpret_cast<const float4*>(p.quats_raw)[i];
-          const float norm = sqrtf(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+          const float norm = sqrtf((x.x * x.x + x.z * x.z) + (x.y * x.y + x.w * x.w));
           if (norm > W32(1e-12)) {
-            const float4 n = reinterpret_cast<const float4*>(p.quats)[i];
+            const float4 n = normalized_quat(p, i);
             const float d = n.x * gq[0] + n.y * gq[1] + n.z * gq[2] + n.w * gq[3];
             gq[0] = (gq[0] - n.x * d) / norm;
             gq[1] = (gq[1] - n.y * d) / norm;

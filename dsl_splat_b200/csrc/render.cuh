@@ -44,9 +44,12 @@ struct RenderParams {
   int pix_stride, ch_stride;
   float* final_t;         // (H,W)
   int* contributors;      // (H,W)
+  float* alpha_image;     // (H,W) or null: receives the appended constant channel
   // backward
-  const float* upstream;  // upstream[pixel * up_pix_stride + c * up_ch_stride]
+  const float* upstream;  // upstream[pixel * up_pix_stride + c * up_ch_stride], or null (0)
   int up_pix_stride, up_ch_stride;
+  const float* upstream_alpha;  // appended channel's upstream (pixel stride), or null: in upstream
+  int alpha_pix_stride;
   float* grad_centers;    // (n,2) accumulated
   float* grad_conics;     // (n,4) accumulated
   float* grad_a;          // (n, ch_a) accumulated, or null
@@ -294,7 +297,13 @@ __global__ void __launch_bounds__(kBlock) render_forward_kernel(RenderParams p) 
     float* out = p.image + static_cast<size_t>(pixel) * p.pix_stride;
 #pragma unroll
     for (int c = 0; c < CHP; ++c)
-      if (c < p.channels) out[c * p.ch_stride] = color[c] + T * p.background[c];
+      if (c < p.channels) {
+        const float v = color[c] + T * p.background[c];
+        if (p.alpha_image && c == p.channels - 1)
+          p.alpha_image[pixel] = v;
+        else
+          out[c * p.ch_stride] = v;
+      }
     p.final_t[pixel] = T;
     p.contributors[pixel] = last_contributor;
   }
@@ -495,12 +504,16 @@ __global__ void __launch_bounds__(kBlock / PX) render_backward_kernel(RenderPara
       const float final_T = p.final_t[pixel];
       T[i] = final_T;
       last_contributor[i] = p.contributors[pixel];
-      const float* up = p.upstream + static_cast<size_t>(pixel) * p.up_pix_stride;
+      const float* up = p.upstream ? p.upstream + static_cast<size_t>(pixel) * p.up_pix_stride
+                                   : nullptr;
       float bg_grad = 0.0f;
 #pragma unroll
       for (int c = 0; c < CHP; ++c)
         if (c < p.channels) {
-          grad[i][c] = up[c * p.up_ch_stride];
+          if (p.upstream_alpha && c == p.channels - 1)
+            grad[i][c] = p.upstream_alpha[static_cast<size_t>(pixel) * p.alpha_pix_stride];
+          else
+            grad[i][c] = up ? up[c * p.up_ch_stride] : 0.0f;
           bg_grad += p.background[c] * grad[i][c];
         }
       bg_term[i] = -final_T * bg_grad;

@@ -77,19 +77,23 @@ ChunkPlan chunk_plan(long long n, int gx, int gy) {
   ChunkPlan c;
   const size_t T = static_cast<size_t>(gx) * gy;
   c.smem_counts = 4 * static_cast<size_t>(gx + 1) * (gy + 1);
-  c.smem_scatter = 4 * (T + 2 * static_cast<size_t>(gx + gy));
+  c.smem_scatter = 4 * T + 16 * static_cast<size_t>(gx + gy);
   if (c.smem_counts > kChunkSmemLimit || c.smem_scatter > kChunkSmemLimit) return c;
   // the uint32 work prefix (tiles + kChunkGaussianCost per Gaussian) must not wrap
   if (n > (1LL << 27)) return c;
   c.use = true;
-  // about 2048 Gaussians per chunk on average (chunks are cut by work, not
-  // by count), fewer chunks when the chunk-by-tile matrix would grow large
-  size_t chunk = 2048;
+  // Chunks are cut by work, not by count: about 1536 Gaussians each, and
+  // large jobs get a whole number of rounds of kScatterSlots resident CTAs
+  // (148 SMs x 6 by shared memory at 1080p; a fixed count keeps the plan
+  // independent of the device queried).  Fewer chunks when the
+  // chunk-by-tile matrix would grow large.
+  constexpr size_t kScatterSlots = 148 * 6;
   const size_t nn = static_cast<size_t>(n > 0 ? n : 1);
-  if (nn * T * 4 / chunk > kChunkMatrixLimit)
-    chunk = ((nn * T * 4 + kChunkMatrixLimit - 1) / kChunkMatrixLimit + 31) / 32 * 32;
-  c.chunk = static_cast<uint32_t>(chunk);
-  c.chunks = static_cast<unsigned>((nn + chunk - 1) / chunk);
+  size_t chunks = (nn + 1535) / 1536;
+  if (chunks > kScatterSlots / 2) chunks = (chunks + kScatterSlots - 1) / kScatterSlots * kScatterSlots;
+  const size_t max_chunks = std::max<size_t>(1, kChunkMatrixLimit / (4 * T));
+  c.chunks = static_cast<unsigned>(std::min(chunks, max_chunks));
+  c.chunk = static_cast<uint32_t>((nn + c.chunks - 1) / c.chunks);
   return c;
 }
 
@@ -350,7 +354,8 @@ int splat_project_forward(int n, const float* means, const float* quats, const f
 }
 
 int splat_project_forward_fused(int n, const float* means, const float* quats,
-                                const float* scales, const float* opacities, const float* view,
+                                int normalize_quats, const float* scales,
+                                const float* opacities, const float* view,
                                 const float* proj, const float* K, int width, int height,
                                 float near_plane, float far_plane, float radius_clip,
                                 float* centers, float* conics, int* radii, int* tiles,
@@ -365,10 +370,12 @@ int splat_project_forward_fused(int n, const float* means, const float* quats,
   if (meta_means2d && (!meta_opacities || !meta_conics))
     return fail(kInvalidArgument, "metadata outputs come together");
   if (!aligned(meta_means2d, 8)) return fail(kInvalidArgument, "means2d needs 8-byte alignment");
+  if (!aligned(quats, 16)) return fail(kInvalidArgument, "quats need 16-byte alignment");
   ProjectParams p{};
   p.n = n;
   p.means = means;
   p.quats = quats;
+  p.normalize_quats = normalize_quats ? 1 : 0;
   p.scales = scales;
   p.opacities = opacities;
   p.view = view;
@@ -453,6 +460,7 @@ int splat_project_backward_fused(int n, const float* means, const float* quats,
   if (grad_sh && (!sh || !active || !grad_colors || sh_degree < 0 || sh_degree > 3 ||
                   sh_k < (sh_degree + 1) * (sh_degree + 1)))
     return fail(kInvalidArgument, "bad SH backward arguments");
+  if (!quats && !quats_raw) return fail(kInvalidArgument, "quats or quats_raw is required");
   if (!aligned(quats, 16) || !aligned(quats_raw, 16) || !aligned(grad_quats, 16) ||
       !aligned(grad_conics, 16) ||
       !aligned(grad_centers, 8))
@@ -717,8 +725,8 @@ int splat_bin_prepare(int n, const float* centers, const int* radii, const int* 
                            static_cast<int>(plan.smem_counts));
     chunk_counts_kernel<<<plan.chunks, 256, plan.smem_counts, counted(s)>>>(
         vals_a, bounds, rects, gx, gy, at<uint2>(ws, L.sorted_rects), cnt);
-    chunk_prefix_kernel<<<blocks_for(T, 32), 256, 0, counted(s)>>>(cnt, plan.chunks, T,
-                                                                     tile_totals);
+    chunk_prefix_kernel<<<blocks_for(T, 32), 1024, 0, counted(s)>>>(cnt, plan.chunks, T,
+                                                                      tile_totals);
     tile_ranges_kernel<<<1, 1024, 0, counted(s)>>>(tile_totals, T, ranges,
                                                    at<uint32_t>(ws, L.tile_starts), totals + 1);
   } else {
@@ -814,9 +822,9 @@ int splat_render_forward_statistics(
     int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
     const float* centers, const float* conics, const float* feat_a, int ch_a, int stride_a,
     const float* feat_b, int ch_b, int stride_b, int append_one, const float* background,
-    float* image, int pix_stride, int ch_stride, float* final_t, int* contributors,
-    int stat_count, int stat_sum_mask, const float* stat_pixels, int* stat_counts,
-    float* stat_sums, void* stream) {
+    float* image, int pix_stride, int ch_stride, float* alpha_image, float* final_t,
+    int* contributors, int stat_count, int stat_sum_mask, const float* stat_pixels,
+    int* stat_counts, float* stat_sums, void* stream) {
   if (width <= 0 || height <= 0 || ch_a < 0 || ch_b < 0 || (ch_b > 0 && !feat_b) || n < 0 ||
       num_ids < 0 || num_ids >= (1LL << 31))
     return fail(kInvalidArgument, "bad render sizes");
@@ -842,9 +850,12 @@ int splat_render_forward_statistics(
   p.append_one = append_one ? 1 : 0;
   p.channels = ch_a + ch_b + p.append_one;
   p.background = background;
+  if (alpha_image && !append_one)
+    return fail(kInvalidArgument, "alpha_image holds the appended constant channel");
   p.image = image;
   p.pix_stride = pix_stride;
   p.ch_stride = ch_stride;
+  p.alpha_image = alpha_image;
   p.final_t = final_t;
   p.contributors = contributors;
   p.stat_count = stat_count;
@@ -861,13 +872,13 @@ int splat_render_forward(int width, int height, const int* ranges, const int* id
                          long long num_ids, int n, const float* centers, const float* conics,
                          const float* feat_a, int ch_a, int stride_a, const float* feat_b,
                          int ch_b, int stride_b, int append_one, const float* background,
-                         float* image, int pix_stride, int ch_stride, float* final_t,
-                         int* contributors, void* stream) {
+                         float* image, int pix_stride, int ch_stride, float* alpha_image,
+                         float* final_t, int* contributors, void* stream) {
   return splat_render_forward_statistics(width, height, ranges, ids, num_ids, n, centers, conics,
                                          feat_a, ch_a, stride_a, feat_b, ch_b, stride_b,
                                          append_one, background, image, pix_stride, ch_stride,
-                                         final_t, contributors, 0, 0, nullptr, nullptr, nullptr,
-                                         stream);
+                                         alpha_image, final_t, contributors, 0, 0, nullptr,
+                                         nullptr, nullptr, stream);
 }
 
 int splat_render_backward(int width, int height, const int* ranges, const int* ids,
@@ -876,7 +887,8 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
                           int ch_a, int stride_a, const float* feat_b, int ch_b, int stride_b,
                           int append_one, const float* background, const float* final_t,
                           const int* contributors, const float* upstream, int up_pix_stride,
-                          int up_ch_stride, float* grad_centers, float* grad_conics,
+                          int up_ch_stride, const float* upstream_alpha, int alpha_pix_stride,
+                          float* grad_centers, float* grad_conics,
                           float* grad_a, float* grad_b, float* abs_centers, int constant_tail,
                           void* stream) {
   if (width <= 0 || height <= 0 || ch_a < 0 || ch_b < 0 || (ch_b > 0 && !feat_b) || n < 0 ||
@@ -903,9 +915,13 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
   p.background = background;
   p.final_t = const_cast<float*>(final_t);
   p.contributors = const_cast<int*>(contributors);
+  if (upstream_alpha && !append_one)
+    return fail(kInvalidArgument, "upstream_alpha belongs to the appended constant channel");
   p.upstream = upstream;
   p.up_pix_stride = up_pix_stride;
   p.up_ch_stride = up_ch_stride;
+  p.upstream_alpha = upstream_alpha;
+  p.alpha_pix_stride = alpha_pix_stride;
   p.grad_centers = grad_centers;
   p.grad_conics = grad_conics;
   p.grad_a = grad_a;

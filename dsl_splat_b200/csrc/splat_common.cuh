@@ -73,6 +73,19 @@ SPLAT_DEV float splat_expf_core(float x) {
   return __fmul_rn(p, scale);
 }
 
+// F.normalize(x, dim=-1) for one wxyz quaternion with the bits Torch's CUDA
+// kernels produce (inputs.py:252): x / clamp_min(|x|, 1e-12), where |x|^2 is
+// summed as (x0^2 + x2^2) + (x1^2 + x3^2) and every operation is a single
+// IEEE float32 operation (NaN norms propagate like clamp_min).
+SPLAT_DEV float4 torch_normalize4(float4 x) {
+  const float sq = __fadd_rn(__fadd_rn(__fmul_rn(x.x, x.x), __fmul_rn(x.z, x.z)),
+                             __fadd_rn(__fmul_rn(x.y, x.y), __fmul_rn(x.w, x.w)));
+  float norm = __fsqrt_rn(sq);
+  if (norm < W32(1e-12)) norm = W32(1e-12);
+  return make_float4(__fdiv_rn(x.x, norm), __fdiv_rn(x.y, norm), __fdiv_rn(x.z, norm),
+                     __fdiv_rn(x.w, norm));
+}
+
 // splatting/geometry.py:22-30 tile_bounds: CUDA getRect truncation.
 SPLAT_DEV int4 tile_bounds(float cx, float cy, int radius, int gx, int gy) {
   const float r = static_cast<float>(radius);

@@ -14,7 +14,6 @@ from numbers import Integral
 from typing import Any, Sequence
 
 import torch
-import torch.nn.functional as F
 from torch import Tensor
 
 from ..camera_prep import ViewConfig, prepare_cameras, prepare_cameras_with_centers
@@ -92,8 +91,8 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
     validate_tile_mode(tile_mode)
     validate_camera_options(width, height, near_plane, far_plane, radius_clip)
     sh_degree = _check_sh(sh_coeffs, sh_degree, features)
-    # Quaternions are normalised per batch below (the same Torch op as
-    # inputs.py:252) outside autograd; ProjectView applies its VJP in-kernel.
+    # Quaternions reach the projection kernels raw: they apply inputs.py:252's
+    # F.normalize with Torch's CUDA bits and its VJP in the backward.
     layout = normalize_inputs(means, quats, scales, opacities,
                               features if sh_coeffs is None else sh_coeffs, viewmats, Ks,
                               backgrounds, extra_features, None, sh_degree,
@@ -116,15 +115,13 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
     for b in range(layout.batch_count):
         bm, bq = layout.means[b], layout.quats[b]
         bs, bo = layout.scales[b], layout.opacities[b]
-        with torch.no_grad():
-            bqn = F.normalize(bq, dim=-1)
         for c in range(layout.cameras):
             view = batch_item(batch_item(layout.viewmats, b), c)
             proj = batch_item(batch_item(full, b), c)
             K = batch_item(batch_item(layout.Ks, b), c)
             campos = batch_item(batch_item(centers, b), c) if with_centers else None
             values = layout.colors.at(b, c)
-            out = ProjectView.apply(bm, bq, bqn, bs, bo,
+            out = ProjectView.apply(bm, bq, bs, bo,
                                     values if sh_degree is not None else None, view, proj,
                                     campos, K, config, sh_degree, grad_enabled)
             ctr, con, col, radii, tiles, depths, m2d, mop, mcon = out
@@ -156,22 +153,28 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
         if statistics else ([], {}))
     bins = stages.bin_and_sort_many([f[7] for f in frames], width, height, camera_status)
     channels = layout.colors.channels
-    images = []
+    blended, alphas = [], []
     for i, (b, c, ctr, con, colors, extras, bg, _state) in enumerate(frames):
         screen = None if training.screen is None else batch_item(batch_item(training.screen, b), c)
         total = channels + (0 if extras is None else extras.shape[-1]) + 1
         packed_bg = ctr.new_zeros(total)
         if bg is not None:
             packed_bg[:channels] = bg
-        image = RenderView.apply(ctr, con, colors, extras, screen, packed_bg, bins[i]["ranges"],
-                                 bins[i]["point_list"], config, training.absolute_targets[i],
-                                 prepared_stats[i] if statistics else None, grad_enabled)
-        images.append(image)
+        main, alpha = RenderView.apply(ctr, con, colors, extras, screen, packed_bg,
+                                       bins[i]["ranges"], bins[i]["point_list"], config,
+                                       training.absolute_targets[i],
+                                       prepared_stats[i] if statistics else None, grad_enabled)
+        blended.append(main)
+        alphas.append(alpha)
     shape = layout.batch_dims + (layout.cameras, height, width)
-    if len(images) == 1:
-        images = images[0].reshape(shape + (images[0].shape[-1],))
-    else:
-        images = torch.stack(images).reshape(shape + (images[0].shape[-1],))
+
+    def assemble(parts: list[Tensor]) -> Tensor:
+        whole = parts[0] if len(parts) == 1 else torch.stack(parts)
+        return whole.reshape(shape + (parts[0].shape[-1],))
+
+    main, alpha = assemble(blended), assemble(alphas)
+    features = main
     if layout.extras is not None:
-        meta["render_extra_signals"] = images[..., channels:-1]
-    return RasterizationResult(images[..., :channels], images[..., -1:], meta, statistics_outputs)
+        meta["render_extra_signals"] = main[..., channels:]
+        features = main[..., :channels]
+    return RasterizationResult(features, alpha, meta, statistics_outputs)

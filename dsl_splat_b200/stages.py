@@ -104,6 +104,7 @@ class RenderedPixels:
     features: Tensor       # (H, W, C') interleaved, or (C', H, W) planar
     transmittance: Tensor  # (H, W)
     contributors: Tensor   # (H, W) int32
+    alpha: Tensor | None = None  # (H, W, 1) when rendered apart (features then hold C'-1)
 
 
 # ---- cameras ---------------------------------------------------------------
@@ -189,8 +190,12 @@ class FusedProjection:
 
 def project_fused(means, quats, scales, opacities, view, projection, intrinsics, width, height,
                   near, far, radius_clip, sh: Tensor | None = None, sh_degree: int = 0,
-                  campos: Tensor | None = None, need_active: bool = True) -> FusedProjection:
-    """One launch for gs3d/api.py:145-189: projection, masked SH and metadata."""
+                  campos: Tensor | None = None, need_active: bool = True,
+                  normalize_quats: bool = False) -> FusedProjection:
+    """One launch for gs3d/api.py:145-189: projection, masked SH and metadata.
+
+    normalize_quats: quats are raw; the kernel applies F.normalize with the
+    bits of Torch's CUDA implementation (inputs.py:252)."""
     pin = Args()
     n = len(means)
     dev = means.device
@@ -204,7 +209,7 @@ def project_fused(means, quats, scales, opacities, view, projection, intrinsics,
     if n:
         sh_c = _c(sh)
         check(lib.splat_project_forward_fused(
-            n, pin(means), pin(quats), pin(scales), pin(opacities),
+            n, pin(means), pin(quats), int(normalize_quats), pin(scales), pin(opacities),
             pin(view), pin(projection), pin(intrinsics), width, height, float(near),
             _far(far), float(radius_clip), ptr(state.centers), ptr(state.conics),
             ptr(state.radii), ptr(state.tile_counts), ptr(state.depths), int(sh_degree),
@@ -369,23 +374,29 @@ def _features(feat_a: Tensor, feat_b: Tensor | None):
 
 def render(state: ProjectedFootprint, bins: dict, feat_a: Tensor, feat_b: Tensor | None,
            append_one: bool, background: Tensor, width: int, height: int,
-           planar: bool = False, statistics=None) -> RenderedPixels:
+           planar: bool = False, statistics=None, separate_alpha: bool = False) -> RenderedPixels:
     """gs3d/render.py:359-406.  Channels: feat_a, feat_b, then a constant 1.
 
     statistics: a PreparedStatistics (statistics.py) whose counts/sums rows
-    receive this view's accepted contributions."""
+    receive this view's accepted contributions.  separate_alpha (interleaved,
+    append_one): the constant channel -- alpha -- goes to its own (H, W, 1)
+    buffer and features hold the other channels."""
     pin = Args()
     a, b, ca, cb = _features(feat_a, feat_b)
     channels = ca + cb + int(append_one)
     dev = a.device
+    if separate_alpha and (planar or not append_one):
+        raise ValueError("separate_alpha needs interleaved output with the constant channel")
+    alpha = a.new_empty((height, width, 1)) if separate_alpha else None
+    stored = channels - int(separate_alpha)
     if planar:
         image = a.new_empty((channels, height, width))
         pix_stride, ch_stride = 1, height * width
     else:
-        image = a.new_empty((height, width, channels))
-        pix_stride, ch_stride = channels, 1
+        image = a.new_empty((height, width, stored))
+        pix_stride, ch_stride = stored, 1
     out = RenderedPixels(image, a.new_empty((height, width)),
-                         torch.empty((height, width), dtype=torch.int32, device=dev))
+                         torch.empty((height, width), dtype=torch.int32, device=dev), alpha)
     if statistics is None:
         stat = (0, 0, None, None, None)
     else:
@@ -397,38 +408,56 @@ def render(state: ProjectedFootprint, bins: dict, feat_a: Tensor, feat_b: Tensor
             width, height, ptr(bins["ranges"]), ptr(bins["point_list"]), len(bins["point_list"]),
             len(state.centers), pin(state.centers),
             pin(state.conics), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
-            pin(background), ptr(image), pix_stride, ch_stride,
+            pin(background), ptr(image), pix_stride, ch_stride, ptr(alpha),
             ptr(out.transmittance), ptr(out.contributors), *stat, nv.stream(dev)), "render_forward")
     return out
 
 
 def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
                     feat_b: Tensor | None, append_one: bool, background: Tensor,
-                    final_t: Tensor, contributors: Tensor, gradient: Tensor, width: int,
+                    final_t: Tensor, contributors: Tensor, gradient: Tensor | None, width: int,
                     height: int, *, planar: bool = False, absgrad: bool = False,
-                    constant_tail: int = 0, need_a: bool = True, need_b: bool = True):
-    """gs3d/render.py:409-463: grads of centers, conics, feat_a, feat_b, abs."""
+                    constant_tail: int = 0, need_a: bool = True, need_b: bool = True,
+                    gradient_alpha: Tensor | None = None, separate_alpha: bool = False,
+                    absolute_out: Tensor | None = None):
+    """gs3d/render.py:409-463: grads of centers, conics, feat_a, feat_b, abs.
+
+    separate_alpha: gradient holds the channels before the constant one
+    (H, W, C'-1) and gradient_alpha (H, W, 1) the constant channel's; either
+    may be None (zero).  absolute_out: a zeroed contiguous (n, 2) buffer that
+    receives the |d centers| sums in place of a new one."""
     pin = Args()
     a, b, ca, cb = _features(feat_a, feat_b)
     channels = ca + cb + int(append_one)
     if not 0 <= constant_tail <= channels:
         raise ValueError("constant_tail must be within the feature channel count")
-    g = gradient.contiguous()
+    if separate_alpha and (planar or not append_one):
+        raise ValueError("separate_alpha needs interleaved output with the constant channel")
+    stored = channels - int(separate_alpha)
+    g = None if gradient is None else gradient.contiguous()
+    g_alpha = None if gradient_alpha is None else gradient_alpha.contiguous()
+    alpha_stride = 1
+    if separate_alpha and g_alpha is None:
+        # the constant channel's upstream is not in `gradient`: read zero
+        g_alpha, alpha_stride = a.new_zeros(1), 0
     if planar:
         pix_stride, ch_stride = 1, height * width
     else:
-        pix_stride, ch_stride = channels, 1
+        pix_stride, ch_stride = stored, 1
     centers = torch.zeros_like(state.centers)
     conics = torch.zeros_like(state.conics)
     ga = torch.zeros_like(a) if need_a else None
     gb = torch.zeros_like(b) if (b is not None and need_b) else None
-    absolute = torch.zeros_like(state.centers) if absgrad else None
+    if absgrad:
+        absolute = absolute_out if absolute_out is not None else torch.zeros_like(state.centers)
+    else:
+        absolute = None
     with _timed("render_backward", a.device):
         check(lib.splat_render_backward(
             width, height, ptr(bins["ranges"]), ptr(bins["point_list"]), len(bins["point_list"]),
             len(state.centers), pin(state.centers),
             pin(state.conics), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
             pin(background), pin(final_t), pin(contributors),
-            ptr(g), pix_stride, ch_stride, ptr(centers), ptr(conics), ptr(ga), ptr(gb),
-            ptr(absolute), constant_tail, nv.stream(a.device)), "render_backward")
+            ptr(g), pix_stride, ch_stride, ptr(g_alpha), alpha_stride, ptr(centers), ptr(conics), ptr(ga),
+            ptr(gb), ptr(absolute), constant_tail, nv.stream(a.device)), "render_backward")
     return centers, conics, ga, gb, absolute

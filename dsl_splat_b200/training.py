@@ -18,11 +18,25 @@ class AbsGradientTarget:
 
     target: Tensor
     gaussian_ids: Tensor | None = None
+    written: bool = False
 
     @torch.no_grad()
     def write(self, gradient: Tensor) -> None:
         value = gradient if self.gaussian_ids is None else gradient[self.gaussian_ids]
         self.target.copy_(value)
+        self.written = True
+
+    def direct_buffer(self) -> Tensor | None:
+        """The target itself when a kernel may accumulate into it directly: a
+        dense, contiguous view that still holds the zeros it was created with
+        (the first backward through it).  Later backwards use write(), which
+        replaces the values as the reference's copy does."""
+        if self.written or self.gaussian_ids is not None or not self.target.is_contiguous():
+            return None
+        if self.target.dtype != torch.float32 or self.target.data_ptr() % 8:
+            return None
+        self.written = True
+        return self.target
 
 
 @dataclass(slots=True)

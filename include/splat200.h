@@ -61,9 +61,12 @@ int splat_project_forward(int n, const float* means, const float* quats, const f
  * (sh.py:44-79; directions means - campos, campos NULL for SH0) writing
  * colors[i*color_stride + 0..2] and active (n,3), and the dense metadata of
  * splatting/metadata.py:34-70 (means2d (n,2), opacities (n), conics (n,3)).
- * sh == NULL skips SH; meta_means2d == NULL skips metadata. */
+ * sh == NULL skips SH; meta_means2d == NULL skips metadata.  normalize_quats != 0:
+ * quats are raw and are normalised in-kernel with the bits of Torch's CUDA
+ * F.normalize(quats, dim=-1) (inputs.py:252). */
 int splat_project_forward_fused(int n, const float* means, const float* quats,
-                                const float* scales, const float* opacities, const float* view,
+                                int normalize_quats, const float* scales,
+                                const float* opacities, const float* view,
                                 const float* proj, const float* K, int width, int height,
                                 float near_plane, float far_plane, float radius_clip,
                                 float* centers, float* conics, int* radii, int* tiles,
@@ -95,7 +98,9 @@ int splat_project_backward(int n, const float* means, const float* quats, const 
  * NULL or float[35] (view 16, proj 16, campos 3), always added into.
  * quats_raw: NULL, or the unnormalised quaternions whose F.normalize gave
  * quats (inputs.py:252); grad_quats then receives the gradient w.r.t.
- * quats_raw (the normalisation's VJP is applied in the kernel). */
+ * quats_raw (the normalisation's VJP is applied in the kernel), and quats
+ * may be NULL (recomputed from quats_raw as splat_project_forward_fused
+ * normalises them). */
 int splat_project_backward_fused(int n, const float* means, const float* quats,
                                  const float* quats_raw, const float* scales,
                                  const float* view, const float* proj,
@@ -168,14 +173,17 @@ int splat_bin_emit(int n, long long pairs, int width, int height, void* workspac
  * ones]) of gs3d/autograd.py:306-311 without materialising it.
  * background (channels).  image[pixel*pix_stride + c*ch_stride]; planar
  * (C,H,W) is pix_stride=1, ch_stride=H*W; interleaved (H,W,C) is
- * pix_stride=C, ch_stride=1.  ids holds num_ids entries (tile ranges are
- * clamped to it) of Gaussian indices in [0, n).  At most 32 channels. */
+ * pix_stride=C, ch_stride=1.  alpha_image (H,W), when not NULL (append_one
+ * only), receives the constant channel -- the alpha output -- instead of
+ * image, so colour and alpha are separate dense buffers.  ids holds num_ids
+ * entries (tile ranges are clamped to it) of Gaussian indices in [0, n).  At
+ * most 32 channels. */
 int splat_render_forward(int width, int height, const int* ranges, const int* ids,
                          long long num_ids, int n, const float* centers, const float* conics,
                          const float* feat_a, int ch_a, int stride_a, const float* feat_b,
                          int ch_b, int stride_b, int append_one, const float* background,
-                         float* image, int pix_stride, int ch_stride, float* final_t,
-                         int* contributors, void* stream);
+                         float* image, int pix_stride, int ch_stride, float* alpha_image,
+                         float* final_t, int* contributors, void* stream);
 
 /* gs3d/render.py:129-169 render with contribution statistics (statistics.py:
  * 47-73, 393-418): as splat_render_forward, plus stat_count requests whose
@@ -188,21 +196,25 @@ int splat_render_forward_statistics(
     int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
     const float* centers, const float* conics, const float* feat_a, int ch_a, int stride_a,
     const float* feat_b, int ch_b, int stride_b, int append_one, const float* background,
-    float* image, int pix_stride, int ch_stride, float* final_t, int* contributors,
-    int stat_count, int stat_sum_mask, const float* stat_pixels, int* stat_counts,
-    float* stat_sums, void* stream);
+    float* image, int pix_stride, int ch_stride, float* alpha_image, float* final_t,
+    int* contributors, int stat_count, int stat_sum_mask, const float* stat_pixels,
+    int* stat_counts, float* stat_sums, void* stream);
 
 /* gs3d/render.py:409-463 backward -> :221-354.  Gradients are ADDED into
  * grad_centers (n,2), grad_conics (n,4), grad_a (n,ch_a), grad_b (n,ch_b)
  * and abs_centers (n,2) (NULL to skip a, b or abs); the last constant_tail
- * channels receive no feature gradient. */
+ * channels receive no feature gradient.  The upstream gradient of channel c
+ * is upstream[pixel*up_pix_stride + c*up_ch_stride] (upstream NULL: zero),
+ * except the appended constant channel when upstream_alpha is not NULL:
+ * upstream_alpha[pixel*alpha_pix_stride]. */
 int splat_render_backward(int width, int height, const int* ranges, const int* ids,
                           long long num_ids, int n, const float* centers, const float* conics,
                           const float* feat_a,
                           int ch_a, int stride_a, const float* feat_b, int ch_b, int stride_b,
                           int append_one, const float* background, const float* final_t,
                           const int* contributors, const float* upstream, int up_pix_stride,
-                          int up_ch_stride, float* grad_centers, float* grad_conics,
+                          int up_ch_stride, const float* upstream_alpha, int alpha_pix_stride,
+                          float* grad_centers, float* grad_conics,
                           float* grad_a, float* grad_b, float* abs_centers, int constant_tail,
                           void* stream);
 

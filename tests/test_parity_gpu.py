@@ -179,6 +179,68 @@ def test_render_backward(case):
 
 
 @pytest.mark.parametrize("case", list(CASES))
+def test_render_separate_alpha(case):
+    """Colour and alpha in separate buffers (forward) and separate upstream
+    gradients (backward) give the combined layout's values exactly."""
+    p, out, bins, r, bg = _render_case(case)
+    d = _dev()
+    bg_t = torch.from_numpy(bg).to(d)
+    px = stages.render(out.state, bins, out.colors, None, True, bg_t, p.W, p.H)
+    sep = stages.render(out.state, bins, out.colors, None, True, bg_t, p.W, p.H,
+                        separate_alpha=True)
+    assert torch.equal(sep.features, px.features[..., :3])
+    assert torch.equal(sep.alpha, px.features[..., 3:])
+    assert torch.equal(sep.contributors, px.contributors)
+    up = torch.from_numpy(np.random.default_rng(7).standard_normal((p.H, p.W, 4))
+                          .astype(np.float32)).to(d)
+    kw = dict(absgrad=True, constant_tail=1)
+    whole = stages.render_backward(out.state, bins, out.colors, None, True, bg_t,
+                                   px.transmittance, px.contributors, up, p.W, p.H, **kw)
+    split = stages.render_backward(out.state, bins, out.colors, None, True, bg_t,
+                                   px.transmittance, px.contributors, up[..., :3].contiguous(),
+                                   p.W, p.H, gradient_alpha=up[..., 3:].contiguous(),
+                                   separate_alpha=True, **kw)
+    for a, b in zip(whole, split):
+        if a is not None:
+            assert rel_l2(b.cpu().numpy(), a.cpu().numpy()) <= 1e-5
+    # a missing alpha gradient reads as zero, not as a neighbouring colour
+    no_alpha = stages.render_backward(out.state, bins, out.colors, None, True, bg_t,
+                                      px.transmittance, px.contributors,
+                                      up[..., :3].contiguous(), p.W, p.H,
+                                      separate_alpha=True, **kw)
+    up0 = up.clone()
+    up0[..., 3] = 0
+    ref0 = stages.render_backward(out.state, bins, out.colors, None, True, bg_t,
+                                  px.transmittance, px.contributors, up0, p.W, p.H, **kw)
+    for a, b in zip(ref0, no_alpha):
+        if a is not None:
+            assert rel_l2(b.cpu().numpy(), a.cpu().numpy()) <= 1e-5
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_projection_normalizes_raw_quaternions(case):
+    """normalize_quats: the kernel's normalisation is bit-identical to Torch's
+    CUDA F.normalize followed by the projection."""
+    p = Prepared(_scene(case))
+    d = _dev()
+    raw = p.s.quats.to(d) * torch.linspace(1e-3, 40.0, len(p.means), device=d)[:, None]
+    ref = stages.project_fused(p.means, F.normalize(raw, dim=-1), p.scales, p.opac, p.view,
+                               p.full, p.K, p.W, p.H, 0.2, float("inf"), 0.0, sh=p.sh,
+                               sh_degree=p.deg, campos=p.campos)
+    got = stages.project_fused(p.means, raw, p.scales, p.opac, p.view, p.full, p.K, p.W, p.H,
+                               0.2, float("inf"), 0.0, sh=p.sh, sh_degree=p.deg,
+                               campos=p.campos, normalize_quats=True)
+    assert torch.equal(got.state.radii, ref.state.radii)
+    assert torch.equal(got.state.tile_counts, ref.state.tile_counts)
+    # culled rows of centers/conics/depths are left unwritten, as the
+    # reference's new_empty outputs are (gs3d/projection.py:324-328)
+    vis = ref.state.radii > 0
+    for name in ("centers", "conics", "depths"):
+        assert torch.equal(getattr(got.state, name)[vis], getattr(ref.state, name)[vis]), name
+    assert torch.equal(got.colors, ref.colors)
+
+
+@pytest.mark.parametrize("case", list(CASES))
 def test_projection_backward(case):
     p = Prepared(_scene(case))
     out = p.project()
