@@ -309,6 +309,130 @@ __global__ void __launch_bounds__(kBlock) render_forward_kernel(RenderParams p) 
   }
 }
 
+// The sample exponent of two pixels in one column (same dx), with
+// sample_power's operation order: (-0.5*((a*dx)*dx + (c*dy)*dy)) - (b*dx)*dy.
+// Scalar on purpose: ptxas contracts a packed multiply feeding a packed add
+// into one fused multiply-add even under --fmad=false and .rn (measured on
+// sm_100a), which would change these bits; the packed exp below has no
+// multiply feeding an add outside its explicit fmas.
+SPLAT_DEV f32x2 sample_power2(float4 q, float dx, float dy0, float dy1) {
+  const float adx2 = (q.x * dx) * dx;
+  const float bdx = q.y * dx;
+  const float p0 = (-0.5f * (adx2 + (q.z * dy0) * dy0)) - bdx * dy0;
+  const float p1 = (-0.5f * (adx2 + (q.z * dy1) * dy1)) - bdx * dy1;
+  return pack2(p0, p1);
+}
+
+// Forward blend with two pixels per lane (kBlock / 2 threads per tile; warp
+// w owns the 8x8 block, lane l the pixels (l % 8, l / 8) and (l % 8,
+// l / 8 + 4)).  Per candidate the exponent, exp, alpha and transmittance of
+// both pixels are computed as f32x2 pairs -- the same bits as the scalar
+// kernel -- and each pixel then blends, ends or skips on its own.
+template <int CHP>
+__global__ void __launch_bounds__(kBlock / 2) render_forward2_kernel(RenderParams p) {
+  extern __shared__ float4 s_dynamic[];  // the staged batch (sizeof(RenderShared<CHP>) bytes)
+  RenderShared<CHP>& s = *reinterpret_cast<RenderShared<CHP>*>(s_dynamic);
+  __shared__ uint8_t s_list[kBlock / 64][kBlock];
+  uint8_t* list = s_list[threadIdx.x >> 5];
+  const int tile = blockIdx.x;
+  const PixelSlot<2> ps = pixel_slot<2>(tile, p.gx);
+  const int x = ps.x, y0 = ps.y, y1 = ps.y + 4;
+  const bool inside0 = x < p.width && y0 < p.height;
+  const bool inside1 = x < p.width && y1 < p.height;
+  const float fx = static_cast<float>(x);
+  const float fy0 = static_cast<float>(y0), fy1 = static_cast<float>(y1);
+  const int first = max(p.ranges[2 * tile], 0);
+  const int last = min(p.ranges[2 * tile + 1], p.num_ids);
+  const float threshold = 1.0f / 255.0f;
+  bool done0 = !inside0, done1 = !inside1;
+  float T0 = 1.0f, T1 = 1.0f;
+  float color0[CHP], color1[CHP];
+#pragma unroll
+  for (int c = 0; c < CHP; ++c) color0[c] = color1[c] = 0.0f;
+  int last0 = 0, last1 = 0;
+  for (int begin = first; begin < last; begin += kBlock) {
+    if (__syncthreads_count(done0 && done1) == static_cast<int>(blockDim.x)) break;
+    for (int slot = threadIdx.x; slot < kBlock; slot += blockDim.x) {
+      const int idx = begin + slot;
+      if (idx < last) stage_gaussian<CHP>(p, s, slot, p.ids[idx]);
+    }
+    __syncthreads();
+    const int count = min(kBlock, last - begin);
+    const int candidates = warp_candidates(s, ps, 0, count, list);
+    for (int k = 0; k < candidates && !(done0 && done1); ++k) {
+      const int j = list[k];
+      const float4 q = s.conic[j];
+      const float4 gm = s.geom[j];
+      const float cut = s.cut[j];
+      const float dx = gm.x - fx;
+      const f32x2 power = sample_power2(q, dx, gm.y - fy0, gm.y - fy1);
+      float pw0, pw1;
+      unpack2(power, pw0, pw1);
+      const bool range0 = !done0 && pw0 <= 0.0f && pw0 >= cut;
+      const bool range1 = !done1 && pw1 <= 0.0f && pw1 >= cut;
+      if (!(range0 || range1)) continue;
+      // a pixel out of range may hold any exponent here; its result is unused
+      float a0, a1;
+      unpack2(mul2(splat2(q.w), splat_expf_core2(power)), a0, a1);
+      a0 = wmin(W32(0.99), a0);
+      a1 = wmin(W32(0.99), a1);
+      const bool accept0 = range0 && a0 >= threshold;
+      const bool accept1 = range1 && a1 >= threshold;
+      if (!(accept0 || accept1)) continue;
+      const f32x2 alpha = pack2(a0, a1), t = pack2(T0, T1);
+      float n0, n1, w0, w1;
+      unpack2(mul2(t, sub2(splat2(1.0f), alpha)), n0, n1);  // T * (1 - alpha)
+      unpack2(mul2(alpha, t), w0, w1);                      // alpha * T
+      float f[CHP];
+      load_features(s, j, f);
+      const int position = begin - first + j + 1;
+      // gs3d/render.py: a sample that would take T below 1e-4 ends the pixel
+      // without being blended
+      if (accept0) {
+        if (n0 < W32(0.0001)) {
+          done0 = true;
+        } else {
+#pragma unroll
+          for (int c = 0; c < CHP; ++c) color0[c] = __fmaf_rn(f[c], w0, color0[c]);
+          if (p.stat_count) observe(p, s.id[j], y0 * p.width + x, w0);
+          T0 = n0;
+          last0 = position;
+        }
+      }
+      if (accept1) {
+        if (n1 < W32(0.0001)) {
+          done1 = true;
+        } else {
+#pragma unroll
+          for (int c = 0; c < CHP; ++c) color1[c] = __fmaf_rn(f[c], w1, color1[c]);
+          if (p.stat_count) observe(p, s.id[j], y1 * p.width + x, w1);
+          T1 = n1;
+          last1 = position;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool inside = i ? inside1 : inside0;
+    if (!inside) continue;
+    const int pixel = (i ? y1 : y0) * p.width + x;
+    const float T = i ? T1 : T0;
+    float* out = p.image + static_cast<size_t>(pixel) * p.pix_stride;
+#pragma unroll
+    for (int c = 0; c < CHP; ++c)
+      if (c < p.channels) {
+        const float v = (i ? color1[c] : color0[c]) + T * p.background[c];
+        if (p.alpha_image && c == p.channels - 1)
+          p.alpha_image[pixel] = v;
+        else
+          out[c * p.ch_stride] = v;
+      }
+    p.final_t[pixel] = T;
+    p.contributors[pixel] = i ? last1 : last0;
+  }
+}
+
 // Butterfly (transpose) reduction of 16 values over the 32 lanes of a warp:
 // 8 + 4 + 2 + 1 + 1 shuffles.  Returns, in every lane, the warp total of
 // value butterfly_index(lane).

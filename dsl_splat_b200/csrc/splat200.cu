@@ -246,6 +246,12 @@ void launch_render(const RenderParams& p, bool backward, cudaStream_t s) {
       cudaFuncSetAttribute(render_backward_kernel<CHP, px>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     render_backward_kernel<CHP, px><<<tiles, kBlock / px, smem, counted(s)>>>(p);
+  } else if (CHP <= 8) {
+    // up to eight channels: two pixels per lane with paired arithmetic
+    if (smem > 32 * 1024)
+      cudaFuncSetAttribute(render_forward2_kernel<CHP>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    render_forward2_kernel<CHP><<<tiles, kBlock / 2, smem, counted(s)>>>(p);
   } else {
     if (smem > 32 * 1024)
       cudaFuncSetAttribute(render_forward_kernel<CHP>,

@@ -86,6 +86,64 @@ SPLAT_DEV float4 torch_normalize4(float4 x) {
                      __fdiv_rn(x.w, norm));
 }
 
+// Packed float32 pairs (sm_100 f32x2 arithmetic): each half is an
+// independent IEEE round-to-nearest float32 operation, so a pair computes
+// the same bits as two scalar operations in one issue slot.  Caution: ptxas
+// fuses a packed multiply whose only use is a packed add/sub into a fused
+// multiply-add, ignoring .rn and --fmad=false; bit-exact code must not chain
+// mul2 into add2/sub2.
+typedef unsigned long long f32x2;
+
+SPLAT_DEV f32x2 pack2(float lo, float hi) {
+  f32x2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+SPLAT_DEV void unpack2(f32x2 v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+SPLAT_DEV f32x2 add2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+SPLAT_DEV f32x2 sub2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+SPLAT_DEV f32x2 mul2(f32x2 a, f32x2 b) {
+  f32x2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+SPLAT_DEV f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+SPLAT_DEV f32x2 splat2(float v) { return pack2(v, v); }
+
+// splat_expf_core on both halves: the same operations, paired.
+SPLAT_DEV f32x2 splat_expf_core2(f32x2 x) {
+  float t0, t1;
+  unpack2(mul2(x, splat2(1.44269504088896341f)), t0, t1);
+  const float n0 = rintf(t0), n1 = rintf(t1);
+  const f32x2 n = pack2(n0, n1);
+  f32x2 r = fma2(n, splat2(-0.693359375f), x);
+  r = fma2(n, splat2(2.12194440054690583e-4f), r);
+  f32x2 p = fma2(splat2(1.98412698e-4f), r, splat2(1.38888889e-3f));
+  p = fma2(p, r, splat2(8.33333377e-3f));
+  p = fma2(p, r, splat2(4.16666679e-2f));
+  p = fma2(p, r, splat2(1.66666672e-1f));
+  p = fma2(p, r, splat2(0.5f));
+  p = fma2(p, r, splat2(1.0f));
+  p = fma2(p, r, splat2(1.0f));
+  const float s0 = __int_as_float((static_cast<int>(n0) + 127) << 23);
+  const float s1 = __int_as_float((static_cast<int>(n1) + 127) << 23);
+  return mul2(p, pack2(s0, s1));
+}
+
 // splatting/geometry.py:22-30 tile_bounds: CUDA getRect truncation.
 SPLAT_DEV int4 tile_bounds(float cx, float cy, int radius, int gx, int gy) {
   const float r = static_cast<float>(radius);
