@@ -634,11 +634,13 @@ __global__ void __launch_bounds__(kBlock / PX) render_backward_kernel(RenderPara
 #pragma unroll
       for (int c = 0; c < CHP; ++c)
         if (c < p.channels) {
-          if (p.upstream_alpha && c == p.channels - 1)
-            grad[i][c] = p.upstream_alpha[static_cast<size_t>(pixel) * p.alpha_pix_stride];
-          else
-            grad[i][c] = up ? up[c * p.up_ch_stride] : 0.0f;
-          bg_grad += p.background[c] * grad[i][c];
+          // the appended channel's upstream may live in its own buffer
+          const float* src = (p.upstream_alpha && c == p.channels - 1)
+                                 ? p.upstream_alpha + static_cast<size_t>(pixel) * p.alpha_pix_stride
+                                 : (up ? up + c * p.up_ch_stride : nullptr);
+          const float g = src ? __ldg(src) : 0.0f;
+          grad[i][c] = g;
+          bg_grad += p.background[c] * g;
         }
       bg_term[i] = -final_T * bg_grad;
     }
@@ -683,16 +685,40 @@ __global__ void __launch_bounds__(kBlock / PX) render_backward_kernel(RenderPara
       float dy[PX], G[PX], alpha[PX];
       bool accept[PX];
       bool any = false;
+      if constexpr (PX == 2) {  // exp and alpha of both pixels as f32x2 pairs
+        const float dy0 = gm.y - fy[0], dy1 = gm.y - fy[1];
+        const float pw0 = sample_power(q, dx, dy0), pw1 = sample_power(q, dx, dy1);
+        const f32x2 g2 = splat_expf_core2(pack2(pw0, pw1));
+        float g0, g1, a0, a1;
+        unpack2(g2, g0, g1);
+        unpack2(mul2(splat2(q.w), g2), a0, a1);
+        a0 = wmin(W32(0.99), a0);
+        a1 = wmin(W32(0.99), a1);
+        const bool acc0 = inside[0] && position < last_contributor[0] && pw0 <= 0.0f &&
+                          pw0 >= cut && a0 >= threshold;
+        const bool acc1 = inside[1] && position < last_contributor[1] && pw1 <= 0.0f &&
+                          pw1 >= cut && a1 >= threshold;
+        dy[0] = dy0;
+        dy[1] = dy1;
+        G[0] = g0;
+        G[1] = g1;
+        alpha[0] = a0;
+        alpha[1] = a1;
+        accept[0] = acc0;
+        accept[1] = acc1;
+        any = acc0 || acc1;
+      } else {
 #pragma unroll
-      for (int i = 0; i < PX; ++i) {
-        dy[i] = gm.y - fy[i];
-        const float power = sample_power(q, dx, dy[i]);
-        const bool in_range =
-            inside[i] && position < last_contributor[i] && power <= 0.0f && power >= cut;
-        G[i] = splat_expf_core(power);
-        alpha[i] = wmin(W32(0.99), q.w * G[i]);
-        accept[i] = in_range && alpha[i] >= threshold;
-        any = any || accept[i];
+        for (int i = 0; i < PX; ++i) {
+          dy[i] = gm.y - fy[i];
+          const float power = sample_power(q, dx, dy[i]);
+          const bool in_range =
+              inside[i] && position < last_contributor[i] && power <= 0.0f && power >= cut;
+          G[i] = splat_expf_core(power);
+          alpha[i] = wmin(W32(0.99), q.w * G[i]);
+          accept[i] = in_range && alpha[i] >= threshold;
+          any = any || accept[i];
+        }
       }
       if (!__any_sync(0xffffffffu, any)) continue;
       float f[CHP];
