@@ -46,13 +46,15 @@ def lib():
         L = ctypes.CDLL(_LIB_PATH)
         L.oracle_expf.argtypes = [_flt]
         L.oracle_expf.restype = _flt
+        L.oracle_logf.argtypes = [_flt]
+        L.oracle_logf.restype = _flt
         L.oracle_cameras_prepare.argtypes = [_int, _f32p, _f32p, _int, _int, _int, _vp, _vp, _vp, _i32p]
         L.oracle_cameras_prepare.restype = _int
         L.oracle_cameras_backward.argtypes = [_int, _f32p, _vp, _int, _int, _vp, _vp, _f32p]
         L.oracle_cameras_backward.restype = None
         L.oracle_project_forward.argtypes = [
             _int, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _int, _int,
-            _flt, _flt, _flt, _f32p, _f32p, _i32p, _i32p, _f32p]
+            _flt, _flt, _flt, _f32p, _f32p, _i32p, _i32p, _f32p, _int]
         L.oracle_project_forward.restype = None
         L.oracle_sh_forward.argtypes = [_int, _int, _int, _f32p, _f32p, _vp, _f32p, _vp]
         L.oracle_sh_forward.restype = None
@@ -60,7 +62,8 @@ def lib():
         L.oracle_sh_backward.restype = None
         L.oracle_scan_counts.argtypes = [_int, _i32p, _i32p]
         L.oracle_scan_counts.restype = ctypes.c_longlong
-        L.oracle_bin_and_sort.argtypes = [_int, _f32p, _i32p, _f32p, _i32p, _int, _int, _u64p, _i32p, _i32p]
+        L.oracle_bin_and_sort.argtypes = [_int, _f32p, _i32p, _f32p, _i32p, _int, _int, _u64p, _i32p, _i32p,
+                                          _vp, _int]
         L.oracle_bin_and_sort.restype = None
         L.oracle_render_forward.argtypes = [
             _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i32p]
@@ -133,15 +136,18 @@ class Projected:
     depths: np.ndarray
 
 
+TILE_MODES = {"radius": 0, "snugbox": 1, "accutile": 2}
+
+
 def project_forward(means, quats, scales, opacities, view, proj, K, width, height,
-                    near=0.2, far=float("inf"), radius_clip=0.0) -> Projected:
+                    near=0.2, far=float("inf"), radius_clip=0.0, tile_mode="radius") -> Projected:
     n = len(means)
     out = Projected(np.zeros((n, 2), np.float32), np.zeros((n, 4), np.float32),
                     np.zeros(n, np.int32), np.zeros(n, np.int32), np.zeros(n, np.float32))
     lib().oracle_project_forward(
         n, _c(means), _c(quats), _c(scales), _c(opacities), _c(view).reshape(16),
         _c(proj).reshape(16), _c(K).reshape(9), width, height, near, far, radius_clip,
-        out.centers, out.conics, out.radii, out.tiles, out.depths)
+        out.centers, out.conics, out.radii, out.tiles, out.depths, TILE_MODES[tile_mode])
     return out
 
 
@@ -173,15 +179,20 @@ def scan_counts(counts):
     return offsets, int(m)
 
 
-def bin_and_sort(centers, radii, depths, offsets, width, height):
+def bin_and_sort(centers, radii, depths, offsets, width, height, conics=None,
+                 tile_mode="radius"):
     n = len(radii)
     m = int(offsets[-1]) if n else 0
     gx, gy = (width + 15) // 16, (height + 15) // 16
     keys = np.zeros(m, np.uint64)
     ids = np.zeros(m, np.int32)
     ranges = np.zeros((gx * gy, 2), np.int32)
+    if tile_mode != "radius" and conics is None:
+        raise ValueError("SnugBox/AccuTile require projected conics")
+    conics_c = None if conics is None else _c(conics)  # alive across the call
     lib().oracle_bin_and_sort(n, _c(centers), _c(radii, np.int32), _c(depths),
-                              _c(offsets, np.int32), width, height, keys, ids, ranges)
+                              _c(offsets, np.int32), width, height, keys, ids, ranges,
+                              _ptr(conics_c), TILE_MODES[tile_mode])
     return keys, ids, ranges
 
 

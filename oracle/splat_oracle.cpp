@@ -86,6 +86,43 @@ float splat_expf(float x) {
   return p * scale;
 }
 
+// log(x) for the tile-mode footprints (splatting/intersections.py:60, whose
+// wp.log is the device logf): x = 2^k m with m in [sqrt(1/2), sqrt(2)),
+// s = (m-1)/(m+1) computed as f/(2+f), log m = 2 atanh(s) summed as
+// 2s (1 + s^2/3 + s^4/5 + s^6/7 + s^8/9) (|s| <= 0.1716, truncation below
+// 2^-27 relative), k ln2 added with ln2 split into 0.693359375 and a
+// correction.  Every step is one IEEE float32 operation, so the CUDA kernels
+// (splat_common.cuh) produce identical bits.  +inf -> +inf, x <= 0 or NaN ->
+// NaN / -inf as logf.
+float splat_logf(float x) {
+  if (!(x > 0.0f)) return x == 0.0f ? -INFINITY : NAN;
+  if (x == INFINITY) return x;
+  uint32_t u = float_bits(x);
+  int k = 0;
+  if (u < 0x00800000u) {  // subnormal: scale into the normal range
+    x = x * 8388608.0f;   // 2^23, exact
+    u = float_bits(x);
+    k = -23;
+  }
+  k += static_cast<int>(u >> 23) - 127;
+  float m = bits_float((u & 0x007FFFFFu) | 0x3F800000u);  // [1, 2)
+  if (m > 1.41421356f) {
+    m = m * 0.5f;  // exact
+    k += 1;
+  }
+  const float f = m - 1.0f;  // exact (Sterbenz)
+  const float s = f / (2.0f + f);
+  const float z = s * s;
+  float p = static_cast<float>(1.0 / 9.0);
+  p = std::fmaf(p, z, static_cast<float>(1.0 / 7.0));
+  p = std::fmaf(p, z, static_cast<float>(1.0 / 5.0));
+  p = std::fmaf(p, z, static_cast<float>(1.0 / 3.0));
+  p = std::fmaf(p, z, 1.0f);
+  const float log_m = (2.0f * s) * p;
+  const float kf = static_cast<float>(k);
+  return kf * 0.693359375f + std::fmaf(kf, -2.12194440054690583e-4f, log_m);
+}
+
 // ---- GLM-order geometry (splatting/math.py, primitives/math.py) --------
 
 // splatting/math.py:54-64 reference_matmul
@@ -183,6 +220,133 @@ void tile_bounds(const float center[2], int radius, int gx, int gy, int b[4]) {
   b[1] = iclamp(f2i((center[1] - r) / 16.0f), 0, gy);
   b[2] = iclamp(f2i(((center[0] + r) + 16.0f - 1.0f) / 16.0f), 0, gx);
   b[3] = iclamp(f2i(((center[1] + r) + 16.0f - 1.0f) / 16.0f), 0, gy);
+}
+
+// ---- tile modes (splatting/intersections.py:21-218) ---------------------
+// 0 radius (the tile_bounds square), 1 snugbox (square clipped to the
+// opacity-aware ellipse box), 2 accutile (per-strip ellipse spans).
+
+struct Footprint {
+  float cx, cy, a, b, c;
+  int bounds[4];
+  bool precise;
+  float level, det, ex, ey;
+};
+
+// intersections.py:45-108 footprint
+Footprint footprint(const float center[2], const float conic[4], int radius, int gx, int gy) {
+  Footprint e{};
+  e.cx = center[0];
+  e.cy = center[1];
+  e.a = conic[0];
+  e.b = conic[1];
+  e.c = conic[2];
+  e.precise = false;
+  tile_bounds(center, radius, gx, gy, e.bounds);
+  const float a = conic[0], b = conic[1], c = conic[2];
+  const float det = static_cast<float>(static_cast<double>(a) * static_cast<double>(c) -
+                                       static_cast<double>(b) * static_cast<double>(b));
+  if (conic[3] < 1.0f / 255.0f) {
+    e.bounds[0] = e.bounds[1] = e.bounds[2] = e.bounds[3] = 0;
+    return e;
+  }
+  if (!(a > 0.0f && c > 0.0f && det > 0.0f)) return e;  // keep the conservative square
+  const float level = 2.0f * splat_logf(conic[3] * 255.0f);
+  const float reach = static_cast<float>(radius) + 32.0f;
+  const float roundoff = (8.0f * 1.1920928955078125e-7f) *
+                         ((((a + 2.0f * std::fabs(b)) + c) * reach * reach + std::fabs(level)) +
+                          1.0f);
+  e.level = wmax(0.0f, level) + roundoff;
+  e.det = det;
+  e.ex = std::sqrt(e.level * c / det);
+  e.ey = std::sqrt(e.level * a / det);
+  if (!(std::isfinite(e.ex) && std::isfinite(e.ey))) return e;
+  const float fgx = static_cast<float>(gx), fgy = static_cast<float>(gy);
+  const int lo_x = f2i(wclamp(std::floor((e.cx - e.ex) / 16.0f), 0.0f, fgx));
+  const int lo_y = f2i(wclamp(std::floor((e.cy - e.ey) / 16.0f), 0.0f, fgy));
+  const int hi_x = f2i(wclamp(std::floor((e.cx + e.ex) / 16.0f) + 1.0f, 0.0f, fgx));
+  const int hi_y = f2i(wclamp(std::floor((e.cy + e.ey) / 16.0f) + 1.0f, 0.0f, fgy));
+  e.bounds[0] = std::max(e.bounds[0], lo_x);
+  e.bounds[1] = std::max(e.bounds[1], lo_y);
+  e.bounds[2] = std::min(e.bounds[2], hi_x);
+  e.bounds[3] = std::min(e.bounds[3], hi_y);
+  e.precise = true;
+  return e;
+}
+
+// intersections.py:117-128 line_intersection: the ellipse's v-range on the
+// grid line u = line*16 (u = x for column strips, y for row strips).
+void line_intersection(const Footprint& e, int line, bool is_y, float out[2]) {
+  float u = e.cx, v = e.cy, c = e.c, extent_u = e.ex;
+  const float b = e.b;
+  if (is_y) {
+    u = e.cy;
+    v = e.cx;
+    c = e.a;
+    extent_u = e.ey;
+  }
+  const float h = wclamp(static_cast<float>(line * 16) - u, -extent_u, extent_u);
+  const float root = std::sqrt(wmax(0.0f, e.level * c - e.det * h * h));
+  out[0] = v + (-b * h - root) / c;
+  out[1] = v + (-b * h + root) / c;
+}
+
+// intersections.py:131-152 strip_span: tile span of strip `row` from the
+// ranges on its two boundary lines and the interior extrema.
+void strip_span(const Footprint& e, int row, bool is_y, const float low[2], const float high[2],
+                int out[2]) {
+  float u = e.cx, v = e.cy, a = e.a, extent = e.ey;
+  const float b = e.b;
+  int lower = e.bounds[1], upper = e.bounds[3];
+  if (is_y) {
+    u = e.cy;
+    v = e.cx;
+    a = e.c;
+    extent = e.ex;
+    lower = e.bounds[0];
+    upper = e.bounds[2];
+  }
+  float lo = wmin(low[0], high[0]), hi = wmax(low[1], high[1]);
+  const float arg_min = b * extent / a, arg_max = -b * extent / a;
+  const float h0 = static_cast<float>(row * 16) - u, h1 = static_cast<float>((row + 1) * 16) - u;
+  if (h0 <= arg_min && arg_min <= h1) lo = v - extent;
+  if (h0 <= arg_max && arg_max <= h1) hi = v + extent;
+  out[0] = f2i(wclamp(std::floor(lo / 16.0f), static_cast<float>(lower), static_cast<float>(upper)));
+  out[1] = f2i(wclamp(std::floor(hi / 16.0f) + 1.0f, static_cast<float>(lower),
+                      static_cast<float>(upper)));
+}
+
+// intersections.py:155-218 visit: the tiles of one Gaussian in emission
+// order (emit(tile)), returning their count.
+template <class Emit>
+int visit_tiles(int mode, const float center[2], const float conic[4], int radius, int gx, int gy,
+                Emit&& emit) {
+  Footprint e{};
+  tile_bounds(center, radius, gx, gy, e.bounds);
+  e.precise = false;
+  if (mode != 0) e = footprint(center, conic, radius, gx, gy);
+  const int* bd = e.bounds;
+  const int nx = std::max(0, bd[2] - bd[0]), ny = std::max(0, bd[3] - bd[1]);
+  if (nx == 0 || ny == 0) return 0;
+  const bool is_y = mode == 2 ? ny < nx : true;
+  const int start = is_y ? bd[1] : bd[0], end = is_y ? bd[3] : bd[2];
+  const bool strips = mode == 2 && e.precise;
+  float low[2] = {0.0f, 0.0f};
+  if (strips) line_intersection(e, start, is_y, low);
+  int count = 0;
+  for (int row = start; row < end; ++row) {
+    int span[2] = {is_y ? bd[0] : bd[1], is_y ? bd[2] : bd[3]};
+    if (strips) {
+      float high[2];
+      line_intersection(e, row + 1, is_y, high);
+      strip_span(e, row, is_y, low, high, span);
+      low[0] = high[0];
+      low[1] = high[1];
+    }
+    for (int col = span[0]; col < span[1]; ++col) emit(is_y ? row * gx + col : col * gx + row);
+    count += std::max(0, span[1] - span[0]);
+  }
+  return count;
 }
 
 // ---- 4x4 inverse (Laplace expansion by 2x2 minors, Eberly 2008) --------
@@ -301,6 +465,7 @@ void sh_basis_grad(const float d[3], int k, float g[3]) {
 extern "C" {
 
 float oracle_expf(float x) { return splat_expf(x); }
+float oracle_logf(float x) { return splat_logf(x); }
 
 // splatting/camera_kernels.py:11-66 prepare_kernel.  Returns nonzero when any
 // camera reports an error (codes in errors[]).
@@ -380,13 +545,15 @@ void oracle_cameras_backward(int count, const float* Ks, const float* grad_full,
   }
 }
 
-// gs3d/projection.py:89-164 project (tile_mode "radius").  Culled rows keep
-// radii = tiles = 0 and leave centers/conics/depths untouched.
+// gs3d/projection.py:89-164 project.  Culled rows keep radii = tiles = 0 and
+// leave centers/conics/depths untouched.  tile_mode != 0 replaces the tile
+// count with the mode's (:150-162); such a Gaussian keeps its radius even
+// when the count is 0.
 void oracle_project_forward(int n, const float* means, const float* quats, const float* scales,
                             const float* opacities, const float* view, const float* proj,
                             const float* K, int width, int height, float near_plane,
                             float far_plane, float radius_clip, float* centers, float* conics,
-                            int* radii, int* tiles, float* depths) {
+                            int* radii, int* tiles, float* depths, int tile_mode) {
   const int gx = (width + 15) / 16, gy = (height + 15) / 16;
   const float fx = K[0], fy = K[4];
 #pragma omp parallel for schedule(static)
@@ -419,6 +586,8 @@ void oracle_project_forward(int n, const float* means, const float* quats, const
     conics[4 * i + 3] = opacities[i];
     radii[i] = radius;
     tiles[i] = count;
+    if (tile_mode != 0)
+      tiles[i] = visit_tiles(tile_mode, center, conics + 4 * i, radius, gx, gy, [](int) {});
     depths[i] = t[2];
   }
 }
@@ -514,7 +683,7 @@ long long oracle_scan_counts(int n, const int* counts, int* offsets) {
 // in full (zeros for empty tiles); keys_out/ids_out hold M entries.
 void oracle_bin_and_sort(int n, const float* centers, const int* radii, const float* depths,
                          const int* offsets, int width, int height, uint64_t* keys_out,
-                         int* ids_out, int* ranges) {
+                         int* ids_out, int* ranges, const float* conics, int tile_mode) {
   const int gx = (width + 15) / 16, gy = (height + 15) / 16;
   const long long M = n ? offsets[n - 1] : 0;
   std::vector<uint64_t> keys(M);
@@ -522,16 +691,15 @@ void oracle_bin_and_sort(int n, const float* centers, const int* radii, const fl
 #pragma omp parallel for schedule(dynamic, 256)
   for (int i = 0; i < n; ++i) {
     if (radii[i] <= 0) continue;
-    int b[4];
-    tile_bounds(centers + 2 * i, radii[i], gx, gy, b);
     long long off = i > 0 ? offsets[i - 1] : 0;
-    for (int y = b[1]; y < b[3]; ++y)
-      for (int x = b[0]; x < b[2]; ++x) {
-        keys[off] = (static_cast<uint64_t>(static_cast<uint32_t>(y * gx + x)) << 32) |
-                    float_bits(depths[i]);
-        ids[off] = i;
-        ++off;
-      }
+    const uint32_t depth = float_bits(depths[i]);
+    // splatting/binning.py:40-67 duplicate_precise emits through the same visit
+    visit_tiles(tile_mode, centers + 2 * i, conics ? conics + 4 * i : nullptr, radii[i], gx, gy,
+                [&](int tile) {
+                  keys[off] = (static_cast<uint64_t>(static_cast<uint32_t>(tile)) << 32) | depth;
+                  ids[off] = i;
+                  ++off;
+                });
   }
   std::vector<long long> order(M);
   for (long long p = 0; p < M; ++p) order[p] = p;

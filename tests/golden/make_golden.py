@@ -19,7 +19,7 @@ Kernels executed (reference file:line):
 Warp library calls restated: array_scan (inclusive cumsum) and
 radix_sort_pairs (a stable sort of the 64-bit keys).
 
-Usage: python tests/golden/make_golden.py [/path/to/reference]
+Usage: python tests/golden/make_golden.py [/path/to/reference] [--tile-modes-only]
 """
 
 from __future__ import annotations
@@ -55,6 +55,7 @@ def load_reference(ref_root: str):
         sys.modules[pkg] = mod
     from oracle import oracle as O
     ws.set_exp(lambda x: np.float32(O.lib().oracle_expf(float(x))))
+    ws.set_log(lambda x: np.float32(O.lib().oracle_logf(float(x))))
     names = {
         "cam": "dsl_splat.splatting.camera_kernels",
         "proj": "dsl_splat.gs3d.projection",
@@ -195,6 +196,83 @@ def golden_case(ref, name, scene: dict, seed: int):
     return out
 
 
+def tile_mode_case(ref, name, scene: dict) -> dict:
+    """Projection tile counts and binning for tile_mode snugbox and accutile
+    (gs3d/projection.py:150-162, splatting/intersections.py:45-218,
+    splatting/binning.py:40-117): the reference's own kernels."""
+    W, H = scene["width"], scene["height"]
+    gx, gy = (W + 15) // 16, (H + 15) // 16
+    T = gx * gy
+    means = scene["means"].astype(np.float32)
+    n = len(means)
+    quats = F.normalize(torch.from_numpy(scene["quats"].astype(np.float32)), dim=-1).numpy()
+    scales = scene["scales"].astype(np.float32)
+    opac = scene["opacities"].astype(np.float32)
+    view = scene["viewmat"].astype(np.float32)
+    K = scene["K"].astype(np.float32)
+    wp = sys.modules["warp"]
+    full = np.zeros((1, 4, 4), np.float32)
+    inverse = np.zeros((1, 4, 4), np.float32)
+    centers_cam = np.zeros((1, 3), np.float32)
+    errors = np.zeros(1, np.int32)
+    ws.launch(ref["cam"].prepare_kernel, 1,
+              [A(view[None].copy()), A(K[None].copy()), W, H, 1, A(full), A(inverse),
+               A(centers_cam), A(errors)])
+    out: dict = dict(width=W, height=H, means=means, quats=quats, scales=scales,
+                     opacities=opac, viewmat=view, K=K, full=full[0])
+    t0 = time.time()
+    for mode in ("snugbox", "accutile"):
+        centers = np.zeros((n, 2), np.float32)
+        conics = np.zeros((n, 4), np.float32)
+        radii = np.zeros(n, np.int32)
+        tiles = np.zeros(n, np.int32)
+        depths = np.zeros(n, np.float32)
+        ws.launch(ref["proj"]._make_project(mode), n,
+                  [A(means, wp.vec3), A(quats, wp.vec4), A(scales, wp.vec3), A(opac),
+                   A(view.copy()), A(full[0].copy()), A(K.copy()), W, H, np.float32(0.2),
+                   np.float32(np.inf), np.float32(0.0), A(centers, wp.vec2),
+                   A(conics, wp.vec4), A(radii), A(tiles), A(depths)])
+        offsets = np.cumsum(tiles, dtype=np.int64).astype(np.int32)
+        m = int(offsets[-1]) if n else 0
+        keys = np.zeros(2 * m, np.uint64)
+        ids = np.zeros(2 * m, np.int32)
+        ws.launch(ref["bin"]._make_duplicate(mode), n,
+                  [A(centers, wp.vec2), A(conics, wp.vec4), A(radii), A(depths), A(offsets),
+                   gx, gy, A(keys), A(ids)])
+        order = np.argsort(keys[:m], kind="stable")
+        ranges = np.zeros((T, 2), np.int32)
+        ws.launch(ref["tiling"].identify_ranges, m, [A(keys[:m][order]), A(ranges)])
+        out.update({f"{mode}_centers": centers, f"{mode}_conics": conics,
+                    f"{mode}_radii": radii, f"{mode}_tiles": tiles, f"{mode}_depths": depths,
+                    f"{mode}_keys": keys[:m][order], f"{mode}_ids": ids[:m][order],
+                    f"{mode}_ranges": ranges})
+        print(f"{name} {mode}: visible={int((radii > 0).sum())} pairs={m}", flush=True)
+    print(f"{name}: {time.time() - t0:.1f}s", flush=True)
+    return out
+
+
+def tile_mode_scenes(base: dict) -> dict:
+    """The c1/dense geometries plus an edge scene: thin rotated ellipses,
+    opacities on both sides of 1/255 and footprints larger than the image."""
+    from dsl_splat_b200.scenes import intrinsics
+    out = {k: base[k] for k in ("c1_sh3", "dense_sh1")}
+    g = torch.Generator().manual_seed(77)
+    n = 300
+    means = (torch.rand(n, 3, generator=g) * 2 - 1) * torch.tensor([1.6, 1.2, 0.0])
+    means[:, 2] = 3.0 + torch.rand(n, generator=g) * 3
+    scales = torch.exp(torch.randn(n, 3, generator=g) * 0.8 - 2.5)
+    scales[:100, 0] *= 20.0                       # long along x
+    scales[100:150, 1] *= 30.0                    # long along y
+    scales[150:160] = torch.tensor([2.5, 2.5, 2.5])  # larger than the image
+    opac = torch.sigmoid(torch.randn(n, generator=g) * 3)
+    opac[160:180] = 1.0 / 255.0 * (0.5 + torch.rand(20, generator=g))  # around the threshold
+    opac[180:185] = 1.0
+    out["edges"] = dict(width=72, height=56, means=means.numpy(), scales=scales.numpy(),
+                        quats=torch.randn(n, 4, generator=g).numpy(), opacities=opac.numpy(),
+                        viewmat=torch.eye(4).numpy(), K=intrinsics(60.0, 60.0, 36.0, 28.0).numpy())
+    return out
+
+
 def scenes():
     """Small seeded scenes with the benchmark configs' distributions."""
     from dsl_splat_b200.scenes import intrinsics, look_at
@@ -249,11 +327,17 @@ def scenes():
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    ref_root = args[0] if args else "/root/reference"
     ref = load_reference(ref_root)
-    for i, (name, scene) in enumerate(scenes().items()):
-        data = golden_case(ref, name, scene, seed=100 + i)
-        np.savez_compressed(os.path.join(HERE, f"gs3d_{name}.npz"), **data)
+    base = scenes()
+    if "--tile-modes-only" not in sys.argv:
+        for i, (name, scene) in enumerate(base.items()):
+            data = golden_case(ref, name, scene, seed=100 + i)
+            np.savez_compressed(os.path.join(HERE, f"gs3d_{name}.npz"), **data)
+    for name, scene in tile_mode_scenes(base).items():
+        data = tile_mode_case(ref, name, scene)
+        np.savez_compressed(os.path.join(HERE, f"tilemodes_{name}.npz"), **data)
 
 
 if __name__ == "__main__":

@@ -536,8 +536,17 @@ def abs(x):  # noqa: A001
     return np.abs(x)
 
 
+_log_impl = None
+
+
+def set_log(fn):
+    """Substitute the float32 log (the kernels' and the oracle's splat_logf)."""
+    global _log_impl
+    _log_impl = fn
+
+
 def log(x):
-    return np.log(x)
+    return _log_impl(x) if _log_impl is not None else np.log(x)
 
 
 _exp_impl = None
@@ -654,6 +663,9 @@ def struct(cls):
                 setattr(self, name, F32(0))
             elif ann is int:
                 setattr(self, name, 0)
+            elif isinstance(ann, _ArrayType):
+                # a default-constructed struct holds null arrays (shape 0)
+                setattr(self, name, Array(np.zeros((0,) * max(ann.ndim, 1), np.float32)))
             else:
                 setattr(self, name, None)
     return type(cls.__name__, (), {"__init__": __init__, "__annotations__": fields})

@@ -119,3 +119,33 @@ def test_metadata(golden):
     np.testing.assert_array_equal(g["meta_means2d"][vis], g["centers"][vis])
     assert not g["meta_means2d"][~vis].any()
     np.testing.assert_array_equal(g["meta_opacities"][vis], g["conics"][vis, 3])
+
+
+TILE_MODE_FIXTURES = sorted(glob.glob(os.path.join(ROOT, "tests", "golden", "tilemodes_*.npz")))
+
+
+@pytest.mark.parametrize("path", TILE_MODE_FIXTURES,
+                         ids=[os.path.basename(p)[10:-4] for p in TILE_MODE_FIXTURES])
+@pytest.mark.parametrize("mode", ["snugbox", "accutile"])
+def test_tile_modes(path, mode):
+    """tile_mode snugbox/accutile (splatting/intersections.py:45-218 through
+    gs3d/projection.py:150-162 and splatting/binning.py:40-117): tile counts,
+    sorted keys, ids and ranges bit-exact."""
+    g = _load(path)
+    W, H = int(g["width"]), int(g["height"])
+    p = O.project_forward(g["means"], g["quats"], g["scales"], g["opacities"], g["viewmat"],
+                          g["full"], g["K"], W, H, tile_mode=mode)
+    np.testing.assert_array_equal(p.radii, g[f"{mode}_radii"])
+    np.testing.assert_array_equal(p.tiles, g[f"{mode}_tiles"])
+    vis = p.radii > 0
+    np.testing.assert_array_equal(p.conics[vis], g[f"{mode}_conics"][vis])
+    off, _ = O.scan_counts(p.tiles)
+    keys, ids, ranges = O.bin_and_sort(p.centers, p.radii, p.depths, off, W, H,
+                                       conics=p.conics, tile_mode=mode)
+    np.testing.assert_array_equal(keys, g[f"{mode}_keys"])
+    np.testing.assert_array_equal(ids, g[f"{mode}_ids"])
+    np.testing.assert_array_equal(ranges, g[f"{mode}_ranges"])
+
+
+def test_tile_mode_fixtures_present():
+    assert len(TILE_MODE_FIXTURES) == 3
