@@ -30,10 +30,10 @@ SIGNATURES: dict[str, tuple] = {
     "splat_cameras_prepare": (_I, [_I, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "splat_cameras_backward": (_I, [_I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "splat_project_forward": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,
-                                   _P, _P, _P, _P, _P, _P]),
+                                   _P, _P, _P, _P, _P, _I, _P]),
     "splat_project_forward_fused": (_I, [_I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,
                                          _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _P,
-                                         _P, _P, _P, _P]),
+                                         _P, _P, _P, _I, _P]),
     "splat_metadata": (_I, [_I, _P, _P, _P, _P, _P, _P, _P]),
     "splat_project_backward": (_I, [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                     _P, _P, _P, _P]),
@@ -45,10 +45,10 @@ SIGNATURES: dict[str, tuple] = {
     "splat_scan_workspace_bytes": (_Z, [_I]),
     "splat_scan_counts": (_I, [_I, _P, _P, _P, _P, _Z, _P]),
     "splat_scan_counts_static": (_I, [_I, _P, _P, _P, _P]),
-    "splat_bin_workspace_bytes": (_Z, [_I, _I, _I]),
-    "splat_bin_pairs_workspace_bytes": (_Z, [_L, _I, _I]),
-    "splat_bin_prepare": (_I, [_I, _P, _P, _P, _P, _I, _I, _P, _Z, _P, _P, _P]),
-    "splat_bin_emit": (_I, [_I, _L, _I, _I, _P, _Z, _P, _Z, _P, _P]),
+    "splat_bin_workspace_bytes": (_Z, [_I, _I, _I, _I]),
+    "splat_bin_pairs_workspace_bytes": (_Z, [_L, _I, _I, _I]),
+    "splat_bin_prepare": (_I, [_I, _P, _P, _P, _P, _P, _I, _I, _I, _P, _Z, _P, _P, _P]),
+    "splat_bin_emit": (_I, [_I, _L, _I, _I, _I, _P, _P, _P, _P, _Z, _P, _Z, _P, _P]),
     "splat_render_forward": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P, _I, _I, _I,
                                   _P, _P, _I, _I, _P, _P, _P, _P]),
     "splat_render_forward_statistics": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P,

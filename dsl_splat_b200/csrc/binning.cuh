@@ -24,6 +24,7 @@
 // and finishes without waiting further.
 #pragma once
 #include "splat_common.cuh"
+#include "tile_modes.cuh"
 
 namespace splat {
 
@@ -45,9 +46,10 @@ SPLAT_DEV void record_device_error(int code) { atomicCAS(&g_splat_device_error, 
 // diff == nullptr selects the chunked path (no difference grid; the pair
 // total is the sum of rectangle areas).
 __global__ void __launch_bounds__(256)
-    bin_prepare_kernel(int n, const float* __restrict__ centers, const int* __restrict__ radii,
-                       const int* __restrict__ tiles, const float* __restrict__ depths, int gx,
-                       int gy, uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
+    bin_prepare_kernel(int n, const float* __restrict__ centers, const float* __restrict__ conics,
+                       const int* __restrict__ radii, const int* __restrict__ tiles,
+                       const float* __restrict__ depths, int gx, int gy, int tile_mode,
+                       uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
                        uint2* __restrict__ rects, int* __restrict__ diff,
                        uint32_t* __restrict__ hist, unsigned long long* __restrict__ total) {
   __shared__ uint32_t s_hist[4 * kRadix];
@@ -70,15 +72,37 @@ __global__ void __launch_bounds__(256)
       if (radius > 0) {
         key = __float_as_uint(depths[i]);
         const float2 c = reinterpret_cast<const float2*>(centers)[i];
-        const int4 b = tile_bounds(c.x, c.y, radius, gx, gy);
+        // the tile rectangle of the mode (snugbox: the clipped box; accutile:
+        // the box bounding its strips)
+        TileVisit tv;
+        if (tile_mode == kTileRadius) {
+          tv.e.bounds = tile_bounds(c.x, c.y, radius, gx, gy);
+          tv.strips = false;
+        } else {
+          tv = tile_visit(tile_mode, c.x, c.y, reinterpret_cast<const float4*>(conics)[i], radius,
+                          gx, gy);
+        }
+        int4 b = tv.e.bounds;
+        if (b.z <= b.x || b.w <= b.y) b = make_int4(0, 0, 0, 0);  // no tiles
         rect = make_uint2(static_cast<uint32_t>(b.x) | (static_cast<uint32_t>(b.y) << 16),
                           static_cast<uint32_t>(b.z) | (static_cast<uint32_t>(b.w) << 16));
         if (diff) {  // onesweep path: per-tile counts from a global difference grid
           const int row = gx + 1;
-          atomicAdd(diff + b.y * row + b.x, 1);
-          atomicAdd(diff + b.y * row + b.z, -1);
-          atomicAdd(diff + b.w * row + b.x, -1);
-          atomicAdd(diff + b.w * row + b.z, 1);
+          if (tv.strips) {  // accutile: one 1-wide rectangle per strip
+            walk_strips(tv, [&](int r, int2 span) {
+              const int x0 = tv.is_y ? span.x : r, x1 = tv.is_y ? span.y : r + 1;
+              const int y0 = tv.is_y ? r : span.x, y1 = tv.is_y ? r + 1 : span.y;
+              atomicAdd(diff + y0 * row + x0, 1);
+              atomicAdd(diff + y0 * row + x1, -1);
+              atomicAdd(diff + y1 * row + x0, -1);
+              atomicAdd(diff + y1 * row + x1, 1);
+            });
+          } else if (b.z > b.x && b.w > b.y) {
+            atomicAdd(diff + b.y * row + b.x, 1);
+            atomicAdd(diff + b.y * row + b.z, -1);
+            atomicAdd(diff + b.w * row + b.x, -1);
+            atomicAdd(diff + b.w * row + b.z, 1);
+          }
           pairs += static_cast<unsigned long long>(max(tiles[i], 0));
         } else {  // chunked path: pairs are the rectangle areas it scatters
           pairs += static_cast<unsigned long long>(max(b.z - b.x, 0)) *
@@ -393,6 +417,40 @@ __global__ void __launch_bounds__(kSortBlock)
     const uint32_t last = n - 1;
     if (last >= base) out[n] = s_val[last - base] + scan_value(values, gather, last, bias);
   }
+}
+
+// ---- accutile emission --------------------------------------------------
+// Pairs of the depth-ordered Gaussians in emission order (the strip walk of
+// intersections.py:155-218), written at their depth-order offsets; stable
+// passes on the tile id then give the reference order.  One thread per
+// Gaussian.
+__global__ void __launch_bounds__(256)
+    emit_strips_kernel(uint32_t n, const uint32_t* __restrict__ order,
+                       const uint32_t* __restrict__ offsets, const float* __restrict__ centers,
+                       const float* __restrict__ conics, const int* __restrict__ radii,
+                       int gx, int gy, uint32_t m, uint32_t* __restrict__ keys,
+                       uint32_t* __restrict__ vals) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t g = order[i];
+  const int radius = radii[g];
+  if (radius <= 0) return;
+  const float2 c = reinterpret_cast<const float2*>(centers)[g];
+  const TileVisit tv = tile_visit(kTileAccutile, c.x, c.y,
+                                  reinterpret_cast<const float4*>(conics)[g], radius, gx, gy);
+  uint32_t pos = offsets[i];
+  const uint32_t end = offsets[i + 1];
+  walk_strips(tv, [&](int r, int2 span) {
+    for (int col = span.x; col < span.y; ++col) {
+      if (pos >= end || pos >= m) {  // counts disagree with the projection's
+        record_device_error(kInconsistentInput);
+        return;
+      }
+      keys[pos] = static_cast<uint32_t>(tv.is_y ? r * gx + col : col * gx + r);
+      vals[pos] = g;
+      ++pos;
+    }
+  });
 }
 
 // ---- chunked stable scatter ----------------------------------------------

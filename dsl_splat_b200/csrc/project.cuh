@@ -10,6 +10,7 @@
 // (splatting/math.py:13-28), plus the SH VJP (primitives/sh.py:82-138).
 #pragma once
 #include "splat_common.cuh"
+#include "tile_modes.cuh"
 
 namespace splat {
 
@@ -18,6 +19,7 @@ struct ProjectParams {
   const float* means;      // (n,3)
   const float* quats;      // (n,4) normalised wxyz, or raw when normalize_quats
   int normalize_quats;     // normalise in-kernel exactly as Torch's F.normalize does on CUDA
+  int tile_mode;           // kTileRadius / kTileSnugbox / kTileAccutile (tile count only)
   const float* scales;     // (n,3)
   const float* opacities;  // (n)
   const float* view;       // 4x4 row-major world->camera
@@ -325,6 +327,10 @@ __global__ void __launch_bounds__(kProjectBlock) project_forward_kernel(ProjectP
     p.depths[i] = t2;
     radius_out = radius;
     count_out = count;
+    // gs3d/projection.py:150-162: the mode's tile count replaces the square's
+    // (the Gaussian keeps its radius even when that count is 0)
+    if (p.tile_mode != kTileRadius)
+      count_out = tile_count(tile_visit(p.tile_mode, center.x, center.y, conic, radius, gx, gy));
   } while (false);
   p.radii[i] = radius_out;
   p.tiles[i] = count_out;

@@ -73,8 +73,10 @@ struct ChunkPlan {
   size_t smem_scatter = 0;
 };
 
-ChunkPlan chunk_plan(long long n, int gx, int gy) {
+ChunkPlan chunk_plan(long long n, int gx, int gy, int tile_mode) {
   ChunkPlan c;
+  // accutile tile sets are strips, not rectangles: the onesweep path emits them
+  if (tile_mode == kTileAccutile) return c;
   const size_t T = static_cast<size_t>(gx) * gy;
   c.smem_counts = 4 * static_cast<size_t>(gx + 1) * (gy + 1);
   c.smem_scatter = 4 * T + 16 * static_cast<size_t>(gx + gy);
@@ -107,10 +109,10 @@ struct BinLayout {
   size_t bytes;
 };
 
-BinLayout bin_layout(long long n, int width, int height) {
+BinLayout bin_layout(long long n, int width, int height, int tile_mode) {
   const int gx = (width + 15) / 16, gy = (height + 15) / 16;
   const size_t sort_tiles = static_cast<size_t>(blocks_for(n > 0 ? n : 1, kSortTile));
-  const ChunkPlan plan = chunk_plan(n, gx, gy);
+  const ChunkPlan plan = chunk_plan(n, gx, gy, tile_mode);
   const size_t T = static_cast<size_t>(gx) * gy;
   BinLayout L{};
   size_t o = 0;
@@ -148,13 +150,15 @@ struct PairLayout {
   size_t keys0, vals0, keys1, vals1, status, counters, bytes;
 };
 
-PairLayout pair_layout(long long pairs, int width, int height) {
+PairLayout pair_layout(long long pairs, int width, int height, int tile_mode) {
   const int gx = (width + 15) / 16, gy = (height + 15) / 16;
   const int tiles = gx * gy;
   const int passes = tile_passes(tiles);
   const size_t sort_tiles = static_cast<size_t>(blocks_for(pairs > 0 ? pairs : 1, kSortTile));
   PairLayout L{};
-  if (chunk_plan(1, gx, gy).use) return L;  // the chunked scatter needs no pair workspace
+  if (chunk_plan(1, gx, gy, tile_mode).use) return L;  // the chunked scatter needs no pair workspace
+  // accutile materialises its pairs (keys0/vals0) before the first pass
+  const bool emitted = tile_mode == kTileAccutile;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     const size_t at = o;
@@ -163,8 +167,8 @@ PairLayout pair_layout(long long pairs, int width, int height) {
   };
   L.keys0 = take(4 * pairs);
   L.vals0 = take(4 * pairs);
-  L.keys1 = take(passes > 2 ? 4 * pairs : 0);
-  L.vals1 = take(passes > 2 ? 4 * pairs : 0);
+  L.keys1 = take(passes > 2 || (emitted && passes > 1) ? 4 * pairs : 0);
+  L.vals1 = take(passes > 2 || (emitted && passes > 1) ? 4 * pairs : 0);
   L.status = take(4 * passes * sort_tiles * kRadix);
   L.counters = take(4 * 4);
   L.bytes = o;
@@ -333,12 +337,15 @@ int splat_project_forward(int n, const float* means, const float* quats, const f
                           const float* opacities, const float* view, const float* proj,
                           const float* K, int width, int height, float near_plane,
                           float far_plane, float radius_clip, float* centers, float* conics,
-                          int* radii, int* tiles, float* depths, void* stream) {
+                          int* radii, int* tiles, float* depths, int tile_mode, void* stream) {
   if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (tile_mode < kTileRadius || tile_mode > kTileAccutile)
+    return fail(kInvalidArgument, "tile_mode must be 0 (radius), 1 (snugbox) or 2 (accutile)");
   if (!aligned(quats, 16) || !aligned(conics, 16) || !aligned(centers, 8))
     return fail(kInvalidArgument, "quats/conics need 16-byte and centers 8-byte alignment");
   ProjectParams p{};
   p.n = n;
+  p.tile_mode = tile_mode;
   p.means = means;
   p.quats = quats;
   p.scales = scales;
@@ -368,8 +375,11 @@ int splat_project_forward_fused(int n, const float* means, const float* quats,
                                 float* depths, int sh_degree, int sh_k, const float* sh,
                                 const float* campos, float* colors, int color_stride,
                                 unsigned char* active, float* meta_means2d,
-                                float* meta_opacities, float* meta_conics, void* stream) {
+                                float* meta_opacities, float* meta_conics, int tile_mode,
+                                void* stream) {
   if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (tile_mode < kTileRadius || tile_mode > kTileAccutile)
+    return fail(kInvalidArgument, "tile_mode must be 0 (radius), 1 (snugbox) or 2 (accutile)");
   if (sh && (sh_degree < 0 || sh_degree > 3 || sh_k < (sh_degree + 1) * (sh_degree + 1) ||
              !colors || color_stride < 3))
     return fail(kInvalidArgument, "bad SH arguments");
@@ -382,6 +392,7 @@ int splat_project_forward_fused(int n, const float* means, const float* quats,
   p.means = means;
   p.quats = quats;
   p.normalize_quats = normalize_quats ? 1 : 0;
+  p.tile_mode = tile_mode;
   p.scales = scales;
   p.opacities = opacities;
   p.view = view;
@@ -647,23 +658,29 @@ int splat_scan_counts_static(int n, const int* counts, int* offsets, long long* 
 
 // ---- binning ------------------------------------------------------------------
 
-size_t splat_bin_workspace_bytes(int n, int width, int height) {
-  return bin_layout(n, width, height).bytes;
+size_t splat_bin_workspace_bytes(int n, int width, int height, int tile_mode) {
+  return bin_layout(n, width, height, tile_mode).bytes;
 }
 
-size_t splat_bin_pairs_workspace_bytes(long long pairs, int width, int height) {
-  return pair_layout(pairs, width, height).bytes;
+size_t splat_bin_pairs_workspace_bytes(long long pairs, int width, int height, int tile_mode) {
+  return pair_layout(pairs, width, height, tile_mode).bytes;
 }
 
-int splat_bin_prepare(int n, const float* centers, const int* radii, const int* tiles,
-                      const float* depths, int width, int height, void* workspace,
-                      size_t workspace_bytes, int* ranges, long long* pairs, void* stream) {
+int splat_bin_prepare(int n, const float* centers, const float* conics, const int* radii,
+                      const int* tiles, const float* depths, int width, int height, int tile_mode,
+                      void* workspace, size_t workspace_bytes, int* ranges, long long* pairs,
+                      void* stream) {
   if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad binning sizes");
+  if (tile_mode < kTileRadius || tile_mode > kTileAccutile)
+    return fail(kInvalidArgument, "tile_mode must be 0 (radius), 1 (snugbox) or 2 (accutile)");
+  if (tile_mode != kTileRadius && !conics)
+    return fail(kInvalidArgument, "SnugBox/AccuTile require projected conics");
+  if (!aligned(conics, 16)) return fail(kInvalidArgument, "conics need 16-byte alignment");
   const int gx = (width + 15) / 16, gy = (height + 15) / 16;
   if (gx > 65535 || gy > 65535 || static_cast<long long>(gx) * gy >= (1LL << 24))
     return fail(kTooLarge, "image has too many tiles");
   if (n >= (1 << 30)) return fail(kTooLarge, "too many Gaussians");
-  const BinLayout L = bin_layout(n, width, height);
+  const BinLayout L = bin_layout(n, width, height, tile_mode);
   if (!workspace || workspace_bytes < L.bytes) return fail(kWorkspaceTooSmall, "bin workspace too small");
   if (!ranges || !pairs) return fail(kInvalidArgument, "null ranges/pairs");
   if (!aligned(centers, 8) || !aligned(workspace, 256))
@@ -694,14 +711,15 @@ int splat_bin_prepare(int n, const float* centers, const int* radii, const int* 
   uint32_t* depth_digits = at<uint32_t>(ws, L.depth_digits);
   uint32_t* tile_digits = at<uint32_t>(ws, L.tile_digits);
   const unsigned sort_tiles = blocks_for(n, kSortTile);
-  const ChunkPlan plan = chunk_plan(n, gx, gy);
+  const ChunkPlan plan = chunk_plan(n, gx, gy, tile_mode);
   if (plan.use) diff = nullptr;
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const unsigned prep_grid = std::min<unsigned>(blocks_for(n, 256), static_cast<unsigned>(sms * 8));
   unsigned long long* total64 = at<unsigned long long>(ws, L.totals + 8);
-  bin_prepare_kernel<<<prep_grid, 256, 0, counted(s)>>>(n, centers, radii, tiles, depths, gx, gy, keys_a,
-                                               vals_a, rects, diff, hist, total64);
+  bin_prepare_kernel<<<prep_grid, 256, 0, counted(s)>>>(n, centers, conics, radii, tiles, depths,
+                                                        gx, gy, tile_mode, keys_a, vals_a, rects,
+                                                        diff, hist, total64);
   digit_offsets_kernel<<<1, kRadix, 0, counted(s)>>>(hist, 4, depth_digits);
   // four stable passes over the 32-bit depth keys: a -> b -> a -> b -> a
   for (int pass = 0; pass < 4; ++pass) {
@@ -750,14 +768,21 @@ int splat_bin_prepare(int n, const float* centers, const int* radii, const int* 
   return check_launch("bin_prepare");
 }
 
-int splat_bin_emit(int n, long long pairs, int width, int height, void* workspace,
+int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
+                   const float* centers, const float* conics, const int* radii, void* workspace,
                    size_t workspace_bytes, void* pairs_workspace, size_t pairs_workspace_bytes,
                    int* ids, void* stream) {
   if (n < 0 || pairs < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad sizes");
   if (pairs >= (1LL << 30)) return fail(kTooLarge, "more than 2^30 Gaussian-tile pairs");
+  if (tile_mode < kTileRadius || tile_mode > kTileAccutile)
+    return fail(kInvalidArgument, "tile_mode must be 0 (radius), 1 (snugbox) or 2 (accutile)");
+  if (tile_mode == kTileAccutile && (!centers || !conics || !radii))
+    return fail(kInvalidArgument, "AccuTile emission needs centers, conics and radii");
+  if (!aligned(centers, 8) || !aligned(conics, 16))
+    return fail(kInvalidArgument, "centers need 8-byte and conics 16-byte alignment");
   if (pairs == 0) return kOk;
-  const BinLayout L = bin_layout(n, width, height);
-  const PairLayout P = pair_layout(pairs, width, height);
+  const BinLayout L = bin_layout(n, width, height, tile_mode);
+  const PairLayout P = pair_layout(pairs, width, height, tile_mode);
   if (!workspace || workspace_bytes < L.bytes) return fail(kWorkspaceTooSmall, "bin workspace too small");
   if (P.bytes > 0 && (!pairs_workspace || pairs_workspace_bytes < P.bytes))
     return fail(kWorkspaceTooSmall, "pair workspace too small");
@@ -768,7 +793,7 @@ int splat_bin_emit(int n, long long pairs, int width, int height, void* workspac
   const int passes = tile_passes(gx * gy);
   cudaStream_t s = as_stream(stream);
   char* ws = static_cast<char*>(workspace);
-  const ChunkPlan plan = chunk_plan(n, gx, gy);
+  const ChunkPlan plan = chunk_plan(n, gx, gy, tile_mode);
   if (plan.use) {
     if (plan.smem_scatter > 48 * 1024)
       cudaFuncSetAttribute(tile_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -795,6 +820,31 @@ int splat_bin_emit(int n, long long pairs, int width, int height, void* workspac
   uint32_t* k1 = at<uint32_t>(pw, P.keys1);
   uint32_t* v1 = at<uint32_t>(pw, P.vals1);
   uint32_t* out = reinterpret_cast<uint32_t*>(ids);
+  if (tile_mode == kTileAccutile) {
+    // pairs of the depth-ordered Gaussians at their depth-order offsets, then
+    // stable passes over the tile id
+    emit_strips_kernel<<<blocks_for(n, 256), 256, 0, counted(s)>>>(
+        static_cast<uint32_t>(n), at<uint32_t>(ws, L.vals_a), at<uint32_t>(ws, L.offsets),
+        centers, conics, radii, gx, gy, m, k0, v0);
+    uint32_t* src_k = k0;
+    uint32_t* src_v = v0;
+    for (int pass = 0; pass < passes; ++pass) {
+      const bool last = pass == passes - 1;
+      KeyValueLoader ld{src_k, src_v};
+      uint32_t* dst_k = (src_k == k0) ? k1 : k0;
+      uint32_t* dst_v = last ? out : ((src_v == v0) ? v1 : v0);
+      uint32_t* st = status + static_cast<size_t>(pass) * sort_tiles * kRadix;
+      if (last)
+        onesweep_kernel<KeyValueLoader, false><<<sort_tiles, kSortBlock, 0, counted(s)>>>(
+            ld, m, 8 * pass, tile_digits + pass * kRadix, st, counters + pass, nullptr, dst_v);
+      else
+        onesweep_kernel<KeyValueLoader, true><<<sort_tiles, kSortBlock, 0, counted(s)>>>(
+            ld, m, 8 * pass, tile_digits + pass * kRadix, st, counters + pass, dst_k, dst_v);
+      src_k = dst_k;
+      src_v = dst_v;
+    }
+    return check_launch("bin_emit");
+  }
   if (passes == 1) {
     onesweep_kernel<EmitLoader, false><<<sort_tiles, kSortBlock, 0, counted(s)>>>(
         emit, m, 0, tile_digits, status, counters, nullptr, out);

@@ -31,8 +31,6 @@ def validate_tile_mode(mode) -> None:
     """splatting/intersections.py:24-26."""
     if mode not in TILE_MODES:
         raise ValueError("tile_mode must be 'radius', 'snugbox' or 'accutile'")
-    if mode != "radius":
-        raise NotImplementedError(f"tile_mode {mode!r} is not implemented on the B200 path yet")
 
 
 @dataclass(slots=True)
@@ -151,7 +149,8 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
                            batch_count=layout.batch_count, cameras=layout.cameras, n=layout.n,
                            width=width, height=height, device=layout.device)
         if statistics else ([], {}))
-    bins = stages.bin_and_sort_many([f[7] for f in frames], width, height, camera_status)
+    bins = stages.bin_and_sort_many([f[7] for f in frames], width, height, camera_status,
+                                    tile_mode=tile_mode)
     channels = layout.colors.channels
     blended, alphas = [], []
     for i, (b, c, ctr, con, colors, extras, bg, _state) in enumerate(frames):

@@ -40,7 +40,7 @@ class ProjectView(torch.autograd.Function):
             full.contiguous(), intrinsics.contiguous(), config.width, config.height, config.near,
             config.far, config.radius_clip, sh=None if sh is None else sh.contiguous(),
             sh_degree=sh_degree or 0, campos=None if campos is None else campos.contiguous(),
-            need_active=grad_enabled, normalize_quats=True)
+            need_active=grad_enabled, normalize_quats=True, tile_mode=config.tile_mode)
         st = out.state
         colors = out.colors if out.colors is not None else means.new_empty((0, 3))
         if grad_enabled and any(ctx.needs_input_grad[:8]):

@@ -58,7 +58,8 @@ class _Project(torch.autograd.Function):
     def forward(ctx: Any, means, quats, scales, opacities, view, full, intrinsics,
                 config: ViewConfig, grad_enabled: bool):
         st = stages.project(means, quats, scales, opacities, view, full, intrinsics, config.width,
-                            config.height, config.near, config.far, config.radius_clip)
+                            config.height, config.near, config.far, config.radius_clip,
+                            config.tile_mode)
         if grad_enabled and any(ctx.needs_input_grad[:6]):
             ctx.save_for_backward(means, quats, scales, opacities, view, full, intrinsics,
                                   st.centers, st.conics, st.radii, st.tile_counts, st.depths)
@@ -136,7 +137,8 @@ def prepare_gaussians(means: Tensor, quats: Tensor, scales: Tensor, opacities: T
 
 def bin_and_sort(geometry: GaussianGeometry) -> GaussianTiles:
     """gs3d/ops.py:262-270."""
-    bins = stages.bin_and_sort(geometry._state(), geometry._config.width, geometry._config.height)
+    bins = stages.bin_and_sort(geometry._state(), geometry._config.width, geometry._config.height,
+                               tile_mode=geometry._config.tile_mode)
     return GaussianTiles(bins["ranges"], bins["point_list"], geometry)
 
 

@@ -159,9 +159,19 @@ def cameras_backward(Ks: Tensor, grad_full: Tensor | None, width: int, height: i
 
 # ---- projection --------------------------------------------------------------
 
+TILE_MODES = {"radius": 0, "snugbox": 1, "accutile": 2}
+
+
+def _tile_mode(mode: str) -> int:
+    """splatting/intersections.py:24-26 validate_tile_mode, as the C code."""
+    if mode not in TILE_MODES:
+        raise ValueError("tile_mode must be 'radius', 'snugbox' or 'accutile'")
+    return TILE_MODES[mode]
+
+
 def project(means, quats, scales, opacities, view, projection, intrinsics, width, height,
-            near, far, radius_clip) -> ProjectedGaussians:
-    """gs3d/projection.py:309-354 prepare."""
+            near, far, radius_clip, tile_mode: str = "radius") -> ProjectedGaussians:
+    """gs3d/projection.py:309-354 prepare (tile counts of tile_mode)."""
     pin = Args()
     n = len(means)
     state = ProjectedGaussians(means.new_empty((n, 2)), means.new_empty((n, 4)),
@@ -173,8 +183,8 @@ def project(means, quats, scales, opacities, view, projection, intrinsics, width
             n, pin(means), pin(quats), pin(scales), pin(opacities),
             pin(view), pin(projection), pin(intrinsics), width, height, float(near),
             _far(far), float(radius_clip), ptr(state.centers), ptr(state.conics),
-            ptr(state.radii), ptr(state.tile_counts), ptr(state.depths), _stream(means)),
-            "project_forward")
+            ptr(state.radii), ptr(state.tile_counts), ptr(state.depths), _tile_mode(tile_mode),
+            _stream(means)), "project_forward")
     return state
 
 
@@ -191,7 +201,7 @@ class FusedProjection:
 def project_fused(means, quats, scales, opacities, view, projection, intrinsics, width, height,
                   near, far, radius_clip, sh: Tensor | None = None, sh_degree: int = 0,
                   campos: Tensor | None = None, need_active: bool = True,
-                  normalize_quats: bool = False) -> FusedProjection:
+                  normalize_quats: bool = False, tile_mode: str = "radius") -> FusedProjection:
     """One launch for gs3d/api.py:145-189: projection, masked SH and metadata.
 
     normalize_quats: quats are raw; the kernel applies F.normalize with the
@@ -214,7 +224,8 @@ def project_fused(means, quats, scales, opacities, view, projection, intrinsics,
             _far(far), float(radius_clip), ptr(state.centers), ptr(state.conics),
             ptr(state.radii), ptr(state.tile_counts), ptr(state.depths), int(sh_degree),
             sh_c.shape[1] if sh_c is not None else 0, ptr(sh_c), pin(campos), ptr(colors), 3,
-            ptr(active), ptr(m2d), ptr(mop), ptr(mcon), _stream(means)), "project_forward_fused")
+            ptr(active), ptr(m2d), ptr(mop), ptr(mcon), _tile_mode(tile_mode), _stream(means)),
+            "project_forward_fused")
     return FusedProjection(state, colors, active, m2d, mop, mcon)
 
 
@@ -309,42 +320,51 @@ def scan_counts(counts: Tensor) -> tuple[Tensor, int]:
 class BinPlan:
     """Phase 1 of binning for one view (depth sort, offsets, ranges, count)."""
 
-    def __init__(self, state: ProjectedGaussians, width: int, height: int):
+    def __init__(self, state: ProjectedGaussians, width: int, height: int,
+                 tile_mode: str = "radius"):
         dev = state.radii.device
         n = len(state.radii)
+        self.mode = _tile_mode(tile_mode)
         self.n, self.width, self.height = n, width, height
+        self.state = state
         gx, gy = (width + 15) // 16, (height + 15) // 16
         self.ranges = torch.empty((gx * gy, 2), dtype=torch.int32, device=dev)
         self.pairs_dev = torch.zeros(1, dtype=torch.int64, device=dev)
-        self.workspace = torch.empty(lib.splat_bin_workspace_bytes(n, width, height),
+        self.workspace = torch.empty(lib.splat_bin_workspace_bytes(n, width, height, self.mode),
                                      dtype=torch.uint8, device=dev)
-        pin = Args()
+        self.pin = Args()  # the projected rows stay referenced until emit
+        pin = self.pin
         check(lib.splat_bin_prepare(
-            n, pin(state.centers), pin(state.radii), pin(state.tile_counts), pin(state.depths),
-            width, height, ptr(self.workspace), self.workspace.numel(), ptr(self.ranges),
-            ptr(self.pairs_dev), nv.stream(dev)), "bin_prepare")
+            n, pin(state.centers), pin(state.conics), pin(state.radii), pin(state.tile_counts),
+            pin(state.depths), width, height, self.mode, ptr(self.workspace),
+            self.workspace.numel(), ptr(self.ranges), ptr(self.pairs_dev), nv.stream(dev)),
+            "bin_prepare")
 
     def emit(self, pairs: int) -> Tensor:
         dev = self.ranges.device
         ids = torch.empty(pairs, dtype=torch.int32, device=dev)
         if pairs:
-            pws = torch.empty(lib.splat_bin_pairs_workspace_bytes(pairs, self.width, self.height),
+            pws = torch.empty(lib.splat_bin_pairs_workspace_bytes(pairs, self.width, self.height,
+                                                                  self.mode),
                               dtype=torch.uint8, device=dev)
-            check(lib.splat_bin_emit(self.n, pairs, self.width, self.height, ptr(self.workspace),
-                                     self.workspace.numel(), ptr(pws), pws.numel(), ptr(ids),
-                                     nv.stream(dev)), "bin_emit")
+            pin, st = self.pin, self.state
+            check(lib.splat_bin_emit(self.n, pairs, self.width, self.height, self.mode,
+                                     pin(st.centers), pin(st.conics), pin(st.radii),
+                                     ptr(self.workspace), self.workspace.numel(), ptr(pws),
+                                     pws.numel(), ptr(ids), nv.stream(dev)), "bin_emit")
         self.workspace = None
+        self.pin = None
         return ids
 
 
 def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
-                      camera_status: list | None = None):
+                      camera_status: list | None = None, tile_mode: str = "radius"):
     """Bin several views with one host read of all pair counts.
 
     camera_status: deferred camera status tensors (cameras_prepare's
     status_sink); they are read in the same synchronisation and their errors
     raised before any pair is emitted."""
-    plans = [BinPlan(s, width, height) for s in states]
+    plans = [BinPlan(s, width, height, tile_mode) for s in states]
     parts = [p.pairs_dev for p in plans]
     ncodes = 0
     if camera_status:
@@ -359,9 +379,11 @@ def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
     return [dict(point_list=p.emit(int(m)), ranges=p.ranges) for p, m in zip(plans, counts)]
 
 
-def bin_and_sort(state: ProjectedGaussians, width: int, height: int) -> dict[str, Tensor]:
-    """splatting/binning.py:171-217 (tile_mode "radius"): point_list and ranges."""
-    return bin_and_sort_many([state], width, height)[0]
+def bin_and_sort(state: ProjectedGaussians, width: int, height: int,
+                 tile_mode: str = "radius") -> dict[str, Tensor]:
+    """splatting/binning.py:171-217: point_list and ranges.  state.tile_counts
+    must come from the projection with the same tile_mode."""
+    return bin_and_sort_many([state], width, height, tile_mode=tile_mode)[0]
 
 
 # ---- blending ----------------------------------------------------------------

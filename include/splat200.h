@@ -46,15 +46,17 @@ int splat_cameras_backward(int count, const float* Ks, const float* grad_full, i
                            int height, const float* inverse, const float* grad_centers,
                            float* grad_views, void* stream);
 
-/* gs3d/projection.py:309-354 prepare -> project kernel :89-164 (tile_mode "radius").
+/* gs3d/projection.py:309-354 prepare -> project kernel :89-164.
  * Outputs centers (n,2), conics (n,4), radii (n), tiles (n), depths (n);
  * rows with radii == 0 leave centers/conics/depths unwritten, as the
- * reference does. */
+ * reference does.  tile_mode: 0 radius, 1 snugbox, 2 accutile
+ * (splatting/intersections.py:21-218); modes 1 and 2 replace tiles[i] with
+ * the mode's tile count (:150-162) and keep the radius even when it is 0. */
 int splat_project_forward(int n, const float* means, const float* quats, const float* scales,
                           const float* opacities, const float* view, const float* proj,
                           const float* K, int width, int height, float near_plane,
                           float far_plane, float radius_clip, float* centers, float* conics,
-                          int* radii, int* tiles, float* depths, void* stream);
+                          int* radii, int* tiles, float* depths, int tile_mode, void* stream);
 
 /* gs3d/api.py:145-189 per-view preparation in one launch: the projection above,
  * the masked SH evaluation of primitives/spherical_harmonics.py:18-59
@@ -73,7 +75,8 @@ int splat_project_forward_fused(int n, const float* means, const float* quats,
                                 float* depths, int sh_degree, int sh_k, const float* sh,
                                 const float* campos, float* colors, int color_stride,
                                 unsigned char* active, float* meta_means2d,
-                                float* meta_opacities, float* meta_conics, void* stream);
+                                float* meta_opacities, float* meta_conics, int tile_mode,
+                                void* stream);
 
 /* splatting/metadata.py:34-70 prepare_metadata -> _prepare :12-31. */
 int splat_metadata(int n, const int* radii, const float* centers, const float* conics,
@@ -147,9 +150,11 @@ int splat_scan_counts(int n, const int* counts, int* offsets, long long* total, 
 int splat_scan_counts_static(int n, const int* counts, int* offsets, long long* total,
                              void* stream);
 
-/* splatting/binning.py:171-217 bin_and_sort (tile_mode "radius"), split in
- * two calls around the one host read of the pair count that the reference
- * also makes (primitives/tiling.py:64):
+/* splatting/binning.py:171-217 bin_and_sort, split in two calls around the
+ * one host read of the pair count that the reference also makes
+ * (primitives/tiling.py:64).  tile_mode as for the projection (conics are
+ * required for modes 1 and 2; tiles must be the projection's counts for the
+ * same mode):
  *   splat_bin_prepare: depth-key sort, pair offsets, per-tile ranges (T,2)
  *     (zeros for empty tiles, as identify_ranges leaves them) and the pair
  *     count M into *pairs (device int64).
@@ -158,12 +163,14 @@ int splat_scan_counts_static(int n, const int* counts, int* offsets, long long* 
  *     (float bits of depth, index), identical to the stable 64-bit key sort
  *     of primitives/tiling.py:80-86.
  * The workspace passed to prepare must be passed unchanged to emit. */
-size_t splat_bin_workspace_bytes(int n, int width, int height);
-size_t splat_bin_pairs_workspace_bytes(long long pairs, int width, int height);
-int splat_bin_prepare(int n, const float* centers, const int* radii, const int* tiles,
-                      const float* depths, int width, int height, void* workspace,
-                      size_t workspace_bytes, int* ranges, long long* pairs, void* stream);
-int splat_bin_emit(int n, long long pairs, int width, int height, void* workspace,
+size_t splat_bin_workspace_bytes(int n, int width, int height, int tile_mode);
+size_t splat_bin_pairs_workspace_bytes(long long pairs, int width, int height, int tile_mode);
+int splat_bin_prepare(int n, const float* centers, const float* conics, const int* radii,
+                      const int* tiles, const float* depths, int width, int height, int tile_mode,
+                      void* workspace, size_t workspace_bytes, int* ranges, long long* pairs,
+                      void* stream);
+int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
+                   const float* centers, const float* conics, const int* radii, void* workspace,
                    size_t workspace_bytes, void* pairs_workspace, size_t pairs_workspace_bytes,
                    int* ids, void* stream);
 

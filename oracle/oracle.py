@@ -263,7 +263,8 @@ class ViewResult:
 
 def gs3d_view_forward(means, quats_n, scales, opacities, viewmat, K, width, height, *,
                       sh_coeffs=None, sh_degree=None, features=None, extras=None,
-                      background=None, near=0.2, far=float("inf"), radius_clip=0.0):
+                      background=None, near=0.2, far=float("inf"), radius_clip=0.0,
+                      tile_mode="radius"):
     """quats_n must already be normalised (the reference normalises with Torch)."""
     with_centers = sh_coeffs is not None and sh_degree > 0
     full, inverse, campos, errors = cameras_prepare(viewmat[None], K[None], width, height,
@@ -271,7 +272,7 @@ def gs3d_view_forward(means, quats_n, scales, opacities, viewmat, K, width, heig
     if errors[0]:
         raise ValueError(f"camera error code {errors[0]}")
     p = project_forward(means, quats_n, scales, opacities, viewmat, full[0], K, width,
-                        height, near, far, radius_clip)
+                        height, near, far, radius_clip, tile_mode=tile_mode)
     active = None
     if sh_coeffs is not None:
         dirs = (np.asarray(means, np.float32) - campos[0][None]) if with_centers else np.asarray(means, np.float32)
@@ -287,7 +288,8 @@ def gs3d_view_forward(means, quats_n, scales, opacities, viewmat, K, width, heig
     if background is not None:
         bg[: colors.shape[1]] = background
     offsets, m = scan_counts(p.tiles)
-    keys, ids, ranges = bin_and_sort(p.centers, p.radii, p.depths, offsets, width, height)
+    keys, ids, ranges = bin_and_sort(p.centers, p.radii, p.depths, offsets, width, height,
+                                     conics=p.conics, tile_mode=tile_mode)
     image, final_t, contrib = render_forward(width, height, ranges, ids, p.centers, p.conics,
                                              attrs, bg)
     return ViewResult(image, final_t, contrib, p, keys, ids, ranges, attrs, active, full[0],

@@ -25,7 +25,7 @@ IMG_TOL = 1e-5
 GRAD_TOL = 1e-3
 
 
-def _run(scene, *, use_features=False, absgrad=True, background=None):
+def _run(scene, *, use_features=False, absgrad=True, background=None, tile_mode="radius"):
     d = torch.device("cuda", 0)
     p = {k: getattr(scene, k).to(d).requires_grad_(True)
          for k in ("means", "quats", "scales", "opacities")}
@@ -41,7 +41,7 @@ def _run(scene, *, use_features=False, absgrad=True, background=None):
     if background is not None:
         kw["backgrounds"] = background.to(d)
     res = gs3d.rasterize(p["means"], p["quats"], p["scales"], p["opacities"], viewmats, Ks,
-                         scene.width, scene.height, absgrad=absgrad, **kw)
+                         scene.width, scene.height, absgrad=absgrad, tile_mode=tile_mode, **kw)
     C = scene.viewmats.shape[0]
     g = torch.Generator().manual_seed(11)
     gF = torch.randn(C, scene.height, scene.width, 3, generator=g)
@@ -51,7 +51,7 @@ def _run(scene, *, use_features=False, absgrad=True, background=None):
     return res, p, viewmats, colors, gF, gA
 
 
-def _oracle(scene, gF, gA, *, use_features=False, background=None):
+def _oracle(scene, gF, gA, *, use_features=False, background=None, tile_mode="radius"):
     d = torch.device("cuda", 0)
     qn_gpu = F.normalize(scene.quats.to(d), dim=-1).cpu()
     C = scene.viewmats.shape[0]
@@ -65,7 +65,7 @@ def _oracle(scene, gF, gA, *, use_features=False, background=None):
         r, bg = O.gs3d_view_forward(means, qn, scene.scales.numpy(), scene.opacities.numpy(),
                                     scene.viewmats[c].numpy(), scene.Ks[c].numpy(), scene.width,
                                     scene.height, background=None if background is None else
-                                    background[c].numpy(), **kw)
+                                    background[c].numpy(), tile_mode=tile_mode, **kw)
         up = np.concatenate([gF[c].numpy(), gA[c].numpy()], axis=-1)
         if use_features:
             g = O.gs3d_view_backward(r, bg, means, qn, scene.scales.numpy(),
@@ -187,3 +187,25 @@ def test_error_paths():
     with pytest.raises(torch.linalg.LinAlgError):
         gs3d.rasterize(args[0], args[1], args[2], args[3], singular, scene.Ks.to(d), scene.width,
                        scene.height, sh_coeffs=sh3)
+
+
+@pytest.mark.parametrize("tile_mode", ["snugbox", "accutile"])
+def test_rasterize_tile_modes(tile_mode):
+    """gs3d.rasterize(tile_mode=...) end to end: images, gradients and the
+    tiles_per_gauss metadata of the mode against the oracle."""
+    scene = make_scene(config=1, n=20000, width=480, height=270)
+    res, p, viewmats, colors, gF, gA = _run(scene, tile_mode=tile_mode)
+    images, per_view, acc = _oracle(scene, gF, gA, tile_mode=tile_mode)
+    got = torch.cat([res.features, res.alpha], -1).detach().cpu().numpy()
+    assert np.abs(np.moveaxis(got[0], -1, 0) - images[0]).max() <= IMG_TOL
+    for name in ("means", "quats", "scales", "opacities"):
+        assert rel_l2(p[name].grad.cpu(), acc[name]) <= GRAD_TOL, name
+    assert rel_l2(colors.grad.cpu(), acc["colors"]) <= GRAD_TOL
+    assert res.meta["tile_mode"] == tile_mode
+    qn = F.normalize(scene.quats.to("cuda:0"), dim=-1).cpu().numpy()
+    full, _, _, _ = O.cameras_prepare(scene.viewmats[:1].numpy(), scene.Ks[:1].numpy(),
+                                      scene.width, scene.height, False)
+    ref = O.project_forward(scene.means.numpy(), qn, scene.scales.numpy(),
+                            scene.opacities.numpy(), scene.viewmats[0].numpy(), full[0],
+                            scene.Ks[0].numpy(), scene.width, scene.height, tile_mode=tile_mode)
+    np.testing.assert_array_equal(res.meta["tiles_per_gauss"][0].cpu().numpy(), ref.tiles)

@@ -344,6 +344,45 @@ def test_tile_pass_counts(width, height):
     np.testing.assert_array_equal(bins["point_list"].cpu().numpy(), ids)
 
 
+@pytest.mark.parametrize("mode", ["snugbox", "accutile"])
+@pytest.mark.parametrize("size", [(480, 270), (1, 1), (3000, 2000), (4096, 4096), (4200, 4100)])
+def test_tile_modes_bit_exact(mode, size):
+    """tile_mode snugbox/accutile: tile counts, point_list and ranges against
+    the oracle; snugbox on the chunked scatter and (>40K tiles) the onesweep
+    path, accutile on the strip emission with 1-3 tile-id passes; then the
+    blend over those bins (contributors bit-exact)."""
+    width, height = size
+    s = make_scene(1, n=6000, width=width, height=height)
+    d = _dev()
+    s.Ks[0] = torch.tensor([[width * 0.9, 0, width / 2], [0, width * 0.9, height / 2], [0, 0, 1]])
+    view, K = s.viewmats[0].to(d), s.Ks[0].to(d)
+    full, _, _ = stages.cameras_prepare(view[None], K[None], width, height, False)
+    q = F.normalize(s.quats.to(d), dim=-1)
+    opac = s.opacities.clone()
+    opac[::17] = 1.0 / 255.0 * (0.5 + torch.rand(len(opac[::17])))  # around the cut-off
+    st = stages.project(s.means.to(d), q, s.scales.to(d), opac.to(d), view, full[0], K,
+                        width, height, 0.2, float("inf"), 0.0, tile_mode=mode)
+    ref = O.project_forward(s.means.numpy(), q.cpu().numpy(), s.scales.numpy(), opac.numpy(),
+                            view.cpu().numpy(), full[0].cpu().numpy(), K.cpu().numpy(), width,
+                            height, tile_mode=mode)
+    np.testing.assert_array_equal(st.radii.cpu().numpy(), ref.radii)
+    np.testing.assert_array_equal(st.tile_counts.cpu().numpy(), ref.tiles)
+    bins = stages.bin_and_sort(st, width, height, tile_mode=mode)
+    off, _ = O.scan_counts(ref.tiles)
+    _, ids, ranges = O.bin_and_sort(ref.centers, ref.radii, ref.depths, off, width, height,
+                                    conics=ref.conics, tile_mode=mode)
+    np.testing.assert_array_equal(bins["ranges"].cpu().numpy(), ranges)
+    np.testing.assert_array_equal(bins["point_list"].cpu().numpy(), ids)
+    if width * height <= 480 * 270:
+        feats = torch.rand(len(q), 3, device=d)
+        bg = torch.zeros(4, device=d)
+        px = stages.render(st, bins, feats, None, True, bg, width, height)
+        attrs = np.concatenate([feats.cpu().numpy(), np.ones((len(q), 1), np.float32)], 1)
+        _, _, contrib = O.render_forward(width, height, ranges, ids, ref.centers, ref.conics,
+                                         attrs, np.zeros(4, np.float32))
+        np.testing.assert_array_equal(px.contributors.cpu().numpy(), contrib)
+
+
 def test_huge_footprint_and_out_of_view():
     """A Gaussian covering every tile, plus Gaussians outside the image."""
     d = _dev()
