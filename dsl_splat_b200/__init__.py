@@ -8,5 +8,7 @@ CUDA for sm_100a) reached through the C ABI in include/splat200.h.
 from .cameras import PinholeCamera
 from .statistics import MaskedContributionCount, WeightedContributionSum
 from . import gs3d
+from . import torch_ops  # registers torch.ops.splat200.*
 
-__all__ = ["gs3d", "PinholeCamera", "MaskedContributionCount", "WeightedContributionSum"]
+__all__ = ["gs3d", "torch_ops", "PinholeCamera", "MaskedContributionCount",
+           "WeightedContributionSum"]

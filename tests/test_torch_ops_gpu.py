@@ -1,0 +1,95 @@
+"""torch.ops.splat200.* on the GPU: the same results as the stage wrappers,
+autograd through the operators equal to gs3d.rasterize's gradients, and a
+torch.compile trace of the forward chain."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import rel_l2
+import dsl_splat_b200  # noqa: F401
+from dsl_splat_b200 import gs3d, stages
+from dsl_splat_b200.scenes import make_scene
+
+pytestmark = pytest.mark.gpu
+
+
+def _inputs():
+    d = torch.device("cuda", 0)
+    s = make_scene(1, n=20000, width=480, height=270)
+    view, K = s.viewmats[0].to(d).contiguous(), s.Ks[0].to(d).contiguous()
+    full, _, campos = torch.ops.splat200.cameras_prepare(view[None], K[None], s.width, s.height,
+                                                         True)
+    return s, d, view, K, full[0], campos[0]
+
+
+def _chain(s, d, view, K, full, campos, means, quats_n, scales, opac, sh, tile_mode="radius"):
+    ctr, con, radii, tiles, depths = torch.ops.splat200.project(
+        means, quats_n, scales, opac, view, full, K, s.width, s.height, 0.2, float("inf"), 0.0,
+        tile_mode)
+    ranges, ids = torch.ops.splat200.bin_and_sort(ctr, con, radii, tiles, depths, s.width,
+                                                  s.height, tile_mode)
+    colors, _ = torch.ops.splat200.sh_forward(sh, means - campos, s.sh_degree, radii)
+    bg = torch.zeros(4, device=d)
+    image, alpha, final_t, contrib = torch.ops.splat200.render(ctr, con, ranges, ids, colors, bg,
+                                                               s.width, s.height)
+    return image, alpha, final_t, contrib, ranges, ids
+
+
+@pytest.mark.parametrize("tile_mode", ["radius", "accutile"])
+def test_ops_match_stages(tile_mode):
+    s, d, view, K, full, campos = _inputs()
+    means, q = s.means.to(d), F.normalize(s.quats.to(d), dim=-1)
+    scales, opac, sh = s.scales.to(d), s.opacities.to(d), s.sh_coeffs.to(d)
+    image, alpha, final_t, contrib, ranges, ids = _chain(s, d, view, K, full, campos, means, q,
+                                                         scales, opac, sh, tile_mode)
+    st = stages.project(means, q, scales, opac, view, full, K, s.width, s.height, 0.2,
+                        float("inf"), 0.0, tile_mode)
+    bins = stages.bin_and_sort(st, s.width, s.height, tile_mode=tile_mode)
+    assert torch.equal(ranges, bins["ranges"]) and torch.equal(ids, bins["point_list"])
+    colors, _ = stages.sh_forward(sh, means - campos, s.sh_degree, st.radii, True)
+    px = stages.render(st, bins, colors, None, True, torch.zeros(4, device=d), s.width, s.height,
+                       separate_alpha=True)
+    assert torch.equal(image, px.features) and torch.equal(alpha, px.alpha)
+    assert torch.equal(final_t, px.transmittance) and torch.equal(contrib, px.contributors)
+
+
+def test_ops_autograd_matches_rasterize():
+    s, d, view, K, full, campos = _inputs()
+    leaves = {k: getattr(s, k).to(d).requires_grad_(True)
+              for k in ("means", "quats", "scales", "opacities")}
+    sh = s.sh_coeffs.to(d).requires_grad_(True)
+    g = torch.Generator().manual_seed(5)
+    gF = torch.randn(s.height, s.width, 3, generator=g).to(d)
+    gA = torch.randn(s.height, s.width, 1, generator=g).to(d)
+    image, alpha, *_ = _chain(s, d, view, K, full, campos, leaves["means"],
+                              F.normalize(leaves["quats"], dim=-1), leaves["scales"],
+                              leaves["opacities"], sh)
+    ((image * gF).sum() + (alpha * gA).sum()).backward()
+    ref = {k: getattr(s, k).to(d).requires_grad_(True)
+           for k in ("means", "quats", "scales", "opacities")}
+    ref_sh = s.sh_coeffs.to(d).requires_grad_(True)
+    res = gs3d.rasterize(ref["means"], ref["quats"], ref["scales"], ref["opacities"],
+                         view[None], K[None], s.width, s.height, sh_coeffs=ref_sh,
+                         sh_degree=s.sh_degree)
+    assert torch.equal(res.features[0], image) and torch.equal(res.alpha[0], alpha)
+    ((res.features[0] * gF).sum() + (res.alpha[0] * gA).sum()).backward()
+    for k in leaves:
+        assert rel_l2(leaves[k].grad.cpu(), ref[k].grad.cpu()) <= 1e-4, k
+    assert rel_l2(sh.grad.cpu(), ref_sh.grad.cpu()) <= 1e-4
+
+
+def test_ops_trace_with_torch_compile():
+    s, d, view, K, full, campos = _inputs()
+    means, q = s.means.to(d), F.normalize(s.quats.to(d), dim=-1)
+    scales, opac, sh = s.scales.to(d), s.opacities.to(d), s.sh_coeffs.to(d)
+
+    def forward(means, q, scales, opac, sh):
+        image, alpha, *_ = _chain(s, d, view, K, full, campos, means, q, scales, opac, sh)
+        return image, alpha
+
+    eager = forward(means, q, scales, opac, sh)
+    torch._dynamo.reset()
+    compiled = torch.compile(forward, fullgraph=True, backend="eager")(means, q, scales, opac,
+                                                                        sh)
+    assert torch.equal(eager[0], compiled[0]) and torch.equal(eager[1], compiled[1])
