@@ -138,7 +138,14 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
             (layout.batch_count, layout.cameras, layout.n) + tuple(rows[0].shape[1:]))
         for name, rows in dense.items()
     }
-    training = prepare_training_metadata(geometry, layout, packed=packed, absgrad=absgrad)
+    # Binning reads the pair counts (and camera status) in one host
+    # synchronisation; the packed metadata's visible counts ride along.
+    visible = [(f[7].radii > 0).sum() for f in frames] if packed else []
+    bins, visible_counts = stages.bin_and_sort_many([f[7] for f in frames], width, height,
+                                                    camera_status, tile_mode=tile_mode,
+                                                    host_reads=visible)
+    training = prepare_training_metadata(geometry, layout, packed=packed, absgrad=absgrad,
+                                         visible_counts=visible_counts if packed else None)
     meta = training.values
     meta.update(width=width, height=height, tile_size=16, tile_width=(width + 15) // 16,
                 tile_height=(height + 15) // 16, n_cameras=layout.cameras, packed=packed,
@@ -149,8 +156,6 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
                            batch_count=layout.batch_count, cameras=layout.cameras, n=layout.n,
                            width=width, height=height, device=layout.device)
         if statistics else ([], {}))
-    bins = stages.bin_and_sort_many([f[7] for f in frames], width, height, camera_status,
-                                    tile_mode=tile_mode)
     channels = layout.colors.channels
     blended, alphas = [], []
     for i, (b, c, ctr, con, colors, extras, bg, _state) in enumerate(frames):

@@ -358,12 +358,15 @@ class BinPlan:
 
 
 def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
-                      camera_status: list | None = None, tile_mode: str = "radius"):
+                      camera_status: list | None = None, tile_mode: str = "radius",
+                      host_reads: list[Tensor] | None = None):
     """Bin several views with one host read of all pair counts.
 
     camera_status: deferred camera status tensors (cameras_prepare's
     status_sink); they are read in the same synchronisation and their errors
-    raised before any pair is emitted."""
+    raised before any pair is emitted.  host_reads: further integer scalars
+    the caller needs on the host, read in that same synchronisation; when
+    given, (bins, their values) is returned."""
     plans = [BinPlan(s, width, height, tile_mode) for s in states]
     parts = [p.pairs_dev for p in plans]
     ncodes = 0
@@ -371,12 +374,15 @@ def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
         codes_dev = torch.cat([c.to(torch.int64) for c in camera_status])
         ncodes = len(codes_dev)
         parts = [codes_dev] + parts
-    if not parts:
-        return []
-    values = torch.cat(parts).tolist()
+    extra = [t.reshape(1).to(torch.int64) for t in (host_reads or [])]
+    parts = parts + extra
+    values = torch.cat(parts).tolist() if parts else []
     raise_camera_errors(values[:ncodes])
-    counts = values[ncodes:]
-    return [dict(point_list=p.emit(int(m)), ranges=p.ranges) for p, m in zip(plans, counts)]
+    counts = values[ncodes:ncodes + len(plans)]
+    bins = [dict(point_list=p.emit(int(m)), ranges=p.ranges) for p, m in zip(plans, counts)]
+    if host_reads is None:
+        return bins
+    return bins, values[ncodes + len(plans):]
 
 
 def bin_and_sort(state: ProjectedGaussians, width: int, height: int,

@@ -47,10 +47,21 @@ class TrainingMetadata:
 
 
 def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packed: bool,
-                              absgrad: bool) -> TrainingMetadata:
-    """training.py:24-76: dense or packed metadata, the means2d leaf and absgrad."""
+                              absgrad: bool,
+                              visible_counts: list[int] | None = None) -> TrainingMetadata:
+    """training.py:24-76: dense or packed metadata, the means2d leaf and absgrad.
+
+    visible_counts (packed): the per-view number of visible Gaussians, already
+    read on the host (gs3d.rasterize reads them with the pair counts); the
+    packed indices then come from nonzero_static and this function makes no
+    host synchronisation of its own."""
     if packed:
-        batch_ids, camera_ids, gaussian_ids = (dense["radii"] > 0).all(-1).nonzero(as_tuple=True)
+        mask = (dense["radii"] > 0).all(-1)
+        if visible_counts is None:
+            batch_ids, camera_ids, gaussian_ids = mask.nonzero(as_tuple=True)
+        else:
+            idx = torch.nonzero_static(mask, size=int(sum(visible_counts)))
+            batch_ids, camera_ids, gaussian_ids = idx.unbind(1)
         values = {name: v[batch_ids, camera_ids, gaussian_ids] for name, v in dense.items()}
     else:
         batch_ids = camera_ids = gaussian_ids = None
@@ -71,8 +82,11 @@ def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packe
         absolute = torch.zeros_like(screen)
         setattr(screen, "absgrad", absolute)
         if packed:
-            counts = ([len(screen)] if len(targets) == 1
-                      else (dense["radii"] > 0).all(-1).sum(-1).flatten().tolist())
+            if visible_counts is not None:
+                counts = list(visible_counts)
+            else:
+                counts = ([len(screen)] if len(targets) == 1
+                          else (dense["radii"] > 0).all(-1).sum(-1).flatten().tolist())
             begin = 0
             for i, count in enumerate(counts):
                 end = begin + count

@@ -209,3 +209,34 @@ def test_rasterize_tile_modes(tile_mode):
                             scene.opacities.numpy(), scene.viewmats[0].numpy(), full[0],
                             scene.Ks[0].numpy(), scene.width, scene.height, tile_mode=tile_mode)
     np.testing.assert_array_equal(res.meta["tiles_per_gauss"][0].cpu().numpy(), ref.tiles)
+
+
+def test_single_host_synchronisation_per_call():
+    """One host read per rasterize call (pair counts, camera status and, when
+    packed, the visible counts together), as the reference's single .item()
+    (primitives/tiling.py:64); packed metadata adds no synchronisation."""
+    import warnings
+    scene = make_scene(config=2, n=30000, width=324, height=210, cameras=3)
+    d = torch.device("cuda", 0)
+    args = [getattr(scene, k).to(d) for k in ("means", "quats", "scales", "opacities")]
+    vm, Ks, sh = scene.viewmats.to(d), scene.Ks.to(d), scene.sh_coeffs.to(d)
+    for packed in (False, True):
+        gs3d.rasterize(*args, vm, Ks, scene.width, scene.height, sh_coeffs=sh, packed=packed,
+                       absgrad=True)  # warm-up (allocator, first-use setup)
+        torch.cuda.synchronize()
+        torch.cuda.set_sync_debug_mode("warn")
+        try:
+            with warnings.catch_warnings(record=True) as caught:
+                warnings.simplefilter("always")
+                res = gs3d.rasterize(*args, vm, Ks, scene.width, scene.height, sh_coeffs=sh,
+                                     packed=packed, absgrad=True)
+        finally:
+            torch.cuda.set_sync_debug_mode(0)
+        syncs = [w for w in caught if "synchroniz" in str(w.message)]
+        assert len(syncs) == 1, [str(w.message)[:120] for w in syncs]
+        if packed:
+            dense = gs3d.rasterize(*args, vm, Ks, scene.width, scene.height, sh_coeffs=sh,
+                                   absgrad=True)
+            mask = (dense.radii > 0).all(-1)
+            assert torch.equal(res.meta["radii"], dense.radii[mask])
+            assert torch.equal(res.meta["means2d"].detach(), dense.means2d.detach()[mask])
