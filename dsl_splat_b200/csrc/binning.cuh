@@ -242,22 +242,27 @@ struct EmitLoader {
   }
 };
 
-template <class Loader, bool WRITE_KEYS>
-__global__ void __launch_bounds__(kSortBlock)
+// THREADS >= 256: the first 256 threads own one digit each in the look-back;
+// larger blocks shorten the look-back chain at the cost of fewer blocks.
+template <class Loader, bool WRITE_KEYS, int THREADS = kSortBlock>
+__global__ void __launch_bounds__(THREADS)
     onesweep_kernel(Loader ld, uint32_t n, int shift, const uint32_t* __restrict__ digit_offsets,
                     uint32_t* __restrict__ status, uint32_t* __restrict__ counter,
                     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out) {
-  __shared__ uint32_t s_hist[kSortWarps][kRadix];
+  constexpr int kWarps = THREADS / 32;
+  constexpr uint32_t kTile = static_cast<uint32_t>(THREADS) * kSortItems;
+  static_assert(THREADS >= kRadix && THREADS % 32 == 0, "one thread per digit");
+  __shared__ uint32_t s_hist[kWarps][kRadix];
   __shared__ uint32_t s_base[kRadix];
   __shared__ uint32_t s_tile;
   __shared__ typename Loader::Shared s_ld;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) s_tile = atomicAdd(counter, 1u);
-  for (int k = threadIdx.x; k < kSortWarps * kRadix; k += kSortBlock) (&s_hist[0][0])[k] = 0u;
+  for (int k = threadIdx.x; k < kWarps * kRadix; k += THREADS) (&s_hist[0][0])[k] = 0u;
   __syncthreads();
   const uint32_t tile = s_tile;
-  const uint32_t base = tile * kSortTile;
-  const uint32_t end = min(base + static_cast<uint32_t>(kSortTile), n);
+  const uint32_t base = tile * kTile;
+  const uint32_t end = min(base + kTile, n);
   ld.prepare(base, end, s_ld);
 
   uint32_t keys[kSortItems], vals[kSortItems], rank[kSortItems];
@@ -281,11 +286,11 @@ __global__ void __launch_bounds__(kSortBlock)
   }
   __syncthreads();
 
-  {
+  if (threadIdx.x < kRadix) {
     const int d = threadIdx.x;
     uint32_t total = 0u;
 #pragma unroll
-    for (int w = 0; w < kSortWarps; ++w) {
+    for (int w = 0; w < kWarps; ++w) {
       const uint32_t c = s_hist[w][d];
       s_hist[w][d] = total;
       total += c;
