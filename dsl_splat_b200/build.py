@@ -1,9 +1,17 @@
 """Builds libsplat200.so in place for sm_100a (nvcc, no JIT cache).
 
--fmad=false keeps every multiply-add two IEEE roundings unless the source
-asks for __fmaf_rn, which is what makes radii, tile counts and sort keys
-reproducible on the CPU.  Division and square root stay IEEE-rounded (the
-nvcc defaults -prec-div=true -prec-sqrt=true, no --use_fast_math).
+Two translation units, compiled in parallel and linked into one library:
+
+* splat200.cu (entry points, forward kernels, binning, blending) with
+  -fmad=false: every multiply-add stays two IEEE roundings unless the source
+  asks for __fmaf_rn, which is what makes radii, tile counts, sort keys and
+  the blended image reproducible on the CPU;
+* project_backward.cu (the projection + SH backward) with -fmad=true: its
+  outputs are gradients, compared within a relative tolerance, and
+  contraction removes a large part of its arithmetic.
+
+Division and square root stay IEEE-rounded everywhere (the nvcc defaults
+-prec-div=true -prec-sqrt=true, no --use_fast_math).
 """
 
 from __future__ import annotations
@@ -16,13 +24,15 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libsplat200.so")
-SOURCES = ["splat200.cu"]
-HEADERS = ["splat_common.cuh", "cameras.cuh", "project.cuh", "binning.cuh", "render.cuh"]
+BUILD_DIR = os.path.join(HERE, "_build")
+# source -> its contraction flag
+SOURCES = {"splat200.cu": "-fmad=false", "project_backward.cu": "-fmad=true"}
+HEADERS = ["splat_common.cuh", "cameras.cuh", "project.cuh", "binning.cuh", "render.cuh",
+           "footprint.cuh", "tile_modes.cuh", "host_runtime.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
-    "-lineinfo", "-O3", "-std=c++17", "-fmad=false",
-    "-Xcompiler", "-fPIC", "-shared",
+    "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
 ]
 
 
@@ -36,7 +46,7 @@ def needs_build() -> bool:
     if not os.path.exists(LIB):
         return True
     built = os.path.getmtime(LIB)
-    inputs = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
+    inputs = [os.path.join(CSRC, f) for f in [*SOURCES, *HEADERS]]
     inputs.append(os.path.join(ROOT, "include", "splat200.h"))
     return any(os.path.exists(f) and os.path.getmtime(f) > built for f in inputs)
 
@@ -44,11 +54,24 @@ def needs_build() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not needs_build():
         return LIB
-    cmd = [nvcc(), *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-o", LIB + ".tmp",
-           *[os.path.join(CSRC, f) for f in SOURCES]]
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    objects, jobs = [], []
+    for src, fmad in SOURCES.items():
+        obj = os.path.join(BUILD_DIR, os.path.splitext(src)[0] + ".o")
+        cmd = [nvcc(), *NVCC_FLAGS, fmad, "-I", os.path.join(ROOT, "include"), "-c",
+               os.path.join(CSRC, src), "-o", obj]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        jobs.append((cmd, subprocess.Popen(cmd)))
+        objects.append(obj)
+    failed = [cmd for cmd, job in jobs if job.wait() != 0]
+    if failed:
+        raise subprocess.CalledProcessError(1, failed[0])
+    link = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", LIB + ".tmp",
+            *objects]
     if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True)
+        print(" ".join(link), file=sys.stderr)
+    subprocess.run(link, check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB
 

@@ -1,13 +1,11 @@
-// gs3d projection forward/backward, fused with SH0-3 and metadata.
+// gs3d projection forward, fused with SH0-3 and metadata, and the shared
+// math of the backward.
 //
 // Forward restates gs3d/projection.py:37-164 (screen_covariance, project),
 // splatting/geometry.py:22-123 and primitives/sh.py:7-79 operation by
 // operation (compiled with -fmad=false; __fmaf_rn where the reference calls
-// fmaf).  Backward is the hand-derived VJP of projection_loss
-// (gs3d/projection.py:198-285) with the reference's custom adjoints for the
-// Jacobian clamp (splatting/geometry.py:42-51), the regularised inverse
-// covariance (splatting/geometry.py:61-71) and the quaternion rotation
-// (splatting/math.py:13-28), plus the SH VJP (primitives/sh.py:82-138).
+// fmaf).  The projection backward kernel lives in project_backward.cu; the
+// standalone SH VJP (primitives/sh.py:82-138) is here.
 #pragma once
 #include "splat_common.cuh"
 #include "tile_modes.cuh"
@@ -368,7 +366,7 @@ __global__ void __launch_bounds__(kProjectBlock) project_forward_kernel(ProjectP
 }
 
 // splatting/metadata.py:12-31 _prepare (standalone stage).
-__global__ void metadata_kernel(int n, const int* __restrict__ radii,
+static __global__ void metadata_kernel(int n, const int* __restrict__ radii,
                                 const float* __restrict__ centers,
                                 const float* __restrict__ conics, float* __restrict__ means2d,
                                 float* __restrict__ opacities, float* __restrict__ conics3) {
@@ -562,292 +560,9 @@ struct ProjectBackwardParams {
   float* grad_sh;             // (n,K,3)
 };
 
-// Normalised quaternion of Gaussian i: given, or recomputed from quats_raw.
-SPLAT_DEV float4 normalized_quat(const ProjectBackwardParams& p, int i) {
-  if (p.quats) return reinterpret_cast<const float4*>(p.quats)[i];
-  return torch_normalize4(reinterpret_cast<const float4*>(p.quats_raw)[i]);
-}
-
-// Hand-derived VJP of gs3d/projection.py:198-210 projection_loss for one
-// visible Gaussian.  Returns grads through the out-parameters; camera
-// partials are added into cv (view, 16) and cp (proj, 16).
-SPLAT_DEV void projection_vjp(const ProjectBackwardParams& p, int i, float m0, float m1, float m2,
-                              float gm[3], float gq[4], float gs[3], float cv[16], float cp[16]) {
-  const float fx = p.K[0], fy = p.K[4];
-  const float* view = p.view;
-  const float* proj = p.proj;
-  const float4 q = normalized_quat(p, i);
-  const float s[3] = {p.scales[3 * i], p.scales[3 * i + 1], p.scales[3 * i + 2]};
-  const float2 sc = reinterpret_cast<const float2*>(p.seed_centers)[i];
-  const float4 sq = reinterpret_cast<const float4*>(p.seed_conics)[i];
-  const float m[3] = {m0, m1, m2};
-  const float t0 = point_row(view, 0, m0, m1, m2);
-  const float t1 = point_row(view, 1, m0, m1, m2);
-  const float tz = point_row(view, 2, m0, m1, m2);
-  const float limx = W32(1.3) * static_cast<float>(p.width) / (2.0f * fx);
-  const float limy = W32(1.3) * static_cast<float>(p.height) / (2.0f * fy);
-  const float xr = t0 / tz, yr = t1 / tz;
-  const float tcx = wclamp(xr, -limx, limx) * tz;
-  const float tcy = wclamp(yr, -limy, limy) * tz;
-  const Mat3 R = glm_rotation(q.x, q.y, q.z, q.w);
-  float M[3][3], Sig[3][3];
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int c = 0; c < 3; ++c) M[r][c] = s[r] * R.m[r][c];
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int c = 0; c < 3; ++c) Sig[r][c] = M[0][r] * M[0][c] + M[1][r] * M[1][c] + M[2][r] * M[2][c];
-  const float J[3][3] = {{fx / tz, 0.0f, 0.0f},
-                         {0.0f, fy / tz, 0.0f},
-                         {-(fx * tcx) / (tz * tz), -(fy * tcy) / (tz * tz), 0.0f}};
-  const float Wc[3][3] = {{view[0], view[4], view[8]}, {view[1], view[5], view[9]},
-                          {view[2], view[6], view[10]}};
-  float Tm[3][3], A[3][3], P[3][3];
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int c = 0; c < 3; ++c) Tm[r][c] = Wc[r][0] * J[0][c] + Wc[r][1] * J[1][c] + Wc[r][2] * J[2][c];
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int c = 0; c < 3; ++c)
-      A[r][c] = Tm[0][r] * Sig[c][0] + Tm[1][r] * Sig[c][1] + Tm[2][r] * Sig[c][2];
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int c = 0; c < 3; ++c) P[r][c] = A[r][0] * Tm[0][c] + A[r][1] * Tm[1][c] + A[r][2] * Tm[2][c];
-  const float a = P[0][0] + W32(0.3), b = P[1][0], c = P[1][1] + W32(0.3);
-  // adj_invert_covariance (splatting/geometry.py:61-71)
-  const float det = a * c - b * b;
-  const float factor = 1.0f / (det * det + W32(0.0000001));
-  const float X = sq.x, Y = sq.y, Z = sq.z;
-  const float da = factor * (-c * c * X + b * c * Y + (det - a * c) * Z);
-  const float db = factor * (2.0f * b * c * X - (det + 2.0f * b * b) * Y + 2.0f * a * b * Z);
-  const float dc = factor * (-a * a * Z + a * b * Y + (det - a * c) * X);
-  const float dP[3][3] = {{da, 0.0f, 0.0f}, {db, dc, 0.0f}, {0.0f, 0.0f, 0.0f}};
-  float dA[3][3], dTm[3][3], dSig[3][3];
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      dA[r][k] = dP[r][0] * Tm[k][0] + dP[r][1] * Tm[k][1] + dP[r][2] * Tm[k][2];
-      dTm[r][k] = A[0][r] * dP[0][k] + A[1][r] * dP[1][k] + A[2][r] * dP[2][k];
-    }
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      dTm[r][k] += Sig[0][r] * dA[k][0] + Sig[1][r] * dA[k][1] + Sig[2][r] * dA[k][2];
-      dSig[r][k] = dA[0][r] * Tm[k][0] + dA[1][r] * Tm[k][1] + dA[2][r] * Tm[k][2];
-    }
-  float dWc[3][3], dJ[3][3];
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-      dWc[r][k] = dTm[r][0] * J[k][0] + dTm[r][1] * J[k][1] + dTm[r][2] * J[k][2];
-      dJ[r][k] = Wc[0][r] * dTm[0][k] + Wc[1][r] * dTm[1][k] + Wc[2][r] * dTm[2][k];
-    }
-  float dR[3][3];
-#pragma unroll
-  for (int r = 0; r < 3; ++r) {
-    float dM[3];
-#pragma unroll
-    for (int k = 0; k < 3; ++k)
-      dM[k] = M[r][0] * (dSig[0][k] + dSig[k][0]) + M[r][1] * (dSig[1][k] + dSig[k][1]) +
-              M[r][2] * (dSig[2][k] + dSig[k][2]);
-    gs[r] = dM[0] * R.m[r][0] + dM[1] * R.m[r][1] + dM[2] * R.m[r][2];
-#pragma unroll
-    for (int k = 0; k < 3; ++k) dR[r][k] = s[r] * dM[k];
-  }
-  // adj_reference_rotation (splatting/math.py:13-28)
-  {
-    const float qr = q.x, qx = q.y, qy = q.z, qz = q.w;
-    gq[0] = 2.0f * (qz * (dR[0][1] - dR[1][0]) + qy * (dR[2][0] - dR[0][2]) + qx * (dR[1][2] - dR[2][1]));
-    gq[1] = 2.0f * (qy * (dR[0][1] + dR[1][0]) + qz * (dR[0][2] + dR[2][0]) + qr * (dR[1][2] - dR[2][1])) -
-            4.0f * qx * (dR[1][1] + dR[2][2]);
-    gq[2] = 2.0f * (qx * (dR[0][1] + dR[1][0]) + qr * (dR[2][0] - dR[0][2]) + qz * (dR[1][2] + dR[2][1])) -
-            4.0f * qy * (dR[0][0] + dR[2][2]);
-    gq[3] = 2.0f * (qr * (dR[0][1] - dR[1][0]) + qx * (dR[0][2] + dR[2][0]) + qy * (dR[1][2] + dR[2][1])) -
-            4.0f * qz * (dR[0][0] + dR[1][1]);
-  }
-  const float tz2 = tz * tz, tz3 = tz2 * tz;
-  const float dtcx = dJ[2][0] * (-fx / tz2);
-  const float dtcy = dJ[2][1] * (-fy / tz2);
-  const float dtcz = dJ[0][0] * (-fx / tz2) + dJ[1][1] * (-fy / tz2) +
-                     dJ[2][0] * (2.0f * fx * tcx / tz3) + dJ[2][1] * (2.0f * fy * tcy / tz3);
-  // adj_clamp_point (splatting/geometry.py:42-51)
-  const float dt[3] = {(xr >= -limx && xr <= limx) ? dtcx : 0.0f,
-                       (yr >= -limy && yr <= limy) ? dtcy : 0.0f, dtcz};
-#pragma unroll
-  for (int j = 0; j < 3; ++j) gm[j] = view[j] * dt[0] + view[4 + j] * dt[1] + view[8 + j] * dt[2];
-#pragma unroll
-  for (int r = 0; r < 3; ++r) {
-#pragma unroll
-    for (int j = 0; j < 3; ++j) cv[r * 4 + j] += dt[r] * m[j];
-    cv[r * 4 + 3] += dt[r];
-  }
-#pragma unroll
-  for (int r = 0; r < 3; ++r)
-#pragma unroll
-    for (int k = 0; k < 3; ++k) cv[k * 4 + r] += dWc[r][k];
-  // pixel_center (splatting/geometry.py:106-123)
-  const float c0 = point_row(proj, 0, m0, m1, m2);
-  const float c1 = point_row(proj, 1, m0, m1, m2);
-  const float c3 = point_row(proj, 3, m0, m1, m2);
-  const float iw = 1.0f / (c3 + W32(1e-7));
-  const float dnx = sc.x * static_cast<float>(p.width) * 0.5f;
-  const float dny = sc.y * static_cast<float>(p.height) * 0.5f;
-  const float dc0 = dnx * iw, dc1 = dny * iw;
-  const float diw = dnx * c0 + dny * c1;
-  const float dc3 = -diw * iw * iw;
-#pragma unroll
-  for (int j = 0; j < 3; ++j) {
-    gm[j] += proj[j] * dc0 + proj[4 + j] * dc1 + proj[12 + j] * dc3;
-    cp[0 + j] += dc0 * m[j];
-    cp[4 + j] += dc1 * m[j];
-    cp[12 + j] += dc3 * m[j];
-  }
-  cp[3] += dc0;
-  cp[7] += dc1;
-  cp[15] += dc3;
-}
-
-template <int DEG, bool CAMERA>
-__global__ void __launch_bounds__(kProjectBlock) project_backward_kernel(ProjectBackwardParams p) {
-  constexpr int kCam = 35;
-  constexpr int S = ShTile<DEG>::kStride;
-  __shared__ float s_sh[kProjectWarps][32 * S];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float* tile = s_sh[warp];
-  float* my_row = tile + lane * S;
-  const bool sh_grads = DEG >= 0 && p.grad_sh != nullptr;
-  float cam[kCam];
-  if (CAMERA) {
-#pragma unroll
-    for (int j = 0; j < kCam; ++j) cam[j] = 0.0f;
-  }
-  // Warp-uniform loop over chunks of 32 Gaussians (the SH rows of a chunk
-  // are staged in shared memory).
-  const int warps = gridDim.x * kProjectWarps;
-  for (int base = (blockIdx.x * kProjectWarps + warp) * 32; base < p.n; base += warps * 32) {
-    if (sh_grads) warp_load_sh<DEG>(p.sh, p.sh_k * 3, base, p.n, tile);
-    const int i = base + lane;
-    if (i < p.n) {
-      float gm[3] = {0.0f, 0.0f, 0.0f}, gq[4] = {0.0f, 0.0f, 0.0f, 0.0f}, gs[3] = {0.0f, 0.0f, 0.0f};
-      float go = 0.0f;
-      const bool visible = p.radii[i] > 0;
-      const float m0 = p.means[3 * i], m1 = p.means[3 * i + 1], m2 = p.means[3 * i + 2];
-      if (visible) {
-        float cv_local[16], cp_local[16];
-        if (CAMERA) {
-          projection_vjp(p, i, m0, m1, m2, gm, gq, gs, cam, cam + 16);
-        } else {
-          projection_vjp(p, i, m0, m1, m2, gm, gq, gs, cv_local, cp_local);
-        }
-        go = p.seed_conics[4 * i + 3];
-        if (p.quats_raw) {
-          // VJP of F.normalize(x) = x / max(|x|, 1e-12) (inputs.py:252):
-          // (g - n (n . g)) / |x|, or g / 1e-12 where the norm is clamped.
-          const float4 x = reinterpret_cast<const float4*>(p.quats_raw)[i];
-          const float norm = sqrtf((x.x * x.x + x.z * x.z) + (x.y * x.y + x.w * x.w));
-          if (norm > W32(1e-12)) {
-            const float4 n = normalized_quat(p, i);
-            const float d = n.x * gq[0] + n.y * gq[1] + n.z * gq[2] + n.w * gq[3];
-            gq[0] = (gq[0] - n.x * d) / norm;
-            gq[1] = (gq[1] - n.y * d) / norm;
-            gq[2] = (gq[2] - n.z * d) / norm;
-            gq[3] = (gq[3] - n.w * d) / norm;
-          } else {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) gq[k] = gq[k] / W32(1e-12);
-          }
-        }
-      }
-      if (sh_grads) {
-        if (visible) {
-          const float* sc = p.seed_colors + static_cast<size_t>(i) * p.color_stride;
-          const float3 cg = make_float3(p.active[3 * i] ? sc[0] : 0.0f,
-                                        p.active[3 * i + 1] ? sc[1] : 0.0f,
-                                        p.active[3 * i + 2] ? sc[2] : 0.0f);
-          float d0 = m0, d1 = m1, d2 = m2;
-          if (p.campos) {
-            d0 = m0 - p.campos[0];
-            d1 = m1 - p.campos[1];
-            d2 = m2 - p.campos[2];
-          }
-          const float3 dd = sh_vjp_row<(DEG < 0 ? 0 : DEG)>(my_row, d0, d1, d2, cg);
-          if (DEG > 0) {
-            gm[0] += dd.x;
-            gm[1] += dd.y;
-            gm[2] += dd.z;
-            if (CAMERA && p.campos) {
-              cam[32] -= dd.x;
-              cam[33] -= dd.y;
-              cam[34] -= dd.z;
-            }
-          }
-        } else {
-          for (int k = 0; k < ShTile<DEG>::kCols; ++k) my_row[k] = 0.0f;
-        }
-      }
-      if (p.accumulate) {
-        if (p.grad_means) {
-          p.grad_means[3 * i] += gm[0];
-          p.grad_means[3 * i + 1] += gm[1];
-          p.grad_means[3 * i + 2] += gm[2];
-        }
-        if (p.grad_quats) {
-          float4* o = reinterpret_cast<float4*>(p.grad_quats) + i;
-          float4 v = *o;
-          v.x += gq[0];
-          v.y += gq[1];
-          v.z += gq[2];
-          v.w += gq[3];
-          *o = v;
-        }
-        if (p.grad_scales) {
-          p.grad_scales[3 * i] += gs[0];
-          p.grad_scales[3 * i + 1] += gs[1];
-          p.grad_scales[3 * i + 2] += gs[2];
-        }
-        if (p.grad_opacities) p.grad_opacities[i] += go;
-      } else {
-        if (p.grad_means) {
-          p.grad_means[3 * i] = gm[0];
-          p.grad_means[3 * i + 1] = gm[1];
-          p.grad_means[3 * i + 2] = gm[2];
-        }
-        if (p.grad_quats) reinterpret_cast<float4*>(p.grad_quats)[i] = make_float4(gq[0], gq[1], gq[2], gq[3]);
-        if (p.grad_scales) {
-          p.grad_scales[3 * i] = gs[0];
-          p.grad_scales[3 * i + 1] = gs[1];
-          p.grad_scales[3 * i + 2] = gs[2];
-        }
-        if (p.grad_opacities) p.grad_opacities[i] = go;
-      }
-    }
-    if (sh_grads) warp_store_sh<DEG>(p.grad_sh, p.sh_k * 3, base, p.n, tile, p.accumulate != 0);
-    __syncwarp();
-  }
-  if (CAMERA) {
-    // Warp shuffles, then warp leaders through shared memory, then one
-    // atomic per entry per block (gs3d/projection.py:269-283).
-    __shared__ float s_cam[kProjectWarps][kCam];
-#pragma unroll
-    for (int j = 0; j < kCam; ++j) {
-      const float v = warp_sum(cam[j]);
-      if (lane == 0) s_cam[warp][j] = v;
-    }
-    __syncthreads();
-    if (threadIdx.x < kCam) {
-      float v = 0.0f;
-      for (int w = 0; w < (blockDim.x >> 5); ++w) v += s_cam[w][threadIdx.x];
-      atomicAdd(p.cam_grads + threadIdx.x, v);
-    }
-  }
-}
+// Projection (+ SH) backward launch (project_backward.cu, compiled with
+// multiply-add contraction: gradients are compared within tolerance, not
+// bit for bit).  Returns a status code.
+int project_backward_dispatch(const ProjectBackwardParams& p, cudaStream_t s);
 
 }  // namespace splat

@@ -13,15 +13,26 @@
 
 #include "binning.cuh"
 #include "cameras.cuh"
+#include "host_runtime.h"
 #include "project.cuh"
 #include "render.cuh"
 #include "splat_common.cuh"
 
 using namespace splat;
+using namespace splat::host;
 
 namespace {
 
 thread_local std::string g_last_error;
+
+// Every kernel launch passes its stream through counted(), so
+// splat_launch_count() reports how many kernels this library has launched.
+unsigned long long g_launches = 0;
+
+}  // namespace
+
+namespace splat {
+namespace host {
 
 int fail(int status, const char* what) {
   g_last_error = what;
@@ -37,25 +48,26 @@ int check_launch(const char* what) {
   return kOk;
 }
 
-inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
-
-// Every kernel launch passes its stream through counted(), so
-// splat_launch_count() reports how many kernels this library has launched.
-unsigned long long g_launches = 0;
-inline cudaStream_t counted(cudaStream_t s) {
+cudaStream_t counted(cudaStream_t s) {
   __atomic_fetch_add(&g_launches, 1ULL, __ATOMIC_RELAXED);
   return s;
 }
-inline unsigned blocks_for(long long n, int block) {
-  return static_cast<unsigned>((n + block - 1) / block);
-}
-inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-// Kernels read float2/float4 rows and issue red.global.add.v2/v4: their
-// addresses must be 8/16-byte aligned (NULL passes; it means "absent").
-inline bool aligned(const void* p, uintptr_t a) {
-  return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
+int sm_count() {
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
 }
+
+}  // namespace host
+}  // namespace splat
+
+namespace {
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
 int tile_passes(int tiles) { return tiles <= 256 ? 1 : (tiles <= 65536 ? 2 : 3); }
 
@@ -199,42 +211,6 @@ int project_forward_dispatch(const ProjectParams& p, cudaStream_t s) {
     }
   }
   return check_launch("project_forward");
-}
-
-template <int DEG, bool CAMERA>
-void launch_project_backward(const ProjectBackwardParams& p, cudaStream_t s) {
-  int sms = 148;
-  int dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  unsigned grid = blocks_for(p.n, kProjectBlock);
-  // With camera gradients each block ends in one atomic per camera entry:
-  // cap the grid (warps then loop over several chunks of 32 Gaussians).
-  if (CAMERA) grid = std::min(grid, static_cast<unsigned>(sms * 16));
-  project_backward_kernel<DEG, CAMERA><<<grid, kProjectBlock, 0, counted(s)>>>(p);
-}
-
-template <bool CAMERA>
-int project_backward_deg(const ProjectBackwardParams& p, cudaStream_t s) {
-  if (p.grad_sh == nullptr) {
-    launch_project_backward<-1, CAMERA>(p, s);
-    return kOk;
-  }
-  switch (p.sh_degree) {
-    case 0: launch_project_backward<0, CAMERA>(p, s); break;
-    case 1: launch_project_backward<1, CAMERA>(p, s); break;
-    case 2: launch_project_backward<2, CAMERA>(p, s); break;
-    case 3: launch_project_backward<3, CAMERA>(p, s); break;
-    default: return fail(kInvalidArgument, "sh_degree must be in [0,3]");
-  }
-  return kOk;
-}
-
-int project_backward_dispatch(const ProjectBackwardParams& p, cudaStream_t s) {
-  if (p.n == 0) return kOk;
-  const int r = p.cam_grads ? project_backward_deg<true>(p, s) : project_backward_deg<false>(p, s);
-  if (r != kOk) return r;
-  return check_launch("project_backward");
 }
 
 template <int CHP>
@@ -718,8 +694,7 @@ int splat_bin_prepare(int n, const float* centers, const float* conics, const in
   const unsigned depth_tiles = blocks_for(n, kDepthThreads * kSortItems);
   const ChunkPlan plan = chunk_plan(n, gx, gy, tile_mode);
   if (plan.use) diff = nullptr;
-  int sms = 148, dev = 0;
-  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int sms = sm_count();
   const unsigned prep_grid = std::min<unsigned>(blocks_for(n, 256), static_cast<unsigned>(sms * 8));
   unsigned long long* total64 = at<unsigned long long>(ws, L.totals + 8);
   bin_prepare_kernel<<<prep_grid, 256, 0, counted(s)>>>(n, centers, conics, radii, tiles, depths,

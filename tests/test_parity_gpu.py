@@ -259,6 +259,109 @@ def test_projection_backward(case):
         assert rel_l2(got.cpu().numpy(), want) <= GRAD_TOL
 
 
+def _offset_copy(t: torch.Tensor, offset: int) -> torch.Tensor:
+    """t copied into a buffer starting `offset` elements past an allocation
+    (offset 1: 4-byte aligned only, which sends the kernel's staging of that
+    input down its plain-copy path)."""
+    flat = torch.zeros(t.numel() + 8, dtype=t.dtype, device=t.device)
+    view = flat[offset:offset + t.numel()].view(t.shape)
+    view.copy_(t)
+    return view
+
+
+FUSED_VARIANTS = [
+    # degree, sh_k, camera grads, accumulate, misaligned inputs, raw quaternions
+    (0, 1, False, False, False, False),
+    (1, 4, True, False, True, False),
+    (1, 16, False, False, False, True),
+    (2, 9, False, True, True, False),
+    (2, 16, True, True, False, True),
+    (3, 16, True, False, False, True),
+    (3, 16, False, True, True, False),
+    (3, 20, False, False, False, False),
+]
+
+
+@pytest.mark.parametrize("deg,sh_k,camera,accumulate,misalign,raw", FUSED_VARIANTS)
+def test_fused_projection_backward_variants(deg, sh_k, camera, accumulate, misalign, raw):
+    """splat_project_backward_fused (projection VJP + SH VJP + normalisation
+    VJP, staged per warp) against the oracle's projection and SH backward,
+    over SH degrees, row strides, camera gradients, accumulation, a ragged
+    last chunk and inputs without 16-byte alignment."""
+    from dsl_splat_b200._native import check, lib, stream
+
+    p = Prepared(_scene("c1_small"))
+    out = p.project()
+    d = _dev()
+    n = len(p.means) - 13  # a partial last chunk of 32
+    rng = np.random.default_rng(deg * 10 + sh_k)
+    radii = out.state.radii[:n].contiguous()
+    sh = torch.zeros((n, sh_k, 3), device=d)
+    used = min(sh_k, 16)
+    sh[:, :used] = p.sh[:n, :used]
+    dirs = p.means[:n] - p.campos
+    _, active = O.sh_forward(sh.cpu().numpy(), dirs.cpu().numpy(), deg, radii.cpu().numpy())
+    seed_c = rng.standard_normal((n, 2)).astype(np.float32)
+    seed_q = (rng.standard_normal((n, 4)) * 1e-2).astype(np.float32)
+    seed_col = rng.standard_normal((n, 3)).astype(np.float32)
+    quats_raw = (p.quats[:n] * torch.from_numpy(
+        rng.uniform(0.5, 2.0, (n, 1)).astype(np.float32)).to(d)).contiguous()
+    quats_n = F.normalize(quats_raw, dim=-1) if raw else p.quats[:n].contiguous()
+
+    off = 1 if misalign else 0
+    means = _offset_copy(p.means[:n], off)
+    scales = _offset_copy(p.scales[:n], off)
+    radii_in = _offset_copy(radii, off)
+    sh_in = _offset_copy(sh, off)
+    active_in = _offset_copy(torch.from_numpy(active).to(d), off)
+    gcol = _offset_copy(torch.from_numpy(seed_col).to(d), off)
+    prefill = {k: torch.from_numpy(rng.standard_normal(shape).astype(np.float32)).to(d)
+               for k, shape in (("m", (n, 3)), ("q", (n, 4)), ("s", (n, 3)), ("o", (n,)),
+                                ("sh", (n, sh_k, 3)))}
+    outs = {k: _offset_copy(v, off if k != "q" else 0) if accumulate
+            else _offset_copy(torch.full_like(v, float("nan")), off if k != "q" else 0)
+            for k, v in prefill.items()}
+    cam = torch.zeros(35, device=d) if camera else None
+    # held in names: a temporary freed inside the argument list would hand its
+    # block to the next allocation
+    seed_c_t, seed_q_t = torch.from_numpy(seed_c).to(d), torch.from_numpy(seed_q).to(d)
+    check(lib.splat_project_backward_fused(
+        n, means.data_ptr(), None if raw else quats_n.data_ptr(),
+        quats_raw.data_ptr() if raw else None, scales.data_ptr(), p.view.data_ptr(),
+        p.full.data_ptr(), p.K.data_ptr(), p.W, p.H, radii_in.data_ptr(),
+        seed_c_t.data_ptr(), seed_q_t.data_ptr(),
+        outs["m"].data_ptr(), outs["q"].data_ptr(), outs["s"].data_ptr(), outs["o"].data_ptr(),
+        int(accumulate), None if cam is None else cam.data_ptr(), deg, sh_k,
+        sh_in.data_ptr(), p.campos.data_ptr(), active_in.data_ptr(), gcol.data_ptr(), 3,
+        outs["sh"].data_ptr(), stream(d)), "project_backward_fused")
+    torch.cuda.synchronize(d)
+
+    r_np = radii.cpu().numpy()
+    gm, gq, gs, go, gv, gp = O.project_backward(
+        p.np["means"][:n], quats_n.cpu().numpy(), p.np["scales"][:n], p.np["opac"][:n],
+        p.np["view"], p.np["full"], p.np["K"], p.W, p.H, r_np, seed_c, seed_q)
+    gsh, gdir = O.sh_backward(sh.cpu().numpy(), dirs.cpu().numpy(), deg, r_np, active, seed_col)
+    if deg > 0:
+        gm = gm + gdir
+    if raw:
+        x = quats_raw.cpu().requires_grad_(True)
+        F.normalize(x, dim=-1).backward(torch.from_numpy(gq))
+        gq = x.grad.numpy()
+    want = {"m": gm, "q": gq, "s": gs, "o": go, "sh": gsh}
+    for k, v in want.items():
+        got = outs[k].cpu().numpy()
+        if accumulate:
+            got = got - prefill[k].cpu().numpy()
+        assert np.isfinite(got).all(), k
+        assert rel_l2(got, v) <= GRAD_TOL, k
+    if camera:
+        c = cam.cpu().numpy().astype(np.float64)
+        assert rel_l2(c[:16].reshape(4, 4), gv) <= GRAD_TOL
+        assert rel_l2(c[16:32].reshape(4, 4), gp) <= GRAD_TOL
+        if deg > 0:
+            assert rel_l2(c[32:35], -gdir.astype(np.float64).sum(0)) <= GRAD_TOL
+
+
 @pytest.mark.parametrize("case", list(CASES))
 def test_sh_standalone(case):
     p = Prepared(_scene(case))
