@@ -47,6 +47,10 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--config", type=int, default=1)
+    ap.add_argument("--buckets", type=int, default=1,
+                    help="N > 1: Gaussian-range buckets of the gradient all-reduce (more "
+                         "than one overlaps it with the projection backward; measured slower "
+                         "on 2 B200s: 762 / 733 / 722 / 668 frames/s for 1 / 2 / 4 / 8)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
@@ -279,14 +283,25 @@ def main():
     W, H = s.width, s.height
     last = {}
 
+    # N > 1: the per-Gaussian gradients go through sharding.GradientSync (one
+    # buffer per parameter, all-reduced in --buckets Gaussian ranges)
+    sync = (sharding.GradientSync(means, quats, scales, opac, sh, group=dist.group.WORLD,
+                                  buckets=args.buckets)
+            if pg is not None else None)
+
     def step():
         for p in params:
             p.grad = None
-        res = gs3d.rasterize(means, quats, scales, opac, viewmats, Ks, W, H, sh_coeffs=sh,
-                             absgrad=True)
-        torch.autograd.backward([res.features, res.alpha], [gF, gA])
-        if pg is not None:
-            sharding.allreduce_parameter_grads(params)
+        if sync is None:
+            res = gs3d.rasterize(means, quats, scales, opac, viewmats, Ks, W, H, sh_coeffs=sh,
+                                 absgrad=True)
+            torch.autograd.backward([res.features, res.alpha], [gF, gA])
+        else:
+            with sync:
+                res = gs3d.rasterize(means, quats, scales, opac, viewmats, Ks, W, H,
+                                     sh_coeffs=sh, absgrad=True)
+                torch.autograd.backward([res.features, res.alpha], [gF, gA])
+            sync.wait()
         last["res"] = res
 
     def barrier():
@@ -351,6 +366,12 @@ def main():
         bufs = [(torch.empty_like(target_host, device=dev), torch.empty_like(view_host, device=dev),
                  torch.empty_like(k_host, device=dev)) for _ in range(2)]
         ready = [torch.cuda.Event() for _ in range(2)]
+        # step k's loss is copied into pinned memory on the compute stream and
+        # read by the host at step k+1 (after the copy's event), as a training
+        # loop logs its loss, so the read does not stall the launch queue
+        loss_host = [torch.empty((), dtype=torch.float32).pin_memory() for _ in range(2)]
+        loss_copied = [torch.cuda.Event() for _ in range(2)]
+        losses = []
 
         def prefetch(k):
             copy_stream.wait_stream(torch.cuda.current_stream(dev))
@@ -366,13 +387,26 @@ def main():
             target, vm, kk = bufs[k % 2]
             if not last:
                 prefetch(k + 1)
-            r = gs3d.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
-                               absgrad=True)
-            loss = (r.features - target).abs().mean()
-            loss.backward()
-            if pg is not None:
-                sharding.allreduce_parameter_grads(params)
-            return float(loss.item())
+            if sync is None:
+                r = gs3d.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
+                                   absgrad=True)
+                loss = (r.features - target).abs().mean()
+                loss.backward()
+            else:
+                with sync:
+                    r = gs3d.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
+                                       absgrad=True)
+                    loss = (r.features - target).abs().mean()
+                    loss.backward()
+                sync.wait()
+            loss_host[k % 2].copy_(loss.detach(), non_blocking=True)
+            loss_copied[k % 2].record()
+            if k > 0:
+                loss_copied[(k - 1) % 2].synchronize()
+                losses.append(float(loss_host[(k - 1) % 2]))
+            if last:
+                loss_copied[k % 2].synchronize()
+                losses.append(float(loss_host[k % 2]))
 
         prefetch(0)
         for k in range(2):
@@ -385,6 +419,7 @@ def main():
             e2e_step(k, k == args.steps - 1)
         e1.record()
         barrier()
+        assert len(losses) == args.steps + 2 and all(math.isfinite(v) for v in losses)
         et = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
         if pg is not None:
             pg.all_reduce(et, op=pg.ReduceOp.MAX)
@@ -393,7 +428,8 @@ def main():
                + k_host.numel() * 4, "d2h_bytes_per_step": 4,
                "path": "gs3d.rasterize + L1 loss + backward; target image, viewmat, K copied "
                        "H2D from pinned memory every step (prefetched one step ahead on a copy "
-                       "stream) and the loss read back every step"}
+                       "stream) and the loss copied D2H into pinned memory every step, read by the "
+                       "host one step later"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -407,7 +443,12 @@ def main():
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded, BASELINE config distributions)",
-                "config": describe(s, world), "roofline": roofline, "cpu_baseline": cpu,
+                "config": dict(describe(s, world), **(
+                    {"gradient_allreduce": f"NCCL, {args.buckets} Gaussian-range bucket(s)"
+                                           + (" overlapped with the projection backward"
+                                              if args.buckets > 1 else "")}
+                    if world > 1 else {})),
+                "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
 

@@ -16,7 +16,7 @@ import torch
 from torch import Tensor
 from torch.autograd.function import once_differentiable
 
-from .. import stages
+from .. import sharding, stages
 from .._native import check, lib, ptr, stream
 from ..camera_prep import ViewConfig
 from ..training import AbsGradientTarget
@@ -43,6 +43,13 @@ class ProjectView(torch.autograd.Function):
             need_active=grad_enabled, normalize_quats=True, tile_mode=config.tile_mode)
         st = out.state
         colors = out.colors if out.colors is not None else means.new_empty((0, 3))
+        sync = sharding.current_sync() if grad_enabled else None
+        if (sync is not None and any(ctx.needs_input_grad[:5])
+                and sync.claims(means, quats_raw, scales, opacities, sh)):
+            sync.register_view()
+        else:
+            sync = None
+        ctx.sync = sync
         if grad_enabled and any(ctx.needs_input_grad[:8]):
             ctx.save_for_backward(means, quats_raw, scales, view, full, intrinsics, st.radii,
                                   None if sh is None else sh.contiguous(),
@@ -59,22 +66,35 @@ class ProjectView(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx: Any, g_centers, g_conics, g_colors, *unused):
-        if g_centers is None and g_conics is None and g_colors is None:
+        # a GradientSync counts every view's backward (the last one reduces),
+        # so a view without upstream gradients still runs, on zeros
+        if g_centers is None and g_conics is None and g_colors is None and ctx.sync is None:
             return (None,) * 12
         means, quats_raw, scales, view, full, intrinsics, radii, sh, campos, active = ctx.saved_tensors
         # inputs: 0 means, 1 quats_raw, 2 scales, 3 opacities, 4 sh, 5 view, 6 full, 7 campos
         needs = ctx.needs_input_grad
         n = len(means)
         cfg = ctx.config
+        sync = ctx.sync
         g_centers = torch.zeros((n, 2), device=means.device) if g_centers is None else g_centers.contiguous()
         g_conics = torch.zeros((n, 4), device=means.device) if g_conics is None else g_conics.contiguous()
-        gm = torch.empty_like(means) if needs[0] else None
-        gq = torch.empty_like(quats_raw) if needs[1] else None
-        gs = torch.empty_like(scales) if needs[2] else None
-        go = means.new_empty(n) if needs[3] else None
-        gsh = None
-        if sh is not None and (needs[4] or (needs[0] and ctx.sh_degree > 0) or needs[7]):
-            gsh = torch.empty_like(sh)
+        if sync is not None:
+            # per-Gaussian gradients accumulate in the sync's buffers
+            buffers, accumulate, last = sync.begin_view()
+            gm, gq, gs, go = (buffers.get(k) for k in ("means", "quats", "scales", "opacities"))
+            gsh = buffers.get("sh")
+            if (gsh is None and sh is not None and ctx.sh_degree > 0
+                    and (gm is not None or needs[7])):
+                gsh = torch.empty_like(sh)  # direction gradient only; values unused
+        else:
+            accumulate, last = False, False
+            gm = torch.empty_like(means) if needs[0] else None
+            gq = torch.empty_like(quats_raw) if needs[1] else None
+            gs = torch.empty_like(scales) if needs[2] else None
+            go = means.new_empty(n) if needs[3] else None
+            gsh = None
+            if sh is not None and (needs[4] or (needs[0] and ctx.sh_degree > 0) or needs[7]):
+                gsh = torch.empty_like(sh)
         want_cam = needs[5] or needs[6] or needs[7]
         cam = means.new_zeros(35) if want_cam else None
         if gsh is not None:
@@ -82,14 +102,33 @@ class ProjectView(torch.autograd.Function):
                     else g_colors.contiguous())
         else:
             gcol = None
-        if n:
+
+        def launch(lo: int, hi: int) -> None:
+            def rows(t):
+                return None if t is None else t[lo:hi]
             pin = stages.Args()
             check(lib.splat_project_backward_fused(
-                n, pin(means), None, pin(quats_raw), pin(scales), pin(view), pin(full),
-                pin(intrinsics), cfg.width, cfg.height, pin(radii), pin(g_centers),
-                pin(g_conics), ptr(gm), ptr(gq), ptr(gs), ptr(go), 0, ptr(cam), ctx.sh_degree,
-                0 if sh is None else sh.shape[1], pin(sh), pin(campos), pin(active), pin(gcol), 3,
-                ptr(gsh), stream(means.device)), "project_backward_fused")
+                hi - lo, pin(rows(means)), None, pin(rows(quats_raw)), pin(rows(scales)),
+                pin(view), pin(full), pin(intrinsics), cfg.width, cfg.height, pin(rows(radii)),
+                pin(rows(g_centers)), pin(rows(g_conics)), ptr(rows(gm)), ptr(rows(gq)),
+                ptr(rows(gs)), ptr(rows(go)), int(accumulate), ptr(cam), ctx.sh_degree,
+                0 if sh is None else sh.shape[1], pin(rows(sh)), pin(campos), pin(rows(active)),
+                pin(rows(gcol)), 3, ptr(rows(gsh)), stream(means.device)),
+                "project_backward_fused")
+
+        if n and sync is not None and last:
+            # bucket b's all-reduce is queued right behind its kernel, so it
+            # runs on NCCL's stream while bucket b+1 computes
+            for lo, hi in sharding.bucket_bounds(n, sync.buckets):
+                launch(lo, hi)
+                sync.reduce_range(lo, hi)
+        elif n:
+            launch(0, n)
+        if sync is not None:
+            if last:
+                sync.finish()
+            gm = gq = gs = go = None
+            gsh = None
         gview = cam[:16].reshape(4, 4) if needs[5] else None
         gfull = cam[16:32].reshape(4, 4) if needs[6] else None
         gcampos = cam[32:35].clone() if needs[7] else None

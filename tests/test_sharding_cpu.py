@@ -120,3 +120,95 @@ def test_rank_that_leaves_is_detected_by_timeout(tmp_path):
     results = _run(2, "leave", tmp_path)
     assert results[1] is None
     assert results[0]["status"].startswith("error")
+
+
+def _contribution(shape, rank, view, step):
+    n = shape[0]
+    base = torch.arange(n, dtype=torch.float32).reshape((n,) + (1,) * (len(shape) - 1))
+    return (base + 1000.0 * rank + 100.0 * view + 10.0 * step).expand(shape).contiguous()
+
+
+SYNC_SHAPES = [(101, 3), (101, 4), (101, 3), (101,), (101, 16, 3)]
+
+
+def _sync_worker(rank, world, port, outdir):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    from dsl_splat_b200 import sharding
+    sharding.init_process_group("gloo", timeout_s=30.0)
+    params = [torch.zeros(s, requires_grad=True) for s in SYNC_SHAPES]
+    sync = sharding.GradientSync(*params, group=dist.group.WORLD, buckets=3)
+    flags = []
+    for step in range(2):  # the second step accumulates into the first's p.grad
+        with sync:
+            for _ in range(2):
+                sync.register_view()
+            for view in range(2):
+                bufs, accumulate, last = sync.begin_view()
+                flags.append((accumulate, last))
+                for (name, buf), shape in zip(bufs.items(), SYNC_SHAPES):
+                    g = _contribution(shape, rank, view, step)
+                    if accumulate:
+                        buf.add_(g)
+                    else:
+                        buf.copy_(g)
+                if last:
+                    for lo, hi in sharding.bucket_bounds(SYNC_SHAPES[0][0], sync.buckets):
+                        sync.reduce_range(lo, hi)
+                    sync.finish()
+        sync.wait()
+    torch.save({"grads": [p.grad.clone() for p in params], "flags": flags},
+               os.path.join(outdir, f"rank{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_gradient_sync_buckets_equal_full_sum(tmp_path):
+    """GradientSync with gloo ranks: per-view accumulation, the last view's
+    bucketed all-reduce, and p.grad accumulation across steps give the sum of
+    every rank's and view's gradients."""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_sync_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish")
+    for r in range(2):
+        res = torch.load(os.path.join(tmp_path, f"rank{r}.pt"))
+        # each step: view 0 overwrites the step's buffers, view 1 accumulates
+        # and reduces; step 1's reduced sum is added to step 0's p.grad
+        assert res["flags"] == [(False, False), (True, True), (False, False), (True, True)]
+        for got, shape in zip(res["grads"], SYNC_SHAPES):
+            want = sum(_contribution(shape, rank, view, step)
+                       for rank in range(2) for view in range(2) for step in range(2))
+            assert torch.equal(got, want)
+
+
+def test_bucket_bounds_and_incomplete_backward():
+    from dsl_splat_b200.sharding import GradientSync, bucket_bounds
+    for n in (0, 1, 31, 32, 33, 1000, 1_000_000):
+        for b in (1, 3, 4, 7):
+            ranges = bucket_bounds(n, b)
+            assert len(ranges) <= b
+            if not n:
+                assert ranges == []
+                continue
+            assert [lo for lo, _ in ranges] == [0] + [hi for _, hi in ranges[:-1]]
+            assert ranges[-1][1] == n and all(lo < hi for lo, hi in ranges)
+            assert all(lo % 32 == 0 for lo, _ in ranges)
+    params = [torch.zeros(s, requires_grad=True) for s in SYNC_SHAPES]
+    sync = GradientSync(*params)
+    with sync:
+        sync.register_view()
+        sync.register_view()
+        sync.begin_view()  # the second view's backward never runs
+    with pytest.raises(RuntimeError, match="1 of 2"):
+        sync.wait()
+    with sync:
+        with pytest.raises(RuntimeError, match="nest"):
+            with GradientSync(*params):
+                pass
