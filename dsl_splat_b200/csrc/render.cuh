@@ -578,9 +578,10 @@ SPLAT_DEV void accumulate_sample(float (&val)[NV], float4 q, const float (&f)[CH
   val[7] += fabsf(g1);
 }
 
-// Reverse replay with PX pixels per lane (kBlock / PX threads per tile).
-// Four channels (RGB + the constant alpha channel) reduce 12 values with
-// butterfly12; wider layouts reduce groups of 16 with butterfly16.
+// Reverse replay with PX pixels per lane (kBlock / PX threads per tile),
+// launched with PX = 1 for views of more than four channels, which reduce
+// groups of 16 values with butterfly16 (four-channel views use
+// render_backward2_kernel).
 template <int CHP, int PX>
 __global__ void __launch_bounds__(kBlock / PX) render_backward_kernel(RenderParams p) {
   constexpr int kThreads = kBlock / PX;
@@ -685,29 +686,7 @@ __global__ void __launch_bounds__(kBlock / PX) render_backward_kernel(RenderPara
       float dy[PX], G[PX], alpha[PX];
       bool accept[PX];
       bool any = false;
-      if constexpr (PX == 2) {  // exp and alpha of both pixels as f32x2 pairs
-        const float dy0 = gm.y - fy[0], dy1 = gm.y - fy[1];
-        const float pw0 = sample_power(q, dx, dy0), pw1 = sample_power(q, dx, dy1);
-        const f32x2 g2 = splat_expf_core2(pack2(pw0, pw1));
-        float g0, g1, a0, a1;
-        unpack2(g2, g0, g1);
-        unpack2(mul2(splat2(q.w), g2), a0, a1);
-        a0 = wmin(W32(0.99), a0);
-        a1 = wmin(W32(0.99), a1);
-        const bool acc0 = inside[0] && position < last_contributor[0] && pw0 <= 0.0f &&
-                          pw0 >= cut && a0 >= threshold;
-        const bool acc1 = inside[1] && position < last_contributor[1] && pw1 <= 0.0f &&
-                          pw1 >= cut && a1 >= threshold;
-        dy[0] = dy0;
-        dy[1] = dy1;
-        G[0] = g0;
-        G[1] = g1;
-        alpha[0] = a0;
-        alpha[1] = a1;
-        accept[0] = acc0;
-        accept[1] = acc1;
-        any = acc0 || acc1;
-      } else {
+      {
 #pragma unroll
         for (int i = 0; i < PX; ++i) {
           dy[i] = gm.y - fy[i];
@@ -747,6 +726,183 @@ __global__ void __launch_bounds__(kBlock / PX) render_backward_kernel(RenderPara
           if (d.base) red_add(d.base + g * d.stride, total);
         }
       }
+    }
+  }
+}
+
+// Gradient contributions of one staged Gaussian to both pixels of a lane,
+// as f32x2 pairs (low half: the lane's first pixel, high half: its second),
+// summed over the two pixels into the 12 reduction values.  Per pixel the
+// replay carries S = sum_c acc_c dL/dC_c instead of the blended colour acc
+// behind the sample: dL/dalpha needs only sum_c (colour_c - acc_c) dL/dC_c
+// = F - S with F = sum_c colour_c dL/dC_c, and acc += alpha (colour - acc)
+// becomes S += alpha (F - S).  A pixel that does not take the sample enters
+// with alpha = G = 0: rcp(1 - 0) = 1 and alpha (F - S) = 0 leave its T and
+// S unchanged, and every contribution is an exact zero (all operands are
+// finite).  feature_grads: channels whose gradient is written (the rest
+// stay zero).
+SPLAT_DEV void accumulate_pair(float (&val)[12], float4 q, const float (&f)[4], f32x2 G2,
+                               f32x2 alpha2, float dx, f32x2 dy2, f32x2& T2, f32x2 bg2,
+                               const f32x2 (&grad2)[4], f32x2& S2, int feature_grads) {
+  float a0, a1;
+  unpack2(alpha2, a0, a1);
+  const f32x2 inv2 = pack2(rcp_approx(1.0f - a0), rcp_approx(1.0f - a1));
+  T2 = mul2(T2, inv2);
+  f32x2 F2 = mul2(splat2(f[0]), grad2[0]);
+#pragma unroll
+  for (int c = 1; c < 4; ++c) F2 = fma2(splat2(f[c]), grad2[c], F2);
+  const f32x2 d2 = sub2(F2, S2);
+  S2 = fma2(alpha2, d2, S2);
+  const f32x2 w2 = mul2(alpha2, T2);
+  float lo, hi;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    if (c < 3 || feature_grads > 3) {
+      unpack2(mul2(w2, grad2[c]), lo, hi);
+      val[8 + c] = lo + hi;
+    } else {
+      val[8 + c] = 0.0f;
+    }
+  }
+  const f32x2 ga2 = fma2(d2, T2, mul2(bg2, inv2));    // dL/dalpha
+  const f32x2 ngv2 = mul2(splat2(-q.w), ga2);         // -dL/dpower
+  const f32x2 hgv2 = mul2(splat2(-0.5f * q.w), ga2);  // -0.5 dL/dpower
+  const f32x2 gdx2 = mul2(G2, splat2(dx)), gdy2 = mul2(G2, dy2);
+  const f32x2 g0 = mul2(ngv2, fma2(gdy2, splat2(q.y), mul2(gdx2, splat2(q.x))));
+  const f32x2 g1 = mul2(ngv2, fma2(gdx2, splat2(q.y), mul2(gdy2, splat2(q.z))));
+  float g0a, g0b, g1a, g1b;
+  unpack2(g0, g0a, g0b);
+  unpack2(g1, g1a, g1b);
+  val[0] = g0a + g0b;
+  val[1] = g1a + g1b;
+  val[6] = fabsf(g0a) + fabsf(g0b);
+  val[7] = fabsf(g1a) + fabsf(g1b);
+  unpack2(mul2(mul2(gdx2, splat2(dx)), hgv2), lo, hi);
+  val[2] = lo + hi;
+  unpack2(mul2(mul2(gdx2, dy2), ngv2), lo, hi);
+  val[3] = lo + hi;
+  unpack2(mul2(mul2(gdy2, dy2), hgv2), lo, hi);
+  val[4] = lo + hi;
+  unpack2(mul2(G2, ga2), lo, hi);
+  val[5] = lo + hi;
+}
+
+// Reverse replay for four channels with two pixels per lane, the per-pixel
+// state and the gradient arithmetic held as f32x2 pairs (accumulate_pair).
+// Acceptance decisions use the forward's exact sample exponent, so the
+// replay visits the same samples the forward blended.
+__global__ void __launch_bounds__(kBlock / 2) render_backward2_kernel(RenderParams p) {
+  constexpr int CHP = 4;
+  constexpr int kThreads = kBlock / 2;
+  extern __shared__ float4 s_dynamic[];  // the staged batch (sizeof(RenderShared<4>) bytes)
+  RenderShared<CHP>& s = *reinterpret_cast<RenderShared<CHP>*>(s_dynamic);
+  __shared__ uint8_t s_list[kThreads / 32][kBlock];
+  __shared__ int s_max_last;
+  // destination of the value that lane l holds after butterfly12 (the same
+  // for every warp); null for odd lanes and unused values
+  __shared__ GradientSlot s_dst[32];
+  uint8_t* list = s_list[threadIdx.x >> 5];
+  const int tile = blockIdx.x;
+  const int wl = threadIdx.x & 31;
+  const PixelSlot<2> ps = pixel_slot<2>(tile, p.gx);
+  const int first = max(p.ranges[2 * tile], 0);
+  const int last = min(p.ranges[2 * tile + 1], p.num_ids);
+  const float threshold = 1.0f / 255.0f;
+  const float fx = static_cast<float>(ps.x);
+  // per pixel: T in front of the current sample, S = sum_c acc_c dL/dC_c
+  // over the blended colour acc of the accepted samples behind it, and
+  // bg = -T_final * sum_c background_c dL/dC_c
+  float fy[2], T[2], bg[2], grad[2][CHP];
+  int last_contributor[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int y = ps.y + 4 * i;
+    fy[i] = static_cast<float>(y);
+    T[i] = 0.0f;
+    bg[i] = 0.0f;
+    last_contributor[i] = 0;  // 0 outside the image: no position passes
+#pragma unroll
+    for (int c = 0; c < CHP; ++c) grad[i][c] = 0.0f;
+    if (ps.x < p.width && y < p.height) {
+      const int pixel = y * p.width + ps.x;
+      const float final_T = p.final_t[pixel];
+      T[i] = final_T;
+      last_contributor[i] = p.contributors[pixel];
+      const float* up = p.upstream ? p.upstream + static_cast<size_t>(pixel) * p.up_pix_stride
+                                   : nullptr;
+      float bg_grad = 0.0f;
+#pragma unroll
+      for (int c = 0; c < CHP; ++c)
+        if (c < p.channels) {
+          // the appended channel's upstream may live in its own buffer
+          const float* src = (p.upstream_alpha && c == p.channels - 1)
+                                 ? p.upstream_alpha + static_cast<size_t>(pixel) * p.alpha_pix_stride
+                                 : (up ? up + c * p.up_ch_stride : nullptr);
+          const float g = src ? __ldg(src) : 0.0f;
+          grad[i][c] = g;
+          bg_grad += p.background[c] * g;
+        }
+      bg[i] = -final_T * bg_grad;
+    }
+  }
+  f32x2 T2 = pack2(T[0], T[1]), bg2 = pack2(bg[0], bg[1]), S2 = splat2(0.0f);
+  f32x2 grad2[CHP];
+#pragma unroll
+  for (int c = 0; c < CHP; ++c) grad2[c] = pack2(grad[0][c], grad[1][c]);
+  const int feature_grads = p.channels - p.constant_tail;
+  const int lane_last = max(last_contributor[0], last_contributor[1]);
+  if (threadIdx.x == 0) s_max_last = 0;
+  if (threadIdx.x < 32) {
+    GradientSlot d = gradient_slot(p, butterfly12_index(wl), p.channels - p.constant_tail);
+    if ((wl & 1) || butterfly12_index(wl) >= 8 + CHP) d.base = nullptr;
+    s_dst[wl] = d;
+  }
+  __syncthreads();
+  const int warp_last = __reduce_max_sync(0xffffffffu, lane_last);
+  if (wl == 0 && warp_last > 0) atomicMax(&s_max_last, warp_last);
+  __syncthreads();
+  const int stop = min(first + s_max_last, last);  // later positions contribute nowhere
+  for (int end = stop; end > first; end -= kBlock) {
+    __syncthreads();
+    for (int slot = threadIdx.x; slot < kBlock; slot += kThreads) {
+      const int idx = end - 1 - slot;
+      if (idx >= first) stage_gaussian<CHP>(p, s, slot, p.ids[idx]);
+    }
+    __syncthreads();
+    const int count = min(kBlock, end - first);
+    // only positions below warp_last (position = end - 1 - j - first) can
+    // contribute to this warp's pixels
+    const int candidates =
+        warp_candidates(s, ps, max(0, end - first - warp_last), count, list);
+    for (int k = 0; k < candidates; ++k) {
+      const int j = list[k];
+      const float4 gm = s.geom[j];
+      const int position = end - 1 - j - first;  // contributor index - 1
+      const float4 q = s.conic[j];
+      const float cut = s.cut[j];
+      const float dx = gm.x - fx;
+      const float dy0 = gm.y - fy[0], dy1 = gm.y - fy[1];
+      const float pw0 = sample_power(q, dx, dy0), pw1 = sample_power(q, dx, dy1);
+      const f32x2 e2 = splat_expf_core2(pack2(pw0, pw1));
+      float g0, g1, a0, a1;
+      unpack2(e2, g0, g1);
+      unpack2(mul2(splat2(q.w), e2), a0, a1);
+      a0 = wmin(W32(0.99), a0);
+      a1 = wmin(W32(0.99), a1);
+      const bool acc0 = position < last_contributor[0] && pw0 <= 0.0f && pw0 >= cut &&
+                        a0 >= threshold;
+      const bool acc1 = position < last_contributor[1] && pw1 <= 0.0f && pw1 >= cut &&
+                        a1 >= threshold;
+      if (!__any_sync(0xffffffffu, acc0 || acc1)) continue;
+      float f[CHP];
+      load_features(s, j, f);
+      float val[12];
+      accumulate_pair(val, q, f, pack2(acc0 ? g0 : 0.0f, acc1 ? g1 : 0.0f),
+                      pack2(acc0 ? a0 : 0.0f, acc1 ? a1 : 0.0f), dx, pack2(dy0, dy1), T2, bg2,
+                      grad2, S2, feature_grads);
+      const float total = butterfly12(val, wl);
+      const GradientSlot d = s_dst[wl];
+      if (d.base) red_add(d.base + static_cast<size_t>(s.id[j]) * d.stride, total);
     }
   }
 }

@@ -220,12 +220,15 @@ void launch_render(const RenderParams& p, bool backward, cudaStream_t s) {
   // needs more than the default 48 KB (opt-in, per device, cheap to repeat).
   const size_t smem = sizeof(RenderShared<CHP>);
   if (backward) {
-    // four channels: two pixels per lane (128 threads per tile)
-    constexpr int px = CHP == 4 ? 2 : 1;
-    if (smem > 32 * 1024)
-      cudaFuncSetAttribute(render_backward_kernel<CHP, px>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    render_backward_kernel<CHP, px><<<tiles, kBlock / px, smem, counted(s)>>>(p);
+    if constexpr (CHP == 4) {
+      // four channels: two pixels per lane as f32x2 pairs (128 threads per tile)
+      render_backward2_kernel<<<tiles, kBlock / 2, smem, counted(s)>>>(p);
+    } else {
+      if (smem > 32 * 1024)
+        cudaFuncSetAttribute(render_backward_kernel<CHP, 1>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      render_backward_kernel<CHP, 1><<<tiles, kBlock, smem, counted(s)>>>(p);
+    }
   } else if (CHP <= 8) {
     // up to eight channels: two pixels per lane with paired arithmetic
     if (smem > 32 * 1024)
