@@ -36,6 +36,14 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "fwd+bwd frames/s, 3DGS SH3 1M Gaussians @1080p"
+# other configs (parity cases, or --config 2 for the batched multi-view scene)
+# report the same unit under their own name
+CONFIG_METRICS = {2: "fwd+bwd frames/s (camera views), 3DGS SH3 3M Gaussians, 8 cameras "
+                     "1296x840"}
+
+
+def metric_for(config: int) -> str:
+    return CONFIG_METRICS.get(config, METRIC)
 UNIT = "frames/s"
 CHANNELS = 4  # RGB + the appended alpha column (gs3d/autograd.py:306-311)
 
@@ -66,21 +74,34 @@ def dist_env():
 
 
 def workload(config: int, rank: int, world: int):
-    """The config scene; rank r looks from an orbit angle 2*pi*r/world."""
+    """The config scene.  Single-view configs: rank r looks from an orbit
+    angle 2*pi*r/world (one view per rank).  Multi-view configs (config 2's
+    8-camera batch): rank r renders the cameras k with k mod world == r."""
     from dsl_splat_b200.scenes import look_at, make_scene
+    from dsl_splat_b200.sharding import local_cameras
     s = make_scene(config)
-    if world > 1 and rank > 0:
+    cams = s.viewmats.shape[0]
+    if cams > 1:
+        idx = local_cameras(cams, rank, world)
+        if not idx:
+            raise SystemExit(f"config {config} has {cams} cameras: at most {cams} ranks")
+        for name in ("viewmats", "Ks", "target", "grad_image", "grad_alpha"):
+            setattr(s, name, getattr(s, name)[idx].contiguous())
+        s.meta["cameras"] = cams
+    elif world > 1 and rank > 0:
         th = 2.0 * math.pi * rank / world
         s.viewmats[0] = look_at(torch.tensor([8.0 * math.sin(th), 0.0, -8.0 * math.cos(th)]))
     return s
 
 
 def describe(s, world):
+    views = s.viewmats.shape[0]
+    total = s.meta.get("cameras", world)
     return {
         "workload": f"config{s.meta['config']}: gs3d.rasterize SH{s.sh_degree} "
                     f"{s.means.shape[0]} Gaussians {s.width}x{s.height}, fwd+bwd, absgrad",
         "n_gaussians": int(s.means.shape[0]), "width": s.width, "height": s.height,
-        "sh_degree": s.sh_degree, "views_per_gpu": 1, "global_batch": world,
+        "sh_degree": s.sh_degree, "views_per_gpu": views, "global_batch": total,
         "parallelism": f"camera-sharded dp{world}",
         "l2": "inputs larger than L2 (236 MB of Gaussian parameters+grads per step); no flush",
     }
@@ -208,7 +229,7 @@ def run_reference(args, rank, world):
     sample = (f"oracle (C++ restatement of dsl_splat gs3d; the Warp reference needs warp-lang, "
               f"absent) with {threads} OpenMP threads, image rows 0-{rows} of {s.height} "
               f"({frac:.3f} frame) per step; value = frame fraction / time")
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+    line = {"metric": metric_for(args.config), "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, BASELINE config distributions)", "impl": "reference",
@@ -283,11 +304,15 @@ def main():
     W, H = s.width, s.height
     last = {}
 
-    # N > 1: the per-Gaussian gradients go through sharding.GradientSync (one
-    # buffer per parameter, all-reduced in --buckets Gaussian ranges)
-    sync = (sharding.GradientSync(means, quats, scales, opac, sh, group=dist.group.WORLD,
+    # N > 1 or several views per rank: the per-Gaussian gradients go through
+    # sharding.GradientSync (one buffer per parameter that every local view
+    # accumulates into, all-reduced in --buckets Gaussian ranges when N > 1)
+    views = int(viewmats.shape[0])
+    frames_per_step = int(s.meta.get("cameras", world))
+    sync = (sharding.GradientSync(means, quats, scales, opac, sh,
+                                  group=dist.group.WORLD if pg is not None else None,
                                   buckets=args.buckets)
-            if pg is not None else None)
+            if pg is not None or views > 1 else None)
 
     def step():
         for p in params:
@@ -328,13 +353,13 @@ def main():
     if pg is not None:
         pg.all_reduce(elapsed, op=pg.ReduceOp.MAX)
     ms = float(elapsed.item())
-    value = world * args.steps / (ms / 1000.0)
+    value = frames_per_step * args.steps / (ms / 1000.0)
 
     # live roofline of the dominant kernel over the timed region
     res = last["res"]
     radii = res.meta["radii"][..., 0]
-    nv = int((radii > 0).sum())
-    m = int(res.meta["tiles_per_gauss"].sum())
+    nv = int((radii > 0).sum()) // views  # per view (one launch of each kernel)
+    m = int(res.meta["tiles_per_gauss"].sum()) // views
     n = int(means.shape[0])
     durations = {k: statistics.mean(a.elapsed_time(b) for a, b in v) for k, v in timers.items()}
     kernel = max(durations, key=durations.get)
@@ -356,7 +381,7 @@ def main():
     # end to end through the public API with host buffers each step
     e2e = None
     if not args.no_e2e:
-        target_host = s.target[0:1].contiguous().pin_memory()
+        target_host = s.target.contiguous().pin_memory()
         view_host = s.viewmats.contiguous().pin_memory()
         k_host = s.Ks.contiguous().pin_memory()
         # step k's inputs are copied from pinned memory on a copy stream while
@@ -423,7 +448,7 @@ def main():
         et = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
         if pg is not None:
             pg.all_reduce(et, op=pg.ReduceOp.MAX)
-        e2e = {"value": world * args.steps / (float(et.item()) / 1000.0), "unit": UNIT,
+        e2e = {"value": frames_per_step * args.steps / (float(et.item()) / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": target_host.numel() * 4 + view_host.numel() * 4
                + k_host.numel() * 4, "d2h_bytes_per_step": 4,
                "path": "gs3d.rasterize + L1 loss + backward; target image, viewmat, K copied "
@@ -439,7 +464,8 @@ def main():
         pg.barrier()
         pg.destroy_process_group()
     if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        line = {"metric": metric_for(args.config), "value": value, "unit": UNIT,
+                "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded, BASELINE config distributions)",

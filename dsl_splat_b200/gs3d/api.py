@@ -167,6 +167,7 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
         main, alpha = RenderView.apply(ctr, con, colors, extras, screen, packed_bg,
                                        bins[i]["ranges"], bins[i]["point_list"], config,
                                        training.absolute_targets[i],
+                                       training.screen_targets[i],
                                        prepared_stats[i] if statistics else None, grad_enabled)
         blended.append(main)
         alphas.append(alpha)

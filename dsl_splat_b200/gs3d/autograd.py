@@ -19,7 +19,7 @@ from torch.autograd.function import once_differentiable
 from .. import sharding, stages
 from .._native import check, lib, ptr, stream
 from ..camera_prep import ViewConfig
-from ..training import AbsGradientTarget
+from ..training import AbsGradientTarget, ScreenGradientTarget
 
 
 class ProjectView(torch.autograd.Function):
@@ -146,8 +146,8 @@ class RenderView(torch.autograd.Function):
     @staticmethod
     def forward(ctx: Any, centers: Tensor, conics: Tensor, colors: Tensor, extras: Tensor | None,
                 screen: Tensor | None, background: Tensor, ranges: Tensor, ids: Tensor,
-                config: ViewConfig, absolute: AbsGradientTarget | None, statistics,
-                grad_enabled: bool):
+                config: ViewConfig, absolute: AbsGradientTarget | None,
+                screen_target: ScreenGradientTarget | None, statistics, grad_enabled: bool):
         state = stages.ProjectedFootprint(centers, conics)
         bins = dict(ranges=ranges, point_list=ids)
         out = stages.render(state, bins, colors, extras, True, background, config.width,
@@ -155,7 +155,7 @@ class RenderView(torch.autograd.Function):
         if grad_enabled and any(ctx.needs_input_grad[:5]):
             ctx.save_for_backward(centers, conics, colors, extras, background, ranges, ids,
                                   out.transmittance, out.contributors)
-            ctx.config, ctx.absolute = config, absolute
+            ctx.config, ctx.absolute, ctx.screen_target = config, absolute, screen_target
         ctx.set_materialize_grads(False)
         return out.features, out.alpha
 
@@ -163,7 +163,7 @@ class RenderView(torch.autograd.Function):
     @once_differentiable
     def backward(ctx: Any, g_features: Tensor | None, g_alpha: Tensor | None):
         if g_features is None and g_alpha is None:
-            return (None,) * 12
+            return (None,) * 13
         centers, conics, colors, extras, background, ranges, ids, final_t, contrib = ctx.saved_tensors
         cfg = ctx.config
         needs = ctx.needs_input_grad
@@ -176,5 +176,11 @@ class RenderView(torch.autograd.Function):
             absolute_out=direct)
         if ctx.absolute is not None and direct is None:
             ctx.absolute.write(absolute)
-        return (gc if needs[0] else None, gq if needs[1] else None, ga, gb,
-                gc if needs[4] else None, None, None, None, None, None, None, None)
+        g_screen = None
+        if needs[4]:
+            if ctx.screen_target is not None:
+                ctx.screen_target.add(gc)  # straight into means2d.grad (see training.py)
+            else:
+                g_screen = gc
+        return (gc if needs[0] else None, gq if needs[1] else None, ga, gb, g_screen, None, None,
+                None, None, None, None, None, None)

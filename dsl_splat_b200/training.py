@@ -40,10 +40,39 @@ class AbsGradientTarget:
 
 
 @dataclass(slots=True)
+class ScreenGradientTarget:
+    """Where one view's dL/dmeans2d lands in the means2d leaf's gradient.
+
+    The reference routes it through autograd: each view's means2d is a
+    select (dense) or an index_put + select (packed) of the leaf, whose
+    backward materialises a zero-filled gradient of the whole (views, N, 2)
+    leaf per view and then sums them -- O(views^2 N) work.  Here the render
+    backward adds its centre gradient straight into the view's rows of
+    leaf.grad (created zero-filled on first use): the view's (N, 2) block
+    (dense), or its visible rows gathered by gaussian_ids (packed)."""
+
+    leaf: Tensor
+    index: int = 0                      # dense: view index into (views, N, 2)
+    gaussian_ids: Tensor | None = None  # packed: this view's Gaussians, rows [begin, end)
+    begin: int = 0
+    end: int = 0
+
+    @torch.no_grad()
+    def add(self, gradient: Tensor) -> None:
+        if self.leaf.grad is None:
+            self.leaf.grad = torch.zeros_like(self.leaf)
+        if self.gaussian_ids is None:
+            self.leaf.grad.view(-1, *gradient.shape)[self.index].add_(gradient)
+        else:
+            self.leaf.grad[self.begin:self.end].add_(gradient[self.gaussian_ids])
+
+
+@dataclass(slots=True)
 class TrainingMetadata:
     values: dict[str, Any]
     screen: Tensor | None
     absolute_targets: list[AbsGradientTarget | None]
+    screen_targets: list[ScreenGradientTarget | None]
 
 
 def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packed: bool,
@@ -70,9 +99,25 @@ def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packe
     values.update(batch_ids=batch_ids, camera_ids=camera_ids, gaussian_ids=gaussian_ids)
     screen = values["means2d"].detach().requires_grad_(layout.requires_screen_grad)
     values["means2d"] = screen
-    targets: list[AbsGradientTarget | None] = [None] * (layout.batch_count * layout.cameras)
+    views = layout.batch_count * layout.cameras
+    targets: list[AbsGradientTarget | None] = [None] * views
     if not layout.requires_screen_grad:
-        return TrainingMetadata(values, None, targets)
+        return TrainingMetadata(values, None, targets, [None] * views)
+    counts: list[int] | None = None
+    if packed:
+        if visible_counts is not None:
+            counts = list(visible_counts)
+        else:
+            counts = ([len(screen)] if views == 1
+                      else (dense["radii"] > 0).all(-1).sum(-1).flatten().tolist())
+        screen_targets, begin = [], 0
+        for count in counts:
+            screen_targets.append(ScreenGradientTarget(
+                screen, gaussian_ids=gaussian_ids[begin:begin + count], begin=begin,
+                end=begin + count))
+            begin += count
+    else:
+        screen_targets = [ScreenGradientTarget(screen, index=i) for i in range(views)]
     if packed:
         dense_screen = torch.zeros_like(dense["means2d"]).index_put(
             (batch_ids, camera_ids, gaussian_ids), screen)
@@ -82,11 +127,6 @@ def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packe
         absolute = torch.zeros_like(screen)
         setattr(screen, "absgrad", absolute)
         if packed:
-            if visible_counts is not None:
-                counts = list(visible_counts)
-            else:
-                counts = ([len(screen)] if len(targets) == 1
-                          else (dense["radii"] > 0).all(-1).sum(-1).flatten().tolist())
             begin = 0
             for i, count in enumerate(counts):
                 end = begin + count
@@ -95,4 +135,4 @@ def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packe
         else:
             views = absolute.reshape(layout.batch_count * layout.cameras, layout.n, 2)
             targets = [AbsGradientTarget(v) for v in views]
-    return TrainingMetadata(values, dense_screen, targets)
+    return TrainingMetadata(values, dense_screen, targets, screen_targets)

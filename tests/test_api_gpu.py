@@ -240,3 +240,33 @@ def test_single_host_synchronisation_per_call():
             mask = (dense.radii > 0).all(-1)
             assert torch.equal(res.meta["radii"], dense.radii[mask])
             assert torch.equal(res.meta["means2d"].detach(), dense.means2d.detach()[mask])
+
+
+def test_means2d_gradient_targets_multi_view():
+    """means2d.grad (written by the render backward straight into the leaf's
+    gradient, dense or packed) equals autograd's per-view routing: the packed
+    leaf's rows are the dense gradient at (camera_ids, gaussian_ids), and a
+    second backward through the same graph accumulates."""
+    scene = make_scene(2, n=20000, width=324, height=210, cameras=3)
+    d = torch.device("cuda", 0)
+    args = [t.to(d) for t in (scene.means, scene.quats, scene.scales, scene.opacities)]
+    args[0].requires_grad_(True)
+    views, Ks = scene.viewmats.to(d), scene.Ks.to(d)
+    sh = scene.sh_coeffs.to(d)
+    up = scene.grad_image.to(d)
+    dense = gs3d.rasterize(*args, views, Ks, scene.width, scene.height, sh_coeffs=sh,
+                           absgrad=True)
+    dense.features.backward(up, retain_graph=True)
+    g_dense = dense.means2d.grad.clone()
+    assert g_dense.shape == (3, 20000, 2) and g_dense.abs().sum() > 0
+    packed = gs3d.rasterize(*args, views, Ks, scene.width, scene.height, sh_coeffs=sh,
+                            absgrad=True, packed=True)
+    packed.features.backward(up)
+    meta = packed.meta
+    # two backward passes differ only in the order of their atomic additions
+    want = g_dense[meta["camera_ids"], meta["gaussian_ids"]]
+    assert rel_l2(meta["means2d"].grad.cpu(), want.cpu()) <= 1e-5
+    assert rel_l2(meta["means2d"].absgrad.cpu(),
+                  dense.means2d.absgrad[meta["camera_ids"], meta["gaussian_ids"]].cpu()) <= 1e-5
+    dense.features.backward(up)
+    assert rel_l2(dense.means2d.grad.cpu(), 2 * g_dense.cpu()) <= 1e-5
