@@ -34,12 +34,18 @@ SIGNATURES: dict[str, tuple] = {
     "splat_project_forward_fused": (_I, [_I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,
                                          _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I, _P,
                                          _P, _P, _P, _I, _P]),
+    "splat_project_forward_views": (_I, [_I, _I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _F,
+                                         _F, _F, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _I,
+                                         _P, _P, _P, _P, _I, _P]),
     "splat_metadata": (_I, [_I, _P, _P, _P, _P, _P, _P, _P]),
     "splat_project_backward": (_I, [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P, _P,
                                     _P, _P, _P, _P]),
     "splat_project_backward_fused": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P,
                                           _P, _P, _P, _P, _I, _P, _I, _I, _P, _P, _P, _P,
                                           _I, _P, _P]),
+    "splat_project_backward_views": (_I, [_I, _I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P,
+                                          _P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _I,
+                                          _P, _P]),
     "splat_sh_forward": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P]),
     "splat_sh_backward": (_I, [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "splat_scan_workspace_bytes": (_Z, [_I]),

@@ -552,15 +552,37 @@ __global__ void __launch_bounds__(1024)
   const int t = blockIdx.x * 32 + lane;
   const int per = (chunks + kSegments - 1) / kSegments;
   const int k0 = min(seg * per, chunks), k1 = min(k0 + per, chunks);
+  // kBatch independent loads in flight per step (a segment is tens of chunks)
+  constexpr int kBatch = 8;
   uint32_t sum = 0u;
-  if (t < T)
-    for (int k = k0; k < k1; ++k) sum += cnt[static_cast<size_t>(k) * T + t];
+  if (t < T) {
+    int k = k0;
+    for (; k + kBatch <= k1; k += kBatch) {
+      uint32_t v[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) v[j] = cnt[static_cast<size_t>(k + j) * T + t];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) sum += v[j];
+    }
+    for (; k < k1; ++k) sum += cnt[static_cast<size_t>(k) * T + t];
+  }
   s_seg[seg][lane] = sum;
   __syncthreads();
   uint32_t run = 0u;
   for (int q = 0; q < seg; ++q) run += s_seg[q][lane];
   if (t < T) {
-    for (int k = k0; k < k1; ++k) {
+    int k = k0;
+    for (; k + kBatch <= k1; k += kBatch) {
+      uint32_t v[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) v[j] = cnt[static_cast<size_t>(k + j) * T + t];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        cnt[static_cast<size_t>(k + j) * T + t] = run;
+        run += v[j];
+      }
+    }
+    for (; k < k1; ++k) {
       uint32_t* c = cnt + static_cast<size_t>(k) * T + t;
       const uint32_t v = *c;
       *c = run;
@@ -735,24 +757,11 @@ __global__ void __launch_bounds__(256)
       r = sorted_rects[i];
     }
   };
-  if (warp == 0) {
-    uint32_t g0, g1;
-    uint2 r0, r1;
-    load(begin + lane, g0, r0);
-    load(begin + 32 + lane, g1, r1);
-    publish_wave(s_wave[0], lane, g0, r0, g1, r1);
-    load(begin + kWave + lane, ahead_g0, ahead_r0);
-    load(begin + kWave + 32 + lane, ahead_g1, ahead_r1);
-  }
-  __syncthreads();
-  int buf = 0;
-  for (uint32_t w0 = begin; w0 < end; w0 += kWave, buf ^= 1) {
-    const ScatterWave& wave = s_wave[buf];
-    unsigned long long* col = s_masks + buf * mask_words;
+  // coverage masks of wave w: task q is column or row (q - lines[j]) of
+  // member j; each sets bit j with a 32-bit atomic on the half of the 64-bit
+  // word that holds it
+  auto build_masks = [&](const ScatterWave& wave, unsigned long long* col) {
     unsigned long long* rowm = col + gx;
-    // coverage masks: task q is column or row (q - lines[j]) of member j;
-    // each sets bit j with a 32-bit atomic on the half of the 64-bit word
-    // that holds it
     for (uint32_t q = threadIdx.x; q < wave.lines[kWave]; q += blockDim.x) {
       int j = 0;
 #pragma unroll
@@ -764,7 +773,30 @@ __global__ void __launch_bounds__(256)
       unsigned long long* word = local < x1 - x0 ? col + x0 + local : rowm + y0 + (local - (x1 - x0));
       atomicOr(reinterpret_cast<uint32_t*>(word) + (j >> 5), 1u << (j & 31));
     }
-    __syncthreads();
+  };
+  if (warp == 0) {
+    uint32_t g0, g1;
+    uint2 r0, r1;
+    load(begin + lane, g0, r0);
+    load(begin + 32 + lane, g1, r1);
+    publish_wave(s_wave[0], lane, g0, r0, g1, r1);
+    load(begin + kWave + lane, ahead_g0, ahead_r0);
+    load(begin + kWave + 32 + lane, ahead_g1, ahead_r1);
+  }
+  __syncthreads();
+  build_masks(s_wave[0], s_masks);
+  __syncthreads();
+  // Two barriers per wave w (buffers by parity):
+  //   phase B: pairs of w (read wave[b], masks[b], next); clear masks[b^1]
+  //            and publish wave w+1 into wave[b^1] (both last read in
+  //            phase C of w-1)
+  //   phase C: advance next by w (read wave[b], masks[b]); build masks[b^1]
+  //            of wave w+1
+  int buf = 0;
+  for (uint32_t w0 = begin; w0 < end; w0 += kWave, buf ^= 1) {
+    const ScatterWave& wave = s_wave[buf];
+    unsigned long long* col = s_masks + buf * mask_words;
+    unsigned long long* rowm = col + gx;
     const uint32_t P = wave.pref[kWave];
     uint32_t kept_tile[kKept], kept_add[kKept];
 #pragma unroll
@@ -792,16 +824,6 @@ __global__ void __launch_bounds__(256)
       else
         record_device_error(kInconsistentInput);
     }
-    __syncthreads();
-    // advance each covered tile by the wave's count (its first covering
-    // member does it), clear the other mask buffer, publish the next wave
-#pragma unroll
-    for (int it = 0; it < kKept; ++it)
-      if (kept_add[it]) s_next[kept_tile[it]] += kept_add[it];
-    for (uint32_t p = threadIdx.x + kKept * blockDim.x; p < P; p += blockDim.x) {
-      const WavePair q = wave_pair(wave, p, gx, col, rowm);
-      if ((q.cover & members_below(q.member)) == 0ull) s_next[q.tile] += __popcll(q.cover);
-    }
     unsigned long long* other = s_masks + (buf ^ 1) * mask_words;
     for (int c = threadIdx.x; c < mask_words; c += blockDim.x) other[c] = 0ull;
     if (warp == 0) {
@@ -809,6 +831,17 @@ __global__ void __launch_bounds__(256)
       load(w0 + 2 * kWave + lane, ahead_g0, ahead_r0);
       load(w0 + 2 * kWave + 32 + lane, ahead_g1, ahead_r1);
     }
+    __syncthreads();
+    // advance each covered tile by the wave's count (its first covering
+    // member does it)
+#pragma unroll
+    for (int it = 0; it < kKept; ++it)
+      if (kept_add[it]) s_next[kept_tile[it]] += kept_add[it];
+    for (uint32_t p = threadIdx.x + kKept * blockDim.x; p < P; p += blockDim.x) {
+      const WavePair q = wave_pair(wave, p, gx, col, rowm);
+      if ((q.cover & members_below(q.member)) == 0ull) s_next[q.tile] += __popcll(q.cover);
+    }
+    build_masks(s_wave[buf ^ 1], other);
     __syncthreads();
   }
 }

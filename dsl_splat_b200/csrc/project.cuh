@@ -283,46 +283,84 @@ SPLAT_DEV void warp_store_sh(float* __restrict__ dst, int row_stride, int base, 
   }
 }
 
+// One camera's view of the inputs and the outputs it writes (ProjectParams
+// fields; the multi-view kernel takes them from per-view tables).
+struct ProjectCamera {
+  const float* view;    // 4x4 row-major world->camera
+  const float* proj;    // 4x4 full projection
+  const float* K;       // 3x3 intrinsics
+  const float* campos;  // (3) or null
+};
+
+struct ProjectOutputs {
+  float* centers;
+  float* conics;
+  int* radii;
+  int* tiles;
+  float* depths;
+  float* colors;
+  uint8_t* active;
+  float* meta_means2d;
+  float* meta_opacities;
+  float* meta_conics;
+};
+
+// The per-Gaussian inputs, read once per Gaussian whatever the number of views.
+struct GaussianInput {
+  float m0, m1, m2;
+  float4 q;  // normalised quaternion (w, x, y, z)
+  float3 s;
+  float opacity;
+};
+
+SPLAT_DEV GaussianInput load_gaussian(const float* means, const float* quats, int normalize,
+                                      const float* scales, const float* opacities, int i) {
+  GaussianInput g;
+  g.m0 = means[3 * i];
+  g.m1 = means[3 * i + 1];
+  g.m2 = means[3 * i + 2];
+  g.q = reinterpret_cast<const float4*>(quats)[i];
+  if (normalize) g.q = torch_normalize4(g.q);
+  g.s = make_float3(scales[3 * i], scales[3 * i + 1], scales[3 * i + 2]);
+  g.opacity = opacities[i];
+  return g;
+}
+
 // gs3d/projection.py:89-164 (+ primitives/sh.py:44-79, splatting/metadata.py:12-31)
+// for Gaussian i seen by one camera; `row` is its staged SH row (null: no SH).
+// p supplies the settings shared by all views (image size, planes, clip,
+// tile mode, SH degree and colour stride).
 template <int DEG>
-__global__ void __launch_bounds__(kProjectBlock) project_forward_kernel(ProjectParams p) {
-  __shared__ float s_sh[kProjectWarps][32 * ShTile<DEG>::kStride];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int base = (blockIdx.x * kProjectWarps + warp) * 32;
-  if (base >= p.n) return;  // uniform per warp
-  float* tile = s_sh[warp];
-  if (DEG >= 0 && p.sh != nullptr) warp_load_sh<DEG>(p.sh, p.sh_k * 3, base, p.n, tile);
-  const int i = base + lane;
-  if (i >= p.n) return;
+SPLAT_DEV void project_gaussian(const ProjectParams& p, const ProjectCamera& cam,
+                                const ProjectOutputs& out, int i, const GaussianInput& g,
+                                const float* row) {
   const int gx = (p.width + 15) / 16, gy = (p.height + 15) / 16;
   int radius_out = 0, count_out = 0;
   float2 center = make_float2(0.0f, 0.0f);
   float4 conic = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  const float m0 = p.means[3 * i], m1 = p.means[3 * i + 1], m2 = p.means[3 * i + 2];
+  const float m0 = g.m0, m1 = g.m1, m2 = g.m2;
   do {
-    const float t0 = point_row(p.view, 0, m0, m1, m2);
-    const float t1 = point_row(p.view, 1, m0, m1, m2);
-    const float t2 = point_row(p.view, 2, m0, m1, m2);
+    const float t0 = point_row(cam.view, 0, m0, m1, m2);
+    const float t1 = point_row(cam.view, 1, m0, m1, m2);
+    const float t2 = point_row(cam.view, 2, m0, m1, m2);
     if (t2 <= p.near_plane || t2 >= p.far_plane) break;
-    float4 q = reinterpret_cast<const float4*>(p.quats)[i];
-    if (p.normalize_quats) q = torch_normalize4(q);
-    const float3 s = make_float3(p.scales[3 * i], p.scales[3 * i + 1], p.scales[3 * i + 2]);
-    const float3 cov = screen_covariance(t0, t1, t2, q, s, p.view, p.width, p.height, p.K[0], p.K[4]);
+    const float3 cov = screen_covariance(t0, t1, t2, g.q, g.s, cam.view, p.width, p.height,
+                                         cam.K[0], cam.K[4]);
     const float a = cov.x, b = cov.y, c = cov.z;
     const float det = a * c - b * b;
     if (det == 0.0f) break;
     const float mid = 0.5f * (a + c);
     const int radius = f2i(ceilf(3.0f * sqrtf(mid + sqrtf(wmax(W32(0.1), mid * mid - det)))));
     if (static_cast<float>(radius) <= p.radius_clip) break;
-    center = pixel_center(m0, m1, m2, p.proj, p.width, p.height);
+    center = pixel_center(m0, m1, m2, cam.proj, p.width, p.height);
     const int4 bnd = tile_bounds(center.x, center.y, radius, gx, gy);
     const int count = (bnd.z - bnd.x) * (bnd.w - bnd.y);
     if (count == 0) break;
     const float inverse = 1.0f / (a * c - b * b);
-    conic = make_float4(c * inverse, -b * inverse, a * inverse, p.opacities[i]);
-    reinterpret_cast<float2*>(p.centers)[i] = center;
-    reinterpret_cast<float4*>(p.conics)[i] = conic;
-    p.depths[i] = t2;
+    conic = make_float4(c * inverse, -b * inverse, a * inverse, g.opacity);
+    reinterpret_cast<float2*>(out.centers)[i] = center;
+    reinterpret_cast<float4*>(out.conics)[i] = conic;
+    out.depths[i] = t2;
     radius_out = radius;
     count_out = count;
     // gs3d/projection.py:150-162: the mode's tile count replaces the square's
@@ -330,38 +368,109 @@ __global__ void __launch_bounds__(kProjectBlock) project_forward_kernel(ProjectP
     if (p.tile_mode != kTileRadius)
       count_out = tile_count(tile_visit(p.tile_mode, center.x, center.y, conic, radius, gx, gy));
   } while (false);
-  p.radii[i] = radius_out;
-  p.tiles[i] = count_out;
+  out.radii[i] = radius_out;
+  out.tiles[i] = count_out;
   const bool visible = radius_out > 0;
-  if (DEG >= 0 && p.sh != nullptr) {
+  if (DEG >= 0 && row != nullptr) {
     float3 v = make_float3(0.0f, 0.0f, 0.0f);
     if (visible) {
       float d0 = m0, d1 = m1, d2 = m2;
-      if (p.campos != nullptr) {
-        d0 = m0 - p.campos[0];
-        d1 = m1 - p.campos[1];
-        d2 = m2 - p.campos[2];
+      if (cam.campos != nullptr) {
+        d0 = m0 - cam.campos[0];
+        d1 = m1 - cam.campos[1];
+        d2 = m2 - cam.campos[2];
       }
-      v = sh_eval<(DEG < 0 ? 0 : DEG)>(tile + lane * ShTile<DEG>::kStride, d0, d1, d2);
+      v = sh_eval<(DEG < 0 ? 0 : DEG)>(row, d0, d1, d2);
     }
-    float* col = p.colors + static_cast<size_t>(i) * p.color_stride;
+    float* col = out.colors + static_cast<size_t>(i) * p.color_stride;
     col[0] = wmax(v.x, 0.0f);
     col[1] = wmax(v.y, 0.0f);
     col[2] = wmax(v.z, 0.0f);
-    if (p.active != nullptr) {
-      p.active[3 * i + 0] = visible && v.x >= 0.0f;
-      p.active[3 * i + 1] = visible && v.y >= 0.0f;
-      p.active[3 * i + 2] = visible && v.z >= 0.0f;
+    if (out.active != nullptr) {
+      out.active[3 * i + 0] = visible && v.x >= 0.0f;
+      out.active[3 * i + 1] = visible && v.y >= 0.0f;
+      out.active[3 * i + 2] = visible && v.z >= 0.0f;
     }
   }
-  if (p.meta_means2d != nullptr) {
+  if (out.meta_means2d != nullptr) {
     // culled rows (including those culled after the centre was computed)
     // are zero, as splatting/metadata.py:28-32 writes them
-    reinterpret_cast<float2*>(p.meta_means2d)[i] = visible ? center : make_float2(0.0f, 0.0f);
-    p.meta_opacities[i] = visible ? conic.w : 0.0f;
-    p.meta_conics[3 * i + 0] = visible ? conic.x : 0.0f;
-    p.meta_conics[3 * i + 1] = visible ? conic.y : 0.0f;
-    p.meta_conics[3 * i + 2] = visible ? conic.z : 0.0f;
+    reinterpret_cast<float2*>(out.meta_means2d)[i] = visible ? center : make_float2(0.0f, 0.0f);
+    out.meta_opacities[i] = visible ? conic.w : 0.0f;
+    out.meta_conics[3 * i + 0] = visible ? conic.x : 0.0f;
+    out.meta_conics[3 * i + 1] = visible ? conic.y : 0.0f;
+    out.meta_conics[3 * i + 2] = visible ? conic.z : 0.0f;
+  }
+}
+
+template <int DEG>
+__global__ void __launch_bounds__(kProjectBlock) project_forward_kernel(ProjectParams p) {
+  __shared__ float s_sh[kProjectWarps][32 * ShTile<DEG>::kStride];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = (blockIdx.x * kProjectWarps + warp) * 32;
+  if (base >= p.n) return;  // uniform per warp
+  float* tile = s_sh[warp];
+  const bool sh = DEG >= 0 && p.sh != nullptr;
+  if (sh) warp_load_sh<DEG>(p.sh, p.sh_k * 3, base, p.n, tile);
+  const int i = base + lane;
+  if (i >= p.n) return;
+  const GaussianInput g =
+      load_gaussian(p.means, p.quats, p.normalize_quats, p.scales, p.opacities, i);
+  project_gaussian<DEG>(p, ProjectCamera{p.view, p.proj, p.K, p.campos},
+                        ProjectOutputs{p.centers, p.conics, p.radii, p.tiles, p.depths, p.colors,
+                                       p.active, p.meta_means2d, p.meta_opacities,
+                                       p.meta_conics},
+                        i, g, sh ? tile + lane * ShTile<DEG>::kStride : nullptr);
+}
+
+// Up to kMaxViews cameras of one Gaussian set in one launch: each warp stages
+// its 32 SH rows and each thread loads its Gaussian once, then projects it
+// for every camera (the same arithmetic as project_forward_kernel).  Camera
+// v's matrices are rows v of the stacked arrays; its outputs come from the
+// per-view pointer tables.
+constexpr int kMaxViews = 16;
+
+struct ProjectViewsParams {
+  ProjectParams shared;  // inputs, settings; its camera/output fields are unused
+  int views;
+  const float* viewmats;  // (views,4,4)
+  const float* projs;     // (views,4,4)
+  const float* Ks;        // (views,3,3)
+  const float* campos;    // (views,3) or null
+  float* centers[kMaxViews];
+  float* conics[kMaxViews];
+  int* radii[kMaxViews];
+  int* tiles[kMaxViews];
+  float* depths[kMaxViews];
+  float* colors[kMaxViews];
+  uint8_t* active[kMaxViews];
+  float* meta_means2d[kMaxViews];
+  float* meta_opacities[kMaxViews];
+  float* meta_conics[kMaxViews];
+};
+
+template <int DEG>
+__global__ void __launch_bounds__(kProjectBlock) project_forward_views_kernel(ProjectViewsParams vp) {
+  const ProjectParams& p = vp.shared;
+  __shared__ float s_sh[kProjectWarps][32 * ShTile<DEG>::kStride];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int base = (blockIdx.x * kProjectWarps + warp) * 32;
+  if (base >= p.n) return;  // uniform per warp
+  float* tile = s_sh[warp];
+  const bool sh = DEG >= 0 && p.sh != nullptr;
+  if (sh) warp_load_sh<DEG>(p.sh, p.sh_k * 3, base, p.n, tile);
+  const int i = base + lane;
+  if (i >= p.n) return;
+  const GaussianInput g =
+      load_gaussian(p.means, p.quats, p.normalize_quats, p.scales, p.opacities, i);
+  const float* row = sh ? tile + lane * ShTile<DEG>::kStride : nullptr;
+  for (int v = 0; v < vp.views; ++v) {
+    const ProjectCamera cam{vp.viewmats + 16 * v, vp.projs + 16 * v, vp.Ks + 9 * v,
+                            vp.campos ? vp.campos + 3 * v : nullptr};
+    const ProjectOutputs out{vp.centers[v], vp.conics[v], vp.radii[v], vp.tiles[v],
+                             vp.depths[v], vp.colors[v], vp.active[v], vp.meta_means2d[v],
+                             vp.meta_opacities[v], vp.meta_conics[v]};
+    project_gaussian<DEG>(p, cam, out, i, g, row);
   }
 }
 

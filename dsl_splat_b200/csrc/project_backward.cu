@@ -567,6 +567,261 @@ __global__ void __launch_bounds__(kBackwardBlock)
   }
 }
 
+// ---- several views in one launch ------------------------------------------
+//
+// The backward of project_forward_views_kernel: per chunk of 32 Gaussians a
+// warp stages the SH rows, means, quaternions and scales once, then walks
+// the views, adding each view's projection VJP into registers and its SH
+// coefficient gradient into a second shared-memory row; the (linear)
+// normalisation VJP is applied once to the summed quaternion gradient and
+// every gradient is written once.  Camera gradients are not formed here (the
+// host runs the per-view kernel when they are requested).
+struct ProjectBackwardViewsParams {
+  ProjectBackwardParams shared;  // Gaussian inputs/outputs and settings; per-view fields unused
+  int views;
+  const float* viewmats;  // (views,4,4)
+  const float* projs;     // (views,4,4)
+  const float* Ks;        // (views,3,3)
+  const float* campos;    // (views,3) or null
+  const int* radii[kMaxViews];
+  const float* seed_centers[kMaxViews];
+  const float* seed_conics[kMaxViews];
+  const float* seed_colors[kMaxViews];  // (n, color_stride); null without SH gradients
+  const uint8_t* active[kMaxViews];
+};
+
+template <int DEG>
+struct ViewsStage {
+  using B = BackwardStage<DEG>;
+  static constexpr int kSh0 = 0;                        // coefficient rows
+  static constexpr int kGrad0 = kSh0 + 32 * B::kRow;    // gradient rows
+  static constexpr int kMeans = kGrad0 + 32 * B::kRow;
+  static constexpr int kQuats = kMeans + 96;
+  static constexpr int kScales = kQuats + 128;
+  static constexpr int kWords = kScales + 96;
+  static_assert(kMeans % 4 == 0 && kWords % 4 == 0, "16-byte slices");
+};
+
+// sh_vjp_quads reading the coefficient row and adding the coefficient
+// gradient into a separate row (primitives/sh.py:116-120 summed over views).
+template <int DEG>
+SPLAT_DEV float3 sh_vjp_accumulate(const float* coef, float* grad, float d0, float d1, float d2,
+                                   float3 cg) {
+  constexpr int B = (DEG + 1) * (DEG + 1);
+  constexpr int kGroup = B % 4 == 0 ? 4 : B;
+  constexpr int kGroupQuads = (3 * kGroup + 3) / 4;
+  float ux = 0.0f, uy = 0.0f, uz = 0.0f, length = 1.0f;
+  if (DEG > 0) {
+    length = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
+    const float den = wmax(length, W32(1e-12));
+    ux = d0 / den;
+    uy = d1 / den;
+    uz = d2 / den;
+  }
+  const float4* c4 = reinterpret_cast<const float4*>(coef);
+  float4* g4 = reinterpret_cast<float4*>(grad);
+  float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+#pragma unroll
+  for (int g = 0; g < B / kGroup; ++g) {
+    float c[4 * kGroupQuads], o[4 * kGroupQuads];
+#pragma unroll
+    for (int q = 0; q < kGroupQuads; ++q) {
+      const float4 v = c4[g * kGroupQuads + q], w = g4[g * kGroupQuads + q];
+      c[4 * q] = v.x;
+      c[4 * q + 1] = v.y;
+      c[4 * q + 2] = v.z;
+      c[4 * q + 3] = v.w;
+      o[4 * q] = w.x;
+      o[4 * q + 1] = w.y;
+      o[4 * q + 2] = w.z;
+      o[4 * q + 3] = w.w;
+    }
+#pragma unroll
+    for (int kk = 0; kk < kGroup; ++kk) {
+      const int k = g * kGroup + kk;
+      const float b = sh_basis(ux, uy, uz, k);
+      if (DEG > 0) {
+        const float w = c[3 * kk] * cg.x + c[3 * kk + 1] * cg.y + c[3 * kk + 2] * cg.z;
+        const float3 bg = sh_basis_grad(ux, uy, uz, k);
+        g0 += w * bg.x;
+        g1 += w * bg.y;
+        g2 += w * bg.z;
+      }
+      o[3 * kk] += b * cg.x;
+      o[3 * kk + 1] += b * cg.y;
+      o[3 * kk + 2] += b * cg.z;
+    }
+#pragma unroll
+    for (int q = 0; q < kGroupQuads; ++q)
+      g4[g * kGroupQuads + q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+  }
+  if (DEG == 0) return make_float3(0.0f, 0.0f, 0.0f);
+  const float den = wmax(length, W32(1e-12));
+  float3 dg = make_float3(g0 / den, g1 / den, g2 / den);
+  if (length >= W32(1e-12)) {
+    const float dot = (ux * g0 + uy * g1 + uz * g2) / length;
+    dg.x -= ux * dot;
+    dg.y -= uy * dot;
+    dg.z -= uz * dot;
+  }
+  return dg;
+}
+
+template <int DEG>
+__global__ void __launch_bounds__(kBackwardBlock)
+    project_backward_views_kernel(ProjectBackwardViewsParams vp, unsigned mask) {
+  using L = ViewsStage<DEG>;
+  using B = BackwardStage<DEG>;
+  const ProjectBackwardParams& p = vp.shared;
+  extern __shared__ __align__(16) uint32_t s_stage[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t* st = s_stage + static_cast<size_t>(warp) * L::kWords;
+  float* sf = reinterpret_cast<float*>(st);
+  const bool sh_grads = B::kSh && p.grad_sh != nullptr;
+  const int stride = gridDim.x * kBackwardWarps * 32;
+  for (int base = (blockIdx.x * kBackwardWarps + warp) * 32; base < p.n; base += stride) {
+    const int rows = min(32, p.n - base);
+    const bool full = rows == 32;
+    const size_t b = static_cast<size_t>(base);
+    const float* quats = p.quats_raw ? p.quats_raw : p.quats;
+    stage_slice(st + L::kMeans, p.means + 3 * b, 3 * rows, full && (mask & kAsyncMeans), lane);
+    stage_slice(st + L::kQuats, quats + 4 * b, 4 * rows, full && (mask & kAsyncQuats), lane);
+    stage_slice(st + L::kScales, p.scales + 3 * b, 3 * rows, full && (mask & kAsyncScales), lane);
+    if constexpr (B::kSh) {
+      if (sh_grads) {
+        float* sh = sf + L::kSh0;
+        const size_t rs = static_cast<size_t>(p.sh_k) * 3;
+        bool staged = false;
+        if constexpr (B::kCols % 4 == 0) {
+          if (full && (mask & kAsyncSh)) {
+            constexpr int Q = B::kCols / 4;
+#pragma unroll
+            for (int j = 0; j < Q; ++j) {
+              const int t = lane + 32 * j;
+              const int r = t / Q, q = t - r * Q;
+              cp_async16(sh + r * B::kRow + 4 * q, p.sh + (b + r) * rs + 4 * q);
+            }
+            staged = true;
+          }
+        }
+        if (!staged)
+          for (int t = lane; t < rows * B::kCols; t += 32) {
+            const int r = t / B::kCols, c = t - r * B::kCols;
+            sh[r * B::kRow + c] = __ldg(p.sh + (b + r) * rs + c);
+          }
+        float4* g4 = reinterpret_cast<float4*>(sf + L::kGrad0);
+        for (int t = lane; t < 32 * B::kRowQuads; t += 32) g4[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncwarp();
+    if (lane < rows) {
+      const int i = base + lane;
+      const float m0 = sf[L::kMeans + 3 * lane], m1 = sf[L::kMeans + 3 * lane + 1],
+                  m2 = sf[L::kMeans + 3 * lane + 2];
+      const float4 qs = reinterpret_cast<const float4*>(sf + L::kQuats)[lane];
+      VjpInput in;
+      in.m0 = m0;
+      in.m1 = m1;
+      in.m2 = m2;
+      in.q = p.quats_raw ? torch_normalize4(qs) : qs;
+#pragma unroll
+      for (int k = 0; k < 3; ++k) in.s[k] = sf[L::kScales + 3 * lane + k];
+      float gm[3] = {0.0f, 0.0f, 0.0f}, gq[4] = {0.0f, 0.0f, 0.0f, 0.0f}, gs[3] = {0.0f, 0.0f, 0.0f};
+      float go = 0.0f;
+      for (int v = 0; v < vp.views; ++v) {
+        if (vp.radii[v][i] <= 0) continue;
+        ProjectBackwardParams pv = p;
+        pv.view = vp.viewmats + 16 * v;
+        pv.proj = vp.projs + 16 * v;
+        pv.K = vp.Ks + 9 * v;
+        in.sc = reinterpret_cast<const float2*>(vp.seed_centers[v])[i];
+        in.sq = reinterpret_cast<const float4*>(vp.seed_conics[v])[i];
+        float vm[3], vq[4], vs[3], cv_local[16], cp_local[16];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) vm[k] = vs[k] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) vq[k] = 0.0f;
+        projection_vjp(pv, in, vm, vq, vs, cv_local, cp_local);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+          gm[k] += vm[k];
+          gs[k] += vs[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) gq[k] += vq[k];
+        go += in.sq.w;
+        if constexpr (B::kSh) {
+          if (sh_grads) {
+            const float* col = vp.seed_colors[v] + static_cast<size_t>(i) * p.color_stride;
+            const uint8_t* act = vp.active[v] + 3 * static_cast<size_t>(i);
+            const float3 cg = make_float3(act[0] ? col[0] : 0.0f, act[1] ? col[1] : 0.0f,
+                                          act[2] ? col[2] : 0.0f);
+            float d0 = m0, d1 = m1, d2 = m2;
+            if (vp.campos) {
+              d0 = m0 - vp.campos[3 * v];
+              d1 = m1 - vp.campos[3 * v + 1];
+              d2 = m2 - vp.campos[3 * v + 2];
+            }
+            const float3 dd = sh_vjp_accumulate<DEG>(sf + L::kSh0 + lane * B::kRow,
+                                                     sf + L::kGrad0 + lane * B::kRow, d0, d1,
+                                                     d2, cg);
+            if (DEG > 0) {
+              gm[0] += dd.x;
+              gm[1] += dd.y;
+              gm[2] += dd.z;
+            }
+          }
+        }
+      }
+      if (p.quats_raw) {
+        // the normalisation VJP is linear in the upstream gradient: applied
+        // once to the sum over views
+        const float norm = sqrtf((qs.x * qs.x + qs.z * qs.z) + (qs.y * qs.y + qs.w * qs.w));
+        if (norm > W32(1e-12)) {
+          const float4 n = in.q;
+          const float d = n.x * gq[0] + n.y * gq[1] + n.z * gq[2] + n.w * gq[3];
+          gq[0] = (gq[0] - n.x * d) / norm;
+          gq[1] = (gq[1] - n.y * d) / norm;
+          gq[2] = (gq[2] - n.z * d) / norm;
+          gq[3] = (gq[3] - n.w * d) / norm;
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) gq[k] = gq[k] / W32(1e-12);
+        }
+      }
+      const bool acc = p.accumulate != 0;
+      if (p.grad_means) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) put(p.grad_means + 3 * static_cast<size_t>(i) + k, gm[k], acc);
+      }
+      if (p.grad_quats) {
+        float4* o = reinterpret_cast<float4*>(p.grad_quats) + i;
+        float4 val = make_float4(gq[0], gq[1], gq[2], gq[3]);
+        if (acc) {
+          const float4 old = *o;
+          val = make_float4(old.x + val.x, old.y + val.y, old.z + val.z, old.w + val.w);
+        }
+        *o = val;
+      }
+      if (p.grad_scales) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) put(p.grad_scales + 3 * static_cast<size_t>(i) + k, gs[k], acc);
+      }
+      if (p.grad_opacities) put(p.grad_opacities + i, go, acc);
+    }
+    if constexpr (B::kSh) {
+      if (sh_grads) {
+        __syncwarp();
+        // store_sh_rows reads the gradient rows at the stage's SH offset
+        store_sh_rows<DEG>(p, mask, base, st + L::kGrad0, lane);
+      }
+    }
+    __syncwarp();
+  }
+}
+
 namespace {
 
 using host::aligned;
@@ -626,6 +881,46 @@ int launch_degree(const ProjectBackwardParams& p, cudaStream_t s) {
 
 }  // namespace
 
+template <int DEG>
+int launch_views(const ProjectBackwardViewsParams& vp, cudaStream_t s) {
+  using L = ViewsStage<DEG>;
+  const size_t smem = static_cast<size_t>(kBackwardWarps) * L::kWords * sizeof(uint32_t);
+  auto kernel = project_backward_views_kernel<DEG>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return host::check_launch("project_backward_views smem");
+  static int resident = 0;  // blocks per SM (the same on every device of a process)
+  if (resident == 0) {
+    int r = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, kernel, kBackwardBlock, smem) !=
+            cudaSuccess || r < 1)
+      r = 1;
+    resident = r;
+  }
+  const unsigned grid = std::min(host::blocks_for(vp.shared.n, kBackwardBlock),
+                                 static_cast<unsigned>(host::sm_count() * resident));
+  kernel<<<grid, kBackwardBlock, smem, host::counted(s)>>>(vp, async_mask(vp.shared));
+  return kOk;
+}
+
+int project_backward_views_dispatch(const ProjectBackwardViewsParams& vp, cudaStream_t s) {
+  if (vp.shared.n == 0 || vp.views == 0) return kOk;
+  int r;
+  if (vp.shared.grad_sh == nullptr) {
+    r = launch_views<-1>(vp, s);
+  } else {
+    switch (vp.shared.sh_degree) {
+      case 0: r = launch_views<0>(vp, s); break;
+      case 1: r = launch_views<1>(vp, s); break;
+      case 2: r = launch_views<2>(vp, s); break;
+      case 3: r = launch_views<3>(vp, s); break;
+      default: return host::fail(kInvalidArgument, "sh_degree must be in [0,3]");
+    }
+  }
+  if (r != kOk) return r;
+  return host::check_launch("project_backward_views");
+}
+
 int project_backward_dispatch(const ProjectBackwardParams& p, cudaStream_t s) {
   if (p.n == 0) return kOk;
   const int r = p.cam_grads ? launch_degree<true>(p, s) : launch_degree<false>(p, s);
@@ -634,3 +929,67 @@ int project_backward_dispatch(const ProjectBackwardParams& p, cudaStream_t s) {
 }
 
 }  // namespace splat
+
+using namespace splat;
+
+extern "C" int splat_project_backward_views(
+    int views, int n, const float* means, const float* quats, const float* quats_raw,
+    const float* scales, const float* viewmats, const float* projs, const float* Ks, int width,
+    int height, const int* const* radii, const float* const* grad_centers,
+    const float* const* grad_conics, float* grad_means, float* grad_quats, float* grad_scales,
+    float* grad_opacities, int accumulate, int sh_degree, int sh_k, const float* sh,
+    const float* campos, const unsigned char* const* active, const float* const* grad_colors,
+    int color_stride, float* grad_sh, void* stream) {
+  using host::aligned;
+  using host::fail;
+  if (views < 0 || n < 0 || width <= 0 || height <= 0)
+    return fail(kInvalidArgument, "bad projection sizes");
+  if (grad_sh && (!sh || !active || !grad_colors || sh_degree < 0 || sh_degree > 3 ||
+                  sh_k < (sh_degree + 1) * (sh_degree + 1) || color_stride < 3))
+    return fail(kInvalidArgument, "bad SH backward arguments");
+  if (!quats && !quats_raw) return fail(kInvalidArgument, "quats or quats_raw is required");
+  if (!radii || !grad_centers || !grad_conics)
+    return fail(kInvalidArgument, "the per-view input tables are required");
+  if (!aligned(quats, 16) || !aligned(quats_raw, 16) || !aligned(grad_quats, 16))
+    return fail(kInvalidArgument, "quat rows need 16-byte alignment");
+  for (int v = 0; v < views; ++v)
+    if (!aligned(grad_conics[v], 16) || !aligned(grad_centers[v], 8))
+      return fail(kInvalidArgument, "conic rows need 16-byte, centre rows 8-byte alignment");
+  ProjectBackwardViewsParams vp{};
+  ProjectBackwardParams& p = vp.shared;
+  p.n = n;
+  p.means = means;
+  p.quats = quats;
+  p.quats_raw = quats_raw;
+  p.scales = scales;
+  p.width = width;
+  p.height = height;
+  p.grad_means = grad_means;
+  p.grad_quats = grad_quats;
+  p.grad_scales = grad_scales;
+  p.grad_opacities = grad_opacities;
+  p.sh_degree = sh_degree;
+  p.sh_k = sh_k;
+  p.sh = sh;
+  p.color_stride = color_stride;
+  p.grad_sh = grad_sh;
+  // at most kMaxViews cameras per launch; later launches accumulate
+  for (int v0 = 0; v0 < views; v0 += kMaxViews) {
+    p.accumulate = (accumulate || v0 > 0) ? 1 : 0;
+    vp.views = std::min(kMaxViews, views - v0);
+    vp.viewmats = viewmats + 16 * v0;
+    vp.projs = projs + 16 * v0;
+    vp.Ks = Ks + 9 * v0;
+    vp.campos = campos ? campos + 3 * v0 : nullptr;
+    for (int v = 0; v < vp.views; ++v) {
+      vp.radii[v] = radii[v0 + v];
+      vp.seed_centers[v] = grad_centers[v0 + v];
+      vp.seed_conics[v] = grad_conics[v0 + v];
+      vp.seed_colors[v] = grad_colors ? grad_colors[v0 + v] : nullptr;
+      vp.active[v] = active ? active[v0 + v] : nullptr;
+    }
+    const int r = project_backward_views_dispatch(vp, reinterpret_cast<cudaStream_t>(stream));
+    if (r != kOk) return r;
+  }
+  return kOk;
+}

@@ -213,6 +213,28 @@ int project_forward_dispatch(const ProjectParams& p, cudaStream_t s) {
   return check_launch("project_forward");
 }
 
+template <int DEG>
+void launch_project_forward_views(const ProjectViewsParams& p, cudaStream_t s) {
+  project_forward_views_kernel<DEG>
+      <<<blocks_for(p.shared.n, kProjectBlock), kProjectBlock, 0, counted(s)>>>(p);
+}
+
+int project_forward_views_dispatch(const ProjectViewsParams& p, cudaStream_t s) {
+  if (p.shared.n == 0 || p.views == 0) return kOk;
+  if (p.shared.sh == nullptr) {
+    launch_project_forward_views<-1>(p, s);
+  } else {
+    switch (p.shared.sh_degree) {
+      case 0: launch_project_forward_views<0>(p, s); break;
+      case 1: launch_project_forward_views<1>(p, s); break;
+      case 2: launch_project_forward_views<2>(p, s); break;
+      case 3: launch_project_forward_views<3>(p, s); break;
+      default: return fail(kInvalidArgument, "sh_degree must be in [0,3]");
+    }
+  }
+  return check_launch("project_forward_views");
+}
+
 template <int CHP>
 void launch_render(const RenderParams& p, bool backward, cudaStream_t s) {
   const unsigned tiles = static_cast<unsigned>(p.gx * ((p.height + 15) / 16));
@@ -398,6 +420,77 @@ int splat_project_forward_fused(int n, const float* means, const float* quats,
   p.meta_opacities = meta_opacities;
   p.meta_conics = meta_conics;
   return project_forward_dispatch(p, as_stream(stream));
+}
+
+int splat_project_forward_views(int views, int n, const float* means, const float* quats,
+                                int normalize_quats, const float* scales,
+                                const float* opacities, const float* viewmats,
+                                const float* projs, const float* Ks, int width, int height,
+                                float near_plane, float far_plane, float radius_clip,
+                                float* const* centers, float* const* conics, int* const* radii,
+                                int* const* tiles, float* const* depths, int sh_degree,
+                                int sh_k, const float* sh, const float* campos,
+                                float* const* colors, int color_stride,
+                                unsigned char* const* active, float* const* meta_means2d,
+                                float* const* meta_opacities, float* const* meta_conics,
+                                int tile_mode, void* stream) {
+  if (views < 0 || n < 0 || width <= 0 || height <= 0)
+    return fail(kInvalidArgument, "bad projection sizes");
+  if (tile_mode < kTileRadius || tile_mode > kTileAccutile)
+    return fail(kInvalidArgument, "tile_mode must be 0 (radius), 1 (snugbox) or 2 (accutile)");
+  if (sh && (sh_degree < 0 || sh_degree > 3 || sh_k < (sh_degree + 1) * (sh_degree + 1) ||
+             !colors || color_stride < 3))
+    return fail(kInvalidArgument, "bad SH arguments");
+  if (!centers || !conics || !radii || !tiles || !depths)
+    return fail(kInvalidArgument, "the per-view output tables are required");
+  if (meta_means2d && (!meta_opacities || !meta_conics))
+    return fail(kInvalidArgument, "metadata outputs come together");
+  if (!aligned(quats, 16)) return fail(kInvalidArgument, "quats need 16-byte alignment");
+  for (int v = 0; v < views; ++v)
+    if (!aligned(centers[v], 8) || !aligned(conics[v], 16) ||
+        (meta_means2d && !aligned(meta_means2d[v], 8)))
+      return fail(kInvalidArgument, "centre rows need 8-byte, conic rows 16-byte alignment");
+  ProjectViewsParams vp{};
+  ProjectParams& p = vp.shared;
+  p.n = n;
+  p.means = means;
+  p.quats = quats;
+  p.normalize_quats = normalize_quats ? 1 : 0;
+  p.tile_mode = tile_mode;
+  p.scales = scales;
+  p.opacities = opacities;
+  p.width = width;
+  p.height = height;
+  p.near_plane = near_plane;
+  p.far_plane = far_plane;
+  p.radius_clip = radius_clip;
+  p.sh_degree = sh_degree;
+  p.sh_k = sh_k;
+  p.sh = sh;
+  p.color_stride = color_stride;
+  // at most kMaxViews cameras per launch
+  for (int v0 = 0; v0 < views; v0 += kMaxViews) {
+    vp.views = std::min(kMaxViews, views - v0);
+    vp.viewmats = viewmats + 16 * v0;
+    vp.projs = projs + 16 * v0;
+    vp.Ks = Ks + 9 * v0;
+    vp.campos = campos ? campos + 3 * v0 : nullptr;
+    for (int v = 0; v < vp.views; ++v) {
+      vp.centers[v] = centers[v0 + v];
+      vp.conics[v] = conics[v0 + v];
+      vp.radii[v] = radii[v0 + v];
+      vp.tiles[v] = tiles[v0 + v];
+      vp.depths[v] = depths[v0 + v];
+      vp.colors[v] = colors ? colors[v0 + v] : nullptr;
+      vp.active[v] = active ? active[v0 + v] : nullptr;
+      vp.meta_means2d[v] = meta_means2d ? meta_means2d[v0 + v] : nullptr;
+      vp.meta_opacities[v] = meta_opacities ? meta_opacities[v0 + v] : nullptr;
+      vp.meta_conics[v] = meta_conics ? meta_conics[v0 + v] : nullptr;
+    }
+    const int r = project_forward_views_dispatch(vp, as_stream(stream));
+    if (r != kOk) return r;
+  }
+  return kOk;
 }
 
 int splat_metadata(int n, const int* radii, const float* centers, const float* conics,

@@ -22,7 +22,7 @@ from ..inputs import batch_item, normalize_inputs
 from ..statistics import StatisticsRequest, prepare_statistics
 from ..training import prepare_training_metadata
 from .. import stages
-from .autograd import ProjectView, RenderView
+from .autograd import ProjectView, ProjectViews, RenderView
 
 TILE_MODES = ("radius", "snugbox", "accutile")
 
@@ -108,11 +108,38 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
     config = ViewConfig(width, height, near_plane, far_plane, radius_clip, tile_mode)
     grad_enabled = torch.is_grad_enabled()
     frames = []
+    # per batch: (cameras, n, ...) stacks of the dense metadata
     dense: dict[str, list[Tensor]] = {k: [] for k in ("radii", "means2d", "opacities",
                                                       "tiles_per_gauss", "conics")}
     for b in range(layout.batch_count):
         bm, bq = layout.means[b], layout.quats[b]
         bs, bo = layout.scales[b], layout.opacities[b]
+        shared_sh = sh_degree is not None and not layout.colors.per_view
+        if layout.cameras > 1 and (sh_degree is None or shared_sh):
+            # every camera of the batch in one projection launch each way
+            C = layout.cameras
+            out = ProjectViews.apply(
+                bm, bq, bs, bo, layout.colors.at(b, 0) if sh_degree is not None else None,
+                batch_item(layout.viewmats, b), batch_item(full, b),
+                batch_item(centers, b) if with_centers else None, batch_item(layout.Ks, b),
+                config, sh_degree, grad_enabled)
+            radii, tiles, depths, m2d, mop, mcon = out[3 * C:]
+            for c in range(C):
+                ctr, con, col = out[c], out[C + c], out[2 * C + c]
+                colors = col if sh_degree is not None else layout.colors.at(b, c)
+                extras = None if layout.extras is None else layout.extras.at(b, c)
+                bg = (None if layout.backgrounds is None
+                      else batch_item(batch_item(layout.backgrounds, b), c))
+                frames.append((b, c, ctr, con, colors, extras, bg,
+                               stages.ProjectedGaussians(ctr, con, radii[c], tiles[c],
+                                                         depths[c])))
+            dense["radii"].append(radii[..., None].expand(-1, -1, 2))
+            dense["means2d"].append(m2d)
+            dense["opacities"].append(mop)
+            dense["tiles_per_gauss"].append(tiles)
+            dense["conics"].append(mcon)
+            continue
+        rows: dict[str, list[Tensor]] = {k: [] for k in dense}
         for c in range(layout.cameras):
             view = batch_item(batch_item(layout.viewmats, b), c)
             proj = batch_item(batch_item(full, b), c)
@@ -128,15 +155,17 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
             bg = None if layout.backgrounds is None else batch_item(batch_item(layout.backgrounds, b), c)
             frames.append((b, c, ctr, con, colors, extras, bg,
                            stages.ProjectedGaussians(ctr, con, radii, tiles, depths)))
-            dense["radii"].append(radii[:, None].expand(-1, 2))
-            dense["means2d"].append(m2d)
-            dense["opacities"].append(mop)
-            dense["tiles_per_gauss"].append(tiles)
-            dense["conics"].append(mcon)
+            rows["radii"].append(radii[:, None].expand(-1, 2))
+            rows["means2d"].append(m2d)
+            rows["opacities"].append(mop)
+            rows["tiles_per_gauss"].append(tiles)
+            rows["conics"].append(mcon)
+        for name, r in rows.items():
+            dense[name].append(r[0][None] if len(r) == 1 else torch.stack(r))
     geometry = {
-        name: (rows[0] if len(rows) == 1 else torch.stack(rows)).reshape(
-            (layout.batch_count, layout.cameras, layout.n) + tuple(rows[0].shape[1:]))
-        for name, rows in dense.items()
+        name: (per_batch[0] if len(per_batch) == 1 else torch.stack(per_batch)).reshape(
+            (layout.batch_count, layout.cameras, layout.n) + tuple(per_batch[0].shape[2:]))
+        for name, per_batch in dense.items()
     }
     # Binning reads the pair counts (and camera status) in one host
     # synchronisation; the packed metadata's visible counts ride along.

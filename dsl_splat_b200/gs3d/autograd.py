@@ -136,6 +136,141 @@ class ProjectView(torch.autograd.Function):
                 None, None)
 
 
+class ProjectViews(torch.autograd.Function):
+    """ProjectView for every camera of a batch in one launch each way
+    (gs3d/api.py:132-189's per-camera loop fused: splat_project_forward_views
+    and splat_project_backward_views).
+
+    Outputs: per camera its centres, conics and colours (separate tensors,
+    so each view's gradient arrives on its own and nothing materialises a
+    (views, n, ...) gradient), then the stacked (views, n, ...) radii, tile
+    counts, depths and dense metadata.  The backward sums the views inside
+    the kernel (one read of every Gaussian's inputs, one write of every
+    gradient); when pose gradients are requested it runs the per-view kernel
+    once per camera instead."""
+
+    @staticmethod
+    def forward(ctx: Any, means: Tensor, quats_raw: Tensor, scales: Tensor, opacities: Tensor,
+                sh: Tensor | None, views: Tensor, fulls: Tensor, campos: Tensor | None,
+                intrinsics: Tensor, config: ViewConfig, sh_degree: int, grad_enabled: bool):
+        means, quats_raw, scales = means.contiguous(), quats_raw.contiguous(), scales.contiguous()
+        sh = None if sh is None else sh.contiguous()
+        views, fulls, intrinsics = views.contiguous(), fulls.contiguous(), intrinsics.contiguous()
+        campos = None if campos is None else campos.contiguous()
+        out = stages.project_views(
+            means, quats_raw, scales, opacities.contiguous(), views, fulls, intrinsics,
+            config.width, config.height, config.near, config.far, config.radius_clip, sh=sh,
+            sh_degree=sh_degree or 0, campos=campos, need_active=grad_enabled,
+            normalize_quats=True, tile_mode=config.tile_mode)
+        V = views.shape[0]
+        colors = out.colors if out.colors is not None else [means.new_empty((0, 3))] * V
+        sync = sharding.current_sync() if grad_enabled else None
+        if (sync is not None and any(ctx.needs_input_grad[:5])
+                and sync.claims(means, quats_raw, scales, opacities, sh)):
+            sync.register_view()
+        else:
+            sync = None
+        ctx.sync = sync
+        if grad_enabled and any(ctx.needs_input_grad[:8]):
+            ctx.save_for_backward(means, quats_raw, scales, views, fulls, intrinsics, out.radii,
+                                  sh, campos, out.active)
+            ctx.config, ctx.sh_degree = config, sh_degree or 0
+        ctx.mark_non_differentiable(out.radii, out.tile_counts, out.depths, out.means2d,
+                                    out.opacities, out.conics3)
+        if sh is None:
+            ctx.mark_non_differentiable(*colors)
+        ctx.set_materialize_grads(False)
+        return (*out.centers, *out.conics, *colors, out.radii, out.tile_counts, out.depths,
+                out.means2d, out.opacities, out.conics3)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx: Any, *grads):
+        means, quats_raw, scales, views, fulls, intrinsics, radii, sh, campos, active = \
+            ctx.saved_tensors
+        V, n = views.shape[0], len(means)
+        g_centers, g_conics, g_colors = grads[:V], grads[V:2 * V], grads[2 * V:3 * V]
+        needs = ctx.needs_input_grad
+        cfg, sync = ctx.config, ctx.sync
+        if sync is None and all(g is None for g in grads[:3 * V]):
+            return (None,) * 12
+        dev = means.device
+        g_centers = [torch.zeros((n, 2), device=dev) if g is None else g.contiguous()
+                     for g in g_centers]
+        g_conics = [torch.zeros((n, 4), device=dev) if g is None else g.contiguous()
+                    for g in g_conics]
+        if sync is not None:
+            buffers, accumulate, last = sync.begin_view()
+            gm, gq, gs, go = (buffers.get(k) for k in ("means", "quats", "scales", "opacities"))
+            gsh = buffers.get("sh")
+            if (gsh is None and sh is not None and ctx.sh_degree > 0
+                    and (gm is not None or needs[7])):
+                gsh = torch.empty_like(sh)  # direction gradient only; values unused
+        else:
+            accumulate, last = False, False
+            gm = torch.empty_like(means) if needs[0] else None
+            gq = torch.empty_like(quats_raw) if needs[1] else None
+            gs = torch.empty_like(scales) if needs[2] else None
+            go = means.new_empty(n) if needs[3] else None
+            gsh = None
+            if sh is not None and (needs[4] or (needs[0] and ctx.sh_degree > 0) or needs[7]):
+                gsh = torch.empty_like(sh)
+        gcol = None
+        if gsh is not None:
+            gcol = [torch.zeros((n, 3), device=dev) if g is None else g.contiguous()
+                    for g in g_colors]
+        want_cam = needs[5] or needs[6] or needs[7]
+        cams = means.new_zeros((V, 35)) if want_cam else None
+        K = 0 if sh is None else sh.shape[1]
+
+        def launch(lo: int, hi: int) -> None:
+            def rows(t):
+                return None if t is None else t[lo:hi]
+            pin = stages.Args()
+            if cams is None:
+                check(lib.splat_project_backward_views(
+                    V, hi - lo, pin(rows(means)), None, pin(rows(quats_raw)), pin(rows(scales)),
+                    pin(views), pin(fulls), pin(intrinsics), cfg.width, cfg.height,
+                    stages.pointer_table(r[lo:hi] for r in radii),
+                    stages.pointer_table(g[lo:hi] for g in g_centers),
+                    stages.pointer_table(g[lo:hi] for g in g_conics), ptr(rows(gm)),
+                    ptr(rows(gq)), ptr(rows(gs)), ptr(rows(go)), int(accumulate),
+                    ctx.sh_degree, K, pin(rows(sh)), pin(campos),
+                    stages.pointer_table(a[lo:hi] for a in active) if gsh is not None else None,
+                    stages.pointer_table(g[lo:hi] for g in gcol) if gsh is not None else None, 3,
+                    ptr(rows(gsh)), stream(dev)), "project_backward_views")
+                return
+            # pose gradients: the per-view kernel once per camera (its camera
+            # reduction), views after the first accumulating
+            for v in range(V):
+                check(lib.splat_project_backward_fused(
+                    hi - lo, pin(rows(means)), None, pin(rows(quats_raw)), pin(rows(scales)),
+                    pin(views[v]), pin(fulls[v]), pin(intrinsics[v]), cfg.width, cfg.height,
+                    pin(radii[v, lo:hi]), pin(g_centers[v][lo:hi]), pin(g_conics[v][lo:hi]),
+                    ptr(rows(gm)), ptr(rows(gq)), ptr(rows(gs)), ptr(rows(go)),
+                    int(accumulate or v > 0), ptr(cams[v]), ctx.sh_degree, K, pin(rows(sh)),
+                    pin(None if campos is None else campos[v]),
+                    pin(None if active is None or gsh is None else active[v, lo:hi]),
+                    pin(None if gcol is None else gcol[v][lo:hi]), 3, ptr(rows(gsh)),
+                    stream(dev)), "project_backward_fused")
+
+        if n and sync is not None and last:
+            for lo, hi in sharding.bucket_bounds(n, sync.buckets):
+                launch(lo, hi)
+                sync.reduce_range(lo, hi)
+        elif n:
+            launch(0, n)
+        if sync is not None:
+            if last:
+                sync.finish()
+            gm = gq = gs = go = gsh = None
+        gview = cams[:, :16].reshape(V, 4, 4) if needs[5] else None
+        gfull = cams[:, 16:32].reshape(V, 4, 4) if needs[6] else None
+        gcampos = cams[:, 32:35].clone() if needs[7] else None
+        return (gm, gq, gs, go, gsh if needs[4] else None, gview, gfull, gcampos, None, None,
+                None, None)
+
+
 class RenderView(torch.autograd.Function):
     """Blending of one view over pre-binned tiles (gs3d/autograd.py:19-171).
 

@@ -10,6 +10,7 @@ stream; tensors must be CUDA float32/int32.
 
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 
@@ -227,6 +228,67 @@ def project_fused(means, quats, scales, opacities, view, projection, intrinsics,
             ptr(active), ptr(m2d), ptr(mop), ptr(mcon), _tile_mode(tile_mode), _stream(means)),
             "project_forward_fused")
     return FusedProjection(state, colors, active, m2d, mop, mcon)
+
+
+@dataclass(slots=True)
+class ViewsProjection:
+    """project_views outputs: per-view tensors for the differentiable
+    outputs, stacked (views, n, ...) tensors for the rest."""
+    centers: list[Tensor]        # views x (n,2)
+    conics: list[Tensor]         # views x (n,4)
+    colors: list[Tensor] | None  # views x (n,3)
+    radii: Tensor                # (views,n) int32
+    tile_counts: Tensor          # (views,n) int32
+    depths: Tensor               # (views,n)
+    active: Tensor | None        # (views,n,3) uint8
+    means2d: Tensor              # (views,n,2)
+    opacities: Tensor            # (views,n)
+    conics3: Tensor              # (views,n,3)
+
+    def state(self, v: int) -> ProjectedGaussians:
+        return ProjectedGaussians(self.centers[v], self.conics[v], self.radii[v],
+                                  self.tile_counts[v], self.depths[v])
+
+
+def pointer_table(tensors) -> ctypes.Array:
+    """Host array of device addresses (one per view) for the C ABI."""
+    tensors = list(tensors)
+    return (ctypes.c_void_p * len(tensors))(*[t.data_ptr() for t in tensors])
+
+
+def project_views(means, quats, scales, opacities, views, projections, intrinsics, width,
+                  height, near, far, radius_clip, sh: Tensor | None = None, sh_degree: int = 0,
+                  campos: Tensor | None = None, need_active: bool = True,
+                  normalize_quats: bool = False, tile_mode: str = "radius") -> ViewsProjection:
+    """gs3d/api.py:132-189 for every camera of a batch in one launch
+    (splat_project_forward_views): bit-identical to one project_fused call
+    per camera, with each Gaussian's inputs and SH row read once.
+    views/projections (V,4,4), intrinsics (V,3,3), campos (V,3) or None."""
+    pin = Args()
+    V, n = views.shape[0], len(means)
+    dev = means.device
+    centers = [means.new_empty((n, 2)) for _ in range(V)]
+    conics = [means.new_empty((n, 4)) for _ in range(V)]
+    colors = [means.new_empty((n, 3)) for _ in range(V)] if sh is not None else None
+    radii = torch.empty((V, n), dtype=torch.int32, device=dev)
+    tiles = torch.empty((V, n), dtype=torch.int32, device=dev)
+    depths = means.new_empty((V, n))
+    active = (torch.empty((V, n, 3), dtype=torch.uint8, device=dev)
+              if sh is not None and need_active else None)
+    m2d, mop, mcon = means.new_empty((V, n, 2)), means.new_empty((V, n)), means.new_empty((V, n, 3))
+    if n and V:
+        sh_c = _c(sh)
+        check(lib.splat_project_forward_views(
+            V, n, pin(means), pin(quats), int(normalize_quats), pin(scales), pin(opacities),
+            pin(views), pin(projections), pin(intrinsics), width, height, float(near), _far(far),
+            float(radius_clip), pointer_table(centers), pointer_table(conics),
+            pointer_table(radii), pointer_table(tiles), pointer_table(depths), int(sh_degree),
+            sh_c.shape[1] if sh_c is not None else 0, ptr(sh_c), pin(campos),
+            pointer_table(colors) if colors is not None else None, 3,
+            pointer_table(active) if active is not None else None, pointer_table(m2d),
+            pointer_table(mop), pointer_table(mcon), _tile_mode(tile_mode), _stream(means)),
+            "project_forward_views")
+    return ViewsProjection(centers, conics, colors, radii, tiles, depths, active, m2d, mop, mcon)
 
 
 def metadata(state: ProjectedGaussians) -> dict[str, Tensor]:

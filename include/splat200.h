@@ -78,6 +78,26 @@ int splat_project_forward_fused(int n, const float* means, const float* quats,
                                 float* meta_opacities, float* meta_conics, int tile_mode,
                                 void* stream);
 
+/* gs3d/api.py:132-189 (the per-camera projection loop) as one launch: the
+ * Gaussian set projected for `views` cameras, each Gaussian's inputs and SH
+ * row read once.  viewmats/projs (views,4,4), Ks (views,3,3), campos
+ * (views,3) or NULL are stacked; outputs come through host arrays of
+ * `views` device pointers (a NULL table: that output is absent), each entry
+ * laid out as splat_project_forward_fused's.  Bit-identical to `views` calls
+ * of splat_project_forward_fused. */
+int splat_project_forward_views(int views, int n, const float* means, const float* quats,
+                                int normalize_quats, const float* scales,
+                                const float* opacities, const float* viewmats,
+                                const float* projs, const float* Ks, int width, int height,
+                                float near_plane, float far_plane, float radius_clip,
+                                float* const* centers, float* const* conics, int* const* radii,
+                                int* const* tiles, float* const* depths, int sh_degree,
+                                int sh_k, const float* sh, const float* campos,
+                                float* const* colors, int color_stride,
+                                unsigned char* const* active, float* const* meta_means2d,
+                                float* const* meta_opacities, float* const* meta_conics,
+                                int tile_mode, void* stream);
+
 /* splatting/metadata.py:34-70 prepare_metadata -> _prepare :12-31. */
 int splat_metadata(int n, const int* radii, const float* centers, const float* conics,
                    float* means2d, float* opacities, float* conics3, void* stream);
@@ -114,6 +134,25 @@ int splat_project_backward_fused(int n, const float* means, const float* quats,
                                  int sh_degree, int sh_k, const float* sh, const float* campos,
                                  const unsigned char* active, const float* grad_colors,
                                  int color_stride, float* grad_sh, void* stream);
+
+/* The backward of splat_project_forward_views (the per-view backward calls
+ * of gs3d/projection.py:357-428 + the SH VJP, summed over the views as
+ * autograd sums them): Gaussian inputs and SH rows read once, each
+ * gradient written once (accumulate: added).  Per-view inputs -- radii,
+ * grad_centers, grad_conics, active, grad_colors -- come through host
+ * arrays of `views` device pointers.  No camera gradients: use
+ * splat_project_backward_fused per view for those. */
+int splat_project_backward_views(int views, int n, const float* means, const float* quats,
+                                 const float* quats_raw, const float* scales,
+                                 const float* viewmats, const float* projs, const float* Ks,
+                                 int width, int height, const int* const* radii,
+                                 const float* const* grad_centers,
+                                 const float* const* grad_conics, float* grad_means,
+                                 float* grad_quats, float* grad_scales, float* grad_opacities,
+                                 int accumulate, int sh_degree, int sh_k, const float* sh,
+                                 const float* campos, const unsigned char* const* active,
+                                 const float* const* grad_colors, int color_stride,
+                                 float* grad_sh, void* stream);
 
 /* primitives/spherical_harmonics.py:18-59 _SphericalHarmonics.forward -> sh.py:44-79.
  * sh (n,sh_k,3), dirs (n,3), radii (n) or NULL -> colors (n,3), active (n,3) or NULL. */
