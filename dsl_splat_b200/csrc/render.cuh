@@ -328,7 +328,7 @@ SPLAT_DEV f32x2 sample_power2(float4 q, float dx, float dy0, float dy1) {
 // l / 8 + 4)).  Per candidate the exponent, exp, alpha and transmittance of
 // both pixels are computed as f32x2 pairs -- the same bits as the scalar
 // kernel -- and each pixel then blends, ends or skips on its own.
-template <int CHP>
+template <int CHP, bool STATS>
 __global__ void __launch_bounds__(kBlock / 2) render_forward2_kernel(RenderParams p) {
   extern __shared__ float4 s_dynamic[];  // the staged batch (sizeof(RenderShared<CHP>) bytes)
   RenderShared<CHP>& s = *reinterpret_cast<RenderShared<CHP>*>(s_dynamic);
@@ -346,9 +346,11 @@ __global__ void __launch_bounds__(kBlock / 2) render_forward2_kernel(RenderParam
   const float threshold = 1.0f / 255.0f;
   bool done0 = !inside0, done1 = !inside1;
   float T0 = 1.0f, T1 = 1.0f;
-  float color0[CHP], color1[CHP];
+  // colour of both pixels as f32x2 pairs: a pixel that does not blend the
+  // sample adds f * 0, which leaves its (never negative-zero) sum unchanged
+  f32x2 color2[CHP];
 #pragma unroll
-  for (int c = 0; c < CHP; ++c) color0[c] = color1[c] = 0.0f;
+  for (int c = 0; c < CHP; ++c) color2[c] = splat2(0.0f);
   int last0 = 0, last1 = 0;
   for (int begin = first; begin < last; begin += kBlock) {
     if (__syncthreads_count(done0 && done1) == static_cast<int>(blockDim.x)) break;
@@ -388,30 +390,28 @@ __global__ void __launch_bounds__(kBlock / 2) render_forward2_kernel(RenderParam
       const int position = begin - first + j + 1;
       // gs3d/render.py: a sample that would take T below 1e-4 ends the pixel
       // without being blended
-      if (accept0) {
-        if (n0 < W32(0.0001)) {
-          done0 = true;
-        } else {
+      const bool blend0 = accept0 && n0 >= W32(0.0001);
+      const bool blend1 = accept1 && n1 >= W32(0.0001);
+      done0 = done0 || (accept0 && !blend0);
+      done1 = done1 || (accept1 && !blend1);
+      const f32x2 w2 = pack2(blend0 ? w0 : 0.0f, blend1 ? w1 : 0.0f);
 #pragma unroll
-          for (int c = 0; c < CHP; ++c) color0[c] = __fmaf_rn(f[c], w0, color0[c]);
-          if (p.stat_count) observe(p, s.id[j], y0 * p.width + x, w0);
-          T0 = n0;
-          last0 = position;
-        }
+      for (int c = 0; c < CHP; ++c) color2[c] = fma2(splat2(f[c]), w2, color2[c]);
+      if (blend0) {
+        if (STATS) observe(p, s.id[j], y0 * p.width + x, w0);
+        T0 = n0;
+        last0 = position;
       }
-      if (accept1) {
-        if (n1 < W32(0.0001)) {
-          done1 = true;
-        } else {
-#pragma unroll
-          for (int c = 0; c < CHP; ++c) color1[c] = __fmaf_rn(f[c], w1, color1[c]);
-          if (p.stat_count) observe(p, s.id[j], y1 * p.width + x, w1);
-          T1 = n1;
-          last1 = position;
-        }
+      if (blend1) {
+        if (STATS) observe(p, s.id[j], y1 * p.width + x, w1);
+        T1 = n1;
+        last1 = position;
       }
     }
   }
+  float color0[CHP], color1[CHP];
+#pragma unroll
+  for (int c = 0; c < CHP; ++c) unpack2(color2[c], color0[c], color1[c]);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const bool inside = i ? inside1 : inside0;

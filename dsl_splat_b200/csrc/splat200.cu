@@ -254,9 +254,14 @@ void launch_render(const RenderParams& p, bool backward, cudaStream_t s) {
   } else if (CHP <= 8) {
     // up to eight channels: two pixels per lane with paired arithmetic
     if (smem > 32 * 1024)
-      cudaFuncSetAttribute(render_forward2_kernel<CHP>,
+      cudaFuncSetAttribute(p.stat_count ? render_forward2_kernel<CHP, true>
+                                        : render_forward2_kernel<CHP, false>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    render_forward2_kernel<CHP><<<tiles, kBlock / 2, smem, counted(s)>>>(p);
+    // statistics requests get their own instantiation (no per-sample test)
+    if (p.stat_count)
+      render_forward2_kernel<CHP, true><<<tiles, kBlock / 2, smem, counted(s)>>>(p);
+    else
+      render_forward2_kernel<CHP, false><<<tiles, kBlock / 2, smem, counted(s)>>>(p);
   } else {
     if (smem > 32 * 1024)
       cudaFuncSetAttribute(render_forward_kernel<CHP>,
