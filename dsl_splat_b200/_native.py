@@ -55,14 +55,15 @@ SIGNATURES: dict[str, tuple] = {
     "splat_bin_pairs_workspace_bytes": (_Z, [_L, _I, _I, _I]),
     "splat_bin_prepare": (_I, [_I, _P, _P, _P, _P, _P, _I, _I, _I, _P, _Z, _P, _P, _P]),
     "splat_bin_emit": (_I, [_I, _L, _I, _I, _I, _P, _P, _P, _P, _Z, _P, _Z, _P, _P]),
+    "splat_tile_order": (_I, [_P, _I, _P, _P]),
     "splat_render_forward": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P, _I, _I, _I,
-                                  _P, _P, _I, _I, _P, _P, _P, _P]),
+                                  _P, _P, _I, _I, _P, _P, _P, _P, _P]),
     "splat_render_forward_statistics": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P,
                                              _I, _I, _I, _P, _P, _I, _I, _P, _P, _P, _I, _I,
-                                             _P, _P, _P, _P]),
+                                             _P, _P, _P, _P, _P]),
     "splat_render_backward": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P, _I, _I, _I,
                                    _P, _P, _P, _P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _I,
-                                   _P]),
+                                   _P, _P]),
     "splat_debug_expf": (_I, [_I, _P, _P, _P, _P]),
 }
 

@@ -28,6 +28,7 @@ namespace splat {
 struct RenderParams {
   int width, height, gx;
   const int* ranges;      // (T,2) [start, end) into ids
+  const int* tile_order;  // (T) tile of block b (heaviest first), or null: block b = tile b
   const int* ids;         // sorted Gaussian ids
   int num_ids;            // length of ids (ranges are clamped to it)
   const float* centers;   // (n,2)
@@ -92,6 +93,58 @@ struct RenderShared {
   float4 bound[kBlock];    // EllipseBound ra, rc, level (w unused)
   float4 feat[kBlock][CHP / 4];  // channels of one slot, read with vector loads
 };
+
+// The tile this block blends: blocks run heaviest tile first when the
+// caller passes tile_order (the order only changes which block finishes
+// when; every block writes its own tile).
+SPLAT_DEV int block_tile(const RenderParams& p) {
+  return p.tile_order ? __ldg(p.tile_order + blockIdx.x) : static_cast<int>(blockIdx.x);
+}
+
+// Tiles by descending pair count (ranges), for RenderParams::tile_order: a
+// counting sort of the counts scaled into 256 buckets (order inside a bucket
+// is arbitrary).  One block of 1024 threads.
+__global__ void __launch_bounds__(1024)
+    tile_order_kernel(const int* __restrict__ ranges, int T, int* __restrict__ order) {
+  __shared__ int s_bucket[256];
+  __shared__ int s_max;
+  if (threadIdx.x == 0) s_max = 0;
+  for (int b = threadIdx.x; b < 256; b += blockDim.x) s_bucket[b] = 0;
+  __syncthreads();
+  int local = 0;
+  for (int t = threadIdx.x; t < T; t += blockDim.x)
+    local = max(local, ranges[2 * t + 1] - ranges[2 * t]);
+  local = __reduce_max_sync(0xffffffffu, local);
+  if ((threadIdx.x & 31) == 0) atomicMax(&s_max, local);
+  __syncthreads();
+  const int shift = max(0, 32 - __clz(s_max) - 8);  // the largest count maps below 256
+  for (int t = threadIdx.x; t < T; t += blockDim.x)
+    atomicAdd(&s_bucket[255 - ((ranges[2 * t + 1] - ranges[2 * t]) >> shift)], 1);
+  __syncthreads();
+  if (threadIdx.x < 32) {  // exclusive scan of the 256 buckets by one warp
+    int v[8], sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      v[k] = s_bucket[threadIdx.x * 8 + k];
+      sum += v[k];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (threadIdx.x >= o) incl += y;
+    }
+    int run = incl - sum;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      s_bucket[threadIdx.x * 8 + k] = run;
+      run += v[k];
+    }
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < T; t += blockDim.x)
+    order[atomicAdd(&s_bucket[255 - ((ranges[2 * t + 1] - ranges[2 * t]) >> shift)], 1)] = t;
+}
 
 // All CHP channels of staged slot j (padding channels are zero).
 template <int CHP>
@@ -246,7 +299,7 @@ __global__ void __launch_bounds__(kBlock) render_forward_kernel(RenderParams p) 
   RenderShared<CHP>& s = *reinterpret_cast<RenderShared<CHP>*>(s_dynamic);
   __shared__ uint8_t s_list[kBlock / 32][kBlock];
   uint8_t* list = s_list[threadIdx.x >> 5];
-  const int tile = blockIdx.x;
+  const int tile = block_tile(p);
   const PixelSlot<1> ps = pixel_slot<1>(tile, p.gx);
   const int x = ps.x, y = ps.y;
   const bool inside = x < p.width && y < p.height;
@@ -334,7 +387,7 @@ __global__ void __launch_bounds__(kBlock / 2) render_forward2_kernel(RenderParam
   RenderShared<CHP>& s = *reinterpret_cast<RenderShared<CHP>*>(s_dynamic);
   __shared__ uint8_t s_list[kBlock / 64][kBlock];
   uint8_t* list = s_list[threadIdx.x >> 5];
-  const int tile = blockIdx.x;
+  const int tile = block_tile(p);
   const PixelSlot<2> ps = pixel_slot<2>(tile, p.gx);
   const int x = ps.x, y0 = ps.y, y1 = ps.y + 4;
   const bool inside0 = x < p.width && y0 < p.height;
@@ -596,7 +649,7 @@ __global__ void __launch_bounds__(kBlock / PX) render_backward_kernel(RenderPara
   // grp (the same for every warp); null for odd lanes and unused values
   __shared__ GradientSlot s_dst[kGroups][32];
   uint8_t* list = s_list[threadIdx.x >> 5];
-  const int tile = blockIdx.x;
+  const int tile = block_tile(p);
   const int wl = threadIdx.x & 31;
   const PixelSlot<PX> ps = pixel_slot<PX>(tile, p.gx);
   const int first = max(p.ranges[2 * tile], 0);
@@ -802,7 +855,7 @@ __global__ void __launch_bounds__(kBlock / 2) render_backward2_kernel(RenderPara
   // for every warp); null for odd lanes and unused values
   __shared__ GradientSlot s_dst[32];
   uint8_t* list = s_list[threadIdx.x >> 5];
-  const int tile = blockIdx.x;
+  const int tile = block_tile(p);
   const int wl = threadIdx.x & 31;
   const PixelSlot<2> ps = pixel_slot<2>(tile, p.gx);
   const int first = max(p.ranges[2 * tile], 0);

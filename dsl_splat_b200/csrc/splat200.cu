@@ -956,13 +956,21 @@ int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
 
 // ---- blending -----------------------------------------------------------------
 
+int splat_tile_order(const int* ranges, int tiles, int* order, void* stream) {
+  if (tiles < 0) return fail(kInvalidArgument, "bad tile count");
+  if (tiles == 0) return kOk;
+  if (!ranges || !order) return fail(kInvalidArgument, "null ranges or order");
+  tile_order_kernel<<<1, 1024, 0, counted(as_stream(stream))>>>(ranges, tiles, order);
+  return check_launch("tile_order");
+}
+
 int splat_render_forward_statistics(
     int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
     const float* centers, const float* conics, const float* feat_a, int ch_a, int stride_a,
     const float* feat_b, int ch_b, int stride_b, int append_one, const float* background,
     float* image, int pix_stride, int ch_stride, float* alpha_image, float* final_t,
     int* contributors, int stat_count, int stat_sum_mask, const float* stat_pixels,
-    int* stat_counts, float* stat_sums, void* stream) {
+    int* stat_counts, float* stat_sums, const int* tile_order, void* stream) {
   if (width <= 0 || height <= 0 || ch_a < 0 || ch_b < 0 || (ch_b > 0 && !feat_b) || n < 0 ||
       num_ids < 0 || num_ids >= (1LL << 31))
     return fail(kInvalidArgument, "bad render sizes");
@@ -975,6 +983,7 @@ int splat_render_forward_statistics(
   p.height = height;
   p.gx = (width + 15) / 16;
   p.ranges = ranges;
+  p.tile_order = tile_order;
   p.ids = ids;
   p.num_ids = static_cast<int>(num_ids);
   p.centers = centers;
@@ -1011,12 +1020,13 @@ int splat_render_forward(int width, int height, const int* ranges, const int* id
                          const float* feat_a, int ch_a, int stride_a, const float* feat_b,
                          int ch_b, int stride_b, int append_one, const float* background,
                          float* image, int pix_stride, int ch_stride, float* alpha_image,
-                         float* final_t, int* contributors, void* stream) {
+                         float* final_t, int* contributors, const int* tile_order,
+                         void* stream) {
   return splat_render_forward_statistics(width, height, ranges, ids, num_ids, n, centers, conics,
                                          feat_a, ch_a, stride_a, feat_b, ch_b, stride_b,
                                          append_one, background, image, pix_stride, ch_stride,
                                          alpha_image, final_t, contributors, 0, 0, nullptr,
-                                         nullptr, nullptr, stream);
+                                         nullptr, nullptr, tile_order, stream);
 }
 
 int splat_render_backward(int width, int height, const int* ranges, const int* ids,
@@ -1028,7 +1038,7 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
                           int up_ch_stride, const float* upstream_alpha, int alpha_pix_stride,
                           float* grad_centers, float* grad_conics,
                           float* grad_a, float* grad_b, float* abs_centers, int constant_tail,
-                          void* stream) {
+                          const int* tile_order, void* stream) {
   if (width <= 0 || height <= 0 || ch_a < 0 || ch_b < 0 || (ch_b > 0 && !feat_b) || n < 0 ||
       num_ids < 0 || num_ids >= (1LL << 31))
     return fail(kInvalidArgument, "bad render sizes");
@@ -1037,6 +1047,7 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
   p.height = height;
   p.gx = (width + 15) / 16;
   p.ranges = ranges;
+  p.tile_order = tile_order;
   p.ids = ids;
   p.num_ids = static_cast<int>(num_ids);
   p.n_gaussians = n;

@@ -456,6 +456,19 @@ def bin_and_sort(state: ProjectedGaussians, width: int, height: int,
 
 # ---- blending ----------------------------------------------------------------
 
+def tile_order(bins: dict) -> Tensor:
+    """The blend's block schedule for these bins: tiles by descending pair
+    count (splat_tile_order), computed once per bins dict and cached in it."""
+    order = bins.get("tile_order")
+    if order is None:
+        ranges = bins["ranges"]
+        order = torch.empty(len(ranges), dtype=torch.int32, device=ranges.device)
+        check(lib.splat_tile_order(ptr(ranges), len(ranges), ptr(order),
+                                   nv.stream(ranges.device)), "tile_order")
+        bins["tile_order"] = order
+    return order
+
+
 def _features(feat_a: Tensor, feat_b: Tensor | None):
     a = feat_a.contiguous()
     b = None if feat_b is None else feat_b.contiguous()
@@ -499,7 +512,8 @@ def render(state: ProjectedFootprint, bins: dict, feat_a: Tensor, feat_b: Tensor
             len(state.centers), pin(state.centers),
             pin(state.conics), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
             pin(background), ptr(image), pix_stride, ch_stride, ptr(alpha),
-            ptr(out.transmittance), ptr(out.contributors), *stat, nv.stream(dev)), "render_forward")
+            ptr(out.transmittance), ptr(out.contributors), *stat, ptr(tile_order(bins)),
+            nv.stream(dev)), "render_forward")
     return out
 
 
@@ -549,5 +563,6 @@ def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
             pin(state.conics), ptr(a), ca, ca, ptr(b), cb, cb, int(append_one),
             pin(background), pin(final_t), pin(contributors),
             ptr(g), pix_stride, ch_stride, ptr(g_alpha), alpha_stride, ptr(centers), ptr(conics), ptr(ga),
-            ptr(gb), ptr(absolute), constant_tail, nv.stream(a.device)), "render_backward")
+            ptr(gb), ptr(absolute), constant_tail, ptr(tile_order(bins)), nv.stream(a.device)),
+            "render_backward")
     return centers, conics, ga, gb, absolute

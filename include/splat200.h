@@ -213,6 +213,11 @@ int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
                    size_t workspace_bytes, void* pairs_workspace, size_t pairs_workspace_bytes,
                    int* ids, void* stream);
 
+/* Scheduling order for the blend kernels: the T tiles by descending pair
+ * count (ranges[t][1] - ranges[t][0]), written to order (T).  No reference
+ * counterpart (the reference launches tiles in index order). */
+int splat_tile_order(const int* ranges, int tiles, int* order, void* stream);
+
 /* gs3d/render.py:359-406 render -> evaluate :41-125.  Blended channels are
  * feat_a's ch_a columns (row stride stride_a), then feat_b's ch_b columns,
  * then (append_one) a constant 1 -- the reference's cat([features, extras,
@@ -223,13 +228,17 @@ int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
  * only), receives the constant channel -- the alpha output -- instead of
  * image, so colour and alpha are separate dense buffers.  ids holds num_ids
  * entries (tile ranges are clamped to it) of Gaussian indices in [0, n).  At
- * most 32 channels. */
+ * most 32 channels.  tile_order: NULL, or the (T) permutation from
+ * splat_tile_order -- block b then blends tile tile_order[b], so the heaviest
+ * tiles start first (same outputs, shorter tail; also for the two calls
+ * below). */
 int splat_render_forward(int width, int height, const int* ranges, const int* ids,
                          long long num_ids, int n, const float* centers, const float* conics,
                          const float* feat_a, int ch_a, int stride_a, const float* feat_b,
                          int ch_b, int stride_b, int append_one, const float* background,
                          float* image, int pix_stride, int ch_stride, float* alpha_image,
-                         float* final_t, int* contributors, void* stream);
+                         float* final_t, int* contributors, const int* tile_order,
+                         void* stream);
 
 /* gs3d/render.py:129-169 render with contribution statistics (statistics.py:
  * 47-73, 393-418): as splat_render_forward, plus stat_count requests whose
@@ -244,7 +253,7 @@ int splat_render_forward_statistics(
     const float* feat_b, int ch_b, int stride_b, int append_one, const float* background,
     float* image, int pix_stride, int ch_stride, float* alpha_image, float* final_t,
     int* contributors, int stat_count, int stat_sum_mask, const float* stat_pixels,
-    int* stat_counts, float* stat_sums, void* stream);
+    int* stat_counts, float* stat_sums, const int* tile_order, void* stream);
 
 /* gs3d/render.py:409-463 backward -> :221-354.  Gradients are ADDED into
  * grad_centers (n,2), grad_conics (n,4), grad_a (n,ch_a), grad_b (n,ch_b)
@@ -262,7 +271,7 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
                           int up_ch_stride, const float* upstream_alpha, int alpha_pix_stride,
                           float* grad_centers, float* grad_conics,
                           float* grad_a, float* grad_b, float* abs_centers, int constant_tail,
-                          void* stream);
+                          const int* tile_order, void* stream);
 
 /* Diagnostic: ours[i] = the blend's exp, cuda_exp[i] = CUDA expf, for x (n). */
 int splat_debug_expf(int n, const float* x, float* ours, float* cuda_exp, void* stream);

@@ -61,7 +61,7 @@ def test_invalid_arguments_fail_before_any_launch():
     from dsl_splat_b200._native import lib
 
     assert lib.splat_render_forward(0, 10, None, None, 0, 0, None, None, None, 3, 3, None, 0, 0,
-                                    1, None, None, 4, 1, None, None, None, None) == -1
+                                    1, None, None, 4, 1, None, None, None, None, None) == -1
     assert b"bad render sizes" in lib.splat_last_error()
     assert lib.splat_bin_emit(10, 1 << 31, 64, 64, 0, None, None, None, None, 0, None, 0, None,
                               None) == -4

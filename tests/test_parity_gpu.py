@@ -568,3 +568,41 @@ def test_project_views_matches_per_view(deg, views):
     for name, o, w in zip(("means", "quats", "scales", "opacities", "sh"), outs, want):
         assert torch.isfinite(o).all(), name
         assert rel_l2(o.double().cpu().numpy(), w.double().cpu().numpy()) <= 1e-5, name
+
+
+def test_tile_order_schedule():
+    """splat_tile_order is a permutation of the tiles by descending pair
+    count (within its 256 count buckets), and blending in that block order
+    gives the same image, transmittance and contributors (bit for bit) and
+    the same gradients as index order."""
+    p = Prepared(_scene("c1_small"))
+    out = p.project()
+    bins = stages.bin_and_sort(out.state, p.W, p.H)
+    order = stages.tile_order(bins).cpu().numpy()
+    counts = (bins["ranges"][:, 1] - bins["ranges"][:, 0]).cpu().numpy()
+    assert sorted(order.tolist()) == list(range(len(counts)))
+    shift = max(0, int(counts.max()).bit_length() - 8)
+    buckets = counts[order] >> shift
+    assert (np.diff(buckets) <= 0).all()
+    d = _dev()
+    bg = torch.zeros(4, device=d)
+    ref = stages.render(out.state, dict(ranges=bins["ranges"], point_list=bins["point_list"],
+                                        tile_order=torch.arange(len(counts), dtype=torch.int32,
+                                                                device=d)),
+                        out.colors, None, True, bg, p.W, p.H)
+    got = stages.render(out.state, bins, out.colors, None, True, bg, p.W, p.H)
+    assert torch.equal(got.features, ref.features)
+    assert torch.equal(got.transmittance, ref.transmittance)
+    assert torch.equal(got.contributors, ref.contributors)
+    up = torch.randn_like(got.features)
+    g_ref = stages.render_backward(out.state, dict(ranges=bins["ranges"],
+                                                   point_list=bins["point_list"],
+                                                   tile_order=torch.arange(
+                                                       len(counts), dtype=torch.int32, device=d)),
+                                   out.colors, None, True, bg, ref.transmittance,
+                                   ref.contributors, up, p.W, p.H, constant_tail=1)
+    g_got = stages.render_backward(out.state, bins, out.colors, None, True, bg,
+                                   got.transmittance, got.contributors, up, p.W, p.H,
+                                   constant_tail=1)
+    for a, b in zip(g_got[:3], g_ref[:3]):
+        assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) <= 1e-5
