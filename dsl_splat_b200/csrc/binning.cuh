@@ -244,13 +244,15 @@ struct EmitLoader {
 
 // THREADS >= 256: the first 256 threads own one digit each in the look-back;
 // larger blocks shorten the look-back chain at the cost of fewer blocks.
-template <class Loader, bool WRITE_KEYS, int THREADS = kSortBlock>
+// ITEMS keys per thread: fewer make more, shorter tiles (more blocks in
+// flight and a shorter ranking loop per block, a longer look-back chain).
+template <class Loader, bool WRITE_KEYS, int THREADS = kSortBlock, int ITEMS = kSortItems>
 __global__ void __launch_bounds__(THREADS)
     onesweep_kernel(Loader ld, uint32_t n, int shift, const uint32_t* __restrict__ digit_offsets,
                     uint32_t* __restrict__ status, uint32_t* __restrict__ counter,
                     uint32_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out) {
   constexpr int kWarps = THREADS / 32;
-  constexpr uint32_t kTile = static_cast<uint32_t>(THREADS) * kSortItems;
+  constexpr uint32_t kTile = static_cast<uint32_t>(THREADS) * ITEMS;
   static_assert(THREADS >= kRadix && THREADS % 32 == 0, "one thread per digit");
   __shared__ uint32_t s_hist[kWarps][kRadix];
   __shared__ uint32_t s_base[kRadix];
@@ -265,11 +267,11 @@ __global__ void __launch_bounds__(THREADS)
   const uint32_t end = min(base + kTile, n);
   ld.prepare(base, end, s_ld);
 
-  uint32_t keys[kSortItems], vals[kSortItems], rank[kSortItems];
+  uint32_t keys[ITEMS], vals[ITEMS], rank[ITEMS];
   const uint32_t lt = lanemask_lt();
 #pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
-    const uint32_t idx = base + warp * (32 * kSortItems) + r * 32 + lane;
+  for (int r = 0; r < ITEMS; ++r) {
+    const uint32_t idx = base + warp * (32 * ITEMS) + r * 32 + lane;
     const bool valid = idx < end;
     uint32_t key = 0u, val = 0u;
     if (valid) ld.load(idx, s_ld, key, val);
@@ -325,7 +327,7 @@ __global__ void __launch_bounds__(THREADS)
   __syncthreads();
 
 #pragma unroll
-  for (int r = 0; r < kSortItems; ++r) {
+  for (int r = 0; r < ITEMS; ++r) {
     if (rank[r] == 0xFFFFFFFFu) continue;
     const uint32_t d = (keys[r] >> shift) & 255u;
     const uint32_t pos = s_base[d] + s_hist[warp][d] + rank[r];

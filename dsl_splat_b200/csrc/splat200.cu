@@ -121,6 +121,13 @@ struct BinLayout {
   size_t bytes;
 };
 
+// Depth passes: 256-thread onesweep blocks of kDepthItems keys per thread.
+constexpr int kDepthThreads = 256;
+constexpr int kDepthItems = 8;
+size_t depth_tiles(long long n) {
+  return static_cast<size_t>(blocks_for(n > 0 ? n : 1, kDepthThreads * kDepthItems));
+}
+
 BinLayout bin_layout(long long n, int width, int height, int tile_mode) {
   const int gx = (width + 15) / 16, gy = (height + 15) / 16;
   const size_t sort_tiles = static_cast<size_t>(blocks_for(n > 0 ? n : 1, kSortTile));
@@ -143,7 +150,7 @@ BinLayout bin_layout(long long n, int width, int height, int tile_mode) {
   L.zero_begin = o;
   L.depth_hist = take(4 * 4 * kRadix);
   L.diff = take(plan.use ? 0 : 4 * static_cast<size_t>(gx + 1) * (gy + 1));
-  L.depth_status = take(4 * 4 * sort_tiles * kRadix);
+  L.depth_status = take(4 * 4 * depth_tiles(n) * kRadix);
   L.counters = take(4 * 8);
   L.totals = take(8 * 4);
   L.zero_end = o;
@@ -788,11 +795,10 @@ int splat_bin_prepare(int n, const float* centers, const float* conics, const in
   uint32_t* depth_digits = at<uint32_t>(ws, L.depth_digits);
   uint32_t* tile_digits = at<uint32_t>(ws, L.tile_digits);
   const unsigned sort_tiles = blocks_for(n, kSortTile);
-  // depth passes: 256-thread onesweep blocks (4,096 keys each); 1024-thread
-  // blocks shorten the look-back chain but leave most SMs idle at 1M keys
-  // (measured 36 vs 28 us per pass)
-  constexpr int kDepthThreads = 256;
-  const unsigned depth_tiles = blocks_for(n, kDepthThreads * kSortItems);
+  // depth passes: 256-thread onesweep blocks of kDepthItems keys per thread
+  // (1024-thread blocks of 16 measured 36 us per pass at 1M keys, 256 x 16
+  // 28 us: at this size more blocks in flight beat a shorter look-back chain)
+  const unsigned dtiles = static_cast<unsigned>(depth_tiles(n));
   const ChunkPlan plan = chunk_plan(n, gx, gy, tile_mode);
   if (plan.use) diff = nullptr;
   const int sms = sm_count();
@@ -806,10 +812,10 @@ int splat_bin_prepare(int n, const float* centers, const float* conics, const in
   for (int pass = 0; pass < 4; ++pass) {
     const bool even = (pass % 2) == 0;
     KeyValueLoader ld{even ? keys_a : keys_b, even ? vals_a : vals_b};
-    onesweep_kernel<KeyValueLoader, true, kDepthThreads>
-        <<<depth_tiles, kDepthThreads, 0, counted(s)>>>(
+    onesweep_kernel<KeyValueLoader, true, kDepthThreads, kDepthItems>
+        <<<dtiles, kDepthThreads, 0, counted(s)>>>(
             ld, static_cast<uint32_t>(n), 8 * pass, depth_digits + pass * kRadix,
-            status + static_cast<size_t>(pass) * depth_tiles * kRadix, counters + pass,
+            status + static_cast<size_t>(pass) * dtiles * kRadix, counters + pass,
             even ? keys_b : keys_a, even ? vals_b : vals_a);
   }
   if (plan.use) {

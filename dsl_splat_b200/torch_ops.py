@@ -16,6 +16,8 @@ Operator <- reference code it stands for:
   cameras_prepare     splatting/cameras.py:133-188 (camera_kernels.py:11-66)
   project             gs3d/projection.py:309-354 (tile counts for tile_mode)
   project_backward    gs3d/projection.py:357-428
+  project_views       gs3d/api.py:132-189 (the per-camera projection loop, one launch)
+  project_views_backward  the per-camera backward calls of that loop, summed
   sh_forward          primitives/spherical_harmonics.py:18-59 (sh.py:44-79)
   sh_backward         primitives/spherical_harmonics.py:61-101 (sh.py:82-138)
   bin_and_sort        splatting/binning.py:171-217
@@ -115,6 +117,90 @@ def _project_backward(ctx, g_centers, g_conics, g_radii, g_tiles, g_depths):
 
 
 project.register_autograd(_project_backward, setup_context=_project_setup)
+
+
+@torch.library.custom_op(f"{_NS}::project_views", mutates_args=())
+def project_views(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor,
+                  views: Tensor, fulls: Tensor, Ks: Tensor, width: int, height: int, near: float,
+                  far: float, radius_clip: float, sh: Tensor, sh_degree: int, campos: Tensor,
+                  tile_mode: str) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """All cameras (V) of one Gaussian set in one launch (raw quaternions are
+    normalised in-kernel).  Returns stacked (V, n, ...) centres, conics,
+    colours, radii, tile counts, depths and the active mask."""
+    out = stages.project_views(means, quats, scales, opacities, views, fulls, Ks, width, height,
+                               near, far, radius_clip, sh=sh, sh_degree=sh_degree,
+                               campos=campos, normalize_quats=True, tile_mode=tile_mode)
+    return (torch.stack(out.centers), torch.stack(out.conics), torch.stack(out.colors),
+            out.radii, out.tile_counts, out.depths, out.active)
+
+
+@project_views.register_fake
+def _(means, quats, scales, opacities, views, fulls, Ks, width, height, near, far, radius_clip,
+      sh, sh_degree, campos, tile_mode):
+    V, n = views.shape[0], means.shape[0]
+    return (means.new_empty((V, n, 2)), means.new_empty((V, n, 4)), means.new_empty((V, n, 3)),
+            means.new_empty((V, n), dtype=torch.int32), means.new_empty((V, n), dtype=torch.int32),
+            means.new_empty((V, n)), means.new_empty((V, n, 3), dtype=torch.uint8))
+
+
+@torch.library.custom_op(f"{_NS}::project_views_backward", mutates_args=())
+def project_views_backward(means: Tensor, quats: Tensor, scales: Tensor, views: Tensor,
+                           fulls: Tensor, Ks: Tensor, width: int, height: int, radii: Tensor,
+                           sh: Tensor, sh_degree: int, campos: Tensor, active: Tensor,
+                           grad_centers: Tensor, grad_conics: Tensor, grad_colors: Tensor
+                           ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Gradients of means, raw quaternions, scales, opacities and SH summed
+    over the V cameras (splat_project_backward_views)."""
+    V, n = views.shape[0], means.shape[0]
+    outs = [torch.empty_like(t) for t in (means, quats, scales)]
+    outs.append(means.new_empty(n))
+    outs.append(torch.empty_like(sh))
+    gc, gq, gcol = grad_centers.contiguous(), grad_conics.contiguous(), grad_colors.contiguous()
+    if n and V:
+        pin = stages.Args()
+        from ._native import check, lib, stream
+        check(lib.splat_project_backward_views(
+            V, n, pin(means), None, pin(quats), pin(scales), pin(views), pin(fulls), pin(Ks),
+            width, height, stages.pointer_table(radii), stages.pointer_table(gc),
+            stages.pointer_table(gq), *[o.data_ptr() for o in outs[:4]], 0, sh_degree,
+            sh.shape[1], pin(sh), pin(campos), stages.pointer_table(active),
+            stages.pointer_table(gcol), 3, outs[4].data_ptr(), stream(means.device)),
+            "project_views_backward")
+    return tuple(outs)
+
+
+@project_views_backward.register_fake
+def _(means, quats, scales, views, fulls, Ks, width, height, radii, sh, sh_degree, campos,
+      active, grad_centers, grad_conics, grad_colors):
+    return (torch.empty_like(means), torch.empty_like(quats), torch.empty_like(scales),
+            means.new_empty(means.shape[0]), torch.empty_like(sh))
+
+
+def _project_views_setup(ctx, inputs, output):
+    (means, quats, scales, opacities, views, fulls, Ks, width, height, near, far, radius_clip,
+     sh, sh_degree, campos, tile_mode) = inputs
+    ctx.save_for_backward(means, quats, scales, views, fulls, Ks, sh, campos, output[3],
+                          output[6])
+    ctx.args = (width, height, sh_degree)
+
+
+def _project_views_backward(ctx, g_centers, g_conics, g_colors, *unused):
+    means, quats, scales, views, fulls, Ks, sh, campos, radii, active = ctx.saved_tensors
+    width, height, sh_degree = ctx.args
+    V, n = views.shape[0], means.shape[0]
+
+    def zeros(g, k):
+        return means.new_zeros((V, n, k)) if g is None else g
+
+    grads = torch.ops.splat200.project_views_backward(
+        means, quats, scales, views, fulls, Ks, width, height, radii, sh, sh_degree, campos,
+        active, zeros(g_centers, 2), zeros(g_conics, 4), zeros(g_colors, 3))
+    gm, gq, gs, go, gsh = grads
+    return (gm, gq, gs, go, None, None, None, None, None, None, None, None, gsh, None, None,
+            None)
+
+
+project_views.register_autograd(_project_views_backward, setup_context=_project_views_setup)
 
 
 # ---- spherical harmonics ------------------------------------------------------------
@@ -247,5 +333,6 @@ def _render_backward(ctx, g_image, g_alpha, g_t, g_contrib):
 
 render.register_autograd(_render_backward, setup_context=_render_setup)
 
-OPERATORS = ("cameras_prepare", "project", "project_backward", "sh_forward", "sh_backward",
-             "bin_and_sort", "render", "render_backward")
+OPERATORS = ("cameras_prepare", "project", "project_backward", "project_views",
+             "project_views_backward", "sh_forward", "sh_backward", "bin_and_sort", "render",
+             "render_backward")

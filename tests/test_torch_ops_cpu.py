@@ -57,3 +57,16 @@ def test_fake_shapes():
         assert colors.shape == (n, 3) and active.dtype == torch.uint8
         g_coeffs, g_dirs = torch.ops.splat200.sh_backward(coeffs, dirs, 3, radii, active, colors)
         assert g_coeffs.shape == coeffs.shape and g_dirs.shape == (n, 3)
+        V = 3
+        views, fulls, Ks = (torch.empty(V, 4, 4, **f32), torch.empty(V, 4, 4, **f32),
+                            torch.empty(V, 3, 3, **f32))
+        campos = torch.empty(V, 3, **f32)
+        out = torch.ops.splat200.project_views(means, quats, scales, opac, views, fulls, Ks, W,
+                                               H, 0.2, float("inf"), 0.0, coeffs, 3, campos,
+                                               "radius")
+        assert [tuple(t.shape) for t in out] == [(V, n, 2), (V, n, 4), (V, n, 3), (V, n),
+                                                 (V, n), (V, n), (V, n, 3)]
+        grads = torch.ops.splat200.project_views_backward(
+            means, quats, scales, views, fulls, Ks, W, H, out[3], coeffs, 3, campos, out[6],
+            out[0], out[1], out[2])
+        assert [tuple(g.shape) for g in grads] == [(n, 3), (n, 4), (n, 3), (n,), (n, 16, 3)]

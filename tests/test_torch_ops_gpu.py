@@ -93,3 +93,36 @@ def test_ops_trace_with_torch_compile():
     compiled = torch.compile(forward, fullgraph=True, backend="eager")(means, q, scales, opac,
                                                                         sh)
     assert torch.equal(eager[0], compiled[0]) and torch.equal(eager[1], compiled[1])
+
+
+def test_project_views_op_and_autograd():
+    """torch.ops.splat200.project_views returns the stage's stacked outputs,
+    and its autograd formula calls project_views_backward with the upstream
+    gradients of the stacked centres, conics and colours."""
+    from dsl_splat_b200.scenes import make_scene
+    d = torch.device("cuda", 0)
+    s = make_scene(2, n=5000, width=200, height=130, cameras=3)
+    vm, Ks = s.viewmats.to(d), s.Ks.to(d)
+    full, _, campos = stages.cameras_prepare(vm, Ks, s.width, s.height, True)
+    leaves = [t.to(d).requires_grad_(True) for t in (s.means, s.quats, s.scales, s.opacities,
+                                                      s.sh_coeffs)]
+    means, quats, scales, opac, sh = leaves
+    out = torch.ops.splat200.project_views(means, quats, scales, opac, vm, full, Ks, s.width,
+                                           s.height, 0.2, float("inf"), 0.0, sh, 3, campos,
+                                           "radius")
+    ref = stages.project_views(means.detach(), quats.detach(), scales.detach(), opac.detach(),
+                               vm, full, Ks, s.width, s.height, 0.2, float("inf"), 0.0,
+                               sh=sh.detach(), sh_degree=3, campos=campos,
+                               normalize_quats=True)
+    vis = ref.radii > 0
+    assert torch.equal(out[3], ref.radii) and torch.equal(out[4], ref.tile_counts)
+    assert torch.equal(out[0][vis], torch.stack(ref.centers)[vis])
+    assert torch.equal(out[2], torch.stack(ref.colors))
+    g = torch.Generator(device=d).manual_seed(2)
+    w = [torch.randn(t.shape, device=d, generator=g) for t in out[:3]]
+    (sum((t * wt).sum() for t, wt in zip(out[:3], w))).backward()
+    want = torch.ops.splat200.project_views_backward(
+        means.detach(), quats.detach(), scales.detach(), vm, full, Ks, s.width, s.height,
+        out[3], sh.detach(), 3, campos, out[6], w[0], w[1], w[2])
+    for leaf, wv in zip(leaves, want):
+        assert rel_l2(leaf.grad.cpu(), wv.cpu()) <= 1e-6
