@@ -734,8 +734,13 @@ __global__ void __launch_bounds__(256)
     tile_scatter_kernel(const uint32_t* __restrict__ order, const uint32_t* __restrict__ bounds,
                         const uint2* __restrict__ sorted_rects, int gx, int gy,
                         const uint32_t* __restrict__ prefix, const uint32_t* __restrict__ starts,
-                        uint32_t m, uint32_t* __restrict__ ids) {
+                        uint32_t m, const uint32_t* __restrict__ pair_total,
+                        uint32_t* __restrict__ ids) {
   constexpr int kKept = 4;  // pairs per thread whose tile update stays in registers
+  // ids holds m entries; m may be a capacity above or below the true pair
+  // count: positions past m are skipped (the caller re-emits when m was too
+  // small) and only positions past the true count are an error
+  const uint32_t total = __ldg(pair_total);
   extern __shared__ __align__(16) uint32_t s_dyn[];
   __shared__ ScatterWave s_wave[2];
   const int T = gx * gy;
@@ -812,7 +817,7 @@ __global__ void __launch_bounds__(256)
         const uint32_t pos = s_next[q.tile] + __popcll(below);
         if (pos < m)
           ids[pos] = wave.g[q.member];
-        else
+        else if (pos >= total)
           record_device_error(kInconsistentInput);
         kept_tile[it] = q.tile;
         kept_add[it] = below == 0ull ? __popcll(q.cover) : 0u;  // first covering member
@@ -823,7 +828,7 @@ __global__ void __launch_bounds__(256)
       const uint32_t pos = s_next[q.tile] + __popcll(q.cover & members_below(q.member));
       if (pos < m)
         ids[pos] = wave.g[q.member];
-      else
+      else if (pos >= total)
         record_device_error(kInconsistentInput);
     }
     unsigned long long* other = s_masks + (buf ^ 1) * mask_words;

@@ -890,7 +890,7 @@ int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
         at<uint32_t>(ws, L.vals_a), at<uint32_t>(ws, L.chunk_bounds),
         at<uint2>(ws, L.sorted_rects), gx, gy, at<uint32_t>(ws, L.chunk_counts),
         at<uint32_t>(ws, L.tile_starts), static_cast<uint32_t>(pairs),
-        reinterpret_cast<uint32_t*>(ids));
+        at<uint32_t>(ws, L.totals) + 1, reinterpret_cast<uint32_t*>(ids));
     return check_launch("bin_emit");
   }
   char* pw = static_cast<char*>(pairs_workspace);

@@ -167,14 +167,27 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
             (layout.batch_count, layout.cameras, layout.n) + tuple(per_batch[0].shape[2:]))
         for name, per_batch in dense.items()
     }
+    channels = layout.colors.channels
+    # Work that does not need the pair counts is queued before the host
+    # read, so the GPU is not left idle while the host prepares it after.
+    backgrounds = []
+    for (b, c, ctr, con, colors, extras, bg, _state) in frames:
+        total = channels + (0 if extras is None else extras.shape[-1]) + 1
+        packed_bg = ctr.new_zeros(total)
+        if bg is not None:
+            packed_bg[:channels] = bg
+        backgrounds.append(packed_bg)
+    if not packed:
+        training = prepare_training_metadata(geometry, layout, packed=False, absgrad=absgrad)
     # Binning reads the pair counts (and camera status) in one host
     # synchronisation; the packed metadata's visible counts ride along.
     visible = [(f[7].radii > 0).sum() for f in frames] if packed else []
     bins, visible_counts = stages.bin_and_sort_many([f[7] for f in frames], width, height,
                                                     camera_status, tile_mode=tile_mode,
                                                     host_reads=visible)
-    training = prepare_training_metadata(geometry, layout, packed=packed, absgrad=absgrad,
-                                         visible_counts=visible_counts if packed else None)
+    if packed:
+        training = prepare_training_metadata(geometry, layout, packed=True, absgrad=absgrad,
+                                             visible_counts=visible_counts)
     meta = training.values
     meta.update(width=width, height=height, tile_size=16, tile_width=(width + 15) // 16,
                 tile_height=(height + 15) // 16, n_cameras=layout.cameras, packed=packed,
@@ -185,16 +198,12 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
                            batch_count=layout.batch_count, cameras=layout.cameras, n=layout.n,
                            width=width, height=height, device=layout.device)
         if statistics else ([], {}))
-    channels = layout.colors.channels
     blended, alphas = [], []
     for i, (b, c, ctr, con, colors, extras, bg, _state) in enumerate(frames):
         screen = None if training.screen is None else batch_item(batch_item(training.screen, b), c)
-        total = channels + (0 if extras is None else extras.shape[-1]) + 1
-        packed_bg = ctr.new_zeros(total)
-        if bg is not None:
-            packed_bg[:channels] = bg
-        main, alpha = RenderView.apply(ctr, con, colors, extras, screen, packed_bg,
-                                       bins[i]["ranges"], bins[i]["point_list"], config,
+        main, alpha = RenderView.apply(ctr, con, colors, extras, screen, backgrounds[i],
+                                       bins[i]["ranges"], bins[i]["point_list"],
+                                       bins[i]["tile_order"], config,
                                        training.absolute_targets[i],
                                        training.screen_targets[i],
                                        prepared_stats[i] if statistics else None, grad_enabled)

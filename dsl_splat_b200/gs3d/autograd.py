@@ -281,15 +281,15 @@ class RenderView(torch.autograd.Function):
     @staticmethod
     def forward(ctx: Any, centers: Tensor, conics: Tensor, colors: Tensor, extras: Tensor | None,
                 screen: Tensor | None, background: Tensor, ranges: Tensor, ids: Tensor,
-                config: ViewConfig, absolute: AbsGradientTarget | None,
+                order: Tensor, config: ViewConfig, absolute: AbsGradientTarget | None,
                 screen_target: ScreenGradientTarget | None, statistics, grad_enabled: bool):
         state = stages.ProjectedFootprint(centers, conics)
-        bins = dict(ranges=ranges, point_list=ids)
+        bins = dict(ranges=ranges, point_list=ids, tile_order=order)
         out = stages.render(state, bins, colors, extras, True, background, config.width,
                             config.height, statistics=statistics, separate_alpha=True)
         if grad_enabled and any(ctx.needs_input_grad[:5]):
             ctx.save_for_backward(centers, conics, colors, extras, background, ranges, ids,
-                                  out.transmittance, out.contributors)
+                                  order, out.transmittance, out.contributors)
             ctx.config, ctx.absolute, ctx.screen_target = config, absolute, screen_target
         ctx.set_materialize_grads(False)
         return out.features, out.alpha
@@ -298,13 +298,15 @@ class RenderView(torch.autograd.Function):
     @once_differentiable
     def backward(ctx: Any, g_features: Tensor | None, g_alpha: Tensor | None):
         if g_features is None and g_alpha is None:
-            return (None,) * 13
-        centers, conics, colors, extras, background, ranges, ids, final_t, contrib = ctx.saved_tensors
+            return (None,) * 14
+        centers, conics, colors, extras, background, ranges, ids, order, final_t, contrib = \
+            ctx.saved_tensors
         cfg = ctx.config
         needs = ctx.needs_input_grad
         direct = ctx.absolute.direct_buffer() if ctx.absolute is not None else None
         gc, gq, ga, gb, absolute = stages.render_backward(
-            stages.ProjectedFootprint(centers, conics), dict(ranges=ranges, point_list=ids),
+            stages.ProjectedFootprint(centers, conics),
+            dict(ranges=ranges, point_list=ids, tile_order=order),
             colors, extras, True, background, final_t, contrib, g_features, cfg.width,
             cfg.height, absgrad=ctx.absolute is not None, constant_tail=1, need_a=needs[2],
             need_b=extras is not None and needs[3], gradient_alpha=g_alpha, separate_alpha=True,
@@ -318,4 +320,4 @@ class RenderView(torch.autograd.Function):
             else:
                 g_screen = gc
         return (gc if needs[0] else None, gq if needs[1] else None, ga, gb, g_screen, None, None,
-                None, None, None, None, None, None)
+                None, None, None, None, None, None, None)

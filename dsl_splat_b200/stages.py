@@ -379,6 +379,15 @@ def scan_counts(counts: Tensor) -> tuple[Tensor, int]:
     return offsets, int(total.item())
 
 
+# pair-count capacity of the last binning per (n, width, height, tile mode,
+# view slot): lets the chunked emit run before the host has read the count
+_PAIR_CAPACITY: dict[tuple, int] = {}
+
+
+def _capacity_for(pairs: int) -> int:
+    return pairs + pairs // 8 + 4096
+
+
 class BinPlan:
     """Phase 1 of binning for one view (depth sort, offsets, ranges, count)."""
 
@@ -395,12 +404,36 @@ class BinPlan:
         self.workspace = torch.empty(lib.splat_bin_workspace_bytes(n, width, height, self.mode),
                                      dtype=torch.uint8, device=dev)
         self.pin = Args()  # the projected rows stay referenced until emit
+        # the chunked scatter needs no pair workspace and accepts a capacity
+        self.chunked = lib.splat_bin_pairs_workspace_bytes(1, width, height, self.mode) == 0
+        self.early: Tensor | None = None
         pin = self.pin
         check(lib.splat_bin_prepare(
             n, pin(state.centers), pin(state.conics), pin(state.radii), pin(state.tile_counts),
             pin(state.depths), width, height, self.mode, ptr(self.workspace),
             self.workspace.numel(), ptr(self.ranges), ptr(self.pairs_dev), nv.stream(dev)),
             "bin_prepare")
+
+    def emit_early(self, capacity: int) -> None:
+        """Queue the chunked emit into a capacity-sized buffer before the
+        pair count is known on the host (finish() checks it)."""
+        dev = self.ranges.device
+        self.early = torch.empty(capacity, dtype=torch.int32, device=dev)
+        pin, st = self.pin, self.state
+        check(lib.splat_bin_emit(self.n, capacity, self.width, self.height, self.mode,
+                                 pin(st.centers), pin(st.conics), pin(st.radii),
+                                 ptr(self.workspace), self.workspace.numel(), None, 0,
+                                 ptr(self.early), nv.stream(dev)), "bin_emit")
+
+    def finish(self, pairs: int) -> Tensor:
+        """point_list of `pairs` entries: the early emit's when it fitted,
+        else an exact emit now."""
+        if self.early is not None and pairs <= len(self.early):
+            ids = self.early[:pairs]
+            self.early = self.workspace = self.pin = None
+            return ids
+        self.early = None
+        return self.emit(pairs)
 
     def emit(self, pairs: int) -> Tensor:
         dev = self.ranges.device
@@ -430,6 +463,9 @@ def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
     the caller needs on the host, read in that same synchronisation; when
     given, (bins, their values) is returned."""
     plans = [BinPlan(s, width, height, tile_mode) for s in states]
+    # the blend schedule needs only the ranges: queued before the host read,
+    # so nothing but the emits waits for the pair counts
+    orders = [tile_order(dict(ranges=p.ranges)) for p in plans]
     parts = [p.pairs_dev for p in plans]
     ncodes = 0
     if camera_status:
@@ -438,10 +474,30 @@ def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
         parts = [codes_dev] + parts
     extra = [t.reshape(1).to(torch.int64) for t in (host_reads or [])]
     parts = parts + extra
-    values = torch.cat(parts).tolist() if parts else []
+    values: list = []
+    keys = [(p.n, width, height, p.mode, v) for v, p in enumerate(plans)]
+    if parts:
+        # the counts travel to pinned memory behind an event; chunked emits
+        # with a capacity from the last call are queued after that copy, so
+        # the GPU scatters while the host waits for (only) the counts
+        dev_values = torch.cat(parts)
+        host = torch.empty(len(dev_values), dtype=torch.int64, pin_memory=True)
+        host.copy_(dev_values, non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(dev_values.device))
+        for key, p in zip(keys, plans):
+            capacity = _PAIR_CAPACITY.get(key)
+            if p.chunked and capacity:
+                p.emit_early(capacity)
+        ready.synchronize()
+        values = host.tolist()
     raise_camera_errors(values[:ncodes])
     counts = values[ncodes:ncodes + len(plans)]
-    bins = [dict(point_list=p.emit(int(m)), ranges=p.ranges) for p, m in zip(plans, counts)]
+    bins = []
+    for key, p, m, o in zip(keys, plans, counts, orders):
+        bins.append(dict(point_list=p.finish(int(m)), ranges=p.ranges, tile_order=o))
+        if p.chunked:
+            _PAIR_CAPACITY[key] = _capacity_for(int(m))
     if host_reads is None:
         return bins
     return bins, values[ncodes + len(plans):]

@@ -208,6 +208,11 @@ int splat_bin_prepare(int n, const float* centers, const float* conics, const in
                       const int* tiles, const float* depths, int width, int height, int tile_mode,
                       void* workspace, size_t workspace_bytes, int* ranges, long long* pairs,
                       void* stream);
+/* pairs: the length of ids.  Where splat_bin_pairs_workspace_bytes is 0
+ * (the chunked scatter), pairs may be a capacity instead of the count
+ * splat_bin_prepare returned: ids past the true count are left unwritten,
+ * and pairs past a too-small capacity are dropped (emit again with the true
+ * count).  Elsewhere it must be the true count. */
 int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
                    const float* centers, const float* conics, const int* radii, void* workspace,
                    size_t workspace_bytes, void* pairs_workspace, size_t pairs_workspace_bytes,

@@ -606,3 +606,24 @@ def test_tile_order_schedule():
                                    constant_tail=1)
     for a, b in zip(g_got[:3], g_ref[:3]):
         assert rel_l2(a.cpu().numpy(), b.cpu().numpy()) <= 1e-5
+
+
+def test_early_emit_capacity_paths():
+    """The chunked emit launched before the host reads the pair count (with
+    the last call's count as capacity) gives the exact point list when the
+    capacity fits, re-emits exactly when it is too small, and neither case
+    records a device error."""
+    from dsl_splat_b200._native import device_error
+    p = Prepared(_scene("c1_small"))
+    out = p.project()
+    stages._PAIR_CAPACITY.clear()
+    first = stages.bin_and_sort(out.state, p.W, p.H)          # no capacity yet: exact
+    assert stages._PAIR_CAPACITY, "the chunked path records a capacity"
+    again = stages.bin_and_sort(out.state, p.W, p.H)          # capacity fits
+    assert torch.equal(again["point_list"], first["point_list"])
+    assert torch.equal(again["ranges"], first["ranges"])
+    for key in list(stages._PAIR_CAPACITY):
+        stages._PAIR_CAPACITY[key] = 100                      # far too small
+    small = stages.bin_and_sort(out.state, p.W, p.H)
+    assert torch.equal(small["point_list"], first["point_list"])
+    assert device_error(_dev()) == 0
