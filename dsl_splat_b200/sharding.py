@@ -136,8 +136,10 @@ class GradientSync:
     leaves fall back to autograd.  With group=None nothing is reduced: the
     context still saves the per-view gradient tensors.
 
-    buckets=1 issues one coalesced all-reduce after the last kernel; more
-    buckets overlap the transfers with the remaining kernels.  On two B200s
+    buckets=1 issues one all-reduce of one flat buffer (the per-parameter
+    buffers are views of it) after the last kernel; more buckets all-reduce
+    row ranges of every buffer as coalesced groups, overlapping the transfers
+    with the remaining kernels.  On two B200s
     (config 1, 236 MB of gradients) one bucket measured fastest: NCCL's
     kernels and the projection backward contend for SMs and HBM (762 / 733 /
     722 / 668 frames/s for 1 / 2 / 4 / 8 buckets).
@@ -156,6 +158,7 @@ class GradientSync:
         self.views = 0
         self.done = 0
         self.buffers: dict[str, Tensor] | None = None
+        self.flat: Tensor | None = None
         self.works: list = []
         self.finished = False
 
@@ -189,8 +192,22 @@ class GradientSync:
         """Buffers for the next view's backward, its accumulate flag, and
         whether it is the last local view (the one that reduces)."""
         if self.buffers is None:
-            self.buffers = {k: torch.empty_like(p) for k, p in self.params.items()
-                            if p is not None and p.requires_grad}
+            # views of one flat allocation: a bucket covering every row is then
+            # one all-reduce of one buffer (0.60 ms instead of 0.82 ms for a
+            # coalesced group of the five tensors, 236 MB on 4 B200s)
+            live = {k: p for k, p in self.params.items() if p is not None and p.requires_grad}
+            same = len({(p.dtype, p.device) for p in live.values()}) == 1
+            if live and same:
+                first = next(iter(live.values()))
+                self.flat = torch.empty(sum(p.numel() for p in live.values()),
+                                        dtype=first.dtype, device=first.device)
+                self.buffers, at = {}, 0
+                for k, p in live.items():
+                    self.buffers[k] = self.flat[at:at + p.numel()].view(p.shape)
+                    at += p.numel()
+            else:
+                self.flat = None
+                self.buffers = {k: torch.empty_like(p) for k, p in live.items()}
         accumulate = self.done > 0  # the first view's backward overwrites
         self.done += 1
         return self.buffers, accumulate, self.done == self.views
@@ -198,6 +215,11 @@ class GradientSync:
     def reduce_range(self, lo: int, hi: int) -> None:
         """Issue the all-reduce of rows [lo, hi) of every buffer (async)."""
         if self.group is None:
+            return
+        rows = {len(b) for b in self.buffers.values()}
+        if self.flat is not None and lo == 0 and rows == {hi}:
+            self.works.append(dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=self.group,
+                                              async_op=True))
             return
         tensors = [b[lo:hi] for b in self.buffers.values()]
         if dist.get_backend(self.group) == "nccl" and hasattr(dist, "_coalescing_manager"):

@@ -131,14 +131,14 @@ def _contribution(shape, rank, view, step):
 SYNC_SHAPES = [(101, 3), (101, 4), (101, 3), (101,), (101, 16, 3)]
 
 
-def _sync_worker(rank, world, port, outdir):
+def _sync_worker(rank, world, port, outdir, buckets):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                       WORLD_SIZE=str(world))
     from dsl_splat_b200 import sharding
     sharding.init_process_group("gloo", timeout_s=30.0)
     params = [torch.zeros(s, requires_grad=True) for s in SYNC_SHAPES]
-    sync = sharding.GradientSync(*params, group=dist.group.WORLD, buckets=3)
+    sync = sharding.GradientSync(*params, group=dist.group.WORLD, buckets=buckets)
     flags = []
     for step in range(2):  # the second step accumulates into the first's p.grad
         with sync:
@@ -163,13 +163,16 @@ def _sync_worker(rank, world, port, outdir):
     dist.destroy_process_group()
 
 
-def test_gradient_sync_buckets_equal_full_sum(tmp_path):
+@pytest.mark.parametrize("buckets", [1, 3])
+def test_gradient_sync_buckets_equal_full_sum(tmp_path, buckets):
     """GradientSync with gloo ranks: per-view accumulation, the last view's
-    bucketed all-reduce, and p.grad accumulation across steps give the sum of
-    every rank's and view's gradients."""
+    all-reduce (one flat buffer for one bucket, row ranges for three), and
+    p.grad accumulation across steps give the sum of every rank's and view's
+    gradients."""
     port = _free_port()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_sync_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    procs = [ctx.Process(target=_sync_worker, args=(r, 2, port, str(tmp_path), buckets))
+             for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
