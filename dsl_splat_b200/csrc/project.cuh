@@ -248,41 +248,6 @@ SPLAT_DEV void warp_load_sh(const float* __restrict__ src, int row_stride, int b
   __syncwarp();
 }
 
-// Writes (accumulate: adds) the warp's rows: kCols columns from the tile and
-// zeros for the remaining columns [kCols, row_stride) of each row.
-template <int DEG>
-SPLAT_DEV void warp_store_sh(float* __restrict__ dst, int row_stride, int base, int n,
-                             const float* tile, bool accumulate) {
-  constexpr int C = ShTile<DEG>::kCols, S = ShTile<DEG>::kStride;
-  const int lane = threadIdx.x & 31;
-  __syncwarp();
-  const int rows = min(32, n - base);
-  if (row_stride == C && rows == 32) {
-    float* g = dst + static_cast<size_t>(base) * C;
-#pragma unroll 12
-    for (int k = 0; k < C; ++k) {
-      const int e = k * 32 + lane;
-      const int r = e / C;
-      const float v = tile[r * S + (e - r * C)];
-      if (accumulate)
-        g[e] += v;
-      else
-        g[e] = v;
-    }
-    return;
-  }
-  for (int r = 0; r < rows; ++r) {
-    float* row = dst + static_cast<size_t>(base + r) * row_stride;
-    for (int t = lane; t < row_stride; t += 32) {
-      const float v = t < C ? tile[r * S + t] : 0.0f;
-      if (accumulate)
-        row[t] += v;
-      else
-        row[t] = v;
-    }
-  }
-}
-
 // One camera's view of the inputs and the outputs it writes (ProjectParams
 // fields; the multi-view kernel takes them from per-view tables).
 struct ProjectCamera {
@@ -557,45 +522,6 @@ SPLAT_DEV float3 sh_vjp(const float* __restrict__ coef, int sh_k, float d0, floa
       gcoef[3 * k + 1] = 0.0f;
       gcoef[3 * k + 2] = 0.0f;
     }
-  if (DEG == 0) return make_float3(0.0f, 0.0f, 0.0f);
-  const float den = wmax(length, W32(1e-12));
-  float3 dg = make_float3(g0 / den, g1 / den, g2 / den);
-  if (length >= W32(1e-12)) {
-    const float dot = (ux * g0 + uy * g1 + uz * g2) / length;
-    dg.x -= ux * dot;
-    dg.y -= uy * dot;
-    dg.z -= uz * dot;
-  }
-  return dg;
-}
-
-// sh_vjp on a staged row: reads coefficient triple k from `row`, then
-// overwrites it with the coefficient gradient (primitives/sh.py:116-120).
-template <int DEG>
-SPLAT_DEV float3 sh_vjp_row(float* row, float d0, float d1, float d2, float3 cg) {
-  float ux = 0.0f, uy = 0.0f, uz = 0.0f, length = 1.0f;
-  if (DEG > 0) {
-    length = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
-    const float den = wmax(length, W32(1e-12));
-    ux = d0 / den;
-    uy = d1 / den;
-    uz = d2 / den;
-  }
-  float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
-#pragma unroll
-  for (int k = 0; k < (DEG + 1) * (DEG + 1); ++k) {
-    const float b = sh_basis(ux, uy, uz, k);
-    if (DEG > 0) {
-      const float w = row[3 * k] * cg.x + row[3 * k + 1] * cg.y + row[3 * k + 2] * cg.z;
-      const float3 bg = sh_basis_grad(ux, uy, uz, k);
-      g0 += w * bg.x;
-      g1 += w * bg.y;
-      g2 += w * bg.z;
-    }
-    row[3 * k] = b * cg.x;
-    row[3 * k + 1] = b * cg.y;
-    row[3 * k + 2] = b * cg.z;
-  }
   if (DEG == 0) return make_float3(0.0f, 0.0f, 0.0f);
   const float den = wmax(length, W32(1e-12));
   float3 dg = make_float3(g0 / den, g1 / den, g2 / den);

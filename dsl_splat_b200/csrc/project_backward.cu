@@ -300,7 +300,8 @@ SPLAT_DEV void stage_chunk(const ProjectBackwardParams& p, unsigned mask, int ba
   }
 }
 
-// sh_vjp_row over a staged row read and written as 16-byte quads, four basis
+// The SH VJP (primitives/sh.py:82-138) of one staged row, read and
+// overwritten with its coefficient gradient as 16-byte quads, four basis
 // functions (twelve floats) at a time where the degree allows.
 template <int DEG>
 SPLAT_DEV float3 sh_vjp_quads(float* row, float d0, float d1, float d2, float3 cg) {
