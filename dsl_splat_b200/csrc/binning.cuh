@@ -38,9 +38,74 @@ constexpr uint32_t kFlagInclusive = 2u << 30;
 constexpr uint32_t kValueMask = (1u << 30) - 1u;
 constexpr uint32_t kSpinLimit = 1u << 22;
 
+
 __device__ int g_splat_device_error;
 
 SPLAT_DEV void record_device_error(int code) { atomicCAS(&g_splat_device_error, 0, code); }
+
+// Status word formats of the decoupled look-backs: a 2-bit flag (0 = not
+// yet published, aggregate, inclusive) over the value.
+struct Status32 {
+  using Word = uint32_t;
+  static constexpr Word kAggregate = kFlagAggregate, kInclusive = kFlagInclusive;
+  static constexpr Word kMask = kValueMask;
+  static SPLAT_DEV Word load(const Word* p) { return ld_relaxed(p); }
+};
+struct Status64 {
+  using Word = unsigned long long;
+  static constexpr Word kAggregate = 1ull << 62, kInclusive = 2ull << 62;
+  static constexpr Word kMask = (1ull << 62) - 1ull;
+  static SPLAT_DEV Word load(const Word* p) { return ld_relaxed64(p); }
+};
+
+// Exclusive prefix of tile `tile` from its predecessors' status words
+// (status[t * stride] for tile t): kWindow predecessors are read at once
+// with independent loads, then consumed nearest first, adding aggregates up
+// to the first inclusive value; an unpublished word stops the window and it
+// is read again after a short sleep.  Tile 0 is always inclusive, so the
+// walk ends; a wait longer than kSpinLimit records kDeviceTimeout.
+template <class S, int kWindow>
+SPLAT_DEV typename S::Word lookback(const typename S::Word* status, int64_t tile, size_t stride) {
+  using Word = typename S::Word;
+  Word excl = 0;
+  uint32_t spins = 0;
+  int64_t t = tile - 1;
+  while (t >= 0) {
+    Word w[kWindow];
+#pragma unroll
+    for (int k = 0; k < kWindow; ++k) w[k] = t - k >= 0 ? S::load(status + (t - k) * stride) : 0;
+    Word add = 0;
+    int consumed = 0, state = 0;  // 0 continue, 1 inclusive reached, 2 unpublished
+#pragma unroll
+    for (int k = 0; k < kWindow; ++k) {
+      if (state == 0) {
+        if (t - k < 0) {
+          state = 1;
+        } else {
+          const Word flag = w[k] & ~S::kMask;
+          if (flag == 0) {
+            state = 2;
+          } else {
+            add += w[k] & S::kMask;
+            consumed = k + 1;
+            if (flag == S::kInclusive) state = 1;
+          }
+        }
+      }
+    }
+    excl += add;
+    if (state == 1) break;
+    if (state == 2) {
+      if (++spins > kSpinLimit) {
+        record_device_error(kDeviceTimeout);
+        break;
+      }
+      __nanosleep(32);
+    }
+    t -= consumed;
+  }
+  return excl;
+}
 
 // ---- phase 1: per-Gaussian preparation ---------------------------------
 // diff == nullptr selects the chunked path (no difference grid; the pair
@@ -303,23 +368,7 @@ __global__ void __launch_bounds__(THREADS)
       st_relaxed(mine, kFlagInclusive | total);
     } else {
       st_relaxed(mine, kFlagAggregate | total);
-      int64_t t = static_cast<int64_t>(tile) - 1;
-      uint32_t spins = 0;
-      while (t >= 0) {
-        const uint32_t s = ld_relaxed(status + static_cast<size_t>(t) * kRadix + d);
-        const uint32_t flag = s & ~kValueMask;
-        if (flag == 0u) {
-          if (++spins > kSpinLimit) {
-            record_device_error(kDeviceTimeout);
-            break;
-          }
-          __nanosleep(32);
-          continue;
-        }
-        excl += s & kValueMask;
-        if (flag == kFlagInclusive) break;
-        --t;
-      }
+      excl = lookback<Status32, 8>(status + d, static_cast<int64_t>(tile), kRadix);
       st_relaxed(mine, kFlagInclusive | (excl + total));
     }
     s_base[d] = digit_offsets[d] + excl;
@@ -426,6 +475,104 @@ __global__ void __launch_bounds__(kSortBlock)
   }
 }
 
+// The chunked path's work prefix and chunk bounds in one pass (replacing a
+// block-sum / block-prefix / apply scan and a binary-search kernel).
+// offsets[i] = sum over j < i of (max(values[order[j]], 0) + bias) in depth
+// order, offsets[n] = the total; bounds[k] = the first i in [0, n] with
+// offsets[i] >= floor(W k / chunks) and bounds[chunks] = n, where
+// W = *pair_total + bias * n is bin_prepare's total, known before the scan.
+// Each tile finds the few bounds whose targets fall inside its prefix range
+// by binary search over its exclusive prefixes in shared memory.  Decoupled
+// look-back over
+// kSortTile-element tiles taken in ticket order; 64-bit status words
+// (2-bit flag, 62-bit inclusive/aggregate value).
+__global__ void __launch_bounds__(kSortBlock)
+    work_scan_kernel(const int* __restrict__ values, const uint32_t* __restrict__ order,
+                     uint32_t n, uint32_t bias, const unsigned long long* __restrict__ pair_total,
+                     unsigned chunks, unsigned long long* __restrict__ status,
+                     uint32_t* __restrict__ counter, uint32_t* __restrict__ offsets,
+                     uint32_t* __restrict__ bounds) {
+  __shared__ uint32_t s_val[kSortTile];
+  __shared__ uint32_t s_warp[32];
+  __shared__ uint32_t s_tile, s_excl;
+  if (threadIdx.x == 0) s_tile = atomicAdd(counter, 1u);
+  __syncthreads();
+  const uint32_t tile = s_tile;
+  const uint32_t base = tile * kSortTile;
+  for (int k = 0; k < kSortItems; ++k) {
+    const int j = k * kSortBlock + threadIdx.x;
+    const uint32_t i = base + j;
+    s_val[j] = i < n ? scan_value(values, order, i, bias) : 0u;
+  }
+  __syncthreads();
+  uint32_t local[kSortItems];
+  uint32_t sum = 0u;
+#pragma unroll
+  for (int k = 0; k < kSortItems; ++k) {
+    local[k] = s_val[threadIdx.x * kSortItems + k];
+    sum += local[k];
+  }
+  uint32_t tile_total;
+  uint32_t run = block_exclusive_scan(sum, s_warp, &tile_total);
+  if (threadIdx.x == 0) {
+    unsigned long long* mine = status + tile;
+    unsigned long long excl = 0ull;
+    if (tile == 0) {
+      st_relaxed64(mine, Status64::kInclusive | tile_total);
+    } else {
+      st_relaxed64(mine, Status64::kAggregate | tile_total);
+      excl = lookback<Status64, 16>(status, static_cast<int64_t>(tile), 1);
+      st_relaxed64(mine, Status64::kInclusive | (excl + tile_total));
+    }
+    s_excl = static_cast<uint32_t>(excl);
+  }
+  __syncthreads();
+  run += s_excl;
+#pragma unroll
+  for (int k = 0; k < kSortItems; ++k) {
+    s_val[threadIdx.x * kSortItems + k] = run;
+    run += local[k];
+  }
+  __syncthreads();
+  const unsigned long long W = *pair_total + static_cast<unsigned long long>(bias) * n;
+  // number of k in [0, chunks) whose target floor(W k / chunks) is <= w
+  auto below = [&](uint32_t w) -> uint32_t {
+    if (W == 0ull) return chunks;
+    const unsigned long long c =
+        ((static_cast<unsigned long long>(w) + 1ull) * chunks + W - 1ull) / W;
+    return static_cast<uint32_t>(c < chunks ? c : chunks);
+  };
+  const uint32_t cnt = min(static_cast<uint32_t>(kSortTile), n - base);
+  const bool last = base + cnt == n;
+  for (int k = 0; k < kSortItems; ++k) {  // coalesced
+    const uint32_t j = k * kSortBlock + threadIdx.x;
+    if (j < cnt) offsets[base + j] = s_val[j];
+  }
+  // this tile owns the bounds whose target lies in (e_0, e_end] (e: the
+  // exclusive prefixes, e_end the tile's inclusive total): bound k is
+  // base + (the first j in [1, cnt] with e_j >= target, e_cnt = e_end); tile
+  // 0 also writes those at or below 0, the last tile every bound left and
+  // bounds[chunks] = n.  Each bound is written once, complete and monotone
+  // whatever the totals.
+  const uint32_t e0 = s_val[0], e_end = s_excl + tile_total;
+  const uint32_t k_lo = below(e0), k_hi = last ? chunks : below(e_end);
+  if (tile == 0)
+    for (uint32_t c = threadIdx.x; c < k_lo; c += blockDim.x) bounds[c] = 0u;
+  for (uint32_t c = k_lo + threadIdx.x; c < k_hi; c += blockDim.x) {
+    const unsigned long long target = W * c / chunks;
+    uint32_t lo = 1, hi = cnt;  // first j in [1, cnt] with e_j >= target
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (s_val[mid] >= target) hi = mid; else lo = mid + 1;
+    }
+    bounds[c] = base + lo;
+  }
+  if (last && threadIdx.x == 0) {
+    bounds[chunks] = n;
+    offsets[n] = e_end;
+  }
+}
+
 // ---- accutile emission --------------------------------------------------
 // Pairs of the depth-ordered Gaussians in emission order (the strip walk of
 // intersections.py:155-218), written at their depth-order offsets; stable
@@ -484,22 +631,6 @@ SPLAT_DEV uint32_t rect_area(uint2 r) {
   uint32_t x0, y0, x1, y1;
   unpack_rect(r, x0, y0, x1, y1);
   return (x1 > x0 && y1 > y0) ? (x1 - x0) * (y1 - y0) : 0u;
-}
-
-// bounds[k] = first depth position whose work prefix reaches k/K of the
-// total (work[] exclusive, work[n] = total; strictly increasing).
-__global__ void chunk_bounds_kernel(const uint32_t* __restrict__ work, uint32_t n, unsigned chunks,
-                                    uint32_t* __restrict__ bounds) {
-  const unsigned k = blockIdx.x * blockDim.x + threadIdx.x;
-  if (k > chunks) return;
-  const uint64_t total = work[n];
-  const uint64_t target = total * k / chunks;
-  uint32_t lo = 0, hi = n;  // first i in [0, n] with work[i] >= target
-  while (lo < hi) {
-    const uint32_t mid = lo + ((hi - lo) >> 1);
-    if (work[mid] < target) lo = mid + 1; else hi = mid;
-  }
-  bounds[k] = k == chunks ? n : lo;
 }
 
 // cnt[k * T + t] for chunk k = blockIdx.x, from a difference grid of the

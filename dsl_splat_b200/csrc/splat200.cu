@@ -114,7 +114,7 @@ ChunkPlan chunk_plan(long long n, int gx, int gy, int tile_mode) {
 struct BinLayout {
   size_t keys_a, vals_a, keys_b, vals_b, rects, offsets, block_sums;
   size_t zero_begin;  // everything from here to zero_end is cleared per call
-  size_t depth_hist, diff, depth_status, counters, totals;
+  size_t depth_hist, diff, depth_status, counters, totals, work_status;
   size_t zero_end;
   size_t depth_digits, tile_digits;
   size_t chunk_counts, tile_totals, tile_starts, chunk_bounds, sorted_rects;  // chunked path
@@ -151,8 +151,9 @@ BinLayout bin_layout(long long n, int width, int height, int tile_mode) {
   L.depth_hist = take(4 * 4 * kRadix);
   L.diff = take(plan.use ? 0 : 4 * static_cast<size_t>(gx + 1) * (gy + 1));
   L.depth_status = take(4 * 4 * depth_tiles(n) * kRadix);
-  L.counters = take(4 * 8);
+  L.counters = take(4 * 8);  // onesweep tickets: depth passes 0-3, work scan 4
   L.totals = take(8 * 4);
+  L.work_status = take(plan.use ? 8 * sort_tiles : 0);  // work scan look-back
   L.zero_end = o;
   L.depth_digits = take(4 * 4 * kRadix);
   L.tile_digits = take(plan.use ? 0 : 4 * 3 * kRadix);
@@ -824,14 +825,11 @@ int splat_bin_prepare(int n, const float* centers, const float* conics, const in
     uint32_t* cnt = at<uint32_t>(ws, L.chunk_counts);
     uint32_t* tile_totals = at<uint32_t>(ws, L.tile_totals);
     uint32_t* bounds = at<uint32_t>(ws, L.chunk_bounds);
-    // work prefix in depth order (tiles + a per-Gaussian cost) -> chunk bounds
-    scan_block_sums_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums,
-                                                                      kChunkGaussianCost);
-    scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, sort_tiles, totals + 0);
-    scan_apply_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(tiles, vals_a, n, block_sums, 0,
-                                                                 offsets, kChunkGaussianCost);
-    chunk_bounds_kernel<<<blocks_for(plan.chunks + 1, 256), 256, 0, counted(s)>>>(
-        offsets, static_cast<uint32_t>(n), plan.chunks, bounds);
+    // work prefix in depth order (tiles + a per-Gaussian cost) and the chunk
+    // bounds, one pass (the total is bin_prepare's pair count + cost * n)
+    work_scan_kernel<<<sort_tiles, kSortBlock, 0, counted(s)>>>(
+        tiles, vals_a, static_cast<uint32_t>(n), kChunkGaussianCost, total64, plan.chunks,
+        at<unsigned long long>(ws, L.work_status), counters + 4, offsets, bounds);
     if (plan.smem_counts > 48 * 1024)
       cudaFuncSetAttribute(chunk_counts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(plan.smem_counts));

@@ -199,6 +199,14 @@ SPLAT_DEV uint32_t ld_relaxed(const uint32_t* p) {
 SPLAT_DEV void st_relaxed(uint32_t* p, uint32_t v) {
   asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+SPLAT_DEV unsigned long long ld_relaxed64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+SPLAT_DEV void st_relaxed64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 // Vector reductions into global memory (sm_90+).
 SPLAT_DEV void red_add_v2(float* p, float a, float b) {
