@@ -304,19 +304,24 @@ class RenderView(torch.autograd.Function):
         cfg = ctx.config
         needs = ctx.needs_input_grad
         direct = ctx.absolute.direct_buffer() if ctx.absolute is not None else None
+        # the centre gradient doubles as dL/dmeans2d: written straight into
+        # the view's block of means2d.grad when that block is untouched
+        screen_direct = (ctx.screen_target.direct_buffer()
+                         if needs[4] and ctx.screen_target is not None else None)
         gc, gq, ga, gb, absolute = stages.render_backward(
             stages.ProjectedFootprint(centers, conics),
             dict(ranges=ranges, point_list=ids, tile_order=order),
             colors, extras, True, background, final_t, contrib, g_features, cfg.width,
             cfg.height, absgrad=ctx.absolute is not None, constant_tail=1, need_a=needs[2],
             need_b=extras is not None and needs[3], gradient_alpha=g_alpha, separate_alpha=True,
-            absolute_out=direct)
+            absolute_out=direct, centers_out=screen_direct)
         if ctx.absolute is not None and direct is None:
             ctx.absolute.write(absolute)
         g_screen = None
         if needs[4]:
             if ctx.screen_target is not None:
-                ctx.screen_target.add(gc)  # straight into means2d.grad (see training.py)
+                if screen_direct is None:
+                    ctx.screen_target.add(gc)  # into means2d.grad (see training.py)
             else:
                 g_screen = gc
         return (gc if needs[0] else None, gq if needs[1] else None, ga, gb, g_screen, None, None,

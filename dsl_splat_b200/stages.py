@@ -579,13 +579,14 @@ def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
                     height: int, *, planar: bool = False, absgrad: bool = False,
                     constant_tail: int = 0, need_a: bool = True, need_b: bool = True,
                     gradient_alpha: Tensor | None = None, separate_alpha: bool = False,
-                    absolute_out: Tensor | None = None):
+                    absolute_out: Tensor | None = None, centers_out: Tensor | None = None):
     """gs3d/render.py:409-463: grads of centers, conics, feat_a, feat_b, abs.
 
     separate_alpha: gradient holds the channels before the constant one
     (H, W, C'-1) and gradient_alpha (H, W, 1) the constant channel's; either
     may be None (zero).  absolute_out: a zeroed contiguous (n, 2) buffer that
-    receives the |d centers| sums in place of a new one."""
+    receives the |d centers| sums in place of a new one; centers_out: a zeroed
+    contiguous (n, 2) buffer that receives the centre gradient likewise."""
     pin = Args()
     a, b, ca, cb = _features(feat_a, feat_b)
     channels = ca + cb + int(append_one)
@@ -604,7 +605,7 @@ def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
         pix_stride, ch_stride = 1, height * width
     else:
         pix_stride, ch_stride = stored, 1
-    centers = torch.zeros_like(state.centers)
+    centers = centers_out if centers_out is not None else torch.zeros_like(state.centers)
     conics = torch.zeros_like(state.conics)
     ga = torch.zeros_like(a) if need_a else None
     gb = torch.zeros_like(b) if (b is not None and need_b) else None

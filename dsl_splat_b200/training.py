@@ -56,6 +56,28 @@ class ScreenGradientTarget:
     gaussian_ids: Tensor | None = None  # packed: this view's Gaussians, rows [begin, end)
     begin: int = 0
     end: int = 0
+    # dense targets of one call share it: the gradient tensor this call
+    # created and the views whose block of it is still untouched
+    fresh: dict | None = None
+
+    @torch.no_grad()
+    def direct_buffer(self) -> Tensor | None:
+        """Dense case: this view's (N, 2) block of leaf.grad when the block
+        still holds the zeros this call created (the render backward then
+        accumulates into it directly and add() is not needed), else None."""
+        if self.gaussian_ids is not None or self.fresh is None:
+            return None
+        if self.leaf.grad is None:
+            self.leaf.grad = torch.zeros_like(self.leaf)
+            self.fresh["grad"] = self.leaf.grad
+            self.fresh["views"] = set(range(self.fresh["count"]))
+        if self.leaf.grad is not self.fresh.get("grad") or self.index not in self.fresh["views"]:
+            return None
+        block = self.leaf.grad.view(-1, *self.leaf.shape[-2:])[self.index]
+        if not block.is_contiguous():
+            return None
+        self.fresh["views"].discard(self.index)
+        return block
 
     @torch.no_grad()
     def add(self, gradient: Tensor) -> None:
@@ -117,7 +139,9 @@ def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packe
                 end=begin + count))
             begin += count
     else:
-        screen_targets = [ScreenGradientTarget(screen, index=i) for i in range(views)]
+        fresh = {"count": views}
+        screen_targets = [ScreenGradientTarget(screen, index=i, fresh=fresh)
+                          for i in range(views)]
     if packed:
         dense_screen = torch.zeros_like(dense["means2d"]).index_put(
             (batch_ids, camera_ids, gaussian_ids), screen)
