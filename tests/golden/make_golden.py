@@ -19,7 +19,11 @@ Kernels executed (reference file:line):
 Warp library calls restated: array_scan (inclusive cumsum) and
 radix_sort_pairs (a stable sort of the 64-bit keys).
 
-Usage: python tests/golden/make_golden.py [/path/to/reference] [--tile-modes-only]
+Also: gs3d/render.py:36-208 with statistics.py:47-73's observer and eight
+channels (wide_*.npz).
+
+Usage: python tests/golden/make_golden.py [/path/to/reference]
+       [--tile-modes-only | --wide-only]
 """
 
 from __future__ import annotations
@@ -196,6 +200,57 @@ def golden_case(ref, name, scene: dict, seed: int):
     return out
 
 
+def wide_case(ref, name, scene: dict, seed: int) -> dict:
+    """Eight blended channels (3 SH colours, 4 extras, the constant one) over
+    a random background, with one masked-count and one weighted-sum
+    statistics request, through the reference's own render kernels
+    (gs3d/render.py:36-208 with statistics.py:47-73's observer, and
+    gs3d/render.py:211-356), on the projection and bins of `scene`."""
+    base = golden_case(ref, name, scene, seed)
+    W, H = base["width"], base["height"]
+    T = ((W + 15) // 16) * ((H + 15) // 16)
+    n = len(base["means"])
+    wp = sys.modules["warp"]
+    rng = np.random.default_rng(seed + 1000)
+    extras = rng.standard_normal((n, 4)).astype(np.float32)
+    feats = np.concatenate([base["colors"], extras, np.ones((n, 1), np.float32)], axis=1)
+    C = feats.shape[1]
+    bg = rng.uniform(0.0, 1.0, C).astype(np.float32)
+    Feature = wp.types.vector(C, np.float32)
+    mask = np.zeros((H, W), np.float32)
+    mask[: H // 2] = 1.0
+    weights = rng.uniform(0.0, 1.0, (H, W)).astype(np.float32)
+    pixel_values = np.stack([mask.ravel(), weights.ravel()])  # request 0 count, 1 sum
+    counts = np.zeros((1, n), np.int32)
+    sums = np.zeros((1, n), np.float32)
+    image = np.zeros(C * H * W, np.float32)
+    final_t = np.zeros(H * W, np.float32)
+    contrib = np.zeros(H * W, np.int32)
+    ws.launch(ref["render"]._make_forward(C, (0, 1)), 256 * T,
+              [W, H, A(base["ranges"]), A(base["ids"]), A(base["centers"], wp.vec2),
+               A(base["conics"], wp.vec4), A(feats, Feature), A(bg), A(image), A(final_t),
+               A(contrib), A(pixel_values), A(counts), A(sums)], block=256)
+    upstream = rng.standard_normal((C, H, W)).astype(np.float32)
+    g_centers = np.zeros((n, 2), np.float32)
+    g_conics = np.zeros((n, 4), np.float32)
+    g_feats = np.zeros((n, C), np.float32)
+    g_abs = np.zeros((n, 2), np.float32)
+    ws.launch(ref["render"]._make_backward(C, True, 1), 256 * T,
+              [W, H, A(base["ranges"]), A(base["ids"]), A(base["centers"], wp.vec2),
+               A(base["conics"], wp.vec4), A(feats, Feature), A(bg), A(final_t), A(contrib),
+               A(upstream.ravel().copy()), A(g_centers), A(g_conics), A(g_feats), A(g_abs)],
+              block=256)
+    keep = {k: base[k] for k in ("width", "height", "centers", "conics", "radii", "ranges",
+                                 "ids")}
+    keep.update(features=feats, background=bg, mask=mask, weights=weights,
+                image=image.reshape(C, H, W), final_t=final_t.reshape(H, W),
+                contributors=contrib.reshape(H, W), stat_counts=counts[0], stat_sums=sums[0],
+                upstream=upstream, grad_centers=g_centers, grad_conics=g_conics,
+                grad_features=g_feats, grad_abs=g_abs)
+    print(f"{name} (8 channels, statistics): pairs={len(base['ids'])}", flush=True)
+    return keep
+
+
 def tile_mode_case(ref, name, scene: dict) -> dict:
     """Projection tile counts and binning for tile_mode snugbox and accutile
     (gs3d/projection.py:150-162, splatting/intersections.py:45-218,
@@ -331,10 +386,17 @@ def main():
     ref_root = args[0] if args else "/root/reference"
     ref = load_reference(ref_root)
     base = scenes()
-    if "--tile-modes-only" not in sys.argv:
+    only = {a for a in sys.argv[1:] if a in ("--tile-modes-only", "--wide-only")}
+    if not only:
         for i, (name, scene) in enumerate(base.items()):
             data = golden_case(ref, name, scene, seed=100 + i)
             np.savez_compressed(os.path.join(HERE, f"gs3d_{name}.npz"), **data)
+    if not only or "--wide-only" in only:
+        for name in ("c1_sh3", "dense_sh1"):
+            data = wide_case(ref, name, base[name], seed=300)
+            np.savez_compressed(os.path.join(HERE, f"wide_{name}.npz"), **data)
+    if only and "--tile-modes-only" not in only:
+        return
     for name, scene in tile_mode_scenes(base).items():
         data = tile_mode_case(ref, name, scene)
         np.savez_compressed(os.path.join(HERE, f"tilemodes_{name}.npz"), **data)

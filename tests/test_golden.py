@@ -149,3 +149,29 @@ def test_tile_modes(path, mode):
 
 def test_tile_mode_fixtures_present():
     assert len(TILE_MODE_FIXTURES) == 3
+
+
+WIDE_FIXTURES = sorted(glob.glob(os.path.join(ROOT, "tests", "golden", "wide_*.npz")))
+
+
+@pytest.mark.parametrize("path", WIDE_FIXTURES, ids=[os.path.basename(p)[5:-4]
+                                                     for p in WIDE_FIXTURES])
+def test_oracle_wide_blend(path):
+    """Eight blended channels over a random background, forward and backward:
+    the oracle against the reference's own kernels."""
+    with np.load(path) as z:
+        g = {k: z[k] for k in z.files}
+    W, H = int(g["width"]), int(g["height"])
+    image, final_t, contrib = O.render_forward(W, H, g["ranges"], g["ids"], g["centers"],
+                                               g["conics"], g["features"], g["background"])
+    np.testing.assert_array_equal(contrib, g["contributors"])
+    np.testing.assert_array_equal(final_t, g["final_t"])
+    assert np.abs(image - g["image"]).max() <= 1e-5
+    gc, gq, gf, ga = O.render_backward(W, H, g["ranges"], g["ids"], g["centers"], g["conics"],
+                                       g["features"], g["background"], g["final_t"],
+                                       g["contributors"], g["upstream"], absgrad=True,
+                                       constant_tail=1)
+    assert rel_l2(gc, g["grad_centers"]) <= 1e-5
+    assert rel_l2(gq, g["grad_conics"]) <= 1e-5
+    assert rel_l2(gf, g["grad_features"]) <= 1e-5
+    assert rel_l2(ga, g["grad_abs"]) <= 1e-5

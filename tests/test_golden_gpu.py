@@ -112,3 +112,41 @@ def test_gpu_tile_modes_match_reference_kernels(path, mode):
     bins = stages.bin_and_sort(st, W, H, tile_mode=mode)
     np.testing.assert_array_equal(bins["ranges"].cpu().numpy(), g[f"{mode}_ranges"])
     np.testing.assert_array_equal(bins["point_list"].cpu().numpy(), g[f"{mode}_ids"])
+
+
+WIDE_FIXTURES = sorted(glob.glob(os.path.join(ROOT, "tests", "golden", "wide_*.npz")))
+
+
+@pytest.mark.parametrize("path", WIDE_FIXTURES, ids=[os.path.basename(p)[5:-4]
+                                                     for p in WIDE_FIXTURES])
+def test_gpu_wide_blend_and_statistics(path):
+    """Eight channels (colours, four extras, the constant one) over a random
+    background with a masked-count and a weighted-sum statistics request,
+    forward and backward, against the reference's own kernels."""
+    from dsl_splat_b200.statistics import PreparedStatistics
+    with np.load(path) as z:
+        g = {k: z[k] for k in z.files}
+    W, H = int(g["width"]), int(g["height"])
+    n = len(g["centers"])
+    st = stages.ProjectedFootprint(_t(g["centers"]), _t(g["conics"]))
+    bins = dict(ranges=_t(g["ranges"]), point_list=_t(g["ids"]))
+    feats = g["features"]
+    a, b, bg = _t(feats[:, :3]), _t(feats[:, 3:7]), _t(g["background"])
+    stats = PreparedStatistics(
+        key=(0, 1), pixel_values=_t(np.stack([g["mask"].ravel(), g["weights"].ravel()])),
+        counts=torch.zeros((1, n), dtype=torch.int32, device="cuda:0"),
+        sums=torch.zeros((1, n), device="cuda:0"))
+    px = stages.render(st, bins, a, b, True, bg, W, H, planar=True, statistics=stats)
+    np.testing.assert_array_equal(px.contributors.cpu().numpy(), g["contributors"])
+    np.testing.assert_array_equal(px.transmittance.cpu().numpy(), g["final_t"])
+    assert np.abs(px.features.cpu().numpy() - g["image"]).max() <= 1e-5
+    np.testing.assert_array_equal(stats.counts[0].cpu().numpy(), g["stat_counts"])
+    assert rel_l2(stats.sums[0].cpu().numpy(), g["stat_sums"]) <= 1e-5
+    gc, gq, ga, gb, gabs = stages.render_backward(
+        st, bins, a, b, True, bg, px.transmittance, px.contributors, _t(g["upstream"]), W, H,
+        planar=True, absgrad=True, constant_tail=1)
+    assert rel_l2(gc.cpu(), g["grad_centers"]) <= 1e-3
+    assert rel_l2(gq.cpu(), g["grad_conics"]) <= 1e-3
+    assert rel_l2(ga.cpu(), g["grad_features"][:, :3]) <= 1e-3
+    assert rel_l2(gb.cpu(), g["grad_features"][:, 3:7]) <= 1e-3
+    assert rel_l2(gabs.cpu(), g["grad_abs"]) <= 1e-3
