@@ -175,3 +175,135 @@ def test_oracle_wide_blend(path):
     assert rel_l2(gq, g["grad_conics"]) <= 1e-5
     assert rel_l2(gf, g["grad_features"]) <= 1e-5
     assert rel_l2(ga, g["grad_abs"]) <= 1e-5
+
+
+# ---- projection VJP against float64 autograd with the reference's adjoints --
+#
+# The reference differentiates projection_loss (gs3d/projection.py:198-210)
+# with Warp autodiff, which the shim cannot run; the oracle's VJP is
+# hand-derived.  This restates projection_loss in float64 Torch, with the
+# reference's three custom adjoints as autograd Functions, and checks the
+# oracle's gradients against autograd's.
+
+import torch  # noqa: E402
+
+
+class _Rotation(torch.autograd.Function):
+    """glm_rotation (primitives/math.py:33-45) with adj_reference_rotation
+    (splatting/math.py:13-28)."""
+
+    @staticmethod
+    def forward(ctx, q):
+        ctx.save_for_backward(q)
+        r, x, y, z = q.unbind(-1)
+        rows = [[1 - 2 * (y * y + z * z), 2 * (x * y + r * z), 2 * (x * z - r * y)],
+                [2 * (x * y - r * z), 1 - 2 * (x * x + z * z), 2 * (y * z + r * x)],
+                [2 * (x * z + r * y), 2 * (y * z - r * x), 1 - 2 * (x * x + y * y)]]
+        return torch.stack([torch.stack(row, -1) for row in rows], -2)
+
+    @staticmethod
+    def backward(ctx, g):
+        (q,) = ctx.saved_tensors
+        r, x, y, z = q.unbind(-1)
+        G = lambda i, j: g[..., i, j]  # noqa: E731
+        return torch.stack([
+            2 * (z * (G(0, 1) - G(1, 0)) + y * (G(2, 0) - G(0, 2)) + x * (G(1, 2) - G(2, 1))),
+            2 * (y * (G(0, 1) + G(1, 0)) + z * (G(0, 2) + G(2, 0)) + r * (G(1, 2) - G(2, 1)))
+            - 4 * x * (G(1, 1) + G(2, 2)),
+            2 * (x * (G(0, 1) + G(1, 0)) + r * (G(2, 0) - G(0, 2)) + z * (G(1, 2) + G(2, 1)))
+            - 4 * y * (G(0, 0) + G(2, 2)),
+            2 * (r * (G(0, 1) - G(1, 0)) + x * (G(0, 2) + G(2, 0)) + y * (G(1, 2) + G(2, 1)))
+            - 4 * z * (G(0, 0) + G(1, 1))], -1)
+
+
+class _Clamp(torch.autograd.Function):
+    """clamp_point with adj_clamp_point (splatting/geometry.py:33-51)."""
+
+    @staticmethod
+    def forward(ctx, t, limx, limy):
+        x, y = t[:, 0] / t[:, 2], t[:, 1] / t[:, 2]
+        ctx.save_for_backward((x >= -limx) & (x <= limx), (y >= -limy) & (y <= limy))
+        return torch.stack([x.clamp(-limx, limx) * t[:, 2], y.clamp(-limy, limy) * t[:, 2],
+                            t[:, 2]], -1)
+
+    @staticmethod
+    def backward(ctx, g):
+        in_x, in_y = ctx.saved_tensors
+        return torch.stack([g[:, 0] * in_x, g[:, 1] * in_y, g[:, 2]], -1), None, None
+
+
+class _Inverse(torch.autograd.Function):
+    """invert_covariance with adj_invert_covariance (geometry.py:54-71)."""
+
+    @staticmethod
+    def forward(ctx, cov):
+        ctx.save_for_backward(cov)
+        a, b, c = cov.unbind(-1)
+        inv = 1.0 / (a * c - b * b)
+        return torch.stack([c * inv, -b * inv, a * inv], -1)
+
+    @staticmethod
+    def backward(ctx, g):
+        (cov,) = ctx.saved_tensors
+        a, b, c = cov.unbind(-1)
+        det = a * c - b * b
+        f = 1.0 / (det * det + 1e-7)
+        x, y, z = g.unbind(-1)
+        return f[:, None] * torch.stack([
+            -c * c * x + b * c * y + (det - a * c) * z,
+            2 * b * c * x - (det + 2 * b * b) * y + 2 * a * b * z,
+            -a * a * z + a * b * y + (det - a * c) * x], -1)
+
+
+def _projection_loss(means, quats, scales, opac, view, proj, K, W, H, seed_c, seed_q):
+    """gs3d/projection.py:37-86 screen_covariance + 198-210 projection_loss."""
+    fx, fy = K[0, 0], K[1, 1]
+    pos = means @ view[:3, :3].T + view[:3, 3]
+    t = _Clamp.apply(pos, 1.3 * W / (2 * fx), 1.3 * H / (2 * fy))
+    R = _Rotation.apply(quats)
+    M = scales[:, :, None] * R                       # scaling @ rotation
+    cov = M.transpose(1, 2) @ M
+    z = t[:, 2]
+    zero = torch.zeros_like(z)
+    J = torch.stack([torch.stack([fx / z, zero, zero], -1),
+                     torch.stack([zero, fy / z, zero], -1),
+                     torch.stack([-(fx * t[:, 0]) / (z * z), -(fy * t[:, 1]) / (z * z), zero],
+                                 -1)], -2)
+    camera = view[:3, :3].T                          # rows (v00, v10, v20), ...
+    T = camera @ J
+    P = (T.transpose(1, 2) @ cov.transpose(1, 2)) @ T
+    conic3 = _Inverse.apply(torch.stack([P[:, 0, 0] + 0.3, P[:, 1, 0], P[:, 1, 1] + 0.3], -1))
+    clip = means @ proj[:, :3].T + proj[:, 3]
+    inv_w = 1.0 / (clip[:, 3] + 1e-7)
+    center = torch.stack([((clip[:, 0] * inv_w + 1) * W - 1) * 0.5,
+                          ((clip[:, 1] * inv_w + 1) * H - 1) * 0.5], -1)
+    conic = torch.cat([conic3, opac[:, None]], -1)
+    return (center * seed_c).sum() + (conic * seed_q).sum()
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=[os.path.basename(p)[5:-4] for p in FIXTURES])
+def test_projection_vjp_against_float64_autograd(path):
+    g = _load(path)
+    W, H = int(g["width"]), int(g["height"])
+    vis = g["radii"] > 0
+    n = len(g["means"])
+    rng = np.random.default_rng(7)
+    seed_c = rng.standard_normal((n, 2)).astype(np.float32)
+    seed_q = (rng.standard_normal((n, 4)) * 1e-2).astype(np.float32)
+    gm, gq, gs, go, gv, gp = O.project_backward(
+        g["means"], g["quats"], g["scales"], g["opacities"], g["viewmat"], g["full"], g["K"],
+        W, H, g["radii"], seed_c, seed_q)
+
+    def t(a, grad=False):
+        return torch.tensor(np.asarray(a, np.float64), requires_grad=grad)
+
+    leaves = [t(g[k][vis], True) for k in ("means", "quats", "scales", "opacities")]
+    view, proj = t(g["viewmat"], True), t(g["full"], True)
+    loss = _projection_loss(*leaves, view, proj, t(g["K"]), W, H, t(seed_c[vis]),
+                            t(seed_q[vis]))
+    loss.backward()
+    for got, leaf, name in zip((gm, gq, gs, go), leaves, ("means", "quats", "scales", "op")):
+        assert not np.asarray(got)[~vis].any(), name  # culled rows stay zero
+        assert rel_l2(np.asarray(got)[vis], leaf.grad.numpy()) <= 1e-5, name
+    assert rel_l2(gv, view.grad.numpy()) <= 1e-5
+    assert rel_l2(gp, proj.grad.numpy()) <= 1e-5
