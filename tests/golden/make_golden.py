@@ -20,10 +20,15 @@ Warp library calls restated: array_scan (inclusive cumsum) and
 radix_sort_pairs (a stable sort of the 64-bit keys).
 
 Also: gs3d/render.py:36-208 with statistics.py:47-73's observer and eight
-channels (wide_*.npz).
+channels (wide_*.npz); and the RaDe-GS path (rade_*.npz):
+  rade/projection.py:194-260          project (ray planes, normals, radial depth,
+                                      kernel_size dilation)
+  splatting/binning.py:116-137        duplicate with the radial depths
+  rade/render.py:99-322               render (colour, depth, median, normals)
+  rade/render.py:325-547              backward (warp-reduced atomics)
 
 Usage: python tests/golden/make_golden.py [/path/to/reference]
-       [--tile-modes-only | --wide-only]
+       [--tile-modes-only | --wide-only | --rade-only]
 """
 
 from __future__ import annotations
@@ -52,7 +57,7 @@ def load_reference(ref_root: str):
     # Stub the packages so their __init__ files (which import the AAA stack)
     # are not executed; submodules load from the checkout.
     for pkg in ("dsl_splat", "dsl_splat.gs3d", "dsl_splat.splatting", "dsl_splat.primitives",
-                "dsl_splat.runtime"):
+                "dsl_splat.runtime", "dsl_splat.rade"):
         mod = types.ModuleType(pkg)
         parts = pkg.split(".")[1:]
         mod.__path__ = [os.path.join(pkg_root, *parts)]
@@ -68,6 +73,8 @@ def load_reference(ref_root: str):
         "bin": "dsl_splat.splatting.binning",
         "tiling": "dsl_splat.primitives.tiling",
         "render": "dsl_splat.gs3d.render",
+        "rade_proj": "dsl_splat.rade.projection",
+        "rade_render": "dsl_splat.rade.render",
     }
     return {k: importlib.import_module(v) for k, v in names.items()}
 
@@ -251,6 +258,131 @@ def wide_case(ref, name, scene: dict, seed: int) -> dict:
     return keep
 
 
+def rade_case(ref, name, scene: dict, seed: int, kernel_size: float, extra: int) -> dict:
+    """RaDe-GS projection, radial-depth binning, render and render backward
+    through the reference's own kernels, with SH colours (primitives/sh.py
+    forward, as rade/api.py:153-165 calls it) plus `extra` N(0,1) channels
+    and a random background over them."""
+    W, H = scene["width"], scene["height"]
+    gx, gy = (W + 15) // 16, (H + 15) // 16
+    T = gx * gy
+    deg = scene["sh_degree"]
+    means = scene["means"].astype(np.float32)
+    n = len(means)
+    quats = F.normalize(torch.from_numpy(scene["quats"].astype(np.float32)), dim=-1).numpy()
+    scales = scene["scales"].astype(np.float32)
+    opac = scene["opacities"].astype(np.float32)
+    sh = scene["sh"].astype(np.float32)
+    view = scene["viewmat"].astype(np.float32)
+    K = scene["K"].astype(np.float32)
+    wp = sys.modules["warp"]
+    t0 = time.time()
+    full = np.zeros((1, 4, 4), np.float32)
+    inverse = np.zeros((1, 4, 4), np.float32)
+    campos = np.zeros((1, 3), np.float32)
+    errors = np.zeros(1, np.int32)
+    ws.launch(ref["cam"].prepare_kernel, 1,
+              [A(view[None].copy()), A(K[None].copy()), W, H, 1, A(full), A(inverse),
+               A(campos), A(errors)])
+    assert errors[0] == 0
+    ks = np.float32(kernel_size)
+    out: dict = dict(width=W, height=H, sh_degree=deg, means=means, quats=quats,
+                     scales=scales, opacities=opac, sh=sh, viewmat=view, K=K, full=full[0],
+                     campos=campos[0], kernel_size=ks)
+
+    # rade/projection.py:194-260
+    centers = np.zeros((n, 2), np.float32)
+    conics = np.zeros((n, 4), np.float32)
+    radii = np.zeros(n, np.int32)
+    tiles = np.zeros(n, np.int32)
+    depths = np.zeros(n, np.float32)
+    planes = np.zeros((n, 3), np.float32)
+    normals = np.zeros((n, 3), np.float32)
+    ws.launch(ref["rade_proj"].project, n,
+              [A(means, wp.vec3), A(quats, wp.vec4), A(scales, wp.vec3), A(opac),
+               A(view.copy()), A(full[0].copy()), A(K.copy()), W, H, np.float32(0.2),
+               np.float32(np.inf), np.float32(0.0), ks, A(centers, wp.vec2),
+               A(conics, wp.vec4), A(radii), A(tiles), A(depths), A(planes, wp.vec3),
+               A(normals, wp.vec3)])
+    out.update(centers=centers, conics=conics, radii=radii, tiles=tiles, depths=depths,
+               planes=planes, normals=normals)
+
+    # colours: primitives/sh.py:44-79 with directions means - camera centre
+    dirs = (torch.from_numpy(means) - torch.from_numpy(campos[0])).numpy()
+    colors = np.zeros((n, 3), np.float32)
+    active = np.zeros((n, 3), np.bool_)
+    ws.launch(ref["sh"].forward_kernel(deg, True, True), n,
+              [A(sh), A(dirs), A(radii), A(colors, wp.vec3), A(active)])
+    rng = np.random.default_rng(seed)
+    extras = rng.standard_normal((n, extra)).astype(np.float32)
+    feats = np.concatenate([colors, extras], axis=1)
+    C = feats.shape[1]
+    bg = rng.uniform(0.0, 1.0, C).astype(np.float32)
+    out.update(colors=colors, extras=extras, background=bg)
+
+    # splatting/binning.py:116-137 with the radial sort distance
+    offsets = np.cumsum(tiles, dtype=np.int64).astype(np.int32)
+    m = int(offsets[-1]) if n else 0
+    keys = np.zeros(2 * m, np.uint64)
+    ids = np.zeros(2 * m, np.int32)
+    ws.launch(ref["bin"].duplicate, n, [A(centers, wp.vec2), A(radii), A(depths), A(offsets),
+                                         gx, gy, A(keys), A(ids)])
+    order = np.argsort(keys[:m], kind="stable")
+    keys_sorted, ids_sorted = keys[:m][order], ids[:m][order]
+    ranges = np.zeros((T, 2), np.int32)
+    ws.launch(ref["tiling"].identify_ranges, m, [A(keys_sorted), A(ranges)])
+    out.update(keys=keys_sorted, ids=ids_sorted, ranges=ranges)
+
+    # rade/render.py:99-322
+    Feature = wp.types.vector(C, np.float32)
+    image = np.zeros((C + 6) * H * W, np.float32)
+    aux = np.zeros(2 * H * W, np.float32)
+    contrib = np.zeros(2 * H * W, np.int32)
+    ws.launch(ref["rade_render"]._make_forward(C, ()), 256 * T,
+              [W, H, A(ranges), A(ids_sorted), A(centers, wp.vec2), A(conics, wp.vec4),
+               A(feats, Feature), A(bg), A(image), A(aux), A(contrib), A(planes, wp.vec3),
+               A(normals, wp.vec3), A(K.copy())], block=256)
+    out.update(image=image.reshape(C + 6, H, W), auxiliary=aux.reshape(2, H, W),
+               contributors=contrib.reshape(2, H, W))
+
+    # rade/render.py:325-547 with every upstream image seeded N(0,1)
+    up = {k: rng.standard_normal((H, W, c)).astype(np.float32)
+          for k, c in (("up_features", C), ("up_alpha", 1), ("up_depth", 1), ("up_median", 1),
+                       ("up_normals", 3))}
+    grads = {k: np.zeros((n, c), np.float32)
+             for k, c in (("grad_centers", 2), ("grad_conics", 4), ("grad_features", C),
+                          ("grad_abs", 2), ("grad_planes", 3), ("grad_normals", 3))}
+    ws.launch(ref["rade_render"]._make_backward(C, True), 256 * T,
+              [W, H, A(ranges), A(ids_sorted), A(centers, wp.vec2), A(conics, wp.vec4),
+               A(feats, Feature), A(bg), A(image), A(aux), A(planes, wp.vec3),
+               A(normals, wp.vec3), A(K.copy()), A(contrib),
+               *(A(up[k]) for k in ("up_features", "up_alpha", "up_depth", "up_median",
+                                    "up_normals")),
+               A(grads["grad_centers"], wp.vec2), A(grads["grad_conics"], wp.vec4),
+               A(grads["grad_features"], Feature), A(grads["grad_abs"], wp.vec2),
+               A(grads["grad_planes"], wp.vec3), A(grads["grad_normals"], wp.vec3)],
+              block=256)
+    out.update(up)
+    out.update(grads)
+    print(f"rade_{name}: n={n} visible={int((radii > 0).sum())} pairs={m} tiles={T} C={C} "
+          f"kernel_size={kernel_size} in {time.time() - t0:.1f}s", flush=True)
+    return out
+
+
+def rade_scenes(base: dict) -> dict:
+    """The c1 geometry (SH3), the dense scene (SH1, early termination, culled
+    rows) and its copy with near-degenerate Gaussians: a flat axis below
+    1e-7 (rade/projection.py:150-159's outer-product branch) in each of the
+    three positions."""
+    out = {"c1_sh3": base["c1_sh3"], "dense_sh1": base["dense_sh1"]}
+    flat = {k: (v.copy() if isinstance(v, np.ndarray) else v)
+            for k, v in base["dense_sh1"].items()}
+    for i in range(60, 90):
+        flat["scales"][i, i % 3] = 1e-8
+    out["flat_sh1"] = flat
+    return out
+
+
 def tile_mode_case(ref, name, scene: dict) -> dict:
     """Projection tile counts and binning for tile_mode snugbox and accutile
     (gs3d/projection.py:150-162, splatting/intersections.py:45-218,
@@ -386,7 +518,7 @@ def main():
     ref_root = args[0] if args else "/root/reference"
     ref = load_reference(ref_root)
     base = scenes()
-    only = {a for a in sys.argv[1:] if a in ("--tile-modes-only", "--wide-only")}
+    only = {a for a in sys.argv[1:] if a in ("--tile-modes-only", "--wide-only", "--rade-only")}
     if not only:
         for i, (name, scene) in enumerate(base.items()):
             data = golden_case(ref, name, scene, seed=100 + i)
@@ -395,6 +527,10 @@ def main():
         for name in ("c1_sh3", "dense_sh1"):
             data = wide_case(ref, name, base[name], seed=300)
             np.savez_compressed(os.path.join(HERE, f"wide_{name}.npz"), **data)
+    if not only or "--rade-only" in only:
+        for name, ks, extra in (("c1_sh3", 0.0, 4), ("dense_sh1", 0.3, 0), ("flat_sh1", 0.1, 5)):
+            data = rade_case(ref, name, rade_scenes(base)[name], 500, ks, extra)
+            np.savez_compressed(os.path.join(HERE, f"rade_{name}.npz"), **data)
     if only and "--tile-modes-only" not in only:
         return
     for name, scene in tile_mode_scenes(base).items():

@@ -1,4 +1,5 @@
-"""A CPU stand-in for the subset of NVIDIA Warp used by dsl_splat's gs3d kernels.
+"""A CPU stand-in for the subset of NVIDIA Warp used by dsl_splat's gs3d and
+RaDe-GS kernels.
 
 Test infrastructure only.  warp-lang is not installable here, so to pin the
 CPU oracle against the reference itself, make_golden.py imports the
@@ -15,8 +16,13 @@ reference's own kernel source on the CPU:
   (-ffp-contract=off) and called through ctypes; the block primitives
   (__syncthreads, __syncthreads_count, __shared__ arrays) are emulated by
   running each 256-thread block as 256 Python threads with a barrier;
+  the warp intrinsics (__any_sync, and the shuffle-down lane sums of
+  primitives/warp.py) exchange values among the 32 threads of a warp and
+  reproduce the shuffle-down tree's float32 summation order;
 * `wp.exp` is the same Cody-Waite exp the oracle and the CUDA kernels use
-  (the one deliberate substitution; CUDA's expf is not reproducible here).
+  (a deliberate substitution; CUDA's expf is not reproducible here), and
+  `norm3df` (rade/projection.py:33) is sqrtf(x*x + y*y + z*z) in IEEE
+  float32, as the oracle and the CUDA kernels compute the sort distance.
 
 Arithmetic is IEEE float32 without contraction, i.e. the reference's kernel
 logic, not Warp's NVRTC code generation.
@@ -165,6 +171,18 @@ class Mat:
     def __setitem__(self, idx, value):
         self.m[idx[0]][idx[1]] = _wp_f32(value)
 
+    def __mul__(self, o):
+        """Matrix-vector product, each row summed left to right."""
+        if not isinstance(o, Vec):
+            raise TypeError("matrix * non-vector")
+        out = []
+        for row in self.m:
+            acc = row[0] * o.v[0]
+            for a, b in zip(row[1:], o.v[1:]):
+                acc = acc + a * b
+            out.append(acc)
+        return vector(type(self).rows)(*out)
+
 
 _mat_types: dict = {}
 
@@ -275,6 +293,8 @@ def kernel(fn=None, **options):
 
 
 def func(fn):
+    if fn.__name__ in _FUNC_NATIVES and fn.__module__.endswith("primitives.warp"):
+        return _FUNC_NATIVES[fn.__name__]
     out = _recompile(fn)
     out.__wp_source__ = fn
     return out
@@ -320,6 +340,7 @@ static inline float __fmul_rn(float a, float b) { return a * b; }
 static inline float __fadd_rn(float a, float b) { return a + b; }
 static inline float __fsub_rn(float a, float b) { return a - b; }
 static inline uint32_t __float_as_uint(float v) { uint32_t u; std::memcpy(&u, &v, 4); return u; }
+static inline float norm3df(float a, float b, float c) { return std::sqrt(a * a + b * b + c * c); }
 """
 
 _C_TYPES = {}  # annotation -> (c type, n floats, kind)
@@ -427,6 +448,14 @@ class _Block:
         self.shared: dict = {}
         self.flags = [False] * size
         self.lock = threading.Lock()
+        warps = (size + 31) // 32
+        self.warp_barriers = [threading.Barrier(min(32, size - 32 * w)) for w in range(warps)]
+        self.warp_slots = [[None] * 32 for _ in range(warps)]
+
+    def abort(self):
+        self.barrier.abort()
+        for b in self.warp_barriers:
+            b.abort()
 
 
 def _block() -> _Block:
@@ -446,6 +475,55 @@ def _all_done(done):
     return count == b.size
 
 
+def _warp_exchange(value):
+    """Every lane's value, in lane order, for the 32 threads of this warp."""
+    b = _block()
+    w, lane = _state.lane // 32, _state.lane % 32
+    b.warp_slots[w][lane] = value
+    b.warp_barriers[w].wait()
+    values = list(b.warp_slots[w])
+    b.warp_barriers[w].wait()
+    return values
+
+
+def _any_active(predicate):
+    """__any_sync(0xffffffff, predicate) (primitives/warp.py:12-13)."""
+    return any(bool(v) for v in _warp_exchange(bool(predicate)))
+
+
+def _shuffle_tree(values):
+    """The float32 result of primitives/warp.py:20-25 in every lane: five
+    __shfl_down_sync steps (16, 8, 4, 2, 1); a lane whose source is past the
+    warp reads its own value, as __shfl_down_sync does."""
+    v = list(values)
+    n = len(v)
+    for offset in (16, 8, 4, 2, 1):
+        v = [v[i] + (v[i + offset] if i + offset < n else v[i]) for i in range(n)]
+    return v
+
+
+def _sum_lanes(value):
+    return _shuffle_tree(_warp_exchange(value))[_state.lane % 32]
+
+
+def _sum_vector_lanes(value):
+    """primitives/warp.py:28-32: each component reduced with sum_lanes."""
+    rows = _warp_exchange(value)
+    lane = _state.lane % 32
+    out = [_shuffle_tree([r.v[k] for r in rows])[lane] for k in range(len(value.v))]
+    return value._new(out)
+
+
+def _shared_flat(kind, size):
+    def make():
+        b = _block()
+        with b.lock:
+            if kind not in b.shared:
+                b.shared[kind] = Array(np.zeros(size, np.float32))
+            return b.shared[kind]
+    return make
+
+
 def _shared(kind, dtype):
     def make():
         b = _block()
@@ -459,12 +537,32 @@ def _shared(kind, dtype):
     return make
 
 
+def _shared_rows(kind, rows, dtype):
+    def make():
+        b = _block()
+        with b.lock:
+            if kind not in b.shared:
+                b.shared[kind] = Array(np.zeros((rows, dtype.length), np.float32), dtype)
+            return b.shared[kind]
+    return make
+
+
+# @wp.func bodies replaced by an equivalent of the same float32 arithmetic
+# (lane exchange instead of five shuffles each)
+_FUNC_NATIVES = {"sum_lanes": _sum_lanes, "sum_vector_lanes": _sum_vector_lanes}
+
+
 def _install_block_natives():
     _BLOCK_NATIVES["synchronize"] = _synchronize
     _BLOCK_NATIVES["all_done"] = _all_done
     _BLOCK_NATIVES["shared_ids"] = _shared("ids", int)
     _BLOCK_NATIVES["shared_centers"] = _shared("centers", vector(2))
     _BLOCK_NATIVES["shared_conics"] = _shared("conics", vector(4))
+    # rade/render.py:60-96: channel-major feature cache (up to 32 channels)
+    # and the 512 staged (plane, normal) rows
+    _BLOCK_NATIVES["shared_features"] = _shared_flat("features", 256 * 32)
+    _BLOCK_NATIVES["shared_geometry"] = _shared_rows("geometry", 512, vector(3))
+    _BLOCK_NATIVES["any_active"] = _any_active
 
 
 def tid():
@@ -486,7 +584,7 @@ def launch(kernel_obj: Kernel, dim: int, args, block: int | None = None):
             kernel_obj(*args)
         except BaseException as e:  # surface thread failures
             errors.append(e)
-            blk.barrier.abort()
+            blk.abort()
 
     for start in range(0, dim, block):
         blk = _Block(block)
@@ -572,6 +670,26 @@ def dot(a, b):
     return acc
 
 
+def length_sq(a):
+    return dot(a, a)
+
+
+def normalize(a):
+    """Warp's normalize: a / length(a) per component, zero when length is 0."""
+    n = length(a)
+    if n > 0:
+        return a / n
+    return a._new([0.0] * len(a.v))
+
+
+def outer(a, b):
+    out = matrix(len(a.v), len(b.v))()
+    for r, x in enumerate(a.v):
+        for c, y in enumerate(b.v):
+            out.m[r][c] = x * y
+    return out
+
+
 def length(a):
     return sqrt(dot(a, a))
 
@@ -599,6 +717,9 @@ def atomic_add(arr: Array, *idx_and_value):
     key = tuple(idx) if len(idx) > 1 else idx[0]
     with _atomic_lock:
         old = arr.data[key]
+        if isinstance(value, Vec):
+            arr.data[key] = old + np.array(value.v, dtype=arr.data.dtype)
+            return None
         arr.data[key] = old + value
         return old
 
@@ -700,7 +821,7 @@ def make_module() -> types.ModuleType:
                  "array3d", "tid", "static", "min", "max", "clamp", "sqrt", "ceil", "floor",
                  "abs", "log", "exp", "isfinite", "dot", "length", "transpose", "determinant",
                  "inverse", "atomic_add", "uint64", "uint32", "float64", "grad", "constant",
-                 "adjoint", "launch"):
+                 "adjoint", "launch", "normalize", "outer", "length_sq"):
         setattr(m, name, getattr(this, name))
     m.float32 = F32
     m.int32 = np.int32
