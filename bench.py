@@ -39,7 +39,9 @@ METRIC = "fwd+bwd frames/s, 3DGS SH3 1M Gaussians @1080p"
 # other configs (parity cases, or --config 2 for the batched multi-view scene)
 # report the same unit under their own name
 CONFIG_METRICS = {2: "fwd+bwd frames/s (camera views), 3DGS SH3 3M Gaussians, 8 cameras "
-                     "1296x840"}
+                     "1296x840",
+                  4: "fwd+bwd frames/s, RaDe-GS SH3 1M Gaussians + 32 extra channels, depth/"
+                     "median/normals @1600x1200"}
 
 
 def metric_for(config: int) -> str:
@@ -97,9 +99,11 @@ def workload(config: int, rank: int, world: int):
 def describe(s, world):
     views = s.viewmats.shape[0]
     total = s.meta.get("cameras", world)
+    api = "rade.rasterize" if s.meta["config"] == 4 else "gs3d.rasterize"
+    extra = f" + {s.extras.shape[1]} extra channels" if s.extras is not None else ""
     return {
-        "workload": f"config{s.meta['config']}: gs3d.rasterize SH{s.sh_degree} "
-                    f"{s.means.shape[0]} Gaussians {s.width}x{s.height}, fwd+bwd, absgrad",
+        "workload": f"config{s.meta['config']}: {api} SH{s.sh_degree} "
+                    f"{s.means.shape[0]} Gaussians{extra} {s.width}x{s.height}, fwd+bwd, absgrad",
         "n_gaussians": int(s.means.shape[0]), "width": s.width, "height": s.height,
         "sh_degree": s.sh_degree, "views_per_gpu": views, "global_batch": total,
         "parallelism": f"camera-sharded dp{world}",
@@ -265,11 +269,18 @@ def profile_traffic(kernel: str):
 
 
 def algorithmic_bytes(kernel: str, n: int, nv: int, m: int, pixels: int, c: int = CHANNELS):
-    """Per-launch algorithmic bytes of the blend kernels (the survey's per-view model)."""
+    """Per-launch algorithmic bytes of the blend kernels (the survey's per-view model;
+    RaDe-GS adds the 24-byte plane and normal rows per staged pair, the five
+    geometry planes plus auxiliary and contributor planes per pixel)."""
     if kernel == "render_forward":
         return 4 * m + m * (24 + 4 * c) + pixels * (4 * c + 8)
     if kernel == "render_backward":
         return pixels * (4 * c + 8) + 4 * m + m * (24 + 4 * c) + n * (24 + 4 * c + 8)
+    if kernel == "rade_render_forward":
+        return 4 * m + m * (48 + 4 * c) + pixels * (4 * (c + 6) + 16)
+    if kernel == "rade_render_backward":
+        return (pixels * (4 * (c + 6) + 16 + 4 * (c + 6)) + 4 * m + m * (48 + 4 * c)
+                + n * (24 + 4 * c + 8 + 24))
     raise KeyError(kernel)
 
 
@@ -285,7 +296,7 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     pg = None
-    from dsl_splat_b200 import gs3d, sharding, stages
+    from dsl_splat_b200 import gs3d, rade, sharding, stages
     from dsl_splat_b200._native import lib
     if world > 1:
         import torch.distributed as dist
@@ -303,6 +314,30 @@ def main():
     gF, gA = s.grad_image.to(dev), s.grad_alpha.to(dev)
     W, H = s.width, s.height
     last = {}
+    is_rade = args.config == 4
+    if is_rade:
+        # RaDe-GS: 32 extra channels blended with RGB and
+        # seeded N(0,1) upstream gradients for depth, median depth and normals
+        extras = s.extras.to(dev).requires_grad_(True)
+        params.append(extras)
+        gen = torch.Generator().manual_seed(4004)
+        views0 = s.viewmats.shape[0]
+        gE = (torch.randn(views0, H, W, extras.shape[1], generator=gen) * 1e-3).to(dev)
+        gD, gM = (torch.randn(views0, H, W, 1, generator=gen).to(dev) for _ in range(2))
+        gN = torch.randn(views0, H, W, 3, generator=gen).to(dev)
+
+    def rasterize_view(vm, kk):
+        if is_rade:
+            return rade.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
+                                  extra_features=extras, absgrad=True)
+        return gs3d.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
+                              absgrad=True)
+
+    def outputs_and_grads(res):
+        if is_rade:
+            return ([res.features, res.extra_features, res.alpha, res.depth, res.median_depth,
+                     res.normals], [gF, gE, gA, gD, gM, gN])
+        return [res.features, res.alpha], [gF, gA]
 
     # N > 1 or several views per rank: the per-Gaussian gradients go through
     # sharding.GradientSync (one buffer per parameter that every local view
@@ -318,14 +353,12 @@ def main():
         for p in params:
             p.grad = None
         if sync is None:
-            res = gs3d.rasterize(means, quats, scales, opac, viewmats, Ks, W, H, sh_coeffs=sh,
-                                 absgrad=True)
-            torch.autograd.backward([res.features, res.alpha], [gF, gA])
+            res = rasterize_view(viewmats, Ks)
+            torch.autograd.backward(*outputs_and_grads(res))
         else:
             with sync:
-                res = gs3d.rasterize(means, quats, scales, opac, viewmats, Ks, W, H,
-                                     sh_coeffs=sh, absgrad=True)
-                torch.autograd.backward([res.features, res.alpha], [gF, gA])
+                res = rasterize_view(viewmats, Ks)
+                torch.autograd.backward(*outputs_and_grads(res))
             sync.wait()
         last["res"] = res
 
@@ -364,7 +397,8 @@ def main():
     n = int(means.shape[0])
     durations = {k: statistics.mean(a.elapsed_time(b) for a, b in v) for k, v in timers.items()}
     kernel = max(durations, key=durations.get)
-    per_launch = algorithmic_bytes(kernel, n, nv, m, W * H)
+    channels = 3 + extras.shape[1] if is_rade else CHANNELS
+    per_launch = algorithmic_bytes(kernel, n, nv, m, W * H, channels)
     achieved = per_launch / (durations[kernel] / 1000.0) / 1e9
     peak, peak_kind = measured_peak()
     roofline = {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak,
@@ -413,16 +447,20 @@ def main():
             target, vm, kk = bufs[k % 2]
             if not last:
                 prefetch(k + 1)
-            if sync is None:
-                r = gs3d.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
-                                   absgrad=True)
+            def loss_of(r):
                 loss = (r.features - target).abs().mean()
+                if is_rade:  # the geometry outputs take part in the loss as well
+                    loss = loss + 1e-2 * (r.depth.mean() + r.normals.abs().mean())
+                return loss
+
+            if sync is None:
+                r = rasterize_view(vm, kk)
+                loss = loss_of(r)
                 loss.backward()
             else:
                 with sync:
-                    r = gs3d.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
-                                       absgrad=True)
-                    loss = (r.features - target).abs().mean()
+                    r = rasterize_view(vm, kk)
+                    loss = loss_of(r)
                     loss.backward()
                 sync.wait()
             loss_host[k % 2].copy_(loss.detach(), non_blocking=True)
@@ -452,13 +490,14 @@ def main():
         e2e = {"value": frames_per_step * args.steps / (float(et.item()) / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": target_host.numel() * 4 + view_host.numel() * 4
                + k_host.numel() * 4, "d2h_bytes_per_step": 4,
-               "path": "gs3d.rasterize + L1 loss + backward; target image, viewmat, K copied "
+               "path": f"{'rade' if is_rade else 'gs3d'}.rasterize + L1 loss + backward; target "
+                       "image, viewmat, K copied "
                        "H2D from pinned memory every step (prefetched one step ahead on a copy "
                        "stream) and the loss copied D2H into pinned memory every step, read by the "
                        "host one step later"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not is_rade:
         cpu = cpu_baseline(s, args.cpu_budget)
 
     if pg is not None:

@@ -15,6 +15,7 @@
 #include "cameras.cuh"
 #include "host_runtime.h"
 #include "project.cuh"
+#include "rade.cuh"
 #include "render.cuh"
 #include "splat_common.cuh"
 
@@ -290,6 +291,86 @@ int render_dispatch(const RenderParams& p, bool backward, cudaStream_t s) {
   else
     return fail(kInvalidArgument, "at most 32 blended channels are supported");
   return check_launch(backward ? "render_backward" : "render_forward");
+}
+
+template <int CHP>
+void launch_rade(const RadeRenderParams& p, bool backward, cudaStream_t s) {
+  const unsigned tiles = static_cast<unsigned>(p.base.gx * ((p.base.height + 15) / 16));
+  const size_t smem = sizeof(RenderShared<CHP>) + sizeof(RadeShared);
+  if (backward) {
+    if (smem > 32 * 1024)
+      cudaFuncSetAttribute(rade_backward_kernel<CHP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+    rade_backward_kernel<CHP><<<tiles, kBlock, smem, counted(s)>>>(p);
+  } else {
+    if (smem > 32 * 1024)
+      cudaFuncSetAttribute(rade_forward_kernel<CHP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem));
+    rade_forward_kernel<CHP><<<tiles, kBlock, smem, counted(s)>>>(p);
+  }
+}
+
+int rade_render_dispatch(const RadeRenderParams& p, bool backward, cudaStream_t s) {
+  const int c = p.base.channels;
+  if (c <= 4)
+    launch_rade<4>(p, backward, s);
+  else if (c <= 8)
+    launch_rade<8>(p, backward, s);
+  else if (c <= 16)
+    launch_rade<16>(p, backward, s);
+  else if (c <= 32)
+    launch_rade<32>(p, backward, s);
+  else if (c <= 36)
+    launch_rade<36>(p, backward, s);
+  else if (c <= 48)
+    launch_rade<48>(p, backward, s);
+  else if (c <= 64)
+    launch_rade<64>(p, backward, s);
+  else
+    return fail(kInvalidArgument, "at most 64 blended channels are supported");
+  return check_launch(backward ? "rade_render_backward" : "rade_render_forward");
+}
+
+// Shared argument checks and RenderParams fields of the two rade blend entries.
+int rade_render_params(int width, int height, const int* ranges, const int* tile_order,
+                       const int* ids, long long num_ids, int n, const float* centers,
+                       const float* conics, const float* planes, const float* normals,
+                       const float* colors, int ch_a, int stride_a, const float* extras, int ch_b,
+                       int stride_b, const float* background, const float* K,
+                       RadeRenderParams& p) {
+  if (width <= 0 || height <= 0 || ch_a < 0 || ch_b < 0 || ch_a + ch_b <= 0 || n < 0 ||
+      num_ids < 0 || num_ids >= (1LL << 31) || (ch_a > 0 && (!colors || stride_a < ch_a)) ||
+      (ch_b > 0 && (!extras || stride_b < ch_b)))
+    return fail(kInvalidArgument, "bad rade render sizes");
+  if (!ranges || !ids || !centers || !conics || !planes || !normals || !background || !K)
+    return fail(kInvalidArgument, "null rade render input");
+  if (!aligned(centers, 8) || !aligned(conics, 16))
+    return fail(kInvalidArgument, "center rows need 8-byte and conic rows 16-byte alignment");
+  p = RadeRenderParams{};
+  RenderParams& b = p.base;
+  b.width = width;
+  b.height = height;
+  b.gx = (width + 15) / 16;
+  b.ranges = ranges;
+  b.tile_order = tile_order;
+  b.ids = ids;
+  b.num_ids = static_cast<int>(num_ids);
+  b.n_gaussians = n;
+  b.centers = centers;
+  b.conics = conics;
+  b.feat_a = colors;
+  b.ch_a = ch_a;
+  b.stride_a = stride_a;
+  b.feat_b = extras;
+  b.ch_b = ch_b;
+  b.stride_b = stride_b;
+  b.append_one = 0;
+  b.channels = ch_a + ch_b;
+  b.background = background;
+  p.planes = planes;
+  p.normals = normals;
+  p.K = K;
+  return kOk;
 }
 
 }  // namespace
@@ -1088,6 +1169,161 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
       !aligned(grad_conics, 16) || !aligned(abs_centers, 8))
     return fail(kInvalidArgument, "center rows need 8-byte and conic rows 16-byte alignment");
   return render_dispatch(p, true, as_stream(stream));
+}
+
+// ---- RaDe-GS ----------------------------------------------------------------
+
+int splat_rade_project_forward(int n, const float* means, const float* quats,
+                               const float* scales, const float* opacities, const float* view,
+                               const float* proj, const float* K, int width, int height,
+                               float near_plane, float far_plane, float radius_clip,
+                               float kernel_size, float* centers, float* conics, int* radii,
+                               int* tiles, float* depths, float* planes, float* normals,
+                               void* stream) {
+  if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (!(kernel_size >= 0.0f)) return fail(kInvalidArgument, "kernel_size must be nonnegative");
+  if (n == 0) return kOk;
+  if (!means || !quats || !scales || !opacities || !view || !proj || !K || !centers || !conics ||
+      !radii || !tiles || !depths || !planes || !normals)
+    return fail(kInvalidArgument, "null rade projection buffer");
+  RadeProjectParams p{};
+  p.n = n;
+  p.means = means;
+  p.quats = quats;
+  p.scales = scales;
+  p.opacities = opacities;
+  p.view = view;
+  p.proj = proj;
+  p.K = K;
+  p.width = width;
+  p.height = height;
+  p.near_plane = near_plane;
+  p.far_plane = far_plane;
+  p.radius_clip = radius_clip;
+  p.kernel_size = kernel_size;
+  p.centers = centers;
+  p.conics = conics;
+  p.radii = radii;
+  p.tiles = tiles;
+  p.depths = depths;
+  p.planes = planes;
+  p.normals = normals;
+  rade_project_kernel<<<blocks_for(n, 256), 256, 0, counted(as_stream(stream))>>>(p);
+  return check_launch("rade_project_forward");
+}
+
+int splat_rade_project_backward(int n, const float* means, const float* quats,
+                                const float* scales, const float* opacities, const float* view,
+                                const float* proj, const float* K, int width, int height,
+                                float kernel_size, const int* radii, const float* seed_centers,
+                                const float* seed_conics, const float* seed_planes,
+                                const float* seed_normals, float* grad_means, float* grad_quats,
+                                float* grad_scales, float* grad_opacities, float* grad_view,
+                                float* grad_proj, void* stream) {
+  if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (n == 0) return kOk;
+  if (!means || !quats || !scales || !opacities || !view || !proj || !K || !radii)
+    return fail(kInvalidArgument, "null rade projection buffer");
+  RadeProjectParams p{};
+  p.n = n;
+  p.means = means;
+  p.quats = quats;
+  p.scales = scales;
+  p.opacities = opacities;
+  p.view = view;
+  p.proj = proj;
+  p.K = K;
+  p.width = width;
+  p.height = height;
+  p.kernel_size = kernel_size;
+  p.radii = const_cast<int*>(radii);
+  p.seed_centers = seed_centers;
+  p.seed_conics = seed_conics;
+  p.seed_planes = seed_planes;
+  p.seed_normals = seed_normals;
+  p.grad_means = grad_means;
+  p.grad_quats = grad_quats;
+  p.grad_scales = grad_scales;
+  p.grad_opacities = grad_opacities;
+  p.grad_view = grad_view;
+  p.grad_proj = grad_proj;
+  // grid-stride: a few blocks per SM keep the camera atomics per block few
+  const unsigned blocks = std::min(blocks_for(n, 256), static_cast<unsigned>(4 * sm_count()));
+  rade_project_backward_kernel<<<blocks, 256, 0, counted(as_stream(stream))>>>(p);
+  return check_launch("rade_project_backward");
+}
+
+int splat_rade_render_forward(int width, int height, const int* ranges, const int* ids,
+                              long long num_ids, int n, const float* centers, const float* conics,
+                              const float* planes, const float* normals, const float* colors,
+                              int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
+                              const float* background, const float* K, float* image,
+                              float* auxiliary, int* contributors, int stat_count,
+                              int stat_sum_mask, const float* stat_pixels, int* stat_counts,
+                              float* stat_sums, const int* tile_order, void* stream) {
+  RadeRenderParams p;
+  const int rc = rade_render_params(width, height, ranges, tile_order, ids, num_ids, n, centers,
+                                    conics, planes, normals, colors, ch_a, stride_a, extras, ch_b,
+                                    stride_b, background, K, p);
+  if (rc != kOk) return rc;
+  if (!image || !auxiliary || !contributors) return fail(kInvalidArgument, "null rade output");
+  if (stat_count < 0 || stat_count > 30 || (stat_count > 0 && !stat_pixels))
+    return fail(kInvalidArgument, "bad statistics arguments");
+  p.image = image;
+  p.auxiliary = auxiliary;
+  p.contributors = contributors;
+  p.base.stat_count = stat_count;
+  p.base.stat_sum_mask = stat_sum_mask;
+  p.base.stat_pixels = stat_pixels;
+  p.base.stat_counts = stat_counts;
+  p.base.stat_sums = stat_sums;
+  return rade_render_dispatch(p, false, as_stream(stream));
+}
+
+int splat_rade_render_backward(
+    int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
+    const float* centers, const float* conics, const float* planes, const float* normals,
+    const float* colors, int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
+    const float* background, const float* K, const float* image, const float* auxiliary,
+    const int* contributors, const float* up_features, int up_feat_pix, int up_feat_ch,
+    const float* up_alpha, int up_alpha_pix, const float* up_depth, int up_depth_pix,
+    const float* up_median, int up_median_pix, const float* up_normals, int up_normals_pix,
+    int up_normals_ch, float* grad_centers, float* grad_conics, float* grad_colors,
+    float* grad_extras, float* abs_centers, float* grad_planes, float* grad_normals,
+    const int* tile_order, void* stream) {
+  RadeRenderParams p;
+  const int rc = rade_render_params(width, height, ranges, tile_order, ids, num_ids, n, centers,
+                                    conics, planes, normals, colors, ch_a, stride_a, extras, ch_b,
+                                    stride_b, background, K, p);
+  if (rc != kOk) return rc;
+  if (!image || !auxiliary || !contributors) return fail(kInvalidArgument, "null rade forward output");
+  if (!grad_centers || !grad_conics || !grad_planes || !grad_normals)
+    return fail(kInvalidArgument, "null gradient buffers");
+  if (!aligned(grad_centers, 8) || !aligned(grad_conics, 16) || !aligned(abs_centers, 8))
+    return fail(kInvalidArgument, "center rows need 8-byte and conic rows 16-byte alignment");
+  p.image = const_cast<float*>(image);
+  p.auxiliary = const_cast<float*>(auxiliary);
+  p.contributors = const_cast<int*>(contributors);
+  p.up_features = up_features;
+  p.up_feat_pix = up_feat_pix;
+  p.up_feat_ch = up_feat_ch;
+  p.up_alpha = up_alpha;
+  p.up_alpha_pix = up_alpha_pix;
+  p.up_depth = up_depth;
+  p.up_depth_pix = up_depth_pix;
+  p.up_median = up_median;
+  p.up_median_pix = up_median_pix;
+  p.up_normals = up_normals;
+  p.up_normals_pix = up_normals_pix;
+  p.up_normals_ch = up_normals_ch;
+  p.base.grad_centers = grad_centers;
+  p.base.grad_conics = grad_conics;
+  p.base.grad_a = grad_colors;
+  p.base.grad_b = grad_extras;
+  p.base.abs_centers = abs_centers;
+  p.grad_planes = grad_planes;
+  p.grad_normals = grad_normals;
+  return rade_render_dispatch(p, true, as_stream(stream));
 }
 
 // ---- diagnostics --------------------------------------------------------------

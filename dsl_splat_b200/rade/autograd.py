@@ -1,0 +1,110 @@
+"""RaDe-GS autograd bridges (rade/autograd.py:17-189, rade/ops.py:70-242).
+
+The reference wraps binning, rendering, the render backward and the
+projection backward into one Function per view, with the projection done
+beforehand under no_grad.  Here the projection and the blend are two
+Functions joined by ordinary autograd edges (centers, conics, ray planes,
+normals): the same gradients, with the SH colours (a separate autograd
+Function in both) in between.  The blend Function takes the view's bins
+and the training-metadata targets (|d means2d| sums, the means2d leaf).
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+from torch import Tensor
+from torch.autograd.function import once_differentiable
+
+from ..training import AbsGradientTarget, ScreenGradientTarget
+from . import projection, render
+from .projection import ProjectedGaussians, ViewConfig
+
+
+class Project(torch.autograd.Function):
+    """rade/ops.py:70-165 _Project: differentiable centers, conics, ray
+    planes and normals; radii, tile counts and sort distances are discrete."""
+
+    @staticmethod
+    def forward(ctx: Any, means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor,
+                view: Tensor, full: Tensor, intrinsics: Tensor, config: ViewConfig,
+                grad_enabled: bool):
+        means, quats, scales = means.contiguous(), quats.contiguous(), scales.contiguous()
+        opacities, view, full = opacities.contiguous(), view.contiguous(), full.contiguous()
+        intrinsics = intrinsics.contiguous()
+        st = projection.prepare(means, quats, scales, opacities, view, full, intrinsics, config)
+        if grad_enabled and any(ctx.needs_input_grad[:6]):
+            ctx.save_for_backward(means, quats, scales, opacities, view, full, intrinsics,
+                                  st.radii)
+            ctx.config = config
+        ctx.mark_non_differentiable(st.radii, st.tile_counts, st.depths)
+        ctx.set_materialize_grads(False)
+        return (st.centers, st.conics, st.radii, st.tile_counts, st.depths, st.ray_planes,
+                st.normals)
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx: Any, g_centers, g_conics, _radii, _tiles, _depths, g_planes, g_normals):
+        if all(g is None for g in (g_centers, g_conics, g_planes, g_normals)):
+            return (None,) * 9
+        means, quats, scales, opacities, view, full, intrinsics, radii = ctx.saved_tensors
+        state = ProjectedGaussians(None, None, radii, None, None, None, None)
+        grads = projection.backward(means, quats, scales, opacities, view, full, intrinsics,
+                                    ctx.config, state, g_centers, g_conics, g_planes, g_normals,
+                                    tuple(ctx.needs_input_grad[:6]))
+        return (*grads, None, None, None)
+
+
+class Render(torch.autograd.Function):
+    """rade/autograd.py:17-189 (binning excluded: the bins come in) and
+    rade/ops.py:168-242 _Pixels: the five channel-last images of one view."""
+
+    @staticmethod
+    def forward(ctx: Any, centers: Tensor, conics: Tensor, planes: Tensor, normals: Tensor,
+                colors: Tensor, extras: Tensor | None, screen: Tensor | None,
+                background: Tensor, bins: dict, intrinsics: Tensor, config: ViewConfig,
+                absolute: AbsGradientTarget | None, screen_target: ScreenGradientTarget | None,
+                statistics, grad_enabled: bool):
+        state = ProjectedGaussians(centers, conics, None, None, None, planes, normals)
+        out = render.render(state, bins, colors, extras, background, intrinsics, config.width,
+                            config.height, statistics)
+        if grad_enabled and any(ctx.needs_input_grad[:7]):
+            ctx.save_for_backward(centers, conics, planes, normals, colors, extras, background,
+                                  intrinsics, out.features, out.auxiliary, out.contributors)
+            ctx.bins = {k: bins[k] for k in ("ranges", "point_list", "tile_order") if k in bins}
+            ctx.config, ctx.absolute, ctx.screen_target = config, absolute, screen_target
+        ctx.set_materialize_grads(False)
+        return out.images()
+
+    @staticmethod
+    @once_differentiable
+    def backward(ctx: Any, *gradients: Tensor | None):
+        if all(g is None for g in gradients):
+            return (None,) * 15
+        (centers, conics, planes, normals, colors, extras, background, intrinsics, image, aux,
+         contrib) = ctx.saved_tensors
+        cfg = ctx.config
+        needs = ctx.needs_input_grad
+        direct = ctx.absolute.direct_buffer() if ctx.absolute is not None else None
+        screen_direct = (ctx.screen_target.direct_buffer()
+                         if needs[6] and ctx.screen_target is not None else None)
+        state = ProjectedGaussians(centers, conics, None, None, None, planes, normals)
+        gc, gq, ga, gb, gp, gn, absolute = render.backward(
+            state, ctx.bins, colors, extras, background, intrinsics,
+            render.RenderedPixels(image, aux, contrib), gradients, cfg.width, cfg.height,
+            absgrad=ctx.absolute is not None, need_colors=needs[4],
+            need_extras=extras is not None and needs[5], centers_out=screen_direct,
+            absolute_out=direct)
+        if ctx.absolute is not None and direct is None:
+            ctx.absolute.write(absolute)
+        g_screen = None
+        if needs[6]:
+            if ctx.screen_target is not None:
+                if screen_direct is None:
+                    ctx.screen_target.add(gc)
+            else:
+                g_screen = gc
+        return (gc if needs[0] else None, gq if needs[1] else None, gp if needs[2] else None,
+                gn if needs[3] else None, ga, gb, g_screen, None, None, None, None, None, None,
+                None, None)

@@ -278,6 +278,72 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
                           float* grad_a, float* grad_b, float* abs_centers, int constant_tail,
                           const int* tile_order, void* stream);
 
+/* ---- RaDe-GS ----------------------------------------------------------------
+ * Replaces the Warp launches of rade/projection.py:422-551 (prepare,
+ * backward) and rade/render.py:550-670 (render, backward). */
+
+/* rade/projection.py:194-260 project: as splat_project_forward, with the
+ * covariance dilated by kernel_size (>= 0) and the opacity scaled by
+ * rade/projection.py:50-54's coefficient; depths (n) is the radial distance
+ * of the camera-space centre; planes / normals (n,3) receive the ray plane
+ * and camera-space normal of every visible row. */
+int splat_rade_project_forward(int n, const float* means, const float* quats,
+                               const float* scales, const float* opacities, const float* view,
+                               const float* proj, const float* K, int width, int height,
+                               float near_plane, float far_plane, float radius_clip,
+                               float kernel_size, float* centers, float* conics, int* radii,
+                               int* tiles, float* depths, float* planes, float* normals,
+                               void* stream);
+
+/* rade/projection.py:320-398 project_backward: the VJP of projection_loss
+ * (:294-317) for seeds on centers (n,2), conics (n,4), ray planes and
+ * normals (n,3) (NULL: zero).  Per-Gaussian gradients (NULL to skip) are
+ * WRITTEN, with zeros on culled rows; grad_view / grad_proj (4,4) are
+ * ACCUMULATED (NULL to skip). */
+int splat_rade_project_backward(int n, const float* means, const float* quats,
+                                const float* scales, const float* opacities, const float* view,
+                                const float* proj, const float* K, int width, int height,
+                                float kernel_size, const int* radii, const float* seed_centers,
+                                const float* seed_conics, const float* seed_planes,
+                                const float* seed_normals, float* grad_means, float* grad_quats,
+                                float* grad_scales, float* grad_opacities, float* grad_view,
+                                float* grad_proj, void* stream);
+
+/* rade/render.py:99-322 render / render_statistics.  Channels: colors' ch_a
+ * columns (row stride stride_a) then extras' ch_b columns; background covers
+ * them all.  Writes planar image (C+6,H,W) = C features, alpha, expected
+ * depth, median depth, unit normal xyz; auxiliary (2,H,W) = depth * ray
+ * scale, normal length; contributors (2,H,W) = last and median contributor
+ * (-1 when none).  K: the (3,3) intrinsics on the device.  Statistics and
+ * tile_order as splat_render_forward_statistics.  At most 64 channels. */
+int splat_rade_render_forward(int width, int height, const int* ranges, const int* ids,
+                              long long num_ids, int n, const float* centers, const float* conics,
+                              const float* planes, const float* normals, const float* colors,
+                              int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
+                              const float* background, const float* K, float* image,
+                              float* auxiliary, int* contributors, int stat_count,
+                              int stat_sum_mask, const float* stat_pixels, int* stat_counts,
+                              float* stat_sums, const int* tile_order, void* stream);
+
+/* rade/render.py:325-547 backward, from the forward's image, auxiliary and
+ * contributors.  Upstream images are channel-last: the value of channel c
+ * at pixel p is up[p*pix + c*ch] (NULL: zero) for the features (C
+ * channels), alpha, expected depth, median depth and normals (3 channels).
+ * Gradients are ADDED into grad_centers (n,2), grad_conics (n,4),
+ * grad_colors (n,ch_a), grad_extras (n,ch_b), abs_centers (n,2) (NULL to
+ * skip the last three), grad_planes and grad_normals (n,3). */
+int splat_rade_render_backward(
+    int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
+    const float* centers, const float* conics, const float* planes, const float* normals,
+    const float* colors, int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
+    const float* background, const float* K, const float* image, const float* auxiliary,
+    const int* contributors, const float* up_features, int up_feat_pix, int up_feat_ch,
+    const float* up_alpha, int up_alpha_pix, const float* up_depth, int up_depth_pix,
+    const float* up_median, int up_median_pix, const float* up_normals, int up_normals_pix,
+    int up_normals_ch, float* grad_centers, float* grad_conics, float* grad_colors,
+    float* grad_extras, float* abs_centers, float* grad_planes, float* grad_normals,
+    const int* tile_order, void* stream);
+
 /* Diagnostic: ours[i] = the blend's exp, cuda_exp[i] = CUDA expf, for x (n). */
 int splat_debug_expf(int n, const float* x, float* ours, float* cuda_exp, void* stream);
 

@@ -1,6 +1,7 @@
 """ctypes bindings for the CPU oracle (test infrastructure only).
 
-The oracle restates dsl_splat's gs3d rasteriser on the CPU (see
+The oracle restates dsl_splat's gs3d rasteriser and its RaDe-GS projection
+and render on the CPU (see
 splat_oracle.cpp for the per-function reference citations).  Tests,
 ``__graft_entry__.smoke()`` and bench.py's CPU legs use it as the checker and
 the CPU baseline; the product package never imports it.
@@ -76,6 +77,18 @@ def lib():
             _int, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _int, _int, _i32p, _f32p,
             _f32p, _f32p, _f32p, _f32p, _f32p, _vp, _vp]
         L.oracle_project_backward.restype = None
+        L.oracle_rade_project.argtypes = [
+            _int, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _int, _int, _flt, _flt, _flt,
+            _flt, _f32p, _f32p, _i32p, _i32p, _f32p, _f32p, _f32p]
+        L.oracle_rade_project.restype = None
+        L.oracle_rade_render.argtypes = [
+            _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+            _f32p, _f32p, _i32p]
+        L.oracle_rade_render.restype = None
+        L.oracle_rade_render_backward.argtypes = [
+            _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
+            _f32p, _f32p, _i32p, _vp, _vp, _vp, _vp, _vp, _f64p, _f64p, _f64p, _vp, _f64p, _f64p]
+        L.oracle_rade_render_backward.restype = None
         L.oracle_num_threads.restype = _int
         L.oracle_set_num_threads.argtypes = [_int]
         _lib = L
@@ -339,3 +352,57 @@ def gs3d_view_backward(r: ViewResult, bg, means, quats_n, scales, opacities, vie
     return ViewGrads(gm, gqn, gs, go, gsh, None if sh_coeffs is not None else gcolor,
                      gf[:, n_colors:n_colors + n_extras] if n_extras else None,
                      gview + gv_cam.astype(np.float64), gc, ga)
+
+
+# ---- RaDe-GS ---------------------------------------------------------------
+
+def rade_project(means, quats, scales, opacities, view, proj, K, width, height, *,
+                 near=0.2, far=float("inf"), radius_clip=0.0, kernel_size=0.0):
+    """rade/projection.py:194-260: centers, conics, radii, tiles, depths,
+    planes, normals (culled rows zero)."""
+    means = _c(means).reshape(-1, 3)
+    n = len(means)
+    out = dict(centers=np.zeros((n, 2), np.float32), conics=np.zeros((n, 4), np.float32),
+               radii=np.zeros(n, np.int32), tiles=np.zeros(n, np.int32),
+               depths=np.zeros(n, np.float32), planes=np.zeros((n, 3), np.float32),
+               normals=np.zeros((n, 3), np.float32))
+    lib().oracle_rade_project(
+        n, means, _c(quats), _c(scales), _c(opacities), _c(view), _c(proj), _c(K), width, height,
+        near, far, radius_clip, kernel_size, out["centers"], out["conics"], out["radii"],
+        out["tiles"], out["depths"], out["planes"], out["normals"])
+    return out
+
+
+def rade_render(width, height, ranges, ids, centers, conics, features, background, planes,
+                normals, K):
+    """rade/render.py:106-227: image (C+6,H,W), auxiliary (2,H,W), contributors (2,H,W)."""
+    features = _c(features)
+    C = features.shape[1]
+    image = np.zeros((C + 6, height, width), np.float32)
+    aux = np.zeros((2, height, width), np.float32)
+    contrib = np.zeros((2, height, width), np.int32)
+    lib().oracle_rade_render(width, height, C, _c(ranges, np.int32), _c(ids, np.int32),
+                             _c(centers), _c(conics), features, _c(background), _c(planes),
+                             _c(normals), _c(K), image, aux, contrib)
+    return image, aux, contrib
+
+
+def rade_render_backward(width, height, ranges, ids, centers, conics, features, background,
+                         planes, normals, K, image, aux, contrib, up_features=None,
+                         up_alpha=None, up_depth=None, up_median=None, up_normals=None,
+                         absgrad=True):
+    """rade/render.py:336-545; upstream images channel-last (H,W,k) or None.
+    Returns float64 grads of centers, conics, features, |centers|, planes, normals."""
+    features = _c(features)
+    n, C = features.shape
+    g = dict(centers=np.zeros((n, 2)), conics=np.zeros((n, 4)), features=np.zeros((n, C)),
+             abs=np.zeros((n, 2)) if absgrad else None, planes=np.zeros((n, 3)),
+             normals=np.zeros((n, 3)))
+    ups = [None if u is None else _c(u) for u in (up_features, up_alpha, up_depth, up_median,
+                                                   up_normals)]
+    lib().oracle_rade_render_backward(
+        width, height, C, _c(ranges, np.int32), _c(ids, np.int32), _c(centers), _c(conics),
+        features, _c(background), _c(planes), _c(normals), _c(K), _c(image), _c(aux),
+        _c(contrib, np.int32), *[_ptr(u) for u in ups], g["centers"], g["conics"],
+        g["features"], _ptr(g["abs"]), g["planes"], g["normals"])
+    return g

@@ -1,6 +1,7 @@
 // splat_oracle.cpp -- TEST INFRASTRUCTURE ONLY.
 //
-// A CPU restatement of dsl_splat's original-3DGS (gs3d) rasteriser, used as
+// A CPU restatement of dsl_splat's original-3DGS (gs3d) rasteriser and of its
+// RaDe-GS projection and render (rade/projection.py, rade/render.py), used as
 // the parity checker for the CUDA path and as the timed CPU baseline.  Only
 // tests/, __graft_entry__.smoke() and bench.py's CPU legs may load it; the
 // product path (dsl_splat_b200) never does.
@@ -458,6 +459,127 @@ void sh_basis_grad(const float d[3], int k, float g[3]) {
       g[1] = c9 * (-6.0f * x * y);
       break;
   }
+}
+
+
+// ---- RaDe-GS geometry (rade/projection.py) ------------------------------
+
+// Row-wise matrix-vector product, each row summed left to right (Warp mat*vec).
+void matvec3(const float m[3][3], const float v[3], float out[3]) {
+  float r[3];
+  for (int i = 0; i < 3; ++i) r[i] = m[i][0] * v[0] + m[i][1] * v[1] + m[i][2] * v[2];
+  std::memcpy(out, r, sizeof(r));
+}
+
+// Warp's normalize: v / |v| per component, the zero vector when |v| == 0.
+void normalize3(const float v[3], float out[3]) {
+  const float l = std::sqrt(v[0] * v[0] + v[1] * v[1] + v[2] * v[2]);
+  if (l > 0.0f) {
+    out[0] = v[0] / l;
+    out[1] = v[1] / l;
+    out[2] = v[2] / l;
+  } else {
+    out[0] = out[1] = out[2] = 0.0f;
+  }
+}
+
+struct RayGeometry {
+  float cov[3];     // (a, b, c) of the undilated screen covariance
+  float plane[3];   // ray plane (d/du, d/dv per pixel, distance at the centre)
+  float normal[3];  // unit camera-space normal
+};
+
+// rade/projection.py:102-190 geometry, for the camera-space position t.
+void rade_geometry(const float pos[3], const float q[4], const float s[3], const float* view,
+                   int width, int height, float fx, float fy, RayGeometry& out) {
+  // rade/projection.py:39-47 clamp_point
+  const float limx = W32(1.3) * static_cast<float>(width) / (2.0f * fx);
+  const float limy = W32(1.3) * static_cast<float>(height) / (2.0f * fy);
+  const float t0 = wclamp(pos[0] / pos[2], -limx, limx) * pos[2];
+  const float t1 = wclamp(pos[1] / pos[2], -limy, limy) * pos[2];
+  const float z = pos[2];
+  const float u = t0 / z, v = t1 / z;
+  float R[3][3];
+  glm_rotation(q, R);
+  const float cam[3][3] = {{view[0], view[4], view[8]},
+                           {view[1], view[5], view[9]},
+                           {view[2], view[6], view[10]}};
+  const float J[3][3] = {{fx / z, 0.0f, 0.0f},
+                         {0.0f, fy / z, 0.0f},
+                         {-fx * t0 / (z * z), -fy * t1 / (z * z), 0.0f}};
+  float Tm[3][3];
+  ref_matmul(cam, J, Tm);
+  // rade/projection.py:87-92 raster_covariance
+  const float S[3][3] = {{s[0], 0.0f, 0.0f}, {0.0f, s[1], 0.0f}, {0.0f, 0.0f, s[2]}};
+  float SR[3][3], M[3][3], Mt[3][3], C[3][3];
+  ref_matmul(S, R, SR);
+  ref_matmul(SR, Tm, M);
+  transpose3(M, Mt);
+  ref_matmul(Mt, M, C);
+  out.cov[0] = C[0][0];
+  out.cov[1] = C[1][0];
+  out.cov[2] = C[1][1];
+  // smallest axis with find_min_from_triple's tie order
+  const int bigger = s[0] < s[1] ? 1 : 0;
+  const int i0 = (bigger + 1) % 3, i1 = (bigger + 2) % 3;
+  const int minimum = s[i0] > s[i1] ? i1 : i0;
+  float inv_cov[3][3];
+  if (s[minimum] > W32(1.0e-7)) {
+    const float Si[3][3] = {{1.0f / s[0], 0.0f, 0.0f},
+                            {0.0f, 1.0f / s[1], 0.0f},
+                            {0.0f, 0.0f, 1.0f / s[2]}};
+    float SiR[3][3], Mi[3][3], Mit[3][3];
+    ref_matmul(Si, R, SiR);
+    ref_matmul(SiR, cam, Mi);
+    transpose3(Mi, Mit);
+    ref_matmul(Mit, Mi, inv_cov);
+  } else {
+    const float axis[3] = {R[minimum][0], R[minimum][1], R[minimum][2]};
+    float camt[3][3], ac[3];
+    transpose3(cam, camt);
+    matvec3(camt, axis, ac);
+    for (int i = 0; i < 3; ++i)
+      for (int j = 0; j < 3; ++j) inv_cov[i][j] = ac[i] * ac[j];
+  }
+  const float uvh[3] = {u, v, 1.0f};
+  float d[3], direction[3];
+  matvec3(inv_cov, uvh, d);
+  normalize3(d, direction);
+  const float len_sq = direction[0] * direction[0] + direction[1] * direction[1] +
+                       direction[2] * direction[2];
+  if (len_sq == 0.0f || !std::isfinite(direction[0])) {
+    out.plane[0] = out.plane[1] = out.plane[2] = 0.0f;
+    out.normal[0] = out.normal[1] = 0.0f;
+    out.normal[2] = -1.0f;
+    return;
+  }
+  const float length = std::sqrt(t0 * t0 + t1 * t1 + z * z);
+  const float factor = length / (u * u + v * v + 1.0f);
+  const float nj_inv[3][3] = {{v * v + 1.0f, -u * v, -u}, {-u * v, u * u + 1.0f, -v},
+                              {0.0f, 0.0f, 0.0f}};
+  const float denom = wmax(direction[0] * u + direction[1] * v + direction[2] * 1.0f,
+                           W32(1.0e-7));
+  const float dd[3] = {direction[0] / denom, direction[1] / denom, direction[2] / denom};
+  float plane[3];
+  matvec3(nj_inv, dd, plane);
+  out.plane[0] = plane[0] * factor / fx;
+  out.plane[1] = plane[1] * factor / fy;
+  out.plane[2] = std::sqrt(pos[0] * pos[0] + pos[1] * pos[1] + pos[2] * pos[2]);
+  const float ray_normal[3] = {-plane[0] * factor, -plane[1] * factor, -1.0f};
+  const float nj[3][3] = {{1.0f / z, 0.0f, t0 / length},
+                          {0.0f, 1.0f / z, t1 / length},
+                          {-t0 / (z * z), -t1 / (z * z), z / length}};
+  float n[3];
+  matvec3(nj, ray_normal, n);
+  normalize3(n, out.normal);
+}
+
+// rade/projection.py:50-54 opacity_coefficient
+float opacity_coefficient(const float cov[3], float kernel) {
+  const float det0 = wmax(W32(1.0e-6), cov[0] * cov[2] - cov[1] * cov[1]);
+  const float det1 =
+      wmax(W32(1.0e-6), (cov[0] + kernel) * (cov[2] + kernel) - cov[1] * cov[1]);
+  return std::sqrt(det0 / det1);
 }
 
 }  // namespace
@@ -1036,6 +1158,272 @@ void oracle_project_backward(int n, const float* means, const float* quats,
     for (int j = 0; j < 16; ++j) grad_view[j] += gv[j];
   if (grad_proj)
     for (int j = 0; j < 16; ++j) grad_proj[j] += gp[j];
+}
+
+// ---- RaDe-GS ---------------------------------------------------------------
+
+// rade/projection.py:194-260 project.  Culled rows keep radii = tiles = 0 and
+// leave the other outputs untouched.  depths is the radial distance
+// sqrtf(x*x + y*y + z*z) of the camera-space centre (norm3df's value).
+void oracle_rade_project(int n, const float* means, const float* quats, const float* scales,
+                         const float* opacities, const float* view, const float* proj,
+                         const float* K, int width, int height, float near_plane,
+                         float far_plane, float radius_clip, float kernel_size, float* centers,
+                         float* conics, int* radii, int* tiles, float* depths, float* planes,
+                         float* normals) {
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+  const float fx = K[0], fy = K[4];
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < n; ++i) {
+    radii[i] = 0;
+    tiles[i] = 0;
+    const float* m = means + 3 * i;
+    const float t[3] = {point_row(view, 0, m), point_row(view, 1, m), point_row(view, 2, m)};
+    if (t[2] <= near_plane || t[2] >= far_plane) continue;
+    RayGeometry rays;
+    rade_geometry(t, quats + 4 * i, scales + 3 * i, view, width, height, fx, fy, rays);
+    const float a = rays.cov[0] + kernel_size, b = rays.cov[1], c = rays.cov[2] + kernel_size;
+    const float det = a * c - b * b;
+    if (det == 0.0f) continue;
+    const float mid = 0.5f * (a + c);
+    const int radius =
+        f2i(std::ceil(3.0f * std::sqrt(mid + std::sqrt(wmax(W32(0.1), mid * mid - det)))));
+    if (static_cast<float>(radius) <= radius_clip) continue;
+    float center[2];
+    pixel_center(m, proj, width, height, center);
+    int bnd[4];
+    tile_bounds(center, radius, gx, gy, bnd);
+    const int count = (bnd[2] - bnd[0]) * (bnd[3] - bnd[1]);
+    if (count == 0) continue;
+    const float inverse = 1.0f / (a * c - b * b);
+    centers[2 * i] = center[0];
+    centers[2 * i + 1] = center[1];
+    conics[4 * i + 0] = c * inverse;
+    conics[4 * i + 1] = -b * inverse;
+    conics[4 * i + 2] = a * inverse;
+    conics[4 * i + 3] = opacities[i] * opacity_coefficient(rays.cov, kernel_size);
+    radii[i] = radius;
+    tiles[i] = count;
+    depths[i] = std::sqrt(t[0] * t[0] + t[1] * t[1] + t[2] * t[2]);
+    for (int k = 0; k < 3; ++k) {
+      planes[3 * i + k] = rays.plane[k];
+      normals[3 * i + k] = rays.normal[k];
+    }
+  }
+}
+
+// rade/render.py:106-227 evaluate.  image is planar (C+6, H, W): C features,
+// alpha, expected depth, median depth, unit normal; auxiliary (2, H, W):
+// depth * rln and the normal sum's length; contributors (2, H, W): last and
+// median contributor (-1: none).
+void oracle_rade_render(int width, int height, int channels, const int* ranges, const int* ids,
+                        const float* centers, const float* conics, const float* features,
+                        const float* background, const float* planes, const float* normals,
+                        const float* K, float* image, float* auxiliary, int* contributors) {
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+  const int T = gx * gy;
+  const float threshold = 1.0f / 255.0f;
+  const size_t P = static_cast<size_t>(width) * height;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int tile = 0; tile < T; ++tile) {
+    std::vector<float> color(channels);
+    const int first = ranges[2 * tile], last = ranges[2 * tile + 1];
+    for (int lane = 0; lane < 256; ++lane) {
+      const int x = tile % gx * 16 + lane % 16, y = tile / gx * 16 + lane / 16;
+      if (!(x < width && y < height)) continue;
+      const int pixel = y * width + x;
+      float transmittance = 1.0f, depth = 0.0f, median = 0.0f;
+      float normal[3] = {0.0f, 0.0f, 0.0f};
+      int median_contributor = -1, contributor = 0, last_contributor = 0;
+      std::fill(color.begin(), color.end(), 0.0f);
+      for (int idx = first; idx < last; ++idx) {
+        contributor += 1;
+        const int g = ids[idx];
+        const float dx = centers[2 * g] - static_cast<float>(x);
+        const float dy = centers[2 * g + 1] - static_cast<float>(y);
+        const float* q = conics + 4 * g;
+        const float power = -0.5f * (q[0] * dx * dx + q[2] * dy * dy) - q[1] * dx * dy;
+        if (!(power <= 0.0f)) continue;
+        const float alpha = wmin(W32(0.99), q[3] * splat_expf(power));
+        if (!(alpha >= threshold)) continue;
+        const float next_t = transmittance * (1.0f - alpha);
+        if (next_t < W32(0.0001)) break;
+        const float* v = features + static_cast<size_t>(g) * channels;
+        for (int ch = 0; ch < channels; ++ch)
+          color[ch] = color[ch] + v[ch] * alpha * transmittance;
+        const float* pl = planes + 3 * g;
+        const float distance = pl[0] * dx + pl[1] * dy + pl[2];
+        const float weight = alpha * transmittance;
+        depth += distance * weight;
+        for (int k = 0; k < 3; ++k) normal[k] += normals[3 * g + k] * weight;
+        if (transmittance > 0.5f) {
+          median = distance;
+          median_contributor = contributor;
+        }
+        transmittance = next_t;
+        last_contributor = contributor;
+      }
+      for (int ch = 0; ch < channels; ++ch)
+        image[ch * P + pixel] = color[ch] + transmittance * background[ch];
+      const float u = (static_cast<float>(x) + 0.5f - K[2]) / K[0];
+      const float v = (static_cast<float>(y) + 0.5f - K[5]) / K[4];
+      const float rln = 1.0f / std::sqrt(u * u + v * v + 1.0f);
+      const float alpha = 1.0f - transmittance;
+      const float expected = last_contributor > 0 ? depth * rln / alpha : 0.0f;
+      const float length =
+          std::sqrt(normal[0] * normal[0] + normal[1] * normal[1] + normal[2] * normal[2]);
+      const float scale = wmax(length, W32(1.0e-12));
+      image[(channels + 0) * P + pixel] = alpha;
+      image[(channels + 1) * P + pixel] = expected;
+      image[(channels + 2) * P + pixel] = median * rln;
+      for (int k = 0; k < 3; ++k) image[(channels + 3 + k) * P + pixel] = normal[k] / scale;
+      auxiliary[pixel] = depth * rln;
+      auxiliary[P + pixel] = length;
+      contributors[pixel] = last_contributor;
+      contributors[P + pixel] = median_contributor;
+    }
+  }
+}
+
+// rade/render.py:336-545 backward.  Upstream images are channel-last
+// (H, W, k) and may be null (zero).  Gradients accumulate in double into
+// zeroed buffers; abs_centers may be null.
+void oracle_rade_render_backward(
+    int width, int height, int channels, const int* ranges, const int* ids,
+    const float* centers, const float* conics, const float* features, const float* background,
+    const float* planes, const float* normals, const float* K, const float* image,
+    const float* auxiliary, const int* contributors, const float* up_features,
+    const float* up_alpha, const float* up_depth, const float* up_median,
+    const float* up_normals, double* grad_centers, double* grad_conics, double* grad_features,
+    double* abs_centers, double* grad_planes, double* grad_normals) {
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+  const int T = gx * gy;
+  const float threshold = 1.0f / 255.0f;
+  const size_t P = static_cast<size_t>(width) * height;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int tile = 0; tile < T; ++tile) {
+    std::vector<float> gradient(channels), accumulated(channels), last_color(channels);
+    const int first = ranges[2 * tile], last = ranges[2 * tile + 1];
+    for (int lane = 0; lane < 256; ++lane) {
+      const int x = tile % gx * 16 + lane % 16, y = tile / gx * 16 + lane / 16;
+      if (!(x < width && y < height)) continue;
+      const int pixel = y * width + x;
+      const float final_transmittance = 1.0f - image[channels * P + pixel];
+      float transmittance = final_transmittance;
+      const int last_contributor = contributors[pixel];
+      float background_gradient = 0.0f;
+      for (int ch = 0; ch < channels; ++ch) {
+        gradient[ch] = up_features ? up_features[static_cast<size_t>(pixel) * channels + ch] : 0.0f;
+        background_gradient += background[ch] * gradient[ch];
+        accumulated[ch] = 0.0f;
+        last_color[ch] = 0.0f;
+      }
+      background_gradient -= up_alpha ? up_alpha[pixel] : 0.0f;
+      const int median_contributor = contributors[P + pixel];
+      float depth_gradient = 0.0f, median_gradient = 0.0f;
+      float normal_gradient[3] = {0.0f, 0.0f, 0.0f};
+      const float pixel_alpha = image[channels * P + pixel];
+      if (pixel_alpha > 0.0f) {
+        const float u = (static_cast<float>(x) + 0.5f - K[2]) / K[0];
+        const float v = (static_cast<float>(y) + 0.5f - K[5]) / K[4];
+        const float rln = 1.0f / std::sqrt(u * u + v * v + 1.0f);
+        const float gd = up_depth ? up_depth[pixel] : 0.0f;
+        background_gradient += gd * (auxiliary[pixel] / pixel_alpha) / pixel_alpha;
+        depth_gradient = gd / pixel_alpha * rln;
+        median_gradient = (up_median ? up_median[pixel] : 0.0f) * rln;
+        for (int k = 0; k < 3; ++k) normal_gradient[k] = up_normals ? up_normals[3 * pixel + k] : 0.0f;
+        const float unit[3] = {image[(channels + 3) * P + pixel], image[(channels + 4) * P + pixel],
+                               image[(channels + 5) * P + pixel]};
+        const float length = auxiliary[P + pixel];
+        if (length >= W32(1.0e-12)) {
+          const float d = unit[0] * normal_gradient[0] + unit[1] * normal_gradient[1] +
+                          unit[2] * normal_gradient[2];
+          for (int k = 0; k < 3; ++k) normal_gradient[k] = normal_gradient[k] - unit[k] * d;
+        }
+        const float scale = wmax(length, W32(1.0e-12));
+        for (int k = 0; k < 3; ++k) normal_gradient[k] = normal_gradient[k] / scale;
+      }
+      float last_alpha = 0.0f, accumulated_depth = 0.0f, last_depth = 0.0f;
+      float accumulated_normal[3] = {0.0f, 0.0f, 0.0f}, last_normal[3] = {0.0f, 0.0f, 0.0f};
+      int contributor = last - first;
+      for (int idx = last - 1; idx >= first; --idx) {
+        contributor -= 1;
+        if (contributor >= last_contributor) continue;
+        const int g = ids[idx];
+        const float dx = centers[2 * g] - static_cast<float>(x);
+        const float dy = centers[2 * g + 1] - static_cast<float>(y);
+        const float* q = conics + 4 * g;
+        const float power = -0.5f * (q[0] * dx * dx + q[2] * dy * dy) - q[1] * dx * dy;
+        const float gaussian_value = splat_expf(power);
+        const float alpha = wmin(W32(0.99), q[3] * gaussian_value);
+        if (!(power <= 0.0f) || !(alpha >= threshold)) continue;
+        transmittance = transmittance / (1.0f - alpha);
+        const float* color = features + static_cast<size_t>(g) * channels;
+        float grad_alpha = 0.0f;
+        for (int ch = 0; ch < channels; ++ch) {
+          accumulated[ch] = last_alpha * last_color[ch] + (1.0f - last_alpha) * accumulated[ch];
+          last_color[ch] = color[ch];
+          grad_alpha += (color[ch] - accumulated[ch]) * gradient[ch];
+#pragma omp atomic
+          grad_features[static_cast<size_t>(g) * channels + ch] +=
+              static_cast<double>(alpha * transmittance * gradient[ch]);
+        }
+        const float* pl = planes + 3 * g;
+        const float distance = pl[0] * dx + pl[1] * dy + pl[2];
+        const float* nm = normals + 3 * g;
+        accumulated_depth = last_alpha * last_depth + (1.0f - last_alpha) * accumulated_depth;
+        for (int k = 0; k < 3; ++k)
+          accumulated_normal[k] =
+              last_alpha * last_normal[k] + (1.0f - last_alpha) * accumulated_normal[k];
+        grad_alpha += (distance - accumulated_depth) * depth_gradient +
+                      ((nm[0] - accumulated_normal[0]) * normal_gradient[0] +
+                       (nm[1] - accumulated_normal[1]) * normal_gradient[1] +
+                       (nm[2] - accumulated_normal[2]) * normal_gradient[2]);
+        last_depth = distance;
+        for (int k = 0; k < 3; ++k) last_normal[k] = nm[k];
+        const float weight = alpha * transmittance;
+        float g_distance = weight * depth_gradient;
+        if (contributor == median_contributor - 1) g_distance += median_gradient;
+#pragma omp atomic
+        grad_planes[3 * g + 0] += g_distance * dx;
+#pragma omp atomic
+        grad_planes[3 * g + 1] += g_distance * dy;
+#pragma omp atomic
+        grad_planes[3 * g + 2] += g_distance;
+        for (int k = 0; k < 3; ++k) {
+#pragma omp atomic
+          grad_normals[3 * g + k] += normal_gradient[k] * weight;
+        }
+        grad_alpha = grad_alpha * transmittance +
+                     (-final_transmittance / (1.0f - alpha)) * background_gradient;
+        last_alpha = alpha;
+        const float grad_value = q[3] * grad_alpha;
+        const float gdx = gaussian_value * dx, gdy = gaussian_value * dy;
+        float ddx = grad_value * (-gdx * q[0] - gdy * q[1]);
+        float ddy = grad_value * (-gdy * q[2] - gdx * q[1]);
+        ddx += g_distance * pl[0];
+        ddy += g_distance * pl[1];
+#pragma omp atomic
+        grad_centers[2 * g] += ddx;
+#pragma omp atomic
+        grad_centers[2 * g + 1] += ddy;
+        if (abs_centers) {
+#pragma omp atomic
+          abs_centers[2 * g] += std::fabs(ddx);
+#pragma omp atomic
+          abs_centers[2 * g + 1] += std::fabs(ddy);
+        }
+#pragma omp atomic
+        grad_conics[4 * g + 0] += -0.5f * gdx * dx * grad_value;
+#pragma omp atomic
+        grad_conics[4 * g + 1] += -gdx * dy * grad_value;
+#pragma omp atomic
+        grad_conics[4 * g + 2] += -0.5f * gdy * dy * grad_value;
+#pragma omp atomic
+        grad_conics[4 * g + 3] += gaussian_value * grad_alpha;
+      }
+    }
+  }
 }
 
 int oracle_num_threads(void) {
