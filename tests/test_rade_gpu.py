@@ -174,8 +174,15 @@ def test_rade_rasterize_api_matches_oracle(golden):
                          kernel_size=float(g["kernel_size"]))
     bg = np.concatenate([g["background"][:C], np.zeros(E, np.float32)])
     feats = np.concatenate([g["colors"], g["extras"]], 1)
-    image, aux, contrib = O.rade_render(W, H, g["ranges"], g["ids"], g["centers"], g["conics"],
-                                        feats, bg, g["planes"], g["normals"], g["K"])
+    # the oracle projects the quaternions the API normalised (Torch's CUDA
+    # F.normalize, inputs.py:252), so that every projected float matches
+    qn = torch.nn.functional.normalize(_t(g["quats"]), dim=-1).cpu().numpy()
+    geo = O.rade_project(g["means"], qn, g["scales"], g["opacities"], g["viewmat"], g["full"],
+                         g["K"], W, H, kernel_size=float(g["kernel_size"]))
+    offsets = np.cumsum(geo["tiles"]).astype(np.int32)
+    _, ids, ranges = O.bin_and_sort(geo["centers"], geo["radii"], geo["depths"], offsets, W, H)
+    image, aux, contrib = O.rade_render(W, H, ranges, ids, geo["centers"], geo["conics"], feats,
+                                        bg, geo["planes"], geo["normals"], g["K"])
     img = image.transpose(1, 2, 0)
     np.testing.assert_allclose(res.features[0].detach().cpu().numpy(), img[..., :C], atol=1e-5,
                                rtol=0)
@@ -196,8 +203,8 @@ def test_rade_rasterize_api_matches_oracle(golden):
     if E:
         loss = loss + (res.extra_features[0] * up_f[..., C:]).sum()
     loss.backward()
-    want = O.rade_render_backward(W, H, g["ranges"], g["ids"], g["centers"], g["conics"], feats,
-                                  bg, g["planes"], g["normals"], g["K"], image, aux, contrib,
+    want = O.rade_render_backward(W, H, ranges, ids, geo["centers"], geo["conics"], feats, bg,
+                                  geo["planes"], geo["normals"], g["K"], image, aux, contrib,
                                   g["up_features"], g["up_alpha"], g["up_depth"],
                                   g["up_median"], g["up_normals"])
     assert rel_l2(colors.grad.cpu().numpy(), want["features"][:, :C]) <= 1e-3
@@ -205,13 +212,13 @@ def test_rade_rasterize_api_matches_oracle(golden):
         assert rel_l2(extras.grad.cpu().numpy(), want["features"][:, C:]) <= 1e-3
     assert rel_l2(res.means2d.absgrad[0].cpu().numpy(), want["abs"]) <= 1e-3
     assert rel_l2(res.means2d.grad[0].cpu().numpy(), want["centers"]) <= 1e-3
-    ref = rade_vjp.project_backward(g["means"], g["quats"], g["scales"], g["opacities"],
-                                    g["viewmat"], g["full"], g["K"], W, H, g["radii"],
-                                    want["centers"], want["conics"], want["planes"],
-                                    want["normals"], kernel_size=float(g["kernel_size"]),
-                                    planes=g["planes"])
-    q = g["quats"].astype(np.float64)
-    gq = ref[1] - q * (q * ref[1]).sum(1, keepdims=True)  # through F.normalize at unit quats
+    ref = rade_vjp.project_backward(g["means"], qn, g["scales"], g["opacities"], g["viewmat"],
+                                    g["full"], g["K"], W, H, geo["radii"], want["centers"],
+                                    want["conics"], want["planes"], want["normals"],
+                                    kernel_size=float(g["kernel_size"]), planes=geo["planes"])
+    q = qn.astype(np.float64)
+    raw = np.linalg.norm(g["quats"].astype(np.float64), axis=1, keepdims=True)
+    gq = (ref[1] - q * (q * ref[1]).sum(1, keepdims=True)) / raw  # F.normalize's VJP
     for got, want_g, name in ((means.grad, ref[0], "means"), (quats.grad, gq, "quats"),
                               (scales.grad, ref[2], "scales"), (opac.grad, ref[3], "opacities")):
         assert rel_l2(got.cpu().numpy(), want_g) <= 1e-3, name
@@ -276,7 +283,7 @@ def test_rade_config4_shape_against_oracle():
 
 def test_rade_ops_stages_compose_like_rasterize(golden):
     """rade.ops prepare_gaussians -> bin_and_sort -> rasterize_to_pixels gives
-    the reference kernels' images."""
+    the oracle's bins and images."""
     from dsl_splat_b200 import PinholeCamera
 
     g = golden
@@ -288,7 +295,17 @@ def test_rade_ops_stages_compose_like_rasterize(golden):
     tiles = rade.ops.bin_and_sort(geo)
     feats = np.concatenate([g["colors"], g["extras"]], 1)
     px = rade.ops.rasterize_to_pixels(geo, tiles, _t(feats), _t(g["background"]))
-    img = g["image"].transpose(1, 2, 0)
+    # the oracle on the quaternions prepare_gaussians normalised on the GPU
+    qn = torch.nn.functional.normalize(_t(g["quats"]), dim=-1).cpu().numpy()
+    ref = O.rade_project(g["means"], qn, g["scales"], g["opacities"], g["viewmat"], g["full"],
+                         g["K"], W, H, kernel_size=float(g["kernel_size"]))
+    np.testing.assert_array_equal(geo.radii.cpu().numpy(), ref["radii"])
+    offsets = np.cumsum(ref["tiles"]).astype(np.int32)
+    _, ids, ranges = O.bin_and_sort(ref["centers"], ref["radii"], ref["depths"], offsets, W, H)
+    np.testing.assert_array_equal(tiles.gaussian_ids.cpu().numpy(), ids)
+    image, _, _ = O.rade_render(W, H, ranges, ids, ref["centers"], ref["conics"], feats,
+                                g["background"], ref["planes"], ref["normals"], g["K"])
+    img = image.transpose(1, 2, 0)
     np.testing.assert_allclose(px.features.cpu().numpy(), img[..., :-6], atol=1e-5, rtol=0)
     np.testing.assert_allclose(px.depth.cpu().numpy()[..., 0], img[..., -5], atol=1e-5, rtol=0)
     np.testing.assert_allclose(px.normals.cpu().numpy(), img[..., -3:], atol=1e-5, rtol=0)
