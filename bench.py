@@ -61,6 +61,9 @@ def parse_args():
                     help="N > 1: Gaussian-range buckets of the gradient all-reduce (more "
                          "than one overlaps it with the projection backward; measured slower "
                          "on 2 B200s: 762 / 733 / 722 / 668 frames/s for 1 / 2 / 4 / 8)")
+    ap.add_argument("--gaussians", type=int, default=None,
+                    help="override the config's Gaussian count (smaller cases for ncu "
+                         "captures; the bench line then names the reduced workload)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
@@ -75,13 +78,13 @@ def dist_env():
     return rank, world, local
 
 
-def workload(config: int, rank: int, world: int):
+def workload(config: int, rank: int, world: int, gaussians: int | None = None):
     """The config scene.  Single-view configs: rank r looks from an orbit
     angle 2*pi*r/world (one view per rank).  Multi-view configs (config 2's
     8-camera batch): rank r renders the cameras k with k mod world == r."""
     from dsl_splat_b200.scenes import look_at, make_scene
     from dsl_splat_b200.sharding import local_cameras
-    s = make_scene(config)
+    s = make_scene(config, n=gaussians)
     cams = s.viewmats.shape[0]
     if cams > 1:
         idx = local_cameras(cams, rank, world)
@@ -303,7 +306,7 @@ def main():
         sharding.init_process_group("nccl", timeout_s=180.0, device=dev)
         pg = dist
 
-    s = workload(args.config, rank, world)
+    s = workload(args.config, rank, world, args.gaussians)
     means = s.means.to(dev).requires_grad_(True)
     quats = s.quats.to(dev).requires_grad_(True)
     scales = s.scales.to(dev).requires_grad_(True)

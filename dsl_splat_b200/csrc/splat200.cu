@@ -298,15 +298,17 @@ void launch_rade(const RadeRenderParams& p, bool backward, cudaStream_t s) {
   const unsigned tiles = static_cast<unsigned>(p.base.gx * ((p.base.height + 15) / 16));
   const size_t smem = sizeof(RenderShared<CHP>) + sizeof(RadeShared);
   if (backward) {
+    // one pixel per lane (see rade_backward_kernel on the measured variants)
     if (smem > 32 * 1024)
-      cudaFuncSetAttribute(rade_backward_kernel<CHP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem));
-    rade_backward_kernel<CHP><<<tiles, kBlock, smem, counted(s)>>>(p);
+      cudaFuncSetAttribute(rade_backward_kernel<CHP, 1>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    rade_backward_kernel<CHP, 1><<<tiles, kBlock, smem, counted(s)>>>(p);
   } else {
+    // two pixels per lane with paired arithmetic (kBlock / 2 threads per tile)
     if (smem > 32 * 1024)
-      cudaFuncSetAttribute(rade_forward_kernel<CHP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(rade_forward2_kernel<CHP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
-    rade_forward_kernel<CHP><<<tiles, kBlock, smem, counted(s)>>>(p);
+    rade_forward2_kernel<CHP><<<tiles, kBlock / 2, smem, counted(s)>>>(p);
   }
 }
 
@@ -1257,7 +1259,10 @@ int splat_rade_render_forward(int width, int height, const int* ranges, const in
                               long long num_ids, int n, const float* centers, const float* conics,
                               const float* planes, const float* normals, const float* colors,
                               int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
-                              const float* background, const float* K, float* image,
+                              const float* background, const float* K, float* features,
+                              int feat_pix, int feat_ch, float* alpha, int alpha_pix,
+                              float* depth, int depth_pix, float* median, int median_pix,
+                              float* normal_image, int normal_pix, int normal_ch,
                               float* auxiliary, int* contributors, int stat_count,
                               int stat_sum_mask, const float* stat_pixels, int* stat_counts,
                               float* stat_sums, const int* tile_order, void* stream) {
@@ -1266,10 +1271,22 @@ int splat_rade_render_forward(int width, int height, const int* ranges, const in
                                     conics, planes, normals, colors, ch_a, stride_a, extras, ch_b,
                                     stride_b, background, K, p);
   if (rc != kOk) return rc;
-  if (!image || !auxiliary || !contributors) return fail(kInvalidArgument, "null rade output");
+  if (!features || !alpha || !depth || !median || !normal_image || !auxiliary || !contributors)
+    return fail(kInvalidArgument, "null rade output");
   if (stat_count < 0 || stat_count > 30 || (stat_count > 0 && !stat_pixels))
     return fail(kInvalidArgument, "bad statistics arguments");
-  p.image = image;
+  p.features = features;
+  p.feat_pix = feat_pix;
+  p.feat_ch = feat_ch;
+  p.alpha = alpha;
+  p.alpha_pix = alpha_pix;
+  p.depth = depth;
+  p.depth_pix = depth_pix;
+  p.median = median;
+  p.median_pix = median_pix;
+  p.normal_image = normal_image;
+  p.normal_pix = normal_pix;
+  p.normal_ch = normal_ch;
   p.auxiliary = auxiliary;
   p.contributors = contributors;
   p.base.stat_count = stat_count;
@@ -1284,7 +1301,8 @@ int splat_rade_render_backward(
     int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
     const float* centers, const float* conics, const float* planes, const float* normals,
     const float* colors, int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
-    const float* background, const float* K, const float* image, const float* auxiliary,
+    const float* background, const float* K, const float* alpha, int alpha_pix,
+    const float* normal_image, int normal_pix, int normal_ch, const float* auxiliary,
     const int* contributors, const float* up_features, int up_feat_pix, int up_feat_ch,
     const float* up_alpha, int up_alpha_pix, const float* up_depth, int up_depth_pix,
     const float* up_median, int up_median_pix, const float* up_normals, int up_normals_pix,
@@ -1296,12 +1314,17 @@ int splat_rade_render_backward(
                                     conics, planes, normals, colors, ch_a, stride_a, extras, ch_b,
                                     stride_b, background, K, p);
   if (rc != kOk) return rc;
-  if (!image || !auxiliary || !contributors) return fail(kInvalidArgument, "null rade forward output");
+  if (!alpha || !normal_image || !auxiliary || !contributors)
+    return fail(kInvalidArgument, "null rade forward output");
   if (!grad_centers || !grad_conics || !grad_planes || !grad_normals)
     return fail(kInvalidArgument, "null gradient buffers");
   if (!aligned(grad_centers, 8) || !aligned(grad_conics, 16) || !aligned(abs_centers, 8))
     return fail(kInvalidArgument, "center rows need 8-byte and conic rows 16-byte alignment");
-  p.image = const_cast<float*>(image);
+  p.alpha = const_cast<float*>(alpha);
+  p.alpha_pix = alpha_pix;
+  p.normal_image = const_cast<float*>(normal_image);
+  p.normal_pix = normal_pix;
+  p.normal_ch = normal_ch;
   p.auxiliary = const_cast<float*>(auxiliary);
   p.contributors = const_cast<int*>(contributors);
   p.up_features = up_features;

@@ -162,9 +162,14 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
             backgrounds_packed[i], bins[i], K, config, training.absolute_targets[i],
             training.screen_targets[i], prepared_stats[i] if statistics else None, grad_enabled))
     shape = layout.batch_dims + (layout.cameras, height, width)
-    # each output keeps its own autograd edge (rade/api.py:253-260)
-    features_image, alpha, depth, median, normals = (
-        torch.stack(values).reshape(shape + (values[0].shape[-1],)) for values in zip(*images))
+
+    def assemble(values: tuple[Tensor, ...]) -> Tensor:
+        # each output keeps its own autograd edge (rade/api.py:253-260); one
+        # view needs no stacking copy: the blend wrote a dense tensor per output
+        whole = values[0].unsqueeze(0) if len(values) == 1 else torch.stack(values)
+        return whole.reshape(shape + (values[0].shape[-1],))
+
+    features_image, alpha, depth, median, normals = (assemble(v) for v in zip(*images))
     main_features = features_image
     if layout.extras is not None:
         meta["render_extra_signals"] = features_image[..., channels:]

@@ -71,7 +71,8 @@ class Render(torch.autograd.Function):
                             config.height, statistics)
         if grad_enabled and any(ctx.needs_input_grad[:7]):
             ctx.save_for_backward(centers, conics, planes, normals, colors, extras, background,
-                                  intrinsics, out.features, out.auxiliary, out.contributors)
+                                  intrinsics, out.alpha, out.normals, out.auxiliary,
+                                  out.contributors)
             ctx.bins = {k: bins[k] for k in ("ranges", "point_list", "tile_order") if k in bins}
             ctx.config, ctx.absolute, ctx.screen_target = config, absolute, screen_target
         ctx.set_materialize_grads(False)
@@ -82,8 +83,8 @@ class Render(torch.autograd.Function):
     def backward(ctx: Any, *gradients: Tensor | None):
         if all(g is None for g in gradients):
             return (None,) * 15
-        (centers, conics, planes, normals, colors, extras, background, intrinsics, image, aux,
-         contrib) = ctx.saved_tensors
+        (centers, conics, planes, normals, colors, extras, background, intrinsics, alpha,
+         normal_image, aux, contrib) = ctx.saved_tensors
         cfg = ctx.config
         needs = ctx.needs_input_grad
         direct = ctx.absolute.direct_buffer() if ctx.absolute is not None else None
@@ -92,7 +93,8 @@ class Render(torch.autograd.Function):
         state = ProjectedGaussians(centers, conics, None, None, None, planes, normals)
         gc, gq, ga, gb, gp, gn, absolute = render.backward(
             state, ctx.bins, colors, extras, background, intrinsics,
-            render.RenderedPixels(image, aux, contrib), gradients, cfg.width, cfg.height,
+            render.RenderedPixels(None, alpha, None, None, normal_image, aux, contrib),
+            gradients, cfg.width, cfg.height,
             absgrad=ctx.absolute is not None, need_colors=needs[4],
             need_extras=extras is not None and needs[5], centers_out=screen_direct,
             absolute_out=direct)

@@ -17,20 +17,28 @@ from .projection import ProjectedGaussians
 
 @dataclass(slots=True)
 class RenderedPixels:
-    """rade/render.py:32-47: planar (C+6, H, W) features (C channels, alpha,
-    expected depth, median depth, normal xyz), auxiliary (2, H, W) (depth
-    times the ray scale, normal length) and contributors (2, H, W) (last and
-    median contributor)."""
+    """rade/render.py:32-47, with the five images the reference slices out of
+    its planar (C+6, H, W) buffer written by the kernel as separate dense
+    channel-last tensors: features (H, W, C), alpha, expected depth and
+    median depth (H, W, 1), normals (H, W, 3); plus auxiliary (2, H, W)
+    (depth times the ray scale, normal length) and contributors (2, H, W)
+    (last and median contributor)."""
 
     features: Tensor
+    alpha: Tensor
+    depth: Tensor
+    median: Tensor
+    normals: Tensor
     auxiliary: Tensor
     contributors: Tensor
 
     def images(self) -> tuple[Tensor, ...]:
-        """Feature, alpha, expected depth, median depth and normal HWC views."""
-        image = self.features.permute(1, 2, 0)
-        return (image[..., :-6], image[..., -6:-5], image[..., -5:-4], image[..., -4:-3],
-                image[..., -3:])
+        """Feature, alpha, expected depth, median depth and normal HWC images."""
+        return self.features, self.alpha, self.depth, self.median, self.normals
+
+    def planar(self) -> Tensor:
+        """The reference's (C+6, H, W) layout (a copy)."""
+        return torch.cat(self.images(), -1).permute(2, 0, 1)
 
 
 def _split(colors: Tensor, extras: Tensor | None):
@@ -48,8 +56,9 @@ def render(state: ProjectedGaussians, bins: dict, colors: Tensor, extras: Tensor
     a, b, ca, cb = _split(colors, extras)
     dev = a.device
     channels = ca + cb
-    out = RenderedPixels(a.new_empty((channels + 6, height, width)),
-                         a.new_empty((2, height, width)),
+    out = RenderedPixels(a.new_empty((height, width, channels)), a.new_empty((height, width, 1)),
+                         a.new_empty((height, width, 1)), a.new_empty((height, width, 1)),
+                         a.new_empty((height, width, 3)), a.new_empty((2, height, width)),
                          torch.empty((2, height, width), dtype=torch.int32, device=dev))
     if statistics is None:
         stat = (0, 0, None, None, None)
@@ -62,8 +71,10 @@ def render(state: ProjectedGaussians, bins: dict, colors: Tensor, extras: Tensor
             width, height, ptr(bins["ranges"]), ptr(bins["point_list"]), len(bins["point_list"]),
             len(state.centers), pin(state.centers), pin(state.conics), pin(state.ray_planes),
             pin(state.normals), ptr(a), ca, ca, ptr(b), cb, cb, pin(background),
-            pin(intrinsics), ptr(out.features), ptr(out.auxiliary), ptr(out.contributors),
-            *stat, ptr(stages.tile_order(bins)), nv.stream(dev)), "rade_render_forward")
+            pin(intrinsics), ptr(out.features), channels, 1, ptr(out.alpha), 1, ptr(out.depth), 1,
+            ptr(out.median), 1, ptr(out.normals), 3, 1, ptr(out.auxiliary),
+            ptr(out.contributors), *stat, ptr(stages.tile_order(bins)), nv.stream(dev)),
+            "rade_render_forward")
     return out
 
 
@@ -106,8 +117,9 @@ def backward(state: ProjectedGaussians, bins: dict, colors: Tensor, extras: Tens
             width, height, ptr(bins["ranges"]), ptr(bins["point_list"]), len(bins["point_list"]),
             len(state.centers), pin(state.centers), pin(state.conics), pin(state.ray_planes),
             pin(state.normals), ptr(a), ca, ca, ptr(b), cb, cb, pin(background),
-            pin(intrinsics), pin(output.features), pin(output.auxiliary),
-            pin(output.contributors), pin(gf), pf, cf, pin(ga), pa, pin(gd), pd, pin(gm), pm,
+            pin(intrinsics), pin(output.alpha), 1, pin(output.normals), 3, 1,
+            pin(output.auxiliary), pin(output.contributors), pin(gf), pf, cf, pin(ga), pa,
+            pin(gd), pd, pin(gm), pm,
             pin(gn), pn, cn, ptr(centers), ptr(conics), ptr(g_colors), ptr(g_extras),
             ptr(absolute), ptr(planes), ptr(normals), ptr(stages.tile_order(bins)),
             nv.stream(a.device)), "rade_render_backward")

@@ -311,21 +311,30 @@ int splat_rade_project_backward(int n, const float* means, const float* quats,
 
 /* rade/render.py:99-322 render / render_statistics.  Channels: colors' ch_a
  * columns (row stride stride_a) then extras' ch_b columns; background covers
- * them all.  Writes planar image (C+6,H,W) = C features, alpha, expected
- * depth, median depth, unit normal xyz; auxiliary (2,H,W) = depth * ray
- * scale, normal length; contributors (2,H,W) = last and median contributor
- * (-1 when none).  K: the (3,3) intrinsics on the device.  Statistics and
- * tile_order as splat_render_forward_statistics.  At most 64 channels. */
+ * them all.  Writes the five images of rade/render.py:38-47 RenderedPixels.
+ * images(), each value of channel c at pixel p at base[p*pix + c*ch]: the C
+ * features (feat_pix, feat_ch), alpha = 1 - T, expected depth, median depth
+ * (one channel each) and the unit normal (normal_pix, normal_ch); the
+ * reference's planar (C+6,H,W) image is pix = 1, ch = H*W at offsets 0, C,
+ * C+1, C+2, C+3; channel-last images are pix = channels, ch = 1.  Also
+ * auxiliary (2,H,W) = depth * ray scale, normal length; contributors (2,H,W)
+ * = last and median contributor (-1 when none).  K: the (3,3) intrinsics on
+ * the device.  Statistics and tile_order as splat_render_forward_statistics.
+ * At most 64 channels. */
 int splat_rade_render_forward(int width, int height, const int* ranges, const int* ids,
                               long long num_ids, int n, const float* centers, const float* conics,
                               const float* planes, const float* normals, const float* colors,
                               int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
-                              const float* background, const float* K, float* image,
+                              const float* background, const float* K, float* features,
+                              int feat_pix, int feat_ch, float* alpha, int alpha_pix,
+                              float* depth, int depth_pix, float* median, int median_pix,
+                              float* normal_image, int normal_pix, int normal_ch,
                               float* auxiliary, int* contributors, int stat_count,
                               int stat_sum_mask, const float* stat_pixels, int* stat_counts,
                               float* stat_sums, const int* tile_order, void* stream);
 
-/* rade/render.py:325-547 backward, from the forward's image, auxiliary and
+/* rade/render.py:325-547 backward, from the forward's alpha and normal
+ * images (strides as in splat_rade_render_forward), auxiliary and
  * contributors.  Upstream images are channel-last: the value of channel c
  * at pixel p is up[p*pix + c*ch] (NULL: zero) for the features (C
  * channels), alpha, expected depth, median depth and normals (3 channels).
@@ -336,7 +345,8 @@ int splat_rade_render_backward(
     int width, int height, const int* ranges, const int* ids, long long num_ids, int n,
     const float* centers, const float* conics, const float* planes, const float* normals,
     const float* colors, int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
-    const float* background, const float* K, const float* image, const float* auxiliary,
+    const float* background, const float* K, const float* alpha, int alpha_pix,
+    const float* normal_image, int normal_pix, int normal_ch, const float* auxiliary,
     const int* contributors, const float* up_features, int up_feat_pix, int up_feat_ch,
     const float* up_alpha, int up_alpha_pix, const float* up_depth, int up_depth_pix,
     const float* up_median, int up_median_pix, const float* up_normals, int up_normals_pix,

@@ -47,6 +47,15 @@ def _project(g):
                          _t(g["viewmat"]), _t(g["full"]), _t(g["K"]), _config(g))
 
 
+def _forward_from_planar(g):
+    """The golden forward (planar (C+6,H,W) as the reference stores it) as
+    the five channel-last images the B200 blend writes."""
+    img = _t(g["image"]).permute(1, 2, 0)
+    parts = (img[..., :-6], img[..., -6:-5], img[..., -5:-4], img[..., -4:-3], img[..., -3:])
+    return rrender.RenderedPixels(*(t.contiguous() for t in parts), _t(g["auxiliary"]),
+                                  _t(g["contributors"]))
+
+
 def _golden_state(g):
     return rproj.ProjectedGaussians(_t(g["centers"]), _t(g["conics"]), _t(g["radii"]),
                                     _t(g["tiles"]), _t(g["depths"]), _t(g["planes"]),
@@ -76,7 +85,7 @@ def test_rade_render_matches_reference_kernels(golden):
     out = rrender.render(st, bins, _t(g["colors"]), _t(g["extras"]) if g["extras"].shape[1] else None,
                          _t(g["background"]), _t(g["K"]), W, H)
     np.testing.assert_array_equal(out.contributors.cpu().numpy(), g["contributors"])
-    np.testing.assert_allclose(out.features.cpu().numpy(), g["image"], rtol=0, atol=1e-5)
+    np.testing.assert_allclose(out.planar().cpu().numpy(), g["image"], rtol=0, atol=1e-5)
     np.testing.assert_allclose(out.auxiliary.cpu().numpy(), g["auxiliary"], rtol=0, atol=1e-5)
 
 
@@ -86,7 +95,7 @@ def test_rade_render_backward_matches_reference_kernels(golden):
     st = _golden_state(g)
     bins = dict(ranges=_t(g["ranges"]), point_list=_t(g["ids"]))
     extras = _t(g["extras"]) if g["extras"].shape[1] else None
-    fwd = rrender.RenderedPixels(_t(g["image"]), _t(g["auxiliary"]), _t(g["contributors"]))
+    fwd = _forward_from_planar(g)
     ups = tuple(_t(g[k]) for k in ("up_features", "up_alpha", "up_depth", "up_median",
                                    "up_normals"))
     gc, gq, ga, gb, gp, gn, gabs = rrender.backward(
@@ -107,7 +116,7 @@ def test_rade_render_backward_partial_upstreams(golden):
     bins = dict(ranges=_t(g["ranges"]), point_list=_t(g["ids"]))
     extras = _t(g["extras"]) if g["extras"].shape[1] else None
     feats = np.concatenate([g["colors"], g["extras"]], 1)
-    fwd = rrender.RenderedPixels(_t(g["image"]), _t(g["auxiliary"]), _t(g["contributors"]))
+    fwd = _forward_from_planar(g)
     names = ("up_features", "up_alpha", "up_depth", "up_median", "up_normals")
     for k, name in enumerate(names):
         ups = [None] * 5
@@ -267,7 +276,7 @@ def test_rade_config4_shape_against_oracle():
     image, aux, contrib = O.rade_render(W, H, ranges, ids, ref["centers"], ref["conics"], feats,
                                         bg, ref["planes"], ref["normals"], K.numpy())
     np.testing.assert_array_equal(out.contributors.cpu().numpy(), contrib)
-    np.testing.assert_allclose(out.features.cpu().numpy(), image, atol=1e-5, rtol=1e-6)
+    np.testing.assert_allclose(out.planar().cpu().numpy(), image, atol=1e-5, rtol=1e-6)
     np.testing.assert_allclose(out.auxiliary.cpu().numpy(), aux, atol=1e-5, rtol=1e-6)
     ups = [rng.standard_normal((H, W, k)).astype(np.float32) for k in (35, 1, 1, 1, 3)]
     gc, gq, ga, gb, gp, gn, gabs = rrender.backward(
