@@ -64,10 +64,12 @@ SIGNATURES: dict[str, tuple] = {
     "splat_render_backward": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _I, _I, _P, _I, _I, _I,
                                    _P, _P, _P, _P, _I, _I, _P, _I, _P, _P, _P, _P, _P, _I,
                                    _P, _P]),
-    "splat_rade_project_forward": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F, _F,
-                                        _P, _P, _P, _P, _P, _P, _P, _P]),
-    "splat_rade_project_backward": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P, _P,
-                                         _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "splat_rade_project_forward": (_I, [_I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,
+                                        _F, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P,
+                                        _P, _P, _P, _P, _P]),
+    "splat_rade_project_backward": (_I, [_I, _P, _P, _I, _P, _P, _P, _P, _P, _I, _I, _F, _P,
+                                         _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _P,
+                                         _P, _P, _P, _P, _P, _P]),
     "splat_rade_render_forward": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _P, _P, _I, _I, _P,
                                        _I, _I, _P, _P, _P, _I, _I, _P, _I, _P, _I, _P, _I,
                                        _P, _I, _I, _P, _P, _I, _I, _P, _P, _P, _P, _P]),

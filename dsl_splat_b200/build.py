@@ -28,7 +28,7 @@ BUILD_DIR = os.path.join(HERE, "_build")
 # source -> its contraction flag
 SOURCES = {"splat200.cu": "-fmad=false", "project_backward.cu": "-fmad=true"}
 HEADERS = ["splat_common.cuh", "cameras.cuh", "project.cuh", "binning.cuh", "render.cuh",
-           "footprint.cuh", "tile_modes.cuh", "host_runtime.h", "rade.cuh"]
+           "footprint.cuh", "tile_modes.cuh", "host_runtime.h", "rade.cuh", "rade_project.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -23,6 +23,7 @@
 
 #include "host_runtime.h"
 #include "project.cuh"
+#include "rade_project.cuh"
 #include "splat_common.cuh"
 
 namespace splat {
@@ -927,6 +928,33 @@ int project_backward_dispatch(const ProjectBackwardParams& p, cudaStream_t s) {
   const int r = p.cam_grads ? launch_degree<true>(p, s) : launch_degree<false>(p, s);
   if (r != kOk) return r;
   return host::check_launch("project_backward");
+}
+
+namespace {
+template <int DEG>
+void launch_rade_backward(const RadeProjectParams& p, cudaStream_t s) {
+  // grid-stride, 128 threads (about 150 registers each: three blocks per
+  // SM); a few blocks per SM keep the camera atomics per block few
+  const unsigned blocks =
+      std::min(host::blocks_for(p.n, 128), static_cast<unsigned>(6 * host::sm_count()));
+  rade_project_backward_kernel<DEG><<<blocks, 128, 0, host::counted(s)>>>(p);
+}
+}  // namespace
+
+int rade_project_backward_dispatch(const RadeProjectParams& p, cudaStream_t s) {
+  if (p.n == 0) return kOk;
+  if (p.sh == nullptr) {
+    launch_rade_backward<-1>(p, s);
+  } else {
+    switch (p.sh_degree) {
+      case 0: launch_rade_backward<0>(p, s); break;
+      case 1: launch_rade_backward<1>(p, s); break;
+      case 2: launch_rade_backward<2>(p, s); break;
+      case 3: launch_rade_backward<3>(p, s); break;
+      default: return host::fail(kInvalidArgument, "sh_degree must be in [0,3]");
+    }
+  }
+  return host::check_launch("rade_project_backward");
 }
 
 }  // namespace splat

@@ -1176,14 +1176,21 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
 // ---- RaDe-GS ----------------------------------------------------------------
 
 int splat_rade_project_forward(int n, const float* means, const float* quats,
-                               const float* scales, const float* opacities, const float* view,
-                               const float* proj, const float* K, int width, int height,
-                               float near_plane, float far_plane, float radius_clip,
+                               int normalize_quats, const float* scales, const float* opacities,
+                               const float* view, const float* proj, const float* K, int width,
+                               int height, float near_plane, float far_plane, float radius_clip,
                                float kernel_size, float* centers, float* conics, int* radii,
                                int* tiles, float* depths, float* planes, float* normals,
-                               void* stream) {
+                               int sh_degree, int sh_k, const float* sh, const float* campos,
+                               float* colors, unsigned char* active, float* meta_means2d,
+                               float* meta_opacities, float* meta_conics, void* stream) {
   if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
   if (!(kernel_size >= 0.0f)) return fail(kInvalidArgument, "kernel_size must be nonnegative");
+  if (sh && (sh_degree < 0 || sh_degree > 3 || sh_k < (sh_degree + 1) * (sh_degree + 1) ||
+             !colors))
+    return fail(kInvalidArgument, "bad SH arguments");
+  if (meta_means2d && (!meta_opacities || !meta_conics))
+    return fail(kInvalidArgument, "metadata outputs come together");
   if (n == 0) return kOk;
   if (!means || !quats || !scales || !opacities || !view || !proj || !K || !centers || !conics ||
       !radii || !tiles || !depths || !planes || !normals)
@@ -1192,6 +1199,7 @@ int splat_rade_project_forward(int n, const float* means, const float* quats,
   p.n = n;
   p.means = means;
   p.quats = quats;
+  p.normalize_quats = normalize_quats ? 1 : 0;
   p.scales = scales;
   p.opacities = opacities;
   p.view = view;
@@ -1210,19 +1218,46 @@ int splat_rade_project_forward(int n, const float* means, const float* quats,
   p.depths = depths;
   p.planes = planes;
   p.normals = normals;
-  rade_project_kernel<<<blocks_for(n, 256), 256, 0, counted(as_stream(stream))>>>(p);
+  p.sh_degree = sh_degree;
+  p.sh_k = sh_k;
+  p.sh = sh;
+  p.campos = campos;
+  p.colors = colors;
+  p.active = active;
+  p.meta_means2d = meta_means2d;
+  p.meta_opacities = meta_opacities;
+  p.meta_conics = meta_conics;
+  cudaStream_t s = as_stream(stream);
+  const unsigned blocks = blocks_for(n, 256);
+  if (!sh) {
+    rade_project_kernel<-1><<<blocks, 256, 0, counted(s)>>>(p);
+  } else {
+    switch (sh_degree) {
+      case 0: rade_project_kernel<0><<<blocks, 256, 0, counted(s)>>>(p); break;
+      case 1: rade_project_kernel<1><<<blocks, 256, 0, counted(s)>>>(p); break;
+      case 2: rade_project_kernel<2><<<blocks, 256, 0, counted(s)>>>(p); break;
+      default: rade_project_kernel<3><<<blocks, 256, 0, counted(s)>>>(p); break;
+    }
+  }
   return check_launch("rade_project_forward");
 }
 
 int splat_rade_project_backward(int n, const float* means, const float* quats,
-                                const float* scales, const float* opacities, const float* view,
-                                const float* proj, const float* K, int width, int height,
-                                float kernel_size, const int* radii, const float* seed_centers,
+                                int normalize_quats, const float* scales,
+                                const float* opacities, const float* view, const float* proj,
+                                const float* K, int width, int height, float kernel_size,
+                                const int* radii, const float* seed_centers,
                                 const float* seed_conics, const float* seed_planes,
                                 const float* seed_normals, float* grad_means, float* grad_quats,
                                 float* grad_scales, float* grad_opacities, float* grad_view,
-                                float* grad_proj, void* stream) {
+                                float* grad_proj, int sh_degree, int sh_k, const float* sh,
+                                const float* campos, const unsigned char* active,
+                                const float* seed_colors, float* grad_sh, float* grad_campos,
+                                void* stream) {
   if (n < 0 || width <= 0 || height <= 0) return fail(kInvalidArgument, "bad projection sizes");
+  if (sh && (sh_degree < 0 || sh_degree > 3 || sh_k < (sh_degree + 1) * (sh_degree + 1) ||
+             !active || !grad_sh))
+    return fail(kInvalidArgument, "bad SH backward arguments");
   if (n == 0) return kOk;
   if (!means || !quats || !scales || !opacities || !view || !proj || !K || !radii)
     return fail(kInvalidArgument, "null rade projection buffer");
@@ -1230,6 +1265,7 @@ int splat_rade_project_backward(int n, const float* means, const float* quats,
   p.n = n;
   p.means = means;
   p.quats = quats;
+  p.normalize_quats = normalize_quats ? 1 : 0;
   p.scales = scales;
   p.opacities = opacities;
   p.view = view;
@@ -1249,10 +1285,15 @@ int splat_rade_project_backward(int n, const float* means, const float* quats,
   p.grad_opacities = grad_opacities;
   p.grad_view = grad_view;
   p.grad_proj = grad_proj;
-  // grid-stride: a few blocks per SM keep the camera atomics per block few
-  const unsigned blocks = std::min(blocks_for(n, 256), static_cast<unsigned>(4 * sm_count()));
-  rade_project_backward_kernel<<<blocks, 256, 0, counted(as_stream(stream))>>>(p);
-  return check_launch("rade_project_backward");
+  p.sh_degree = sh_degree;
+  p.sh_k = sh_k;
+  p.sh = sh;
+  p.campos = campos;
+  p.active = const_cast<unsigned char*>(active);
+  p.seed_colors = seed_colors;
+  p.grad_sh = grad_sh;
+  p.grad_campos = grad_campos;
+  return rade_project_backward_dispatch(p, as_stream(stream));
 }
 
 int splat_rade_render_forward(int width, int height, const int* ranges, const int* ids,

@@ -22,7 +22,6 @@ from ..camera_prep import prepare_cameras, prepare_cameras_with_centers
 from ..cameras import validate_camera_options
 from ..gs3d.api import _check_sh
 from ..inputs import batch_item, normalize_inputs
-from ..spherical_harmonics import spherical_harmonics
 from ..statistics import StatisticsRequest, prepare_statistics
 from ..training import prepare_training_metadata
 from .autograd import Project, Render
@@ -81,9 +80,12 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
     validate_kernel_size(kernel_size)
     validate_camera_options(width, height, near_plane, far_plane, radius_clip)
     sh_degree = _check_sh(sh_coeffs, sh_degree, features)
+    # quaternions reach the projection kernels raw: they apply inputs.py:252's
+    # F.normalize with Torch's CUDA bits and its VJP in the backward
     layout = normalize_inputs(means, quats, scales, opacities,
                               features if sh_coeffs is None else sh_coeffs, viewmats, Ks,
-                              backgrounds, extra_features, None, sh_degree)
+                              backgrounds, extra_features, None, sh_degree,
+                              normalize_quats=False)
     with_centers = sh_degree is not None and sh_degree > 0
     camera_status: list = []
     if with_centers:
@@ -106,21 +108,24 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
             view = batch_item(batch_item(layout.viewmats, b), c)
             proj = batch_item(batch_item(full, b), c)
             K = batch_item(batch_item(layout.Ks, b), c).contiguous()
-            ctr, con, radii, tiles, depths, planes, normals = Project.apply(
-                bm, bq, bs, bo, view, proj, K, config, grad_enabled)
-            state = ProjectedGaussians(ctr, con, radii, tiles, depths, planes, normals)
             values = layout.colors.at(b, c)
+            campos = batch_item(batch_item(centers, b), c) if with_centers else None
+            # one launch: projection, SH colours on means - campos, metadata
+            (ctr, con, colors, radii, tiles, depths, planes, normals, m2d, mop,
+             mcon) = Project.apply(bm, bq, bs, bo, values if sh_degree is not None else None,
+                                   view, proj, campos, K, config, sh_degree, grad_enabled)
+            state = ProjectedGaussians(ctr, con, radii, tiles, depths, planes, normals)
             if sh_degree is not None:
-                dirs = bm if centers is None else bm - batch_item(batch_item(centers, b), c)
-                values = spherical_harmonics(values, dirs.contiguous(), sh_degree, radii=radii)
+                values = colors
             extras = None if layout.extras is None else layout.extras.at(b, c)
             bg = (None if layout.backgrounds is None
                   else batch_item(batch_item(layout.backgrounds, b), c))
             frames.append((b, c, state, values, extras, bg, K))
-            meta = stages.metadata(stages.ProjectedGaussians(ctr.detach(), con.detach(), radii,
-                                                             tiles, depths))
-            for name, value in meta.items():
-                rows[name].append(value)
+            rows["radii"].append(radii[:, None].expand(-1, 2))
+            rows["means2d"].append(m2d)
+            rows["opacities"].append(mop)
+            rows["tiles_per_gauss"].append(tiles)
+            rows["conics"].append(mcon)
         for name, r in rows.items():
             dense[name].append(r[0][None] if len(r) == 1 else torch.stack(r))
     geometry = {

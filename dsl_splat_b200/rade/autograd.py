@@ -23,37 +23,59 @@ from .projection import ProjectedGaussians, ViewConfig
 
 
 class Project(torch.autograd.Function):
-    """rade/ops.py:70-165 _Project: differentiable centers, conics, ray
-    planes and normals; radii, tile counts and sort distances are discrete."""
+    """rade/ops.py:70-165 _Project, fused with the SH colours
+    (rade/api.py:153-165) and the dense metadata of the same launch:
+    differentiable centers, conics, colors, ray planes and normals; radii,
+    tile counts, sort distances and the metadata are discrete.  quats_raw
+    is normalised in-kernel with Torch's CUDA F.normalize bits and the
+    backward applies the normalisation's VJP."""
 
     @staticmethod
-    def forward(ctx: Any, means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor,
-                view: Tensor, full: Tensor, intrinsics: Tensor, config: ViewConfig,
-                grad_enabled: bool):
-        means, quats, scales = means.contiguous(), quats.contiguous(), scales.contiguous()
+    def forward(ctx: Any, means: Tensor, quats_raw: Tensor, scales: Tensor, opacities: Tensor,
+                sh: Tensor | None, view: Tensor, full: Tensor, campos: Tensor | None,
+                intrinsics: Tensor, config: ViewConfig, sh_degree: int, grad_enabled: bool):
+        means, quats_raw, scales = means.contiguous(), quats_raw.contiguous(), scales.contiguous()
         opacities, view, full = opacities.contiguous(), view.contiguous(), full.contiguous()
         intrinsics = intrinsics.contiguous()
-        st = projection.prepare(means, quats, scales, opacities, view, full, intrinsics, config)
-        if grad_enabled and any(ctx.needs_input_grad[:6]):
-            ctx.save_for_backward(means, quats, scales, opacities, view, full, intrinsics,
-                                  st.radii)
-            ctx.config = config
-        ctx.mark_non_differentiable(st.radii, st.tile_counts, st.depths)
+        sh = None if sh is None else sh.contiguous()
+        campos = None if campos is None else campos.contiguous()
+        out = projection.prepare_fused(means, quats_raw, scales, opacities, view, full,
+                                       intrinsics, config, normalize_quats=True, sh=sh,
+                                       sh_degree=sh_degree or 0, campos=campos,
+                                       need_active=grad_enabled, metadata=True)
+        st = out.state
+        colors = out.colors if out.colors is not None else means.new_empty((0, 3))
+        if grad_enabled and any(ctx.needs_input_grad[:8]):
+            ctx.save_for_backward(means, quats_raw, scales, opacities, view, full, intrinsics,
+                                  st.radii, sh, campos, out.active)
+            ctx.config, ctx.sh_degree = config, sh_degree or 0
+        ctx.mark_non_differentiable(st.radii, st.tile_counts, st.depths, out.means2d,
+                                    out.opacities, out.conics3)
+        if sh is None:
+            ctx.mark_non_differentiable(colors)
         ctx.set_materialize_grads(False)
-        return (st.centers, st.conics, st.radii, st.tile_counts, st.depths, st.ray_planes,
-                st.normals)
+        return (st.centers, st.conics, colors, st.radii, st.tile_counts, st.depths,
+                st.ray_planes, st.normals, out.means2d, out.opacities, out.conics3)
 
     @staticmethod
     @once_differentiable
-    def backward(ctx: Any, g_centers, g_conics, _radii, _tiles, _depths, g_planes, g_normals):
-        if all(g is None for g in (g_centers, g_conics, g_planes, g_normals)):
-            return (None,) * 9
-        means, quats, scales, opacities, view, full, intrinsics, radii = ctx.saved_tensors
+    def backward(ctx: Any, g_centers, g_conics, g_colors, _radii, _tiles, _depths, g_planes,
+                 g_normals, *unused):
+        if all(g is None for g in (g_centers, g_conics, g_colors, g_planes, g_normals)):
+            return (None,) * 12
+        (means, quats_raw, scales, opacities, view, full, intrinsics, radii, sh, campos,
+         active) = ctx.saved_tensors
+        needs = ctx.needs_input_grad
+        # inputs: 0 means, 1 quats_raw, 2 scales, 3 opacities, 4 sh, 5 view, 6 full, 7 campos
         state = ProjectedGaussians(None, None, radii, None, None, None, None)
-        grads = projection.backward(means, quats, scales, opacities, view, full, intrinsics,
-                                    ctx.config, state, g_centers, g_conics, g_planes, g_normals,
-                                    tuple(ctx.needs_input_grad[:6]))
-        return (*grads, None, None, None)
+        gm, gq, gs, go, gv, gp, gsh, gc = projection.backward(
+            means, quats_raw, scales, opacities, view, full, intrinsics, ctx.config, state,
+            g_centers, g_conics, g_planes, g_normals,
+            (needs[0], needs[1], needs[2], needs[3], needs[5], needs[6]),
+            normalize_quats=True, sh=sh, sh_degree=ctx.sh_degree, campos=campos, active=active,
+            grad_colors=None if g_colors is None else g_colors.contiguous(),
+            need_sh=sh is not None and needs[4], need_campos=campos is not None and needs[7])
+        return (gm, gq, gs, go, gsh, gv, gp, gc, None, None, None, None)
 
 
 class Render(torch.autograd.Function):

@@ -10,7 +10,6 @@ from typing import Sequence
 
 import torch
 from torch import Tensor
-from torch.nn.functional import normalize
 
 from .. import stages
 from ..camera_prep import prepare_camera
@@ -74,10 +73,11 @@ def prepare_gaussians(means: Tensor, quats: Tensor, scales: Tensor, opacities: T
         raise ValueError("kernel_size must be finite and nonnegative")
     config = ViewConfig(config.width, config.height, config.near, config.far,
                         config.radius_clip, "radius", float(kernel_size))
-    out = Project.apply(means.contiguous(), normalize(quats, dim=-1).contiguous(),
-                        scales.contiguous(), opacities.contiguous(), view, full, intrinsics,
-                        config, torch.is_grad_enabled())
-    return GaussianGeometry(*out, intrinsics, config)
+    # quats are normalised in-kernel (Torch's F.normalize bits, with its VJP)
+    ctr, con, _, radii, tiles, depths, planes, normals, *_ = Project.apply(
+        means.contiguous(), quats.contiguous(), scales.contiguous(), opacities.contiguous(),
+        None, view, full, None, intrinsics, config, None, torch.is_grad_enabled())
+    return GaussianGeometry(ctr, con, radii, tiles, depths, planes, normals, intrinsics, config)
 
 
 def bin_and_sort(geometry: GaussianGeometry) -> GaussianTiles:

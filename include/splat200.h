@@ -286,28 +286,46 @@ int splat_render_backward(int width, int height, const int* ranges, const int* i
  * covariance dilated by kernel_size (>= 0) and the opacity scaled by
  * rade/projection.py:50-54's coefficient; depths (n) is the radial distance
  * of the camera-space centre; planes / normals (n,3) receive the ray plane
- * and camera-space normal of every visible row. */
+ * and camera-space normal of every visible row.  normalize_quats: quats are
+ * raw and normalised in-kernel with the bits of Torch's CUDA F.normalize
+ * (inputs.py:252).  Optional, as in splat_project_forward_fused: the SH
+ * colours (sh != NULL: (n,sh_k,3) coefficients of degree sh_degree on
+ * directions means - campos (campos NULL: means), rade/api.py:153-165)
+ * into colors (n,3) with the clamp mask into active (n,3) (may be NULL), and
+ * the dense metadata (meta_means2d (n,2), meta_opacities (n), meta_conics
+ * (n,3); NULL to skip, zero on culled rows). */
 int splat_rade_project_forward(int n, const float* means, const float* quats,
-                               const float* scales, const float* opacities, const float* view,
-                               const float* proj, const float* K, int width, int height,
-                               float near_plane, float far_plane, float radius_clip,
+                               int normalize_quats, const float* scales, const float* opacities,
+                               const float* view, const float* proj, const float* K, int width,
+                               int height, float near_plane, float far_plane, float radius_clip,
                                float kernel_size, float* centers, float* conics, int* radii,
                                int* tiles, float* depths, float* planes, float* normals,
-                               void* stream);
+                               int sh_degree, int sh_k, const float* sh, const float* campos,
+                               float* colors, unsigned char* active, float* meta_means2d,
+                               float* meta_opacities, float* meta_conics, void* stream);
 
 /* rade/projection.py:320-398 project_backward: the VJP of projection_loss
  * (:294-317) for seeds on centers (n,2), conics (n,4), ray planes and
  * normals (n,3) (NULL: zero).  Per-Gaussian gradients (NULL to skip) are
- * WRITTEN, with zeros on culled rows; grad_view / grad_proj (4,4) are
- * ACCUMULATED (NULL to skip). */
+ * WRITTEN, with zeros on culled rows; grad_quats is w.r.t. the raw
+ * quaternions when normalize_quats.  grad_view / grad_proj (4,4) are
+ * ACCUMULATED (NULL to skip).  With sh != NULL also the SH VJP
+ * (primitives/sh.py:82-138) of the colour upstream seed_colors (n,3)
+ * through the forward's clamp mask active: grad_sh (n,sh_k,3) WRITTEN,
+ * the direction gradient added to grad_means and, negated, ACCUMULATED
+ * into grad_campos (3) (NULL to skip). */
 int splat_rade_project_backward(int n, const float* means, const float* quats,
-                                const float* scales, const float* opacities, const float* view,
-                                const float* proj, const float* K, int width, int height,
-                                float kernel_size, const int* radii, const float* seed_centers,
+                                int normalize_quats, const float* scales,
+                                const float* opacities, const float* view, const float* proj,
+                                const float* K, int width, int height, float kernel_size,
+                                const int* radii, const float* seed_centers,
                                 const float* seed_conics, const float* seed_planes,
                                 const float* seed_normals, float* grad_means, float* grad_quats,
                                 float* grad_scales, float* grad_opacities, float* grad_view,
-                                float* grad_proj, void* stream);
+                                float* grad_proj, int sh_degree, int sh_k, const float* sh,
+                                const float* campos, const unsigned char* active,
+                                const float* seed_colors, float* grad_sh, float* grad_campos,
+                                void* stream);
 
 /* rade/render.py:99-322 render / render_statistics.  Channels: colors' ch_a
  * columns (row stride stride_a) then extras' ch_b columns; background covers

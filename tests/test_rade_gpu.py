@@ -318,3 +318,59 @@ def test_rade_ops_stages_compose_like_rasterize(golden):
     np.testing.assert_allclose(px.features.cpu().numpy(), img[..., :-6], atol=1e-5, rtol=0)
     np.testing.assert_allclose(px.depth.cpu().numpy()[..., 0], img[..., -5], atol=1e-5, rtol=0)
     np.testing.assert_allclose(px.normals.cpu().numpy(), img[..., -3:], atol=1e-5, rtol=0)
+
+
+@pytest.mark.parametrize("name", ["c1_sh3", "dense_sh1"])
+def test_rade_fused_sh_matches_composed_sh(name):
+    """rade.rasterize(sh_coeffs=...) (projection, SH colours on means - campos
+    and metadata in one launch each way) against the composition the
+    reference runs: the standalone SH autograd Function on means - campos,
+    then rade.rasterize(features=colours).  Images identical to 1e-5 (same
+    colour bits); gradients of means, quats, scales, opacities, SH
+    coefficients and the view matrix within relative L2 1e-4.  The
+    quaternions are not unit length: a third run normalises them with Torch
+    first, and the in-kernel normalisation's VJP must give the same quats
+    gradient (1e-3)."""
+    from dsl_splat_b200.camera_prep import prepare_cameras_with_centers
+    from dsl_splat_b200.spherical_harmonics import spherical_harmonics
+
+    g = dict(np.load(os.path.join(ROOT, "tests", "golden", f"rade_{name}.npz")))
+    W, H, deg = int(g["width"]), int(g["height"]), int(g["sh_degree"])
+    rng = np.random.default_rng(3)
+    raw_quats = g["quats"] * rng.uniform(0.5, 2.0, (len(g["quats"]), 1)).astype(np.float32)
+    ups = [_t(rng.standard_normal((H, W, k)).astype(np.float32)) for k in (3, 1, 1, 1, 3)]
+
+    def run(mode: str):
+        leaves = [_t(g["means"]), _t(raw_quats), _t(g["scales"]), _t(g["opacities"]),
+                  _t(g["sh"]), _t(g["viewmat"])[None]]
+        for t in leaves:
+            t.requires_grad_()
+        means, quats, scales, opac, sh, view = leaves
+        Ks = _t(g["K"])[None]
+        kw = dict(kernel_size=float(g["kernel_size"]), absgrad=True)
+        if mode == "fused":
+            res = rade.rasterize(means, quats, scales, opac, view, Ks, W, H, sh_coeffs=sh,
+                                 sh_degree=deg, **kw)
+        else:
+            with torch.no_grad():
+                radii = rade.rasterize(means, quats, scales, opac, view, Ks, W, H,
+                                       features=_t(g["colors"]), **kw).radii[0, :, 0]
+            _, campos = prepare_cameras_with_centers(view, Ks, W, H)
+            colors = spherical_harmonics(sh, (means - campos[0]).contiguous(), deg,
+                                         radii=radii.contiguous())
+            q = torch.nn.functional.normalize(quats, dim=-1) if mode == "normalize" else quats
+            res = rade.rasterize(means, q, scales, opac, view, Ks, W, H, features=colors, **kw)
+        outs = (res.features[0], res.alpha[0], res.depth[0], res.median_depth[0],
+                res.normals[0])
+        torch.autograd.backward(outs, ups)
+        return [o.detach().cpu().numpy() for o in outs], [t.grad.cpu().numpy() for t in leaves]
+
+    fused_out, fused_grads = run("fused")
+    ref_out, ref_grads = run("sh")
+    for a, b in zip(fused_out, ref_out):
+        np.testing.assert_allclose(a, b, atol=1e-5, rtol=0)
+    for a, b, what in zip(fused_grads, ref_grads,
+                          ("means", "quats", "scales", "opacities", "sh", "viewmat")):
+        assert rel_l2(a, b) <= 1e-4, what
+    _, torch_grads = run("normalize")
+    assert rel_l2(fused_grads[1], torch_grads[1]) <= 1e-3
