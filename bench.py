@@ -347,10 +347,17 @@ def main():
     # accumulates into, all-reduced in --buckets Gaussian ranges when N > 1)
     views = int(viewmats.shape[0])
     frames_per_step = int(s.meta.get("cameras", world))
+    # RaDe-GS (config 4, one view per rank): its projection does not feed a
+    # GradientSync, so N > 1 all-reduces the parameter gradients (extras
+    # included) in one coalesced NCCL group after each backward
     sync = (sharding.GradientSync(means, quats, scales, opac, sh,
                                   group=dist.group.WORLD if pg is not None else None,
                                   buckets=args.buckets)
-            if pg is not None or views > 1 else None)
+            if (pg is not None or views > 1) and not is_rade else None)
+
+    def reduce_rade_grads():
+        if is_rade and pg is not None:
+            sharding.allreduce_parameter_grads(params, group=dist.group.WORLD)
 
     def step():
         for p in params:
@@ -358,6 +365,7 @@ def main():
         if sync is None:
             res = rasterize_view(viewmats, Ks)
             torch.autograd.backward(*outputs_and_grads(res))
+            reduce_rade_grads()
         else:
             with sync:
                 res = rasterize_view(viewmats, Ks)
@@ -460,6 +468,7 @@ def main():
                 r = rasterize_view(vm, kk)
                 loss = loss_of(r)
                 loss.backward()
+                reduce_rade_grads()
             else:
                 with sync:
                     r = rasterize_view(vm, kk)
@@ -513,9 +522,12 @@ def main():
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded, BASELINE config distributions)",
                 "config": dict(describe(s, world), **(
-                    {"gradient_allreduce": f"NCCL, {args.buckets} Gaussian-range bucket(s)"
-                                           + (" overlapped with the projection backward"
-                                              if args.buckets > 1 else "")}
+                    {"gradient_allreduce": (
+                        "NCCL, one coalesced all-reduce of the parameter gradients after "
+                        "the backward" if is_rade else
+                        f"NCCL, {args.buckets} Gaussian-range bucket(s)"
+                        + (" overlapped with the projection backward"
+                           if args.buckets > 1 else ""))}
                     if world > 1 else {})),
                 "roofline": roofline, "cpu_baseline": cpu,
                 "e2e": e2e, "gpu_launches": int(launches), "clocks": clocks.summary()}
