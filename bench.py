@@ -170,8 +170,47 @@ class ClockSampler:
 
 # ---- CPU baseline (the oracle) ----------------------------------------------------
 
+def cpu_band_step_rade(s, rows: int, y0: int = 0):
+    """One RaDe-GS fwd+bwd of the oracle on image rows [y0, y0+rows) of view 0:
+    camera prep, projection, SH, binning, geometry blend and its backward in
+    the C++ restatement (OpenMP), the projection VJP as float64 Torch
+    autograd (oracle/rade_vjp.py, Torch's host threads) and the SH backward."""
+    from oracle import oracle as O
+    from oracle import rade_vjp
+    import torch.nn.functional as F
+    W = s.width
+    K = s.Ks[0].numpy().copy()
+    K[1, 2] -= y0
+    view = s.viewmats[0].numpy()
+    means, scales, opac = s.means.numpy(), s.scales.numpy(), s.opacities.numpy()
+    qn = F.normalize(s.quats, dim=-1).numpy()
+    full, _, campos, _ = O.cameras_prepare(view[None], K[None], W, rows, True)
+    geo = O.rade_project(means, qn, scales, opac, view, full[0], K, W, rows)
+    dirs = means - campos[0]
+    colors, active = O.sh_forward(s.sh_coeffs.numpy(), dirs, s.sh_degree, geo["radii"])
+    feats = np.concatenate([colors, s.extras.numpy()], 1)
+    offsets = np.cumsum(geo["tiles"]).astype(np.int32)
+    _, ids, ranges = O.bin_and_sort(geo["centers"], geo["radii"], geo["depths"], offsets, W,
+                                    rows)
+    bg = np.zeros(feats.shape[1], np.float32)
+    image, aux, contrib = O.rade_render(W, rows, ranges, ids, geo["centers"], geo["conics"],
+                                        feats, bg, geo["planes"], geo["normals"], K)
+    rng = np.random.default_rng(y0)
+    ups = [rng.standard_normal((rows, W, k)).astype(np.float32)
+           for k in (feats.shape[1], 1, 1, 1, 3)]
+    g = O.rade_render_backward(W, rows, ranges, ids, geo["centers"], geo["conics"], feats, bg,
+                               geo["planes"], geo["normals"], K, image, aux, contrib, *ups)
+    rade_vjp.project_backward(means, qn, scales, opac, view, full[0], K, W, rows, geo["radii"],
+                              g["centers"], g["conics"], g["planes"], g["normals"],
+                              planes=geo["planes"])
+    O.sh_backward(s.sh_coeffs.numpy(), dirs, s.sh_degree, geo["radii"], active,
+                  g["features"][:, :3].astype(np.float32))
+
+
 def cpu_band_step(s, rows: int, y0: int = 0):
     """One fwd+bwd of the oracle on image rows [y0, y0+rows) of view 0."""
+    if s.meta["config"] == 4:
+        return cpu_band_step_rade(s, rows, y0)
     from oracle import oracle as O
     import torch.nn.functional as F
     K = s.Ks[0].numpy().copy()
@@ -233,9 +272,10 @@ def run_reference(args, rank, world):
         times.append(time.perf_counter() - t0)
     frac = rows / s.height
     value = frac * len(times) / sum(times)
-    sample = (f"oracle (C++ restatement of dsl_splat gs3d; the Warp reference needs warp-lang, "
-              f"absent) with {threads} OpenMP threads, image rows 0-{rows} of {s.height} "
-              f"({frac:.3f} frame) per step; value = frame fraction / time")
+    what = "RaDe-GS (projection VJP as float64 Torch autograd)" if args.config == 4 else "gs3d"
+    sample = (f"oracle (C++ restatement of dsl_splat {what}; the Warp reference needs "
+              f"warp-lang, absent) with {threads} OpenMP threads, image rows 0-{rows} of "
+              f"{s.height} ({frac:.3f} frame) per step; value = frame fraction / time")
     line = {"metric": metric_for(args.config), "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
@@ -509,7 +549,7 @@ def main():
                        "host one step later"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not is_rade:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(s, args.cpu_budget)
 
     if pg is not None:
