@@ -23,6 +23,10 @@ Operator <- reference code it stands for:
   bin_and_sort        splatting/binning.py:171-217
   render              gs3d/render.py:359-406 (features + a constant alpha channel)
   render_backward     gs3d/render.py:409-463
+  rade_project        rade/projection.py:422-472 (ray planes, normals, radial depths)
+  rade_project_backward  rade/projection.py:475-551
+  rade_render         rade/render.py:550-601 (colour, alpha, depths, normals)
+  rade_render_backward   rade/render.py:604-670
 """
 
 from __future__ import annotations
@@ -333,6 +337,167 @@ def _render_backward(ctx, g_image, g_alpha, g_t, g_contrib):
 
 render.register_autograd(_render_backward, setup_context=_render_setup)
 
+# ---- RaDe-GS -----------------------------------------------------------------------
+
+def _rade_config(width, height, near, far, radius_clip, kernel_size):
+    from .rade.projection import ViewConfig
+    return ViewConfig(width, height, near, far, radius_clip, "radius", kernel_size)
+
+
+@torch.library.custom_op(f"{_NS}::rade_project", mutates_args=())
+def rade_project(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, view: Tensor,
+                 full: Tensor, K: Tensor, width: int, height: int, near: float, far: float,
+                 radius_clip: float, kernel_size: float
+                 ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Normalised quats.  Returns centers, conics, radii, tile counts, radial
+    sort distances, ray planes and normals."""
+    from .rade import projection as rp
+    st = rp.prepare(means, quats, scales, opacities, view, full, K,
+                    _rade_config(width, height, near, far, radius_clip, kernel_size))
+    return (st.centers, st.conics, st.radii, st.tile_counts, st.depths, st.ray_planes,
+            st.normals)
+
+
+@rade_project.register_fake
+def _(means, quats, scales, opacities, view, full, K, width, height, near, far, radius_clip,
+      kernel_size):
+    n = means.shape[0]
+    i32 = dict(dtype=torch.int32)
+    return (means.new_empty((n, 2)), means.new_empty((n, 4)), means.new_empty((n,), **i32),
+            means.new_empty((n,), **i32), means.new_empty((n,)), means.new_empty((n, 3)),
+            means.new_empty((n, 3)))
+
+
+@torch.library.custom_op(f"{_NS}::rade_project_backward", mutates_args=())
+def rade_project_backward(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor,
+                          view: Tensor, full: Tensor, K: Tensor, width: int, height: int,
+                          kernel_size: float, radii: Tensor, grad_centers: Tensor,
+                          grad_conics: Tensor, grad_planes: Tensor, grad_normals: Tensor
+                          ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    from .rade import projection as rp
+    cfg = _rade_config(width, height, 0.0, 0.0, 0.0, kernel_size)
+    state = rp.ProjectedGaussians(None, None, radii, None, None, None, None)
+    grads = rp.backward(means, quats, scales, opacities, view, full, K, cfg, state,
+                        grad_centers.contiguous(), grad_conics.contiguous(),
+                        grad_planes.contiguous(), grad_normals.contiguous(), (True,) * 6)
+    # the two 4x4 camera gradients are views of one buffer: operator outputs
+    # must not alias each other
+    return tuple(g.clone() if i >= 4 else g for i, g in enumerate(grads[:6]))
+
+
+@rade_project_backward.register_fake
+def _(means, quats, scales, opacities, view, full, K, width, height, kernel_size, radii,
+      grad_centers, grad_conics, grad_planes, grad_normals):
+    return (torch.empty_like(means), torch.empty_like(quats), torch.empty_like(scales),
+            torch.empty_like(opacities), view.new_empty((4, 4)), full.new_empty((4, 4)))
+
+
+def _rade_project_setup(ctx, inputs, output):
+    means, quats, scales, opacities, view, full, K, width, height, *_, kernel_size = inputs
+    ctx.save_for_backward(means, quats, scales, opacities, view, full, K, output[2])
+    ctx.args = (width, height, kernel_size)
+
+
+def _rade_project_backward(ctx, g_centers, g_conics, g_radii, g_tiles, g_depths, g_planes,
+                           g_normals):
+    means, quats, scales, opacities, view, full, K, radii = ctx.saved_tensors
+    n = means.shape[0]
+    zero = means.new_zeros
+    grads = torch.ops.splat200.rade_project_backward(
+        means, quats, scales, opacities, view, full, K, *ctx.args, radii,
+        zero((n, 2)) if g_centers is None else g_centers,
+        zero((n, 4)) if g_conics is None else g_conics,
+        zero((n, 3)) if g_planes is None else g_planes,
+        zero((n, 3)) if g_normals is None else g_normals)
+    return (*grads, None, None, None, None, None, None, None)
+
+
+rade_project.register_autograd(_rade_project_backward, setup_context=_rade_project_setup)
+
+
+@torch.library.custom_op(f"{_NS}::rade_render", mutates_args=())
+def rade_render(centers: Tensor, conics: Tensor, planes: Tensor, normals: Tensor,
+                ranges: Tensor, point_list: Tensor, features: Tensor, background: Tensor,
+                K: Tensor, width: int, height: int
+                ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """features (N, C) and background (C).  Returns the features (H, W, C),
+    alpha, expected depth and median depth (H, W, 1), normals (H, W, 3),
+    auxiliary (2, H, W) and contributors (2, H, W)."""
+    from .rade import projection as rp
+    from .rade import render as rr
+    st = rp.ProjectedGaussians(centers, conics, None, None, None, planes, normals)
+    out = rr.render(st, dict(ranges=ranges, point_list=point_list), features, None,
+                    background, K, width, height)
+    return (out.features, out.alpha, out.depth, out.median, out.normals, out.auxiliary,
+            out.contributors)
+
+
+@rade_render.register_fake
+def _(centers, conics, planes, normals, ranges, point_list, features, background, K, width,
+      height):
+    C = features.shape[1]
+    img = features.new_empty
+    return (img((height, width, C)), img((height, width, 1)), img((height, width, 1)),
+            img((height, width, 1)), img((height, width, 3)), img((2, height, width)),
+            img((2, height, width), dtype=torch.int32))
+
+
+@torch.library.custom_op(f"{_NS}::rade_render_backward", mutates_args=())
+def rade_render_backward(centers: Tensor, conics: Tensor, planes: Tensor, normals: Tensor,
+                         ranges: Tensor, point_list: Tensor, features: Tensor,
+                         background: Tensor, K: Tensor, alpha: Tensor, normal_image: Tensor,
+                         auxiliary: Tensor, contributors: Tensor, grad_features: Tensor,
+                         grad_alpha: Tensor, grad_depth: Tensor, grad_median: Tensor,
+                         grad_normals: Tensor, width: int, height: int
+                         ) -> tuple[Tensor, Tensor, Tensor, Tensor, Tensor, Tensor]:
+    """Gradients of centers, conics, ray planes, normals, features and the
+    |d centers| sums."""
+    from .rade import projection as rp
+    from .rade import render as rr
+    st = rp.ProjectedGaussians(centers, conics, None, None, None, planes, normals)
+    fwd = rr.RenderedPixels(None, alpha, None, None, normal_image, auxiliary, contributors)
+    gc, gq, gf, _, gp, gn, gabs = rr.backward(
+        st, dict(ranges=ranges, point_list=point_list), features, None, background, K, fwd,
+        (grad_features, grad_alpha, grad_depth, grad_median, grad_normals), width, height,
+        absgrad=True)
+    return gc, gq, gp, gn, gf, gabs
+
+
+@rade_render_backward.register_fake
+def _(centers, conics, planes, normals, ranges, point_list, features, background, K, alpha,
+      normal_image, auxiliary, contributors, grad_features, grad_alpha, grad_depth,
+      grad_median, grad_normals, width, height):
+    return (torch.empty_like(centers), torch.empty_like(conics), torch.empty_like(planes),
+            torch.empty_like(normals), torch.empty_like(features), torch.empty_like(centers))
+
+
+def _rade_render_setup(ctx, inputs, output):
+    centers, conics, planes, normals, ranges, point_list, features, background, K, W, H = inputs
+    ctx.save_for_backward(centers, conics, planes, normals, ranges, point_list, features,
+                          background, K, output[1], output[4], output[5], output[6])
+    ctx.size = (W, H)
+
+
+def _rade_render_backward(ctx, g_feat, g_alpha, g_depth, g_median, g_normals, g_aux,
+                          g_contrib):
+    (centers, conics, planes, normals, ranges, point_list, features, background, K, alpha,
+     normal_image, aux, contrib) = ctx.saved_tensors
+    W, H = ctx.size
+    zero = features.new_zeros
+
+    def up(g, k):
+        return zero((H, W, k)) if g is None else g.contiguous()
+
+    gc, gq, gp, gn, gf, _ = torch.ops.splat200.rade_render_backward(
+        centers, conics, planes, normals, ranges, point_list, features, background, K, alpha,
+        normal_image, aux, contrib, up(g_feat, features.shape[1]), up(g_alpha, 1),
+        up(g_depth, 1), up(g_median, 1), up(g_normals, 3), W, H)
+    return gc, gq, gp, gn, None, None, gf, None, None, None, None
+
+
+rade_render.register_autograd(_rade_render_backward, setup_context=_rade_render_setup)
+
 OPERATORS = ("cameras_prepare", "project", "project_backward", "project_views",
              "project_views_backward", "sh_forward", "sh_backward", "bin_and_sort", "render",
-             "render_backward")
+             "render_backward", "rade_project", "rade_project_backward", "rade_render",
+             "rade_render_backward")

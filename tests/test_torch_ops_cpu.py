@@ -70,3 +70,33 @@ def test_fake_shapes():
             means, quats, scales, views, fulls, Ks, W, H, out[3], coeffs, 3, campos, out[6],
             out[0], out[1], out[2])
         assert [tuple(g.shape) for g in grads] == [(n, 3), (n, 4), (n, 3), (n,), (n, 16, 3)]
+
+
+def test_rade_fake_shapes():
+    n, W, H, C = 500, 64, 48, 7
+    with FakeTensorMode(shape_env=ShapeEnv()):
+        f32 = dict(device="cuda", dtype=torch.float32)
+        means, quats = torch.empty(n, 3, **f32), torch.empty(n, 4, **f32)
+        scales, opac = torch.empty(n, 3, **f32), torch.empty(n, **f32)
+        view, full, K = torch.empty(4, 4, **f32), torch.empty(4, 4, **f32), torch.empty(3, 3, **f32)
+        out = torch.ops.splat200.rade_project(means, quats, scales, opac, view, full, K, W, H,
+                                              0.2, float("inf"), 0.0, 0.3)
+        assert [tuple(t.shape) for t in out] == [(n, 2), (n, 4), (n,), (n,), (n,), (n, 3),
+                                                 (n, 3)]
+        ctr, con, radii, tiles, depths, planes, normals = out
+        ranges, ids = torch.ops.splat200.bin_and_sort(ctr, con, radii, tiles, depths, W, H,
+                                                      "radius")
+        feats, bg = torch.empty(n, C, **f32), torch.empty(C, **f32)
+        img = torch.ops.splat200.rade_render(ctr, con, planes, normals, ranges, ids, feats, bg,
+                                             K, W, H)
+        assert [tuple(t.shape) for t in img] == [(H, W, C), (H, W, 1), (H, W, 1), (H, W, 1),
+                                                 (H, W, 3), (2, H, W), (2, H, W)]
+        assert img[6].dtype == torch.int32
+        g = torch.ops.splat200.rade_render_backward(ctr, con, planes, normals, ranges, ids,
+                                                    feats, bg, K, img[1], img[4], img[5],
+                                                    img[6], *img[:5], W, H)
+        assert [tuple(t.shape) for t in g] == [(n, 2), (n, 4), (n, 3), (n, 3), (n, C), (n, 2)]
+        pg = torch.ops.splat200.rade_project_backward(means, quats, scales, opac, view, full,
+                                                      K, W, H, 0.3, radii, g[0], g[1], g[2],
+                                                      g[3])
+        assert [tuple(t.shape) for t in pg] == [(n, 3), (n, 4), (n, 3), (n,), (4, 4), (4, 4)]

@@ -126,3 +126,47 @@ def test_project_views_op_and_autograd():
         out[3], sh.detach(), 3, campos, out[6], w[0], w[1], w[2])
     for leaf, wv in zip(leaves, want):
         assert rel_l2(leaf.grad.cpu(), wv.cpu()) <= 1e-6
+
+
+def test_rade_ops_match_stage_api_and_autograd():
+    """torch.ops.splat200.rade_* chained with autograd against rade.ops
+    (prepare_gaussians -> bin_and_sort -> rasterize_to_pixels): the same five
+    images and the same gradients (quaternions normalised once on each side:
+    by F.normalize before the operators, in-kernel in rade.ops)."""
+    from dsl_splat_b200 import PinholeCamera, rade
+
+    d = torch.device("cuda", 0)
+    s = make_scene(4, n=20000, width=320, height=240)
+    W, H = s.width, s.height
+    view, K = s.viewmats[0].to(d).contiguous(), s.Ks[0].to(d).contiguous()
+    full, _, _ = torch.ops.splat200.cameras_prepare(view[None], K[None], W, H, True)
+    g = torch.Generator().manual_seed(9)
+    feats0 = torch.rand(s.means.shape[0], 35, generator=g).to(d)
+    bg = torch.rand(35, generator=g).to(d)
+    ups = [torch.randn(H, W, k, generator=g).to(d) for k in (35, 1, 1, 1, 3)]
+
+    def leaves():
+        out = [t.to(d).clone().requires_grad_(True)
+               for t in (s.means, s.quats, s.scales, s.opacities, feats0)]
+        return out
+
+    a = leaves()
+    ctr, con, radii, tiles, depths, planes, normals = torch.ops.splat200.rade_project(
+        a[0], F.normalize(a[1], dim=-1), a[2], a[3], view, full[0], K, W, H, 0.2, float("inf"),
+        0.0, 0.0)
+    ranges, ids = torch.ops.splat200.bin_and_sort(ctr, con, radii, tiles, depths, W, H,
+                                                  "radius")
+    img_ops = torch.ops.splat200.rade_render(ctr, con, planes, normals, ranges, ids, a[4], bg, K,
+                                             W, H)[:5]
+    torch.autograd.backward(img_ops, ups)
+
+    b = leaves()
+    geo = rade.ops.prepare_gaussians(b[0], b[1], b[2], b[3], PinholeCamera(view, K, W, H, 0.2))
+    px = rade.ops.rasterize_to_pixels(geo, rade.ops.bin_and_sort(geo), b[4], bg)
+    img_api = (px.features, px.alpha, px.depth, px.median_depth, px.normals)
+    torch.autograd.backward(img_api, ups)
+
+    for x, y in zip(img_ops, img_api):
+        assert (x - y).abs().max().item() <= 1e-5
+    for x, y, name in zip(a, b, ("means", "quats", "scales", "opacities", "features")):
+        assert rel_l2(x.grad.cpu().numpy(), y.grad.cpu().numpy()) <= 1e-4, name
