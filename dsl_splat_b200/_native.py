@@ -75,8 +75,8 @@ SIGNATURES: dict[str, tuple] = {
                                        _P, _I, _I, _P, _P, _I, _I, _P, _P, _P, _P, _P]),
     "splat_rade_render_backward": (_I, [_I, _I, _P, _P, _L, _I, _P, _P, _P, _P, _P, _I, _I,
                                         _P, _I, _I, _P, _P, _P, _I, _P, _I, _I, _P, _P, _P,
-                                        _I, _I, _P, _I, _P, _I, _P, _I, _P, _I, _I, _P, _P,
-                                        _P, _P, _P, _P, _P, _P, _P]),
+                                        _I, _I, _P, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I,
+                                        _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "splat_debug_expf": (_I, [_I, _P, _P, _P, _P]),
 }
 

@@ -39,9 +39,13 @@ struct RadeRenderParams {
   float* auxiliary;
   int* contributors;
   // backward inputs: the forward's outputs and the upstream images
-  // (channel-last (H,W,k) with the given pixel / channel strides; null = 0)
-  const float* up_features;
-  int up_feat_pix, up_feat_ch;
+  // (channel-last (H,W,k) with the given pixel / channel strides; null = 0);
+  // the colour channels [0, ch_a) and the extra channels [ch_a, C) each
+  // from their own image
+  const float* up_colors;
+  int up_colors_pix, up_colors_ch;
+  const float* up_extras;
+  int up_extras_pix, up_extras_ch;
   const float* up_alpha;
   int up_alpha_pix;
   const float* up_depth;
@@ -410,13 +414,21 @@ __global__ void __launch_bounds__(kBlock / PX) rade_backward_kernel(RadeRenderPa
       q.last_contributor = p.contributors[pixel];
       q.median_contributor = p.contributors[P + pixel];
       float bg_grad = 0.0f;
-      const float* up = p.up_features ? p.up_features + static_cast<size_t>(pixel) * p.up_feat_pix
-                                      : nullptr;
+      const float* uc = p.up_colors ? p.up_colors + static_cast<size_t>(pixel) * p.up_colors_pix
+                                    : nullptr;
+      const float* ue = p.up_extras ? p.up_extras + static_cast<size_t>(pixel) * p.up_extras_pix
+                                    : nullptr;
 #pragma unroll
       for (int c = 0; c < CHP; ++c)
         if (c < C) {
-          grad[i][c] = up ? __ldg(up + c * p.up_feat_ch) : 0.0f;
-          bg_grad += b.background[c] * grad[i][c];
+          float gval = 0.0f;
+          if (c < b.ch_a) {
+            if (uc) gval = __ldg(uc + c * p.up_colors_ch);
+          } else if (ue) {
+            gval = __ldg(ue + (c - b.ch_a) * p.up_extras_ch);
+          }
+          grad[i][c] = gval;
+          bg_grad += b.background[c] * gval;
         }
       bg_grad -=
           p.up_alpha ? __ldg(p.up_alpha + static_cast<size_t>(pixel) * p.up_alpha_pix) : 0.0f;

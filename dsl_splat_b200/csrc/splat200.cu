@@ -1344,8 +1344,9 @@ int splat_rade_render_backward(
     const float* colors, int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
     const float* background, const float* K, const float* alpha, int alpha_pix,
     const float* normal_image, int normal_pix, int normal_ch, const float* auxiliary,
-    const int* contributors, const float* up_features, int up_feat_pix, int up_feat_ch,
-    const float* up_alpha, int up_alpha_pix, const float* up_depth, int up_depth_pix,
+    const int* contributors, const float* up_colors, int up_colors_pix, int up_colors_ch,
+    const float* up_extras, int up_extras_pix, int up_extras_ch, const float* up_alpha,
+    int up_alpha_pix, const float* up_depth, int up_depth_pix,
     const float* up_median, int up_median_pix, const float* up_normals, int up_normals_pix,
     int up_normals_ch, float* grad_centers, float* grad_conics, float* grad_colors,
     float* grad_extras, float* abs_centers, float* grad_planes, float* grad_normals,
@@ -1368,9 +1369,12 @@ int splat_rade_render_backward(
   p.normal_ch = normal_ch;
   p.auxiliary = const_cast<float*>(auxiliary);
   p.contributors = const_cast<int*>(contributors);
-  p.up_features = up_features;
-  p.up_feat_pix = up_feat_pix;
-  p.up_feat_ch = up_feat_ch;
+  p.up_colors = up_colors;
+  p.up_colors_pix = up_colors_pix;
+  p.up_colors_ch = up_colors_ch;
+  p.up_extras = up_extras;
+  p.up_extras_pix = up_extras_pix;
+  p.up_extras_ch = up_extras_ch;
   p.up_alpha = up_alpha;
   p.up_alpha_pix = up_alpha_pix;
   p.up_depth = up_depth;

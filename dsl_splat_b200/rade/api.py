@@ -174,11 +174,10 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
         whole = values[0].unsqueeze(0) if len(values) == 1 else torch.stack(values)
         return whole.reshape(shape + (values[0].shape[-1],))
 
-    features_image, alpha, depth, median, normals = (assemble(v) for v in zip(*images))
-    main_features = features_image
+    main_features, extra_image, alpha, depth, median, normals = (
+        assemble(v) for v in zip(*images))
     if layout.extras is not None:
-        meta["render_extra_signals"] = features_image[..., channels:]
-        main_features = features_image[..., :channels]
+        meta["render_extra_signals"] = extra_image
     meta.update(depth=depth, median_depth=median, normals=normals)
     return RasterizationResult(main_features, alpha, depth, median, normals, meta,
                                statistics_outputs)

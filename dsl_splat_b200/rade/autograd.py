@@ -98,12 +98,24 @@ class Render(torch.autograd.Function):
             ctx.bins = {k: bins[k] for k in ("ranges", "point_list", "tile_order") if k in bins}
             ctx.config, ctx.absolute, ctx.screen_target = config, absolute, screen_target
         ctx.set_materialize_grads(False)
-        return out.images()
+        # colour and extra channels as two outputs (views of the blended
+        # buffer): the backward kernel reads their upstream gradients from two
+        # images, where slicing one output would make autograd scatter each
+        # into a zero-filled buffer of all channels
+        split = colors.shape[1]
+        ctx.split = split
+        if extras is None:
+            empty = out.features.new_empty(out.features.shape[:-1] + (0,))
+            ctx.mark_non_differentiable(empty)
+            feats, extra_image = out.features, empty
+        else:
+            feats, extra_image = out.features[..., :split], out.features[..., split:]
+        return feats, extra_image, out.alpha, out.depth, out.median, out.normals
 
     @staticmethod
     @once_differentiable
-    def backward(ctx: Any, *gradients: Tensor | None):
-        if all(g is None for g in gradients):
+    def backward(ctx: Any, g_colors, g_extras, *geometry: Tensor | None):
+        if all(g is None for g in (g_colors, g_extras) + geometry):
             return (None,) * 15
         (centers, conics, planes, normals, colors, extras, background, intrinsics, alpha,
          normal_image, aux, contrib) = ctx.saved_tensors
@@ -113,6 +125,8 @@ class Render(torch.autograd.Function):
         screen_direct = (ctx.screen_target.direct_buffer()
                          if needs[6] and ctx.screen_target is not None else None)
         state = ProjectedGaussians(centers, conics, None, None, None, planes, normals)
+        # the colour and extra upstreams are read in place (None: zero)
+        gradients = ((g_colors, g_extras if extras is not None else None),) + tuple(geometry)
         gc, gq, ga, gb, gp, gn, absolute = render.backward(
             state, ctx.bins, colors, extras, background, intrinsics,
             render.RenderedPixels(None, alpha, None, None, normal_image, aux, contrib),

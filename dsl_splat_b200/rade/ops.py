@@ -110,10 +110,11 @@ def rasterize_to_pixels(geometry: GaussianGeometry, tiles: GaussianTiles, featur
                          if statistics else ([], {}))
     bg = features.new_zeros(channels) if background is None else background.contiguous()
     bins = dict(ranges=tiles.ranges, point_list=tiles.gaussian_ids)
-    images = Render.apply(geometry.centers, geometry.conics, geometry.ray_planes,
-                          geometry.normals, features, None, None, bg, bins, geometry._intrinsics,
-                          cfg, None, None, prepared[0] if statistics else None,
-                          torch.is_grad_enabled())
+    feats, _, *geometry_images = Render.apply(
+        geometry.centers, geometry.conics, geometry.ray_planes, geometry.normals, features, None,
+        None, bg, bins, geometry._intrinsics, cfg, None, None,
+        prepared[0] if statistics else None, torch.is_grad_enabled())
+    images = (feats, *geometry_images)
     return PixelResult(*images, {name: value[0] for name, value in outputs.items()})
 
 

@@ -92,12 +92,24 @@ def backward(state: ProjectedGaussians, bins: dict, colors: Tensor, extras: Tens
              absgrad: bool = False, need_colors: bool = True, need_extras: bool = True,
              centers_out: Tensor | None = None, absolute_out: Tensor | None = None):
     """rade/render.py:604-670.  gradients: upstream of (features, alpha,
-    depth, median depth, normals), each (H, W, k) or None.  Returns grads of
+    depth, median depth, normals), each (H, W, k) or None; the features'
+    upstream is one (H, W, C) image or a pair (colours (H, W, ch_a) or None,
+    extras (H, W, ch_b) or None), read in place.  Returns grads of
     (centers, conics, colors, extras, ray_planes, normals, |centers|)."""
     pin = stages.Args()
     a, b, ca, cb = _split(colors, extras)
     channels = ca + cb
-    gf, pf, cf = _upstream(gradients[0], channels)
+    g0 = gradients[0]
+    if isinstance(g0, tuple):
+        gf, pf, cf = _upstream(g0[0], ca)
+        ge, pe, ce = _upstream(g0[1], cb)
+        up_c, up_e = pin(gf), pin(ge)
+    else:
+        # one image: the extra channels start ca floats into each pixel
+        gf, pf, cf = _upstream(g0, channels)
+        pe, ce = pf, cf
+        up_c = pin(gf)
+        up_e = None if up_c is None or cb == 0 else up_c + 4 * ca
     ga, pa, _ = _upstream(gradients[1], 1)
     gd, pd, _ = _upstream(gradients[2], 1)
     gm, pm, _ = _upstream(gradients[3], 1)
@@ -118,7 +130,7 @@ def backward(state: ProjectedGaussians, bins: dict, colors: Tensor, extras: Tens
             len(state.centers), pin(state.centers), pin(state.conics), pin(state.ray_planes),
             pin(state.normals), ptr(a), ca, ca, ptr(b), cb, cb, pin(background),
             pin(intrinsics), pin(output.alpha), 1, pin(output.normals), 3, 1,
-            pin(output.auxiliary), pin(output.contributors), pin(gf), pf, cf, pin(ga), pa,
+            pin(output.auxiliary), pin(output.contributors), up_c, pf, cf, up_e, pe, ce, pin(ga), pa,
             pin(gd), pd, pin(gm), pm,
             pin(gn), pn, cn, ptr(centers), ptr(conics), ptr(g_colors), ptr(g_extras),
             ptr(absolute), ptr(planes), ptr(normals), ptr(stages.tile_order(bins)),

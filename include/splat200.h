@@ -353,9 +353,11 @@ int splat_rade_render_forward(int width, int height, const int* ranges, const in
 
 /* rade/render.py:325-547 backward, from the forward's alpha and normal
  * images (strides as in splat_rade_render_forward), auxiliary and
- * contributors.  Upstream images are channel-last: the value of channel c
- * at pixel p is up[p*pix + c*ch] (NULL: zero) for the features (C
- * channels), alpha, expected depth, median depth and normals (3 channels).
+ * contributors.  Upstream images: the value of channel c at pixel p is
+ * up[p*pix + c*ch] (NULL: zero) for the colour channels (ch_a, up_colors),
+ * the extra channels (ch_b, up_extras; channel c of the blend is c - ch_a
+ * there), alpha, expected depth, median depth and normals (3 channels); one
+ * (H,W,C) image serves both with up_extras = up_colors + ch_a.
  * Gradients are ADDED into grad_centers (n,2), grad_conics (n,4),
  * grad_colors (n,ch_a), grad_extras (n,ch_b), abs_centers (n,2) (NULL to
  * skip the last three), grad_planes and grad_normals (n,3). */
@@ -365,8 +367,9 @@ int splat_rade_render_backward(
     const float* colors, int ch_a, int stride_a, const float* extras, int ch_b, int stride_b,
     const float* background, const float* K, const float* alpha, int alpha_pix,
     const float* normal_image, int normal_pix, int normal_ch, const float* auxiliary,
-    const int* contributors, const float* up_features, int up_feat_pix, int up_feat_ch,
-    const float* up_alpha, int up_alpha_pix, const float* up_depth, int up_depth_pix,
+    const int* contributors, const float* up_colors, int up_colors_pix, int up_colors_ch,
+    const float* up_extras, int up_extras_pix, int up_extras_ch, const float* up_alpha,
+    int up_alpha_pix, const float* up_depth, int up_depth_pix,
     const float* up_median, int up_median_pix, const float* up_normals, int up_normals_pix,
     int up_normals_ch, float* grad_centers, float* grad_conics, float* grad_colors,
     float* grad_extras, float* abs_centers, float* grad_planes, float* grad_normals,
