@@ -6,12 +6,13 @@ Two translation units, compiled in parallel and linked into one library:
   -fmad=false: every multiply-add stays two IEEE roundings unless the source
   asks for __fmaf_rn, which is what makes radii, tile counts, sort keys and
   the blended image reproducible on the CPU;
-* project_backward.cu (the projection + SH backward) with -fmad=true: its
-  outputs are gradients, compared within a relative tolerance, and
-  contraction removes a large part of its arithmetic.
+* project_backward.cu (the projection + SH backward) with -fmad=true
+  -prec-div=false -prec-sqrt=false: its outputs are gradients, compared
+  within a relative tolerance, and contraction plus the approximate divide
+  and square root (a few ulp) remove a large part of its arithmetic.
 
-Division and square root stay IEEE-rounded everywhere (the nvcc defaults
--prec-div=true -prec-sqrt=true, no --use_fast_math).
+splat200.cu keeps IEEE-rounded division and square root (the nvcc defaults
+-prec-div=true -prec-sqrt=true); nothing is built with --use_fast_math.
 """
 
 from __future__ import annotations
@@ -26,7 +27,8 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libsplat200.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 # source -> its contraction flag
-SOURCES = {"splat200.cu": "-fmad=false", "project_backward.cu": "-fmad=true"}
+SOURCES = {"splat200.cu": ["-fmad=false"],
+           "project_backward.cu": ["-fmad=true", "-prec-div=false", "-prec-sqrt=false"]}
 HEADERS = ["splat_common.cuh", "cameras.cuh", "project.cuh", "binning.cuh", "render.cuh",
            "footprint.cuh", "tile_modes.cuh", "host_runtime.h", "rade.cuh", "rade_project.cuh"]
 
@@ -56,9 +58,9 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return LIB
     os.makedirs(BUILD_DIR, exist_ok=True)
     objects, jobs = [], []
-    for src, fmad in SOURCES.items():
+    for src, flags in SOURCES.items():
         obj = os.path.join(BUILD_DIR, os.path.splitext(src)[0] + ".o")
-        cmd = [nvcc(), *NVCC_FLAGS, fmad, "-I", os.path.join(ROOT, "include"), "-c",
+        cmd = [nvcc(), *NVCC_FLAGS, *flags, "-I", os.path.join(ROOT, "include"), "-c",
                os.path.join(CSRC, src), "-o", obj]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
