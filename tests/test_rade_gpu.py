@@ -374,3 +374,35 @@ def test_rade_fused_sh_matches_composed_sh(name):
         assert rel_l2(a, b) <= 1e-4, what
     _, torch_grads = run("normalize")
     assert rel_l2(fused_grads[1], torch_grads[1]) <= 1e-3
+
+
+def test_rade_statistics_add_up_to_alpha(golden):
+    """rade.rasterize's contribution statistics (statistics.py:47-73 through
+    the rade blend): a weighted sum with pixel weights v adds v * alpha * T
+    per blended sample, so its total over Gaussians is sum_p v_p alpha_p (the
+    blend weights of a pixel sum to 1 - T_final); a masked count counts the
+    blended samples of the masked pixels, at least one per covered pixel."""
+    from dsl_splat_b200 import MaskedContributionCount, WeightedContributionSum
+
+    g = golden
+    W, H = int(g["width"]), int(g["height"])
+    dev = torch.device("cuda", 0)
+    half = torch.zeros(H, W, dtype=torch.bool, device=dev)
+    half[: H // 2] = True
+    ramp = torch.linspace(0.0, 1.0, H * W, device=dev).reshape(H, W)
+    res = rade.rasterize(
+        _t(g["means"]), _t(g["quats"]), _t(g["scales"]), _t(g["opacities"]),
+        _t(g["viewmat"])[None], _t(g["K"])[None], W, H, features=_t(g["colors"]),
+        kernel_size=float(g["kernel_size"]),
+        statistics=[WeightedContributionSum("ones", torch.ones(H, W, device=dev)),
+                    MaskedContributionCount("top", half),
+                    WeightedContributionSum("ramp", ramp)])
+    alpha = res.alpha[0, ..., 0].double()
+    for name, weights in (("ones", torch.ones_like(alpha)), ("ramp", ramp.double())):
+        total = res.statistics[name][0].double().sum()
+        want = (weights * alpha).sum()
+        assert abs(float(total - want)) <= 1e-4 * float(want), name
+    counts = res.statistics["top"][0]
+    assert counts.dtype == torch.int32 and int(counts.min()) >= 0
+    covered = int(((alpha > 0) & half).sum())
+    assert int(counts.sum()) >= covered > 0
