@@ -406,3 +406,40 @@ def test_rade_statistics_add_up_to_alpha(golden):
     assert counts.dtype == torch.int32 and int(counts.min()) >= 0
     covered = int(((alpha > 0) & half).sum())
     assert int(counts.sum()) >= covered > 0
+
+
+def test_rade_gsplat_adapter_modes_and_packed_metadata(golden):
+    """rade.gsplat.rasterization (rade/gsplat.py:82-191): RGB+ED appends the
+    expected depth, D is depth times alpha, and with its default packed=True
+    the means2d gradient and absgrad rows are the visible rows of the dense
+    API's (same call, packed=False)."""
+    from dsl_splat_b200.rade.gsplat import rasterization
+
+    g = golden
+    W, H = int(g["width"]), int(g["height"])
+    ks = float(g["kernel_size"])
+
+    def call(packed, mode):
+        means = _t(g["means"]).requires_grad_()
+        args = (means, _t(g["quats"]), _t(g["scales"]), _t(g["opacities"]), _t(g["colors"]),
+                _t(g["viewmat"])[None], _t(g["K"])[None], W, H)
+        image, alpha, meta = rasterization(*args, near_plane=0.2, eps2d=ks, packed=packed,
+                                           render_mode=mode, absgrad=True)
+        (image * image).sum().backward()
+        return image, alpha, meta, means
+
+    dense_img, dense_alpha, dense_meta, _ = call(False, "RGB+ED")
+    packed_img, packed_alpha, packed_meta, _ = call(True, "RGB+ED")
+    assert dense_img.shape[-1] == 4
+    torch.testing.assert_close(packed_img, dense_img, atol=1e-5, rtol=0)
+    torch.testing.assert_close(dense_img[..., 3:], dense_meta["depth"], atol=0, rtol=0)
+    d_img, d_alpha, _, _ = call(False, "D")
+    torch.testing.assert_close(d_img, dense_meta["depth"] * dense_alpha, atol=1e-5, rtol=1e-6)
+    ids = packed_meta["gaussian_ids"]
+    vis = (dense_meta["radii"][0] > 0).all(-1)
+    assert torch.equal(ids, vis.nonzero()[:, 0])
+    for key in ("grad", "absgrad"):
+        dense = getattr(dense_meta["means2d"], key)[0]
+        packed = getattr(packed_meta["means2d"], key)
+        assert rel_l2(packed.cpu().numpy(), dense[ids].cpu().numpy()) <= 1e-5, key
+        assert not dense[~vis].any(), key
