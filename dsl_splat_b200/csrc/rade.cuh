@@ -357,7 +357,9 @@ SPLAT_DEV GradientSlot rade_gradient_slot(const RadeRenderParams& p, int k) {
 // each.  Measured at config 4 (36 channels), one pixel per lane is fastest:
 // PX = 2 needs 187 registers (8 warps per SM); direct atomics from lanes of
 // sparsely covered samples, or a shared-memory accumulator flushed once per
-// batch, were both slower than the reduction they replace.
+// batch, were both slower than the reduction they replace, and summing the
+// two values past the third group with warp sums (instead of a fourth,
+// mostly padded butterfly) did not change the time.
 template <int PX>
 struct RadePixel {
   float fy, T, bg_term, depth_gradient, median_gradient, S, last_alpha, last_F;
