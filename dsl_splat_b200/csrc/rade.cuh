@@ -359,7 +359,10 @@ SPLAT_DEV GradientSlot rade_gradient_slot(const RadeRenderParams& p, int k) {
 // sparsely covered samples, or a shared-memory accumulator flushed once per
 // batch, were both slower than the reduction they replace, and summing the
 // two values past the third group with warp sums (instead of a fourth,
-// mostly padded butterfly) did not change the time.
+// mostly padded butterfly) did not change the time.  What does limit it is
+// latency at 16 warps per SM: bounding registers for three blocks per SM (80
+// registers, about 300 bytes of spills per thread, 24 warps) took config 4's
+// backward from 4.47 to 4.18 ms.
 template <int PX>
 struct RadePixel {
   float fy, T, bg_term, depth_gradient, median_gradient, S, last_alpha, last_F;
@@ -369,7 +372,7 @@ struct RadePixel {
 };
 
 template <int CHP, int PX>
-__global__ void __launch_bounds__(kBlock / PX) rade_backward_kernel(RadeRenderParams p) {
+__global__ void __launch_bounds__(kBlock / PX, 3) rade_backward_kernel(RadeRenderParams p) {
   constexpr int kThreads = kBlock / PX;
   constexpr int kValues = 14 + CHP;
   constexpr int kGroups = (kValues + 15) / 16;
