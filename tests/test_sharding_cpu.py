@@ -52,6 +52,44 @@ def _scene():
     return make_scene(2, n=3000, width=96, height=64, cameras=4)
 
 
+def _rade_view_grads(scene, c):
+    """One RaDe-GS view through the oracle: projection, SH colours + 5 extra
+    channels, binning, geometry blend and its backward with seeded upstream
+    images, the projection VJP (float64 autograd) and the SH backward.
+    Returns float64 gradients of (means, normalised quats, scales,
+    opacities, SH, extras)."""
+    import torch.nn.functional as F
+    from oracle import oracle as O
+    from oracle import rade_vjp
+    W, H = scene.width, scene.height
+    means, scales, opac = scene.means.numpy(), scene.scales.numpy(), scene.opacities.numpy()
+    qn = F.normalize(scene.quats, dim=-1).numpy()
+    sh, deg = scene.sh_coeffs.numpy(), scene.sh_degree
+    view, K = scene.viewmats[c].numpy(), scene.Ks[c].numpy()
+    extras = np.random.default_rng(1).standard_normal((len(means), 5)).astype(np.float32)
+    full, _, campos, _ = O.cameras_prepare(view[None], K[None], W, H, True)
+    geo = O.rade_project(means, qn, scales, opac, view, full[0], K, W, H)
+    dirs = means - campos[0]
+    colors, active = O.sh_forward(sh, dirs, deg, geo["radii"])
+    feats = np.concatenate([colors, extras], 1)
+    offsets = np.cumsum(geo["tiles"]).astype(np.int32)
+    _, ids, ranges = O.bin_and_sort(geo["centers"], geo["radii"], geo["depths"], offsets, W, H)
+    bg = np.zeros(feats.shape[1], np.float32)
+    image, aux, contrib = O.rade_render(W, H, ranges, ids, geo["centers"], geo["conics"], feats,
+                                        bg, geo["planes"], geo["normals"], K)
+    rng = np.random.default_rng(100 + c)
+    ups = [rng.standard_normal((H, W, k)).astype(np.float32) for k in (8, 1, 1, 1, 3)]
+    g = O.rade_render_backward(W, H, ranges, ids, geo["centers"], geo["conics"], feats, bg,
+                               geo["planes"], geo["normals"], K, image, aux, contrib, *ups)
+    pg = rade_vjp.project_backward(means, qn, scales, opac, view, full[0], K, W, H,
+                                   geo["radii"], g["centers"], g["conics"], g["planes"],
+                                   g["normals"], planes=geo["planes"])
+    g_sh, g_dirs = O.sh_backward(sh, dirs, deg, geo["radii"], active,
+                                 g["features"][:, :3].astype(np.float32))
+    out = [pg[0] + g_dirs, pg[1], pg[2], pg[3], g_sh, g["features"][:, 3:]]
+    return [torch.from_numpy(np.asarray(x, np.float64)) for x in out]
+
+
 def _worker(rank, world, port, outdir, mode):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
@@ -62,9 +100,10 @@ def _worker(rank, world, port, outdir, mode):
     if mode == "leave" and rank == 1:
         return  # leaves between steps, before joining the all-reduce
     idx = sharding.local_cameras(scene.viewmats.shape[0], rank, world)
+    grads_of = _rade_view_grads if mode == "rade" else _view_grads
     total = None
     for c in idx:
-        g = _view_grads(scene, c)
+        g = grads_of(scene, c)
         total = g if total is None else [a + b for a, b in zip(total, g)]
     status = "ok"
     try:
@@ -113,6 +152,22 @@ def test_two_rank_allreduce_equals_sequential_sum(tmp_path):
     for res in results:
         assert res["status"] == "ok"
         for got, ref in zip(res["grads"], want):
+            assert rel_l2(got.numpy(), ref.numpy()) <= 1e-6
+
+
+def test_two_rank_rade_allreduce_equals_sequential_sum(tmp_path):
+    """The RaDe-GS view gradients (bench.py --config 4 at N > 1 all-reduces
+    them after each backward) sharded over two gloo ranks."""
+    results = _run(2, "rade", tmp_path)
+    scene = _scene()
+    want = None
+    for c in range(scene.viewmats.shape[0]):
+        g = _rade_view_grads(scene, c)
+        want = g if want is None else [a + b for a, b in zip(want, g)]
+    for res in results:
+        assert res["status"] == "ok"
+        for got, ref in zip(res["grads"], want):
+            assert np.isfinite(ref.numpy()).all() and ref.abs().sum() > 0
             assert rel_l2(got.numpy(), ref.numpy()) <= 1e-6
 
 
