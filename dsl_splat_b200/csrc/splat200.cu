@@ -341,10 +341,15 @@ int rade_render_params(int width, int height, const int* ranges, const int* tile
                        int stride_b, const float* background, const float* K,
                        RadeRenderParams& p) {
   if (width <= 0 || height <= 0 || ch_a < 0 || ch_b < 0 || ch_a + ch_b <= 0 || n < 0 ||
-      num_ids < 0 || num_ids >= (1LL << 31) || (ch_a > 0 && (!colors || stride_a < ch_a)) ||
-      (ch_b > 0 && (!extras || stride_b < ch_b)))
+      num_ids < 0 || num_ids >= (1LL << 31) || (ch_a > 0 && stride_a < ch_a) ||
+      (ch_b > 0 && stride_b < ch_b))
     return fail(kInvalidArgument, "bad rade render sizes");
-  if (!ranges || !ids || !centers || !conics || !planes || !normals || !background || !K)
+  // per-Gaussian rows are only read when there are Gaussians (an empty
+  // tensor may have a null address)
+  if (n > 0 && ((ch_a > 0 && !colors) || (ch_b > 0 && !extras) || !centers || !conics ||
+                !planes || !normals))
+    return fail(kInvalidArgument, "null rade render input");
+  if (!ranges || (num_ids > 0 && !ids) || !background || !K)
     return fail(kInvalidArgument, "null rade render input");
   if (!aligned(centers, 8) || !aligned(conics, 16))
     return fail(kInvalidArgument, "center rows need 8-byte and conic rows 16-byte alignment");
@@ -1358,7 +1363,7 @@ int splat_rade_render_backward(
   if (rc != kOk) return rc;
   if (!alpha || !normal_image || !auxiliary || !contributors)
     return fail(kInvalidArgument, "null rade forward output");
-  if (!grad_centers || !grad_conics || !grad_planes || !grad_normals)
+  if (n > 0 && (!grad_centers || !grad_conics || !grad_planes || !grad_normals))
     return fail(kInvalidArgument, "null gradient buffers");
   if (!aligned(grad_centers, 8) || !aligned(grad_conics, 16) || !aligned(abs_centers, 8))
     return fail(kInvalidArgument, "center rows need 8-byte and conic rows 16-byte alignment");
