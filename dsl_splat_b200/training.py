@@ -73,7 +73,8 @@ class ScreenGradientTarget:
             self.fresh["views"] = set(range(self.fresh["count"]))
         if self.leaf.grad is not self.fresh.get("grad") or self.index not in self.fresh["views"]:
             return None
-        block = self.leaf.grad.view(-1, *self.leaf.shape[-2:])[self.index]
+        # the view count is explicit: with N == 0 a -1 dimension is ambiguous
+        block = self.leaf.grad.view(self.fresh["count"], *self.leaf.shape[-2:])[self.index]
         if not block.is_contiguous():
             return None
         self.fresh["views"].discard(self.index)
@@ -84,7 +85,8 @@ class ScreenGradientTarget:
         if self.leaf.grad is None:
             self.leaf.grad = torch.zeros_like(self.leaf)
         if self.gaussian_ids is None:
-            self.leaf.grad.view(-1, *gradient.shape)[self.index].add_(gradient)
+            views = self.fresh["count"] if self.fresh is not None else -1
+            self.leaf.grad.view(views, *gradient.shape)[self.index].add_(gradient)
         else:
             self.leaf.grad[self.begin:self.end].add_(gradient[self.gaussian_ids])
 

@@ -443,3 +443,35 @@ def test_rade_gsplat_adapter_modes_and_packed_metadata(golden):
         packed = getattr(packed_meta["means2d"], key)
         assert rel_l2(packed.cpu().numpy(), dense[ids].cpu().numpy()) <= 1e-5, key
         assert not dense[~vis].any(), key
+
+
+@pytest.mark.parametrize("case", ["empty", "behind_camera"])
+def test_rade_rasterize_empty_and_culled(case):
+    """No Gaussians, or only Gaussians behind the camera: the features are the
+    background, alpha, both depths and the normals are zero, nothing is
+    culled wrongly into view, and the backward runs and gives zero
+    gradients (rade/render.py:202-227: uncovered pixels keep zero depth and
+    normal)."""
+    dev = torch.device("cuda", 0)
+    W, H, n = 40, 24, (0 if case == "empty" else 50)
+    g = torch.Generator().manual_seed(8)
+    means = torch.randn(n, 3, generator=g)
+    means[:, 2] = -2.0 - torch.rand(n, generator=g)  # behind an identity camera
+    means = means.to(dev).requires_grad_()
+    quats = torch.randn(n, 4, generator=g).to(dev).requires_grad_()
+    scales = torch.full((n, 3), 0.1).to(dev).requires_grad_()
+    opac = torch.full((n,), 0.8).to(dev).requires_grad_()
+    colors = torch.rand(n, 3, generator=g).to(dev).requires_grad_()
+    K = torch.tensor([[40.0, 0.0, 20.0], [0.0, 40.0, 12.0], [0.0, 0.0, 1.0]], device=dev)
+    bg = torch.tensor([0.2, 0.4, 0.6], device=dev)
+    res = rade.rasterize(means, quats, scales, opac, torch.eye(4, device=dev)[None], K[None], W,
+                         H, features=colors, backgrounds=bg[None], absgrad=True)
+    assert torch.equal(res.features[0], bg.expand(H, W, 3))
+    for image in (res.alpha, res.depth, res.median_depth, res.normals):
+        assert not image.any()
+    assert not res.radii.any()
+    loss = (res.features.sum() + res.alpha.sum() + res.depth.sum() + res.median_depth.sum()
+            + res.normals.sum())
+    loss.backward()
+    for leaf in (means, quats, scales, opac, colors):
+        assert leaf.grad is None or not leaf.grad.any()
