@@ -1,8 +1,9 @@
 """ctypes bindings for the CPU oracle (test infrastructure only).
 
-The oracle restates dsl_splat's gs3d rasteriser and its RaDe-GS projection
-and render on the CPU (see
-splat_oracle.cpp for the per-function reference citations).  Tests,
+The oracle restates dsl_splat's gs3d rasteriser, its RaDe-GS projection
+and render, and the AAA-Gaussians preprocessing on the CPU (see
+splat_oracle.cpp and aaa_oracle.cpp for the per-function reference
+citations).  Tests,
 ``__graft_entry__.smoke()`` and bench.py's CPU legs use it as the checker and
 the CPU baseline; the product package never imports it.
 
@@ -89,6 +90,11 @@ def lib():
             _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p,
             _f32p, _f32p, _i32p, _vp, _vp, _vp, _vp, _vp, _f64p, _f64p, _f64p, _vp, _f64p, _f64p]
         L.oracle_rade_render_backward.restype = None
+        L.oracle_aaa_preprocess.argtypes = [
+            _int, _f32p, _f32p, _f32p, _f32p, _vp, _int, _int, _int, _int, _vp, _f32p, _f32p,
+            _f32p, _int, _int, _flt, _flt, _flt, _flt, _flt, _int, _int, _int, _int, _int, _int,
+            _f32p, _f32p, _f32p, _f32p, _f32p, _i32p, _i32p, _vp, _u8p, _vp, _i32p, _i32p]
+        L.oracle_aaa_preprocess.restype = None
         L.oracle_num_threads.restype = _int
         L.oracle_set_num_threads.argtypes = [_int]
         _lib = L
@@ -406,3 +412,45 @@ def rade_render_backward(width, height, ranges, ids, centers, conics, features, 
         _c(contrib, np.int32), *[_ptr(u) for u in ups], g["centers"], g["conics"],
         g["features"], _ptr(g["abs"]), g["planes"], g["normals"])
     return g
+
+
+AAA_FLAGS = ("ewa", "new_aabb", "near_clipping", "tile_culling", "complete", "cooperative")
+
+
+def aaa_preprocess(means, quats, scales, opacities, view, proj, campos, width, height,
+                   tanfov, principal, *, sh=None, sh_degree=0, filters=None, sort_order=3,
+                   modifier=1.0, flags=None):
+    """aaa/preprocess3d.py:17-245 for one view (aaa_oracle.cpp).
+
+    view / proj are the reference's transposed 4x4 camera arrays
+    (aaa/cameras.py:77-121); flags maps AAA_FLAGS to bools (default: the
+    load-balanced path of aaa/config.py:41-54).  Returns the geometry rows,
+    radii / tiles / valid, the colours when sh is given, and the sorted
+    indices of the Gaussians queued for the collective cull."""
+    flags = dict(dict(ewa=True, new_aabb=True, near_clipping=False, tile_culling=True,
+                      complete=False, cooperative=True), **(flags or {}))
+    n = len(means)
+    use_sh = sh is not None
+    sh_c = _c(sh) if use_sh else None
+    K = sh_c.shape[1] if use_sh else 0
+    filt = _c(filters) if filters is not None else None
+    out = dict(centers=np.zeros((n, 2), np.float32), rects=np.zeros((n, 2), np.float32),
+               depths=np.zeros(n, np.float32), transforms=np.zeros((n, 4, 4), np.float32),
+               opacity=np.zeros(n, np.float32), radii=np.zeros(n, np.int32),
+               tiles=np.zeros(n, np.int32), valid=np.zeros(n, np.uint8))
+    rgb = np.zeros((n, 3), np.float32) if use_sh else None
+    clamped = np.zeros((n, 3), np.uint8) if use_sh else None
+    queued = np.full(max(n, 1), -1, np.int32)
+    size = np.zeros(1, np.int32)
+    lib().oracle_aaa_preprocess(
+        n, _c(means), _c(scales), _c(quats), _c(opacities), _ptr(sh_c), K, int(use_sh),
+        int(sh_degree), int(sort_order), _ptr(filt), _c(campos), _c(view), _c(proj),
+        int(width), int(height), float(tanfov[0]), float(tanfov[1]), float(principal[0]),
+        float(principal[1]), float(modifier), *[int(bool(flags[k])) for k in AAA_FLAGS],
+        out["centers"], out["rects"], out["depths"], out["transforms"], out["opacity"],
+        out["radii"], out["tiles"], _ptr(rgb), out["valid"], _ptr(clamped), queued, size)
+    out["valid"] = out["valid"].astype(bool)
+    if use_sh:
+        out["rgb"], out["clamped"] = rgb, clamped.astype(bool)
+    out["queued"] = np.sort(queued[:size[0]])
+    return out

@@ -27,8 +27,16 @@ channels (wide_*.npz); and the RaDe-GS path (rade_*.npz):
   rade/render.py:99-322               render (colour, depth, median, normals)
   rade/render.py:325-547              backward (warp-reduced atomics)
 
+And the AAA-Gaussians preprocessing (aaa_*.npz), cameras lowered by
+aaa/cameras.py:77-121 (prepare_cameras) and Gaussians run through
+  aaa/preprocess3d.py:17-245          preprocess_3d (adaptive 3D filter,
+                                      perspective-correct bounds, tile culling,
+                                      long-rectangle queue)
+with aaa/native_geometry.py's snippets (frustum depth, axis bounds, screen
+bounds) compiled by g++ against the host libm (atan2f, tanf, fmodf).
+
 Usage: python tests/golden/make_golden.py [/path/to/reference]
-       [--tile-modes-only | --wide-only | --rade-only]
+       [--tile-modes-only | --wide-only | --rade-only | --aaa-only]
 """
 
 from __future__ import annotations
@@ -57,7 +65,7 @@ def load_reference(ref_root: str):
     # Stub the packages so their __init__ files (which import the AAA stack)
     # are not executed; submodules load from the checkout.
     for pkg in ("dsl_splat", "dsl_splat.gs3d", "dsl_splat.splatting", "dsl_splat.primitives",
-                "dsl_splat.runtime", "dsl_splat.rade"):
+                "dsl_splat.runtime", "dsl_splat.rade", "dsl_splat.aaa"):
         mod = types.ModuleType(pkg)
         parts = pkg.split(".")[1:]
         mod.__path__ = [os.path.join(pkg_root, *parts)]
@@ -383,6 +391,107 @@ def rade_scenes(base: dict) -> dict:
     return out
 
 
+# preprocess_3d's switches, in its argument order (aaa/preprocess3d.py:39-44);
+# aaa/preprocess.py:320-321 sets cooperative = load_balancing and tile
+# culling, complete = eval_3D and not cooperative.
+AAA_FLAGS = ("ewa", "new_aabb", "near_clipping", "tile_culling", "complete", "cooperative")
+
+
+def aaa_case(name, scene: dict, flags: dict, use_sh: bool, with_filter: bool) -> dict:
+    """One view through aaa/preprocess3d.py:17-245 (sort order PTD_MAX = 3, the
+    default of aaa/config.py:47)."""
+    cams = importlib.import_module("dsl_splat.aaa.cameras")
+    pre = importlib.import_module("dsl_splat.aaa.preprocess3d")
+    W, H = scene["width"], scene["height"]
+    means = scene["means"].astype(np.float32)
+    n = len(means)
+    quats = F.normalize(torch.from_numpy(scene["quats"].astype(np.float32)), dim=-1).numpy()
+    scales = scene["scales"].astype(np.float32)
+    opac = scene["opacities"].astype(np.float32)
+    deg = scene["sh_degree"] if use_sh else 0
+    sh = scene["sh"].astype(np.float32) if use_sh else np.zeros((n, 0, 3), np.float32)
+    filters = scene["filters"].astype(np.float32) if with_filter else np.zeros(0, np.float32)
+    view = torch.from_numpy(scene["viewmat"].astype(np.float32))
+    K = torch.from_numpy(scene["K"].astype(np.float32))
+    batch = cams.prepare_cameras(view[None, None], K[None, None], W, H, 0.01, 1e10)
+    fx, fy, cx, cy = batch.intrinsics[0][0]
+    tanx, tany = W / (2 * fx), H / (2 * fy)
+    v = batch.transposed_views[0, 0].numpy().copy()
+    proj = batch.projection[0, 0].numpy().copy()
+    campos = batch.centers[0, 0].numpy().astype(np.float32).copy()
+    wp = sys.modules["warp"]
+    centers = np.zeros((n, 2), np.float32)
+    rects = np.zeros((n, 2), np.float32)
+    depths = np.zeros(n, np.float32)
+    transforms = np.zeros((n, 4, 4), np.float32)
+    eff = np.zeros(n, np.float32)
+    radii = np.zeros(n, np.int32)
+    tiles = np.zeros(n, np.int32)
+    rgb = np.zeros((n if use_sh else 0, 3), np.float32)
+    valid = np.zeros(n, np.bool_)
+    clamped = np.zeros((n if use_sh else 0, 3), np.bool_)
+    queued = np.full(n, -1, np.int32)
+    queue_size = np.zeros(1, np.int32)
+    t0 = time.time()
+    ws.launch(pre.preprocess_3d, n, [
+        A(means, wp.vec3), A(scales, wp.vec3), A(quats, wp.vec4), A(opac),
+        A(sh, wp.vec3), use_sh, deg, 3, A(filters), with_filter,
+        A(campos[None], wp.vec3), A(v), A(proj), W, H,
+        np.float32(tanx), np.float32(tany), np.float32(cx), np.float32(cy), np.float32(1.0),
+        *[bool(flags[k]) for k in AAA_FLAGS],
+        A(centers, wp.vec2), A(rects, wp.vec2), A(depths), A(transforms, wp.mat44), A(eff),
+        A(radii), A(tiles), A(rgb, wp.vec3), A(valid), A(clamped), A(queued), A(queue_size)])
+    q = np.sort(queued[:queue_size[0]])
+    print(f"aaa_{name}: n={n} visible={int((radii > 0).sum())} queued={len(q)} "
+          f"valid={int(valid.sum())} in {time.time() - t0:.1f}s")
+    return dict(width=W, height=H, sh_degree=deg, use_sh=use_sh, has_filter=with_filter,
+                means=means, quats=quats, scales=scales, opacities=opac, sh=sh,
+                filters=filters, view=v, proj=proj, campos=campos,
+                tanfov=np.array([tanx, tany], np.float32),
+                principal=np.array([cx, cy], np.float32),
+                flags=np.array([flags[k] for k in AAA_FLAGS], np.bool_),
+                centers=centers, rects=rects, depths=depths, transforms=transforms,
+                opacity=eff, radii=radii, tiles=tiles, rgb=rgb, valid=valid,
+                clamped=clamped, queued=q)
+
+
+def aaa_scenes():
+    """Seeded views with small, long (more than 32 tiles, queued) and culled
+    Gaussians on a 128x96 image (8x6 tiles)."""
+    from dsl_splat_b200.scenes import intrinsics, look_at
+    g = torch.Generator().manual_seed(4242)
+    n = 320
+    means = (torch.rand(n, 3, generator=g) * 2 - 1) * torch.tensor([2.0, 1.5, 1.5])
+    means[:, 2] += 5.0
+    means[:16, 2] = -1.0 - torch.rand(16, generator=g)          # behind the camera
+    means[16:32, 0] += 14.0                                      # off screen
+    means[32:40, 2] = 0.05 + 0.1 * torch.rand(8, generator=g)    # near plane
+    scales = torch.exp(torch.randn(n, 3, generator=g) * 0.5 - 2.6)
+    scales[40:56] = torch.exp(torch.randn(16, 3, generator=g) * 0.3 - 0.2)  # long rects
+    scales[56:64] = torch.tensor([1e-4, 1e-4, 1e-4])             # sub-pixel
+    opac = torch.sigmoid(torch.randn(n, generator=g) + 1.0)
+    opac[64:72] = 0.002                                          # below 1/255
+    sh = torch.empty(n, 16, 3)
+    sh[:, 0] = torch.rand(n, 3, generator=g) * 2 - 0.5
+    sh[:, 1:] = torch.randn(n, 15, 3, generator=g) * 0.2
+    base = dict(width=128, height=96, sh_degree=3, means=means.numpy(), scales=scales.numpy(),
+                quats=torch.randn(n, 4, generator=g).numpy(), opacities=opac.numpy(),
+                sh=sh.numpy(), filters=(torch.rand(n, generator=g) * 0.02).numpy(),
+                viewmat=look_at(torch.tensor([0.6, -0.4, -1.0]),
+                                torch.tensor([0.0, 0.0, 5.0])).numpy(),
+                K=intrinsics(110.0, 104.0, 63.0, 49.5).numpy())
+    coop = dict(ewa=True, new_aabb=True, near_clipping=False, tile_culling=True,
+                complete=False, cooperative=True)
+    return [
+        ("coop", base, coop, False, False),                       # aaa.rasterize defaults
+        ("coop_sh3_filter", base, coop, True, True),
+        ("complete", base, dict(coop, complete=True, cooperative=False), True, False),
+        ("screen_bounds", base, dict(coop, ewa=False, new_aabb=False, near_clipping=True,
+                                     complete=True, cooperative=False), False, True),
+        ("noculling", base, dict(coop, tile_culling=False, cooperative=False), False, False),
+    ]
+
+
 def tile_mode_case(ref, name, scene: dict) -> dict:
     """Projection tile counts and binning for tile_mode snugbox and accutile
     (gs3d/projection.py:150-162, splatting/intersections.py:45-218,
@@ -518,7 +627,8 @@ def main():
     ref_root = args[0] if args else "/root/reference"
     ref = load_reference(ref_root)
     base = scenes()
-    only = {a for a in sys.argv[1:] if a in ("--tile-modes-only", "--wide-only", "--rade-only")}
+    only = {a for a in sys.argv[1:]
+            if a in ("--tile-modes-only", "--wide-only", "--rade-only", "--aaa-only")}
     if not only:
         for i, (name, scene) in enumerate(base.items()):
             data = golden_case(ref, name, scene, seed=100 + i)
@@ -531,6 +641,10 @@ def main():
         for name, ks, extra in (("c1_sh3", 0.0, 4), ("dense_sh1", 0.3, 0), ("flat_sh1", 0.1, 5)):
             data = rade_case(ref, name, rade_scenes(base)[name], 500, ks, extra)
             np.savez_compressed(os.path.join(HERE, f"rade_{name}.npz"), **data)
+    if not only or "--aaa-only" in only:
+        for name, scene, flags, use_sh, with_filter in aaa_scenes():
+            data = aaa_case(name, scene, flags, use_sh, with_filter)
+            np.savez_compressed(os.path.join(HERE, f"aaa_{name}.npz"), **data)
     if only and "--tile-modes-only" not in only:
         return
     for name, scene in tile_mode_scenes(base).items():

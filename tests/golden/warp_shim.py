@@ -172,7 +172,16 @@ class Mat:
         self.m[idx[0]][idx[1]] = _wp_f32(value)
 
     def __mul__(self, o):
-        """Matrix-vector product, each row summed left to right."""
+        """Matrix-vector or matrix-matrix product, each sum left to right."""
+        if isinstance(o, Mat):
+            out = matrix(type(self).rows, type(o).cols)()
+            for r, row in enumerate(self.m):
+                for c in range(type(o).cols):
+                    acc = row[0] * o.m[0][c]
+                    for k in range(1, len(row)):
+                        acc = acc + row[k] * o.m[k][c]
+                    out.m[r][c] = acc
+            return out
         if not isinstance(o, Vec):
             raise TypeError("matrix * non-vector")
         out = []
@@ -207,9 +216,14 @@ class Array:
     def _is_vec(self):
         return isinstance(self.dtype, type) and issubclass(self.dtype, Vec)
 
+    def _is_mat(self):
+        return isinstance(self.dtype, type) and issubclass(self.dtype, Mat)
+
     def __getitem__(self, idx):
         if self._is_vec():
             return self.dtype(*self.data[idx])
+        if self._is_mat():
+            return self.dtype(*self.data[idx].ravel())
         v = self.data[idx]
         if self.data.dtype == np.float32:
             return _wp_f32(v)
@@ -222,6 +236,8 @@ class Array:
     def __setitem__(self, idx, value):
         if self._is_vec():
             self.data[idx] = [float(a) for a in value.v]
+        elif self._is_mat():
+            self.data[idx] = [[float(a) for a in row] for row in value.m]
         else:
             self.data[idx] = value
 
@@ -319,26 +335,56 @@ _NATIVE_HEADER = r"""
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <type_traits>
 namespace wp {
 template <int N, typename T> struct vec_t {
   T c[N];
   vec_t() { for (int i = 0; i < N; ++i) c[i] = T(0); }
-  template <typename... A> vec_t(A... a) : c{static_cast<T>(a)...} {}
+  explicit vec_t(T s) { for (int i = 0; i < N; ++i) c[i] = s; }  // Warp fills
+  template <typename... A, typename = std::enable_if_t<(sizeof...(A) >= 2)>>
+  vec_t(A... a) : c{static_cast<T>(a)...} {}
   T& operator[](int i) { return c[i]; }
   const T& operator[](int i) const { return c[i]; }
 };
+template <int N, typename T> vec_t<N, T> operator+(vec_t<N, T> a, const vec_t<N, T>& b) {
+  for (int i = 0; i < N; ++i) a[i] = a[i] + b[i];
+  return a;
+}
+template <int N, typename T> vec_t<N, T> operator-(vec_t<N, T> a, const vec_t<N, T>& b) {
+  for (int i = 0; i < N; ++i) a[i] = a[i] - b[i];
+  return a;
+}
+template <int N, typename T> vec_t<N, T> operator*(vec_t<N, T> a, T s) {
+  for (int i = 0; i < N; ++i) a[i] = a[i] * s;
+  return a;
+}
+template <int N, typename T> vec_t<N, T> operator*(T s, vec_t<N, T> a) {
+  for (int i = 0; i < N; ++i) a[i] = s * a[i];
+  return a;
+}
+template <int N, typename T> vec_t<N, T> cw_mul(vec_t<N, T> a, const vec_t<N, T>& b) {
+  for (int i = 0; i < N; ++i) a[i] = a[i] * b[i];
+  return a;
+}
 template <int R, int C, typename T> struct mat_t {
   T data[R][C];
   mat_t() { for (int i = 0; i < R * C; ++i) data[i / C][i % C] = T(0); }
-  template <typename... A> mat_t(A... a) {
+  template <typename... A, typename = std::enable_if_t<(sizeof...(A) >= 2)>>
+  mat_t(A... a) {
     const T v[] = {static_cast<T>(a)...};
     for (int i = 0; i < R * C; ++i) data[i / C][i % C] = v[i];
+  }
+  vec_t<C, T> get_row(int r) const {
+    vec_t<C, T> out;
+    for (int i = 0; i < C; ++i) out[i] = data[r][i];
+    return out;
   }
 };
 }
 static inline float __fmul_rn(float a, float b) { return a * b; }
 static inline float __fadd_rn(float a, float b) { return a + b; }
 static inline float __fsub_rn(float a, float b) { return a - b; }
+static inline float __frcp_rn(float a) { return 1.0f / a; }  // correctly rounded
 static inline uint32_t __float_as_uint(float v) { uint32_t u; std::memcpy(&u, &v, 4); return u; }
 static inline float norm3df(float a, float b, float c) { return std::sqrt(a * a + b * b + c * c); }
 """
@@ -351,6 +397,10 @@ def _c_type(ann):
         return "float", 1, "scalar"
     if ann is np.uint32 or ann is uint32:
         return "uint32_t", 1, "u32"
+    if ann is bool:
+        return "bool", 1, "bool"
+    if ann is int:
+        return "int", 1, "int"
     if isinstance(ann, type) and issubclass(ann, Vec):
         return f"wp::vec_t<{ann.length},float>", ann.length, "vec"
     if isinstance(ann, type) and issubclass(ann, Mat):
@@ -372,6 +422,14 @@ def _compile_native(name, snippet, params, ret):
             unpack.append(f"const float {pname} = a{i}[0];")
         elif kind == "vec":
             unpack.append(f"{ctype} {pname}; for (int k = 0; k < {n}; ++k) {pname}[k] = a{i}[k];")
+        elif kind == "mat":
+            cols = ann.cols
+            unpack.append(f"{ctype} {pname}; for (int k = 0; k < {n}; ++k) "
+                          f"{pname}.data[k / {cols}][k % {cols}] = a{i}[k];")
+        elif kind == "bool":
+            unpack.append(f"const bool {pname} = a{i}[0] != 0.0f;")
+        elif kind == "int":
+            unpack.append(f"const int {pname} = static_cast<int>(a{i}[0]);")
         else:
             raise TypeError(kind)
     rtype, rn, rkind = _c_type(ret)
@@ -420,6 +478,9 @@ def func_native(snippet, adj_snippet=None):
                 arr = (ctypes.c_float * max(1, _c_type(ann)[1]))()
                 if isinstance(v, Vec):
                     for k, a in enumerate(v.v):
+                        arr[k] = float(a)
+                elif isinstance(v, Mat):
+                    for k, a in enumerate(x for row in v.m for x in row):
                         arr[k] = float(a)
                 else:
                     arr[0] = float(v)
@@ -674,6 +735,10 @@ def length_sq(a):
     return dot(a, a)
 
 
+def cw_mul(a, b):
+    return a._new([x * y for x, y in zip(a.v, b.v)])
+
+
 def normalize(a):
     """Warp's normalize: a / length(a) per component, zero when length is 0."""
     n = length(a)
@@ -821,7 +886,7 @@ def make_module() -> types.ModuleType:
                  "array3d", "tid", "static", "min", "max", "clamp", "sqrt", "ceil", "floor",
                  "abs", "log", "exp", "isfinite", "dot", "length", "transpose", "determinant",
                  "inverse", "atomic_add", "uint64", "uint32", "float64", "grad", "constant",
-                 "adjoint", "launch", "normalize", "outer", "length_sq"):
+                 "adjoint", "launch", "normalize", "outer", "length_sq", "cw_mul"):
         setattr(m, name, getattr(this, name))
     m.float32 = F32
     m.int32 = np.int32

@@ -1,0 +1,84 @@
+"""The AAA-Gaussians preprocessing oracle (oracle/aaa_oracle.cpp) against
+golden vectors made by executing dsl_splat's own aaa/preprocess3d.py:17-245
+(tests/golden/make_golden.py --aaa-only).
+
+Five flag sets cover every branch of preprocess_3d: the load-balanced
+defaults (aaa/config.py:41-54) with and without SH colours and a stored 3D
+filter, the complete path with serial tile culling, the screen-space
+quadric bounds with near clipping and no EWA compensation, and no tile
+culling.  Integers (radii, tile counts, valid flags, the queue of long
+rectangles) are bit-exact; so is every float, because the restatement keeps
+the kernel's rounding order and both sides share libm and the oracle's log.
+"""
+
+import glob
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CASES = sorted(glob.glob(os.path.join(HERE, "golden", "aaa_*.npz")))
+
+
+def _run(d, **overrides):
+    flags = dict(zip(O.AAA_FLAGS, d["flags"].tolist()))
+    args = dict(sh=d["sh"] if bool(d["use_sh"]) else None, sh_degree=int(d["sh_degree"]),
+                filters=d["filters"] if bool(d["has_filter"]) else None, flags=flags)
+    args.update(overrides)
+    return O.aaa_preprocess(d["means"], d["quats"], d["scales"], d["opacities"], d["view"],
+                            d["proj"], d["campos"], int(d["width"]), int(d["height"]),
+                            d["tanfov"], d["principal"], **args)
+
+
+def test_cases_present():
+    names = {os.path.basename(c)[4:-4] for c in CASES}
+    assert names == {"coop", "coop_sh3_filter", "complete", "screen_bounds", "noculling"}
+
+
+@pytest.mark.parametrize("path", CASES, ids=lambda p: os.path.basename(p)[:-4])
+def test_oracle_matches_reference_kernel(path):
+    d = np.load(path)
+    out = _run(d)
+    for key in ("radii", "tiles", "valid", "queued"):
+        np.testing.assert_array_equal(out[key], d[key], err_msg=key)
+    visible = d["radii"] > 0
+    assert visible.any()
+    for key in ("centers", "rects", "depths", "transforms", "opacity"):
+        np.testing.assert_array_equal(out[key][visible], d[key][visible], err_msg=key)
+    if bool(d["use_sh"]):
+        np.testing.assert_array_equal(out["rgb"][visible], d["rgb"][visible])
+        np.testing.assert_array_equal(out["clamped"][visible], d["clamped"][visible])
+
+
+def test_goldens_cover_the_branches():
+    load = {os.path.basename(c)[4:-4]: np.load(c) for c in CASES}
+    coop, complete = load["coop"], load["complete"]
+    # long rectangles are queued on the load-balanced path only
+    assert len(coop["queued"]) > 0 and len(complete["queued"]) == 0
+    assert np.all(coop["radii"][coop["queued"]] > 0)
+    # culled groups of the scene: behind the camera, off screen, below 1/255
+    for d in load.values():
+        assert not d["radii"][:32].any() and not d["radii"][64:72].any()
+    # valid is only set on the complete or load-balanced paths
+    assert not load["noculling"]["valid"].any() and coop["valid"].sum() == (coop["radii"] > 0).sum()
+    # PTD_MAX depths are camera distances on the valid rows
+    v = coop["valid"]
+    dist = np.linalg.norm(coop["means"][v] - coop["campos"], axis=1)
+    np.testing.assert_allclose(coop["depths"][v], dist, rtol=1e-6)
+    sh = load["coop_sh3_filter"]
+    assert sh["clamped"][sh["valid"]].any() and not sh["clamped"][sh["valid"]].all()
+
+
+def test_oracle_is_sensitive_to_its_inputs():
+    """A planted change in the oracle's inputs moves its outputs (the
+    comparison above is not vacuous)."""
+    d = np.load(os.path.join(HERE, "golden", "aaa_coop.npz"))
+    moved = dict(d)
+    moved["opacities"] = d["opacities"] * np.float32(0.999)
+    out = _run(moved)
+    assert not np.array_equal(out["opacity"], d["opacity"])
+    out = _run(d, flags=dict(zip(O.AAA_FLAGS, d["flags"].tolist()), ewa=False))
+    assert not np.array_equal(out["opacity"], d["opacity"])
