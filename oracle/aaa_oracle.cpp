@@ -492,4 +492,43 @@ void oracle_aaa_preprocess(int n, const float* means, const float* scales, const
   }
 }
 
+// aaa/cooperative_culling.py:152-192 cull_remainder_3d: each queued
+// Gaussian's tiles past the first 32 (the rectangle is recomputed from the
+// stored centre and extent, :39-48) are added to its count; a Gaussian left
+// with no tile is rejected (radius 0, not valid).
+void oracle_aaa_cull_remainder(const int* queued, int queue_size, const float* centers,
+                               const float* rects, const float* transforms,
+                               const float* opacity, int width, int height, int* radii,
+                               int* tiles, unsigned char* valid) {
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int slot = 0; slot < queue_size; ++slot) {
+    const int i = queued[slot];
+    const float* c = centers + 2 * i;
+    const float* e = rects + 2 * i;
+    const int xmin = clampi(to_int(std::floor((c[0] - e[0]) / 16.0f)), 0, gx);
+    const int ymin = clampi(to_int(std::floor((c[1] - e[1]) / 16.0f)), 0, gy);
+    const int xmax = clampi(to_int(std::ceil((c[0] + e[0]) / 16.0f)), 0, gx);
+    const int ymax = clampi(to_int(std::ceil((c[1] + e[1]) / 16.0f)), 0, gy);
+    const int rect_width = xmax - xmin, rect_count = rect_width * (ymax - ymin);
+    M4 g;
+    for (int r = 0; r < 4; ++r)
+      for (int k = 0; k < 4; ++k) g.m[r][k] = transforms[16 * i + 4 * r + k];
+    const float threshold = oracle_logf(opacity[i] / (1.0f / 255.0f));
+    int count = 0;
+    for (int t = 32; t < rect_count; ++t) {
+      const int x = xmin + t % rect_width, y = ymin + t / rect_width;
+      const float lo[2] = {static_cast<float>(x * 16), static_cast<float>(y * 16)};
+      const float hi[2] = {static_cast<float>(x * 16 + 15), static_cast<float>(y * 16 + 15)};
+      if (frustum_depth(g, lo[0], lo[1], hi[0] - lo[0], hi[1] - lo[1], false).half_distance <= threshold)
+        ++count;
+    }
+    tiles[i] += count;
+    if (tiles[i] == 0) {
+      radii[i] = 0;
+      valid[i] = 0;
+    }
+  }
+}
+
 }  // extern "C"

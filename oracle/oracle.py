@@ -95,6 +95,9 @@ def lib():
             _f32p, _int, _int, _flt, _flt, _flt, _flt, _flt, _int, _int, _int, _int, _int, _int,
             _f32p, _f32p, _f32p, _f32p, _f32p, _i32p, _i32p, _vp, _u8p, _vp, _i32p, _i32p]
         L.oracle_aaa_preprocess.restype = None
+        L.oracle_aaa_cull_remainder.argtypes = [
+            _i32p, _int, _f32p, _f32p, _f32p, _f32p, _int, _int, _i32p, _i32p, _u8p]
+        L.oracle_aaa_cull_remainder.restype = None
         L.oracle_num_threads.restype = _int
         L.oracle_set_num_threads.argtypes = [_int]
         _lib = L
@@ -454,3 +457,15 @@ def aaa_preprocess(means, quats, scales, opacities, view, proj, campos, width, h
         out["rgb"], out["clamped"] = rgb, clamped.astype(bool)
     out["queued"] = np.sort(queued[:size[0]])
     return out
+
+
+def aaa_cull_remainder(pre: dict, width: int, height: int) -> dict:
+    """aaa/cooperative_culling.py:152-192 on aaa_preprocess's output: the
+    final radii / tiles / valid of the load-balanced path (new arrays)."""
+    radii, tiles = pre["radii"].copy(), pre["tiles"].copy()
+    valid = pre["valid"].astype(np.uint8)
+    q = _c(pre["queued"], np.int32)
+    lib().oracle_aaa_cull_remainder(
+        q, len(q), _c(pre["centers"]), _c(pre["rects"]), _c(pre["transforms"]),
+        _c(pre["opacity"]), int(width), int(height), radii, tiles, valid)
+    return dict(radii=radii, tiles=tiles, valid=valid.astype(bool))

@@ -32,6 +32,9 @@ aaa/cameras.py:77-121 (prepare_cameras) and Gaussians run through
   aaa/preprocess3d.py:17-245          preprocess_3d (adaptive 3D filter,
                                       perspective-correct bounds, tile culling,
                                       long-rectangle queue)
+  aaa/cooperative_culling.py:152-192  cull_remainder_3d (the queued rectangles'
+                                      tiles past the first 32, 32-lane tile_sum;
+                                      final_* keys of the load-balanced cases)
 with aaa/native_geometry.py's snippets (frustum depth, axis bounds, screen
 bounds) compiled by g++ against the host libm (atan2f, tanf, fmodf).
 
@@ -442,8 +445,18 @@ def aaa_case(name, scene: dict, flags: dict, use_sh: bool, with_filter: bool) ->
         A(centers, wp.vec2), A(rects, wp.vec2), A(depths), A(transforms, wp.mat44), A(eff),
         A(radii), A(tiles), A(rgb, wp.vec3), A(valid), A(clamped), A(queued), A(queue_size)])
     q = np.sort(queued[:queue_size[0]])
+    final = {}
+    if flags["cooperative"]:
+        # aaa/preprocess.py:453-476: min(n, 1024) blocks of 32 lanes
+        cull = importlib.import_module("dsl_splat.aaa.cooperative_culling")
+        f_radii, f_tiles, f_valid = radii.copy(), tiles.copy(), valid.copy()
+        ws.launch_tiled(cull.cull_remainder_3d, min(n, 1024), [
+            A(centers, wp.vec2), A(rects, wp.vec2), A(transforms, wp.mat44), A(eff), W, H,
+            min(n, 1024), A(f_radii), A(f_tiles), A(f_valid), A(queued), A(queue_size)], 32)
+        final = dict(final_radii=f_radii, final_tiles=f_tiles, final_valid=f_valid)
     print(f"aaa_{name}: n={n} visible={int((radii > 0).sum())} queued={len(q)} "
-          f"valid={int(valid.sum())} in {time.time() - t0:.1f}s")
+          f"valid={int(valid.sum())} final valid="
+          f"{int(final['final_valid'].sum()) if final else '-'} in {time.time() - t0:.1f}s")
     return dict(width=W, height=H, sh_degree=deg, use_sh=use_sh, has_filter=with_filter,
                 means=means, quats=quats, scales=scales, opacities=opac, sh=sh,
                 filters=filters, view=v, proj=proj, campos=campos,
@@ -452,7 +465,7 @@ def aaa_case(name, scene: dict, flags: dict, use_sh: bool, with_filter: bool) ->
                 flags=np.array([flags[k] for k in AAA_FLAGS], np.bool_),
                 centers=centers, rects=rects, depths=depths, transforms=transforms,
                 opacity=eff, radii=radii, tiles=tiles, rgb=rgb, valid=valid,
-                clamped=clamped, queued=q)
+                clamped=clamped, queued=q, **final)
 
 
 def aaa_scenes():

@@ -630,6 +630,46 @@ def tid():
     return _state.tid
 
 
+def tile(value):
+    """wp.tile of one value per lane: the lane's own value."""
+    return value
+
+
+def tile_sum(value):
+    """wp.tile_sum over a 32-lane tile: the lanes' values summed in lane
+    order (exact for the integer counts it reduces here), as a 1-tile."""
+    values = _warp_exchange(value)
+    total = values[0]
+    for v in values[1:]:
+        total = total + v
+    return [total]
+
+
+def launch_tiled(kernel_obj: Kernel, dim: int, args, block_dim: int = 32):
+    """wp.launch_tiled: dim blocks of block_dim real threads, wp.tid() =
+    (block, lane)."""
+    errors = []
+
+    def worker(blk, index, lane):
+        _state.block, _state.tid, _state.lane = blk, (index, lane), lane
+        try:
+            kernel_obj(*args)
+        except BaseException as e:  # surface thread failures
+            errors.append(e)
+            blk.abort()
+
+    for index in range(dim):
+        blk = _Block(block_dim)
+        threads = [threading.Thread(target=worker, args=(blk, index, lane))
+                   for lane in range(block_dim)]
+        for th in threads:
+            th.start()
+        for th in threads:
+            th.join()
+        if errors:
+            raise errors[0]
+
+
 def launch(kernel_obj: Kernel, dim: int, args, block: int | None = None):
     """Run a kernel over dim threads; block-cooperative kernels as real blocks."""
     if block is None:
@@ -903,7 +943,8 @@ def make_module() -> types.ModuleType:
     m.ScopedStream = _unsupported
     m.utils = types.SimpleNamespace(array_scan=_unsupported, radix_sort_pairs=_unsupported)
     m.init = lambda: None
-    m.tile = m.tile_sum = m.tile_atomic_add = m.launch_tiled = _unsupported
+    m.tile, m.tile_sum, m.launch_tiled = tile, tile_sum, launch_tiled
+    m.tile_atomic_add = _unsupported
     m.from_torch = m.get_stream = m.stream_from_torch = _unsupported
     m.device_from_torch = m.dtype_from_torch = _unsupported
     m.config = types.SimpleNamespace()

@@ -1,5 +1,6 @@
 """The AAA-Gaussians preprocessing oracle (oracle/aaa_oracle.cpp) against
 golden vectors made by executing dsl_splat's own aaa/preprocess3d.py:17-245
+and, on the load-balanced cases, aaa/cooperative_culling.py:152-192
 (tests/golden/make_golden.py --aaa-only).
 
 Five flag sets cover every branch of preprocess_3d: the load-balanced
@@ -51,6 +52,10 @@ def test_oracle_matches_reference_kernel(path):
     if bool(d["use_sh"]):
         np.testing.assert_array_equal(out["rgb"][visible], d["rgb"][visible])
         np.testing.assert_array_equal(out["clamped"][visible], d["clamped"][visible])
+    if "final_radii" in d:
+        final = O.aaa_cull_remainder(out, int(d["width"]), int(d["height"]))
+        for key in ("radii", "tiles", "valid"):
+            np.testing.assert_array_equal(final[key], d["final_" + key], err_msg="final " + key)
 
 
 def test_goldens_cover_the_branches():
@@ -59,6 +64,12 @@ def test_goldens_cover_the_branches():
     # long rectangles are queued on the load-balanced path only
     assert len(coop["queued"]) > 0 and len(complete["queued"]) == 0
     assert np.all(coop["radii"][coop["queued"]] > 0)
+    # after the remainder cull the load-balanced counts are the complete
+    # path's serial counts, and only queued rows changed
+    np.testing.assert_array_equal(coop["final_tiles"], complete["tiles"])
+    rest = np.setdiff1d(np.arange(len(coop["radii"])), coop["queued"])
+    np.testing.assert_array_equal(coop["final_tiles"][rest], coop["tiles"][rest])
+    assert np.all(coop["final_tiles"][coop["queued"]] > coop["tiles"][coop["queued"]])
     # culled groups of the scene: behind the camera, off screen, below 1/255
     for d in load.values():
         assert not d["radii"][:32].any() and not d["radii"][64:72].any()
@@ -82,3 +93,17 @@ def test_oracle_is_sensitive_to_its_inputs():
     assert not np.array_equal(out["opacity"], d["opacity"])
     out = _run(d, flags=dict(zip(O.AAA_FLAGS, d["flags"].tolist()), ewa=False))
     assert not np.array_equal(out["opacity"], d["opacity"])
+
+
+def test_remainder_cull_rejects_a_rectangle_without_tiles():
+    """cull_remainder_3d's rejection branch (aaa/cooperative_culling.py:188-192),
+    which the golden scene does not reach: a queued Gaussian whose first 32
+    tiles counted none and whose threshold no tile meets loses its radius."""
+    d = np.load(os.path.join(HERE, "golden", "aaa_coop.npz"))
+    pre = _run(d)
+    i, other = int(pre["queued"][0]), int(pre["queued"][1])
+    pre["tiles"][i] = 0
+    pre["opacity"][i] = np.float32(1.0 / 255.0)  # threshold log(1) = 0
+    final = O.aaa_cull_remainder(pre, int(d["width"]), int(d["height"]))
+    assert final["radii"][i] == 0 and not final["valid"][i] and final["tiles"][i] == 0
+    assert final["radii"][other] == pre["radii"][other] and final["valid"][other]
