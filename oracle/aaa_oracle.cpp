@@ -17,6 +17,7 @@
 #include <cfloat>
 #include <climits>
 #include <cmath>
+#include <cstring>
 
 // the oracle's own natural logarithm (splat_oracle.cpp), shared with the
 // golden generator so that both round the opacity threshold alike
@@ -527,6 +528,59 @@ void oracle_aaa_cull_remainder(const int* queued, int queue_size, const float* c
     if (tiles[i] == 0) {
       radii[i] = 0;
       valid[i] = 0;
+    }
+  }
+}
+
+// aaa/binning_native.py:7-135 duplicate_aaa_default, restated serially.
+// The reference's warp visits its long rectangles one owner at a time and
+// ranks each 32-tile batch by ballot, so per Gaussian the output is: its
+// rectangle's tiles in row-major order -- the first 32 tested with the
+// sequential plane products, the rest with the fused ones -- a key for each
+// tile within the threshold, written from offsets[i-1] on and never past
+// offsets[i]; the rest of its range is padding (tile 0xffffffff, depth
+// FLT_MAX, id -1).  Key = tile id << 32 | bits(screen depth + 8).
+// offsets: inclusive scan of the visible Gaussians' tile counts.
+void oracle_aaa_duplicate(int n, const float* centers, const float* rects, const int* radii,
+                          const float* transforms, const float* opacity, const int* offsets,
+                          int width, int height, unsigned long long* keys, int* values,
+                          int num_keys) {
+  const int gx = (width + 15) / 16, gy = (height + 15) / 16;
+  auto key_of = [](unsigned tile, float depth) {
+    unsigned bits;
+    std::memcpy(&bits, &depth, 4);
+    return (static_cast<unsigned long long>(tile) << 32) | bits;
+  };
+#pragma omp parallel for schedule(dynamic, 16)
+  for (int i = 0; i < n; ++i) {
+    if (radii[i] <= 0) continue;
+    const float* c = centers + 2 * i;
+    const float* e = rects + 2 * i;
+    const int xmin = clampi(to_int(std::floor((c[0] - e[0]) / 16.0f)), 0, gx);
+    const int ymin = clampi(to_int(std::floor((c[1] - e[1]) / 16.0f)), 0, gy);
+    const int xmax = clampi(to_int(std::ceil((c[0] + e[0]) / 16.0f)), 0, gx);
+    const int ymax = clampi(to_int(std::ceil((c[1] + e[1]) / 16.0f)), 0, gy);
+    const int rect_width = xmax - xmin, count = rect_width * (ymax - ymin);
+    int pos = i ? offsets[i - 1] : 0;
+    const int stop = offsets[i];
+    M4 g;
+    for (int r = 0; r < 4; ++r)
+      for (int k = 0; k < 4; ++k) g.m[r][k] = transforms[16 * i + 4 * r + k];
+    const float threshold = oracle_logf(opacity[i] / (1.0f / 255.0f));
+    for (int t = 0; t < count; ++t) {
+      const int x = xmin + t % rect_width, y = ymin + t / rect_width;
+      const FrustumDepth f = frustum_depth(g, static_cast<float>(x * 16), static_cast<float>(y * 16),
+                                           15.0f, 15.0f, t < 32);
+      if (f.half_distance > threshold) continue;
+      if (pos < stop && pos < num_keys) {
+        keys[pos] = key_of(static_cast<unsigned>(y * gx + x), f.depth + 8.0f);
+        values[pos] = i;
+      }
+      ++pos;
+    }
+    for (int j = pos; j < stop && j < num_keys; ++j) {
+      keys[j] = key_of(0xffffffffu, FLT_MAX);
+      values[j] = -1;
     }
   }
 }

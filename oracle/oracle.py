@@ -98,6 +98,9 @@ def lib():
         L.oracle_aaa_cull_remainder.argtypes = [
             _i32p, _int, _f32p, _f32p, _f32p, _f32p, _int, _int, _i32p, _i32p, _u8p]
         L.oracle_aaa_cull_remainder.restype = None
+        L.oracle_aaa_duplicate.argtypes = [
+            _int, _f32p, _f32p, _i32p, _f32p, _f32p, _i32p, _int, _int, _u64p, _i32p, _int]
+        L.oracle_aaa_duplicate.restype = None
         L.oracle_num_threads.restype = _int
         L.oracle_set_num_threads.argtypes = [_int]
         _lib = L
@@ -469,3 +472,20 @@ def aaa_cull_remainder(pre: dict, width: int, height: int) -> dict:
         q, len(q), _c(pre["centers"]), _c(pre["rects"]), _c(pre["transforms"]),
         _c(pre["opacity"]), int(width), int(height), radii, tiles, valid)
     return dict(radii=radii, tiles=tiles, valid=valid.astype(bool))
+
+
+def aaa_duplicate(pre: dict, radii, tiles, width: int, height: int, offsets=None):
+    """aaa/binning_native.py:7-135 (aaa_oracle.cpp): keys and Gaussian ids of
+    every visible Gaussian's tiles.  offsets defaults to the inclusive scan of
+    the visible Gaussians' tile counts; returns (offsets, keys, values)."""
+    radii = _c(radii, np.int32)
+    if offsets is None:
+        offsets = np.cumsum(np.where(radii > 0, tiles, 0)).astype(np.int32)
+    offsets = _c(offsets, np.int32)
+    total = int(offsets[-1]) if len(offsets) else 0
+    keys = np.zeros(total, np.uint64)
+    values = np.full(total, -7, np.int32)
+    lib().oracle_aaa_duplicate(
+        len(radii), _c(pre["centers"]), _c(pre["rects"]), radii, _c(pre["transforms"]),
+        _c(pre["opacity"]), offsets, int(width), int(height), keys, values, total)
+    return offsets, keys, values

@@ -35,6 +35,10 @@ aaa/cameras.py:77-121 (prepare_cameras) and Gaussians run through
   aaa/cooperative_culling.py:152-192  cull_remainder_3d (the queued rectangles'
                                       tiles past the first 32, 32-lane tile_sum;
                                       final_* keys of the load-balanced cases)
+  aaa/binning_native.py:7-135         duplicate_aaa_default (the warp-cooperative
+                                      key emission, its snippet compiled with the
+                                      shim's 32-thread warp lanes; dup_* keys of
+                                      aaa_coop)
 with aaa/native_geometry.py's snippets (frustum depth, axis bounds, screen
 bounds) compiled by g++ against the host libm (atan2f, tanf, fmodf).
 
@@ -44,6 +48,7 @@ Usage: python tests/golden/make_golden.py [/path/to/reference]
 
 from __future__ import annotations
 
+import ctypes
 import importlib
 import os
 import sys
@@ -454,6 +459,10 @@ def aaa_case(name, scene: dict, flags: dict, use_sh: bool, with_filter: bool) ->
             A(centers, wp.vec2), A(rects, wp.vec2), A(transforms, wp.mat44), A(eff), W, H,
             min(n, 1024), A(f_radii), A(f_tiles), A(f_valid), A(queued), A(queue_size)], 32)
         final = dict(final_radii=f_radii, final_tiles=f_tiles, final_valid=f_valid)
+        if name == "coop":
+            final.update(aaa_duplicate(dict(final, centers=centers, rects=rects,
+                                            transforms=transforms, opacity=eff,
+                                            width=W, height=H)))
     print(f"aaa_{name}: n={n} visible={int((radii > 0).sum())} queued={len(q)} "
           f"valid={int(valid.sum())} final valid="
           f"{int(final['final_valid'].sum()) if final else '-'} in {time.time() - t0:.1f}s")
@@ -466,6 +475,53 @@ def aaa_case(name, scene: dict, flags: dict, use_sh: bool, with_filter: bool) ->
                 centers=centers, rects=rects, depths=depths, transforms=transforms,
                 opacity=eff, radii=radii, tiles=tiles, rgb=rgb, valid=valid,
                 clamped=clamped, queued=q, **final)
+
+
+_DUPLICATE_DRIVER = r"""
+static void duplicate_body(int i, wp::array_t<wp::vec_t<2, float>> centers,
+                           wp::array_t<wp::vec_t<2, float>> extents, wp::array_t<int> radii,
+                           wp::array_t<wp::mat_t<4, 4, float>> transforms,
+                           wp::array_t<float> opacity3d, wp::array_t<int> offsets, int width,
+                           int height, wp::array_t<uint64_t> keys, wp::array_t<int> values) {
+SNIPPET
+}
+extern "C" void run(int n, float* centers, float* extents, int* radii, float* transforms,
+                    float* opacity, int* offsets, int width, int height, uint64_t* keys,
+                    int* values, int nkeys) {
+  using V2 = wp::vec_t<2, float>;
+  using M4 = wp::mat_t<4, 4, float>;
+  wp::array_t<V2> c{reinterpret_cast<V2*>(centers), {n}}, e{reinterpret_cast<V2*>(extents), {n}};
+  wp::array_t<int> r{radii, {n}}, off{offsets, {n}}, v{values, {nkeys}};
+  wp::array_t<M4> t{reinterpret_cast<M4*>(transforms), {n}};
+  wp::array_t<float> o{opacity, {n}};
+  wp::array_t<uint64_t> k{keys, {nkeys}};
+  // aaa/binning_native.py:134-135: threads rounded up to whole warps
+  run_warps(((n + 31) / 32) * 32, [&](int i) { duplicate_body(i, c, e, r, t, o, off, width, height, k, v); });
+}
+"""
+
+
+def aaa_duplicate(d: dict) -> dict:
+    """aaa/binning_native.py:85-135 on a load-balanced case's final rows:
+    offsets are the inclusive scan of the visible Gaussians' tile counts."""
+    bn = importlib.import_module("dsl_splat.aaa.binning_native")
+    snippet = bn._duplicate_cooperative.__wp_snippet__
+    lib = ws.compile_warp_snippet(_DUPLICATE_DRIVER.replace("SNIPPET", snippet), "aaa_duplicate")
+    radii = d["final_radii"].astype(np.int32)
+    offsets = np.cumsum(np.where(radii > 0, d["final_tiles"], 0)).astype(np.int32)
+    total = int(offsets[-1])
+    keys = np.zeros(total, np.uint64)
+    values = np.full(total, -7, np.int32)
+    f32 = lambda a: np.ascontiguousarray(a, np.float32)
+    centers, rects, transforms, opacity = (f32(d[k]) for k in ("centers", "rects", "transforms",
+                                                                "opacity"))
+    ptr = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    lib.run.restype = None
+    lib.run(ctypes.c_int(len(radii)), ptr(centers), ptr(rects), ptr(radii), ptr(transforms),
+            ptr(opacity), ptr(offsets), ctypes.c_int(int(d["width"])),
+            ctypes.c_int(int(d["height"])), ptr(keys), ptr(values), ctypes.c_int(total))
+    assert (values != -7).all()
+    return dict(dup_offsets=offsets, dup_keys=keys, dup_values=values)
 
 
 def aaa_scenes():

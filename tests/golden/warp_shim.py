@@ -369,6 +369,7 @@ template <int N, typename T> vec_t<N, T> cw_mul(vec_t<N, T> a, const vec_t<N, T>
 template <int R, int C, typename T> struct mat_t {
   T data[R][C];
   mat_t() { for (int i = 0; i < R * C; ++i) data[i / C][i % C] = T(0); }
+  explicit mat_t(T s) { for (int i = 0; i < R * C; ++i) data[i / C][i % C] = s; }
   template <typename... A, typename = std::enable_if_t<(sizeof...(A) >= 2)>>
   mat_t(A... a) {
     const T v[] = {static_cast<T>(a)...};
@@ -388,6 +389,86 @@ static inline float __frcp_rn(float a) { return 1.0f / a; }  // correctly rounde
 static inline uint32_t __float_as_uint(float v) { uint32_t u; std::memcpy(&u, &v, 4); return u; }
 static inline float norm3df(float a, float b, float c) { return std::sqrt(a * a + b * b + c * c); }
 """
+
+# Warp-cooperative snippets (ballot / shuffle across the 32 lanes of a warp)
+# run as 32 std::threads per warp; every intrinsic is an exchange through
+# one slot per lane between two barriers, so all lanes must reach it, as on
+# the GPU.  Arrays are wp::array_t views with .data and .shape[0].
+WARP_LANES_HEADER = r"""
+#include <algorithm>
+#include <barrier>
+#include <thread>
+#include <vector>
+using std::max;
+using std::min;
+namespace wp {
+template <typename T> struct array_t {
+  T* data;
+  int shape[1];
+};
+}
+struct Dim3 { int x; };
+struct WarpLanes {
+  std::barrier<> bar{32};
+  uint64_t slot[32];
+};
+thread_local Dim3 threadIdx;
+thread_local WarpLanes* warp_lanes;
+static inline unsigned __ballot_sync(unsigned, bool predicate) {
+  warp_lanes->slot[threadIdx.x & 31] = predicate ? 1u : 0u;
+  warp_lanes->bar.arrive_and_wait();
+  unsigned out = 0;
+  for (int l = 0; l < 32; ++l) out |= static_cast<unsigned>(warp_lanes->slot[l]) << l;
+  warp_lanes->bar.arrive_and_wait();
+  return out;
+}
+template <typename T> static inline T __shfl_sync(unsigned, T value, int source) {
+  static_assert(sizeof(T) <= 8, "shuffle of a scalar");
+  uint64_t bits = 0;
+  std::memcpy(&bits, &value, sizeof(T));
+  warp_lanes->slot[threadIdx.x & 31] = bits;
+  warp_lanes->bar.arrive_and_wait();
+  bits = warp_lanes->slot[source & 31];
+  warp_lanes->bar.arrive_and_wait();
+  T out;
+  std::memcpy(&out, &bits, sizeof(T));
+  return out;
+}
+static inline int __popc(unsigned x) { return __builtin_popcount(x); }
+static inline int __ffs(int x) { return __builtin_ffs(x); }
+// run body(thread index) over `threads` lanes (a multiple of 32), one warp
+// of real threads at a time
+template <typename F> static void run_warps(int threads, F body) {
+  for (int start = 0; start < threads; start += 32) {
+    WarpLanes lanes;
+    std::vector<std::thread> pool;
+    for (int lane = 0; lane < 32; ++lane)
+      pool.emplace_back([&, lane] {
+        threadIdx.x = lane;
+        warp_lanes = &lanes;
+        body(start + lane);
+      });
+    for (auto& t : pool) t.join();
+  }
+}
+"""
+
+
+def compile_warp_snippet(source: str, name: str):
+    """g++ a C++ translation unit made of the float32 prelude, the warp-lane
+    prelude and `source`; returns the ctypes library."""
+    tmp = tempfile.mkdtemp(prefix="warp_shim_")
+    path = os.path.join(tmp, f"{name}.cpp")
+    with open(path, "w") as f:
+        f.write(_NATIVE_HEADER + WARP_LANES_HEADER + source)
+    so = os.path.join(tmp, f"{name}.so")
+    subprocess.run(["g++", "-O1", "-std=c++20", "-pthread", "-fPIC", "-shared",
+                    "-ffp-contract=off", "-march=x86-64-v3", "-Wno-unknown-pragmas", "-o", so,
+                    path], check=True)
+    lib = ctypes.CDLL(so)
+    _native_libs[name] = lib
+    return lib
+
 
 _C_TYPES = {}  # annotation -> (c type, n floats, kind)
 
@@ -465,7 +546,7 @@ def func_native(snippet, adj_snippet=None):
         if name in _BLOCK_NATIVES:
             return _BLOCK_NATIVES[name]
         hints = {k: v for k, v in fn.__annotations__.items()}
-        ret = hints.pop("return")
+        ret = hints.pop("return", None)  # None: a void snippet, not callable here
         params = list(hints.items())
         compiled = {}
 
@@ -496,6 +577,7 @@ def func_native(snippet, adj_snippet=None):
             return rtype(*[F32(x) for x in out])
 
         call.__name__ = name
+        call.__wp_snippet__ = snippet
         return call
     return deco
 

@@ -1,6 +1,7 @@
 """The AAA-Gaussians preprocessing oracle (oracle/aaa_oracle.cpp) against
 golden vectors made by executing dsl_splat's own aaa/preprocess3d.py:17-245
-and, on the load-balanced cases, aaa/cooperative_culling.py:152-192
+and, on the load-balanced cases, aaa/cooperative_culling.py:152-192 and
+(aaa_coop) the key emission aaa/binning_native.py:7-135
 (tests/golden/make_golden.py --aaa-only).
 
 Five flag sets cover every branch of preprocess_3d: the load-balanced
@@ -56,6 +57,12 @@ def test_oracle_matches_reference_kernel(path):
         final = O.aaa_cull_remainder(out, int(d["width"]), int(d["height"]))
         for key in ("radii", "tiles", "valid"):
             np.testing.assert_array_equal(final[key], d["final_" + key], err_msg="final " + key)
+    if "dup_keys" in d:
+        offsets, keys, values = O.aaa_duplicate(out, final["radii"], final["tiles"],
+                                                int(d["width"]), int(d["height"]))
+        np.testing.assert_array_equal(offsets, d["dup_offsets"])
+        np.testing.assert_array_equal(keys, d["dup_keys"])
+        np.testing.assert_array_equal(values, d["dup_values"])
 
 
 def test_goldens_cover_the_branches():
@@ -107,3 +114,22 @@ def test_remainder_cull_rejects_a_rectangle_without_tiles():
     final = O.aaa_cull_remainder(pre, int(d["width"]), int(d["height"]))
     assert final["radii"][i] == 0 and not final["valid"][i] and final["tiles"][i] == 0
     assert final["radii"][other] == pre["radii"][other] and final["valid"][other]
+
+
+def test_duplicate_pads_a_short_range():
+    """The emission's padding (aaa/binning_native.py:76-81), which the golden
+    scene does not reach: a Gaussian given more key slots than it has tiles
+    fills the rest with tile 0xffffffff, depth FLT_MAX and id -1, and the
+    other Gaussians' keys only shift."""
+    d = np.load(os.path.join(HERE, "golden", "aaa_coop.npz"))
+    pre = _run(d)
+    radii, tiles = d["final_radii"], d["final_tiles"].copy()
+    i = int(np.flatnonzero(radii > 0)[3])
+    tiles[i] += 2
+    offsets, keys, values = O.aaa_duplicate(pre, radii, tiles, int(d["width"]), int(d["height"]))
+    pad = keys[offsets[i] - 2:offsets[i]]
+    assert np.all(values[offsets[i] - 2:offsets[i]] == -1)
+    assert np.all(pad >> np.uint64(32) == np.uint64(0xffffffff))
+    assert np.all((pad & np.uint64(0xffffffff)) == np.uint64(0x7f7fffff))
+    real = values >= 0
+    np.testing.assert_array_equal(keys[real], d["dup_keys"])
