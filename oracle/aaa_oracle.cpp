@@ -585,4 +585,130 @@ void oracle_aaa_duplicate(int n, const float* centers, const float* rects, const
   }
 }
 
+// aaa/backward_preprocess.py:130-268 preprocess_adjoint: the reference's
+// analytic adjoint of the preprocessing (not exact AD: the filter variance is
+// recomputed from |view depth| / focal_x and held fixed, the 3D filter and
+// scale modifier get no gradient, and the mean gradient is the transform's
+// translation column plus the EWA compensation's direction term).
+//   up_transforms: (n, 4, 4) dL/d(Gaussian-to-screen), the layout the
+//   forward writes; up_opacity: dL/d(effective opacity).  Rows with radius 0
+//   get zero geometry gradients and pass the opacity gradient through.
+void oracle_aaa_preprocess_backward(int n, const float* means, const float* scales,
+                                    const float* quats, const float* opacities, const int* radii,
+                                    const float* view, const float* proj, const float* campos,
+                                    int width, int height, float focal_x, int ewa,
+                                    const float* up_transforms, const float* up_opacity,
+                                    float* grad_opacity, float* grad_means, float* grad_scales,
+                                    float* grad_quats) {
+  const M4 V = load_transposed(view), P = load_transposed(proj);
+  const float W = static_cast<float>(width), H = static_cast<float>(height);
+  float viewport[4][4] = {{W / 2.0f, 0.0f, 0.0f, W / 2.0f - 0.5f},
+                          {0.0f, H / 2.0f, 0.0f, H / 2.0f - 0.5f},
+                          {0.0f, 0.0f, 1.0f, 0.0f},
+                          {0.0f, 0.0f, 0.0f, 1.0f}};
+  // Warp's 4x4 product, sums left to right
+  auto mul4 = [](const float a[4][4], const float b[4][4], float out[4][4]) {
+    for (int r = 0; r < 4; ++r)
+      for (int c = 0; c < 4; ++c) {
+        float acc = a[r][0] * b[0][c];
+        for (int k = 1; k < 4; ++k) acc = acc + a[r][k] * b[k][c];
+        out[r][c] = acc;
+      }
+  };
+  float world_to_screen[4][4];
+  mul4(viewport, P.m, world_to_screen);
+  float screen_t[4][4];
+  for (int r = 0; r < 4; ++r)
+    for (int c = 0; c < 4; ++c) screen_t[r][c] = world_to_screen[c][r];
+  const float root_03 = std::sqrt(0.3f);
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < n; ++i) {
+    grad_opacity[i] = up_opacity[i];
+    float* gm = grad_means + 3 * i;
+    float* gs = grad_scales + 3 * i;
+    float* gq = grad_quats + 4 * i;
+    if (radii[i] <= 0) {
+      for (int k = 0; k < 3; ++k) gm[k] = gs[k] = 0.0f;
+      for (int k = 0; k < 4; ++k) gq[k] = 0.0f;
+      continue;
+    }
+    const float* mean = means + 3 * i;
+    const float view_z = ((V.m[2][0] * mean[0] + V.m[2][1] * mean[1]) + V.m[2][2] * mean[2]) + V.m[2][3];
+    const float filter_scale = std::fabs(view_z) / focal_x * root_03;
+    const float variance = filter_scale * filter_scale;
+    const float* scale = scales + 3 * i;
+    float squared[3], dil_sq[3], dilated[3];
+    for (int k = 0; k < 3; ++k) {
+      squared[k] = scale[k] * scale[k];
+      dil_sq[k] = squared[k] + variance;
+      dilated[k] = std::sqrt(dil_sq[k]);
+    }
+    // quaternion rotation with rows = GLM columns, the plain expression order
+    const float* q = quats + 4 * i;
+    const float qr = q[0], qx = q[1], qy = q[2], qz = q[3];
+    const float R[3][3] = {
+        {1.0f - 2.0f * (qy * qy + qz * qz), 2.0f * (qx * qy + qr * qz), 2.0f * (qx * qz - qr * qy)},
+        {2.0f * (qx * qy - qr * qz), 1.0f - 2.0f * (qx * qx + qz * qz), 2.0f * (qy * qz + qr * qx)},
+        {2.0f * (qx * qz + qr * qy), 2.0f * (qy * qz - qr * qx), 1.0f - 2.0f * (qx * qx + qy * qy)}};
+    // world_grad = transpose(world_to_screen) * transpose(dL/dg2s)
+    float up_t[4][4], world_grad[4][4];
+    for (int r = 0; r < 4; ++r)
+      for (int c = 0; c < 4; ++c) up_t[r][c] = up_transforms[16 * i + 4 * c + r];
+    mul4(screen_t, up_t, world_grad);
+    float columns[3][3];
+    for (int r = 0; r < 3; ++r)
+      for (int c = 0; c < 3; ++c) columns[r][c] = world_grad[c][r];
+    float mean_grad[3] = {world_grad[0][3], world_grad[1][3], world_grad[2][3]};
+    float comp_scale[3] = {0.0f, 0.0f, 0.0f}, comp_dir[3] = {0.0f, 0.0f, 0.0f};
+    float direction[3] = {0.0f, 0.0f, 0.0f};
+    if (ewa) {
+      const float ray[3] = {mean[0] - campos[0], mean[1] - campos[1], mean[2] - campos[2]};
+      const float len = std::sqrt(dot3_plain(ray, ray));
+      for (int k = 0; k < 3; ++k) direction[k] = ray[k] / len;
+      float rotated[3];
+      mat3_vec(R, direction, rotated);
+      const float rs[3] = {rotated[0] * rotated[0], rotated[1] * rotated[1], rotated[2] * rotated[2]};
+      const float before[3] = {squared[1] * squared[2], squared[0] * squared[2], squared[0] * squared[1]};
+      const float after[3] = {dil_sq[1] * dil_sq[2], dil_sq[0] * dil_sq[2], dil_sq[0] * dil_sq[1]};
+      const float a = dot3_plain(rs, before), b = dot3_plain(rs, after);
+      const float compensation = std::sqrt(a / b);
+      const float factor = up_opacity[i] * opacities[i] * compensation / (a * b);
+      grad_opacity[i] = up_opacity[i] * compensation;
+      const float da[3] = {scale[0] * (rs[1] * squared[2] + rs[2] * squared[1]),
+                           scale[1] * (rs[0] * squared[2] + rs[2] * squared[0]),
+                           scale[2] * (rs[0] * squared[1] + rs[1] * squared[0])};
+      const float db[3] = {scale[0] * (rs[1] * dil_sq[2] + rs[2] * dil_sq[1]),
+                           scale[1] * (rs[0] * dil_sq[2] + rs[2] * dil_sq[0]),
+                           scale[2] * (rs[0] * dil_sq[1] + rs[1] * dil_sq[0])};
+      for (int k = 0; k < 3; ++k) {
+        comp_scale[k] = factor * (b * da[k] - a * db[k]);
+        comp_dir[k] = factor * (b * (rotated[k] * before[k]) - a * (rotated[k] * after[k]));
+      }
+      float Rt[3][3];
+      for (int r = 0; r < 3; ++r)
+        for (int c = 0; c < 3; ++c) Rt[r][c] = R[c][r];
+      float d_dir[3];
+      mat3_vec(Rt, comp_dir, d_dir);
+      const float along = dot3_plain(direction, d_dir);
+      for (int k = 0; k < 3; ++k) mean_grad[k] = mean_grad[k] + (d_dir[k] - direction[k] * along) / len;
+    }
+    for (int axis = 0; axis < 3; ++axis) {
+      gs[axis] = scale[axis] * dot3_plain(R[axis], columns[axis]) / dilated[axis] + comp_scale[axis];
+      for (int k = 0; k < 3; ++k)
+        columns[axis][k] = columns[axis][k] * dilated[axis] + direction[k] * comp_dir[axis];
+    }
+    for (int k = 0; k < 3; ++k) gm[k] = mean_grad[k];
+    // quaternion gradient of the rotation's columns
+    const float (*d)[3] = columns;
+    gq[0] = (2.0f * qz * (d[0][1] - d[1][0]) + 2.0f * qy * (d[2][0] - d[0][2])) +
+            2.0f * qx * (d[1][2] - d[2][1]);
+    gq[1] = ((2.0f * qy * (d[1][0] + d[0][1]) + 2.0f * qz * (d[2][0] + d[0][2])) +
+             2.0f * qr * (d[1][2] - d[2][1])) - 4.0f * qx * (d[2][2] + d[1][1]);
+    gq[2] = ((2.0f * qx * (d[1][0] + d[0][1]) + 2.0f * qr * (d[2][0] - d[0][2])) +
+             2.0f * qz * (d[1][2] + d[2][1])) - 4.0f * qy * (d[2][2] + d[0][0]);
+    gq[3] = ((2.0f * qr * (d[0][1] - d[1][0]) + 2.0f * qx * (d[2][0] + d[0][2])) +
+             2.0f * qy * (d[1][2] + d[2][1])) - 4.0f * qz * (d[1][1] + d[0][0]);
+  }
+}
+
 }  // extern "C"

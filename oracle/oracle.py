@@ -101,6 +101,10 @@ def lib():
         L.oracle_aaa_duplicate.argtypes = [
             _int, _f32p, _f32p, _i32p, _f32p, _f32p, _i32p, _int, _int, _u64p, _i32p, _int]
         L.oracle_aaa_duplicate.restype = None
+        L.oracle_aaa_preprocess_backward.argtypes = [
+            _int, _f32p, _f32p, _f32p, _f32p, _i32p, _f32p, _f32p, _f32p, _int, _int, _flt, _int,
+            _f32p, _f32p, _f32p, _f32p, _f32p, _f32p]
+        L.oracle_aaa_preprocess_backward.restype = None
         L.oracle_num_threads.restype = _int
         L.oracle_set_num_threads.argtypes = [_int]
         _lib = L
@@ -489,3 +493,19 @@ def aaa_duplicate(pre: dict, radii, tiles, width: int, height: int, offsets=None
         len(radii), _c(pre["centers"]), _c(pre["rects"]), radii, _c(pre["transforms"]),
         _c(pre["opacity"]), offsets, int(width), int(height), keys, values, total)
     return offsets, keys, values
+
+
+def aaa_preprocess_backward(means, quats, scales, opacities, radii, view, proj, campos, width,
+                            height, focal_x, up_transforms, up_opacity, *, ewa=True):
+    """aaa/backward_preprocess.py:130-268 (aaa_oracle.cpp): the gradients of
+    the opacities, means, scales and quaternions from the gradients of the
+    Gaussian-to-screen transforms and effective opacities."""
+    n = len(means)
+    out = dict(opacity=np.zeros(n, np.float32), means=np.zeros((n, 3), np.float32),
+               scales=np.zeros((n, 3), np.float32), quats=np.zeros((n, 4), np.float32))
+    lib().oracle_aaa_preprocess_backward(
+        n, _c(means), _c(scales), _c(quats), _c(opacities), _c(radii, np.int32), _c(view),
+        _c(proj), _c(campos), int(width), int(height), float(focal_x), int(bool(ewa)),
+        _c(up_transforms), _c(up_opacity), out["opacity"], out["means"], out["scales"],
+        out["quats"])
+    return out

@@ -39,6 +39,8 @@ aaa/cameras.py:77-121 (prepare_cameras) and Gaussians run through
                                       key emission, its snippet compiled with the
                                       shim's 32-thread warp lanes; dup_* keys of
                                       aaa_coop)
+  aaa/backward_preprocess.py:130-268  preprocess_adjoint (seeded N(0,1) transform
+                                      and opacity upstreams; adj_* keys)
 with aaa/native_geometry.py's snippets (frustum depth, axis bounds, screen
 bounds) compiled by g++ against the host libm (atan2f, tanf, fmodf).
 
@@ -450,6 +452,22 @@ def aaa_case(name, scene: dict, flags: dict, use_sh: bool, with_filter: bool) ->
         A(centers, wp.vec2), A(rects, wp.vec2), A(depths), A(transforms, wp.mat44), A(eff),
         A(radii), A(tiles), A(rgb, wp.vec3), A(valid), A(clamped), A(queued), A(queue_size)])
     q = np.sort(queued[:queue_size[0]])
+    # aaa/backward_preprocess.py:318-345: focal_x = width / (2 tanfovx) in
+    # double, a float32 kernel argument; the raw input opacities
+    bwd = importlib.import_module("dsl_splat.aaa.backward_preprocess")
+    gen = np.random.default_rng(700 + len(name))
+    up_transforms = gen.standard_normal((n, 4, 4)).astype(np.float32)
+    up_opacity = gen.standard_normal(n).astype(np.float32)
+    focal_x = np.float32(W / (2.0 * tanx))
+    adj = dict(opacity=np.zeros(n, np.float32), means=np.zeros((n, 3), np.float32),
+               scales=np.zeros((n, 3), np.float32), quats=np.zeros((n, 4), np.float32))
+    ws.launch(bwd.preprocess_adjoint, n, [
+        A(means, wp.vec3), A(scales, wp.vec3), A(quats, wp.vec4), A(opac), A(radii), A(v),
+        A(proj), A(campos[None], wp.vec3), W, H, focal_x, bool(flags["ewa"]),
+        A(up_transforms, wp.mat44), A(up_opacity), A(adj["opacity"]), A(adj["means"], wp.vec3),
+        A(adj["scales"], wp.vec3), A(adj["quats"], wp.vec4)])
+    adjoint = dict(adj_up_transforms=up_transforms, adj_up_opacity=up_opacity,
+                   adj_focal_x=focal_x, **{f"adj_{k}": a for k, a in adj.items()})
     final = {}
     if flags["cooperative"]:
         # aaa/preprocess.py:453-476: min(n, 1024) blocks of 32 lanes
@@ -474,7 +492,7 @@ def aaa_case(name, scene: dict, flags: dict, use_sh: bool, with_filter: bool) ->
                 flags=np.array([flags[k] for k in AAA_FLAGS], np.bool_),
                 centers=centers, rects=rects, depths=depths, transforms=transforms,
                 opacity=eff, radii=radii, tiles=tiles, rgb=rgb, valid=valid,
-                clamped=clamped, queued=q, **final)
+                clamped=clamped, queued=q, **final, **adjoint)
 
 
 _DUPLICATE_DRIVER = r"""

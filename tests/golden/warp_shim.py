@@ -169,7 +169,10 @@ class Mat:
         return vector(type(self).cols)(*self.m[idx])
 
     def __setitem__(self, idx, value):
-        self.m[idx[0]][idx[1]] = _wp_f32(value)
+        if isinstance(idx, tuple):
+            self.m[idx[0]][idx[1]] = _wp_f32(value)
+        else:  # a whole row from a vector
+            self.m[idx] = [_wp_f32(a) for a in value.v]
 
     def __mul__(self, o):
         """Matrix-vector or matrix-matrix product, each sum left to right."""

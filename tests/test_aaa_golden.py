@@ -1,8 +1,9 @@
 """The AAA-Gaussians preprocessing oracle (oracle/aaa_oracle.cpp) against
 golden vectors made by executing dsl_splat's own aaa/preprocess3d.py:17-245
 and, on the load-balanced cases, aaa/cooperative_culling.py:152-192 and
-(aaa_coop) the key emission aaa/binning_native.py:7-135
-(tests/golden/make_golden.py --aaa-only).
+(aaa_coop) the key emission aaa/binning_native.py:7-135, and on every case
+the preprocessing adjoint aaa/backward_preprocess.py:130-268 with seeded
+upstream gradients (tests/golden/make_golden.py --aaa-only).
 
 Five flag sets cover every branch of preprocess_3d: the load-balanced
 defaults (aaa/config.py:41-54) with and without SH colours and a stored 3D
@@ -133,3 +134,18 @@ def test_duplicate_pads_a_short_range():
     assert np.all((pad & np.uint64(0xffffffff)) == np.uint64(0x7f7fffff))
     real = values >= 0
     np.testing.assert_array_equal(keys[real], d["dup_keys"])
+
+
+@pytest.mark.parametrize("path", CASES, ids=lambda p: os.path.basename(p)[:-4])
+def test_preprocess_adjoint_matches_reference_kernel(path):
+    d = np.load(path)
+    ewa = bool(dict(zip(O.AAA_FLAGS, d["flags"].tolist()))["ewa"])
+    out = O.aaa_preprocess_backward(
+        d["means"], d["quats"], d["scales"], d["opacities"], d["radii"], d["view"], d["proj"],
+        d["campos"], int(d["width"]), int(d["height"]), d["adj_focal_x"],
+        d["adj_up_transforms"], d["adj_up_opacity"], ewa=ewa)
+    for key in ("opacity", "means", "scales", "quats"):
+        np.testing.assert_array_equal(out[key], d["adj_" + key], err_msg=key)
+    visible = d["radii"] > 0
+    assert np.abs(d["adj_quats"][visible]).sum() > 0
+    assert not d["adj_means"][~visible].any()
