@@ -711,4 +711,167 @@ void oracle_aaa_preprocess_backward(int n, const float* means, const float* scal
   }
 }
 
+// aaa/backward_camera.py:14-53 sh_basis_gradient: d(basis k)/d(direction).
+static void sh_basis_gradient(const float d[3], int k, float g[3]) {
+  const float x = d[0], y = d[1], z = d[2];
+  auto set = [&](float c, float a, float b, float e) { g[0] = c * a; g[1] = c * b; g[2] = c * e; };
+  switch (k) {
+    case 0: g[0] = g[1] = g[2] = 0.0f; return;
+    case 1: g[0] = 0.0f; g[1] = -0.4886025119029199f; g[2] = 0.0f; return;
+    case 2: g[0] = 0.0f; g[1] = 0.0f; g[2] = 0.4886025119029199f; return;
+    case 3: g[0] = -0.4886025119029199f; g[1] = 0.0f; g[2] = 0.0f; return;
+    case 4: set(1.0925484305920792f, y, x, 0.0f); return;
+    case 5: set(-1.0925484305920792f, 0.0f, z, y); return;
+    case 6: set(0.31539156525252005f, -2.0f * x, -2.0f * y, 4.0f * z); return;
+    case 7: set(-1.0925484305920792f, z, 0.0f, x); return;
+    case 8: set(0.5462742152960396f, 2.0f * x, -2.0f * y, 0.0f); return;
+    case 9: set(-0.5900435899266435f, 6.0f * x * y, 3.0f * (x * x - y * y), 0.0f); return;
+    case 10: set(2.890611442640554f, y * z, x * z, x * y); return;
+    case 11: set(0.4570457994644658f, 2.0f * x * y, x * x + 3.0f * y * y - 4.0f * z * z, -8.0f * y * z); return;
+    case 12: set(0.3731763325901154f, -6.0f * x * z, -6.0f * y * z, 6.0f * z * z - 3.0f * (x * x + y * y)); return;
+    case 13: set(0.4570457994644658f, 3.0f * x * x + y * y - 4.0f * z * z, 2.0f * x * y, -8.0f * x * z); return;
+    case 14: set(1.445305721320277f, 2.0f * x * z, -2.0f * y * z, x * x - y * y); return;
+    default: set(-0.5900435899266435f, 3.0f * (x * x - y * y), -6.0f * x * y, 0.0f); return;
+  }
+}
+
+// aaa/backward_camera.py:61-224 camera_adjoint: each visible Gaussian's
+// contribution to the camera gradients, 23 floats -- dL/d(projection
+// matrix) in the reference's transposed storage (16), the adaptive filter's
+// depth term times (mean, 1) (4), dL/d(camera position) through the EWA
+// compensation and the SH view direction (3).  The host sums the rows.
+//   up_colors: (n*3) dL/d(SH colour), masked where the forward clamped.
+void oracle_aaa_camera_backward(int n, const float* means, const float* scales, const float* quats,
+                                const float* filters, const int* radii,
+                                const float* effective_opacity, const float* view,
+                                const float* proj, const float* campos, int width, int height,
+                                float focal, float modifier, int ewa, const float* up_transforms,
+                                const float* up_opacity, const float* sh, int K, int degree,
+                                const unsigned char* clamped, const float* up_colors,
+                                float* rows) {
+  const M4 V = load_transposed(view), P = load_transposed(proj);
+  const float W = static_cast<float>(width), H = static_cast<float>(height);
+  const float viewport[4][4] = {{W / 2.0f, 0.0f, 0.0f, W / 2.0f - 0.5f},
+                                {0.0f, H / 2.0f, 0.0f, H / 2.0f - 0.5f},
+                                {0.0f, 0.0f, 1.0f, 0.0f},
+                                {0.0f, 0.0f, 0.0f, 1.0f}};
+  auto mul4 = [](const float a[4][4], const float b[4][4], float out[4][4]) {
+    for (int r = 0; r < 4; ++r)
+      for (int c = 0; c < 4; ++c) {
+        float acc = a[r][0] * b[0][c];
+        for (int k = 1; k < 4; ++k) acc = acc + a[r][k] * b[k][c];
+        out[r][c] = acc;
+      }
+  };
+  auto transpose4 = [](const float a[4][4], float out[4][4]) {
+    for (int r = 0; r < 4; ++r)
+      for (int c = 0; c < 4; ++c) out[r][c] = a[c][r];
+  };
+  float viewport_t[4][4], clip[4][4], clip_t[4][4];
+  transpose4(viewport, viewport_t);
+  mul4(viewport, P.m, clip);
+  transpose4(clip, clip_t);
+  const float root_modifier = std::sqrt(modifier);
+#pragma omp parallel for schedule(static)
+  for (int i = 0; i < n; ++i) {
+    float* row = rows + 23 * i;
+    if (radii[i] <= 0) {
+      for (int k = 0; k < 23; ++k) row[k] = 0.0f;
+      continue;
+    }
+    const float* mean = means + 3 * i;
+    const float depth = ((V.m[2][0] * mean[0] + V.m[2][1] * mean[1]) + V.m[2][2] * mean[2]) + V.m[2][3] * 1.0f;
+    const float adaptive = 0.3f * (depth / focal) * (depth / focal);
+    float variance = adaptive;
+    bool filter_active = true;
+    if (filters) {
+      const float fixed = filters[i] * filters[i];
+      variance = std::fmax(variance, fixed);
+      filter_active = adaptive > fixed;
+    }
+    const float* scale = scales + 3 * i;
+    float squared[3], dil_sq[3], dilated[3];
+    for (int k = 0; k < 3; ++k) {
+      squared[k] = scale[k] * scale[k];
+      dil_sq[k] = squared[k] + variance;
+      dilated[k] = std::sqrt(dil_sq[k]);
+    }
+    const float* q = quats + 4 * i;
+    const float qr = q[0], qx = q[1], qy = q[2], qz = q[3];
+    const float R[3][3] = {
+        {1.0f - 2.0f * (qy * qy + qz * qz), 2.0f * (qx * qy + qr * qz), 2.0f * (qx * qz - qr * qy)},
+        {2.0f * (qx * qy - qr * qz), 1.0f - 2.0f * (qx * qx + qz * qz), 2.0f * (qy * qz + qr * qx)},
+        {2.0f * (qx * qz + qr * qy), 2.0f * (qy * qz - qr * qx), 1.0f - 2.0f * (qx * qx + qy * qy)}};
+    float D[3][3] = {{dilated[0], 0.0f, 0.0f}, {0.0f, dilated[1], 0.0f}, {0.0f, 0.0f, dilated[2]}};
+    float DR[3][3];
+    mat3_mul(D, R, DR);
+    float world[4][4] = {};
+    for (int r = 0; r < 3; ++r) {
+      for (int c = 0; c < 3; ++c) world[r][c] = DR[c][r] * root_modifier;
+      world[r][3] = mean[r];
+    }
+    world[3][3] = 1.0f;
+    float screen_gradient[4][4], world_t[4][4], tmp[4][4], projection_gradient[4][4], world_gradient[4][4];
+    for (int r = 0; r < 4; ++r)
+      for (int c = 0; c < 4; ++c) screen_gradient[r][c] = up_transforms[16 * i + 4 * c + r];
+    transpose4(world, world_t);
+    mul4(viewport_t, screen_gradient, tmp);
+    mul4(tmp, world_t, projection_gradient);
+    mul4(clip_t, screen_gradient, world_gradient);
+    float variance_gradient = 0.0f;
+    for (int axis = 0; axis < 3; ++axis) {
+      const float column[3] = {world_gradient[0][axis], world_gradient[1][axis], world_gradient[2][axis]};
+      variance_gradient = variance_gradient + dot3_plain(column, R[axis]) * root_modifier / (2.0f * dilated[axis]);
+    }
+    float camera_gradient[3] = {0.0f, 0.0f, 0.0f};
+    const float ray[3] = {mean[0] - campos[0], mean[1] - campos[1], mean[2] - campos[2]};
+    const float distance = std::sqrt(dot3_plain(ray, ray));
+    const float direction[3] = {ray[0] / distance, ray[1] / distance, ray[2] / distance};
+    float Rt[3][3];
+    for (int r = 0; r < 3; ++r)
+      for (int c = 0; c < 3; ++c) Rt[r][c] = R[c][r];
+    auto tangent_step = [&](const float g[3]) {  // camera -= (g - d (d.g)) / distance
+      const float along = dot3_plain(direction, g);
+      for (int k = 0; k < 3; ++k)
+        camera_gradient[k] = camera_gradient[k] - (g[k] - direction[k] * along) / distance;
+    };
+    if (ewa) {
+      float rotated[3];
+      mat3_vec(R, direction, rotated);
+      const float rs[3] = {rotated[0] * rotated[0], rotated[1] * rotated[1], rotated[2] * rotated[2]};
+      const float before[3] = {squared[1] * squared[2], squared[0] * squared[2], squared[0] * squared[1]};
+      const float after[3] = {dil_sq[1] * dil_sq[2], dil_sq[0] * dil_sq[2], dil_sq[0] * dil_sq[1]};
+      const float a = dot3_plain(rs, before), b = dot3_plain(rs, after);
+      const float factor = up_opacity[i] * effective_opacity[i];
+      float rotated_gradient[3], direction_gradient[3];
+      for (int k = 0; k < 3; ++k)
+        rotated_gradient[k] = factor * ((rotated[k] * before[k]) / a - (rotated[k] * after[k]) / b);
+      mat3_vec(Rt, rotated_gradient, direction_gradient);
+      tangent_step(direction_gradient);
+      const float area[3] = {dil_sq[1] + dil_sq[2], dil_sq[0] + dil_sq[2], dil_sq[0] + dil_sq[1]};
+      variance_gradient = variance_gradient - 0.5f * factor * dot3_plain(rs, area) / b;
+    }
+    if (sh) {
+      float color_grad[3];
+      for (int c = 0; c < 3; ++c) color_grad[c] = clamped[3 * i + c] ? 0.0f : up_colors[3 * i + c];
+      float direction_grad[3] = {0.0f, 0.0f, 0.0f};
+      const int count = (degree + 1) * (degree + 1);
+      for (int k = 0; k < count; ++k) {
+        const float* coeff = sh + (static_cast<long long>(i) * K + k) * 3;
+        const float weight = dot3_plain(coeff, color_grad);
+        float basis[3];
+        sh_basis_gradient(direction, k, basis);
+        for (int c = 0; c < 3; ++c) direction_grad[c] = direction_grad[c] + weight * basis[c];
+      }
+      tangent_step(direction_grad);
+    }
+    const float depth_gradient = filter_active ? variance_gradient * 0.6f * depth / (focal * focal) : 0.0f;
+    for (int r = 0; r < 4; ++r) {
+      for (int c = 0; c < 4; ++c) row[r * 4 + c] = projection_gradient[c][r];
+      row[16 + r] = depth_gradient * (r < 3 ? mean[r] : 1.0f);
+    }
+    for (int k = 0; k < 3; ++k) row[20 + k] = camera_gradient[k];
+  }
+}
+
 }  // extern "C"

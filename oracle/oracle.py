@@ -105,6 +105,10 @@ def lib():
             _int, _f32p, _f32p, _f32p, _f32p, _i32p, _f32p, _f32p, _f32p, _int, _int, _flt, _int,
             _f32p, _f32p, _f32p, _f32p, _f32p, _f32p]
         L.oracle_aaa_preprocess_backward.restype = None
+        L.oracle_aaa_camera_backward.argtypes = [
+            _int, _f32p, _f32p, _f32p, _vp, _i32p, _f32p, _f32p, _f32p, _f32p, _int, _int, _flt,
+            _flt, _int, _f32p, _f32p, _vp, _int, _int, _vp, _f32p, _f32p]
+        L.oracle_aaa_camera_backward.restype = None
         L.oracle_num_threads.restype = _int
         L.oracle_set_num_threads.argtypes = [_int]
         _lib = L
@@ -509,3 +513,23 @@ def aaa_preprocess_backward(means, quats, scales, opacities, radii, view, proj, 
         _c(up_transforms), _c(up_opacity), out["opacity"], out["means"], out["scales"],
         out["quats"])
     return out
+
+
+def aaa_camera_backward(means, quats, scales, radii, effective_opacity, view, proj, campos,
+                        width, height, focal, up_transforms, up_opacity, up_colors, *,
+                        filters=None, sh=None, sh_degree=0, clamped=None, ewa=True,
+                        modifier=1.0):
+    """aaa/backward_camera.py:61-224 (aaa_oracle.cpp): per-Gaussian (n, 23)
+    camera-gradient rows (the reference sums them over Gaussians)."""
+    n = len(means)
+    rows = np.zeros((n, 23), np.float32)
+    sh_c = _c(sh) if sh is not None else None
+    cl = _c(clamped, np.uint8) if sh is not None else None
+    filt = _c(filters) if filters is not None else None
+    lib().oracle_aaa_camera_backward(
+        n, _c(means), _c(scales), _c(quats), _ptr(filt), _c(radii, np.int32),
+        _c(effective_opacity), _c(view), _c(proj), _c(campos), int(width), int(height),
+        float(focal), float(modifier), int(bool(ewa)), _c(up_transforms), _c(up_opacity),
+        _ptr(sh_c), sh_c.shape[1] if sh_c is not None else 0, int(sh_degree), _ptr(cl),
+        _c(up_colors), rows)
+    return rows

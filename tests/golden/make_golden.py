@@ -41,6 +41,9 @@ aaa/cameras.py:77-121 (prepare_cameras) and Gaussians run through
                                       aaa_coop)
   aaa/backward_preprocess.py:130-268  preprocess_adjoint (seeded N(0,1) transform
                                       and opacity upstreams; adj_* keys)
+  aaa/backward_camera.py:61-224       camera_adjoint (the same upstreams and a
+                                      seeded colour gradient; cam_* keys, the
+                                      per-Gaussian 23-float rows)
 with aaa/native_geometry.py's snippets (frustum depth, axis bounds, screen
 bounds) compiled by g++ against the host libm (atan2f, tanf, fmodf).
 
@@ -468,6 +471,17 @@ def aaa_case(name, scene: dict, flags: dict, use_sh: bool, with_filter: bool) ->
         A(adj["scales"], wp.vec3), A(adj["quats"], wp.vec4)])
     adjoint = dict(adj_up_transforms=up_transforms, adj_up_opacity=up_opacity,
                    adj_focal_x=focal_x, **{f"adj_{k}": a for k, a in adj.items()})
+    # aaa/backward_camera.py:259-290: focal = max of the two focal lengths
+    cam_mod = importlib.import_module("dsl_splat.aaa.backward_camera")
+    up_colors = gen.standard_normal(n * 3).astype(np.float32)
+    focal = np.float32(max(W / (2 * tanx), H / (2 * tany)))
+    rows = np.zeros((n, 23), np.float32)
+    ws.launch(cam_mod.camera_adjoint, n, [
+        A(means, wp.vec3), A(scales, wp.vec3), A(quats, wp.vec4), A(filters), with_filter,
+        A(radii), A(eff), A(v), A(proj), A(campos[None], wp.vec3), W, H, focal, np.float32(1.0),
+        bool(flags["ewa"]), A(up_transforms, wp.mat44), A(up_opacity), A(sh, wp.vec3), use_sh,
+        deg, A(clamped), A(up_colors), A(rows)])
+    adjoint.update(cam_up_colors=up_colors, cam_focal=focal, cam_rows=rows)
     final = {}
     if flags["cooperative"]:
         # aaa/preprocess.py:453-476: min(n, 1024) blocks of 32 lanes

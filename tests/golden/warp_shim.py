@@ -185,8 +185,10 @@ class Mat:
                         acc = acc + row[k] * o.m[k][c]
                     out.m[r][c] = acc
             return out
-        if not isinstance(o, Vec):
-            raise TypeError("matrix * non-vector")
+        if not isinstance(o, Vec):  # matrix * scalar, element-wise
+            out = type(self)()
+            out.m = [[_wp_f32(a * o) for a in row] for row in self.m]
+            return out
         out = []
         for row in self.m:
             acc = row[0] * o.v[0]

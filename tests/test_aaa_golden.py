@@ -2,8 +2,9 @@
 golden vectors made by executing dsl_splat's own aaa/preprocess3d.py:17-245
 and, on the load-balanced cases, aaa/cooperative_culling.py:152-192 and
 (aaa_coop) the key emission aaa/binning_native.py:7-135, and on every case
-the preprocessing adjoint aaa/backward_preprocess.py:130-268 with seeded
-upstream gradients (tests/golden/make_golden.py --aaa-only).
+the preprocessing adjoint aaa/backward_preprocess.py:130-268 and the camera
+adjoint aaa/backward_camera.py:61-224 with seeded upstream gradients
+(tests/golden/make_golden.py --aaa-only).
 
 Five flag sets cover every branch of preprocess_3d: the load-balanced
 defaults (aaa/config.py:41-54) with and without SH colours and a stored 3D
@@ -149,3 +150,26 @@ def test_preprocess_adjoint_matches_reference_kernel(path):
     visible = d["radii"] > 0
     assert np.abs(d["adj_quats"][visible]).sum() > 0
     assert not d["adj_means"][~visible].any()
+
+
+@pytest.mark.parametrize("path", CASES, ids=lambda p: os.path.basename(p)[:-4])
+def test_camera_adjoint_matches_reference_kernel(path):
+    d = np.load(path)
+    use_sh = bool(d["use_sh"])
+    rows = O.aaa_camera_backward(
+        d["means"], d["quats"], d["scales"], d["radii"], d["opacity"], d["view"], d["proj"],
+        d["campos"], int(d["width"]), int(d["height"]), d["cam_focal"], d["adj_up_transforms"],
+        d["adj_up_opacity"], d["cam_up_colors"],
+        filters=d["filters"] if bool(d["has_filter"]) else None,
+        sh=d["sh"] if use_sh else None, sh_degree=int(d["sh_degree"]),
+        clamped=d["clamped"] if use_sh else None,
+        ewa=bool(dict(zip(O.AAA_FLAGS, d["flags"].tolist()))["ewa"]))
+    np.testing.assert_array_equal(rows, d["cam_rows"])
+    visible = d["radii"] > 0
+    ewa = bool(dict(zip(O.AAA_FLAGS, d["flags"].tolist()))["ewa"])
+    assert np.abs(d["cam_rows"][visible][:, :20]).sum() > 0
+    # the camera position only receives gradient through the EWA
+    # compensation and the SH view direction
+    camera_terms = np.abs(d["cam_rows"][visible][:, 20:]).sum()
+    assert (camera_terms > 0) == (ewa or use_sh)
+    assert not d["cam_rows"][~visible].any()
