@@ -14,7 +14,8 @@ N > 1 is launched with torchrun, one rank per GPU: every rank renders its
 own camera of the shared scene (weak scaling) and the per-Gaussian gradients
 are summed with an NCCL all-reduce each step (the path's only exchange).
 `--impl reference` times the reference algorithm's CPU restatement (the
-oracle: dsl_splat's Warp code cannot run here) on the host.
+oracle: dsl_splat's Warp code needs warp-lang, which is not installed) on
+the host cores, without importing this package.
 """
 
 from __future__ import annotations
@@ -47,7 +48,7 @@ CONFIG_METRICS = {2: "fwd+bwd frames/s (camera views), 3DGS SH3 3M Gaussians, 8 
 def metric_for(config: int) -> str:
     return CONFIG_METRICS.get(config, METRIC)
 UNIT = "frames/s"
-CHANNELS = 4  # RGB + the appended alpha column (gs3d/autograd.py:306-311)
+CHANNELS = 4  # RGB + the appended alpha column (gs3d/autograd.py:42-46)
 
 
 def parse_args():
@@ -78,16 +79,32 @@ def dist_env():
     return rank, world, local
 
 
+def scenes_module():
+    """dsl_splat_b200/scenes.py loaded by file path: the scene generator needs
+    only torch, and loading it this way keeps the package __init__ (which maps
+    libsplat200.so) out of the reference arm's process."""
+    import importlib.util
+    name = "_bench_scenes"
+    if name not in sys.modules:
+        spec = importlib.util.spec_from_file_location(
+            name, os.path.join(ROOT, "dsl_splat_b200", "scenes.py"))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+    return sys.modules[name]
+
+
 def workload(config: int, rank: int, world: int, gaussians: int | None = None):
     """The config scene.  Single-view configs: rank r looks from an orbit
     angle 2*pi*r/world (one view per rank).  Multi-view configs (config 2's
-    8-camera batch): rank r renders the cameras k with k mod world == r."""
-    from dsl_splat_b200.scenes import look_at, make_scene
-    from dsl_splat_b200.sharding import local_cameras
+    8-camera batch): rank r renders the cameras k with k mod world == r
+    (the round robin of sharding.local_cameras)."""
+    sc = scenes_module()
+    look_at, make_scene = sc.look_at, sc.make_scene
     s = make_scene(config, n=gaussians)
     cams = s.viewmats.shape[0]
     if cams > 1:
-        idx = local_cameras(cams, rank, world)
+        idx = [k for k in range(cams) if k % world == rank]
         if not idx:
             raise SystemExit(f"config {config} has {cams} cameras: at most {cams} ranks")
         for name in ("viewmats", "Ks", "target", "grad_image", "grad_alpha"):

@@ -20,6 +20,7 @@ _I = ctypes.c_int
 _F = ctypes.c_float
 _Z = ctypes.c_size_t
 _L = ctypes.c_longlong
+_U = ctypes.c_uint
 
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
@@ -27,6 +28,8 @@ SIGNATURES: dict[str, tuple] = {
     "splat_last_error": (ctypes.c_char_p, []),
     "splat_launch_count": (ctypes.c_ulonglong, []),
     "splat_device_error": (_I, [_P, _P]),
+    "splat_device_error_read": (_I, [_P, _P]),
+    "splat_test_lookback_expiry": (_I, [_P, _U, _P, _P]),
     "splat_cameras_prepare": (_I, [_I, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "splat_cameras_backward": (_I, [_I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "splat_project_forward": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,

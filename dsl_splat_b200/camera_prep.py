@@ -72,7 +72,7 @@ def prepare_cameras_with_centers(views: Tensor, Ks: Tensor, width: int, height: 
 
 
 def prepare_camera(camera: PinholeCamera, radius_clip: float):
-    """splatting/cameras.py:253-281 for the stage-level API."""
+    """splatting/cameras.py:147-175 for the stage-level API."""
     validate_camera_options(camera.width, camera.height, camera.near_plane, camera.far_plane,
                             radius_clip)
     if not isinstance(camera.viewmat, Tensor) or not camera.viewmat.is_cuda:

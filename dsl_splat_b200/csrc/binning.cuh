@@ -65,7 +65,8 @@ struct Status64 {
 // is read again after a short sleep.  Tile 0 is always inclusive, so the
 // walk ends; a wait longer than kSpinLimit records kDeviceTimeout.
 template <class S, int kWindow>
-SPLAT_DEV typename S::Word lookback(const typename S::Word* status, int64_t tile, size_t stride) {
+SPLAT_DEV typename S::Word lookback(const typename S::Word* status, int64_t tile, size_t stride,
+                                    uint32_t spin_limit = kSpinLimit) {
   using Word = typename S::Word;
   Word excl = 0;
   uint32_t spins = 0;
@@ -96,7 +97,7 @@ SPLAT_DEV typename S::Word lookback(const typename S::Word* status, int64_t tile
     excl += add;
     if (state == 1) break;
     if (state == 2) {
-      if (++spins > kSpinLimit) {
+      if (++spins > spin_limit) {
         record_device_error(kDeviceTimeout);
         break;
       }
@@ -105,6 +106,16 @@ SPLAT_DEV typename S::Word lookback(const typename S::Word* status, int64_t tile
     t -= consumed;
   }
   return excl;
+}
+
+// One thread walks the look-back of tile 1 over `status` (two words the
+// caller zeroed, i.e. never published) with a short spin limit: the wait
+// runs out, kDeviceTimeout is recorded and the thread returns.  This is how
+// the tests check that an expired wait ends and is reported, without
+// faulting or hanging anything.
+__global__ void lookback_expiry_kernel(const uint32_t* __restrict__ status, uint32_t spin_limit,
+                                       uint32_t* __restrict__ out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *out = lookback<Status32, 1>(status, 1, 1, spin_limit);
 }
 
 // ---- phase 1: per-Gaussian preparation ---------------------------------
@@ -432,6 +443,70 @@ __global__ void scan_block_prefix_kernel(uint32_t* __restrict__ block_sums, uint
     __syncthreads();
   }
   if (threadIdx.x == 0) *total = s_carry;
+}
+
+// ---- count scan (splat_scan_counts*): 64-bit total ----------------------------
+// The offsets are int32 (as the reference's array_scan output), so a count
+// total above INT32_MAX cannot be represented; the total itself is formed in
+// 64 bits so that it never wraps, and exceeding INT32_MAX is reported.
+
+SPLAT_DEV unsigned long long block_sum_u64(unsigned long long v, unsigned long long* s_warp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = (blockDim.x + 31) >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  if (lane == 0) s_warp[warp] = v;
+  __syncthreads();
+  unsigned long long sum = 0ull;
+  for (int w = 0; w < warps; ++w) sum += s_warp[w];
+  __syncthreads();
+  return sum;
+}
+
+// Per block of kSortTile counts: the sum in 64 bits, stored saturated at
+// 0xFFFFFFFF (a block sum that large already puts the total past INT32_MAX).
+__global__ void __launch_bounds__(kSortBlock)
+    scan_count_block_sums_kernel(const int* __restrict__ values, uint32_t n,
+                                 uint32_t* __restrict__ block_sums) {
+  __shared__ unsigned long long s_warp[32];
+  const uint32_t base = blockIdx.x * kSortTile;
+  unsigned long long sum = 0ull;
+  for (int k = 0; k < kSortItems; ++k) {
+    const uint32_t i = base + k * kSortBlock + threadIdx.x;
+    if (i < n) sum += static_cast<unsigned long long>(scan_value(values, nullptr, i, 0u));
+  }
+  const unsigned long long total = block_sum_u64(sum, s_warp);
+  if (threadIdx.x == 0) block_sums[blockIdx.x] = total > 0xFFFFFFFFull ? 0xFFFFFFFFu
+                                                                        : static_cast<uint32_t>(total);
+}
+
+// One block: exclusive scan of the block sums in place (exact whenever the
+// total fits int32) and their 64-bit sum into *total (may be null).  A total
+// above INT32_MAX records kTooLarge in the device error word: the offsets of
+// that call are not valid.
+__global__ void scan_count_prefix_kernel(uint32_t* __restrict__ block_sums, uint32_t nblocks,
+                                         long long* __restrict__ total) {
+  __shared__ uint32_t s_warp[32];
+  __shared__ unsigned long long s_warp64[32];
+  __shared__ uint32_t s_carry;
+  if (threadIdx.x == 0) s_carry = 0u;
+  __syncthreads();
+  unsigned long long mine = 0ull;
+  for (uint32_t base = 0; base < nblocks; base += blockDim.x) {
+    const uint32_t i = base + threadIdx.x;
+    const uint32_t v = i < nblocks ? block_sums[i] : 0u;
+    mine += v;
+    uint32_t chunk;
+    const uint32_t before = block_exclusive_scan(v, s_warp, &chunk);
+    if (i < nblocks) block_sums[i] = s_carry + before;
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry += chunk;
+    __syncthreads();
+  }
+  const unsigned long long sum = block_sum_u64(mine, s_warp64);
+  if (threadIdx.x == 0) {
+    if (total) *total = static_cast<long long>(sum);
+    if (sum > 0x7FFFFFFFull) record_device_error(kTooLarge);
+  }
 }
 
 // out[i] = exclusive (or inclusive) prefix; when exclusive, out[n] = total.

@@ -48,7 +48,7 @@ struct Mat3 {
   float m[3][3];
 };
 
-// splatting/math.py:54-64 reference_matmul
+// splatting/math.py:31-42 reference_matmul
 SPLAT_DEV Mat3 ref_matmul(const Mat3& a, const Mat3& b) {
   Mat3 r;
 #pragma unroll
@@ -69,7 +69,7 @@ SPLAT_DEV Mat3 transpose(const Mat3& a) {
   return r;
 }
 
-// splatting/math.py:67-70 point_row
+// splatting/math.py:44-47 point_row
 SPLAT_DEV float point_row(const float* m, int row, float p0, float p1, float p2) {
   const float xy = __fmaf_rn(m[row * 4 + 0], p0, m[row * 4 + 1] * p1);
   return __fmaf_rn(m[row * 4 + 2], p2, xy) + m[row * 4 + 3];

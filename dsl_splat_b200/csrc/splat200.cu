@@ -407,6 +407,26 @@ int splat_device_error(int* code, void* stream) {
   return kOk;
 }
 
+int splat_device_error_read(int* device_dst, void* stream) {
+  if (!device_dst) return fail(kInvalidArgument, "device_dst must not be null");
+  cudaStream_t s = as_stream(stream);
+  void* word = nullptr;
+  if (cudaGetSymbolAddress(&word, g_splat_device_error) != cudaSuccess)
+    return check_launch("splat_device_error_read: symbol");
+  if (cudaMemcpyAsync(device_dst, word, sizeof(int), cudaMemcpyDeviceToDevice, s) != cudaSuccess ||
+      cudaMemsetAsync(word, 0, sizeof(int), s) != cudaSuccess)
+    return check_launch("splat_device_error_read");
+  return kOk;
+}
+
+int splat_test_lookback_expiry(const unsigned* status, unsigned spin_limit, unsigned* out,
+                               void* stream) {
+  if (!status || !out) return fail(kInvalidArgument, "null status/out");
+  if (spin_limit > (1u << 20)) return fail(kInvalidArgument, "spin_limit above 2^20");
+  lookback_expiry_kernel<<<1, 32, 0, counted(as_stream(stream))>>>(status, spin_limit, out);
+  return check_launch("test_lookback_expiry");
+}
+
 // ---- cameras -------------------------------------------------------------
 
 int splat_cameras_prepare(int count, const float* views, const float* Ks, int width, int height,
@@ -735,21 +755,17 @@ int splat_scan_counts(int n, const int* counts, int* offsets, long long* total, 
   cudaStream_t s = as_stream(stream);
   uint32_t* block_sums = static_cast<uint32_t*>(workspace);
   const unsigned nb = blocks_for(n > 0 ? n : 1, kSortTile);
-  uint32_t* tot = block_sums + nb + 1;
   if (n == 0) {
     if (total && cudaMemsetAsync(total, 0, sizeof(long long), s) != cudaSuccess)
       return check_launch("scan_counts");
     return kOk;
   }
-  scan_block_sums_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, nullptr, n, block_sums);
-  scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, nb, tot);
+  // the total is summed in 64 bits (never wraps); above INT32_MAX the device
+  // error word receives kTooLarge, since the int32 offsets cannot hold it
+  scan_count_block_sums_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, n, block_sums);
+  scan_count_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, nb, total);
   scan_apply_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, nullptr, n, block_sums, 1,
                                              reinterpret_cast<uint32_t*>(offsets));
-  if (total) {
-    if (cudaMemsetAsync(total, 0, sizeof(long long), s) != cudaSuccess ||
-        cudaMemcpyAsync(total, tot, sizeof(uint32_t), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-      return check_launch("scan_counts total");
-  }
   return check_launch("scan_counts");
 }
 
@@ -772,7 +788,10 @@ static __device__ __align__(256) uint32_t g_static_scan_scratch[kStaticScanBlock
 
 // Device address of g_static_scan_scratch per device ordinal.  The host-side
 // symbol is only a stand-in; the address comes from cudaGetSymbolAddress,
-// called once per device with that device current.
+// called once per device with that device current.  The cached address
+// belongs to that device's context: a process that resets the device
+// (cudaDeviceReset) and keeps using this library must not call the static
+// scan again afterwards (the address would be stale).
 std::mutex g_static_scan_mutex;
 void* g_static_scan_address[256] = {};
 
@@ -816,16 +835,10 @@ int splat_scan_counts_static(int n, const int* counts, int* offsets, long long* 
   // Each call overwrites every block sum and the total it reads, so nothing
   // left by an earlier call needs clearing.
   const unsigned nb = blocks_for(n, kSortTile);
-  uint32_t* tot = block_sums + kStaticScanBlocks + 1;
-  scan_block_sums_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, nullptr, n, block_sums);
-  scan_block_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, nb, tot);
+  scan_count_block_sums_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, n, block_sums);
+  scan_count_prefix_kernel<<<1, 1024, 0, counted(s)>>>(block_sums, nb, total);
   scan_apply_kernel<<<nb, kSortBlock, 0, counted(s)>>>(counts, nullptr, n, block_sums, 1,
                                                        reinterpret_cast<uint32_t*>(offsets));
-  if (total) {
-    if (cudaMemsetAsync(total, 0, sizeof(long long), s) != cudaSuccess ||
-        cudaMemcpyAsync(total, tot, sizeof(uint32_t), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
-      return check_launch("scan_counts_static total");
-  }
   return check_launch("scan_counts_static");
 }
 

@@ -5,7 +5,7 @@ separate Functions for projection and SH.  Here projection and SH are one
 Function (one forward kernel, one fused backward kernel) and binning +
 blending another; gradients reach the same inputs with the same meaning:
 means2d receives dL/dcenters and its absgrad the per-pixel |dL/dcenters|
-sums (gs3d/autograd.py:386-401).
+sums (gs3d/autograd.py:120-140).
 """
 
 from __future__ import annotations

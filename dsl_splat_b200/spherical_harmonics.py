@@ -43,7 +43,7 @@ def spherical_harmonics(coefficients: Tensor, directions: Tensor, degree: int, *
                         radii: Tensor | None = None) -> Tensor:
     """SH colour max(sum + 0.5, 0); rows with radii <= 0 return zero.
 
-    Same validation and messages as primitives/spherical_harmonics.py:284-339.
+    Same validation and messages as primitives/spherical_harmonics.py:104-159.
     """
     if isinstance(degree, bool) or not isinstance(degree, Integral) or degree not in range(4):
         raise ValueError("SH degree must be an integer in [0,3]")

@@ -1,9 +1,9 @@
 """Stage wrappers: allocate outputs with Torch and launch one C-ABI call.
 
 These are the swap points of the reference's L2 stage wrappers:
-gs3d/projection.py:309-428 (prepare/backward), splatting/binning.py:171-217
+gs3d/projection.py:309-428 (prepare/backward), splatting/binning.py:72-117
 (bin_and_sort), gs3d/render.py:359-463 (render/backward),
-primitives/spherical_harmonics.py:18-101, splatting/cameras.py:133-221 and
+primitives/spherical_harmonics.py:18-101, splatting/cameras.py:27-115 and
 splatting/metadata.py:34-70.  Everything runs on the caller's current CUDA
 stream; tensors must be CUDA float32/int32.
 """
@@ -111,7 +111,7 @@ class RenderedPixels:
 # ---- cameras ---------------------------------------------------------------
 
 def raise_camera_errors(codes) -> None:
-    """splatting/cameras.py:170-180: the reference's exceptions for status codes."""
+    """splatting/cameras.py:64-74: the reference's exceptions for status codes."""
     if 2 in codes:
         raise ValueError("Ks must be finite with positive fx/fy")
     if 1 in codes:
@@ -122,7 +122,7 @@ def raise_camera_errors(codes) -> None:
 
 def cameras_prepare(views: Tensor, Ks: Tensor, width: int, height: int, with_centers: bool,
                     status_sink: list | None = None):
-    """splatting/cameras.py:133-188: full (…,4,4), inverse (C,4,4), centers (…,3).
+    """splatting/cameras.py:29-85: full (…,4,4), inverse (C,4,4), centers (…,3).
 
     Only status codes cross to the host, as in the reference.  With a
     status_sink the (C,) int32 codes are appended to it instead of being read
@@ -376,7 +376,11 @@ def scan_counts(counts: Tensor) -> tuple[Tensor, int]:
     total = torch.zeros(1, dtype=torch.int64, device=counts.device)
     check(lib.splat_scan_counts(n, pin(counts), ptr(offsets), ptr(total), ptr(ws),
                                 ws.numel(), _stream(counts)), "scan_counts")
-    return offsets, int(total.item())
+    value = int(total.item())
+    if value > 2**31 - 1:
+        nv.device_error(counts.device)  # clears the -4 this call recorded
+        raise nv.SplatError(f"scan_counts: total {value} exceeds the int32 offsets")
+    return offsets, value
 
 
 # pair-count capacity of the last binning per (n, width, height, tile mode,
@@ -452,6 +456,18 @@ class BinPlan:
         return ids
 
 
+_DEVICE_ERRORS = {-3: "a bounded device wait expired (look-back timeout)",
+                  -4: "a count total exceeded INT32_MAX",
+                  -6: "a device guard met an out-of-range index (inconsistent input)"}
+
+
+def raise_device_error(code: int) -> None:
+    """Raise SplatError for a non-zero device error word: the binning of this
+    call (or the kernels queued since the last read) cannot be trusted."""
+    if code:
+        raise nv.SplatError(f"device error {code}: {_DEVICE_ERRORS.get(code, 'unknown code')}")
+
+
 def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
                       camera_status: list | None = None, tile_mode: str = "radius",
                       host_reads: list[Tensor] | None = None):
@@ -474,6 +490,14 @@ def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
         parts = [codes_dev] + parts
     extra = [t.reshape(1).to(torch.int64) for t in (host_reads or [])]
     parts = parts + extra
+    # the device error word (bounded waits that expired, guards that met an
+    # out-of-range index) rides along in the same read and is reset behind it
+    err_word = None
+    if plans:
+        err_word = torch.empty(1, dtype=torch.int32, device=plans[0].ranges.device)
+        check(lib.splat_device_error_read(ptr(err_word), nv.stream(err_word.device)),
+              "device_error_read")
+        parts = parts + [err_word.to(torch.int64)]
     values: list = []
     keys = [(p.n, width, height, p.mode, v) for v, p in enumerate(plans)]
     if parts:
@@ -491,6 +515,8 @@ def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
                 p.emit_early(capacity)
         ready.synchronize()
         values = host.tolist()
+    if err_word is not None:
+        raise_device_error(int(values.pop()))
     raise_camera_errors(values[:ncodes])
     counts = values[ncodes:ncodes + len(plans)]
     bins = []
@@ -505,7 +531,7 @@ def bin_and_sort_many(states: list[ProjectedGaussians], width: int, height: int,
 
 def bin_and_sort(state: ProjectedGaussians, width: int, height: int,
                  tile_mode: str = "radius") -> dict[str, Tensor]:
-    """splatting/binning.py:171-217: point_list and ranges.  state.tile_counts
+    """splatting/binning.py:72-117: point_list and ranges.  state.tile_counts
     must come from the projection with the same tile_mode."""
     return bin_and_sort_many([state], width, height, tile_mode=tile_mode)[0]
 

@@ -13,14 +13,14 @@ size for point_list, which is what the reference's `.item()` read
 (primitives/tiling.py:64) becomes in a traced graph.
 
 Operator <- reference code it stands for:
-  cameras_prepare     splatting/cameras.py:133-188 (camera_kernels.py:11-66)
+  cameras_prepare     splatting/cameras.py:29-85 (camera_kernels.py:11-66)
   project             gs3d/projection.py:309-354 (tile counts for tile_mode)
   project_backward    gs3d/projection.py:357-428
   project_views       gs3d/api.py:132-189 (the per-camera projection loop, one launch)
   project_views_backward  the per-camera backward calls of that loop, summed
   sh_forward          primitives/spherical_harmonics.py:18-59 (sh.py:44-79)
   sh_backward         primitives/spherical_harmonics.py:61-101 (sh.py:82-138)
-  bin_and_sort        splatting/binning.py:171-217
+  bin_and_sort        splatting/binning.py:72-117
   render              gs3d/render.py:359-406 (features + a constant alpha channel)
   render_backward     gs3d/render.py:409-463
   rade_project        rade/projection.py:422-472 (ray planes, normals, radial depths)

@@ -32,7 +32,24 @@ unsigned long long splat_launch_count(void);
  * the stream).  *code is 0 when no wait expired. */
 int splat_device_error(int* code, void* stream);
 
-/* splatting/cameras.py:133-188 _PrepareCameras.forward -> camera_kernels.py:11-66.
+/* No counterpart in the reference (Warp reports no device-side errors).
+ * Queues, on stream, a copy of the device error word into device_dst (one
+ * device int32) followed by its reset to zero; no host synchronisation, so a
+ * caller can fold the word into a read it already makes.  Codes: -3 a bounded
+ * wait expired, -4 a count total above INT32_MAX, -6 a guard met an
+ * out-of-range index. */
+int splat_device_error_read(int* device_dst, void* stream);
+
+/* No counterpart in the reference; test support.  One thread runs the
+ * decoupled look-back of tile 1 over status[0..1] (device uint32, zeroed by
+ * the caller: never published) with spin_limit polls (at most 2^20): the
+ * wait expires, the device error word receives -3 and the kernel returns,
+ * writing the partial prefix to *out.  Shows on a GPU that an expired wait
+ * ends and is reported. */
+int splat_test_lookback_expiry(const unsigned* status, unsigned spin_limit, unsigned* out,
+                               void* stream);
+
+/* splatting/cameras.py:29-85 _PrepareCameras.forward -> camera_kernels.py:11-66.
  * views (C,4,4), Ks (C,3,3) -> full (C,4,4), inverse/centers when
  * with_centers (C,4,4)/(C,3), errors (C) with the reference's codes
  * 1 (skewed K), 2 (non-finite or non-positive focal), 3 (singular view). */
@@ -40,7 +57,7 @@ int splat_cameras_prepare(int count, const float* views, const float* Ks, int wi
                           int with_centers, float* full, float* inverse, float* centers,
                           int* errors, void* stream);
 
-/* splatting/cameras.py:190-221 _PrepareCameras.backward -> camera_kernels.py:69-106.
+/* splatting/cameras.py:86-115 _PrepareCameras.backward -> camera_kernels.py:69-106.
  * grad_full (C,4,4) or NULL, grad_centers (C,3) or NULL -> grad_views (C,4,4). */
 int splat_cameras_backward(int count, const float* Ks, const float* grad_full, int width,
                            int height, const float* inverse, const float* grad_centers,
@@ -166,7 +183,10 @@ int splat_sh_backward(int n, int degree, int sh_k, const float* sh, const float*
                       float* grad_sh, float* grad_dirs, void* stream);
 
 /* primitives/tiling.py:57-64 scan_counts: inclusive int32 offsets of counts
- * (n); *total (device int64) receives the sum. */
+ * (n); *total (device int64, may be NULL) receives the sum, formed in 64 bits
+ * so that it never wraps.  A sum above INT32_MAX does not fit the int32
+ * offsets: the device error word (splat_device_error) then reads -4 and the
+ * offsets of that call are not valid. */
 size_t splat_scan_workspace_bytes(int n);
 int splat_scan_counts(int n, const int* counts, int* offsets, long long* total, void* workspace,
                       size_t workspace_bytes, void* stream);
@@ -185,11 +205,14 @@ int splat_scan_counts(int n, const int* counts, int* offsets, long long* total, 
  * the array, so calls that overlap on the GPU (different streams, or
  * different host threads without ordering) race; serialise them on one
  * stream.  Each call rewrites the scratch it reads, so nothing needs
- * clearing between calls.  Results are identical to splat_scan_counts. */
+ * clearing between calls.  Results are identical to splat_scan_counts,
+ * including the 64-bit total and the -4 device error above INT32_MAX.  The
+ * cached address belongs to the device's current context: after a
+ * cudaDeviceReset in the same process, do not call this entry again. */
 int splat_scan_counts_static(int n, const int* counts, int* offsets, long long* total,
                              void* stream);
 
-/* splatting/binning.py:171-217 bin_and_sort, split in two calls around the
+/* splatting/binning.py:72-117 bin_and_sort, split in two calls around the
  * one host read of the pair count that the reference also makes
  * (primitives/tiling.py:64).  tile_mode as for the projection (conics are
  * required for modes 1 and 2; tiles must be the projection's counts for the
@@ -226,7 +249,7 @@ int splat_tile_order(const int* ranges, int tiles, int* order, void* stream);
 /* gs3d/render.py:359-406 render -> evaluate :41-125.  Blended channels are
  * feat_a's ch_a columns (row stride stride_a), then feat_b's ch_b columns,
  * then (append_one) a constant 1 -- the reference's cat([features, extras,
- * ones]) of gs3d/autograd.py:306-311 without materialising it.
+ * ones]) of gs3d/autograd.py:42-46 without materialising it.
  * background (channels).  image[pixel*pix_stride + c*ch_stride]; planar
  * (C,H,W) is pix_stride=1, ch_stride=H*W; interleaved (H,W,C) is
  * pix_stride=C, ch_stride=1.  alpha_image (H,W), when not NULL (append_one

@@ -263,7 +263,7 @@ int to_int(float v) {
 
 int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
 
-// primitives/sh.py:142-196 evaluate_sh, in its own term order: constants
+// primitives/sh.py:141-180 evaluate_sh, in its own term order: constants
 // times direction products first, then times the coefficient, each term
 // added or subtracted in turn, plus 0.5.
 void evaluate_sh(const float* coeffs, int degree, const float mean[3], const float camera[3],

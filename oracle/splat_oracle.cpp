@@ -126,7 +126,7 @@ float splat_logf(float x) {
 
 // ---- GLM-order geometry (splatting/math.py, primitives/math.py) --------
 
-// splatting/math.py:54-64 reference_matmul
+// splatting/math.py:31-42 reference_matmul
 void ref_matmul(const float a[3][3], const float b[3][3], float out[3][3]) {
   float r[3][3];
   for (int row = 0; row < 3; ++row)
@@ -143,7 +143,7 @@ void transpose3(const float a[3][3], float out[3][3]) {
   std::memcpy(out, r, sizeof(r));
 }
 
-// splatting/math.py:67-70 point_row
+// splatting/math.py:44-47 point_row
 inline float point_row(const float* m, int row, const float p[3]) {
   const float xy = std::fmaf(m[row * 4 + 0], p[0], m[row * 4 + 1] * p[1]);
   return std::fmaf(m[row * 4 + 2], p[2], xy) + m[row * 4 + 3];
@@ -799,7 +799,7 @@ long long oracle_scan_counts(int n, const int* counts, int* offsets) {
   return total;
 }
 
-// splatting/binning.py:116-137 duplicate, primitives/tiling.py:67-100
+// splatting/binning.py:16-37 duplicate, primitives/tiling.py:67-100
 // sort_tile_pairs (stable radix sort of (tile<<32 | depth bits, id) pairs)
 // and primitives/tiling.py:39-54 identify_ranges.  ranges: (T, 2), written
 // in full (zeros for empty tiles); keys_out/ids_out hold M entries.

@@ -1,7 +1,7 @@
 """Generate golden vectors from dsl_splat's own gs3d kernels (test infrastructure).
 
-Runs in a container that has the reference checkout (default
-/root/reference, or argv[1]); the committed .npz files are what the tests
+Runs where a dsl_splat checkout is available (its root as argv[1] or in the
+DSL_SPLAT_REFERENCE environment variable); the committed .npz files are what the tests
 read, so nothing at test time needs the reference.  warp-lang is absent, so
 the reference modules are imported with warp_shim registered as `warp` (see
 that module for exactly what is emulated and the one substitution, exp).
@@ -12,7 +12,7 @@ Kernels executed (reference file:line):
   gs3d/projection.py:89-164           project (tile_mode "radius")
   primitives/sh.py:44-79, 82-138      SH forward / backward kernels
   splatting/metadata.py:12-31         _prepare
-  splatting/binning.py:116-137        duplicate
+  splatting/binning.py:16-37        duplicate
   primitives/tiling.py:39-54          identify_ranges
   gs3d/render.py:36-208               render (forward blend, 256-thread blocks)
   gs3d/render.py:211-356              backward (reverse blend, 256-thread blocks)
@@ -23,7 +23,7 @@ Also: gs3d/render.py:36-208 with statistics.py:47-73's observer and eight
 channels (wide_*.npz); and the RaDe-GS path (rade_*.npz):
   rade/projection.py:194-260          project (ray planes, normals, radial depth,
                                       kernel_size dilation)
-  splatting/binning.py:116-137        duplicate with the radial depths
+  splatting/binning.py:16-37        duplicate with the radial depths
   rade/render.py:99-322               render (colour, depth, median, normals)
   rade/render.py:325-547              backward (warp-reduced atomics)
 
@@ -165,7 +165,7 @@ def golden_case(ref, name, scene: dict, seed: int):
     out.update(meta_means2d=m2d, meta_opacities=mop, meta_conics=mcon)
 
     # primitives/tiling.py:57-64 (Warp array_scan, inclusive) and
-    # splatting/binning.py:116-137 duplicate
+    # splatting/binning.py:16-37 duplicate
     offsets = np.cumsum(tiles, dtype=np.int64).astype(np.int32)
     m = int(offsets[-1]) if n else 0
     keys = np.zeros(2 * m, np.uint64)
@@ -180,7 +180,7 @@ def golden_case(ref, name, scene: dict, seed: int):
     ws.launch(ref["tiling"].identify_ranges, m, [A(keys_sorted), A(ranges)])
     out.update(offsets=offsets, keys=keys_sorted, ids=ids_sorted, ranges=ranges)
 
-    # gs3d/autograd.py:306-315: features = cat(colours, ones); black background
+    # gs3d/autograd.py:42-46: features = cat(colours, ones); black background
     feats = np.concatenate([colors, np.ones((n, 1), np.float32)], axis=1)
     C = feats.shape[1]
     bg = np.zeros(C, np.float32)
@@ -341,7 +341,7 @@ def rade_case(ref, name, scene: dict, seed: int, kernel_size: float, extra: int)
     bg = rng.uniform(0.0, 1.0, C).astype(np.float32)
     out.update(colors=colors, extras=extras, background=bg)
 
-    # splatting/binning.py:116-137 with the radial sort distance
+    # splatting/binning.py:16-37 with the radial sort distance
     offsets = np.cumsum(tiles, dtype=np.int64).astype(np.int32)
     m = int(offsets[-1]) if n else 0
     keys = np.zeros(2 * m, np.uint64)
@@ -725,7 +725,10 @@ def scenes():
 
 def main():
     args = [a for a in sys.argv[1:] if not a.startswith("--")]
-    ref_root = args[0] if args else "/root/reference"
+    ref_root = args[0] if args else os.environ.get("DSL_SPLAT_REFERENCE")
+    if not ref_root:
+        raise SystemExit("usage: make_golden.py <dsl_splat checkout> [--...-only] "
+                         "(or set DSL_SPLAT_REFERENCE)")
     ref = load_reference(ref_root)
     base = scenes()
     only = {a for a in sys.argv[1:]

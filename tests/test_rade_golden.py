@@ -160,7 +160,7 @@ def test_rade_vjp_oracle_matches_finite_differences_without_custom_adjoints():
 
 def test_rade_api_validation_cpu():
     """Argument checks run before any device work (rade/api.py:82-99,
-    rade/gsplat.py:17-79, rade/filtering.py:33-39)."""
+    rade/gsplat.py:17-79, rade/filtering.py:7-26)."""
     from dsl_splat_b200 import rade
     from dsl_splat_b200.rade.gsplat import rasterization
 

@@ -186,6 +186,61 @@ def _contribution(shape, rank, view, step):
 SYNC_SHAPES = [(101, 3), (101, 4), (101, 3), (101,), (101, 16, 3)]
 
 
+def _zero_view_worker(rank, world, port, outdir, buckets):
+    """One camera, two ranks: rank 0 renders the view (driven here as the
+    projection backward drives GradientSync), rank 1 has no local view and
+    only calls wait(); both must end with rank 0's gradients, and the
+    plain all-reduce of parameter gradients must line up the same way."""
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                      WORLD_SIZE=str(world))
+    from dsl_splat_b200 import sharding
+    sharding.init_process_group("gloo", timeout_s=30.0)
+    assert sharding.local_cameras(1, rank, world) == ([0] if rank == 0 else [])
+    params = [torch.zeros(s, requires_grad=True) for s in SYNC_SHAPES]
+    sync = sharding.GradientSync(*params, group=dist.group.WORLD, buckets=buckets)
+    with sync:
+        if rank == 0:
+            sync.register_view()
+            bufs, _, last = sync.begin_view()
+            for buf, shape in zip(bufs.values(), SYNC_SHAPES):
+                buf.copy_(_contribution(shape, 0, 0, 0))
+            for lo, hi in sharding.bucket_bounds(SYNC_SHAPES[0][0], sync.buckets):
+                sync.reduce_range(lo, hi)
+            sync.finish()
+    sync.wait()
+    plain = [torch.zeros(s, requires_grad=True) for s in SYNC_SHAPES]
+    if rank == 0:
+        for p, shape in zip(plain, SYNC_SHAPES):
+            p.grad = _contribution(shape, 0, 1, 0)
+    sharding.allreduce_parameter_grads(plain, group=dist.group.WORLD)
+    torch.save({"sync": [p.grad.clone() for p in params],
+                "plain": [p.grad.clone() for p in plain]},
+               os.path.join(outdir, f"rank{rank}.pt"))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("buckets", [1, 3])
+def test_rank_without_views_joins_reductions(tmp_path, buckets):
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_zero_view_worker, args=(r, 2, port, str(tmp_path), buckets))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=180)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("rank did not finish (collectives did not line up)")
+    for r in range(2):
+        res = torch.load(os.path.join(tmp_path, f"rank{r}.pt"))
+        for got, shape in zip(res["sync"], SYNC_SHAPES):
+            assert torch.equal(got, _contribution(shape, 0, 0, 0))
+        for got, shape in zip(res["plain"], SYNC_SHAPES):
+            assert torch.equal(got, _contribution(shape, 0, 1, 0))
+
+
 def _sync_worker(rank, world, port, outdir, buckets):
     sys.path.insert(0, ROOT)
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
