@@ -109,6 +109,14 @@ def lib():
             _int, _f32p, _f32p, _f32p, _vp, _i32p, _f32p, _f32p, _f32p, _f32p, _int, _int, _flt,
             _flt, _int, _f32p, _f32p, _vp, _int, _int, _vp, _f32p, _f32p]
         L.oracle_aaa_camera_backward.restype = None
+        L.oracle_aaa_render.argtypes = [
+            _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _int, _f32p, _f32p,
+            _i32p]
+        L.oracle_aaa_render.restype = _int
+        L.oracle_aaa_render_backward.argtypes = [
+            _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _int, _f32p, _f32p,
+            _f32p, _f64p, _f64p, _f64p, _vp, _vp]
+        L.oracle_aaa_render_backward.restype = _int
         L.oracle_num_threads.restype = _int
         L.oracle_set_num_threads.argtypes = [_int]
         _lib = L
@@ -533,3 +541,65 @@ def aaa_camera_backward(means, quats, scales, radii, effective_opacity, view, pr
         _ptr(sh_c), sh_c.shape[1] if sh_c is not None else 0, int(sh_degree), _ptr(cl),
         _c(up_colors), rows)
     return rows
+
+
+def aaa_sort(keys, values, tiles_total):
+    """primitives/tiling.py:67-100 on AAA keys: a stable sort of the pairs on
+    key bits [0, 32 + bit_length(T)) (Warp's radix_sort_pairs end_bit; the
+    padding tile 0xffffffff then sorts after every real tile), and the tile
+    ranges of identify_ranges (:39-54), which skips the padding tile."""
+    keys = np.asarray(keys, np.uint64)
+    end_bit = 32 + int(tiles_total).bit_length()
+    masked = keys & np.uint64((1 << end_bit) - 1)
+    order = np.argsort(masked, kind="stable")
+    skeys, svals = keys[order], np.asarray(values, np.int32)[order]
+    ranges = np.zeros((tiles_total, 2), np.int32)
+    tile = (skeys >> np.uint64(32)).astype(np.int64)
+    real = tile != 0xFFFFFFFF
+    if real.any():
+        idx = np.nonzero(real)[0]
+        t = tile[idx]
+        starts = np.r_[True, t[1:] != t[:-1]]
+        ends = np.r_[t[1:] != t[:-1], True]
+        ranges[t[starts], 0] = idx[starts]
+        ranges[t[ends], 1] = idx[ends] + 1
+    return skeys, svals, ranges
+
+
+def aaa_render(width, height, ranges, points, transforms, opacity, colors, bg, cull=True):
+    """aaa/render_hierarchical_warp.py:599-691 (aaa_render_oracle.cpp): the
+    HIER 64/8/4 blend.  Returns image (C, H, W), final_t (H, W) and the
+    evaluated-sample counts (H, W)."""
+    colors = _c(colors)
+    C = colors.shape[1]
+    image = np.zeros((C, height, width), np.float32)
+    final_t = np.zeros((height, width), np.float32)
+    contrib = np.zeros((height, width), np.int32)
+    assert lib().oracle_aaa_render(
+        int(width), int(height), C, _c(ranges, np.int32), _c(points, np.int32),
+        _c(transforms), _c(opacity), colors, _c(bg), int(bool(cull)), image, final_t,
+        contrib) == 0
+    return image, final_t, contrib
+
+
+def aaa_render_backward(width, height, ranges, points, transforms, opacity, colors, bg, image,
+                        final_t, pixel_grad, cull=True, screen=False, absgrad=False):
+    """aaa/backward_render.py:75-248 (aaa_render_oracle.cpp): float64 sums of
+    the replay's gradients -- transforms (n, 16) in the reference's transposed
+    layout, opacity (n), colours (n, C), and the optional screen-translation
+    statistics (n, 2) and their absolute sums (n, 2)."""
+    colors = _c(colors)
+    n, C = colors.shape
+    out = dict(transforms=np.zeros((n, 16)), opacity=np.zeros(n), colors=np.zeros((n, C)))
+    scr = np.zeros((n, 2)) if screen else None
+    sabs = np.zeros((n, 2)) if screen and absgrad else None
+    assert lib().oracle_aaa_render_backward(
+        int(width), int(height), C, _c(ranges, np.int32), _c(points, np.int32),
+        _c(transforms), _c(opacity), colors, _c(bg), int(bool(cull)), _c(image), _c(final_t),
+        _c(pixel_grad), out["transforms"], out["opacity"], out["colors"], _ptr(scr),
+        _ptr(sabs)) == 0
+    if screen:
+        out["screen"] = scr
+    if absgrad:
+        out["screen_abs"] = sabs
+    return out

@@ -593,6 +593,100 @@ def aaa_scenes():
     ]
 
 
+def aaa_render_case(name, scene: dict, channels: int, cull: bool, seed: int) -> dict:
+    """The AAA HIER 64/8/4 blend and its replay backward, the reference's own
+    Warp kernels, on one view of the load-balanced path:
+      aaa/preprocess3d.py:17-245 + aaa/cooperative_culling.py:152-192 +
+      aaa/binning_native.py:7-135 (through aaa_case / aaa_duplicate),
+      the 64-bit key sort restated (stable, end_bit = 32 + bit_length(T)),
+      primitives/tiling.py:39-54              identify_ranges,
+      aaa/render_hierarchical_warp.py:599-691 render (C channels),
+      aaa/backward_render.py:75-137           replay (screen and absgrad
+                                              statistics on).
+    Features are seeded U[0,1] with a constant last channel (aaa/api.py:
+    67-71 appends ones), the background seeded U[0,1] (0 for the constant
+    channel), the upstream image gradient seeded N(0,1)."""
+    flags = dict(ewa=True, new_aabb=True, near_clipping=False, tile_culling=True,
+                 complete=False, cooperative=True)
+    pre = aaa_case("coop", scene, flags, False, False)
+    W, H = int(pre["width"]), int(pre["height"])
+    gx, gy = (W + 15) // 16, (H + 15) // 16
+    T = gx * gy
+    keys, values = pre["dup_keys"], pre["dup_values"]
+    end_bit = 32 + T.bit_length()
+    order = np.argsort(keys & np.uint64((1 << end_bit) - 1), kind="stable")
+    skeys, ids = keys[order], values[order].astype(np.int32)
+    tiling = importlib.import_module("dsl_splat.primitives.tiling")
+    ranges = np.zeros((T, 2), np.int32)
+    wp = sys.modules["warp"]
+    if len(skeys):
+        ws.launch(tiling.identify_ranges, len(skeys), [A(skeys), A(ranges)])
+    n = len(pre["means"])
+    gen = np.random.default_rng(seed)
+    feats = gen.uniform(0, 1, (n, channels)).astype(np.float32)
+    feats[:, -1] = 1.0
+    bg = gen.uniform(0, 1, channels).astype(np.float32)
+    bg[-1] = 0.0
+    warp_render = importlib.import_module("dsl_splat.aaa.render_hierarchical_warp")
+    backward = importlib.import_module("dsl_splat.aaa.backward_render")
+    ftype = wp.types.vector(channels, wp.float32)
+    image = np.zeros(channels * H * W, np.float32)
+    final_t = np.zeros(H * W, np.float32)
+    contrib = np.zeros(H * W, np.int32)
+    transforms = pre["transforms"].astype(np.float32)
+    opacity = pre["opacity"].astype(np.float32)
+    t0 = time.time()
+    kernel = warp_render._make_kernel(cull, channels)
+    ws.launch(kernel, 256 * T, [W, H, A(ranges.reshape(-1)), A(ids), A(transforms, wp.mat44),
+                                A(opacity), A(feats, ftype), A(bg), A(image), A(final_t),
+                                A(contrib)], block=256)
+    t1 = time.time()
+    up = gen.standard_normal(channels * H * W).astype(np.float32)
+    g_tr = np.zeros(n * 16, np.float32)
+    g_op = np.zeros(n, np.float32)
+    g_col = np.zeros(n * channels, np.float32)
+    g_scr = np.zeros(n * 2, np.float32)
+    g_abs = np.zeros(n * 2, np.float32)
+    replay = backward._make_backward(cull, channels, True, True)
+    ws.launch(replay, 256 * T, [W, H, A(ranges.reshape(-1)), A(ids), A(feats, ftype), A(image),
+                                A(final_t), A(contrib), A(transforms, wp.mat44), A(opacity),
+                                A(bg), A(up), A(g_tr), A(g_op), A(g_col), A(g_scr), A(g_abs)],
+              block=256)
+    print(f"aaa_render_{name}: {W}x{H} C={channels} cull={cull} pairs={len(ids)} "
+          f"max contributors={contrib.max()} forward {t1 - t0:.1f}s "
+          f"backward {time.time() - t1:.1f}s")
+    return dict(width=W, height=H, channels=channels, cull=cull, ranges=ranges, ids=ids,
+                transforms=transforms, opacity=opacity, features=feats, background=bg,
+                image=image.reshape(channels, H, W), final_t=final_t.reshape(H, W),
+                contributors=contrib.reshape(H, W), upstream=up.reshape(channels, H, W),
+                grad_transforms=g_tr.reshape(n, 16), grad_opacity=g_op,
+                grad_features=g_col.reshape(n, channels), grad_screen=g_scr.reshape(n, 2),
+                grad_screen_abs=g_abs.reshape(n, 2))
+
+
+def aaa_render_scenes():
+    """Render cases: the sparse preprocessing scene, and a dense one (700
+    Gaussians on a 44x36 image, ragged tiles) whose 4x4 tails overflow, so
+    every queue path (tail drains, mid merges, full heads, early
+    termination) runs."""
+    from dsl_splat_b200.scenes import intrinsics, look_at
+    base = aaa_scenes()[0][1]
+    g = torch.Generator().manual_seed(777)
+    n = 700
+    means = (torch.rand(n, 3, generator=g) * 2 - 1) * torch.tensor([1.2, 1.0, 0.8])
+    means[:, 2] += 4.0
+    scales = torch.exp(torch.randn(n, 3, generator=g) * 0.4 - 2.0)
+    opac = torch.sigmoid(torch.randn(n, generator=g) + 0.5)
+    dense = dict(width=44, height=36, sh_degree=3, means=means.numpy(), scales=scales.numpy(),
+                 quats=torch.randn(n, 4, generator=g).numpy(), opacities=opac.numpy(),
+                 sh=np.zeros((n, 16, 3), np.float32), filters=np.zeros(n, np.float32),
+                 viewmat=look_at(torch.tensor([0.2, -0.1, -1.0]),
+                                 torch.tensor([0.0, 0.0, 4.0])).numpy(),
+                 K=intrinsics(40.0, 38.0, 21.5, 17.5).numpy())
+    return [("sparse_c4", base, 4, True, 11), ("dense_c7", dense, 7, True, 12),
+            ("dense_nocull_c4", dense, 4, False, 13)]
+
+
 def tile_mode_case(ref, name, scene: dict) -> dict:
     """Projection tile counts and binning for tile_mode snugbox and accutile
     (gs3d/projection.py:150-162, splatting/intersections.py:45-218,
@@ -732,7 +826,8 @@ def main():
     ref = load_reference(ref_root)
     base = scenes()
     only = {a for a in sys.argv[1:]
-            if a in ("--tile-modes-only", "--wide-only", "--rade-only", "--aaa-only")}
+            if a in ("--tile-modes-only", "--wide-only", "--rade-only", "--aaa-only",
+                     "--aaa-render-only")}
     if not only:
         for i, (name, scene) in enumerate(base.items()):
             data = golden_case(ref, name, scene, seed=100 + i)
@@ -749,6 +844,10 @@ def main():
         for name, scene, flags, use_sh, with_filter in aaa_scenes():
             data = aaa_case(name, scene, flags, use_sh, with_filter)
             np.savez_compressed(os.path.join(HERE, f"aaa_{name}.npz"), **data)
+    if not only or "--aaa-render-only" in only:
+        for name, scene, channels, cull, seed in aaa_render_scenes():
+            data = aaa_render_case(name, scene, channels, cull, seed)
+            np.savez_compressed(os.path.join(HERE, f"aaa_render_{name}.npz"), **data)
     if only and "--tile-modes-only" not in only:
         return
     for name, scene in tile_mode_scenes(base).items():

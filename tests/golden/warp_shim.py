@@ -159,6 +159,8 @@ class Mat:
             self.m = [[_wp_f32(0) for _ in range(C)] for _ in range(R)]
         elif len(args) == 1 and isinstance(args[0], Mat):
             self.m = [list(r) for r in args[0].m]
+        elif len(args) == 1:  # Warp fills every entry with the scalar
+            self.m = [[_wp_f32(args[0]) for _ in range(C)] for _ in range(R)]
         else:
             assert len(args) == R * C
             self.m = [[_wp_f32(args[r * C + c]) for c in range(C)] for r in range(R)]
@@ -496,6 +498,9 @@ def _c_type(ann):
 
 _native_libs: dict = {}
 _BLOCK_NATIVES = {}
+# natives of one reference module (name clashes across modules: the AAA
+# renderer's shared_ids / any_active differ from gs3d's)
+_MODULE_NATIVES = {}
 
 
 def _compile_native(name, snippet, params, ret):
@@ -548,6 +553,9 @@ def _compile_native(name, snippet, params, ret):
 def func_native(snippet, adj_snippet=None):
     def deco(fn):
         name = fn.__name__
+        qualified = (fn.__module__, name)
+        if qualified in _MODULE_NATIVES:
+            return _MODULE_NATIVES[qualified]
         if name in _BLOCK_NATIVES:
             return _BLOCK_NATIVES[name]
         hints = {k: v for k, v in fn.__annotations__.items()}
@@ -599,11 +607,23 @@ class _Block:
         warps = (size + 31) // 32
         self.warp_barriers = [threading.Barrier(min(32, size - 32 * w)) for w in range(warps)]
         self.warp_slots = [[None] * 32 for _ in range(warps)]
+        self.group_barriers: dict = {}
+
+    def group_barrier(self, warp: int, mask: int):
+        """The barrier of the lanes of `mask` in `warp` (__syncwarp(mask))."""
+        key = (warp, mask)
+        with self.lock:
+            if key not in self.group_barriers:
+                self.group_barriers[key] = threading.Barrier(bin(mask).count("1"))
+            return self.group_barriers[key]
 
     def abort(self):
         self.barrier.abort()
         for b in self.warp_barriers:
             b.abort()
+        with self.lock:
+            for b in self.group_barriers.values():
+                b.abort()
 
 
 def _block() -> _Block:
@@ -672,6 +692,16 @@ def _shared_flat(kind, size):
     return make
 
 
+def _shared_flat_int(kind, size):
+    def make():
+        b = _block()
+        with b.lock:
+            if kind not in b.shared:
+                b.shared[kind] = Array(np.zeros(size, np.int32))
+            return b.shared[kind]
+    return make
+
+
 def _shared(kind, dtype):
     def make():
         b = _block()
@@ -695,6 +725,60 @@ def _shared_rows(kind, rows, dtype):
     return make
 
 
+# ---- masked warp intrinsics of the AAA HIER renderer ----------------------------------
+# aaa/render_warp_intrinsics.py: __syncwarp(mask), __any_sync, __popc(__ballot_sync)
+# and __shfl_sync(mask, v, src, width) among the lanes of `mask` (all of which
+# reach the call, as the renderer guarantees), through the warp's slots.
+
+def _group_exchange(mask, value):
+    b = _block()
+    w, lane = _state.lane // 32, _state.lane % 32
+    bar = b.group_barrier(w, int(mask))
+    b.warp_slots[w][lane] = value
+    bar.wait()
+    values = list(b.warp_slots[w])
+    bar.wait()
+    return values
+
+
+def _masked_sync(mask):
+    b = _block()
+    b.group_barrier(_state.lane // 32, int(mask)).wait()
+
+
+def _masked_any(mask, predicate):
+    m = int(mask)
+    values = _group_exchange(m, bool(predicate))
+    return any(values[l] for l in range(32) if (m >> l) & 1)
+
+
+def _masked_count(mask, predicate):
+    m = int(mask)
+    values = _group_exchange(m, bool(predicate))
+    return sum(1 for l in range(32) if (m >> l) & 1 and values[l])
+
+
+def _masked_shuffle(mask, value, source, width):
+    values = _group_exchange(int(mask), value)
+    lane = _state.lane % 32
+    return values[(lane & ~(int(width) - 1)) + int(source) % int(width)]
+
+
+def _load_matrix(matrices, index):
+    return matrices[int(index)]
+
+
+def _reciprocal(value):
+    return F32(1.0) / F32(value)  # __frcp_rn: the correctly rounded 1/x
+
+
+def _global_atomic_add(values, index, value):
+    with _atomic_lock:
+        previous = F32(values.data[int(index)])
+        values.data[int(index)] = previous + F32(value)
+    return previous
+
+
 # @wp.func bodies replaced by an equivalent of the same float32 arithmetic
 # (lane exchange instead of five shuffles each)
 _FUNC_NATIVES = {"sum_lanes": _sum_lanes, "sum_vector_lanes": _sum_vector_lanes}
@@ -711,6 +795,17 @@ def _install_block_natives():
     _BLOCK_NATIVES["shared_features"] = _shared_flat("features", 256 * 32)
     _BLOCK_NATIVES["shared_geometry"] = _shared_rows("geometry", 512, vector(3))
     _BLOCK_NATIVES["any_active"] = _any_active
+    hier = "dsl_splat.aaa.render_warp_intrinsics"
+    _MODULE_NATIVES[(hier, "shared_depths")] = _shared_flat("hier_depths", 1536)
+    _MODULE_NATIVES[(hier, "shared_ids")] = _shared_flat_int("hier_ids", 1536)
+    _MODULE_NATIVES[(hier, "sync")] = _masked_sync
+    _MODULE_NATIVES[(hier, "any_active")] = _masked_any
+    _MODULE_NATIVES[(hier, "count_active")] = _masked_count
+    _MODULE_NATIVES[(hier, "shuffle_int")] = _masked_shuffle
+    _MODULE_NATIVES[(hier, "shuffle_float")] = _masked_shuffle
+    _MODULE_NATIVES[(hier, "load_matrix")] = _load_matrix
+    _MODULE_NATIVES[("dsl_splat.aaa.render_warp_geometry", "reciprocal")] = _reciprocal
+    _MODULE_NATIVES[("dsl_splat.primitives.atomics", "global_atomic_add")] = _global_atomic_add
 
 
 def tid():
@@ -849,6 +944,16 @@ def exp(x):
 
 def isfinite(x):
     return bool(np.isfinite(x))
+
+
+def copysign(x, y):
+    return F32(np.copysign(np.float32(x), np.float32(y)))
+
+
+def cross(a, b):
+    """wp.cross: (a1 b2 - a2 b1, a2 b0 - a0 b2, a0 b1 - a1 b0)."""
+    return a._new([a.v[1] * b.v[2] - a.v[2] * b.v[1], a.v[2] * b.v[0] - a.v[0] * b.v[2],
+                   a.v[0] * b.v[1] - a.v[1] * b.v[0]])
 
 
 def dot(a, b):
@@ -1013,7 +1118,8 @@ def make_module() -> types.ModuleType:
                  "array3d", "tid", "static", "min", "max", "clamp", "sqrt", "ceil", "floor",
                  "abs", "log", "exp", "isfinite", "dot", "length", "transpose", "determinant",
                  "inverse", "atomic_add", "uint64", "uint32", "float64", "grad", "constant",
-                 "adjoint", "launch", "normalize", "outer", "length_sq", "cw_mul"):
+                 "adjoint", "launch", "normalize", "outer", "length_sq", "cw_mul", "copysign",
+                 "cross"):
         setattr(m, name, getattr(this, name))
     m.float32 = F32
     m.int32 = np.int32

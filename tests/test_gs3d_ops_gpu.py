@@ -58,8 +58,10 @@ def test_gs3d_ops_chain_matches_oracle_and_rasterize():
     ((res.features[0] * gF).sum() + (res.alpha[0] * gA).sum()).backward()
     assert torch.equal(px.features, res.features[0])
     assert torch.equal(px.alpha, res.alpha[0])
-    for name in ("half", "weighted"):
-        assert torch.equal(px.statistics[name], res.statistics[name][0]), name
+    # counts are integers (exact); weighted sums are float32 atomics in
+    # arbitrary order
+    assert torch.equal(px.statistics["half"], res.statistics["half"][0])
+    assert rel_l2(px.statistics["weighted"].cpu(), res.statistics["weighted"][0].cpu()) <= 1e-5
     assert int(px.statistics["half"].sum()) > 0
     for name in p:
         assert rel_l2(p[name].grad.cpu(), q[name].grad.cpu()) <= 1e-4, name
