@@ -81,7 +81,31 @@ SIGNATURES: dict[str, tuple] = {
                                         _I, _I, _P, _I, _I, _P, _I, _P, _I, _P, _I, _P, _I,
                                         _I, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "splat_debug_expf": (_I, [_I, _P, _P, _P, _P]),
+    "splat_aaa_preprocess": (_I, [_P] + [_P] * 12 + [_P]),
+    "splat_aaa_cull_remainder": (_I, [_I, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
+    "splat_aaa_bin_workspace_bytes": (_Z, [_L]),
+    "splat_aaa_bin": (_I, [_I, _L, _P, _P, _P, _P, _P, _P, _I, _I, _P, _Z, _P, _P, _P]),
+    "splat_aaa_emit": (_I, [_I, _L, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
+    "splat_aaa_render": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "splat_aaa_render_backward": (_I, [_I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                       _P, _P, _P, _P, _P, _P]),
+    "splat_aaa_preprocess_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "splat_aaa_camera_backward": (_I, [_P, _P, _P, _P, _P, _P, _P]),
 }
+
+
+class SplatAaaFrame(ctypes.Structure):
+    """include/splat200.h SplatAaaFrame: one AAA view's inputs (device
+    pointers) and switches."""
+
+    _fields_ = [("n", _I), ("width", _I), ("height", _I),
+                ("means", _P), ("scales", _P), ("quats", _P), ("opacities", _P),
+                ("sh", _P), ("sh_k", _I), ("sh_degree", _I), ("filters", _P),
+                ("campos", _P), ("view", _P), ("proj", _P),
+                ("tanfov_x", _F), ("tanfov_y", _F), ("principal_x", _F), ("principal_y", _F),
+                ("scale_modifier", _F), ("focal_x", _F), ("focal_max", _F),
+                ("sort_order", _I), ("ewa", _I), ("new_aabb", _I), ("near_clipping", _I),
+                ("tile_culling", _I), ("complete", _I), ("cooperative", _I)]
 
 
 def _load() -> ctypes.CDLL:

@@ -30,7 +30,8 @@ BUILD_DIR = os.path.join(HERE, "_build")
 SOURCES = {"splat200.cu": ["-fmad=false"],
            "project_backward.cu": ["-fmad=true", "-prec-div=false", "-prec-sqrt=false"]}
 HEADERS = ["splat_common.cuh", "cameras.cuh", "project.cuh", "binning.cuh", "render.cuh",
-           "footprint.cuh", "tile_modes.cuh", "host_runtime.h", "rade.cuh", "rade_project.cuh"]
+           "footprint.cuh", "tile_modes.cuh", "host_runtime.h", "rade.cuh", "rade_project.cuh",
+           "aaa.cuh", "aaa_render.cuh", "aaa_api.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

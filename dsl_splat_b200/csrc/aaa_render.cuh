@@ -1,0 +1,617 @@
+// AAA-Gaussians hierarchical (StopThePop HIER 64/8/4) blend and its replay
+// backward: the B200 kernels for aaa/render_hierarchical_warp.py:105-691
+// (K24) and aaa/backward_render.py:23-137 with aaa/render_adjoint.py:279-352
+// (K27).
+//
+// One 256-thread CTA per 16x16 tile.  Each warp owns two 4x4 pixel regions
+// (one per half warp) and their 64-entry tail queues, and eight 2x2 quads
+// with 8-entry mid queues; every pixel keeps a 4-entry head in registers.
+// The tile's depth-sorted Gaussians arrive in batches of 32 (one per lane):
+// each is culled against and sampled at both regions' centres, the batch is
+// sorted with Batcher's network and merged into the tails; a tail past 32
+// entries drains 16 at a time through its quads' mid queues (sampled at the
+// quad centre) into the pixel heads (sampled at the pixel), and the head's
+// front sample is blended whenever a head is full.  The blend order is the
+// approximate depth order these queues produce, so every comparison, tie
+// rule and barrier of the reference is kept: the queue contents, and with
+// them the images and counts, are bit-identical to the reference's (with
+// the library's exp).  All synchronisation is warp-local (__syncwarp with
+// the warp, half-warp or quad mask), as in the reference.
+//
+// The replay backward runs the same traversal from the start and, per
+// blended sample, derives the colour weight and the alpha gradient from the
+// saved final image and transmittance (front to back: the colour behind a
+// sample is (final - accumulated) / T_next); it adds 13 gradient terms per
+// sample (colour channels, 9 + 3 transform entries, opacity) plus the
+// optional screen-translation statistics with red.global.add.
+//
+// Memory guards the reference does not have: an entry id of -1 never
+// indexes the Gaussian arrays (the reference reads before the array start on
+// degenerate depths, e.g. an infinite one; such entries get depth FLT_MAX,
+// amplitude 0 and colour 0 here).  Scenes with finite depths never reach
+// them.
+#pragma once
+#include "aaa.cuh"
+
+namespace splat {
+namespace aaa {
+
+constexpr float kInf = FLT_MAX;  // the renderer's INF (3.4028234663852886e38)
+constexpr unsigned kFull = 0xffffffffu;
+
+SPLAT_DEV float wp_min(float a, float b) { return a < b ? a : b; }  // wp.min on floats
+
+// ---- aaa/render_warp_geometry.py ------------------------------------------------
+
+SPLAT_DEV float rdot4(const float a[4], const float b[4]) {
+  return (a[0] * b[0] + a[1] * b[1]) + (a[2] * b[2] + a[3] * b[3]);
+}
+
+SPLAT_DEV float rdot3(const float a[3], const float b[3]) { return (a[0] * b[0] + a[1] * b[1]) + a[2] * b[2]; }
+
+// g[r] - g[3] * s, component by component
+SPLAT_DEV void plane_of(const M4& g, int r, float s, float out[4]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) out[k] = g.m[r][k] - g.m[3][k] * s;
+}
+
+// :41-57 closest_ray: the point of the line where planes a and b meet that
+// lies closest to the Gaussian's centre, and its squared distance
+SPLAT_DEV float closest_ray(const float a[4], const float b[4], float pos[4]) {
+  const float d[3] = {a[1] * b[2] - a[2] * b[1], a[2] * b[0] - a[0] * b[2], a[0] * b[1] - a[1] * b[0]};
+  const float m[3] = {a[3] * b[0] - a[0] * b[3], a[3] * b[1] - a[1] * b[3], a[3] * b[2] - a[2] * b[3]};
+  const float dd = rdot3(d, d);
+  const float s[3] = {m[0] / dd, m[1] / dd, m[2] / dd};
+  pos[0] = d[1] * s[2] - s[1] * d[2];
+  pos[1] = d[2] * s[0] - s[2] * d[0];
+  pos[2] = d[0] * s[1] - s[0] * d[1];
+  pos[3] = 1.0f;
+  return rdot3(m, s);
+}
+
+// :60-64 sample: -distance^2 / 2 and the screen depth of the ray of (x, y)
+SPLAT_DEV void ray_sample(const M4& g, float x, float y, float& power, float& depth) {
+  float a[4], b[4], pos[4];
+  plane_of(g, 0, x, a);
+  plane_of(g, 1, y, b);
+  const float sq = closest_ray(a, b, pos);
+  const float g2[4] = {g.m[2][0], g.m[2][1], g.m[2][2], g.m[2][3]};
+  const float g3[4] = {g.m[3][0], g.m[3][1], g.m[3][2], g.m[3][3]};
+  depth = rdot4(g2, pos) * __frcp_rn(rdot4(g3, pos));
+  power = -0.5f * sq;
+}
+
+SPLAT_DEV void rtransform(const M4& g, const float p[4], float out[4]) {
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const float row[4] = {g.m[r][0], g.m[r][1], g.m[r][2], g.m[r][3]};
+    out[r] = rdot4(row, p);
+  }
+}
+
+// :67-120 frustum: half the smallest squared Gaussian-space distance from
+// the centre to the frustum of the w x h pixel rectangle at (x, y)
+SPLAT_DEV float region_frustum(const M4& g, float x, float y, float w, float h) {
+  const float start[3] = {x, y, -1.0f}, extent[3] = {w, h, 2.0f};
+  auto inside = [&](const float p[4], int axis) {
+    const float delta = p[axis] - start[axis] * p[3];
+    return delta > 0.0f && delta < extent[axis] * p[3];
+  };
+  const float mean[4] = {g.m[0][3], g.m[1][3], g.m[2][3], g.m[3][3]};
+  float best = FLT_MAX;
+  if (inside(mean, 0) && inside(mean, 1) && inside(mean, 2)) {
+    best = 0.0f;
+  } else {
+    const float dx = copysignf(w * 0.5f, (mean[0] - x * mean[3]) - w * 0.5f * mean[3]);
+    const float dy = copysignf(h * 0.5f, (mean[1] - y * mean[3]) - h * 0.5f * mean[3]);
+    float ax[4], ay[4], other[4], pos[4], screen[4];
+    plane_of(g, 0, x + w * 0.5f + dx, ax);
+    plane_of(g, 1, y + h * 0.5f + dy, ay);
+    auto test_plane = [&](const float a[4], int other_axis) {
+      const float norm = a[3] / ((a[0] * a[0] + a[1] * a[1]) + a[2] * a[2]);
+      const float p[4] = {-a[0] * norm, -a[1] * norm, -a[2] * norm, 1.0f};
+      rtransform(g, p, screen);
+      const float value = a[3] * norm;
+      if (value < best && inside(screen, other_axis) && inside(screen, 2)) best = value;
+    };
+    auto test_edge = [&](const float a[4], const float b[4]) {
+      const float sq = closest_ray(a, b, pos);
+      rtransform(g, pos, screen);
+      if (sq < best && inside(screen, 2)) best = sq;
+    };
+    test_plane(ax, 1);
+    test_plane(ay, 0);
+    test_edge(ax, ay);
+    plane_of(g, 1, y + h * 0.5f - dy, other);
+    test_edge(ax, other);
+    plane_of(g, 0, x + w * 0.5f - dx, other);
+    test_edge(other, ay);
+  }
+  return 0.5f * best;
+}
+
+// ---- kernel state -------------------------------------------------------------------
+
+struct HierParams {
+  int width, height, channels, cull;
+  const int* ranges;        // (T,2)
+  const int* points;        // sorted Gaussian ids
+  const float* transforms;  // (n,4,4), 16-byte aligned
+  const float* opacity;     // (n)
+  const float* colors;      // (n,C)
+  const float* bg;          // (C)
+  const int* tile_order;    // block -> tile schedule, or null
+  // forward outputs: planar (C,H,W), (H,W), (H,W)
+  float* image;
+  float* final_t;
+  int* contributors;
+  // replay inputs (the forward's outputs) and gradients
+  const float* image_in;
+  const float* final_t_in;
+  const float* pixel_grad;  // (C,H,W)
+  float* grad_transforms;   // (n,16), the reference's transposed layout
+  float* grad_opacity;      // (n)
+  float* grad_colors;       // (n,C)
+  float* grad_screen;       // (n,2) or null
+  float* grad_screen_abs;   // (n,2) or null
+};
+
+struct WarpQueues {  // per warp: two 4x4 tails, eight 2x2 mids
+  float tail_d[2][64];
+  int tail_id[2][64];
+  float mid_d[8][8];
+  int mid_id[8][8];
+};
+
+template <int CHP, bool BWD>
+struct HierPixel {
+  bool active;
+  float T;
+  int contributors, tail_count, mid_count, head_count;
+  float hd[4], ha[4], hg[4];
+  int hid[4];
+  float color[CHP];
+  float gradient[BWD ? CHP : 1], final_color[BWD ? CHP : 1];
+  float final_T, bg_grad;
+};
+
+// render_adjoint.py:285-351 accumulate: one accepted sample's gradients
+template <bool SCREEN, bool ABS>
+SPLAT_DEV void accumulate_ray_gradient(const HierParams& p, int id, float x, float y, float gaussian,
+                                       float alpha_gradient) {
+  const M4 g = load_m4(p.transforms, id);
+  float a[4], b[4];
+  plane_of(g, 0, x, a);
+  plane_of(g, 1, y, b);
+  const float nx[3] = {a[0], a[1], a[2]}, ny[3] = {b[0], b[1], b[2]};
+  const float dx = a[3], dy = b[3];
+  float moment[3], direction[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) moment[k] = dx * ny[k] - dy * nx[k];
+  direction[0] = nx[1] * ny[2] - nx[2] * ny[1];
+  direction[1] = nx[2] * ny[0] - nx[0] * ny[2];
+  direction[2] = nx[0] * ny[1] - nx[1] * ny[0];
+  const float dd = rdot3(direction, direction), mm = rdot3(moment, moment);
+  const float xx = rdot3(nx, nx), yy = rdot3(ny, ny), xy = rdot3(nx, ny);
+  const float ym = rdot3(ny, moment), xm = rdot3(nx, moment);
+  const float xyy = x * yy, yxx = y * xx, ndy = -dy, cross = dy * x - dx * y;
+  const float factor = p.opacity[id] * alpha_gradient * gaussian;
+  const float inverse_dd = __frcp_rn(dd);
+  const float ratio = mm / dd * inverse_dd;
+  float screen_x = 0.0f, screen_y = 0.0f;
+  float* t = p.grad_transforms + 16ll * id;
+#pragma unroll
+  for (int axis = 0; axis < 3; ++axis) {
+    const float dd0 = yy * nx[axis] - xy * ny[axis];
+    const float dd1 = xx * ny[axis] - xy * nx[axis];
+    const float dd3 = (xy * (y * nx[axis] + x * ny[axis]) - xyy * nx[axis]) - yxx * ny[axis];
+    const float d0 = factor * (ratio * dd0 - (ndy * moment[axis]) * inverse_dd);
+    const float d1 = factor * (ratio * dd1 - (dx * moment[axis]) * inverse_dd);
+    const float d3 = factor * (ratio * dd3 - (cross * moment[axis]) * inverse_dd);
+    if (SCREEN) {
+      screen_x += d0 * g.m[3][axis];
+      screen_y += d1 * g.m[3][axis];
+    }
+    red_add_v2(t + axis * 4, d0, d1);
+    red_add(t + axis * 4 + 3, d3);
+  }
+  const float tr0 = factor * -ym * inverse_dd;
+  const float tr1 = factor * xm * inverse_dd;
+  const float tr3 = factor * -(y * xm - x * ym) * inverse_dd;
+  red_add_v2(t + 12, tr0, tr1);
+  red_add(t + 15, tr3);
+  red_add(p.grad_opacity + id, gaussian * alpha_gradient);
+  if (SCREEN) {
+    screen_x += tr0 * g.m[3][3];
+    screen_y += tr1 * g.m[3][3];
+    red_add_v2(p.grad_screen + 2ll * id, screen_x, screen_y);
+    if (ABS) red_add_v2(p.grad_screen_abs + 2ll * id, fabsf(screen_x), fabsf(screen_y));
+  }
+}
+
+template <int CHP, bool BWD, bool SCREEN, bool ABS>
+struct HierWarp {
+  const HierParams& p;
+  WarpQueues& q;
+  int lane, half, hl, quad, mr;
+  int x0, y0, tile_x;
+  unsigned half_mask, quad_mask;
+  HierPixel<CHP, BWD> px;
+  int x, y;
+
+  SPLAT_DEV HierWarp(const HierParams& params, WarpQueues& queues) : p(params), q(queues) {}
+
+  // blend_step (render_hierarchical_warp.py:146-171) / blend_backward
+  // (backward_render.py:32-70): the head's front sample
+  SPLAT_DEV void blend() {
+    px.head_count -= 1;
+    if (!px.active) return;
+    const float alpha = px.ha[0];
+    const float next_t = px.T * (1.0f - alpha);
+    if (next_t < 0.0001f) {
+      px.active = false;  // the sample that would terminate is not blended
+      return;
+    }
+    const int id = px.hid[0];
+    const int C = p.channels;
+    const float* rgb = p.colors + static_cast<long long>(id) * C;
+    if (!BWD) {
+#pragma unroll
+      for (int c = 0; c < CHP; ++c)
+        if (c < C) px.color[c] = px.color[c] + (id >= 0 ? rgb[c] : 0.0f) * alpha * px.T;
+    } else {
+      float alpha_gradient = 0.0f;
+      const float weight = alpha * px.T;
+#pragma unroll
+      for (int c = 0; c < CHP; ++c) {
+        if (c < C) {
+          const float v = id >= 0 ? rgb[c] : 0.0f;
+          px.color[c] = px.color[c] + v * alpha * px.T;
+          const float behind = (px.final_color[c] - px.color[c]) / next_t;
+          alpha_gradient += (v - behind) * px.gradient[c];
+          if (id >= 0) red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * px.gradient[c]);
+        }
+      }
+      alpha_gradient *= px.T;
+      alpha_gradient += (-px.final_T / (1.0f - alpha)) * px.bg_grad;
+      if (id >= 0)
+        accumulate_ray_gradient<SCREEN, ABS>(p, id, static_cast<float>(x), static_cast<float>(y),
+                                             px.hg[0], alpha_gradient);
+    }
+    px.T = next_t;
+#pragma unroll
+    for (int j = 1; j < 4; ++j) {
+      px.hd[j - 1] = px.hd[j];
+      px.ha[j - 1] = px.ha[j];
+      px.hid[j - 1] = px.hid[j];
+      if (BWD) px.hg[j - 1] = px.hg[j];
+    }
+    px.hd[3] = kInf;
+  }
+
+  // :221-238 insert_head: strict comparison keeps equal-depth entries first
+  SPLAT_DEV void insert_head(float depth, float alpha, int id, float gaussian) {
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      if (depth < px.hd[s]) {
+        const float od = px.hd[s], oa = px.ha[s], og = px.hg[s];
+        const int oi = px.hid[s];
+        px.hd[s] = depth;
+        px.ha[s] = alpha;
+        px.hid[s] = id;
+        px.hg[s] = gaussian;
+        depth = od;
+        alpha = oa;
+        id = oi;
+        gaussian = og;
+      }
+    }
+    px.head_count += 1;
+  }
+
+  // :176-214 merge: the sorted N-entry run at qd[old..old+N) and the incoming
+  // sorted run (lane `rank` of the group holds entry rank) into qd[0..2N)
+  template <int N>
+  SPLAT_DEV void merge(float* qd, int* qi, unsigned mask, int rank, int old, float depth, int id) {
+    int new_pos = 0;
+#pragma unroll
+    for (int stride = N / 2; stride > 0; stride /= 2)
+      if (qd[old + new_pos + stride] <= depth) new_pos += stride;
+    new_pos += 1;
+    if (qd[old] > depth) new_pos = 0;
+    new_pos += rank;
+    const float old_depth = qd[old + rank];
+    __syncwarp(mask);
+    qd[old + rank] = depth;
+    __syncwarp(mask);
+    int old_pos = 0;
+#pragma unroll
+    for (int stride = N / 2; stride > 0; stride /= 2)
+      if (qd[old + old_pos + stride] < old_depth) old_pos += stride;
+    old_pos += 1;
+    if (qd[old] >= old_depth) old_pos = 0;
+    old_pos += rank;
+    const int old_id = qi[old + rank];
+    __syncwarp(mask);
+    qd[new_pos] = depth;
+    qi[new_pos] = id;
+    qd[old_pos] = old_depth;
+    qi[old_pos] = old_id;
+    __syncwarp(mask);
+  }
+
+  // :360-390 sort_batch: Batcher's network over the half's incoming run
+  // [32, 64) of its tail, sixteen lanes, one compare-exchange each per step
+  SPLAT_DEV void sort_batch() {
+    float* qd = q.tail_d[half];
+    int* qi = q.tail_id[half];
+    auto exchange = [&](int a, int b) {
+      const float da = qd[a], db = qd[b];
+      if (da > db) {
+        const int ia = qi[a], ib = qi[b];
+        qd[a] = db;
+        qi[a] = ib;
+        qd[b] = da;
+        qi[b] = ia;
+      }
+    };
+#pragma unroll
+    for (int size = 2; size <= 32; size *= 2) {
+      int stride = size / 2;
+      const int offset = hl & (stride - 1);
+      __syncwarp(half_mask);
+      int pos = 2 * hl - (hl & (stride - 1));
+      exchange(32 + pos, 32 + pos + stride);
+#pragma unroll
+      for (stride /= 2; stride > 0; stride /= 2) {
+        __syncwarp(half_mask);
+        pos = 2 * hl - (hl & (stride - 1));
+        if (offset >= stride) exchange(32 + pos - stride, 32 + pos);
+      }
+    }
+  }
+
+  // :262-306 front_mid: the quad consumes the front four entries of its mid
+  // queue, sampling each at its own pixel
+  SPLAT_DEV void front_mid(bool check_valid) {
+    const float* md = q.mid_d[quad];
+    const int* mi = q.mid_id[quad];
+    if (__any_sync(quad_mask, px.active)) {
+      const int load_id = mi[mr];
+      float amplitude = 0.0f;
+      if ((!check_valid || load_id != -1) && load_id >= 0) amplitude = p.opacity[load_id];
+      for (int inner = 0; inner < 4; ++inner) {
+        if (px.head_count >= 4) blend();
+        const int id = mi[inner];
+        if (check_valid && id == -1) continue;
+        const int gid = __shfl_sync(quad_mask, load_id, inner, 4);
+        const float weight = __shfl_sync(quad_mask, amplitude, inner, 4);
+        if (!px.active) continue;
+        px.contributors += 1;
+        if (gid < 0) continue;  // guard (see the header)
+        float power, depth;
+        ray_sample(load_m4(p.transforms, gid), static_cast<float>(x), static_cast<float>(y), power,
+                   depth);
+        if (depth < -1.0f || depth > 1.0f) continue;
+        const float gaussian = splat_expf(power);
+        const float alpha = wp_min(0.99f, weight * gaussian);
+        if (alpha < 1.0f / 255.0f) continue;
+        insert_head(depth, alpha, id, gaussian);
+      }
+    }
+    (void)md;
+    px.mid_count -= 4;
+    __syncwarp(half_mask);
+  }
+
+  // :308-355 push_mid: sixteen tail entries through the half's four quads
+  SPLAT_DEV void push_mid(bool check_valid) {
+    const float* td = q.tail_d[half];
+    const int* ti = q.tail_id[half];
+    float* md = q.mid_d[quad];
+    int* mi = q.mid_id[quad];
+    const int load_id = ti[hl];
+    const int mg = hl >> 2;
+    for (int batch = 0; batch < 4; ++batch) {
+      if (check_valid && px.tail_count == 0) break;
+      const int source = 4 * batch + mr;
+      const int id = ti[source];
+      const int gid = __shfl_sync(half_mask, load_id, source, 16);
+      float depth = kInf;
+      if ((!check_valid || gid != -1) && gid >= 0) {
+        float power;
+        ray_sample(load_m4(p.transforms, gid), static_cast<float>(x0 + 1 + 2 * (mg & 1)),
+                   static_cast<float>(y0 + 1 + 2 * (mg >> 1)), power, depth);
+      }
+      if (check_valid && id == -1) depth = kInf;
+      // :243-252 rank_mid
+      int rank = 0;
+#pragma unroll
+      for (int j = 1; j < 4; ++j) {
+        const int other_rank = (mr + j) & 3;
+        const float other = __shfl_sync(quad_mask, depth, other_rank, 4);
+        if (other < depth || (other == depth && other_rank < mr)) ++rank;
+      }
+      md[rank] = depth;
+      mi[rank] = id;
+      __syncwarp(quad_mask);
+      const float d = md[mr];
+      const int i = mi[mr];
+      px.mid_count += 4;
+      if (batch != 0 || px.mid_count > 4) {
+        merge<4>(md, mi, quad_mask, mr, 4, d, i);
+        front_mid(false);
+      } else {
+        md[4 + mr] = d;
+        mi[4 + mr] = i;
+      }
+      __syncwarp(quad_mask);
+      if (check_valid) px.tail_count -= min(4, px.tail_count);
+    }
+    if (!check_valid) px.tail_count -= 16;
+  }
+
+  SPLAT_DEV void run(int tile) {
+    const int gx = (p.width + 15) / 16;
+    tile_x = tile % gx * 16;
+    const int tile_y = tile / gx * 16;
+    const int local = threadIdx.x;
+    lane = local & 31;
+    half = lane >> 4;
+    hl = lane & 15;
+    quad = lane >> 2;
+    mr = lane & 3;
+    const int tail = local >> 4;
+    x0 = tile_x + 4 * (tail & 3);
+    y0 = tile_y + 4 * (tail >> 2);
+    const int mg = hl >> 2;
+    x = x0 + 2 * (mg & 1) + (mr & 1);
+    y = y0 + 2 * (mg >> 1) + (mr >> 1);
+    half_mask = 0xFFFFu << (lane & 16);
+    quad_mask = 0xFu << (lane & 28);
+    const int C = p.channels;
+    px.active = x < p.width && y < p.height;
+    px.T = 1.0f;
+    px.contributors = px.tail_count = px.mid_count = px.head_count = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      px.hd[k] = kInf;
+      px.ha[k] = 0.0f;
+      px.hg[k] = 0.0f;
+      px.hid[k] = -1;
+    }
+#pragma unroll
+    for (int c = 0; c < CHP; ++c) px.color[c] = 0.0f;
+    px.final_T = 0.0f;
+    px.bg_grad = 0.0f;
+    if (BWD) {
+#pragma unroll
+      for (int c = 0; c < CHP; ++c) px.gradient[c] = px.final_color[c] = 0.0f;
+      if (px.active) {
+        const long long idx = static_cast<long long>(y) * p.width + x;
+        const long long plane = static_cast<long long>(p.width) * p.height;
+        px.final_T = p.final_t_in[idx];
+#pragma unroll
+        for (int c = 0; c < CHP; ++c) {
+          if (c < C) {
+            px.gradient[c] = p.pixel_grad[c * plane + idx];
+            px.final_color[c] = p.image_in[c * plane + idx] - px.final_T * p.bg[c];
+            px.bg_grad += p.bg[c] * px.gradient[c];
+          }
+        }
+      }
+    }
+    const int first = p.ranges[2 * tile], last = p.ranges[2 * tile + 1];
+    const int tail0 = (tail & ~1);
+    for (int progress = first; progress < last; progress += 32) {
+      if (!__any_sync(kFull, px.active)) break;
+      const int gid = progress + lane < last ? p.points[progress + lane] : -1;
+      M4 g = {};
+      float amplitude = 0.0f;
+      if (gid >= 0) {
+        g = load_m4(p.transforms, gid);
+        if (p.cull) amplitude = p.opacity[gid];
+      }
+      int culled = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int og = tail0 + h;
+        if (p.cull && gid != -1) {
+          const float power = region_frustum(g, static_cast<float>(tile_x + 4 * (og & 3)),
+                                             static_cast<float>(y0), 3.0f, 3.0f);
+          if (wp_min(0.99f, amplitude * splat_expf(-power)) < 1.0f / 255.0f) culled |= 1 << h;
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int og = tail0 + h;
+        float depth = kInf;
+        if (gid != -1 && (!p.cull || !(culled & (1 << h)))) {
+          float power;
+          ray_sample(g, static_cast<float>(tile_x + 4 * (og & 3) + 2), static_cast<float>(y0 + 2),
+                     power, depth);
+        }
+        q.tail_d[h][32 + lane] = depth;
+        q.tail_id[h][32 + lane] = depth == kInf ? -1 : gid;
+      }
+      __syncwarp(kFull);
+      sort_batch();
+      __syncwarp(kFull);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float* qd = q.tail_d[h];
+        int* qi = q.tail_id[h];
+        const int old_count = __shfl_sync(kFull, px.tail_count, h * 16);
+        const float key = qd[32 + lane];
+        const int id = qi[32 + lane];
+        const int added = __popc(__ballot_sync(kFull, id != -1));
+        if (h == half) px.tail_count += added;
+        if (old_count != 0) {
+          merge<32>(qd, qi, kFull, lane, 0, key, id);
+        } else {
+          qd[lane] = key;
+          qi[lane] = id;
+        }
+      }
+      __syncwarp(kFull);
+#pragma unroll
+      for (int it = 0; it < 2; ++it) {
+        if (px.tail_count > 32) {
+          push_mid(false);
+          __syncwarp(half_mask);
+          float* qd = q.tail_d[half];
+          int* qi = q.tail_id[half];
+          for (int index = 0; index < 3 - it; ++index) {
+            const int dest = hl + index * 16;
+            qd[dest] = qd[dest + 16];
+            qi[dest] = qi[dest + 16];
+          }
+          __syncwarp(half_mask);
+        }
+      }
+      __syncwarp(kFull);
+    }
+    if (__any_sync(kFull, px.active)) {
+      if (px.tail_count != 0) {
+        for (int it = 0; it < 2; ++it) {
+          push_mid(true);
+          if (it == 0 && px.tail_count == 0) break;
+          if (it == 0) {
+            q.tail_d[half][hl] = q.tail_d[half][hl + 16];
+            q.tail_id[half][hl] = q.tail_id[half][hl + 16];
+            __syncwarp(half_mask);
+          }
+        }
+      }
+      if (__any_sync(kFull, px.active)) {
+        if (px.mid_count != 0) {
+          q.mid_d[quad][mr] = q.mid_d[quad][4 + mr];
+          q.mid_id[quad][mr] = q.mid_id[quad][4 + mr];
+          __syncwarp(quad_mask);
+          front_mid(true);
+        }
+        while (px.active && px.head_count != 0) blend();
+      }
+    }
+    if (!BWD && x < p.width && y < p.height) {
+      const long long idx = static_cast<long long>(y) * p.width + x;
+      const long long plane = static_cast<long long>(p.width) * p.height;
+#pragma unroll
+      for (int c = 0; c < CHP; ++c)
+        if (c < C) p.image[c * plane + idx] = px.color[c] + px.T * p.bg[c];
+      p.final_t[idx] = px.T;
+      p.contributors[idx] = px.contributors;
+    }
+  }
+};
+
+template <int CHP, bool BWD, bool SCREEN, bool ABS>
+__global__ void __launch_bounds__(256) aaa_hier_kernel(HierParams p) {
+  __shared__ WarpQueues queues[8];
+  const int tile = p.tile_order ? p.tile_order[blockIdx.x] : static_cast<int>(blockIdx.x);
+  HierWarp<CHP, BWD, SCREEN, ABS> w(p, queues[threadIdx.x >> 5]);
+  w.run(tile);
+}
+
+}  // namespace aaa
+}  // namespace splat

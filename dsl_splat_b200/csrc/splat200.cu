@@ -1431,3 +1431,6 @@ extern "C" int splat_debug_expf(int n, const float* x, float* ours, float* cuda_
   expf_probe_kernel<<<blocks_for(n, 256), 256, 0, counted(as_stream(stream))>>>(n, x, ours, cuda_exp);
   return check_launch("debug_expf");
 }
+
+// ---- AAA-Gaussians --------------------------------------------------------------
+#include "aaa_api.cuh"

@@ -149,31 +149,11 @@ def normalize_inputs(means, quats, scales, opacities, colors, viewmats, Ks, back
     )
 
 
-def torch_spherical_harmonics(coefficients: Tensor, directions: Tensor, degree: int) -> Tensor:
-    """inputs.py:63-98: Torch SH for CPU / float64 callers (not the CUDA path)."""
-    u = F.normalize(directions, dim=-1)
-    x, y, z = u.unbind(-1)
-    basis = [torch.full_like(x, 0.28209479177387814)]
-    if degree >= 1:
-        basis += [-0.4886025119029199 * y, 0.4886025119029199 * z, -0.4886025119029199 * x]
-    if degree >= 2:
-        xx, yy, zz = x * x, y * y, z * z
-        basis += [1.0925484305920792 * x * y, -1.0925484305920792 * y * z,
-                  0.31539156525252005 * (2 * zz - xx - yy), -1.0925484305920792 * x * z,
-                  0.5462742152960396 * (xx - yy)]
-    if degree >= 3:
-        basis += [-0.5900435899266435 * y * (3 * xx - yy), 2.890611442640554 * x * y * z,
-                  -0.4570457994644658 * y * (4 * zz - xx - yy),
-                  0.3731763325901154 * z * (2 * zz - 3 * xx - 3 * yy),
-                  -0.4570457994644658 * x * (4 * zz - xx - yy),
-                  1.445305721320277 * z * (xx - yy), -0.5900435899266435 * x * (xx - 3 * yy)]
-    w = torch.stack(basis, dim=-1)
-    return ((coefficients[:, : len(basis)] * w[..., None]).sum(-2) + 0.5).clamp_min(0)
-
-
 def spherical_harmonics(coefficients: Tensor, directions: Tensor, degree: int) -> Tensor:
-    """inputs.py:54-60: the CUDA kernel for CUDA float32, Torch otherwise."""
-    if coefficients.is_cuda and coefficients.dtype == directions.dtype == torch.float32:
-        from .spherical_harmonics import spherical_harmonics as cuda_sh
-        return cuda_sh(coefficients, directions, degree)
-    return torch_spherical_harmonics(coefficients, directions, degree)
+    """inputs.py:54-60 on the CUDA SH kernel.  The reference's Torch branch
+    for CPU / float64 callers has no counterpart: this library has no CPU
+    compute path, so other inputs are rejected."""
+    if not (coefficients.is_cuda and coefficients.dtype == directions.dtype == torch.float32):
+        raise ValueError("spherical_harmonics needs CUDA float32 coefficients and directions")
+    from .spherical_harmonics import spherical_harmonics as cuda_sh
+    return cuda_sh(coefficients, directions, degree)

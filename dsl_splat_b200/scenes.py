@@ -8,6 +8,8 @@ Config 1: 1M Gaussians from 64 isotropic clusters in a radius-5 ball, SH3,
           one 1920x1080 camera at distance 8 looking at the origin.
 Config 2: 3M Gaussians (config-1 distributions), 8 cameras 1296x840 on a
           radius-6 orbit at height 1.
+Config 3: 2M Gaussians (config-1 distributions), SH3, one 1920x1080 camera
+          (the AAA-Gaussians benchmark, aaa.rasterize).
 Config 4: 1M Gaussians, SH3, 1600x1200, 32 extra channels (RaDe-GS shapes).
 
 Sampling order: means, log-scales, quats, opacity logits, colours/SH, extras,
@@ -103,8 +105,9 @@ def make_scene(config: int, *, n: int | None = None, width: int | None = None,
         f = width * 1.0
         viewmats = torch.eye(4)[None]
         Ks = intrinsics(f, f, width / 2, height / 2)[None]
-    elif config in (1, 2, 4):
+    elif config in (1, 2, 3, 4):
         defaults = {1: (1_000_000, 1920, 1080, 1100.0, 1),
+                    3: (2_000_000, 1920, 1080, 1100.0, 1),
                     2: (3_000_000, 1296, 840, 1000.0, 8),
                     4: (1_000_000, 1600, 1200, 1200.0, 1)}[config]
         n = defaults[0] if n is None else n

@@ -398,6 +398,117 @@ int splat_rade_render_backward(
     float* grad_extras, float* abs_centers, float* grad_planes, float* grad_normals,
     const int* tile_order, void* stream);
 
+/* ---- AAA-Gaussians (dsl_splat/aaa) ------------------------------------------
+ * One view of aaa.rasterize: adaptive 3D filter, 3D ray evaluation,
+ * StopThePop HIER 64/8/4 hierarchical sorting.  The camera arrays are the
+ * reference's lowered, transposed 4x4 storage (aaa/cameras.py:77-121:
+ * viewmatrix = V^T, projmatrix = (P V)^T, device float32). */
+typedef struct SplatAaaFrame {
+  int n, width, height;
+  const float* means;      /* (n,3) */
+  const float* scales;     /* (n,3) activated */
+  const float* quats;      /* (n,4) normalised wxyz, 16-byte aligned */
+  const float* opacities;  /* (n) activated */
+  const float* sh;         /* (n,sh_k,3) SH inputs of preprocess_3d, or NULL */
+  int sh_k, sh_degree;
+  const float* filters;    /* (n) stored 3D filter, or NULL */
+  const float* campos;     /* (3) */
+  const float* view;       /* (4,4) viewmatrix storage */
+  const float* proj;       /* (4,4) projmatrix storage */
+  float tanfov_x, tanfov_y, principal_x, principal_y, scale_modifier;
+  float focal_x;           /* width / (2 tanfov_x), computed in double (backward_preprocess.py:332) */
+  float focal_max;         /* max of both focal lengths (backward_camera.py:267-270) */
+  int sort_order;          /* 0-3 (aaa/settings.py GlobalSortOrder; 3 = PTD_MAX) */
+  int ewa, new_aabb, near_clipping, tile_culling;
+  int complete;            /* eval_3D and not cooperative (aaa/preprocess.py:321-322) */
+  int cooperative;         /* load_balancing and tile_based_culling */
+} SplatAaaFrame;
+
+/* aaa/preprocess.py:165-451 -> aaa/preprocess3d.py:17-245 preprocess_3d
+ * (adaptive 3D filter, EWA opacity compensation, Gaussian-to-screen
+ * transform, frustum culling, axis bounds, first-32-tile culling).  Outputs
+ * (n): centers/rects (n,2) float2, depths, transforms (n,4,4), opacity
+ * (effective), radii, tiles, valid (u8), rgb/clamped (n,3) when sh; rows of
+ * rejected Gaussians keep radii = tiles = valid = 0 and are otherwise left
+ * unwritten.  cooperative: rectangles of more than 32 tiles are appended to
+ * queued (n), *queue_size (device int, zeroed here) counts them.  atan2,
+ * tan, exp and log are this library's own functions (the CPU oracle's). */
+int splat_aaa_preprocess(const SplatAaaFrame* frame, float* centers, float* rects, float* depths,
+                         float* transforms, float* opacity, int* radii, int* tiles, float* rgb,
+                         unsigned char* valid, unsigned char* clamped, int* queued,
+                         int* queue_size, void* stream);
+
+/* aaa/preprocess.py:452-476 -> aaa/cooperative_culling.py:152-192
+ * cull_remainder_3d: the queued Gaussians' tiles past the first 32 are
+ * added to tiles; a Gaussian left without a tile gets radius 0, not valid. */
+int splat_aaa_cull_remainder(int n, const int* queued, const int* queue_size,
+                             const float* centers, const float* rects, const float* transforms,
+                             const float* opacity, int width, int height, int* radii, int* tiles,
+                             unsigned char* valid, void* stream);
+
+/* aaa/binning.py:278-342 bin_and_sort after the count scan (splat_scan_counts
+ * of tiles, its total read by the host as the reference does at
+ * primitives/tiling.py:64): aaa/binning_native.py:7-135's key emission
+ * (tile, screen depth + 8 of the tile's closest point, Gaussian id; padding
+ * pairs where the recount finds fewer tiles), the stable sort of the keys
+ * (primitives/tiling.py:67-100) and identify_ranges (:39-54).  point_list
+ * (pairs) ends with the padding ids (-1); ranges (T,2), zero for empty
+ * tiles.  Images up to 65535 tiles, up to 2^30 pairs. */
+size_t splat_aaa_bin_workspace_bytes(long long pairs);
+int splat_aaa_bin(int n, long long pairs, const int* offsets, const float* centers,
+                  const float* rects, const int* radii, const float* transforms,
+                  const float* opacity, int width, int height, void* workspace,
+                  size_t workspace_bytes, int* point_list, int* ranges, void* stream);
+
+/* The emission alone (aaa/binning_native.py:85-135), unsorted, pairs in
+ * Gaussian order: tiles_out (tile id; padding 2^b - 1 with b the bit length
+ * of the tile count), depth_keys (float bits of depth + 8 minus those of
+ * 7.0), ids (-1 for padding). */
+int splat_aaa_emit(int n, long long pairs, const int* offsets, const float* centers,
+                   const float* rects, const int* radii, const float* transforms,
+                   const float* opacity, int width, int height, unsigned* tiles_out,
+                   unsigned* depth_keys, int* ids, void* stream);
+
+/* aaa/render.py:11-28 -> aaa/render_hierarchical_warp.py:694-801 render
+ * (HIER 64/8/4 blend, 4x4 culling when cull): image (C,H,W) planar
+ * = blended features + T * bg, final_t and contributors (H,W).  colors (n,C)
+ * row-major, C = 1..64; tile_order (T) a block schedule (splat_tile_order)
+ * or NULL. */
+int splat_aaa_render(int width, int height, int channels, int cull, const int* ranges,
+                     const int* points, const float* transforms, const float* opacity,
+                     const float* colors, const float* bg, const int* tile_order, float* image,
+                     float* final_t, int* contributors, void* stream);
+
+/* aaa/backward_render.py:140-248 backward_render: replay of the forward's
+ * queues; gradients ADDED into grad_transforms (n,16, the reference's
+ * transposed layout, 16-byte aligned), grad_opacity (n), grad_colors (n,C),
+ * grad_screen (n,2) and grad_screen_abs (n,2) (NULL to skip; abs requires
+ * screen).  image/final_t: the forward's outputs; pixel_grad (C,H,W). */
+int splat_aaa_render_backward(int width, int height, int channels, int cull, const int* ranges,
+                              const int* points, const float* transforms, const float* opacity,
+                              const float* colors, const float* bg, const int* tile_order,
+                              const float* image, const float* final_t, const float* pixel_grad,
+                              float* grad_transforms, float* grad_opacity, float* grad_colors,
+                              float* grad_screen, float* grad_screen_abs, void* stream);
+
+/* aaa/backward_preprocess.py:270-346 -> preprocess_adjoint (:130-268):
+ * gradients of the input opacities (n), means (n,3), scales (n,3) and
+ * normalised quaternions (n,4, 16-byte aligned) from the replay's
+ * transform (n,16) and effective-opacity (n) gradients (fully written).
+ * Uses frame->focal_x. */
+int splat_aaa_preprocess_backward(const SplatAaaFrame* frame, const int* radii,
+                                  const float* up_transforms, const float* up_opacity,
+                                  float* grad_opacity, float* grad_means, float* grad_scales,
+                                  float* grad_quats, void* stream);
+
+/* aaa/backward_camera.py:225-294 backward_camera -> camera_adjoint
+ * (:61-224) without SH, rows summed on the device: camera_sums (23) =
+ * projmatrix gradient (16, storage order), viewmatrix column-2 gradient (4),
+ * campos gradient (3).  Uses frame->focal_max. */
+int splat_aaa_camera_backward(const SplatAaaFrame* frame, const int* radii,
+                              const float* effective_opacity, const float* up_transforms,
+                              const float* up_opacity, float* camera_sums, void* stream);
+
 /* Diagnostic: ours[i] = the blend's exp, cuda_exp[i] = CUDA expf, for x (n). */
 int splat_debug_expf(int n, const float* x, float* ours, float* cuda_exp, void* stream);
 

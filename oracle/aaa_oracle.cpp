@@ -23,6 +23,70 @@
 // golden generator so that both round the opacity threshold alike
 extern "C" float oracle_logf(float);
 
+// ---- atan2 and tan: the arithmetic both sides of the comparison use ----------
+// aaa/native_geometry.py's bound_axis calls atan2f and tanf; CUDA's and the
+// host libm's results may differ in the last bit, and the axis bounds feed
+// integer tile counts.  The oracle and the CUDA kernels therefore both
+// evaluate these two functions as written here: in double precision from
+// their power series (no library call), rounded once to float.  The double
+// result is within a few 1e-16 relative of the true value, so the float is
+// the correctly rounded one except in (rare) near-halfway cases -- it then
+// agrees with any correctly rounded libm as well.
+
+// atan(t) for 0 <= t <= 1: two half-angle steps atan(t) = 2 atan(t / (1 +
+// sqrt(1 + t^2))) bring the argument below tan(pi/16) ~ 0.199, where the
+// alternating Taylor series sum_k (-1)^k u^(2k+1) / (2k+1) has converged to
+// double precision after 12 terms (Horner in u^2).
+static double atan_unit(double t) {
+  double u = t / (1.0 + std::sqrt(1.0 + t * t));
+  u = u / (1.0 + std::sqrt(1.0 + u * u));
+  const double u2 = u * u;
+  double p = 1.0 / 23.0;
+  for (int k = 10; k >= 0; --k) p = 1.0 / (2 * k + 1) - u2 * p;
+  return 4.0 * (u * p);
+}
+
+extern "C" float oracle_atan2f(float yf, float xf) {
+  const double kPi = 3.141592653589793, kHalfPi = 1.5707963267948966;
+  if (std::isnan(yf) || std::isnan(xf)) return yf + xf;
+  const double y = yf, x = xf;
+  if (y == 0.0) return static_cast<float>(std::signbit(x) ? std::copysign(kPi, y) : y);
+  if (x == 0.0) return static_cast<float>(std::copysign(kHalfPi, y));
+  if (std::isinf(y) || std::isinf(x)) {
+    double r;
+    if (std::isinf(y) && std::isinf(x)) r = x > 0 ? kPi / 4 : 3 * kPi / 4;
+    else if (std::isinf(y)) r = kHalfPi;
+    else r = x > 0 ? 0.0 : kPi;
+    return static_cast<float>(std::copysign(r, y));
+  }
+  const double ax = std::fabs(x), ay = std::fabs(y);
+  double r = ay <= ax ? atan_unit(ay / ax) : kHalfPi - atan_unit(ax / ay);
+  if (x < 0.0) r = kPi - r;
+  return static_cast<float>(std::copysign(r, y));
+}
+
+// tan(x): x reduced by the nearest multiple k of pi/2 (pi/2 split into three
+// parts of 33, 33 and 53 significant bits, so k * part is exact for the
+// arguments that occur, |x| < 2^20); sin and cos of the remainder |r| <=
+// pi/4 from their Taylor series (to r^25 / 25!), tan = sin / cos, or
+// -cos / sin for odd k.
+extern "C" float oracle_tanf(float xf) {
+  if (std::isnan(xf) || std::isinf(xf)) return xf - xf;
+  const double x = xf;
+  const double k = std::nearbyint(x / 1.5707963267948966);
+  const double r = ((x - k * 1.5707963267341256) - k * 6.077100506303966e-11) -
+                   k * 2.0222662487959506e-21;
+  const double r2 = r * r;
+  double s = 1.0, c = 1.0;
+  for (int j = 12; j >= 1; --j) {
+    s = 1.0 - r2 / ((2.0 * j) * (2.0 * j + 1.0)) * s;
+    c = 1.0 - r2 / ((2.0 * j - 1.0) * (2.0 * j)) * c;
+  }
+  s *= r;
+  const bool odd = std::fmod(std::fabs(k), 2.0) == 1.0;
+  return static_cast<float>(odd ? -c / s : s / c);
+}
+
 namespace {
 
 struct V4 {
@@ -196,7 +260,7 @@ void bound_axis(const M4& g2v, const float mean[3], float cutoff, int axis, floa
   const float length_squared = (mean[0] * mean[0] + mean[1] * mean[1]) + mean[2] * mean[2];
   const float norm = 1.0f / std::sqrt(length_squared);
   const float direction[3] = {mean[0] * norm, mean[1] * norm, mean[2] * norm};
-  const float theta_mu = std::atan2(direction[axis], direction[2]);
+  const float theta_mu = oracle_atan2f(direction[axis], direction[2]);
   const V4 t{{cutoff, cutoff, cutoff, -1.0f}};
   const V4 a = g2v.row(axis), z = g2v.row(2);
   const float aa = pdot4(t, cw(a, a)), zz = pdot4(t, cw(z, z)), az = pdot4(t, cw(a, z));
@@ -204,7 +268,7 @@ void bound_axis(const M4& g2v, const float mean[3], float cutoff, int axis, floa
   float lower = -(1.57079632679489661923f - 1e-5f), upper = -lower;
   if (discriminant > 0.0f) {
     const float root = std::sqrt(discriminant);
-    float lo = std::atan2(-(az + root), -zz), hi = std::atan2(-(az - root), -zz);
+    float lo = oracle_atan2f(-(az + root), -zz), hi = oracle_atan2f(-(az - root), -zz);
     // both angles and theta_mu lie in [-pi, pi]: a few steps at most
     for (int k = 0; k < 8 && lo > theta_mu; ++k) lo -= pi;
     for (int k = 0; k < 8 && lo < theta_mu - pi; ++k) lo += pi;
@@ -227,8 +291,8 @@ void bound_axis(const M4& g2v, const float mean[3], float cutoff, int axis, floa
     lower = std::fmax(lower, lo);
     upper = std::fmin(upper, hi);
   }
-  out[0] = std::tan(lower);
-  out[1] = std::tan(upper);
+  out[0] = oracle_tanf(lower);
+  out[1] = oracle_tanf(upper);
 }
 
 // aaa/native_geometry.py:224-247 screen_bounds_native: centre and half

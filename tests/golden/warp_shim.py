@@ -20,7 +20,9 @@ reference's own kernel source on the CPU:
   primitives/warp.py) exchange values among the 32 threads of a warp and
   reproduce the shuffle-down tree's float32 summation order;
 * `wp.exp` is the same Cody-Waite exp the oracle and the CUDA kernels use
-  (a deliberate substitution; CUDA's expf is not reproducible here), and
+  (a deliberate substitution; CUDA's expf is not reproducible here), the
+  AAA snippets' atan2f / tanf / logf are the oracle's own (see
+  _SUBSTITUTIONS), and
   `norm3df` (rade/projection.py:33) is sqrtf(x*x + y*y + z*z) in IEEE
   float32, as the oracle and the CUDA kernels compute the sort distance.
 
@@ -461,17 +463,36 @@ template <typename F> static void run_warps(int threads, F body) {
 """
 
 
+# The transcendental functions on the AAA decision path (aaa/native_geometry.py's
+# atan2f / tanf, aaa/binning_native.py's logf) are the oracle's own
+# implementations in every snippet (oracle/aaa_oracle.cpp, splat_oracle.cpp),
+# the ones the CUDA kernels use too: the host libm's float versions are not
+# correctly rounded, and the tile bounds they feed are integers.  Defined
+# after every library header, so only snippet text is affected.
+_ORACLE_DIR = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(
+    os.path.abspath(__file__)))), "oracle")
+_SUBSTITUTIONS = r"""
+extern "C" float oracle_atan2f(float, float);
+extern "C" float oracle_tanf(float);
+extern "C" float oracle_logf(float);
+#define atan2f oracle_atan2f
+#define tanf oracle_tanf
+#define logf oracle_logf
+"""
+_LINK_ORACLE = ["-L" + _ORACLE_DIR, "-l:libsplat_oracle.so", "-Wl,-rpath," + _ORACLE_DIR]
+
+
 def compile_warp_snippet(source: str, name: str):
     """g++ a C++ translation unit made of the float32 prelude, the warp-lane
     prelude and `source`; returns the ctypes library."""
     tmp = tempfile.mkdtemp(prefix="warp_shim_")
     path = os.path.join(tmp, f"{name}.cpp")
     with open(path, "w") as f:
-        f.write(_NATIVE_HEADER + WARP_LANES_HEADER + source)
+        f.write(_NATIVE_HEADER + WARP_LANES_HEADER + _SUBSTITUTIONS + source)
     so = os.path.join(tmp, f"{name}.so")
     subprocess.run(["g++", "-O1", "-std=c++20", "-pthread", "-fPIC", "-shared",
                     "-ffp-contract=off", "-march=x86-64-v3", "-Wno-unknown-pragmas", "-o", so,
-                    path], check=True)
+                    path, *_LINK_ORACLE], check=True)
     lib = ctypes.CDLL(so)
     _native_libs[name] = lib
     return lib
@@ -526,7 +547,7 @@ def _compile_native(name, snippet, params, ret):
     rtype, rn, rkind = _c_type(ret)
     body = textwrap.indent(snippet.strip(), "  ")
     sig = ", ".join(f"{_c_type(ann)[0]} {pname}" for pname, ann in params)
-    src = _NATIVE_HEADER + f"\nstatic {rtype} impl_{name}({sig}) {{\n{body}\n}}\n"
+    src = _NATIVE_HEADER + _SUBSTITUTIONS + f"\nstatic {rtype} impl_{name}({sig}) {{\n{body}\n}}\n"
     call = ", ".join(pname for pname, _ in params)
     cols = getattr(ret, "cols", 1)
     store = {"scalar": "out[0] = r;",
@@ -542,7 +563,7 @@ def _compile_native(name, snippet, params, ret):
         f.write(src)
     so = os.path.join(tmp, f"{name}.so")
     subprocess.run(["g++", "-O1", "-std=c++17", "-fPIC", "-shared", "-ffp-contract=off",
-                    "-march=x86-64-v3", "-o", so, path], check=True)
+                    "-march=x86-64-v3", "-o", so, path, *_LINK_ORACLE], check=True)
     lib = ctypes.CDLL(so)
     fn = getattr(lib, f"call_{name}")
     fn.restype = None
