@@ -211,7 +211,7 @@ def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, wi
         contrib.zero_()
         return image, final_t, contrib
     pin = Args()
-    check(lib.splat_aaa_render(width, height, C, int(cull), ptr(bins["ranges"]),
+    check(lib.splat_aaa_render(features.shape[0], width, height, C, int(cull), ptr(bins["ranges"]),
                                ptr(bins["point_list"]), pin(state.transforms), pin(state.opacity),
                                pin(features), pin(background), ptr(bins.get("tile_order")),
                                ptr(image), ptr(final_t), ptr(contrib), nv.stream(dev)),
@@ -240,7 +240,7 @@ def render_backward(state: AaaState, bins: dict, features: Tensor, background: T
     if n:
         pin = Args()
         check(lib.splat_aaa_render_backward(
-            width, height, C, int(cull), ptr(bins["ranges"]), ptr(bins["point_list"]),
+            n, width, height, C, int(cull), ptr(bins["ranges"]), ptr(bins["point_list"]),
             pin(state.transforms), pin(state.opacity), pin(features), pin(background),
             ptr(bins.get("tile_order")), pin(image), pin(final_t), pin(grad_image), ptr(g_tr),
             ptr(g_op), ptr(g_col), ptr(g_scr), ptr(g_abs), nv.stream(dev)), "aaa_render_backward")

@@ -286,14 +286,16 @@ int splat_aaa_bin(int n, long long pairs, const int* offsets, const float* cente
   return check_launch("aaa_bin");
 }
 
-int splat_aaa_render(int width, int height, int channels, int cull, const int* ranges,
+int splat_aaa_render(int n, int width, int height, int channels, int cull, const int* ranges,
                      const int* points, const float* transforms, const float* opacity,
                      const float* colors, const float* bg, const int* tile_order, float* image,
                      float* final_t, int* contributors, void* stream) {
   int r = check_hier_inputs(width, height, channels, ranges, points, transforms, opacity, colors, bg);
   if (r != kOk) return r;
   if (!image || !final_t || !contributors) return fail(kInvalidArgument, "null AAA blend output");
+  if (n < 0) return fail(kInvalidArgument, "n < 0");
   HierParams p{};
+  p.n = n;
   p.width = width;
   p.height = height;
   p.channels = channels;
@@ -311,7 +313,8 @@ int splat_aaa_render(int width, int height, int channels, int cull, const int* r
   return dispatch_hier(p, false, false, false, as_stream(stream));
 }
 
-int splat_aaa_render_backward(int width, int height, int channels, int cull, const int* ranges,
+int splat_aaa_render_backward(int n, int width, int height, int channels, int cull,
+                              const int* ranges,
                               const int* points, const float* transforms, const float* opacity,
                               const float* colors, const float* bg, const int* tile_order,
                               const float* image, const float* final_t, const float* pixel_grad,
@@ -325,7 +328,9 @@ int splat_aaa_render_backward(int width, int height, int channels, int cull, con
     return fail(kInvalidArgument, "absolute screen gradients require the screen gradients");
   if (!aligned(grad_transforms, 16) || !aligned(grad_screen, 8) || !aligned(grad_screen_abs, 8))
     return fail(kInvalidArgument, "AAA gradient buffers misaligned");
+  if (n < 0) return fail(kInvalidArgument, "n < 0");
   HierParams p{};
+  p.n = n;
   p.width = width;
   p.height = height;
   p.channels = channels;

@@ -134,6 +134,7 @@ SPLAT_DEV float region_frustum(const M4& g, float x, float y, float w, float h) 
 
 struct HierParams {
   int width, height, channels, cull;
+  int n;                    // Gaussians (ids outside [0, n) are never read)
   const int* ranges;        // (T,2)
   const int* points;        // sorted Gaussian ids
   const float* transforms;  // (n,4,4), 16-byte aligned
@@ -252,7 +253,7 @@ struct HierWarp {
       px.active = false;  // the sample that would terminate is not blended
       return;
     }
-    const int id = px.hid[0];
+    const int id = px.hid[0] < p.n ? px.hid[0] : -1;
     const int C = p.channels;
     const float* rgb = p.colors + static_cast<long long>(id) * C;
     if (!BWD) {
@@ -374,12 +375,12 @@ struct HierWarp {
   // :262-306 front_mid: the quad consumes the front four entries of its mid
   // queue, sampling each at its own pixel
   SPLAT_DEV void front_mid(bool check_valid) {
-    const float* md = q.mid_d[quad];
     const int* mi = q.mid_id[quad];
     if (__any_sync(quad_mask, px.active)) {
       const int load_id = mi[mr];
       float amplitude = 0.0f;
-      if ((!check_valid || load_id != -1) && load_id >= 0) amplitude = p.opacity[load_id];
+      if ((!check_valid || load_id != -1) && load_id >= 0 && load_id < p.n)
+        amplitude = p.opacity[load_id];
       for (int inner = 0; inner < 4; ++inner) {
         if (px.head_count >= 4) blend();
         const int id = mi[inner];
@@ -388,7 +389,7 @@ struct HierWarp {
         const float weight = __shfl_sync(quad_mask, amplitude, inner, 4);
         if (!px.active) continue;
         px.contributors += 1;
-        if (gid < 0) continue;  // guard (see the header)
+        if (gid < 0 || gid >= p.n) continue;  // guard (see the header)
         float power, depth;
         ray_sample(load_m4(p.transforms, gid), static_cast<float>(x), static_cast<float>(y), power,
                    depth);
@@ -399,14 +400,12 @@ struct HierWarp {
         insert_head(depth, alpha, id, gaussian);
       }
     }
-    (void)md;
     px.mid_count -= 4;
     __syncwarp(half_mask);
   }
 
   // :308-355 push_mid: sixteen tail entries through the half's four quads
   SPLAT_DEV void push_mid(bool check_valid) {
-    const float* td = q.tail_d[half];
     const int* ti = q.tail_id[half];
     float* md = q.mid_d[quad];
     int* mi = q.mid_id[quad];
@@ -418,7 +417,7 @@ struct HierWarp {
       const int id = ti[source];
       const int gid = __shfl_sync(half_mask, load_id, source, 16);
       float depth = kInf;
-      if ((!check_valid || gid != -1) && gid >= 0) {
+      if ((!check_valid || gid != -1) && gid >= 0 && gid < p.n) {
         float power;
         ray_sample(load_m4(p.transforms, gid), static_cast<float>(x0 + 1 + 2 * (mg & 1)),
                    static_cast<float>(y0 + 1 + 2 * (mg >> 1)), power, depth);
@@ -505,7 +504,8 @@ struct HierWarp {
     const int tail0 = (tail & ~1);
     for (int progress = first; progress < last; progress += 32) {
       if (!__any_sync(kFull, px.active)) break;
-      const int gid = progress + lane < last ? p.points[progress + lane] : -1;
+      int gid = progress + lane < last ? p.points[progress + lane] : -1;
+      if (gid >= p.n) gid = -1;  // guard: sorted ids always lie in [0, n)
       M4 g = {};
       float amplitude = 0.0f;
       if (gid >= 0) {
@@ -609,6 +609,26 @@ template <int CHP, bool BWD, bool SCREEN, bool ABS>
 __global__ void __launch_bounds__(256) aaa_hier_kernel(HierParams p) {
   __shared__ WarpQueues queues[8];
   const int tile = p.tile_order ? p.tile_order[blockIdx.x] : static_cast<int>(blockIdx.x);
+  // every queue entry starts as an empty one (FLT_MAX, -1); the algorithm
+  // writes each entry before reading it, so this only keeps unwritten shared
+  // memory from ever being read as an id
+  {
+    WarpQueues& q = queues[threadIdx.x >> 5];
+    const int lane = threadIdx.x & 31;
+    float* d = &q.tail_d[0][0];
+    int* i = &q.tail_id[0][0];
+    for (int k = lane; k < 128; k += 32) {
+      d[k] = kInf;
+      i[k] = -1;
+    }
+    d = &q.mid_d[0][0];
+    i = &q.mid_id[0][0];
+    for (int k = lane; k < 64; k += 32) {
+      d[k] = kInf;
+      i[k] = -1;
+    }
+    __syncwarp();
+  }
   HierWarp<CHP, BWD, SCREEN, ABS> w(p, queues[threadIdx.x >> 5]);
   w.run(tile);
 }

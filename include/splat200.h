@@ -471,10 +471,10 @@ int splat_aaa_emit(int n, long long pairs, const int* offsets, const float* cent
 
 /* aaa/render.py:11-28 -> aaa/render_hierarchical_warp.py:694-801 render
  * (HIER 64/8/4 blend, 4x4 culling when cull): image (C,H,W) planar
- * = blended features + T * bg, final_t and contributors (H,W).  colors (n,C)
- * row-major, C = 1..64; tile_order (T) a block schedule (splat_tile_order)
- * or NULL. */
-int splat_aaa_render(int width, int height, int channels, int cull, const int* ranges,
+ * = blended features + T * bg, final_t and contributors (H,W).  n Gaussians
+ * (ids outside [0, n) are never read); colors (n,C) row-major, C = 1..64;
+ * tile_order (T) a block schedule (splat_tile_order) or NULL. */
+int splat_aaa_render(int n, int width, int height, int channels, int cull, const int* ranges,
                      const int* points, const float* transforms, const float* opacity,
                      const float* colors, const float* bg, const int* tile_order, float* image,
                      float* final_t, int* contributors, void* stream);
@@ -484,8 +484,8 @@ int splat_aaa_render(int width, int height, int channels, int cull, const int* r
  * transposed layout, 16-byte aligned), grad_opacity (n), grad_colors (n,C),
  * grad_screen (n,2) and grad_screen_abs (n,2) (NULL to skip; abs requires
  * screen).  image/final_t: the forward's outputs; pixel_grad (C,H,W). */
-int splat_aaa_render_backward(int width, int height, int channels, int cull, const int* ranges,
-                              const int* points, const float* transforms, const float* opacity,
+int splat_aaa_render_backward(int n, int width, int height, int channels, int cull,
+                              const int* ranges, const int* points, const float* transforms, const float* opacity,
                               const float* colors, const float* bg, const int* tile_order,
                               const float* image, const float* final_t, const float* pixel_grad,
                               float* grad_transforms, float* grad_opacity, float* grad_colors,
