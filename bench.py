@@ -41,8 +41,10 @@ METRIC = "fwd+bwd frames/s, 3DGS SH3 1M Gaussians @1080p"
 # report the same unit under their own name
 CONFIG_METRICS = {2: "fwd+bwd frames/s (camera views), 3DGS SH3 3M Gaussians, 8 cameras "
                      "1296x840",
+                  3: "fwd+bwd frames/s, AAA-Gaussians SH3 2M Gaussians @1080p",
                   4: "fwd+bwd frames/s, RaDe-GS SH3 1M Gaussians + 32 extra channels, depth/"
                      "median/normals @1600x1200"}
+API_OF = {3: "aaa.rasterize", 4: "rade.rasterize"}
 
 
 def metric_for(config: int) -> str:
@@ -119,7 +121,7 @@ def workload(config: int, rank: int, world: int, gaussians: int | None = None):
 def describe(s, world):
     views = s.viewmats.shape[0]
     total = s.meta.get("cameras", world)
-    api = "rade.rasterize" if s.meta["config"] == 4 else "gs3d.rasterize"
+    api = API_OF.get(s.meta["config"], "gs3d.rasterize")
     extra = f" + {s.extras.shape[1]} extra channels" if s.extras is not None else ""
     return {
         "workload": f"config{s.meta['config']}: {api} SH{s.sh_degree} "
@@ -224,10 +226,72 @@ def cpu_band_step_rade(s, rows: int, y0: int = 0):
                   g["features"][:, :3].astype(np.float32))
 
 
+def aaa_lowered_camera(view, K, width: int, height: int, near: float = 0.01, far: float = 1e10):
+    """aaa/cameras.py:78-121 on the host for one camera (the same Torch
+    arithmetic as dsl_splat_b200.aaa.cameras, without importing the package):
+    V^T and (P V)^T storage, the camera centre, tan(fov/2) and (cx, cy)."""
+    fx, fy, cx, cy = float(K[0, 0]), float(K[1, 1]), float(K[0, 2]), float(K[1, 2])
+    p = torch.zeros(4, 4, dtype=torch.float32)
+    k = torch.as_tensor(K, dtype=torch.float32)
+    p[0, 0] = 2 * k[0, 0] / width
+    p[1, 1] = 2 * k[1, 1] / height
+    p[0, 2] = 2 * k[0, 2] / width - 1
+    p[1, 2] = 2 * k[1, 2] / height - 1
+    p[2, 2] = far / (far - near)
+    p[2, 3] = -far * near / (far - near)
+    p[3, 2] = 1
+    v = torch.as_tensor(view, dtype=torch.float32)
+    full = (p @ v).T.contiguous().numpy()
+    campos = torch.linalg.inv(v)[:3, 3].contiguous().numpy()
+    return (v.T.contiguous().numpy(), full, campos, (width / (2 * fx), height / (2 * fy)),
+            (cx, cy))
+
+
+def cpu_band_step_aaa(s, rows: int, y0: int = 0):
+    """One aaa.rasterize fwd+bwd of the oracle on image rows [y0, y0+rows) of
+    view 0 (principal point shifted by y0): SH colours, preprocessing,
+    remainder cull, key emission and sort, HIER blend and its replay, the
+    preprocessing and camera adjoints and the SH backward."""
+    from oracle import oracle as O
+    import torch.nn.functional as F
+    W = s.width
+    K = s.Ks[0].numpy().copy()
+    K[1, 2] -= y0
+    vt, full, campos, tanfov, principal = aaa_lowered_camera(s.viewmats[0].numpy(), K, W, rows)
+    means, scales, opac = s.means.numpy(), s.scales.numpy(), s.opacities.numpy()
+    qn = F.normalize(s.quats, dim=-1).numpy()
+    pre = O.aaa_preprocess(means, qn, scales, opac, vt, full, campos, W, rows, tanfov, principal)
+    final = O.aaa_cull_remainder(pre, W, rows)
+    dirs = means - campos
+    colors, active = O.sh_forward(s.sh_coeffs.numpy(), dirs, s.sh_degree, final["radii"])
+    feats = np.concatenate([colors, np.ones((len(means), 1), np.float32)], 1)
+    _, keys, values = O.aaa_duplicate(pre, final["radii"], final["tiles"], W, rows)
+    T = ((W + 15) // 16) * ((rows + 15) // 16)
+    _, ids, ranges = O.aaa_sort(keys, values, T)
+    bg = np.zeros(4, np.float32)
+    image, final_t, _ = O.aaa_render(W, rows, ranges, ids, pre["transforms"], pre["opacity"],
+                                     feats, bg)
+    up = np.concatenate([s.grad_image[0, y0:y0 + rows].numpy(),
+                         s.grad_alpha[0, y0:y0 + rows].numpy()], -1)
+    g = O.aaa_render_backward(W, rows, ranges, ids, pre["transforms"], pre["opacity"], feats, bg,
+                              image, final_t, np.moveaxis(up, -1, 0).copy(), screen=True,
+                              absgrad=True)
+    up_t, up_o = g["transforms"].astype(np.float32), g["opacity"].astype(np.float32)
+    O.aaa_preprocess_backward(means, qn, scales, opac, final["radii"], vt, full, campos, W, rows,
+                              np.float32(W / (2.0 * tanfov[0])), up_t, up_o)
+    O.aaa_camera_backward(means, qn, scales, final["radii"], pre["opacity"], vt, full, campos, W,
+                          rows, np.float32(max(W / (2 * tanfov[0]), rows / (2 * tanfov[1]))),
+                          up_t, up_o, np.zeros(3 * len(means), np.float32))
+    O.sh_backward(s.sh_coeffs.numpy(), dirs, s.sh_degree, final["radii"], active,
+                  g["colors"][:, :3].astype(np.float32))
+
+
 def cpu_band_step(s, rows: int, y0: int = 0):
     """One fwd+bwd of the oracle on image rows [y0, y0+rows) of view 0."""
     if s.meta["config"] == 4:
         return cpu_band_step_rade(s, rows, y0)
+    if s.meta["config"] == 3:
+        return cpu_band_step_aaa(s, rows, y0)
     from oracle import oracle as O
     import torch.nn.functional as F
     K = s.Ks[0].numpy().copy()
@@ -289,7 +353,8 @@ def run_reference(args, rank, world):
         times.append(time.perf_counter() - t0)
     frac = rows / s.height
     value = frac * len(times) / sum(times)
-    what = "RaDe-GS (projection VJP as float64 Torch autograd)" if args.config == 4 else "gs3d"
+    what = {3: "AAA-Gaussians (HIER 64/8/4 blend and replay)",
+            4: "RaDe-GS (projection VJP as float64 Torch autograd)"}.get(args.config, "gs3d")
     sample = (f"oracle (C++ restatement of dsl_splat {what}; the Warp reference needs "
               f"warp-lang, absent) with {threads} OpenMP threads, image rows 0-{rows} of "
               f"{s.height} ({frac:.3f} frame) per step; value = frame fraction / time")
@@ -316,9 +381,9 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
-def profile_traffic(kernel: str):
+def profile_traffic(kernel: str, config: int = 1):
     """dram read+write bytes per launch from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", f"{kernel}_config1.md")
+    path = os.path.join(ROOT, "profiles", f"{kernel}_config{config}.md")
     try:
         for line in open(path):
             if line.startswith("traffic_bytes_per_launch:"):
@@ -341,6 +406,15 @@ def algorithmic_bytes(kernel: str, n: int, nv: int, m: int, pixels: int, c: int 
     if kernel == "rade_render_backward":
         return (pixels * (4 * (c + 6) + 16 + 4 * (c + 6)) + 4 * m + m * (48 + 4 * c)
                 + n * (24 + 4 * c + 8 + 24))
+    # AAA HIER blend: per (tile, Gaussian) pair its id, 4x4 Gaussian-to-screen
+    # transform and opacity (68 B) and its features; per pixel the image,
+    # transmittance and count; the replay adds the upstream image and the
+    # saved forward per pixel and writes the transform, opacity, feature and
+    # screen gradients per Gaussian
+    if kernel == "aaa_render_forward":
+        return 4 * m + m * (68 + 4 * c) + pixels * (4 * c + 8)
+    if kernel == "aaa_render_backward":
+        return pixels * (8 * c + 4) + 4 * m + m * (68 + 4 * c) + n * (64 + 4 + 4 * c + 16)
     raise KeyError(kernel)
 
 
@@ -356,7 +430,7 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     pg = None
-    from dsl_splat_b200 import gs3d, rade, sharding, stages
+    from dsl_splat_b200 import aaa, gs3d, rade, sharding, stages
     from dsl_splat_b200._native import lib
     if world > 1:
         import torch.distributed as dist
@@ -375,6 +449,7 @@ def main():
     W, H = s.width, s.height
     last = {}
     is_rade = args.config == 4
+    is_aaa = args.config == 3
     if is_rade:
         # RaDe-GS: 32 extra channels blended with RGB and
         # seeded N(0,1) upstream gradients for depth, median depth and normals
@@ -387,6 +462,9 @@ def main():
         gN = torch.randn(views0, H, W, 3, generator=gen).to(dev)
 
     def rasterize_view(vm, kk):
+        if is_aaa:
+            return aaa.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
+                                 absgrad=True)
         if is_rade:
             return rade.rasterize(means, quats, scales, opac, vm, kk, W, H, sh_coeffs=sh,
                                   extra_features=extras, absgrad=True)
@@ -410,10 +488,10 @@ def main():
     sync = (sharding.GradientSync(means, quats, scales, opac, sh,
                                   group=dist.group.WORLD if pg is not None else None,
                                   buckets=args.buckets)
-            if (pg is not None or views > 1) and not is_rade else None)
+            if (pg is not None or views > 1) and not (is_rade or is_aaa) else None)
 
     def reduce_rade_grads():
-        if is_rade and pg is not None:
+        if (is_rade or is_aaa) and pg is not None:
             sharding.allreduce_parameter_grads(params, group=dist.group.WORLD)
 
     def step():
@@ -459,7 +537,7 @@ def main():
 
     # live roofline of the dominant kernel over the timed region
     res = last["res"]
-    radii = res.meta["radii"][..., 0]
+    radii = res.meta["radii"].amax(-1)
     nv = int((radii > 0).sum()) // views  # per view (one launch of each kernel)
     m = int(res.meta["tiles_per_gauss"].sum()) // views
     n = int(means.shape[0])
@@ -471,7 +549,7 @@ def main():
     peak, peak_kind = measured_peak()
     roofline = {"bound": "hbm", "kernel": kernel, "achieved": achieved, "peak": peak,
                 "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
-                "traffic": profile_traffic(kernel),
+                "traffic": profile_traffic(kernel, args.config),
                 "algorithmic_bytes_per_launch": per_launch,
                 "launch_ms": durations[kernel], "pairs": m, "visible": nv,
                 "kernel_ms": durations,
@@ -559,7 +637,8 @@ def main():
         e2e = {"value": frames_per_step * args.steps / (float(et.item()) / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": target_host.numel() * 4 + view_host.numel() * 4
                + k_host.numel() * 4, "d2h_bytes_per_step": 4,
-               "path": f"{'rade' if is_rade else 'gs3d'}.rasterize + L1 loss + backward; target "
+               "path": f"{'rade' if is_rade else 'aaa' if is_aaa else 'gs3d'}.rasterize + L1 loss "
+                       "+ backward; target "
                        "image, viewmat, K copied "
                        "H2D from pinned memory every step (prefetched one step ahead on a copy "
                        "stream) and the loss copied D2H into pinned memory every step, read by the "

@@ -211,11 +211,12 @@ def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, wi
         contrib.zero_()
         return image, final_t, contrib
     pin = Args()
-    check(lib.splat_aaa_render(features.shape[0], width, height, C, int(cull), ptr(bins["ranges"]),
-                               ptr(bins["point_list"]), pin(state.transforms), pin(state.opacity),
-                               pin(features), pin(background), ptr(bins.get("tile_order")),
-                               ptr(image), ptr(final_t), ptr(contrib), nv.stream(dev)),
-          "aaa_render")
+    with core._timed("aaa_render_forward", dev):
+        check(lib.splat_aaa_render(features.shape[0], width, height, C, int(cull),
+                                   ptr(bins["ranges"]), ptr(bins["point_list"]),
+                                   pin(state.transforms), pin(state.opacity), pin(features),
+                                   pin(background), ptr(bins.get("tile_order")), ptr(image),
+                                   ptr(final_t), ptr(contrib), nv.stream(dev)), "aaa_render")
     return image, final_t, contrib
 
 
@@ -239,11 +240,13 @@ def render_backward(state: AaaState, bins: dict, features: Tensor, background: T
     g_abs = storage[(19 + C) * n: (21 + C) * n].view(n, 2) if absgrad else None
     if n:
         pin = Args()
-        check(lib.splat_aaa_render_backward(
-            n, width, height, C, int(cull), ptr(bins["ranges"]), ptr(bins["point_list"]),
-            pin(state.transforms), pin(state.opacity), pin(features), pin(background),
-            ptr(bins.get("tile_order")), pin(image), pin(final_t), pin(grad_image), ptr(g_tr),
-            ptr(g_op), ptr(g_col), ptr(g_scr), ptr(g_abs), nv.stream(dev)), "aaa_render_backward")
+        with core._timed("aaa_render_backward", dev):
+            check(lib.splat_aaa_render_backward(
+                n, width, height, C, int(cull), ptr(bins["ranges"]), ptr(bins["point_list"]),
+                pin(state.transforms), pin(state.opacity), pin(features), pin(background),
+                ptr(bins.get("tile_order")), pin(image), pin(final_t), pin(grad_image), ptr(g_tr),
+                ptr(g_op), ptr(g_col), ptr(g_scr), ptr(g_abs), nv.stream(dev)),
+                "aaa_render_backward")
     return g_tr, g_op, g_col, g_scr, g_abs
 
 

@@ -136,10 +136,12 @@ def _emit(d, radii, tiles, centers, rects, transforms, opacity, offsets=None):
     d_out = torch.full((m,), 7, dtype=torch.int32, device=_dev())
     i_out = torch.full((m,), -7, dtype=torch.int32, device=_dev())
     s = torch.cuda.current_stream(_dev()).cuda_stream
-    check(lib.splat_aaa_emit(n, m, _t(offsets).data_ptr(), centers.data_ptr(), rects.data_ptr(),
-                             _t(radii).data_ptr(), transforms.data_ptr(), opacity.data_ptr(), W,
+    offsets_d, radii_d = _t(offsets), _t(radii)  # referenced until the kernel ran
+    check(lib.splat_aaa_emit(n, m, offsets_d.data_ptr(), centers.data_ptr(), rects.data_ptr(),
+                             radii_d.data_ptr(), transforms.data_ptr(), opacity.data_ptr(), W,
                              H, t_out.data_ptr(), d_out.data_ptr(), i_out.data_ptr(), s),
           "aaa_emit")
+    torch.cuda.synchronize(_dev())
     T = ((W + 15) // 16) * ((H + 15) // 16)
     pad = (1 << T.bit_length()) - 1
     tiles_np = t_out.cpu().numpy().view(np.uint32).astype(np.uint64)
@@ -170,10 +172,12 @@ def test_emission_and_binning_match_reference_kernel():
     point_list = torch.empty(m, dtype=torch.int32, device=_dev())
     ranges = torch.full((T, 2), 7, dtype=torch.int32, device=_dev())
     s = torch.cuda.current_stream(_dev()).cuda_stream
-    check(lib.splat_aaa_bin(len(d["means"]), m, _t(offsets).data_ptr(), args[0].data_ptr(),
-                            args[1].data_ptr(), _t(d["final_radii"]).data_ptr(),
-                            args[2].data_ptr(), args[3].data_ptr(), W, H, ws.data_ptr(),
-                            ws.numel(), point_list.data_ptr(), ranges.data_ptr(), s), "aaa_bin")
+    offsets_d, radii_d = _t(offsets), _t(d["final_radii"])
+    check(lib.splat_aaa_bin(len(d["means"]), m, offsets_d.data_ptr(), args[0].data_ptr(),
+                            args[1].data_ptr(), radii_d.data_ptr(), args[2].data_ptr(),
+                            args[3].data_ptr(), W, H, ws.data_ptr(), ws.numel(),
+                            point_list.data_ptr(), ranges.data_ptr(), s), "aaa_bin")
+    torch.cuda.synchronize(_dev())
     np.testing.assert_array_equal(point_list.cpu().numpy(), want_ids)
     np.testing.assert_array_equal(ranges.cpu().numpy(), want_ranges)
 
@@ -287,8 +291,9 @@ def test_preprocess_and_camera_adjoints_match_reference_kernels(pre_golden):
                 _t(d["filters"]) if bool(d["has_filter"]) else None, pin, flags=flags)
     f.focal_max = float(d["cam_focal"])
     sums = torch.empty(23, device=_dev())
-    check(lib.splat_aaa_camera_backward(S.ctypes_ref(f), _t(d["radii"]).data_ptr(),
-                                        _t(d["opacity"]).data_ptr(), up_t.data_ptr(),
+    radii_d, opacity_d = _t(d["radii"]), _t(d["opacity"])
+    check(lib.splat_aaa_camera_backward(S.ctypes_ref(f), radii_d.data_ptr(),
+                                        opacity_d.data_ptr(), up_t.data_ptr(),
                                         up_o.data_ptr(), sums.data_ptr(), s),
           "aaa_camera_backward")
     want = d["cam_rows"].astype(np.float64).sum(0)
