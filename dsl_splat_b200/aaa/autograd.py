@@ -26,11 +26,14 @@ class RasterizeView(torch.autograd.Function):
                 bins: dict, background, filters, absgrad_target, grad_enabled: bool):
         cull = bool(settings.culling_settings.hierarchical_4x4_culling)
         features = features.contiguous()
-        image, final_t, contrib = stages.render(state, bins, features, background, view.width,
-                                                view.height, cull)
+        needs_backward = grad_enabled and any(ctx.needs_input_grad[:9])
+        # a forward that will be differentiated keeps its blend records, so
+        # the backward reads each pixel's samples instead of replaying queues
+        image, final_t, contrib, records = stages.render(
+            state, bins, features, background, view.width, view.height, cull,
+            record_capacity=stages.RECORD_CAPACITY if needs_backward else 0)
         if means.shape[0] == 0:
             image.zero_()
-        needs_backward = grad_enabled and any(ctx.needs_input_grad[:9])
         ctx.mark_non_differentiable(final_t, contrib)
         ctx.set_materialize_grads(False)
         if not needs_backward:
@@ -38,6 +41,7 @@ class RasterizeView(torch.autograd.Function):
         ctx.save_for_backward(means, quats, scales, opacities, features, image, final_t,
                               background)
         ctx.view, ctx.settings, ctx.state, ctx.bins, ctx.cull = view, settings, state, bins, cull
+        ctx.records = records
         ctx.filters = filters
         ctx.screen = means2d is not None
         ctx.absgrad_target = absgrad_target
@@ -54,7 +58,8 @@ class RasterizeView(torch.autograd.Function):
         absgrad = ctx.absgrad_target is not None
         g_tr, g_op, g_col, g_scr, g_abs = stages.render_backward(
             st, ctx.bins, features, background, image, final_t, grad_image.contiguous(),
-            view.width, view.height, ctx.cull, screen=ctx.screen, absgrad=absgrad)
+            view.width, view.height, ctx.cull, screen=ctx.screen, absgrad=absgrad,
+            records=ctx.records)
         if absgrad:
             ctx.absgrad_target.write(g_abs)
         needs = ctx.needs_input_grad

@@ -196,10 +196,17 @@ def bin_and_sort_many(states: list[AaaState], width: int, height: int,
     return bins, values[len(states):]
 
 
+# Blend records kept by the forward for the backward: per pixel up to this
+# many blended samples (8 bytes each); pixels past it send their tile to the
+# replay kernel.
+RECORD_CAPACITY = 64
+
+
 def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, width: int,
-           height: int, cull: bool) -> tuple[Tensor, Tensor, Tensor]:
+           height: int, cull: bool, record_capacity: int = 0):
     """aaa/render_hierarchical_warp.py:694-801: color (C,H,W), final_T and
-    contributors (H,W)."""
+    contributors (H,W); with record_capacity > 0 also the blend records
+    (a dict the backward takes), else None."""
     dev = features.device
     C = features.shape[1]
     image = torch.empty((C, height, width), device=dev, dtype=torch.float32)
@@ -209,20 +216,34 @@ def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, wi
         image.zero_()
         final_t.fill_(1.0)
         contrib.zero_()
-        return image, final_t, contrib
+        return image, final_t, contrib, None
+    records = None
+    if record_capacity > 0:
+        tiles = ((width + 15) // 16) * ((height + 15) // 16)
+        slots = tiles * 256 * record_capacity
+        records = dict(capacity=record_capacity,
+                       ids=torch.empty(slots, device=dev, dtype=torch.int32),
+                       gauss=torch.empty(slots, device=dev, dtype=torch.float32),
+                       counts=torch.empty(tiles * 256, device=dev, dtype=torch.int32),
+                       overflow=torch.empty(tiles, device=dev, dtype=torch.int32))
+    rec = records or {}
     pin = Args()
     with core._timed("aaa_render_forward", dev):
         check(lib.splat_aaa_render(features.shape[0], width, height, C, int(cull),
                                    ptr(bins["ranges"]), ptr(bins["point_list"]),
                                    pin(state.transforms), pin(state.opacity), pin(features),
                                    pin(background), ptr(bins.get("tile_order")), ptr(image),
-                                   ptr(final_t), ptr(contrib), nv.stream(dev)), "aaa_render")
-    return image, final_t, contrib
+                                   ptr(final_t), ptr(contrib), rec.get("capacity", 0),
+                                   ptr(rec.get("ids")), ptr(rec.get("gauss")),
+                                   ptr(rec.get("counts")), ptr(rec.get("overflow")),
+                                   nv.stream(dev)), "aaa_render")
+    return image, final_t, contrib, records
 
 
 def render_backward(state: AaaState, bins: dict, features: Tensor, background: Tensor,
                     image: Tensor, final_t: Tensor, grad_image: Tensor, width: int, height: int,
-                    cull: bool, screen: bool = False, absgrad: bool = False):
+                    cull: bool, screen: bool = False, absgrad: bool = False,
+                    records: dict | None = None):
     """aaa/backward_render.py:140-248: gradients of the transforms (N,4,4,
     the reference's transposed layout), effective opacities (N), features
     (N,C) and, when asked, the screen translations (N,2) and their absolute
@@ -240,13 +261,15 @@ def render_backward(state: AaaState, bins: dict, features: Tensor, background: T
     g_abs = storage[(19 + C) * n: (21 + C) * n].view(n, 2) if absgrad else None
     if n:
         pin = Args()
+        rec = records or {}
         with core._timed("aaa_render_backward", dev):
             check(lib.splat_aaa_render_backward(
                 n, width, height, C, int(cull), ptr(bins["ranges"]), ptr(bins["point_list"]),
                 pin(state.transforms), pin(state.opacity), pin(features), pin(background),
                 ptr(bins.get("tile_order")), pin(image), pin(final_t), pin(grad_image), ptr(g_tr),
-                ptr(g_op), ptr(g_col), ptr(g_scr), ptr(g_abs), nv.stream(dev)),
-                "aaa_render_backward")
+                ptr(g_op), ptr(g_col), ptr(g_scr), ptr(g_abs), rec.get("capacity", 0),
+                ptr(rec.get("ids")), ptr(rec.get("gauss")), ptr(rec.get("counts")),
+                ptr(rec.get("overflow")), nv.stream(dev)), "aaa_render_backward")
     return g_tr, g_op, g_col, g_scr, g_abs
 
 
@@ -286,5 +309,5 @@ def camera_backward(view: AaaView, settings: ExtendedSettings, means: Tensor, qu
     return g_view, sums[:16].view(4, 4), sums[20:23]
 
 
-__all__ = ["AaaView", "AaaState", "preprocess", "bin_and_sort_many", "render",
+__all__ = ["AaaView", "AaaState", "RECORD_CAPACITY", "preprocess", "bin_and_sort_many", "render",
            "render_backward", "preprocess_backward", "camera_backward", "default_binning"]

@@ -79,14 +79,29 @@ template <int CHP>
 int launch_hier(const HierParams& p, int tiles, bool backward, bool screen, bool absgrad,
                 cudaStream_t s) {
   using namespace splat::aaa;
+  const unsigned blocks = static_cast<unsigned>(tiles) * kHierBlocksPerTile;
+  const bool records = backward && p.record_ids;
+  if (records) {  // the recorded tiles per pixel, then the replay of the overflowed ones
+    if (!screen)
+      aaa_record_backward_kernel<CHP, false, false><<<tiles, 256, 0, counted(s)>>>(p);
+    else if (!absgrad)
+      aaa_record_backward_kernel<CHP, true, false><<<tiles, 256, 0, counted(s)>>>(p);
+    else
+      aaa_record_backward_kernel<CHP, true, true><<<tiles, 256, 0, counted(s)>>>(p);
+  }
+  HierParams q = p;
+  if (records) {
+    q.only_flagged = p.tile_overflow;
+    q.record_ids = nullptr;
+  }
   if (!backward)
-    aaa_hier_kernel<CHP, false, false, false><<<tiles, 256, 0, counted(s)>>>(p);
+    aaa_hier_kernel<CHP, false, false, false><<<blocks, kHierThreads, 0, counted(s)>>>(q);
   else if (!screen)
-    aaa_hier_kernel<CHP, true, false, false><<<tiles, 256, 0, counted(s)>>>(p);
+    aaa_hier_kernel<CHP, true, false, false><<<blocks, kHierThreads, 0, counted(s)>>>(q);
   else if (!absgrad)
-    aaa_hier_kernel<CHP, true, true, false><<<tiles, 256, 0, counted(s)>>>(p);
+    aaa_hier_kernel<CHP, true, true, false><<<blocks, kHierThreads, 0, counted(s)>>>(q);
   else
-    aaa_hier_kernel<CHP, true, true, true><<<tiles, 256, 0, counted(s)>>>(p);
+    aaa_hier_kernel<CHP, true, true, true><<<blocks, kHierThreads, 0, counted(s)>>>(q);
   return check_launch("aaa_hier");
 }
 
@@ -286,13 +301,28 @@ int splat_aaa_bin(int n, long long pairs, const int* offsets, const float* cente
   return check_launch("aaa_bin");
 }
 
+size_t splat_aaa_record_bytes(int width, int height, int capacity) {
+  const size_t tiles = static_cast<size_t>((width + 15) / 16) * ((height + 15) / 16);
+  return tiles * 256 * (8 * static_cast<size_t>(capacity > 0 ? capacity : 0) + 4) + 4 * tiles;
+}
+
 int splat_aaa_render(int n, int width, int height, int channels, int cull, const int* ranges,
                      const int* points, const float* transforms, const float* opacity,
                      const float* colors, const float* bg, const int* tile_order, float* image,
-                     float* final_t, int* contributors, void* stream) {
+                     float* final_t, int* contributors, int record_capacity, int* record_ids,
+                     float* record_gauss, int* record_counts, int* tile_overflow, void* stream) {
   int r = check_hier_inputs(width, height, channels, ranges, points, transforms, opacity, colors, bg);
   if (r != kOk) return r;
   if (!image || !final_t || !contributors) return fail(kInvalidArgument, "null AAA blend output");
+  const bool records = record_ids != nullptr;
+  if (records && (record_capacity <= 0 || !record_gauss || !record_counts || !tile_overflow))
+    return fail(kInvalidArgument, "blend records need a capacity and all four buffers");
+  const long long tiles = static_cast<long long>((width + 15) / 16) * ((height + 15) / 16);
+  if (records && tiles * 256 * static_cast<long long>(record_capacity) >= (1LL << 40))
+    return fail(kTooLarge, "blend record capacity too large");
+  if (records &&
+      cudaMemsetAsync(tile_overflow, 0, sizeof(int) * tiles, as_stream(stream)) != cudaSuccess)
+    return check_launch("aaa_render records");
   if (n < 0) return fail(kInvalidArgument, "n < 0");
   HierParams p{};
   p.n = n;
@@ -310,6 +340,13 @@ int splat_aaa_render(int n, int width, int height, int channels, int cull, const
   p.image = image;
   p.final_t = final_t;
   p.contributors = contributors;
+  if (records) {
+    p.record_capacity = record_capacity;
+    p.record_ids = record_ids;
+    p.record_gauss = record_gauss;
+    p.record_counts = record_counts;
+    p.tile_overflow = tile_overflow;
+  }
   return dispatch_hier(p, false, false, false, as_stream(stream));
 }
 
@@ -319,7 +356,9 @@ int splat_aaa_render_backward(int n, int width, int height, int channels, int cu
                               const float* colors, const float* bg, const int* tile_order,
                               const float* image, const float* final_t, const float* pixel_grad,
                               float* grad_transforms, float* grad_opacity, float* grad_colors,
-                              float* grad_screen, float* grad_screen_abs, void* stream) {
+                              float* grad_screen, float* grad_screen_abs, int record_capacity,
+                              const int* record_ids, const float* record_gauss,
+                              const int* record_counts, const int* tile_overflow, void* stream) {
   int r = check_hier_inputs(width, height, channels, ranges, points, transforms, opacity, colors, bg);
   if (r != kOk) return r;
   if (!image || !final_t || !pixel_grad || !grad_transforms || !grad_opacity || !grad_colors)
@@ -350,6 +389,15 @@ int splat_aaa_render_backward(int n, int width, int height, int channels, int cu
   p.grad_colors = grad_colors;
   p.grad_screen = grad_screen;
   p.grad_screen_abs = grad_screen_abs;
+  if (record_ids) {
+    if (record_capacity <= 0 || !record_gauss || !record_counts || !tile_overflow)
+      return fail(kInvalidArgument, "blend records need a capacity and all four buffers");
+    p.record_capacity = record_capacity;
+    p.record_ids = const_cast<int*>(record_ids);
+    p.record_gauss = const_cast<float*>(record_gauss);
+    p.record_counts = const_cast<int*>(record_counts);
+    p.tile_overflow = const_cast<int*>(tile_overflow);
+  }
   return dispatch_hier(p, true, grad_screen != nullptr, grad_screen_abs != nullptr,
                        as_stream(stream));
 }

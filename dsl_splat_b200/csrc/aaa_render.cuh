@@ -155,6 +155,15 @@ struct HierParams {
   float* grad_colors;       // (n,C)
   float* grad_screen;       // (n,2) or null
   float* grad_screen_abs;   // (n,2) or null
+  // blend records (forward, optional): per tile-local pixel its blended
+  // samples (Gaussian id, Gaussian value) in blend order, at most
+  // record_capacity; record index ((tile * capacity + j) << 8) + local
+  int record_capacity;
+  int* record_ids;
+  float* record_gauss;
+  int* record_counts;       // (T*256): count, or -1 when the capacity overflowed
+  int* tile_overflow;       // (T): 1 when a pixel of the tile overflowed
+  const int* only_flagged;  // replay: run only the tiles whose flag is set
 };
 
 struct WarpQueues {  // per warp: two 4x4 tails, eight 2x2 mids
@@ -174,6 +183,7 @@ struct HierPixel {
   float color[CHP];
   float gradient[BWD ? CHP : 1], final_color[BWD ? CHP : 1];
   float final_T, bg_grad;
+  int records;
 };
 
 // render_adjoint.py:285-351 accumulate: one accepted sample's gradients
@@ -213,14 +223,14 @@ SPLAT_DEV void accumulate_ray_gradient(const HierParams& p, int id, float x, flo
       screen_x += d0 * g.m[3][axis];
       screen_y += d1 * g.m[3][axis];
     }
-    red_add_v2(t + axis * 4, d0, d1);
-    red_add(t + axis * 4 + 3, d3);
+    // one vector reduction per row; the screen-depth entry (column 2 of the
+    // reference's float4 blocks) receives +0 and stays zero
+    red_add_v4(t + axis * 4, d0, d1, 0.0f, d3);
   }
   const float tr0 = factor * -ym * inverse_dd;
   const float tr1 = factor * xm * inverse_dd;
   const float tr3 = factor * -(y * xm - x * ym) * inverse_dd;
-  red_add_v2(t + 12, tr0, tr1);
-  red_add(t + 15, tr3);
+  red_add_v4(t + 12, tr0, tr1, 0.0f, tr3);
   red_add(p.grad_opacity + id, gaussian * alpha_gradient);
   if (SCREEN) {
     screen_x += tr0 * g.m[3][3];
@@ -234,7 +244,7 @@ template <int CHP, bool BWD, bool SCREEN, bool ABS>
 struct HierWarp {
   const HierParams& p;
   WarpQueues& q;
-  int lane, half, hl, quad, mr;
+  int lane, half, hl, quad, mr, tile, local;
   int x0, y0, tile_x;
   unsigned half_mask, quad_mask;
   HierPixel<CHP, BWD> px;
@@ -260,6 +270,14 @@ struct HierWarp {
 #pragma unroll
       for (int c = 0; c < CHP; ++c)
         if (c < C) px.color[c] = px.color[c] + (id >= 0 ? rgb[c] : 0.0f) * alpha * px.T;
+      if (p.record_ids) {
+        if (px.records < p.record_capacity) {
+          const long long at = ((static_cast<long long>(tile) * p.record_capacity + px.records) << 8) + local;
+          p.record_ids[at] = id;
+          p.record_gauss[at] = px.hg[0];
+        }
+        ++px.records;
+      }
     } else {
       float alpha_gradient = 0.0f;
       const float weight = alpha * px.T;
@@ -270,8 +288,14 @@ struct HierWarp {
           px.color[c] = px.color[c] + v * alpha * px.T;
           const float behind = (px.final_color[c] - px.color[c]) / next_t;
           alpha_gradient += (v - behind) * px.gradient[c];
-          if (id >= 0) red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * px.gradient[c]);
+          if (id >= 0 && !(CHP == 4 && C == 4 && (reinterpret_cast<uintptr_t>(p.grad_colors) & 15) == 0))
+            red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * px.gradient[c]);
         }
+      }
+      if (id >= 0 && CHP == 4 && C == 4 && (reinterpret_cast<uintptr_t>(p.grad_colors) & 15) == 0) {
+        // RGB + the constant channel: the four colour gradients in one reduction
+        red_add_v4(p.grad_colors + 4ll * id, weight * px.gradient[0], weight * px.gradient[1],
+                   weight * px.gradient[2], weight * px.gradient[3]);
       }
       alpha_gradient *= px.T;
       alpha_gradient += (-px.final_T / (1.0f - alpha)) * px.bg_grad;
@@ -285,7 +309,7 @@ struct HierWarp {
       px.hd[j - 1] = px.hd[j];
       px.ha[j - 1] = px.ha[j];
       px.hid[j - 1] = px.hid[j];
-      if (BWD) px.hg[j - 1] = px.hg[j];
+      px.hg[j - 1] = px.hg[j];
     }
     px.hd[3] = kInf;
   }
@@ -450,11 +474,14 @@ struct HierWarp {
     if (!check_valid) px.tail_count -= 16;
   }
 
-  SPLAT_DEV void run(int tile) {
+  // local: the thread's index among the tile's 256 (the block may hold a
+  // part of the tile's warps)
+  SPLAT_DEV void run(int tile_id, int local_index) {
+    tile = tile_id;
+    local = local_index;
     const int gx = (p.width + 15) / 16;
     tile_x = tile % gx * 16;
     const int tile_y = tile / gx * 16;
-    const int local = threadIdx.x;
     lane = local & 31;
     half = lane >> 4;
     hl = lane & 15;
@@ -483,6 +510,7 @@ struct HierWarp {
     for (int c = 0; c < CHP; ++c) px.color[c] = 0.0f;
     px.final_T = 0.0f;
     px.bg_grad = 0.0f;
+    px.records = 0;
     if (BWD) {
 #pragma unroll
       for (int c = 0; c < CHP; ++c) px.gradient[c] = px.final_color[c] = 0.0f;
@@ -602,13 +630,30 @@ struct HierWarp {
       p.final_t[idx] = px.T;
       p.contributors[idx] = px.contributors;
     }
+    if (!BWD && p.record_ids) {
+      const bool overflow = px.records > p.record_capacity;
+      p.record_counts[(static_cast<long long>(tile) << 8) + local] = overflow ? -1 : px.records;
+      if (overflow) p.tile_overflow[tile] = 1;
+    }
   }
 };
 
+// The warps of a tile never interact, so a block holds two of them (a
+// quarter of the tile): smaller blocks let more warps reside per SM at the
+// kernels' register counts.  blockIdx.x = 4 * (tile slot) + quarter.
+constexpr int kHierWarps = 2;
+constexpr int kHierThreads = 32 * kHierWarps;
+constexpr int kHierBlocksPerTile = 256 / kHierThreads;
+
+// Register budget: the forward at 12 blocks (24 warps) per SM, the replay
+// (run for overflowed tiles only) at 8.
 template <int CHP, bool BWD, bool SCREEN, bool ABS>
-__global__ void __launch_bounds__(256) aaa_hier_kernel(HierParams p) {
-  __shared__ WarpQueues queues[8];
-  const int tile = p.tile_order ? p.tile_order[blockIdx.x] : static_cast<int>(blockIdx.x);
+__global__ void __launch_bounds__(kHierThreads, BWD ? 8 : 12) aaa_hier_kernel(HierParams p) {
+  __shared__ WarpQueues queues[kHierWarps];
+  const int slot = blockIdx.x / kHierBlocksPerTile;
+  const int tile = p.tile_order ? p.tile_order[slot] : slot;
+  if (p.only_flagged && !p.only_flagged[tile]) return;
+  const int local = (blockIdx.x % kHierBlocksPerTile) * kHierThreads + threadIdx.x;
   // every queue entry starts as an empty one (FLT_MAX, -1); the algorithm
   // writes each entry before reading it, so this only keeps unwritten shared
   // memory from ever being read as an id
@@ -630,7 +675,73 @@ __global__ void __launch_bounds__(256) aaa_hier_kernel(HierParams p) {
     __syncwarp();
   }
   HierWarp<CHP, BWD, SCREEN, ABS> w(p, queues[threadIdx.x >> 5]);
-  w.run(tile);
+  w.run(tile, local);
+}
+
+// ---- backward from the forward's blend records ---------------------------------
+// One thread per pixel (256 per tile): the pixel's blended samples in the
+// forward's order, each with the replay's arithmetic (alpha = min(0.99,
+// opacity * gaussian) as at insertion, T and the accumulated colour by the
+// same products), so every gradient term equals the replay's; tiles with an
+// overflowed pixel are left to the replay kernel.
+template <int CHP, bool SCREEN, bool ABS>
+__global__ void __launch_bounds__(256) aaa_record_backward_kernel(HierParams p) {
+  const int tile = blockIdx.x;
+  if (p.tile_overflow[tile]) return;
+  const int local = threadIdx.x;
+  const int gx = (p.width + 15) / 16;
+  const int tail = local >> 4, hl = local & 15, mg = hl >> 2, mr = local & 3;
+  const int x = tile % gx * 16 + 4 * (tail & 3) + 2 * (mg & 1) + (mr & 1);
+  const int y = tile / gx * 16 + 4 * (tail >> 2) + 2 * (mg >> 1) + (mr >> 1);
+  if (x >= p.width || y >= p.height) return;
+  const int count = p.record_counts[(static_cast<long long>(tile) << 8) + local];
+  if (count <= 0) return;
+  const int C = p.channels;
+  const long long idx = static_cast<long long>(y) * p.width + x;
+  const long long plane = static_cast<long long>(p.width) * p.height;
+  float gradient[CHP], final_color[CHP], color[CHP];
+  float bg_grad = 0.0f;
+  const float final_T = p.final_t_in[idx];
+#pragma unroll
+  for (int c = 0; c < CHP; ++c) {
+    gradient[c] = final_color[c] = color[c] = 0.0f;
+    if (c < C) {
+      gradient[c] = p.pixel_grad[c * plane + idx];
+      final_color[c] = p.image_in[c * plane + idx] - final_T * p.bg[c];
+      bg_grad += p.bg[c] * gradient[c];
+    }
+  }
+  const bool v4 = CHP == 4 && C == 4 && (reinterpret_cast<uintptr_t>(p.grad_colors) & 15) == 0;
+  float T = 1.0f;
+  for (int j = 0; j < count; ++j) {
+    const long long at = ((static_cast<long long>(tile) * p.record_capacity + j) << 8) + local;
+    const int id = p.record_ids[at];
+    const float gaussian = p.record_gauss[at];
+    if (id < 0 || id >= p.n) continue;  // guard: recorded ids lie in [0, n)
+    const float alpha = wp_min(0.99f, p.opacity[id] * gaussian);
+    const float next_t = T * (1.0f - alpha);
+    const float* rgb = p.colors + static_cast<long long>(id) * C;
+    float alpha_gradient = 0.0f;
+    const float weight = alpha * T;
+#pragma unroll
+    for (int c = 0; c < CHP; ++c) {
+      if (c < C) {
+        const float v = rgb[c];
+        color[c] = color[c] + v * alpha * T;
+        const float behind = (final_color[c] - color[c]) / next_t;
+        alpha_gradient += (v - behind) * gradient[c];
+        if (!v4) red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * gradient[c]);
+      }
+    }
+    if (v4)
+      red_add_v4(p.grad_colors + 4ll * id, weight * gradient[0], weight * gradient[1],
+                 weight * gradient[2], weight * gradient[3]);
+    alpha_gradient *= T;
+    alpha_gradient += (-final_T / (1.0f - alpha)) * bg_grad;
+    accumulate_ray_gradient<SCREEN, ABS>(p, id, static_cast<float>(x), static_cast<float>(y),
+                                         gaussian, alpha_gradient);
+    T = next_t;
+  }
 }
 
 }  // namespace aaa

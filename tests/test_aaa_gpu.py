@@ -241,8 +241,8 @@ def test_hier_blend_matches_reference_kernel(render_golden):
         if order:
             from dsl_splat_b200 import stages as core
             bins["tile_order"] = core.tile_order(dict(ranges=bins["ranges"]))
-        image, final_t, contrib = S.render(st, bins, _t(g["features"]), _t(g["background"]), W, H,
-                                           bool(g["cull"]))
+        image, final_t, contrib, _ = S.render(st, bins, _t(g["features"]), _t(g["background"]),
+                                              W, H, bool(g["cull"]))
         np.testing.assert_array_equal(contrib.cpu().numpy(), g["contributors"])
         np.testing.assert_array_equal(final_t.cpu().numpy(), g["final_t"])
         np.testing.assert_array_equal(image.cpu().numpy(), g["image"])
@@ -263,6 +263,38 @@ def test_hier_replay_matches_reference_kernel(render_golden):
             assert rel_l2(g_scr.cpu(), g["grad_screen"]) <= GRAD_TOL
         if absgrad:
             assert rel_l2(g_abs.cpu(), g["grad_screen_abs"]) <= GRAD_TOL
+
+
+@pytest.mark.parametrize("capacity", [64, 3])
+def test_recorded_backward_matches_reference_kernel(render_golden, capacity):
+    """The backward from the forward's blend records: a large capacity
+    records every pixel; capacity 3 overflows most tiles, which the replay
+    kernel then handles while the others use their records.  Both must give
+    the reference replay's gradients, and the forward is unchanged by
+    recording."""
+    g = render_golden
+    W, H = int(g["width"]), int(g["height"])
+    st, bins = _render_inputs(g)
+    feats, bg = _t(g["features"]), _t(g["background"])
+    image, final_t, contrib, rec = S.render(st, bins, feats, bg, W, H, bool(g["cull"]),
+                                            record_capacity=capacity)
+    np.testing.assert_array_equal(image.cpu().numpy(), g["image"])
+    np.testing.assert_array_equal(contrib.cpu().numpy(), g["contributors"])
+    overflowed = int(rec["overflow"].sum())
+    if capacity == 64:
+        assert overflowed == 0
+    else:
+        assert 0 < overflowed < len(rec["overflow"]) or overflowed == len(rec["overflow"])
+    counts = rec["counts"].cpu().numpy()
+    assert counts.max() <= capacity and (counts == -1).any() == (capacity == 3)
+    g_tr, g_op, g_col, g_scr, g_abs = S.render_backward(
+        st, bins, feats, bg, image, final_t, _t(g["upstream"]), W, H, bool(g["cull"]),
+        screen=True, absgrad=True, records=rec)
+    assert rel_l2(g_tr.reshape(-1, 16).cpu(), g["grad_transforms"]) <= GRAD_TOL
+    assert rel_l2(g_op.cpu(), g["grad_opacity"]) <= GRAD_TOL
+    assert rel_l2(g_col.cpu(), g["grad_features"]) <= GRAD_TOL
+    assert rel_l2(g_scr.cpu(), g["grad_screen"]) <= GRAD_TOL
+    assert rel_l2(g_abs.cpu(), g["grad_screen_abs"]) <= GRAD_TOL
 
 
 def test_preprocess_and_camera_adjoints_match_reference_kernels(pre_golden):
