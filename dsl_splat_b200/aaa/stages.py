@@ -197,9 +197,11 @@ def bin_and_sort_many(states: list[AaaState], width: int, height: int,
 
 
 # Blend records kept by the forward for the backward: per pixel up to this
-# many blended samples (8 bytes each); pixels past it send their tile to the
-# replay kernel.
-RECORD_CAPACITY = 64
+# many blended samples (8 bytes each; T*256*capacity slots, 3.2 GB at 1080p,
+# of which only the blended samples are written and read); a pixel past it
+# sends its tile to the replay kernel.  The BASELINE config-3 scene (2M
+# Gaussians @1080p) blends 63 samples per pixel on average, at most 146.
+RECORD_CAPACITY = 192
 
 
 def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, width: int,

@@ -265,10 +265,10 @@ def test_hier_replay_matches_reference_kernel(render_golden):
             assert rel_l2(g_abs.cpu(), g["grad_screen_abs"]) <= GRAD_TOL
 
 
-@pytest.mark.parametrize("capacity", [64, 3])
+@pytest.mark.parametrize("capacity", [256, 3])
 def test_recorded_backward_matches_reference_kernel(render_golden, capacity):
-    """The backward from the forward's blend records: a large capacity
-    records every pixel; capacity 3 overflows most tiles, which the replay
+    """The backward from the forward's blend records: capacity 256 records
+    every pixel of the golden scenes; capacity 3 overflows most tiles, which the replay
     kernel then handles while the others use their records.  Both must give
     the reference replay's gradients, and the forward is unchanged by
     recording."""
@@ -281,7 +281,7 @@ def test_recorded_backward_matches_reference_kernel(render_golden, capacity):
     np.testing.assert_array_equal(image.cpu().numpy(), g["image"])
     np.testing.assert_array_equal(contrib.cpu().numpy(), g["contributors"])
     overflowed = int(rec["overflow"].sum())
-    if capacity == 64:
+    if capacity == 256:
         assert overflowed == 0
     else:
         assert 0 < overflowed < len(rec["overflow"]) or overflowed == len(rec["overflow"])
