@@ -75,19 +75,33 @@ int bit_length(int v) {
   return b;
 }
 
+template <int CHP, bool SCREEN, bool ABS>
+int launch_record(const HierParams& p, int tiles, size_t smem, cudaStream_t s) {
+  using namespace splat::aaa;
+  auto kernel = aaa_record_backward_kernel<CHP, SCREEN, ABS>;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return check_launch("aaa_record_backward attribute");
+  kernel<<<tiles, 256, smem, counted(s)>>>(p);
+  return check_launch("aaa_record_backward");
+}
+
 template <int CHP>
 int launch_hier(const HierParams& p, int tiles, bool backward, bool screen, bool absgrad,
                 cudaStream_t s) {
   using namespace splat::aaa;
+  int r = kOk;
   const unsigned blocks = static_cast<unsigned>(tiles) * kHierBlocksPerTile;
   const bool records = backward && p.record_ids;
   if (records) {  // the recorded tiles per pixel, then the replay of the overflowed ones
+    const size_t smem = sizeof(float) * kRecordWindow * kAccStride;
     if (!screen)
-      aaa_record_backward_kernel<CHP, false, false><<<tiles, 256, 0, counted(s)>>>(p);
+      r = launch_record<CHP, false, false>(p, tiles, smem, s);
     else if (!absgrad)
-      aaa_record_backward_kernel<CHP, true, false><<<tiles, 256, 0, counted(s)>>>(p);
+      r = launch_record<CHP, true, false>(p, tiles, smem, s);
     else
-      aaa_record_backward_kernel<CHP, true, true><<<tiles, 256, 0, counted(s)>>>(p);
+      r = launch_record<CHP, true, true>(p, tiles, smem, s);
+    if (r != kOk) return r;
   }
   HierParams q = p;
   if (records) {

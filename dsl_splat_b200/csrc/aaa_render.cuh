@@ -246,6 +246,17 @@ struct HierWarp {
   WarpQueues& q;
   int lane, half, hl, quad, mr, tile, local;
   int x0, y0, tile_x;
+  int first, range_size;  // the tile's slice of point_list
+
+  // The queues and heads carry an entry's position in the tile's slice of
+  // point_list (an equivalent payload to the reference's Gaussian id: the
+  // algorithm only moves it and tests it against -1); the Gaussian id of a
+  // position, or -1.
+  SPLAT_DEV int gaussian_of(int pos) const {
+    if (pos < 0 || pos >= range_size) return -1;
+    const int g = p.points[first + pos];
+    return g >= 0 && g < p.n ? g : -1;
+  }
   unsigned half_mask, quad_mask;
   HierPixel<CHP, BWD> px;
   int x, y;
@@ -263,7 +274,7 @@ struct HierWarp {
       px.active = false;  // the sample that would terminate is not blended
       return;
     }
-    const int id = px.hid[0] < p.n ? px.hid[0] : -1;
+    const int id = gaussian_of(px.hid[0]);
     const int C = p.channels;
     const float* rgb = p.colors + static_cast<long long>(id) * C;
     if (!BWD) {
@@ -273,7 +284,7 @@ struct HierWarp {
       if (p.record_ids) {
         if (px.records < p.record_capacity) {
           const long long at = ((static_cast<long long>(tile) * p.record_capacity + px.records) << 8) + local;
-          p.record_ids[at] = id;
+          p.record_ids[at] = px.hid[0];  // the position; the backward maps it to the id
           p.record_gauss[at] = px.hg[0];
         }
         ++px.records;
@@ -401,19 +412,19 @@ struct HierWarp {
   SPLAT_DEV void front_mid(bool check_valid) {
     const int* mi = q.mid_id[quad];
     if (__any_sync(quad_mask, px.active)) {
-      const int load_id = mi[mr];
+      const int load_pos = mi[mr];
+      const int load_gid = gaussian_of(load_pos);
       float amplitude = 0.0f;
-      if ((!check_valid || load_id != -1) && load_id >= 0 && load_id < p.n)
-        amplitude = p.opacity[load_id];
+      if ((!check_valid || load_pos != -1) && load_gid >= 0) amplitude = p.opacity[load_gid];
       for (int inner = 0; inner < 4; ++inner) {
         if (px.head_count >= 4) blend();
         const int id = mi[inner];
         if (check_valid && id == -1) continue;
-        const int gid = __shfl_sync(quad_mask, load_id, inner, 4);
+        const int gid = __shfl_sync(quad_mask, load_gid, inner, 4);
         const float weight = __shfl_sync(quad_mask, amplitude, inner, 4);
         if (!px.active) continue;
         px.contributors += 1;
-        if (gid < 0 || gid >= p.n) continue;  // guard (see the header)
+        if (gid < 0) continue;  // guard (see the header)
         float power, depth;
         ray_sample(load_m4(p.transforms, gid), static_cast<float>(x), static_cast<float>(y), power,
                    depth);
@@ -433,15 +444,16 @@ struct HierWarp {
     const int* ti = q.tail_id[half];
     float* md = q.mid_d[quad];
     int* mi = q.mid_id[quad];
-    const int load_id = ti[hl];
+    const int load_pos = ti[hl];
     const int mg = hl >> 2;
     for (int batch = 0; batch < 4; ++batch) {
       if (check_valid && px.tail_count == 0) break;
       const int source = 4 * batch + mr;
       const int id = ti[source];
-      const int gid = __shfl_sync(half_mask, load_id, source, 16);
+      const int gpos = __shfl_sync(half_mask, load_pos, source, 16);
+      const int gid = gaussian_of(gpos);
       float depth = kInf;
-      if ((!check_valid || gid != -1) && gid >= 0 && gid < p.n) {
+      if ((!check_valid || gpos != -1) && gid >= 0) {
         float power;
         ray_sample(load_m4(p.transforms, gid), static_cast<float>(x0 + 1 + 2 * (mg & 1)),
                    static_cast<float>(y0 + 1 + 2 * (mg >> 1)), power, depth);
@@ -528,12 +540,14 @@ struct HierWarp {
         }
       }
     }
-    const int first = p.ranges[2 * tile], last = p.ranges[2 * tile + 1];
+    first = p.ranges[2 * tile];
+    const int last = p.ranges[2 * tile + 1];
+    range_size = last - first;
     const int tail0 = (tail & ~1);
     for (int progress = first; progress < last; progress += 32) {
       if (!__any_sync(kFull, px.active)) break;
-      int gid = progress + lane < last ? p.points[progress + lane] : -1;
-      if (gid >= p.n) gid = -1;  // guard: sorted ids always lie in [0, n)
+      const int pos = progress + lane < last ? progress + lane - first : -1;
+      const int gid = gaussian_of(pos);
       M4 g = {};
       float amplitude = 0.0f;
       if (gid >= 0) {
@@ -560,7 +574,7 @@ struct HierWarp {
                      power, depth);
         }
         q.tail_d[h][32 + lane] = depth;
-        q.tail_id[h][32 + lane] = depth == kInf ? -1 : gid;
+        q.tail_id[h][32 + lane] = depth == kInf ? -1 : pos;
       }
       __syncwarp(kFull);
       sort_batch();
@@ -684,63 +698,181 @@ __global__ void __launch_bounds__(kHierThreads, BWD ? 8 : 12) aaa_hier_kernel(Hi
 // opacity * gaussian) as at insertion, T and the accumulated colour by the
 // same products), so every gradient term equals the replay's; tiles with an
 // overflowed pixel are left to the replay kernel.
+//
+// The terms are summed per tile in shared memory before they reach global
+// memory: a sample is recorded by its position in the tile's slice of
+// point_list, and the slice is taken in windows of kRecordWindow positions.
+// In window w every thread walks its records (in blend order) while their
+// positions lie below the window's end, adding each term into the window's
+// accumulator row with a shared-memory atomic (a position below the window,
+// i.e. blended out of list order, goes straight to global memory); then the
+// rows are added to the global gradients with one vector reduction per
+// Gaussian and group of terms.  A Gaussian blended by many pixels of a tile
+// so costs one set of global reductions per tile instead of one per sample.
+constexpr int kRecordWindow = 512;
+// accumulator row: transform rows 0-2 (d0, d1, d3) and the translation row
+// (t0, t1, t3), opacity, screen x / y, |screen| x / y, four colours
+constexpr int kAccTransform = 0, kAccOpacity = 12, kAccScreen = 13, kAccAbs = 15,
+              kAccColor = 17, kAccStride = 21;
+
+template <int CHP, bool SCREEN, bool ABS>
+SPLAT_DEV void sample_gradients(const HierParams& p, int id, float x, float y, float gaussian,
+                                float alpha_gradient, float out[kAccStride]) {
+  const M4 g = load_m4(p.transforms, id);
+  float a[4], b[4];
+  plane_of(g, 0, x, a);
+  plane_of(g, 1, y, b);
+  const float nx[3] = {a[0], a[1], a[2]}, ny[3] = {b[0], b[1], b[2]};
+  const float dx = a[3], dy = b[3];
+  float moment[3], direction[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) moment[k] = dx * ny[k] - dy * nx[k];
+  direction[0] = nx[1] * ny[2] - nx[2] * ny[1];
+  direction[1] = nx[2] * ny[0] - nx[0] * ny[2];
+  direction[2] = nx[0] * ny[1] - nx[1] * ny[0];
+  const float dd = rdot3(direction, direction), mm = rdot3(moment, moment);
+  const float xx = rdot3(nx, nx), yy = rdot3(ny, ny), xy = rdot3(nx, ny);
+  const float ym = rdot3(ny, moment), xm = rdot3(nx, moment);
+  const float xyy = x * yy, yxx = y * xx, ndy = -dy, cross = dy * x - dx * y;
+  const float factor = p.opacity[id] * alpha_gradient * gaussian;
+  const float inverse_dd = __frcp_rn(dd);
+  const float ratio = mm / dd * inverse_dd;
+  float screen_x = 0.0f, screen_y = 0.0f;
+#pragma unroll
+  for (int axis = 0; axis < 3; ++axis) {
+    const float dd0 = yy * nx[axis] - xy * ny[axis];
+    const float dd1 = xx * ny[axis] - xy * nx[axis];
+    const float dd3 = (xy * (y * nx[axis] + x * ny[axis]) - xyy * nx[axis]) - yxx * ny[axis];
+    const float d0 = factor * (ratio * dd0 - (ndy * moment[axis]) * inverse_dd);
+    const float d1 = factor * (ratio * dd1 - (dx * moment[axis]) * inverse_dd);
+    const float d3 = factor * (ratio * dd3 - (cross * moment[axis]) * inverse_dd);
+    screen_x += d0 * g.m[3][axis];
+    screen_y += d1 * g.m[3][axis];
+    out[kAccTransform + 3 * axis] = d0;
+    out[kAccTransform + 3 * axis + 1] = d1;
+    out[kAccTransform + 3 * axis + 2] = d3;
+  }
+  const float tr0 = factor * -ym * inverse_dd;
+  const float tr1 = factor * xm * inverse_dd;
+  out[kAccTransform + 9] = tr0;
+  out[kAccTransform + 10] = tr1;
+  out[kAccTransform + 11] = factor * -(y * xm - x * ym) * inverse_dd;
+  out[kAccOpacity] = gaussian * alpha_gradient;
+  screen_x += tr0 * g.m[3][3];
+  screen_y += tr1 * g.m[3][3];
+  out[kAccScreen] = SCREEN ? screen_x : 0.0f;
+  out[kAccScreen + 1] = SCREEN ? screen_y : 0.0f;
+  out[kAccAbs] = ABS ? fabsf(screen_x) : 0.0f;
+  out[kAccAbs + 1] = ABS ? fabsf(screen_y) : 0.0f;
+}
+
+// one accumulator row (or one sample's terms) into the global gradients
+template <int CHP, bool SCREEN, bool ABS>
+SPLAT_DEV void flush_row(const HierParams& p, int id, const float* v) {
+  float* t = p.grad_transforms + 16ll * id;
+#pragma unroll
+  for (int axis = 0; axis < 4; ++axis)
+    red_add_v4(t + 4 * axis, v[kAccTransform + 3 * axis], v[kAccTransform + 3 * axis + 1], 0.0f,
+               v[kAccTransform + 3 * axis + 2]);
+  red_add(p.grad_opacity + id, v[kAccOpacity]);
+  if (SCREEN) red_add_v2(p.grad_screen + 2ll * id, v[kAccScreen], v[kAccScreen + 1]);
+  if (ABS) red_add_v2(p.grad_screen_abs + 2ll * id, v[kAccAbs], v[kAccAbs + 1]);
+  if (CHP == 4 && p.channels == 4)
+    red_add_v4(p.grad_colors + 4ll * id, v[kAccColor], v[kAccColor + 1], v[kAccColor + 2],
+               v[kAccColor + 3]);
+}
+
 template <int CHP, bool SCREEN, bool ABS>
 __global__ void __launch_bounds__(256) aaa_record_backward_kernel(HierParams p) {
+  extern __shared__ float s_acc[];  // kRecordWindow rows of kAccStride
   const int tile = blockIdx.x;
   if (p.tile_overflow[tile]) return;
+  const int first = p.ranges[2 * tile], range_size = p.ranges[2 * tile + 1] - first;
+  if (range_size <= 0) return;
   const int local = threadIdx.x;
   const int gx = (p.width + 15) / 16;
   const int tail = local >> 4, hl = local & 15, mg = hl >> 2, mr = local & 3;
   const int x = tile % gx * 16 + 4 * (tail & 3) + 2 * (mg & 1) + (mr & 1);
   const int y = tile / gx * 16 + 4 * (tail >> 2) + 2 * (mg >> 1) + (mr >> 1);
-  if (x >= p.width || y >= p.height) return;
-  const int count = p.record_counts[(static_cast<long long>(tile) << 8) + local];
-  if (count <= 0) return;
+  const bool inside = x < p.width && y < p.height;
+  const int count = inside ? p.record_counts[(static_cast<long long>(tile) << 8) + local] : 0;
   const int C = p.channels;
-  const long long idx = static_cast<long long>(y) * p.width + x;
+  const long long idx = inside ? static_cast<long long>(y) * p.width + x : 0;
   const long long plane = static_cast<long long>(p.width) * p.height;
   float gradient[CHP], final_color[CHP], color[CHP];
   float bg_grad = 0.0f;
-  const float final_T = p.final_t_in[idx];
+  const float final_T = inside ? p.final_t_in[idx] : 0.0f;
 #pragma unroll
   for (int c = 0; c < CHP; ++c) {
     gradient[c] = final_color[c] = color[c] = 0.0f;
-    if (c < C) {
+    if (c < C && inside) {
       gradient[c] = p.pixel_grad[c * plane + idx];
       final_color[c] = p.image_in[c * plane + idx] - final_T * p.bg[c];
       bg_grad += p.bg[c] * gradient[c];
     }
   }
-  const bool v4 = CHP == 4 && C == 4 && (reinterpret_cast<uintptr_t>(p.grad_colors) & 15) == 0;
+  const bool rows_hold_colors = CHP == 4 && C == 4;
   float T = 1.0f;
-  for (int j = 0; j < count; ++j) {
-    const long long at = ((static_cast<long long>(tile) * p.record_capacity + j) << 8) + local;
-    const int id = p.record_ids[at];
-    const float gaussian = p.record_gauss[at];
-    if (id < 0 || id >= p.n) continue;  // guard: recorded ids lie in [0, n)
-    const float alpha = wp_min(0.99f, p.opacity[id] * gaussian);
-    const float next_t = T * (1.0f - alpha);
-    const float* rgb = p.colors + static_cast<long long>(id) * C;
-    float alpha_gradient = 0.0f;
-    const float weight = alpha * T;
+  int j = 0;
+  const long long base = static_cast<long long>(tile) * p.record_capacity;
+  for (int w0 = 0; w0 < range_size; w0 += kRecordWindow) {
+    const int w1 = w0 + kRecordWindow;
+    for (int k = threadIdx.x; k < kRecordWindow * kAccStride; k += blockDim.x) s_acc[k] = 0.0f;
+    __syncthreads();
+    while (j < count) {
+      const long long at = ((base + j) << 8) + local;
+      const int pos = p.record_ids[at];
+      if (pos >= w1) break;  // a later window
+      const float gaussian = p.record_gauss[at];
+      ++j;
+      const int id = pos >= 0 && pos < range_size ? p.points[first + pos] : -1;
+      if (id < 0 || id >= p.n) continue;  // guard: recorded positions lie in the slice
+      const float alpha = wp_min(0.99f, p.opacity[id] * gaussian);
+      const float next_t = T * (1.0f - alpha);
+      const float* rgb = p.colors + static_cast<long long>(id) * C;
+      float alpha_gradient = 0.0f;
+      const float weight = alpha * T;
+      float terms[kAccStride];
 #pragma unroll
-    for (int c = 0; c < CHP; ++c) {
-      if (c < C) {
-        const float v = rgb[c];
-        color[c] = color[c] + v * alpha * T;
-        const float behind = (final_color[c] - color[c]) / next_t;
-        alpha_gradient += (v - behind) * gradient[c];
-        if (!v4) red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * gradient[c]);
+      for (int c = 0; c < CHP; ++c) {
+        if (c < C) {
+          const float v = rgb[c];
+          color[c] = color[c] + v * alpha * T;
+          const float behind = (final_color[c] - color[c]) / next_t;
+          alpha_gradient += (v - behind) * gradient[c];
+          if (rows_hold_colors) terms[kAccColor + c] = weight * gradient[c];
+          else red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * gradient[c]);
+        }
+      }
+      alpha_gradient *= T;
+      alpha_gradient += (-final_T / (1.0f - alpha)) * bg_grad;
+      sample_gradients<CHP, SCREEN, ABS>(p, id, static_cast<float>(x), static_cast<float>(y),
+                                         gaussian, alpha_gradient, terms);
+      if (!rows_hold_colors) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) terms[kAccColor + c] = 0.0f;
+      }
+      T = next_t;
+      if (pos >= w0) {
+        float* row = s_acc + (pos - w0) * kAccStride;
+#pragma unroll
+        for (int k = 0; k < kAccStride; ++k) atomicAdd(row + k, terms[k]);
+      } else {
+        flush_row<CHP, SCREEN, ABS>(p, id, terms);  // blended out of list order
       }
     }
-    if (v4)
-      red_add_v4(p.grad_colors + 4ll * id, weight * gradient[0], weight * gradient[1],
-                 weight * gradient[2], weight * gradient[3]);
-    alpha_gradient *= T;
-    alpha_gradient += (-final_T / (1.0f - alpha)) * bg_grad;
-    accumulate_ray_gradient<SCREEN, ABS>(p, id, static_cast<float>(x), static_cast<float>(y),
-                                         gaussian, alpha_gradient);
-    T = next_t;
+    __syncthreads();
+    const int rows = min(kRecordWindow, range_size - w0);
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+      const float* row = s_acc + r * kAccStride;
+      bool any = false;
+#pragma unroll
+      for (int k = 0; k < kAccStride; ++k) any |= row[k] != 0.0f;
+      if (!any) continue;
+      const int id = p.points[first + w0 + r];
+      if (id >= 0 && id < p.n) flush_row<CHP, SCREEN, ABS>(p, id, row);
+    }
+    __syncthreads();
   }
 }
 
