@@ -78,11 +78,7 @@ int bit_length(int v) {
 template <int CHP, bool SCREEN, bool ABS>
 int launch_record(const HierParams& p, int tiles, size_t smem, cudaStream_t s) {
   using namespace splat::aaa;
-  auto kernel = aaa_record_backward_kernel<CHP, SCREEN, ABS>;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) != cudaSuccess)
-    return check_launch("aaa_record_backward attribute");
-  kernel<<<tiles, 256, smem, counted(s)>>>(p);
+  aaa_record_backward_kernel<CHP, SCREEN, ABS><<<tiles, 256, smem, counted(s)>>>(p);
   return check_launch("aaa_record_backward");
 }
 
@@ -94,7 +90,7 @@ int launch_hier(const HierParams& p, int tiles, bool backward, bool screen, bool
   const unsigned blocks = static_cast<unsigned>(tiles) * kHierBlocksPerTile;
   const bool records = backward && p.record_ids;
   if (records) {  // the recorded tiles per pixel, then the replay of the overflowed ones
-    const size_t smem = sizeof(float) * kRecordWindow * kAccStride;
+    const size_t smem = 0;
     if (!screen)
       r = launch_record<CHP, false, false>(p, tiles, smem, s);
     else if (!absgrad)

@@ -697,19 +697,10 @@ __global__ void __launch_bounds__(kHierThreads, BWD ? 8 : 12) aaa_hier_kernel(Hi
 // forward's order, each with the replay's arithmetic (alpha = min(0.99,
 // opacity * gaussian) as at insertion, T and the accumulated colour by the
 // same products), so every gradient term equals the replay's; tiles with an
-// overflowed pixel are left to the replay kernel.
-//
-// The terms are summed per tile in shared memory before they reach global
-// memory: a sample is recorded by its position in the tile's slice of
-// point_list, and the slice is taken in windows of kRecordWindow positions.
-// In window w every thread walks its records (in blend order) while their
-// positions lie below the window's end, adding each term into the window's
-// accumulator row with a shared-memory atomic (a position below the window,
-// i.e. blended out of list order, goes straight to global memory); then the
-// rows are added to the global gradients with one vector reduction per
-// Gaussian and group of terms.  A Gaussian blended by many pixels of a tile
-// so costs one set of global reductions per tile instead of one per sample.
-constexpr int kRecordWindow = 512;
+// overflowed pixel are left to the replay kernel.  A record holds the
+// sample's position in the tile's slice of point_list and its Gaussian
+// value.  Each sample's 21 terms (transform 12, opacity, screen 2, |screen|
+// 2, colours 4) leave as vector reductions into global memory.
 // accumulator row: transform rows 0-2 (d0, d1, d3) and the translation row
 // (t0, t1, t3), opacity, screen x / y, |screen| x / y, four colours
 constexpr int kAccTransform = 0, kAccOpacity = 12, kAccScreen = 13, kAccAbs = 15,
@@ -784,7 +775,6 @@ SPLAT_DEV void flush_row(const HierParams& p, int id, const float* v) {
 
 template <int CHP, bool SCREEN, bool ABS>
 __global__ void __launch_bounds__(256) aaa_record_backward_kernel(HierParams p) {
-  extern __shared__ float s_acc[];  // kRecordWindow rows of kAccStride
   const int tile = blockIdx.x;
   if (p.tile_overflow[tile]) return;
   const int first = p.ranges[2 * tile], range_size = p.ranges[2 * tile + 1] - first;
@@ -794,85 +784,58 @@ __global__ void __launch_bounds__(256) aaa_record_backward_kernel(HierParams p) 
   const int tail = local >> 4, hl = local & 15, mg = hl >> 2, mr = local & 3;
   const int x = tile % gx * 16 + 4 * (tail & 3) + 2 * (mg & 1) + (mr & 1);
   const int y = tile / gx * 16 + 4 * (tail >> 2) + 2 * (mg >> 1) + (mr >> 1);
-  const bool inside = x < p.width && y < p.height;
-  const int count = inside ? p.record_counts[(static_cast<long long>(tile) << 8) + local] : 0;
+  if (x >= p.width || y >= p.height) return;
+  const int count = p.record_counts[(static_cast<long long>(tile) << 8) + local];
+  if (count <= 0) return;
   const int C = p.channels;
-  const long long idx = inside ? static_cast<long long>(y) * p.width + x : 0;
+  const long long idx = static_cast<long long>(y) * p.width + x;
   const long long plane = static_cast<long long>(p.width) * p.height;
   float gradient[CHP], final_color[CHP], color[CHP];
   float bg_grad = 0.0f;
-  const float final_T = inside ? p.final_t_in[idx] : 0.0f;
+  const float final_T = p.final_t_in[idx];
 #pragma unroll
   for (int c = 0; c < CHP; ++c) {
     gradient[c] = final_color[c] = color[c] = 0.0f;
-    if (c < C && inside) {
+    if (c < C) {
       gradient[c] = p.pixel_grad[c * plane + idx];
       final_color[c] = p.image_in[c * plane + idx] - final_T * p.bg[c];
       bg_grad += p.bg[c] * gradient[c];
     }
   }
   const bool rows_hold_colors = CHP == 4 && C == 4;
-  float T = 1.0f;
-  int j = 0;
   const long long base = static_cast<long long>(tile) * p.record_capacity;
-  for (int w0 = 0; w0 < range_size; w0 += kRecordWindow) {
-    const int w1 = w0 + kRecordWindow;
-    for (int k = threadIdx.x; k < kRecordWindow * kAccStride; k += blockDim.x) s_acc[k] = 0.0f;
-    __syncthreads();
-    while (j < count) {
-      const long long at = ((base + j) << 8) + local;
-      const int pos = p.record_ids[at];
-      if (pos >= w1) break;  // a later window
-      const float gaussian = p.record_gauss[at];
-      ++j;
-      const int id = pos >= 0 && pos < range_size ? p.points[first + pos] : -1;
-      if (id < 0 || id >= p.n) continue;  // guard: recorded positions lie in the slice
-      const float alpha = wp_min(0.99f, p.opacity[id] * gaussian);
-      const float next_t = T * (1.0f - alpha);
-      const float* rgb = p.colors + static_cast<long long>(id) * C;
-      float alpha_gradient = 0.0f;
-      const float weight = alpha * T;
-      float terms[kAccStride];
+  float T = 1.0f;
+  for (int j = 0; j < count; ++j) {
+    const long long at = ((base + j) << 8) + local;
+    const int pos = p.record_ids[at];
+    const float gaussian = p.record_gauss[at];
+    const int id = pos >= 0 && pos < range_size ? p.points[first + pos] : -1;
+    if (id < 0 || id >= p.n) continue;  // guard: recorded positions lie in the slice
+    const float alpha = wp_min(0.99f, p.opacity[id] * gaussian);
+    const float next_t = T * (1.0f - alpha);
+    const float* rgb = p.colors + static_cast<long long>(id) * C;
+    float alpha_gradient = 0.0f;
+    const float weight = alpha * T;
+    float terms[kAccStride];
 #pragma unroll
-      for (int c = 0; c < CHP; ++c) {
-        if (c < C) {
-          const float v = rgb[c];
-          color[c] = color[c] + v * alpha * T;
-          const float behind = (final_color[c] - color[c]) / next_t;
-          alpha_gradient += (v - behind) * gradient[c];
-          if (rows_hold_colors) terms[kAccColor + c] = weight * gradient[c];
-          else red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * gradient[c]);
-        }
-      }
-      alpha_gradient *= T;
-      alpha_gradient += (-final_T / (1.0f - alpha)) * bg_grad;
-      sample_gradients<CHP, SCREEN, ABS>(p, id, static_cast<float>(x), static_cast<float>(y),
-                                         gaussian, alpha_gradient, terms);
-      if (!rows_hold_colors) {
+    for (int c = 0; c < 4; ++c) terms[kAccColor + c] = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) terms[kAccColor + c] = 0.0f;
-      }
-      T = next_t;
-      if (pos >= w0) {
-        float* row = s_acc + (pos - w0) * kAccStride;
-#pragma unroll
-        for (int k = 0; k < kAccStride; ++k) atomicAdd(row + k, terms[k]);
-      } else {
-        flush_row<CHP, SCREEN, ABS>(p, id, terms);  // blended out of list order
+    for (int c = 0; c < CHP; ++c) {
+      if (c < C) {
+        const float v = rgb[c];
+        color[c] = color[c] + v * alpha * T;
+        const float behind = (final_color[c] - color[c]) / next_t;
+        alpha_gradient += (v - behind) * gradient[c];
+        if (rows_hold_colors) terms[kAccColor + c] = weight * gradient[c];
+        else red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * gradient[c]);
       }
     }
-    __syncthreads();
-    const int rows = min(kRecordWindow, range_size - w0);
-    for (int r = threadIdx.x; r < rows; r += blockDim.x) {
-      const float* row = s_acc + r * kAccStride;
-      bool any = false;
-#pragma unroll
-      for (int k = 0; k < kAccStride; ++k) any |= row[k] != 0.0f;
-      if (!any) continue;
-      const int id = p.points[first + w0 + r];
-      if (id >= 0 && id < p.n) flush_row<CHP, SCREEN, ABS>(p, id, row);
-    }
-    __syncthreads();
+    alpha_gradient *= T;
+    alpha_gradient += (-final_T / (1.0f - alpha)) * bg_grad;
+    sample_gradients<CHP, SCREEN, ABS>(p, id, static_cast<float>(x), static_cast<float>(y),
+                                       gaussian, alpha_gradient, terms);
+    flush_row<CHP, SCREEN, ABS>(p, id, terms);
+    T = next_t;
   }
 }
 
