@@ -69,16 +69,29 @@ SPLAT_DEV float closest_ray(const float a[4], const float b[4], float pos[4]) {
   return rdot3(m, s);
 }
 
-// :60-64 sample: -distance^2 / 2 and the screen depth of the ray of (x, y)
-SPLAT_DEV void ray_sample(const M4& g, float x, float y, float& power, float& depth) {
-  float a[4], b[4], pos[4];
-  plane_of(g, 0, x, a);
-  plane_of(g, 1, y, b);
+// :60-64 sample: -distance^2 / 2 and the screen depth of the ray of (x, y).
+// Kept out of line (as region_frustum), with the transform passed by value
+// in registers: the blend calls it from seven places, and one copy keeps
+// the kernel's instruction footprint small.
+__device__ __noinline__ float2 ray_sample_rows(float4 r0, float4 r1, float4 r2, float4 r3, float x,
+                                               float y) {
+  const float a[4] = {r0.x - r3.x * x, r0.y - r3.y * x, r0.z - r3.z * x, r0.w - r3.w * x};
+  const float b[4] = {r1.x - r3.x * y, r1.y - r3.y * y, r1.z - r3.z * y, r1.w - r3.w * y};
+  float pos[4];
   const float sq = closest_ray(a, b, pos);
-  const float g2[4] = {g.m[2][0], g.m[2][1], g.m[2][2], g.m[2][3]};
-  const float g3[4] = {g.m[3][0], g.m[3][1], g.m[3][2], g.m[3][3]};
-  depth = rdot4(g2, pos) * __frcp_rn(rdot4(g3, pos));
-  power = -0.5f * sq;
+  const float g2[4] = {r2.x, r2.y, r2.z, r2.w};
+  const float g3[4] = {r3.x, r3.y, r3.z, r3.w};
+  return make_float2(-0.5f * sq, rdot4(g2, pos) * __frcp_rn(rdot4(g3, pos)));
+}
+
+SPLAT_DEV float4 row4(const M4& g, int r) {
+  return make_float4(g.m[r][0], g.m[r][1], g.m[r][2], g.m[r][3]);
+}
+
+SPLAT_DEV void ray_sample(const M4& g, float x, float y, float& power, float& depth) {
+  const float2 v = ray_sample_rows(row4(g, 0), row4(g, 1), row4(g, 2), row4(g, 3), x, y);
+  power = v.x;
+  depth = v.y;
 }
 
 SPLAT_DEV void rtransform(const M4& g, const float p[4], float out[4]) {
@@ -91,7 +104,17 @@ SPLAT_DEV void rtransform(const M4& g, const float p[4], float out[4]) {
 
 // :67-120 frustum: half the smallest squared Gaussian-space distance from
 // the centre to the frustum of the w x h pixel rectangle at (x, y)
-SPLAT_DEV float region_frustum(const M4& g, float x, float y, float w, float h) {
+__device__ __noinline__ float region_frustum_rows(float4 r0, float4 r1, float4 r2, float4 r3,
+                                                  float x, float y, float w, float h) {
+  M4 g;
+  const float4 rows[4] = {r0, r1, r2, r3};
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    g.m[r][0] = rows[r].x;
+    g.m[r][1] = rows[r].y;
+    g.m[r][2] = rows[r].z;
+    g.m[r][3] = rows[r].w;
+  }
   const float start[3] = {x, y, -1.0f}, extent[3] = {w, h, 2.0f};
   auto inside = [&](const float p[4], int axis) {
     const float delta = p[axis] - start[axis] * p[3];
@@ -128,6 +151,10 @@ SPLAT_DEV float region_frustum(const M4& g, float x, float y, float w, float h) 
     test_edge(other, ay);
   }
   return 0.5f * best;
+}
+
+SPLAT_DEV float region_frustum(const M4& g, float x, float y, float w, float h) {
+  return region_frustum_rows(row4(g, 0), row4(g, 1), row4(g, 2), row4(g, 3), x, y, w, h);
 }
 
 // ---- kernel state -------------------------------------------------------------------
@@ -284,7 +311,7 @@ struct HierWarp {
       if (p.record_ids) {
         if (px.records < p.record_capacity) {
           const long long at = ((static_cast<long long>(tile) * p.record_capacity + px.records) << 8) + local;
-          p.record_ids[at] = px.hid[0];  // the position; the backward maps it to the id
+          p.record_ids[at] = id;
           p.record_gauss[at] = px.hg[0];
         }
         ++px.records;
@@ -706,13 +733,39 @@ __global__ void __launch_bounds__(kHierThreads, BWD ? 8 : 12) aaa_hier_kernel(Hi
 constexpr int kAccTransform = 0, kAccOpacity = 12, kAccScreen = 13, kAccAbs = 15,
               kAccColor = 17, kAccStride = 21;
 
-template <int CHP, bool SCREEN, bool ABS>
-SPLAT_DEV void sample_gradients(const HierParams& p, int id, float x, float y, float gaussian,
+// The Gaussian data a sample's gradient needs: transform rows 0, 1 and 3 (row
+// 2, the screen depth, does not enter the ray gradient), opacity and up to
+// four colours.
+struct SampleData {
+  float4 r0, r1, r3, rgb;
+  float opacity;
+};
+
+SPLAT_DEV SampleData load_sample(const HierParams& p, int id) {
+  SampleData d;
+  const float4* rows = reinterpret_cast<const float4*>(p.transforms) + 4ll * id;
+  d.r0 = rows[0];
+  d.r1 = rows[1];
+  d.r3 = rows[3];
+  d.opacity = p.opacity[id];
+  d.rgb = p.channels == 4 ? reinterpret_cast<const float4*>(p.colors)[id]
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  return d;
+}
+
+// render_adjoint.py:285-351 for one sample, the terms in an accumulator row
+template <bool SCREEN, bool ABS>
+SPLAT_DEV void sample_gradients(const SampleData& s, float x, float y, float gaussian,
                                 float alpha_gradient, float out[kAccStride]) {
-  const M4 g = load_m4(p.transforms, id);
+  const float g0[4] = {s.r0.x, s.r0.y, s.r0.z, s.r0.w};
+  const float g1[4] = {s.r1.x, s.r1.y, s.r1.z, s.r1.w};
+  const float g3[4] = {s.r3.x, s.r3.y, s.r3.z, s.r3.w};
   float a[4], b[4];
-  plane_of(g, 0, x, a);
-  plane_of(g, 1, y, b);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    a[k] = g0[k] - g3[k] * x;
+    b[k] = g1[k] - g3[k] * y;
+  }
   const float nx[3] = {a[0], a[1], a[2]}, ny[3] = {b[0], b[1], b[2]};
   const float dx = a[3], dy = b[3];
   float moment[3], direction[3];
@@ -725,7 +778,7 @@ SPLAT_DEV void sample_gradients(const HierParams& p, int id, float x, float y, f
   const float xx = rdot3(nx, nx), yy = rdot3(ny, ny), xy = rdot3(nx, ny);
   const float ym = rdot3(ny, moment), xm = rdot3(nx, moment);
   const float xyy = x * yy, yxx = y * xx, ndy = -dy, cross = dy * x - dx * y;
-  const float factor = p.opacity[id] * alpha_gradient * gaussian;
+  const float factor = s.opacity * alpha_gradient * gaussian;
   const float inverse_dd = __frcp_rn(dd);
   const float ratio = mm / dd * inverse_dd;
   float screen_x = 0.0f, screen_y = 0.0f;
@@ -737,8 +790,8 @@ SPLAT_DEV void sample_gradients(const HierParams& p, int id, float x, float y, f
     const float d0 = factor * (ratio * dd0 - (ndy * moment[axis]) * inverse_dd);
     const float d1 = factor * (ratio * dd1 - (dx * moment[axis]) * inverse_dd);
     const float d3 = factor * (ratio * dd3 - (cross * moment[axis]) * inverse_dd);
-    screen_x += d0 * g.m[3][axis];
-    screen_y += d1 * g.m[3][axis];
+    screen_x += d0 * g3[axis];
+    screen_y += d1 * g3[axis];
     out[kAccTransform + 3 * axis] = d0;
     out[kAccTransform + 3 * axis + 1] = d1;
     out[kAccTransform + 3 * axis + 2] = d3;
@@ -749,16 +802,16 @@ SPLAT_DEV void sample_gradients(const HierParams& p, int id, float x, float y, f
   out[kAccTransform + 10] = tr1;
   out[kAccTransform + 11] = factor * -(y * xm - x * ym) * inverse_dd;
   out[kAccOpacity] = gaussian * alpha_gradient;
-  screen_x += tr0 * g.m[3][3];
-  screen_y += tr1 * g.m[3][3];
-  out[kAccScreen] = SCREEN ? screen_x : 0.0f;
-  out[kAccScreen + 1] = SCREEN ? screen_y : 0.0f;
-  out[kAccAbs] = ABS ? fabsf(screen_x) : 0.0f;
-  out[kAccAbs + 1] = ABS ? fabsf(screen_y) : 0.0f;
+  screen_x += tr0 * g3[3];
+  screen_y += tr1 * g3[3];
+  out[kAccScreen] = screen_x;
+  out[kAccScreen + 1] = screen_y;
+  out[kAccAbs] = fabsf(screen_x);
+  out[kAccAbs + 1] = fabsf(screen_y);
 }
 
-// one accumulator row (or one sample's terms) into the global gradients
-template <int CHP, bool SCREEN, bool ABS>
+// one sample's terms into the global gradients
+template <bool SCREEN, bool ABS, bool COLORS4>
 SPLAT_DEV void flush_row(const HierParams& p, int id, const float* v) {
   float* t = p.grad_transforms + 16ll * id;
 #pragma unroll
@@ -768,17 +821,15 @@ SPLAT_DEV void flush_row(const HierParams& p, int id, const float* v) {
   red_add(p.grad_opacity + id, v[kAccOpacity]);
   if (SCREEN) red_add_v2(p.grad_screen + 2ll * id, v[kAccScreen], v[kAccScreen + 1]);
   if (ABS) red_add_v2(p.grad_screen_abs + 2ll * id, v[kAccAbs], v[kAccAbs + 1]);
-  if (CHP == 4 && p.channels == 4)
+  if (COLORS4)
     red_add_v4(p.grad_colors + 4ll * id, v[kAccColor], v[kAccColor + 1], v[kAccColor + 2],
                v[kAccColor + 3]);
 }
 
 template <int CHP, bool SCREEN, bool ABS>
-__global__ void __launch_bounds__(256) aaa_record_backward_kernel(HierParams p) {
+__global__ void __launch_bounds__(256, 3) aaa_record_backward_kernel(HierParams p) {
   const int tile = blockIdx.x;
   if (p.tile_overflow[tile]) return;
-  const int first = p.ranges[2 * tile], range_size = p.ranges[2 * tile + 1] - first;
-  if (range_size <= 0) return;
   const int local = threadIdx.x;
   const int gx = (p.width + 15) / 16;
   const int tail = local >> 4, hl = local & 15, mg = hl >> 2, mr = local & 3;
@@ -802,40 +853,55 @@ __global__ void __launch_bounds__(256) aaa_record_backward_kernel(HierParams p) 
       bg_grad += p.bg[c] * gradient[c];
     }
   }
-  const bool rows_hold_colors = CHP == 4 && C == 4;
+  const bool colors4 = CHP == 4 && C == 4;
   const long long base = static_cast<long long>(tile) * p.record_capacity;
+  auto record = [&](int j) { return ((base + j) << 8) + local; };
+  auto valid = [&](int id) { return id >= 0 && id < p.n; };  // guard: recorded ids lie in [0, n)
+  // software pipeline: sample j + 1's record and Gaussian data are requested
+  // while sample j is computed
+  int id = p.record_ids[record(0)];
+  float gaussian = p.record_gauss[record(0)];
+  SampleData data = valid(id) ? load_sample(p, id) : SampleData{};
   float T = 1.0f;
   for (int j = 0; j < count; ++j) {
-    const long long at = ((base + j) << 8) + local;
-    const int pos = p.record_ids[at];
-    const float gaussian = p.record_gauss[at];
-    const int id = pos >= 0 && pos < range_size ? p.points[first + pos] : -1;
-    if (id < 0 || id >= p.n) continue;  // guard: recorded positions lie in the slice
-    const float alpha = wp_min(0.99f, p.opacity[id] * gaussian);
-    const float next_t = T * (1.0f - alpha);
-    const float* rgb = p.colors + static_cast<long long>(id) * C;
-    float alpha_gradient = 0.0f;
-    const float weight = alpha * T;
-    float terms[kAccStride];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) terms[kAccColor + c] = 0.0f;
-#pragma unroll
-    for (int c = 0; c < CHP; ++c) {
-      if (c < C) {
-        const float v = rgb[c];
-        color[c] = color[c] + v * alpha * T;
-        const float behind = (final_color[c] - color[c]) / next_t;
-        alpha_gradient += (v - behind) * gradient[c];
-        if (rows_hold_colors) terms[kAccColor + c] = weight * gradient[c];
-        else red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * gradient[c]);
-      }
+    int next_id = -1;
+    float next_gaussian = 0.0f;
+    SampleData next{};
+    if (j + 1 < count) {
+      next_id = p.record_ids[record(j + 1)];
+      next_gaussian = p.record_gauss[record(j + 1)];
+      if (valid(next_id)) next = load_sample(p, next_id);
     }
-    alpha_gradient *= T;
-    alpha_gradient += (-final_T / (1.0f - alpha)) * bg_grad;
-    sample_gradients<CHP, SCREEN, ABS>(p, id, static_cast<float>(x), static_cast<float>(y),
-                                       gaussian, alpha_gradient, terms);
-    flush_row<CHP, SCREEN, ABS>(p, id, terms);
-    T = next_t;
+    if (valid(id)) {
+      const float alpha = wp_min(0.99f, data.opacity * gaussian);
+      const float next_t = T * (1.0f - alpha);
+      const float rgb4[4] = {data.rgb.x, data.rgb.y, data.rgb.z, data.rgb.w};
+      const float* rgb = p.colors + static_cast<long long>(id) * C;
+      float alpha_gradient = 0.0f;
+      const float weight = alpha * T;
+      float terms[kAccStride];
+#pragma unroll
+      for (int c = 0; c < CHP; ++c) {
+        if (c < C) {
+          const float v = colors4 ? rgb4[c & 3] : rgb[c];
+          color[c] = color[c] + v * alpha * T;
+          const float behind = (final_color[c] - color[c]) / next_t;
+          alpha_gradient += (v - behind) * gradient[c];
+          if (colors4) terms[kAccColor + (c & 3)] = weight * gradient[c];
+          else red_add(p.grad_colors + static_cast<long long>(id) * C + c, weight * gradient[c]);
+        }
+      }
+      alpha_gradient *= T;
+      alpha_gradient += (-final_T / (1.0f - alpha)) * bg_grad;
+      sample_gradients<SCREEN, ABS>(data, static_cast<float>(x), static_cast<float>(y), gaussian,
+                                    alpha_gradient, terms);
+      if (colors4) flush_row<SCREEN, ABS, true>(p, id, terms);
+      else flush_row<SCREEN, ABS, false>(p, id, terms);
+      T = next_t;
+    }
+    id = next_id;
+    gaussian = next_gaussian;
+    data = next;
   }
 }
 
