@@ -197,10 +197,12 @@ def bin_and_sort_many(states: list[AaaState], width: int, height: int,
 
 
 # Blend records kept by the forward for the backward: per pixel up to this
-# many blended samples (8 bytes each; T*256*capacity slots, 3.2 GB at 1080p,
-# of which only the blended samples are written and read); a pixel past it
-# sends its tile to the replay kernel.  The BASELINE config-3 scene (2M
-# Gaussians @1080p) blends 63 samples per pixel on average, at most 146.
+# many blended samples (at most 256; 8 bytes each; T*256*capacity slots,
+# 3.2 GB at 1080p, of which only the blended samples are written and read);
+# a pixel past it sends its tile to the replay kernel.  The 2M-Gaussian
+# 1080p benchmark scene (bench.py --config 3) blends 63 samples per pixel on
+# average, at most 146.  The backward consumes the records (it overwrites
+# them); a second backward of the same forward replays.
 RECORD_CAPACITY = 192
 
 
@@ -224,8 +226,7 @@ def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, wi
         tiles = ((width + 15) // 16) * ((height + 15) // 16)
         slots = tiles * 256 * record_capacity
         records = dict(capacity=record_capacity,
-                       ids=torch.empty(slots, device=dev, dtype=torch.int32),
-                       gauss=torch.empty(slots, device=dev, dtype=torch.float32),
+                       entries=torch.empty((slots, 2), device=dev, dtype=torch.float32),
                        counts=torch.empty(tiles * 256, device=dev, dtype=torch.int32),
                        overflow=torch.empty(tiles, device=dev, dtype=torch.int32))
     rec = records or {}
@@ -236,8 +237,8 @@ def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, wi
                                    pin(state.transforms), pin(state.opacity), pin(features),
                                    pin(background), ptr(bins.get("tile_order")), ptr(image),
                                    ptr(final_t), ptr(contrib), rec.get("capacity", 0),
-                                   ptr(rec.get("ids")), ptr(rec.get("gauss")),
-                                   ptr(rec.get("counts")), ptr(rec.get("overflow")),
+                                   ptr(rec.get("entries")), ptr(rec.get("counts")),
+                                   ptr(rec.get("overflow")),
                                    nv.stream(dev)), "aaa_render")
     return image, final_t, contrib, records
 
@@ -261,6 +262,8 @@ def render_backward(state: AaaState, bins: dict, features: Tensor, background: T
     g_op = storage[(16 + C) * n: (17 + C) * n]
     g_scr = storage[(17 + C) * n: (19 + C) * n].view(n, 2) if screen else None
     g_abs = storage[(19 + C) * n: (21 + C) * n].view(n, 2) if absgrad else None
+    if records is not None and records.get("consumed"):
+        records = None  # a second backward of the same forward replays the queues
     if n:
         pin = Args()
         rec = records or {}
@@ -270,8 +273,10 @@ def render_backward(state: AaaState, bins: dict, features: Tensor, background: T
                 pin(state.transforms), pin(state.opacity), pin(features), pin(background),
                 ptr(bins.get("tile_order")), pin(image), pin(final_t), pin(grad_image), ptr(g_tr),
                 ptr(g_op), ptr(g_col), ptr(g_scr), ptr(g_abs), rec.get("capacity", 0),
-                ptr(rec.get("ids")), ptr(rec.get("gauss")), ptr(rec.get("counts")),
-                ptr(rec.get("overflow")), nv.stream(dev)), "aaa_render_backward")
+                ptr(rec.get("entries")), ptr(rec.get("counts")), ptr(rec.get("overflow")),
+                nv.stream(dev)), "aaa_render_backward")
+        if records is not None:
+            records["consumed"] = True  # the backward overwrote the entries
     return g_tr, g_op, g_col, g_scr, g_abs
 
 

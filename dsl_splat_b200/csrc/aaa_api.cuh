@@ -76,8 +76,17 @@ int bit_length(int v) {
 }
 
 template <int CHP, bool SCREEN, bool ABS>
-int launch_record(const HierParams& p, int tiles, size_t smem, cudaStream_t s) {
+int launch_record(const HierParams& p, int tiles, cudaStream_t s) {
   using namespace splat::aaa;
+  const size_t smem = sizeof(TileShared);
+  static bool configured = false;  // the shared-memory opt-in, once per instantiation
+  if (!configured) {
+    if (cudaFuncSetAttribute(aaa_record_backward_kernel<CHP, SCREEN, ABS>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem)) != cudaSuccess)
+      return check_launch("aaa_record_backward shared memory");
+    configured = true;
+  }
   aaa_record_backward_kernel<CHP, SCREEN, ABS><<<tiles, 256, smem, counted(s)>>>(p);
   return check_launch("aaa_record_backward");
 }
@@ -88,21 +97,20 @@ int launch_hier(const HierParams& p, int tiles, bool backward, bool screen, bool
   using namespace splat::aaa;
   int r = kOk;
   const unsigned blocks = static_cast<unsigned>(tiles) * kHierBlocksPerTile;
-  const bool records = backward && p.record_ids;
-  if (records) {  // the recorded tiles per pixel, then the replay of the overflowed ones
-    const size_t smem = 0;
+  const bool records = backward && p.records;
+  if (records) {  // the recorded tiles from their records, then the replay of the overflowed ones
     if (!screen)
-      r = launch_record<CHP, false, false>(p, tiles, smem, s);
+      r = launch_record<CHP, false, false>(p, tiles, s);
     else if (!absgrad)
-      r = launch_record<CHP, true, false>(p, tiles, smem, s);
+      r = launch_record<CHP, true, false>(p, tiles, s);
     else
-      r = launch_record<CHP, true, true>(p, tiles, smem, s);
+      r = launch_record<CHP, true, true>(p, tiles, s);
     if (r != kOk) return r;
   }
   HierParams q = p;
   if (records) {
     q.only_flagged = p.tile_overflow;
-    q.record_ids = nullptr;
+    q.records = nullptr;
   }
   if (!backward)
     aaa_hier_kernel<CHP, false, false, false><<<blocks, kHierThreads, 0, counted(s)>>>(q);
@@ -319,18 +327,18 @@ size_t splat_aaa_record_bytes(int width, int height, int capacity) {
 int splat_aaa_render(int n, int width, int height, int channels, int cull, const int* ranges,
                      const int* points, const float* transforms, const float* opacity,
                      const float* colors, const float* bg, const int* tile_order, float* image,
-                     float* final_t, int* contributors, int record_capacity, int* record_ids,
-                     float* record_gauss, int* record_counts, int* tile_overflow, void* stream) {
+                     float* final_t, int* contributors, int record_capacity, float* records,
+                     int* record_counts, int* tile_overflow, void* stream) {
   int r = check_hier_inputs(width, height, channels, ranges, points, transforms, opacity, colors, bg);
   if (r != kOk) return r;
   if (!image || !final_t || !contributors) return fail(kInvalidArgument, "null AAA blend output");
-  const bool records = record_ids != nullptr;
-  if (records && (record_capacity <= 0 || !record_gauss || !record_counts || !tile_overflow))
-    return fail(kInvalidArgument, "blend records need a capacity and all four buffers");
+  const bool has_records = records != nullptr;
+  if (has_records && (record_capacity <= 0 || record_capacity > 256 || !record_counts ||
+                      !tile_overflow || !aligned(records, 8)))
+    return fail(kInvalidArgument,
+                "blend records need a capacity in [1, 256], counts, flags and 8-byte entries");
   const long long tiles = static_cast<long long>((width + 15) / 16) * ((height + 15) / 16);
-  if (records && tiles * 256 * static_cast<long long>(record_capacity) >= (1LL << 40))
-    return fail(kTooLarge, "blend record capacity too large");
-  if (records &&
+  if (has_records &&
       cudaMemsetAsync(tile_overflow, 0, sizeof(int) * tiles, as_stream(stream)) != cudaSuccess)
     return check_launch("aaa_render records");
   if (n < 0) return fail(kInvalidArgument, "n < 0");
@@ -350,10 +358,9 @@ int splat_aaa_render(int n, int width, int height, int channels, int cull, const
   p.image = image;
   p.final_t = final_t;
   p.contributors = contributors;
-  if (records) {
+  if (has_records) {
     p.record_capacity = record_capacity;
-    p.record_ids = record_ids;
-    p.record_gauss = record_gauss;
+    p.records = reinterpret_cast<float2*>(records);
     p.record_counts = record_counts;
     p.tile_overflow = tile_overflow;
   }
@@ -367,8 +374,8 @@ int splat_aaa_render_backward(int n, int width, int height, int channels, int cu
                               const float* image, const float* final_t, const float* pixel_grad,
                               float* grad_transforms, float* grad_opacity, float* grad_colors,
                               float* grad_screen, float* grad_screen_abs, int record_capacity,
-                              const int* record_ids, const float* record_gauss,
-                              const int* record_counts, const int* tile_overflow, void* stream) {
+                              float* records, const int* record_counts, const int* tile_overflow,
+                              void* stream) {
   int r = check_hier_inputs(width, height, channels, ranges, points, transforms, opacity, colors, bg);
   if (r != kOk) return r;
   if (!image || !final_t || !pixel_grad || !grad_transforms || !grad_opacity || !grad_colors)
@@ -399,12 +406,13 @@ int splat_aaa_render_backward(int n, int width, int height, int channels, int cu
   p.grad_colors = grad_colors;
   p.grad_screen = grad_screen;
   p.grad_screen_abs = grad_screen_abs;
-  if (record_ids) {
-    if (record_capacity <= 0 || !record_gauss || !record_counts || !tile_overflow)
-      return fail(kInvalidArgument, "blend records need a capacity and all four buffers");
+  if (records) {
+    if (record_capacity <= 0 || record_capacity > 256 || !record_counts || !tile_overflow ||
+        !aligned(records, 8))
+      return fail(kInvalidArgument,
+                  "blend records need a capacity in [1, 256], counts, flags and 8-byte entries");
     p.record_capacity = record_capacity;
-    p.record_ids = const_cast<int*>(record_ids);
-    p.record_gauss = const_cast<float*>(record_gauss);
+    p.records = reinterpret_cast<float2*>(records);
     p.record_counts = const_cast<int*>(record_counts);
     p.tile_overflow = const_cast<int*>(tile_overflow);
   }

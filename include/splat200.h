@@ -477,18 +477,19 @@ int splat_aaa_emit(int n, long long pairs, const int* offsets, const float* cent
 int splat_aaa_render(int n, int width, int height, int channels, int cull, const int* ranges,
                      const int* points, const float* transforms, const float* opacity,
                      const float* colors, const float* bg, const int* tile_order, float* image,
-                     float* final_t, int* contributors, int record_capacity, int* record_ids,
-                     float* record_gauss, int* record_counts, int* tile_overflow, void* stream);
+                     float* final_t, int* contributors, int record_capacity, float* records,
+                     int* record_counts, int* tile_overflow, void* stream);
 
 /* Bytes of the optional blend records of splat_aaa_render for a capacity
- * (record_ids and record_gauss: T*256*capacity each, record_counts: T*256,
- * tile_overflow: T).  With records (record_ids non-NULL) the blend also
- * stores, per pixel, the id and Gaussian value of every sample it blends
- * (in blend order, up to record_capacity; record j of tile-local pixel l
- * of tile t at ((t * capacity + j) * 256 + l)), the per-pixel count (-1
- * past the capacity) and a per-tile overflow flag; the backward then reads
- * them instead of replaying the queues (the reference keeps no history:
- * aaa/backward_render.py:1-5). */
+ * (records: T*256*capacity entries of two floats, 8-byte aligned;
+ * record_counts: T*256; tile_overflow: T).  With records (non-NULL,
+ * capacity 1..256) the blend also stores, per pixel, every sample it blends
+ * in blend order, up to record_capacity: entry j of tile-local pixel l of
+ * tile t, at index ((t * capacity + j) * 256 + l), holds the sample's
+ * position in the tile's slice of points (int bits) and its Gaussian value;
+ * plus the per-pixel count (-1 past the capacity) and a per-tile overflow
+ * flag.  The backward then reads them instead of replaying the queues (the
+ * reference keeps no history: aaa/backward_render.py:1-5). */
 size_t splat_aaa_record_bytes(int width, int height, int capacity);
 
 /* aaa/backward_render.py:140-248 backward_render: replay of the forward's
@@ -496,17 +497,19 @@ size_t splat_aaa_record_bytes(int width, int height, int capacity);
  * transposed layout, 16-byte aligned), grad_opacity (n), grad_colors (n,C),
  * grad_screen (n,2) and grad_screen_abs (n,2) (NULL to skip; abs requires
  * screen).  image/final_t: the forward's outputs; pixel_grad (C,H,W).
- * With the forward's blend records (record_ids non-NULL, the same capacity)
+ * With the forward's blend records (records non-NULL, the same capacity)
  * each recorded pixel's samples are taken from them with the replay's
- * arithmetic, and only the tiles flagged in tile_overflow are replayed. */
+ * arithmetic and summed per Gaussian and tile, and only the tiles flagged in
+ * tile_overflow are replayed.  The records are consumed: the backward
+ * overwrites their entries, so a second backward must replay (records NULL). */
 int splat_aaa_render_backward(int n, int width, int height, int channels, int cull,
                               const int* ranges, const int* points, const float* transforms, const float* opacity,
                               const float* colors, const float* bg, const int* tile_order,
                               const float* image, const float* final_t, const float* pixel_grad,
                               float* grad_transforms, float* grad_opacity, float* grad_colors,
                               float* grad_screen, float* grad_screen_abs, int record_capacity,
-                              const int* record_ids, const float* record_gauss,
-                              const int* record_counts, const int* tile_overflow, void* stream);
+                              float* records, const int* record_counts, const int* tile_overflow,
+                              void* stream);
 
 /* aaa/backward_preprocess.py:270-346 -> preprocess_adjoint (:130-268):
  * gradients of the input opacities (n), means (n,3), scales (n,3) and
