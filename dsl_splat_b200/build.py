@@ -1,15 +1,16 @@
 """Builds libsplat200.so in place for sm_100a (nvcc, no JIT cache).
 
-Two translation units, compiled in parallel and linked into one library:
+Three translation units, compiled in parallel and linked into one library:
 
 * splat200.cu (entry points, forward kernels, binning, blending) with
   -fmad=false: every multiply-add stays two IEEE roundings unless the source
   asks for __fmaf_rn, which is what makes radii, tile counts, sort keys and
   the blended image reproducible on the CPU;
-* project_backward.cu (the projection + SH backward) with -fmad=true
-  -prec-div=false -prec-sqrt=false: its outputs are gradients, compared
-  within a relative tolerance, and contraction plus the approximate divide
-  and square root (a few ulp) remove a large part of its arithmetic.
+* project_backward.cu (the projection + SH backward) and aaa_backward.cu
+  (the AAA blend's record backward) with -fmad=true -prec-div=false
+  -prec-sqrt=false: their outputs are gradients, compared within a relative
+  tolerance, and contraction plus the approximate divide and square root (a
+  few ulp) remove a large part of their arithmetic.
 
 splat200.cu keeps IEEE-rounded division and square root (the nvcc defaults
 -prec-div=true -prec-sqrt=true); nothing is built with --use_fast_math.
@@ -28,10 +29,12 @@ LIB = os.path.join(HERE, "libsplat200.so")
 BUILD_DIR = os.path.join(HERE, "_build")
 # source -> its contraction flag
 SOURCES = {"splat200.cu": ["-fmad=false"],
-           "project_backward.cu": ["-fmad=true", "-prec-div=false", "-prec-sqrt=false"]}
+           "project_backward.cu": ["-fmad=true", "-prec-div=false", "-prec-sqrt=false"],
+           "aaa_backward.cu": ["-fmad=true", "-prec-div=false", "-prec-sqrt=false"]}
 HEADERS = ["splat_common.cuh", "cameras.cuh", "project.cuh", "binning.cuh", "render.cuh",
            "footprint.cuh", "tile_modes.cuh", "host_runtime.h", "rade.cuh", "rade_project.cuh",
-           "aaa.cuh", "aaa_render.cuh", "aaa_api.cuh"]
+           "aaa.cuh", "aaa_render.cuh", "aaa_api.cuh", "aaa_blend_params.cuh",
+           "aaa_backward.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -75,22 +75,6 @@ int bit_length(int v) {
   return b;
 }
 
-template <int CHP, bool SCREEN, bool ABS>
-int launch_record(const HierParams& p, int tiles, cudaStream_t s) {
-  using namespace splat::aaa;
-  const size_t smem = sizeof(TileShared);
-  static bool configured = false;  // the shared-memory opt-in, once per instantiation
-  if (!configured) {
-    if (cudaFuncSetAttribute(aaa_record_backward_kernel<CHP, SCREEN, ABS>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return check_launch("aaa_record_backward shared memory");
-    configured = true;
-  }
-  aaa_record_backward_kernel<CHP, SCREEN, ABS><<<tiles, 256, smem, counted(s)>>>(p);
-  return check_launch("aaa_record_backward");
-}
-
 template <int CHP>
 int launch_hier(const HierParams& p, int tiles, bool backward, bool screen, bool absgrad,
                 cudaStream_t s) {
@@ -99,12 +83,7 @@ int launch_hier(const HierParams& p, int tiles, bool backward, bool screen, bool
   const unsigned blocks = static_cast<unsigned>(tiles) * kHierBlocksPerTile;
   const bool records = backward && p.records;
   if (records) {  // the recorded tiles from their records, then the replay of the overflowed ones
-    if (!screen)
-      r = launch_record<CHP, false, false>(p, tiles, s);
-    else if (!absgrad)
-      r = launch_record<CHP, true, false>(p, tiles, s);
-    else
-      r = launch_record<CHP, true, true>(p, tiles, s);
+    r = record_backward_dispatch(p, tiles, screen, absgrad, s);
     if (r != kOk) return r;
   }
   HierParams q = p;
