@@ -30,6 +30,7 @@ SIGNATURES: dict[str, tuple] = {
     "splat_device_error": (_I, [_P, _P]),
     "splat_device_error_read": (_I, [_P, _P]),
     "splat_test_lookback_expiry": (_I, [_P, _U, _P, _P]),
+    "splat_test_trig": (_I, [_I, _P, _P, _P, _P, _P]),
     "splat_cameras_prepare": (_I, [_I, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "splat_cameras_backward": (_I, [_I, _P, _P, _I, _I, _P, _P, _P, _P]),
     "splat_project_forward": (_I, [_I, _P, _P, _P, _P, _P, _P, _P, _I, _I, _F, _F, _F,

@@ -25,21 +25,43 @@ namespace splat {
 namespace aaa {
 
 // ---- atan2 and tan -----------------------------------------------------------
-// Evaluated in double precision from their power series (no library call)
-// and rounded once to float: the float result is the correctly rounded one
-// except in near-halfway cases, and the CPU oracle runs the same steps.
+// Evaluated in double precision (no library call) and rounded once to float:
+// the float result is the correctly rounded one except in near-halfway
+// cases, and the CPU oracle runs the same steps.  The constants are the
+// nearest doubles to their exact values (trig_constants.py prints them).
+// atan(i / 8)
+__constant__ double kAtanTable[9] = {
+    0.0, 0.12435499454676144, 0.24497866312686414, 0.35877067027057225, 0.4636476090008061,
+    0.5585993153435624, 0.6435011087932844, 0.7188299996216245, 0.7853981633974483};
+// 1 / (2k + 1)
+__constant__ double kAtanSeries[8] = {
+    1.0, 0.3333333333333333, 0.2, 0.14285714285714285, 0.1111111111111111, 0.09090909090909091,
+    0.07692307692307693, 0.06666666666666667};
+// 1 / (2j + 1)!
+__constant__ double kSinSeries[11] = {
+    1.0, 0.16666666666666666, 0.008333333333333333, 0.0001984126984126984,
+    2.7557319223985893e-06, 2.505210838544172e-08, 1.6059043836821613e-10,
+    7.647163731819816e-13, 2.8114572543455206e-15, 8.22063524662433e-18, 1.9572941063391263e-20};
+// 1 / (2j)!
+__constant__ double kCosSeries[12] = {
+    1.0, 0.5, 0.041666666666666664, 0.001388888888888889, 2.48015873015873e-05,
+    2.755731922398589e-07, 2.08767569878681e-09, 1.1470745597729725e-11, 4.779477332387385e-14,
+    1.5619206968586225e-16, 4.110317623312165e-19, 8.896791392450574e-22};
+constexpr double kTwoOverPi = 0.6366197723675814;
 
-// atan(t), 0 <= t <= 1: two half-angle steps atan(t) = 2 atan(t / (1 +
-// sqrt(1 + t^2))) bring the argument below tan(pi/16); there the
-// alternating series sum_k (-1)^k u^(2k+1) / (2k+1) (12 terms, Horner in u^2)
-// has converged to double precision.
+// atan(t), 0 <= t <= 1: with c the nearest multiple of 1/8, atan(t) =
+// atan(c) + atan(u), u = (t - c) / (1 + t c), |u| <= 1/16, and atan(u) from
+// its alternating series to u^15 / 15 (Horner in u^2; the next term is below
+// 2^-69 relative).
 SPLAT_DEV double atan_unit(double t) {
-  double u = __ddiv_rn(t, __dadd_rn(1.0, __dsqrt_rn(__dadd_rn(1.0, __dmul_rn(t, t)))));
-  u = __ddiv_rn(u, __dadd_rn(1.0, __dsqrt_rn(__dadd_rn(1.0, __dmul_rn(u, u)))));
+  const int i = static_cast<int>(__dadd_rn(__dmul_rn(t, 8.0), 0.5));
+  const double c = __dmul_rn(static_cast<double>(i), 0.125);
+  const double u = __ddiv_rn(__dsub_rn(t, c), __dadd_rn(1.0, __dmul_rn(t, c)));
   const double u2 = __dmul_rn(u, u);
-  double p = __ddiv_rn(1.0, 23.0);
-  for (int k = 10; k >= 0; --k) p = __dsub_rn(__ddiv_rn(1.0, 2.0 * k + 1.0), __dmul_rn(u2, p));
-  return __dmul_rn(4.0, __dmul_rn(u, p));
+  double p = kAtanSeries[7];
+#pragma unroll
+  for (int k = 6; k >= 0; --k) p = __dsub_rn(kAtanSeries[k], __dmul_rn(u2, p));
+  return __dadd_rn(kAtanTable[i], __dmul_rn(u, p));
 }
 
 SPLAT_DEV float splat_atan2f(float yf, float xf) {
@@ -63,24 +85,34 @@ SPLAT_DEV float splat_atan2f(float yf, float xf) {
 
 // tan(x): reduction by the nearest multiple k of pi/2 (pi/2 in three parts
 // of 33, 33 and 53 significant bits, derived from Machin's formula, so that
-// k * part is exact for |x| < 2^20), sin and cos of the remainder from their
-// Taylor series to r^25 / 25!, tan = sin / cos (-cos / sin for odd k).
+// k * part is exact for |x| < 2^20); sin and cos of the remainder |r| <~
+// pi/4 from their Taylor series (to r^21 / 21! and r^22 / 22!, Horner in
+// r^2), tan = sin / cos (-cos / sin for odd k).
 SPLAT_DEV float splat_tanf(float xf) {
   if (isnan(xf) || isinf(xf)) return xf - xf;
   const double x = xf;
-  const double k = nearbyint(__ddiv_rn(x, 1.5707963267948966));
+  const double k = nearbyint(__dmul_rn(x, kTwoOverPi));
   const double r = __dsub_rn(__dsub_rn(__dsub_rn(x, __dmul_rn(k, 1.5707963267341256)),
                                        __dmul_rn(k, 6.077100506303966e-11)),
                              __dmul_rn(k, 2.0222662487959506e-21));
   const double r2 = __dmul_rn(r, r);
-  double s = 1.0, c = 1.0;
-  for (int j = 12; j >= 1; --j) {
-    s = __dsub_rn(1.0, __dmul_rn(__ddiv_rn(r2, __dmul_rn(2.0 * j, 2.0 * j + 1.0)), s));
-    c = __dsub_rn(1.0, __dmul_rn(__ddiv_rn(r2, __dmul_rn(2.0 * j - 1.0, 2.0 * j)), c));
-  }
-  s = __dmul_rn(s, r);
+  double s = kSinSeries[10], c = kCosSeries[11];
+#pragma unroll
+  for (int j = 9; j >= 0; --j) s = __dsub_rn(kSinSeries[j], __dmul_rn(r2, s));
+#pragma unroll
+  for (int j = 10; j >= 0; --j) c = __dsub_rn(kCosSeries[j], __dmul_rn(r2, c));
+  s = __dmul_rn(r, s);
   const bool odd = fmod(fabs(k), 2.0) == 1.0;
   return static_cast<float>(odd ? __ddiv_rn(-c, s) : __ddiv_rn(s, c));
+}
+
+// test support: splat_atan2f(y, x) and splat_tanf(x) element-wise
+__global__ void trig_probe_kernel(int n, const float* y, const float* x, float* atan2_out,
+                                  float* tan_out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  atan2_out[i] = splat_atan2f(y[i], x[i]);
+  tan_out[i] = splat_tanf(x[i]);
 }
 
 // ---- matrices -------------------------------------------------------------------

@@ -129,6 +129,16 @@ int check_hier_inputs(int width, int height, int channels, const int* ranges, co
 
 extern "C" {
 
+int splat_test_trig(int n, const float* y, const float* x, float* atan2_out, float* tan_out,
+                    void* stream) {
+  if (n < 0) return fail(kInvalidArgument, "n < 0");
+  if (n == 0) return kOk;
+  if (!y || !x || !atan2_out || !tan_out) return fail(kInvalidArgument, "null trig buffer");
+  splat::aaa::trig_probe_kernel<<<blocks_for(n, 256), 256, 0, counted(as_stream(stream))>>>(
+      n, y, x, atan2_out, tan_out);
+  return check_launch("test_trig");
+}
+
 int splat_aaa_preprocess(const SplatAaaFrame* f, float* centers, float* rects, float* depths,
                          float* transforms, float* opacity, int* radii, int* tiles, float* rgb,
                          unsigned char* valid, unsigned char* clamped, int* queued, int* queue_size,

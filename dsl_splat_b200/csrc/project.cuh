@@ -459,18 +459,55 @@ static __global__ void metadata_kernel(int n, const int* __restrict__ radii,
   conics3[3 * i + 2] = q.z;
 }
 
+// rows [base, base+32) of a (n, row_stride) array from the warp's tile: the
+// first kCols columns from the tile, any further ones as zeros; consecutive
+// lanes store consecutive addresses.
+template <int DEG>
+SPLAT_DEV void warp_store_sh(float* __restrict__ dst, int row_stride, int base, int n,
+                             const float* tile) {
+  constexpr int C = ShTile<DEG>::kCols, S = ShTile<DEG>::kStride;
+  const int lane = threadIdx.x & 31;
+  const int rows = min(32, n - base);
+  __syncwarp();
+  if (row_stride == C && rows == 32) {
+    float* g = dst + static_cast<size_t>(base) * C;
+#pragma unroll 12
+    for (int k = 0; k < C; ++k) {
+      const int e = k * 32 + lane;
+      const int r = e / C;
+      g[e] = tile[r * S + (e - r * C)];
+    }
+  } else {
+    for (int r = 0; r < rows; ++r) {
+      float* row = dst + static_cast<size_t>(base + r) * row_stride;
+      for (int t = lane; t < row_stride; t += 32) row[t] = t < C ? tile[r * S + t] : 0.0f;
+    }
+  }
+}
+
+// The standalone SH kernels stage each warp's 32 coefficient rows through
+// shared memory (warp_load_sh / warp_store_sh): a lane reading its own
+// Gaussian's 48 floats straight from global memory touches 32 cache lines
+// per warp-wide load.  128 threads per block.
+
 // primitives/sh.py:44-79 standalone SH forward (masked when radii != null).
 template <int DEG>
-__global__ void sh_forward_kernel(int n, int sh_k, const float* __restrict__ sh,
-                                  const float* __restrict__ dirs, const int* __restrict__ radii,
-                                  float* __restrict__ colors, uint8_t* __restrict__ active) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(kProjectBlock)
+sh_forward_kernel(int n, int sh_k, const float* __restrict__ sh, const float* __restrict__ dirs,
+                  const int* __restrict__ radii, float* __restrict__ colors,
+                  uint8_t* __restrict__ active) {
+  constexpr int S = ShTile<DEG>::kStride;
+  __shared__ float tiles[kProjectWarps][32 * S];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int base = (blockIdx.x * kProjectWarps + warp) * 32;
+  if (base >= n) return;
+  float* tile = tiles[warp];
+  warp_load_sh<DEG>(sh, 3 * sh_k, base, n, tile);
+  const int i = base + lane;
   if (i >= n) return;
   const bool visible = radii ? radii[i] > 0 : true;
   float3 v = make_float3(0.0f, 0.0f, 0.0f);
-  if (visible)
-    v = sh_eval<DEG>(sh + static_cast<size_t>(i) * sh_k * 3, dirs[3 * i], dirs[3 * i + 1],
-                     dirs[3 * i + 2]);
+  if (visible) v = sh_eval<DEG>(tile + lane * S, dirs[3 * i], dirs[3 * i + 1], dirs[3 * i + 2]);
   colors[3 * i + 0] = wmax(v.x, 0.0f);
   colors[3 * i + 1] = wmax(v.y, 0.0f);
   colors[3 * i + 2] = wmax(v.z, 0.0f);
@@ -481,11 +518,53 @@ __global__ void sh_forward_kernel(int n, int sh_k, const float* __restrict__ sh,
   }
 }
 
-// primitives/sh.py:82-138 VJP for one Gaussian: writes the (K,3) coefficient
-// gradient (zeros past (DEG+1)^2) and returns the direction gradient.
+// primitives/sh.py:82-138 VJP for one Gaussian, in place: row holds the
+// first (DEG+1)^2 coefficient triples and receives their gradient; returns
+// the direction gradient.
 template <int DEG>
-SPLAT_DEV float3 sh_vjp(const float* __restrict__ coef, int sh_k, float d0, float d1, float d2,
-                        float3 cg, float* __restrict__ gcoef, bool accumulate) {
+SPLAT_DEV float3 sh_vjp(float* row, float d0, float d1, float d2, float3 cg) {
+  float ux = 0.0f, uy = 0.0f, uz = 0.0f, length = 1.0f;
+  if (DEG > 0) {
+    length = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
+    const float den = wmax(length, W32(1e-12));
+    ux = d0 / den;
+    uy = d1 / den;
+    uz = d2 / den;
+  }
+  float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f;
+#pragma unroll
+  for (int k = 0; k < (DEG + 1) * (DEG + 1); ++k) {
+    const float b = sh_basis(ux, uy, uz, k);
+    float* o = row + 3 * k;
+    if (DEG > 0) {  // the coefficients' weight, read before the row is overwritten
+      const float w = o[0] * cg.x + o[1] * cg.y + o[2] * cg.z;
+      const float3 bg = sh_basis_grad(ux, uy, uz, k);
+      g0 += w * bg.x;
+      g1 += w * bg.y;
+      g2 += w * bg.z;
+    }
+    o[0] = b * cg.x;
+    o[1] = b * cg.y;
+    o[2] = b * cg.z;
+  }
+  if (DEG == 0) return make_float3(0.0f, 0.0f, 0.0f);
+  const float den = wmax(length, W32(1e-12));
+  float3 dg = make_float3(g0 / den, g1 / den, g2 / den);
+  if (length >= W32(1e-12)) {
+    const float dot = (ux * g0 + uy * g1 + uz * g2) / length;
+    dg.x -= ux * dot;
+    dg.y -= uy * dot;
+    dg.z -= uz * dot;
+  }
+  return dg;
+}
+
+// primitives/sh.py:82-138 VJP for one Gaussian from global rows: writes (or
+// adds into) the (K,3) coefficient gradient (zeros past (DEG+1)^2 when
+// writing) and returns the direction gradient.
+template <int DEG>
+SPLAT_DEV float3 sh_vjp_global(const float* __restrict__ coef, int sh_k, float d0, float d1,
+                               float d2, float3 cg, float* __restrict__ gcoef, bool accumulate) {
   float ux = 0.0f, uy = 0.0f, uz = 0.0f, length = 1.0f;
   if (DEG > 0) {
     length = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
@@ -535,30 +614,38 @@ SPLAT_DEV float3 sh_vjp(const float* __restrict__ coef, int sh_k, float d0, floa
 }
 
 template <int DEG>
-__global__ void sh_backward_kernel(int n, int sh_k, const float* __restrict__ sh,
-                                   const float* __restrict__ dirs, const int* __restrict__ radii,
-                                   const uint8_t* __restrict__ active,
-                                   const float* __restrict__ upstream,
-                                   float* __restrict__ grad_sh, float* __restrict__ grad_dirs) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const bool visible = radii ? radii[i] > 0 : true;
-  float* gcoef = grad_sh + static_cast<size_t>(i) * sh_k * 3;
-  float3 dg = make_float3(0.0f, 0.0f, 0.0f);
-  if (visible) {
-    const float3 cg = make_float3(active[3 * i] ? upstream[3 * i] : 0.0f,
-                                  active[3 * i + 1] ? upstream[3 * i + 1] : 0.0f,
-                                  active[3 * i + 2] ? upstream[3 * i + 2] : 0.0f);
-    dg = sh_vjp<DEG>(sh + static_cast<size_t>(i) * sh_k * 3, sh_k, dirs[3 * i], dirs[3 * i + 1],
-                     dirs[3 * i + 2], cg, gcoef, false);
-  } else {
-    for (int k = 0; k < 3 * sh_k; ++k) gcoef[k] = 0.0f;
+__global__ void __launch_bounds__(kProjectBlock)
+sh_backward_kernel(int n, int sh_k, const float* __restrict__ sh, const float* __restrict__ dirs,
+                   const int* __restrict__ radii, const uint8_t* __restrict__ active,
+                   const float* __restrict__ upstream, float* __restrict__ grad_sh,
+                   float* __restrict__ grad_dirs) {
+  constexpr int C = ShTile<DEG>::kCols, S = ShTile<DEG>::kStride;
+  __shared__ float tiles[kProjectWarps][32 * S];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int base = (blockIdx.x * kProjectWarps + warp) * 32;
+  if (base >= n) return;
+  float* tile = tiles[warp];
+  warp_load_sh<DEG>(sh, 3 * sh_k, base, n, tile);
+  const int i = base + lane;
+  if (i < n) {
+    const bool visible = radii ? radii[i] > 0 : true;
+    float* row = tile + lane * S;
+    float3 dg = make_float3(0.0f, 0.0f, 0.0f);
+    if (visible) {
+      const float3 cg = make_float3(active[3 * i] ? upstream[3 * i] : 0.0f,
+                                    active[3 * i + 1] ? upstream[3 * i + 1] : 0.0f,
+                                    active[3 * i + 2] ? upstream[3 * i + 2] : 0.0f);
+      dg = sh_vjp<DEG>(row, dirs[3 * i], dirs[3 * i + 1], dirs[3 * i + 2], cg);
+    } else {
+      for (int k = 0; k < C; ++k) row[k] = 0.0f;
+    }
+    if (grad_dirs) {
+      grad_dirs[3 * i + 0] = dg.x;
+      grad_dirs[3 * i + 1] = dg.y;
+      grad_dirs[3 * i + 2] = dg.z;
+    }
   }
-  if (grad_dirs) {
-    grad_dirs[3 * i + 0] = dg.x;
-    grad_dirs[3 * i + 1] = dg.y;
-    grad_dirs[3 * i + 2] = dg.z;
-  }
+  warp_store_sh<DEG>(grad_sh, 3 * sh_k, base, n, tile);
 }
 
 struct ProjectBackwardParams {

@@ -599,8 +599,9 @@ SPLAT_DEV void rade_project_vjp(const RadeProjectParams& p, int i, float (&gv)[1
           p.seed_colors && p.active[3 * i] ? p.seed_colors[3 * i] : 0.0f,
           p.seed_colors && p.active[3 * i + 1] ? p.seed_colors[3 * i + 1] : 0.0f,
           p.seed_colors && p.active[3 * i + 2] ? p.seed_colors[3 * i + 2] : 0.0f);
-      const float3 dg = sh_vjp<DEG>(p.sh + static_cast<size_t>(i) * p.sh_k * 3, p.sh_k, d0, d1,
-                                    d2, cg, p.grad_sh + static_cast<size_t>(i) * p.sh_k * 3, false);
+      const float3 dg = sh_vjp_global<DEG>(p.sh + static_cast<size_t>(i) * p.sh_k * 3, p.sh_k, d0,
+                                           d1, d2, cg,
+                                           p.grad_sh + static_cast<size_t>(i) * p.sh_k * 3, false);
       g_mean[0] += dg.x;
       g_mean[1] += dg.y;
       g_mean[2] += dg.z;

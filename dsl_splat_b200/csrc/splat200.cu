@@ -714,12 +714,12 @@ int splat_sh_forward(int n, int degree, int sh_k, const float* sh, const float* 
     return fail(kInvalidArgument, "bad SH arguments");
   if (n == 0) return kOk;
   cudaStream_t s = as_stream(stream);
-  const unsigned g = blocks_for(n, 256);
+  const unsigned g = blocks_for(n, kProjectBlock);
   switch (degree) {
-    case 0: sh_forward_kernel<0><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
-    case 1: sh_forward_kernel<1><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
-    case 2: sh_forward_kernel<2><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
-    default: sh_forward_kernel<3><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
+    case 0: sh_forward_kernel<0><<<g, kProjectBlock, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
+    case 1: sh_forward_kernel<1><<<g, kProjectBlock, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
+    case 2: sh_forward_kernel<2><<<g, kProjectBlock, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
+    default: sh_forward_kernel<3><<<g, kProjectBlock, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, colors, active); break;
   }
   return check_launch("sh_forward");
 }
@@ -731,12 +731,12 @@ int splat_sh_backward(int n, int degree, int sh_k, const float* sh, const float*
     return fail(kInvalidArgument, "bad SH arguments");
   if (n == 0) return kOk;
   cudaStream_t s = as_stream(stream);
-  const unsigned g = blocks_for(n, 256);
+  const unsigned g = blocks_for(n, kProjectBlock);
   switch (degree) {
-    case 0: sh_backward_kernel<0><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
-    case 1: sh_backward_kernel<1><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
-    case 2: sh_backward_kernel<2><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
-    default: sh_backward_kernel<3><<<g, 256, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
+    case 0: sh_backward_kernel<0><<<g, kProjectBlock, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
+    case 1: sh_backward_kernel<1><<<g, kProjectBlock, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
+    case 2: sh_backward_kernel<2><<<g, kProjectBlock, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
+    default: sh_backward_kernel<3><<<g, kProjectBlock, 0, counted(s)>>>(n, sh_k, sh, dirs, radii, active, upstream, grad_sh, grad_dirs); break;
   }
   return check_launch("sh_backward");
 }

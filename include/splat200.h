@@ -46,6 +46,13 @@ int splat_device_error_read(int* device_dst, void* stream);
  * wait expires, the device error word receives -3 and the kernel returns,
  * writing the partial prefix to *out.  Shows on a GPU that an expired wait
  * ends and is reported. */
+/* No counterpart in the reference (its native snippets call the C
+ * library's atan2f and tanf); test support.  atan2_out[i] =
+ * splat_atan2f(y[i], x[i]) and tan_out[i] = splat_tanf(x[i]), the AAA
+ * preprocessing's own functions, for comparison with the CPU oracle's. */
+int splat_test_trig(int n, const float* y, const float* x, float* atan2_out, float* tan_out,
+                    void* stream);
+
 int splat_test_lookback_expiry(const unsigned* status, unsigned spin_limit, unsigned* out,
                                void* stream);
 

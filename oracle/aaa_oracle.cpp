@@ -33,17 +33,39 @@ extern "C" float oracle_logf(float);
 // the correctly rounded one except in (rare) near-halfway cases -- it then
 // agrees with any correctly rounded libm as well.
 
-// atan(t) for 0 <= t <= 1: two half-angle steps atan(t) = 2 atan(t / (1 +
-// sqrt(1 + t^2))) bring the argument below tan(pi/16) ~ 0.199, where the
-// alternating Taylor series sum_k (-1)^k u^(2k+1) / (2k+1) has converged to
-// double precision after 12 terms (Horner in u^2).
+// The constants of atan2 and tan, the nearest doubles to their exact values
+// (dsl_splat_b200/csrc/trig_constants.py prints them).
+// atan(i / 8)
+static const double kAtanTable[9] = {
+    0.0, 0.12435499454676144, 0.24497866312686414, 0.35877067027057225, 0.4636476090008061,
+    0.5585993153435624, 0.6435011087932844, 0.7188299996216245, 0.7853981633974483};
+// 1 / (2k + 1)
+static const double kAtanSeries[8] = {
+    1.0, 0.3333333333333333, 0.2, 0.14285714285714285, 0.1111111111111111, 0.09090909090909091,
+    0.07692307692307693, 0.06666666666666667};
+// 1 / (2j + 1)!
+static const double kSinSeries[11] = {
+    1.0, 0.16666666666666666, 0.008333333333333333, 0.0001984126984126984,
+    2.7557319223985893e-06, 2.505210838544172e-08, 1.6059043836821613e-10,
+    7.647163731819816e-13, 2.8114572543455206e-15, 8.22063524662433e-18, 1.9572941063391263e-20};
+// 1 / (2j)!
+static const double kCosSeries[12] = {
+    1.0, 0.5, 0.041666666666666664, 0.001388888888888889, 2.48015873015873e-05,
+    2.755731922398589e-07, 2.08767569878681e-09, 1.1470745597729725e-11, 4.779477332387385e-14,
+    1.5619206968586225e-16, 4.110317623312165e-19, 8.896791392450574e-22};
+static const double kTwoOverPi = 0.6366197723675814;
+
+// atan(t) for 0 <= t <= 1: with c the nearest multiple of 1/8, atan(t) =
+// atan(c) + atan(u), u = (t - c) / (1 + t c), |u| <= 1/16, and atan(u) from
+// its alternating series to u^15 / 15 (Horner in u^2).
 static double atan_unit(double t) {
-  double u = t / (1.0 + std::sqrt(1.0 + t * t));
-  u = u / (1.0 + std::sqrt(1.0 + u * u));
+  const int i = static_cast<int>(t * 8.0 + 0.5);
+  const double c = i * 0.125;
+  const double u = (t - c) / (1.0 + t * c);
   const double u2 = u * u;
-  double p = 1.0 / 23.0;
-  for (int k = 10; k >= 0; --k) p = 1.0 / (2 * k + 1) - u2 * p;
-  return 4.0 * (u * p);
+  double p = kAtanSeries[7];
+  for (int k = 6; k >= 0; --k) p = kAtanSeries[k] - u2 * p;
+  return kAtanTable[i] + u * p;
 }
 
 extern "C" float oracle_atan2f(float yf, float xf) {
@@ -67,21 +89,19 @@ extern "C" float oracle_atan2f(float yf, float xf) {
 
 // tan(x): x reduced by the nearest multiple k of pi/2 (pi/2 split into three
 // parts of 33, 33 and 53 significant bits, so k * part is exact for the
-// arguments that occur, |x| < 2^20); sin and cos of the remainder |r| <=
-// pi/4 from their Taylor series (to r^25 / 25!), tan = sin / cos, or
-// -cos / sin for odd k.
+// arguments that occur, |x| < 2^20); sin and cos of the remainder |r| <~
+// pi/4 from their Taylor series (to r^21 / 21! and r^22 / 22!, Horner in
+// r^2), tan = sin / cos, or -cos / sin for odd k.
 extern "C" float oracle_tanf(float xf) {
   if (std::isnan(xf) || std::isinf(xf)) return xf - xf;
   const double x = xf;
-  const double k = std::nearbyint(x / 1.5707963267948966);
+  const double k = std::nearbyint(x * kTwoOverPi);
   const double r = ((x - k * 1.5707963267341256) - k * 6.077100506303966e-11) -
                    k * 2.0222662487959506e-21;
   const double r2 = r * r;
-  double s = 1.0, c = 1.0;
-  for (int j = 12; j >= 1; --j) {
-    s = 1.0 - r2 / ((2.0 * j) * (2.0 * j + 1.0)) * s;
-    c = 1.0 - r2 / ((2.0 * j - 1.0) * (2.0 * j)) * c;
-  }
+  double s = kSinSeries[10], c = kCosSeries[11];
+  for (int j = 9; j >= 0; --j) s = kSinSeries[j] - r2 * s;
+  for (int j = 10; j >= 0; --j) c = kCosSeries[j] - r2 * c;
   s *= r;
   const bool odd = std::fmod(std::fabs(k), 2.0) == 1.0;
   return static_cast<float>(odd ? -c / s : s / c);

@@ -50,6 +50,10 @@ def lib():
         L.oracle_expf.restype = _flt
         L.oracle_logf.argtypes = [_flt]
         L.oracle_logf.restype = _flt
+        L.oracle_atan2f.argtypes = [_flt, _flt]
+        L.oracle_atan2f.restype = _flt
+        L.oracle_tanf.argtypes = [_flt]
+        L.oracle_tanf.restype = _flt
         L.oracle_cameras_prepare.argtypes = [_int, _f32p, _f32p, _int, _int, _int, _vp, _vp, _vp, _i32p]
         L.oracle_cameras_prepare.restype = _int
         L.oracle_cameras_backward.argtypes = [_int, _f32p, _vp, _int, _int, _vp, _vp, _f32p]
@@ -141,6 +145,20 @@ def num_threads() -> int:
 
 def expf(x: np.ndarray) -> np.ndarray:
     f = lib().oracle_expf
+    x = _c(x).ravel()
+    return np.array([f(float(v)) for v in x], dtype=np.float32)
+
+
+def atan2f(y: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """aaa_oracle.cpp oracle_atan2f element-wise (the AAA bounds' atan2)."""
+    f = lib().oracle_atan2f
+    y, x = _c(y).ravel(), _c(x).ravel()
+    return np.array([f(float(a), float(b)) for a, b in zip(y, x)], dtype=np.float32)
+
+
+def tanf(x: np.ndarray) -> np.ndarray:
+    """aaa_oracle.cpp oracle_tanf element-wise (the AAA bounds' tan)."""
+    f = lib().oracle_tanf
     x = _c(x).ravel()
     return np.array([f(float(v)) for v in x], dtype=np.float32)
 
