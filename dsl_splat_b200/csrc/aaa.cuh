@@ -401,6 +401,72 @@ SPLAT_DEV M4 load_m4(const float* t, long long i) {
   return g;
 }
 
+// ---- the first 32 tiles of each rectangle, flattened over the warp ----------------
+// Each lane brings up to 32 tiles of its Gaussian's rectangle (row-major from
+// (bx, by), rw tiles wide) and the warp walks the concatenation of all lanes'
+// tiles 32 at a time, so the walk takes ceil(sum / 32) steps instead of the
+// largest lane's count (4x fewer at 1080p: most rectangles are small, a few
+// reach 32).  Every lane calls visit(owner, pass, rank, x, y, depth) once per
+// step (it may shuffle): owner is the lane whose tile this lane tested, pass
+// whether the tile is within the owner's threshold, rank the number of the
+// owner's passing tiles before this one.  Returns the lane's own passing
+// tiles.  All 32 lanes must call it.
+template <bool SEQUENTIAL, typename Visit>
+SPLAT_DEV int warp_first_tiles(int tiles, int bx, int by, int rw, const M4& g, float threshold,
+                               Visit&& visit) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  int inclusive = tiles;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int v = __shfl_up_sync(full, inclusive, d);
+    if (lane >= d) inclusive += v;
+  }
+  const int start = inclusive - tiles;
+  const int total = __shfl_sync(full, inclusive, 31);
+  int own_hits = 0;
+  for (int base = 0; base < total; base += 32) {
+    const int f = base + lane;
+    int owner = 0;  // the last lane whose tiles start at or before f (it has tiles)
+#pragma unroll
+    for (int step = 16; step >= 1; step >>= 1) {
+      const int candidate = owner + step;
+      if (__shfl_sync(full, start, candidate) <= f) owner = candidate;
+    }
+    const int owner_start = __shfl_sync(full, start, owner);
+    const int obx = __shfl_sync(full, bx, owner), oby = __shfl_sync(full, by, owner);
+    const int orw = __shfl_sync(full, rw, owner);
+    const float limit = __shfl_sync(full, threshold, owner);
+    M4 og;
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) og.m[r][c] = __shfl_sync(full, g.m[r][c], owner);
+    bool pass = false;
+    int x = 0, y = 0;
+    float depth = 0.0f;
+    if (f < total) {
+      const int t = f - owner_start;
+      x = obx + t % orw;
+      y = oby + t / orw;
+      const FrustumDepth fd = frustum_depth(og, static_cast<float>(x * 16),
+                                            static_cast<float>(y * 16), 15.0f, 15.0f, SEQUENTIAL);
+      pass = fd.half_distance <= limit;
+      depth = fd.depth;
+    }
+    const unsigned hits = __ballot_sync(full, pass);
+    const int first_lane = owner_start > base ? owner_start - base : 0;  // owner's first item here
+    const unsigned earlier = hits & lanemask_lt() & ~((1u << first_lane) - 1u);
+    const int rank = __shfl_sync(full, own_hits, owner) + __popc(earlier);
+    visit(owner, pass, rank, x, y, depth);
+    const int lo = min(max(start - base, 0), 32), hi = min(max(start + tiles - base, 0), 32);
+    const unsigned upto_hi = hi >= 32 ? full : (1u << hi) - 1u;
+    const unsigned upto_lo = lo >= 32 ? full : (1u << lo) - 1u;
+    own_hits += __popc(hits & upto_hi & ~upto_lo);
+  }
+  return own_hits;
+}
+
 // ---- K19: preprocessing ------------------------------------------------------------
 
 struct PreprocessParams {
@@ -435,145 +501,157 @@ struct PreprocessParams {
 
 __global__ void __launch_bounds__(128) aaa_preprocess_kernel(PreprocessParams p) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= p.n) return;
-  p.radii[i] = 0;
-  p.tiles[i] = 0;
-  p.valid[i] = 0;
-  const M4 V = load_transposed(p.view), P = load_transposed(p.proj);
-  const float fx = static_cast<float>(p.width) / (2.0f * p.tanx);
-  const float fy = static_cast<float>(p.height) / (2.0f * p.tany);
-  const float W = static_cast<float>(p.width), H = static_cast<float>(p.height);
-  M4 viewport = {};
-  viewport.m[0][0] = W / 2.0f;
-  viewport.m[0][3] = W / 2.0f - 0.5f;
-  viewport.m[1][1] = H / 2.0f;
-  viewport.m[1][3] = H / 2.0f - 0.5f;
-  viewport.m[2][2] = 1.0f;
-  viewport.m[3][3] = 1.0f;
-  const M4 clip = glm_matmul(viewport, P);
-  const int gx = (p.width + 15) / 16, gy = (p.height + 15) / 16;
-  const float pm[3] = {p.means[3 * i], p.means[3 * i + 1], p.means[3 * i + 2]};
-  // primitives/math.py:89-94 glm_view_position; the load-balanced
-  // specialisation rounds the z product before the sum
-  float t[3];
-#pragma unroll
-  for (int r = 0; r < 3; ++r) {
-    const float xy = __fmaf_rn(V.m[r][0], pm[0], V.m[r][1] * pm[1]);
-    const float total = (!p.complete && r == 2) ? xy + V.m[r][2] * pm[2]
-                                                : __fmaf_rn(V.m[r][2], pm[2], xy);
-    t[r] = total + V.m[r][3];
+  if (i < p.n) {
+    p.radii[i] = 0;
+    p.tiles[i] = 0;
+    p.valid[i] = 0;
   }
-  if (p.near_clipping && t[2] < 0.2f) return;
-  float R[3][3];
-  {
-    const float4 q = reinterpret_cast<const float4*>(p.quats)[i];
-    glm_rotation(q.x, q.y, q.z, q.w, R);
-  }
-  const float* cam = p.campos;
-  const float rel[3] = {pm[0] - cam[0], pm[1] - cam[1], pm[2] - cam[2]};
-  const float inv_len = 1.0f / sqrtf((rel[0] * rel[0] + rel[1] * rel[1]) + rel[2] * rel[2]);
-  const float dir[3] = {rel[0] * inv_len, rel[1] * inv_len, rel[2] * inv_len};
-  float ray[3];
-  mat3_vec(R, dir, ray);
-  const float s[3] = {p.scales[3 * i], p.scales[3 * i + 1], p.scales[3 * i + 2]};
-  const float var[3] = {s[0] * s[0], s[1] * s[1], s[2] * s[2]};
-  // primitives/math.py:71-86 glm_filter_view_depth
-  const float depth = __fmaf_rn(V.m[2][0], pm[0], V.m[2][1] * pm[1]) + (V.m[2][2] * pm[2] + V.m[2][3]);
-  const float focal = fmaxf(fx, fy);
-  float filter_variance = (depth / focal) * (depth / focal) * 0.3f;
-  if (p.filters) filter_variance = fmaxf(p.filters[i] * p.filters[i], filter_variance);
-  float dilated[3];
+  // the per-Gaussian part up to the rectangle; false: rejected (lanes stay
+  // for the warp's tile walk)
+  float pm[3], t[3], cam[3], opacity = 0.0f, threshold = 0.0f, center[2], extent[2];
+  M4 g2s = {};
+  int4 b = make_int4(0, 0, 0, 0);
+  int count = 0, radius = 0;
+  auto front = [&]() -> bool {
+    const M4 V = load_transposed(p.view), P = load_transposed(p.proj);
+    const float fx = static_cast<float>(p.width) / (2.0f * p.tanx);
+    const float fy = static_cast<float>(p.height) / (2.0f * p.tany);
+    const float W = static_cast<float>(p.width), H = static_cast<float>(p.height);
+    M4 viewport = {};
+    viewport.m[0][0] = W / 2.0f;
+    viewport.m[0][3] = W / 2.0f - 0.5f;
+    viewport.m[1][1] = H / 2.0f;
+    viewport.m[1][3] = H / 2.0f - 0.5f;
+    viewport.m[2][2] = 1.0f;
+    viewport.m[3][3] = 1.0f;
+    const M4 clip = glm_matmul(viewport, P);
+    const int gx = (p.width + 15) / 16, gy = (p.height + 15) / 16;
+    pm[0] = p.means[3 * i];
+    pm[1] = p.means[3 * i + 1];
+    pm[2] = p.means[3 * i + 2];
+    // primitives/math.py:89-94 glm_view_position; the load-balanced
+    // specialisation rounds the z product before the sum
 #pragma unroll
-  for (int k = 0; k < 3; ++k) dilated[k] = sqrtf(s[k] * s[k] + filter_variance);
-  const float ray2[3] = {ray[0] * ray[0], ray[1] * ray[1], ray[2] * ray[2]};
-  const float before_terms[3] = {var[1] * var[2], var[0] * var[2], var[0] * var[1]};
-  const float area_before = dot3p(ray2, before_terms);
-  const float sd[3] = {dilated[0] * dilated[0], dilated[1] * dilated[1], dilated[2] * dilated[2]};
-  const float after_terms[3] = {sd[1] * sd[2], sd[0] * sd[2], sd[0] * sd[1]};
-  const float area_after = dot3p(ray2, after_terms);
-  float opacity = p.opacities[i];
-  if (p.ewa) opacity *= sqrtf(area_before / area_after);
-  const float min_alpha = 1.0f / 255.0f;
-  if (opacity < min_alpha) return;
-  const float threshold = splat_logf(opacity / min_alpha);
-  const float cutoff = fminf(11.11f, 2.0f * threshold);
-  const float root_mod = sqrtf(p.modifier);
-  const float scale[3] = {dilated[0] * root_mod, dilated[1] * root_mod, dilated[2] * root_mod};
-  const float invscale[3] = {(1.0f / dilated[0]) / root_mod, (1.0f / dilated[1]) / root_mod,
-                             (1.0f / dilated[2]) / root_mod};
-  // camera inside the cutoff ellipsoid: rejected
-  {
-    const float D[3][3] = {{invscale[0], 0.0f, 0.0f}, {0.0f, invscale[1], 0.0f}, {0.0f, 0.0f, invscale[2]}};
-    float world2gauss[3][3];
-    mat3_mul(D, R, world2gauss);
-    const float to_camera[3] = {cam[0] - pm[0], cam[1] - pm[1], cam[2] - pm[2]};
-    float cam_gauss[3];
-    mat3_vec(world2gauss, to_camera, cam_gauss);
-    if (dot3p(cam_gauss, cam_gauss) < cutoff) return;
-  }
-  const float S[3][3] = {{scale[0], 0.0f, 0.0f}, {0.0f, scale[1], 0.0f}, {0.0f, 0.0f, scale[2]}};
-  float SR[3][3];
-  mat3_mul(S, R, SR);
-  M4 world = {};
-#pragma unroll
-  for (int r = 0; r < 3; ++r) {
-#pragma unroll
-    for (int c = 0; c < 3; ++c) world.m[r][c] = SR[c][r];
-    world.m[r][3] = pm[r];
-  }
-  world.m[3][3] = 1.0f;
-  const M4 g2s = glm_matmul(clip, world);
-  if (frustum_depth(g2s, 0.0f, 0.0f, W - 1.0f, H - 1.0f, false).half_distance > threshold) return;
-  float center[2], extent[2];
-  if (p.new_aabb) {
-    M4 g2v = glm_matmul(V, world);
-#pragma unroll
-    for (int r = 0; r < 3; ++r) g2v.m[r][3] = t[r];
-    float bx[2], by[2];
-    bound_axis(g2v, t, cutoff, 0, bx);
-    bound_axis(g2v, t, cutoff, 1, by);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      bx[k] = p.principal_x + fx * bx[k];
-      by[k] = p.principal_y + fy * by[k];
+    for (int r = 0; r < 3; ++r) {
+      const float xy = __fmaf_rn(V.m[r][0], pm[0], V.m[r][1] * pm[1]);
+      const float total = (!p.complete && r == 2) ? xy + V.m[r][2] * pm[2]
+                                                  : __fmaf_rn(V.m[r][2], pm[2], xy);
+      t[r] = total + V.m[r][3];
     }
-    center[0] = (bx[1] + bx[0]) / 2.0f;
-    center[1] = (by[1] + by[0]) / 2.0f;
-    extent[0] = (bx[1] - bx[0]) / 2.0f;
-    extent[1] = (by[1] - by[0]) / 2.0f;
-  } else if (!screen_bounds(g2s, cutoff, center, extent)) {
-    return;
-  }
-  const int4 b = bounds_rect(center[0], center[1], extent[0], extent[1], gx, gy);
-  int count = (b.z - b.x) * (b.w - b.y);
-  if (count == 0) return;
-  if (p.complete && p.tile_culling) {
-    count = 0;
-    for (int y = b.y; y < b.w; ++y)
-      for (int x = b.x; x < b.z; ++x)
-        if (frustum_depth(g2s, static_cast<float>(x * 16), static_cast<float>(y * 16), 15.0f, 15.0f,
-                          true).half_distance <= threshold)
-          ++count;
-    if (count == 0) return;
-  }
-  const int radius = f2i(ceilf(fmaxf(extent[0], extent[1])));
-  if (p.complete && radius <= 0) return;
-  if (p.cooperative) {
-    if (radius == 0) return;
-    const int rect_count = count, rect_width = b.z - b.x;
-    count = 0;
-    const int first = rect_count < 32 ? rect_count : 32;
-    for (int k = 0; k < first; ++k) {
-      const int x = b.x + k % rect_width, y = b.y + k / rect_width;
-      if (frustum_depth(g2s, static_cast<float>(x * 16), static_cast<float>(y * 16), 15.0f, 15.0f,
-                        false).half_distance <= threshold)
-        ++count;
+    if (p.near_clipping && t[2] < 0.2f) return false;
+    float R[3][3];
+    {
+      const float4 q = reinterpret_cast<const float4*>(p.quats)[i];
+      glm_rotation(q.x, q.y, q.z, q.w, R);
     }
+    cam[0] = p.campos[0];
+    cam[1] = p.campos[1];
+    cam[2] = p.campos[2];
+    const float rel[3] = {pm[0] - cam[0], pm[1] - cam[1], pm[2] - cam[2]};
+    const float inv_len = 1.0f / sqrtf((rel[0] * rel[0] + rel[1] * rel[1]) + rel[2] * rel[2]);
+    const float dir[3] = {rel[0] * inv_len, rel[1] * inv_len, rel[2] * inv_len};
+    float ray[3];
+    mat3_vec(R, dir, ray);
+    const float s[3] = {p.scales[3 * i], p.scales[3 * i + 1], p.scales[3 * i + 2]};
+    const float var[3] = {s[0] * s[0], s[1] * s[1], s[2] * s[2]};
+    // primitives/math.py:71-86 glm_filter_view_depth
+    const float depth =
+        __fmaf_rn(V.m[2][0], pm[0], V.m[2][1] * pm[1]) + (V.m[2][2] * pm[2] + V.m[2][3]);
+    const float focal = fmaxf(fx, fy);
+    float filter_variance = (depth / focal) * (depth / focal) * 0.3f;
+    if (p.filters) filter_variance = fmaxf(p.filters[i] * p.filters[i], filter_variance);
+    float dilated[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) dilated[k] = sqrtf(s[k] * s[k] + filter_variance);
+    const float ray2[3] = {ray[0] * ray[0], ray[1] * ray[1], ray[2] * ray[2]};
+    const float before_terms[3] = {var[1] * var[2], var[0] * var[2], var[0] * var[1]};
+    const float area_before = dot3p(ray2, before_terms);
+    const float sd[3] = {dilated[0] * dilated[0], dilated[1] * dilated[1], dilated[2] * dilated[2]};
+    const float after_terms[3] = {sd[1] * sd[2], sd[0] * sd[2], sd[0] * sd[1]};
+    const float area_after = dot3p(ray2, after_terms);
+    opacity = p.opacities[i];
+    if (p.ewa) opacity *= sqrtf(area_before / area_after);
+    const float min_alpha = 1.0f / 255.0f;
+    if (opacity < min_alpha) return false;
+    threshold = splat_logf(opacity / min_alpha);
+    const float cutoff = fminf(11.11f, 2.0f * threshold);
+    const float root_mod = sqrtf(p.modifier);
+    const float scale[3] = {dilated[0] * root_mod, dilated[1] * root_mod, dilated[2] * root_mod};
+    const float invscale[3] = {(1.0f / dilated[0]) / root_mod, (1.0f / dilated[1]) / root_mod,
+                               (1.0f / dilated[2]) / root_mod};
+    // camera inside the cutoff ellipsoid: rejected
+    {
+      const float D[3][3] = {
+          {invscale[0], 0.0f, 0.0f}, {0.0f, invscale[1], 0.0f}, {0.0f, 0.0f, invscale[2]}};
+      float world2gauss[3][3];
+      mat3_mul(D, R, world2gauss);
+      const float to_camera[3] = {cam[0] - pm[0], cam[1] - pm[1], cam[2] - pm[2]};
+      float cam_gauss[3];
+      mat3_vec(world2gauss, to_camera, cam_gauss);
+      if (dot3p(cam_gauss, cam_gauss) < cutoff) return false;
+    }
+    const float S[3][3] = {{scale[0], 0.0f, 0.0f}, {0.0f, scale[1], 0.0f}, {0.0f, 0.0f, scale[2]}};
+    float SR[3][3];
+    mat3_mul(S, R, SR);
+    M4 world = {};
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+#pragma unroll
+      for (int c = 0; c < 3; ++c) world.m[r][c] = SR[c][r];
+      world.m[r][3] = pm[r];
+    }
+    world.m[3][3] = 1.0f;
+    g2s = glm_matmul(clip, world);
+    if (frustum_depth(g2s, 0.0f, 0.0f, W - 1.0f, H - 1.0f, false).half_distance > threshold)
+      return false;
+    if (p.new_aabb) {
+      M4 g2v = glm_matmul(V, world);
+#pragma unroll
+      for (int r = 0; r < 3; ++r) g2v.m[r][3] = t[r];
+      float bx[2], by[2];
+      bound_axis(g2v, t, cutoff, 0, bx);
+      bound_axis(g2v, t, cutoff, 1, by);
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        bx[k] = p.principal_x + fx * bx[k];
+        by[k] = p.principal_y + fy * by[k];
+      }
+      center[0] = (bx[1] + bx[0]) / 2.0f;
+      center[1] = (by[1] + by[0]) / 2.0f;
+      extent[0] = (bx[1] - bx[0]) / 2.0f;
+      extent[1] = (by[1] - by[0]) / 2.0f;
+    } else if (!screen_bounds(g2s, cutoff, center, extent)) {
+      return false;
+    }
+    b = bounds_rect(center[0], center[1], extent[0], extent[1], gx, gy);
+    count = (b.z - b.x) * (b.w - b.y);
+    if (count == 0) return false;
+    if (p.complete && p.tile_culling) {
+      count = 0;
+      for (int y = b.y; y < b.w; ++y)
+        for (int x = b.x; x < b.z; ++x)
+          if (frustum_depth(g2s, static_cast<float>(x * 16), static_cast<float>(y * 16), 15.0f,
+                            15.0f, true).half_distance <= threshold)
+            ++count;
+      if (count == 0) return false;
+    }
+    radius = f2i(ceilf(fmaxf(extent[0], extent[1])));
+    if (p.complete && radius <= 0) return false;
+    return true;
+  };
+  const bool alive = i < p.n && front() && (!p.cooperative || radius != 0);
+  if (p.cooperative) {  // the first 32 tiles; longer rectangles queue for the remainder
+    const int rect_count = alive ? count : 0;
+    count = warp_first_tiles<false>(min(rect_count, 32), b.x, b.y, b.z - b.x, g2s, threshold,
+                                    [](int, bool, int, int, int, float) {});
+    if (!alive) return;
     if (rect_count > 32) {
       p.queued[atomicAdd(p.queue_size, 1)] = i;
     } else if (count == 0) {
       return;
     }
+  } else if (!alive) {
+    return;
   }
   reinterpret_cast<float2*>(p.centers)[i] = make_float2(center[0], center[1]);
   reinterpret_cast<float2*>(p.rects)[i] = make_float2(extent[0], extent[1]);
@@ -646,7 +724,8 @@ __global__ void __launch_bounds__(256)
 
 // ---- K22: keys of every visible Gaussian's tiles ------------------------------------
 // Per Gaussian i: its rectangle's tiles in row-major order -- the first 32
-// tested with the sequential plane products, the rest with the fused ones --
+// tested with the sequential plane products (walked by the whole warp:
+// warp_first_tiles), the rest with the fused ones --
 // one pair per tile within the threshold, written from offsets[i-1] on and
 // never at or past offsets[i]; the rest of that range is padding.  A pair is
 // stored as three words: the tile (padding: pad_tile = 2^b - 1, b the bit
@@ -691,20 +770,22 @@ __global__ void __launch_bounds__(128)
     stop = offsets[i];
     threshold = splat_logf(opacity[i] / (1.0f / 255.0f));
     g = load_m4(transforms, i);
-    const int first = count < 32 ? count : 32;
-    for (int t = 0; t < first; ++t) {
-      const int x = b.x + t % rw, y = b.y + t / rw;
-      const FrustumDepth f = frustum_depth(g, static_cast<float>(x * 16), static_cast<float>(y * 16),
-                                           15.0f, 15.0f, true);
-      if (f.half_distance <= threshold) {
-        if (off < stop && off < num_pairs) {
-          tile_out[off] = static_cast<uint32_t>(y * gx + x);
-          depth_out[off] = depth_key(f.depth);
-          id_out[off] = i;
-        }
-        ++off;
-      }
-    }
+  }
+  {  // the first 32 tiles of every rectangle, walked by the whole warp
+    const long long first_off = off;
+    const int hits = warp_first_tiles<true>(
+        active ? min(count, 32) : 0, b.x, b.y, rw, g, threshold,
+        [&](int owner, bool pass, int rank, int x, int y, float depth) {
+          const long long target = __shfl_sync(full, first_off, owner) + rank;
+          const long long end = __shfl_sync(full, stop, owner);
+          const int id = __shfl_sync(full, i, owner);
+          if (pass && target < end && target < num_pairs) {
+            tile_out[target] = static_cast<uint32_t>(y * gx + x);
+            depth_out[target] = depth_key(depth);
+            id_out[target] = id;
+          }
+        });
+    off = first_off + hits;
   }
   // long rectangles: the warp takes them one owner at a time, 32 tiles per
   // step, and ranks each step's hits by ballot (row-major order kept)
