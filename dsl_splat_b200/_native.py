@@ -90,6 +90,7 @@ SIGNATURES: dict[str, tuple] = {
     "splat_aaa_render": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                               _I, _P, _P, _P, _P]),
     "splat_aaa_record_bytes": (_Z, [_I, _I, _I]),
+    "splat_aaa_metadata": (_I, [_I, _P, _F, _F, _F, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
     "splat_aaa_render_backward": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                                        _P, _P, _P, _P, _P, _P, _I, _P, _P, _P, _P]),
     "splat_aaa_preprocess_backward": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P]),
@@ -108,7 +109,8 @@ class SplatAaaFrame(ctypes.Structure):
                 ("tanfov_x", _F), ("tanfov_y", _F), ("principal_x", _F), ("principal_y", _F),
                 ("scale_modifier", _F), ("focal_x", _F), ("focal_max", _F),
                 ("sort_order", _I), ("ewa", _I), ("new_aabb", _I), ("near_clipping", _I),
-                ("tile_culling", _I), ("complete", _I), ("cooperative", _I)]
+                ("tile_culling", _I), ("complete", _I), ("cooperative", _I),
+                ("normalize_quats", _I)]
 
 
 def _load() -> ctypes.CDLL:

@@ -25,7 +25,7 @@ from ..statistics import StatisticsRequest
 from ..training import prepare_training_metadata
 from . import stages
 from .autograd import RasterizeView
-from .cameras import _camera_matmul, prepare_cameras
+from .cameras import prepare_cameras
 from .config import default_settings, validate_settings
 from .settings import ExtendedSettings
 
@@ -71,26 +71,22 @@ def _check_arguments(features, sh_coeffs, sh_degree):
 def _dense_geometry(frames, states, layout) -> dict[str, Tensor]:
     """aaa/metadata.py:55-91 _geometry: per view the pixel projection of the
     means (densification statistics only), radii = ceil of the bounding half
-    extents, effective opacities and tile counts; zero for culled rows."""
-    rows: dict[str, list[Tensor]] = {k: [] for k in ("radii", "means2d", "opacities",
-                                                     "tiles_per_gauss")}
-    for (b, c, view, _features, _bg), st in zip(frames, states):
+    extents, effective opacities and tile counts; zero for culled rows (one
+    kernel per view, stages.metadata)."""
+    views, n, dev = len(frames), layout.n, layout.device
+    radii = torch.empty((views, n, 2), device=dev, dtype=torch.int32)
+    means2d = torch.empty((views, n, 2), device=dev, dtype=torch.float32)
+    opacities = torch.empty((views, n), device=dev, dtype=torch.float32)
+    for v, ((b, c, view, _features, _bg), st) in enumerate(zip(frames, states)):
         vm = batch_item(batch_item(layout.viewmats, b), c)
-        means = layout.means[b]
-        points = _camera_matmul(means, vm[:3, :3].T) + vm[:3, 3]
-        fx = view.width / (2 * view.tanfovx)
-        fy = view.height / (2 * view.tanfovy)
-        cx, cy = view.principal
-        z = points[:, 2].clamp_min(1e-12)
-        valid = st.radii > 0
-        screen = torch.stack((fx * points[:, 0] / z + cx, fy * points[:, 1] / z + cy), dim=-1)
-        rows["radii"].append(torch.where(valid[:, None], st.rects.ceil().to(torch.int32), 0))
-        rows["means2d"].append(torch.where(valid[:, None], screen, 0))
-        rows["opacities"].append(torch.where(valid, st.opacity, 0))
-        rows["tiles_per_gauss"].append(st.tiles)
-    return {name: (r[0] if len(r) == 1 else torch.stack(r)).reshape(
-        (layout.batch_count, layout.cameras, layout.n) + tuple(r[0].shape[1:]))
-        for name, r in rows.items()}
+        focal = (view.width / (2 * view.tanfovx), view.height / (2 * view.tanfovy))
+        stages.metadata(vm, focal, view.principal, layout.means[b], st, radii[v], means2d[v],
+                        opacities[v])
+    tiles = torch.stack([st.tiles for st in states]) if states else torch.empty(
+        (0, n), device=dev, dtype=torch.int32)
+    shape = (layout.batch_count, layout.cameras, n)
+    return {"radii": radii.reshape(shape + (2,)), "means2d": means2d.reshape(shape + (2,)),
+            "opacities": opacities.reshape(shape), "tiles_per_gauss": tiles.reshape(shape)}
 
 
 def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, viewmats: Tensor,
@@ -111,9 +107,12 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
     not supported (as in the reference)."""
     validate_camera_options(width, height, near_plane, far_plane, radius_clip)
     sh_degree = _check_arguments(features, sh_coeffs, sh_degree)
+    # the raw quaternions go to the kernels, which normalise them with
+    # F.normalize's bits and return their gradient (inputs.py:252)
     layout = normalize_inputs(means, quats, scales, opacities,
                               features if sh_coeffs is None else sh_coeffs, viewmats, Ks,
-                              backgrounds, extra_features, filter3d, sh_degree)
+                              backgrounds, extra_features, filter3d, sh_degree,
+                              normalize_quats=False)
     if settings is not None:
         validate_settings(settings)
     config = default_settings() if settings is None else settings.copy()
@@ -147,7 +146,7 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
                                view.projmatrix.detach(), view.campos.detach()),
                 config, bm.detach(), layout.quats[b].detach(), layout.scales[b].detach(),
                 layout.opacities[b].detach(), None if filters is None else filters.detach(),
-                radius_clip))
+                radius_clip, raw_quats=True))
             frames.append((b, c, view, feats, bg))
     dense = _dense_geometry(frames, states, layout)
     # packed metadata keeps the rows whose rounded extents are positive

@@ -58,6 +58,9 @@ class AaaState:
     radii: Tensor
     tiles: Tensor        # tiles_touched
     valid: Tensor        # bool (N)
+    # the quaternions given to the kernels are raw: they normalise them (with
+    # F.normalize's bits) and the preprocessing adjoint returns their gradient
+    raw_quats: bool = False
 
 
 def default_binning(settings: ExtendedSettings) -> bool:
@@ -78,7 +81,8 @@ def require_supported(settings: ExtendedSettings) -> None:
 
 def frame(view: AaaView, settings: ExtendedSettings, means: Tensor, quats: Tensor,
           scales: Tensor, opacities: Tensor, filters: Tensor | None, pin: Args,
-          sh: Tensor | None = None, sh_degree: int = 0, flags: dict | None = None):
+          sh: Tensor | None = None, sh_degree: int = 0, flags: dict | None = None,
+          raw_quats: bool = False):
     """The SplatAaaFrame of one view (device pointers kept alive by pin).
 
     flags overrides the preprocessing switches (the golden tests drive
@@ -107,7 +111,8 @@ def frame(view: AaaView, settings: ExtendedSettings, means: Tensor, quats: Tenso
                   new_aabb=bool(getattr(settings, "new_aabb", True)),
                   near_clipping=bool(getattr(settings, "near_clipping", False)),
                   tile_culling=bool(culling.tile_based_culling),
-                  complete=bool(settings.eval_3D) and not cooperative, cooperative=cooperative)
+                  complete=bool(settings.eval_3D) and not cooperative, cooperative=cooperative,
+                  normalize_quats=raw_quats)
     values.update(flags or {})
     for name, value in values.items():
         setattr(f, name, int(value))
@@ -116,16 +121,17 @@ def frame(view: AaaView, settings: ExtendedSettings, means: Tensor, quats: Tenso
 
 def preprocess(view: AaaView, settings: ExtendedSettings, means: Tensor, quats: Tensor,
                scales: Tensor, opacities: Tensor, filters: Tensor | None = None,
-               radius_clip: float = 0.0) -> AaaState:
-    """aaa/preprocess.py:165-560 + aaa/frame.py:51-58 (radius clip)."""
+               radius_clip: float = 0.0, raw_quats: bool = False) -> AaaState:
+    """aaa/preprocess.py:165-560 + aaa/frame.py:51-58 (radius clip); raw_quats:
+    quats are unnormalised (the kernels normalise them)."""
     n, dev = len(means), means.device
     pin = Args()
-    f = frame(view, settings, means, quats, scales, opacities, filters, pin)
+    f = frame(view, settings, means, quats, scales, opacities, filters, pin, raw_quats=raw_quats)
     empty = lambda *shape: torch.empty(shape, device=dev, dtype=torch.float32)  # noqa: E731
     st = AaaState(empty(n, 2), empty(n, 2), empty(n), empty(n, 4, 4), empty(n),
                   torch.empty(n, device=dev, dtype=torch.int32),
                   torch.empty(n, device=dev, dtype=torch.int32),
-                  torch.empty(n, device=dev, dtype=torch.uint8))
+                  torch.empty(n, device=dev, dtype=torch.uint8), raw_quats)
     queued = torch.empty(max(n, 1), device=dev, dtype=torch.int32)
     size = torch.empty(1, device=dev, dtype=torch.int32)
     s = nv.stream(dev)
@@ -194,6 +200,24 @@ def bin_and_sort_many(states: list[AaaState], width: int, height: int,
         b["tile_order"] = core.tile_order(b)
         bins.append(b)
     return bins, values[len(states):]
+
+
+def metadata(view_matrix: Tensor, focal: tuple[float, float], principal: tuple[float, float],
+             means: Tensor, state: AaaState, radii: Tensor, means2d: Tensor,
+             opacities: Tensor) -> None:
+    """aaa/metadata.py:55-91 _geometry of one view into preallocated rows:
+    radii (N,2) int32 = ceil of the half extents, means2d (N,2) the pixel
+    projection of the means, opacities (N) the effective opacities; zeros
+    where state.radii <= 0.  view_matrix: (4,4) world-to-camera."""
+    n = len(means)
+    if n == 0:
+        return
+    pin = Args()
+    check(lib.splat_aaa_metadata(n, pin(view_matrix.contiguous()), float(focal[0]),
+                                 float(focal[1]), float(principal[0]), float(principal[1]),
+                                 pin(means), ptr(state.rects), ptr(state.radii),
+                                 ptr(state.opacity), ptr(radii), ptr(means2d), ptr(opacities),
+                                 nv.stream(means.device)), "aaa_metadata")
 
 
 # Blend records kept by the forward for the backward: per pixel up to this
@@ -284,7 +308,7 @@ def preprocess_backward(view: AaaView, settings: ExtendedSettings, means: Tensor
                         scales: Tensor, opacities: Tensor, state: AaaState, grad_transforms: Tensor,
                         grad_opacity: Tensor):
     """aaa/backward_preprocess.py:270-346: (opacities, means, scales, quats)
-    gradients."""
+    gradients (of the raw quaternions when state.raw_quats)."""
     n, dev = len(means), means.device
     g_o = torch.empty(n, device=dev)
     g_m = torch.empty((n, 3), device=dev)
@@ -292,7 +316,8 @@ def preprocess_backward(view: AaaView, settings: ExtendedSettings, means: Tensor
     g_q = torch.empty((n, 4), device=dev)
     if n:
         pin = Args()
-        f = frame(view, settings, means, quats, scales, opacities, None, pin)
+        f = frame(view, settings, means, quats, scales, opacities, None, pin,
+                  raw_quats=state.raw_quats)
         check(lib.splat_aaa_preprocess_backward(
             ctypes_ref(f), ptr(state.radii), pin(grad_transforms), pin(grad_opacity), ptr(g_o),
             ptr(g_m), ptr(g_s), ptr(g_q), nv.stream(dev)), "aaa_preprocess_backward")
@@ -307,7 +332,8 @@ def camera_backward(view: AaaView, settings: ExtendedSettings, means: Tensor, qu
     dev = means.device
     sums = torch.empty(23, device=dev)
     pin = Args()
-    f = frame(view, settings, means, quats, scales, state.opacity, filters, pin)
+    f = frame(view, settings, means, quats, scales, state.opacity, filters, pin,
+              raw_quats=state.raw_quats)
     check(lib.splat_aaa_camera_backward(ctypes_ref(f), ptr(state.radii), pin(state.opacity),
                                         pin(grad_transforms), pin(grad_opacity), ptr(sums),
                                         nv.stream(dev)), "aaa_camera_backward")
@@ -316,5 +342,6 @@ def camera_backward(view: AaaView, settings: ExtendedSettings, means: Tensor, qu
     return g_view, sums[:16].view(4, 4), sums[20:23]
 
 
-__all__ = ["AaaView", "AaaState", "RECORD_CAPACITY", "preprocess", "bin_and_sort_many", "render",
-           "render_backward", "preprocess_backward", "camera_backward", "default_binning"]
+__all__ = ["AaaView", "AaaState", "RECORD_CAPACITY", "preprocess", "metadata", "bin_and_sort_many",
+           "render", "render_backward", "preprocess_backward", "camera_backward",
+           "default_binning"]

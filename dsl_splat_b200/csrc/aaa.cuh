@@ -473,7 +473,8 @@ struct PreprocessParams {
   int n;
   const float* means;       // (n,3)
   const float* scales;      // (n,3)
-  const float* quats;       // (n,4) normalised
+  const float* quats;       // (n,4) normalised, or raw when normalize_quats
+  int normalize_quats;      // normalise in-kernel with the bits of Torch's F.normalize
   const float* opacities;   // (n)
   const float* sh;          // (n,K,3) or null
   int sh_k, degree, sort_order;
@@ -541,7 +542,8 @@ __global__ void __launch_bounds__(128) aaa_preprocess_kernel(PreprocessParams p)
     if (p.near_clipping && t[2] < 0.2f) return false;
     float R[3][3];
     {
-      const float4 q = reinterpret_cast<const float4*>(p.quats)[i];
+      float4 q = reinterpret_cast<const float4*>(p.quats)[i];
+      if (p.normalize_quats) q = torch_normalize4(q);
       glm_rotation(q.x, q.y, q.z, q.w, R);
     }
     cam[0] = p.campos[0];
@@ -720,6 +722,41 @@ __global__ void __launch_bounds__(256)
       }
     }
   }
+}
+
+// ---- metadata: aaa/metadata.py:55-91 _geometry for one view ---------------------
+// Per Gaussian with radii > 0 (after the remainder cull): the half extents
+// rounded up (int2), the pixel projection of the mean (fx x/z + cx, fy y/z +
+// cy, z clamped to 1e-12; densification statistics only) and the effective
+// opacity; zeros elsewhere.  One launch instead of the reference's Torch
+// matmul and masks.
+__global__ void __launch_bounds__(256)
+    aaa_metadata_kernel(int n, const float* __restrict__ view, float fx, float fy, float cx,
+                        float cy, const float* __restrict__ means,
+                        const float* __restrict__ rects, const int* __restrict__ radii,
+                        const float* __restrict__ opacity, int* __restrict__ out_radii,
+                        float* __restrict__ out_means2d, float* __restrict__ out_opacity) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int2 r = make_int2(0, 0);
+  float2 m2 = make_float2(0.0f, 0.0f);
+  float o = 0.0f;
+  if (radii[i] > 0) {
+    const float2 e = reinterpret_cast<const float2*>(rects)[i];
+    r = make_int2(f2i(ceilf(e.x)), f2i(ceilf(e.y)));
+    const float m[3] = {means[3 * i], means[3 * i + 1], means[3 * i + 2]};
+    float v[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k)
+      v[k] = ((view[4 * k] * m[0] + view[4 * k + 1] * m[1]) + view[4 * k + 2] * m[2]) +
+             view[4 * k + 3];
+    const float z = fmaxf(v[2], 1e-12f);
+    m2 = make_float2(fx * v[0] / z + cx, fy * v[1] / z + cy);
+    o = opacity[i];
+  }
+  reinterpret_cast<int2*>(out_radii)[i] = r;
+  reinterpret_cast<float2*>(out_means2d)[i] = m2;
+  out_opacity[i] = o;
 }
 
 // ---- K22: keys of every visible Gaussian's tiles ------------------------------------
@@ -947,7 +984,8 @@ struct AdjointParams {
   int n;
   const float* means;
   const float* scales;
-  const float* quats;
+  const float* quats;          // normalised, or raw when normalize_quats
+  int normalize_quats;         // K28 then returns the gradient of the raw quaternions
   const float* opacities;      // raw input opacities (K28) / effective (K29)
   const int* radii;
   const float* filters;        // K29: (n) or null
@@ -1007,7 +1045,8 @@ __global__ void __launch_bounds__(128) aaa_preprocess_adjoint_kernel(AdjointPara
     dil_sq[k] = squared[k] + variance;
     dilated[k] = sqrtf(dil_sq[k]);
   }
-  const float4 q4 = reinterpret_cast<const float4*>(p.quats)[i];
+  const float4 raw_q = reinterpret_cast<const float4*>(p.quats)[i];
+  const float4 q4 = p.normalize_quats ? torch_normalize4(raw_q) : raw_q;
   const float qr = q4.x, qx = q4.y, qy = q4.z, qz = q4.w;
   float R[3][3];
   plain_rotation(qr, qx, qy, qz, R);
@@ -1085,7 +1124,21 @@ __global__ void __launch_bounds__(128) aaa_preprocess_adjoint_kernel(AdjointPara
                     2.0f * qz * (d[1][2] + d[2][1])) - 4.0f * qy * (d[2][2] + d[0][0]);
   const float g3 = ((2.0f * qr * (d[0][1] - d[1][0]) + 2.0f * qx * (d[2][0] + d[0][2])) +
                     2.0f * qy * (d[1][2] + d[2][1])) - 4.0f * qz * (d[1][1] + d[0][0]);
-  reinterpret_cast<float4*>(gq)[0] = make_float4(g0, g1, g2, g3);
+  float4 g = make_float4(g0, g1, g2, g3);
+  if (p.normalize_quats) {
+    // VJP of F.normalize(x) = x / max(|x|, 1e-12) (inputs.py:252):
+    // (g - n (n . g)) / |x|, or g / 1e-12 where the norm is clamped
+    const float norm = sqrtf((raw_q.x * raw_q.x + raw_q.z * raw_q.z) +
+                             (raw_q.y * raw_q.y + raw_q.w * raw_q.w));
+    if (norm > 1e-12f) {
+      const float d = ((q4.x * g.x + q4.y * g.y) + q4.z * g.z) + q4.w * g.w;
+      g = make_float4((g.x - q4.x * d) / norm, (g.y - q4.y * d) / norm, (g.z - q4.z * d) / norm,
+                      (g.w - q4.w * d) / norm);
+    } else {
+      g = make_float4(g.x / 1e-12f, g.y / 1e-12f, g.z / 1e-12f, g.w / 1e-12f);
+    }
+  }
+  reinterpret_cast<float4*>(gq)[0] = g;
 }
 
 // ---- K29: camera adjoint -------------------------------------------------------------
@@ -1137,7 +1190,8 @@ __global__ void __launch_bounds__(128) aaa_camera_adjoint_kernel(AdjointParams p
       dil_sq[k] = squared[k] + variance;
       dilated[k] = sqrtf(dil_sq[k]);
     }
-    const float4 q4 = reinterpret_cast<const float4*>(p.quats)[i];
+    float4 q4 = reinterpret_cast<const float4*>(p.quats)[i];
+    if (p.normalize_quats) q4 = torch_normalize4(q4);
     float R[3][3];
     plain_rotation(q4.x, q4.y, q4.z, q4.w, R);
     const float D[3][3] = {{dilated[0], 0.0f, 0.0f}, {0.0f, dilated[1], 0.0f}, {0.0f, 0.0f, dilated[2]}};

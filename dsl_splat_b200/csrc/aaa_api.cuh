@@ -160,6 +160,7 @@ int splat_aaa_preprocess(const SplatAaaFrame* f, float* centers, float* rects, f
   p.means = f->means;
   p.scales = f->scales;
   p.quats = f->quats;
+  p.normalize_quats = f->normalize_quats;
   p.opacities = f->opacities;
   p.sh = f->sh;
   p.sh_k = f->sh_k;
@@ -215,6 +216,22 @@ int splat_aaa_cull_remainder(int n, const int* queued, const int* queue_size, co
   splat::aaa::aaa_cull_remainder_kernel<<<blocks_for(warps, 8), 256, 0, counted(as_stream(stream))>>>(
       queued, queue_size, centers, rects, transforms, opacity, width, height, radii, tiles, valid);
   return check_launch("aaa_cull_remainder");
+}
+
+int splat_aaa_metadata(int n, const float* view, float fx, float fy, float cx, float cy,
+                       const float* means, const float* rects, const int* radii,
+                       const float* opacity, int* out_radii, float* out_means2d,
+                       float* out_opacity, void* stream) {
+  if (n < 0) return fail(kInvalidArgument, "n < 0");
+  if (n == 0) return kOk;
+  if (!view || !means || !rects || !radii || !opacity || !out_radii || !out_means2d ||
+      !out_opacity)
+    return fail(kInvalidArgument, "null AAA metadata argument");
+  if (!aligned(rects, 8) || !aligned(out_radii, 8) || !aligned(out_means2d, 8))
+    return fail(kInvalidArgument, "AAA metadata rows misaligned");
+  splat::aaa::aaa_metadata_kernel<<<blocks_for(n, 256), 256, 0, counted(as_stream(stream))>>>(
+      n, view, fx, fy, cx, cy, means, rects, radii, opacity, out_radii, out_means2d, out_opacity);
+  return check_launch("aaa_metadata");
 }
 
 size_t splat_aaa_bin_workspace_bytes(long long pairs) { return aaa_bin_layout(pairs).bytes; }
@@ -426,6 +443,7 @@ int splat_aaa_preprocess_backward(const SplatAaaFrame* f, const int* radii,
   p.means = f->means;
   p.scales = f->scales;
   p.quats = f->quats;
+  p.normalize_quats = f->normalize_quats;
   p.opacities = f->opacities;
   p.radii = radii;
   p.view = f->view;
@@ -464,6 +482,7 @@ int splat_aaa_camera_backward(const SplatAaaFrame* f, const int* radii,
   p.means = f->means;
   p.scales = f->scales;
   p.quats = f->quats;
+  p.normalize_quats = f->normalize_quats;
   p.opacities = effective_opacity;
   p.radii = radii;
   p.filters = f->filters;

@@ -34,8 +34,8 @@ namespace aaa {
 constexpr int kAccTransform = 0, kAccOpacity = 12, kAccScreen = 13, kAccAbs = 15,
               kAccColor = 17, kAccStride = 21;
 constexpr int kTilePositions = 1024;  // positions filed per tile
-constexpr int kTileSamples = 32768;   // samples filed per tile (16-bit entries: j << 8 | pixel)
-constexpr int kTileCache = 640;       // positions whose id, opacity and colours are staged
+constexpr int kTileSamples = 24576;   // samples filed per tile (16-bit entries: j << 8 | pixel)
+constexpr int kTileCache = 512;       // positions whose id, opacity and colours are staged
 
 struct TileShared {
   float4 rgb[kTileCache];           // colours (four-channel features)
@@ -179,7 +179,7 @@ SPLAT_DEV int2 local_pixel(int l) {
 }
 
 template <int CHP, bool SCREEN, bool ABS>
-__global__ void __launch_bounds__(256, 2) aaa_record_backward_kernel(HierParams p) {
+__global__ void __launch_bounds__(256, 3) aaa_record_backward_kernel(HierParams p) {
   extern __shared__ float4 tile_shared_raw[];
   TileShared& s = *reinterpret_cast<TileShared*>(tile_shared_raw);
   const int tile = blockIdx.x;
@@ -209,14 +209,13 @@ __global__ void __launch_bounds__(256, 2) aaa_record_backward_kernel(HierParams 
     s.fallback = 0;
   }
   __syncthreads();
-  int my_max = -1, my_samples = 0;
+  int my_max = -1;
 #pragma unroll 4
   for (int j = 0; j < count; ++j) {
     const int pos = __float_as_int(rec[(static_cast<long long>(j) << 8) + local].x);
     if (pos >= 0 && pos < kTilePositions) {
       atomicAdd(&s.cursor[pos], 1);
       my_max = max(my_max, pos);
-      ++my_samples;
     } else {
       s.fallback = 1;
     }
@@ -359,10 +358,17 @@ __global__ void __launch_bounds__(256, 2) aaa_record_backward_kernel(HierParams 
     float acc[32];
 #pragma unroll
     for (int c = 0; c < 32; ++c) acc[c] = 0.0f;
-    for (int k = b + lane; k < e; k += 32) {
-      const unsigned code = s.list[k];
-      const int j = static_cast<int>(code >> 8), l = static_cast<int>(code & 255u);
-      const float2 v = rec[(static_cast<long long>(j) << 8) + l];
+    // the entry code (j << 8) | pixel is also the record's index in the
+    // tile; the next chunk's entry is requested before this one is computed
+    int k = b + lane;
+    unsigned code = k < e ? s.list[k] : 0u;
+    float2 v = k < e ? rec[code] : make_float2(0.0f, 0.0f);
+    for (; k - lane < e; k += 32) {
+      const int kn = k + 32;
+      const unsigned code_next = kn < e ? s.list[kn] : 0u;
+      const float2 v_next = kn < e ? rec[code_next] : make_float2(0.0f, 0.0f);
+      if (k >= e) break;
+      const int l = static_cast<int>(code & 255u);
       const int2 pxy = local_pixel(l);
       float terms[kAccStride];
       ray_terms<SCREEN, ABS>(r0, r1, r3, static_cast<float>(tile_x + pxy.x),
@@ -380,6 +386,8 @@ __global__ void __launch_bounds__(256, 2) aaa_record_backward_kernel(HierParams 
       }
 #pragma unroll
       for (int c = 0; c < kAccStride; ++c) acc[c] += terms[c];
+      code = code_next;
+      v = v_next;
     }
     const float total = warp_row_sum(acc, lane);
     float* dst = colors4 ? component_address<SCREEN, ABS, true>(p, id, lane)

@@ -586,7 +586,10 @@ struct HierWarp {
         }
       }
       __syncwarp(kFull);
-#pragma unroll
+      // not unrolled: each unrolled copy would inline push_mid (and its
+      // front_mid and blend) once more; the smaller kernel measured 9 %
+      // faster (instruction-cache misses were its top stall)
+#pragma unroll 1
       for (int it = 0; it < 2; ++it) {
         if (px.tail_count > 32) {
           push_mid(false);
@@ -605,6 +608,7 @@ struct HierWarp {
     }
     if (__any_sync(kFull, px.active)) {
       if (px.tail_count != 0) {
+#pragma unroll 1
         for (int it = 0; it < 2; ++it) {
           push_mid(true);
           if (it == 0 && px.tail_count == 0) break;

@@ -414,7 +414,8 @@ typedef struct SplatAaaFrame {
   int n, width, height;
   const float* means;      /* (n,3) */
   const float* scales;     /* (n,3) activated */
-  const float* quats;      /* (n,4) normalised wxyz, 16-byte aligned */
+  const float* quats;      /* (n,4) wxyz, 16-byte aligned: normalised, or raw when
+                              normalize_quats */
   const float* opacities;  /* (n) activated */
   const float* sh;         /* (n,sh_k,3) SH inputs of preprocess_3d, or NULL */
   int sh_k, sh_degree;
@@ -429,6 +430,9 @@ typedef struct SplatAaaFrame {
   int ewa, new_aabb, near_clipping, tile_culling;
   int complete;            /* eval_3D and not cooperative (aaa/preprocess.py:321-322) */
   int cooperative;         /* load_balancing and tile_based_culling */
+  int normalize_quats;     /* 1: quats are raw; the kernels normalise them with the bits of
+                              Torch's F.normalize (inputs.py:252) and the preprocessing
+                              adjoint returns the raw quaternions' gradient */
 } SplatAaaFrame;
 
 /* aaa/preprocess.py:165-451 -> aaa/preprocess3d.py:17-245 preprocess_3d
@@ -452,6 +456,17 @@ int splat_aaa_cull_remainder(int n, const int* queued, const int* queue_size,
                              const float* centers, const float* rects, const float* transforms,
                              const float* opacity, int width, int height, int* radii, int* tiles,
                              unsigned char* valid, void* stream);
+
+/* aaa/metadata.py:55-91 _geometry for one view (after the remainder cull):
+ * per Gaussian with radii > 0 the half extents rounded up (out_radii (n,2)
+ * int32), the pixel projection of the mean (out_means2d (n,2): fx x/z + cx,
+ * fy y/z + cy with (x, y, z) = view (row-major 4x4 world-to-camera) * mean
+ * and z clamped to 1e-12) and the effective opacity (out_opacity (n));
+ * zeros for the other rows.  rects/out_* 8-byte aligned. */
+int splat_aaa_metadata(int n, const float* view, float fx, float fy, float cx, float cy,
+                       const float* means, const float* rects, const int* radii,
+                       const float* opacity, int* out_radii, float* out_means2d,
+                       float* out_opacity, void* stream);
 
 /* aaa/binning.py:278-342 bin_and_sort after the count scan (splat_scan_counts
  * of tiles, its total read by the host as the reference does at

@@ -471,3 +471,38 @@ def test_rasterize_empty_and_culled(case):
     want = bg.view(1, 1, 1, 3).expand(1, sc.height, sc.width, 3)
     assert torch.equal(res.features, want)
     assert not res.alpha.any()
+
+
+def test_recorded_backward_dense_tile_takes_the_per_sample_path():
+    """A tile whose blended samples exceed the record backward's per-tile list
+    (24,576 samples) is reduced sample by sample; its gradients equal the
+    replay's, and a second backward of the same records replays."""
+    dev = _dev()
+    n, W, H = 200, 64, 64
+    gen = torch.Generator().manual_seed(5)
+    means = torch.cat([torch.randn(n, 2, generator=gen) * 0.05,
+                       4.0 + torch.rand(n, 1, generator=gen)], 1)
+    quats = F.normalize(torch.randn(n, 4, generator=gen), dim=-1)
+    scales = torch.full((n, 3), 2.0)
+    opacities = torch.full((n,), 0.01)
+    K = torch.tensor([[100.0, 0.0, 32.0], [0.0, 100.0, 32.0], [0.0, 0.0, 1.0]])
+    cams = aaa.cameras.prepare_cameras(torch.eye(4)[None, None].to(dev), K[None, None].to(dev),
+                                       W, H, 0.01, 1e10)
+    st = S.preprocess(cams.view(0, 0), aaa.default_settings(), means.to(dev), quats.to(dev),
+                      scales.to(dev), opacities.to(dev))
+    bins, _ = S.bin_and_sort_many([st], W, H)
+    feats = torch.rand(n, 4, generator=gen).to(dev)
+    feats[:, 3] = 1.0
+    bg = torch.zeros(4, device=dev)
+    image, final_t, _, rec = S.render(st, bins[0], feats, bg, W, H, True, record_capacity=256)
+    assert int(rec["overflow"].sum()) == 0
+    assert int(rec["counts"].view(-1, 256).sum(1).max()) > 24576
+    up = torch.randn(4, H, W, generator=gen).to(dev)
+    args = (st, bins[0], feats, bg, image, final_t, up, W, H, True)
+    got = S.render_backward(*args, screen=True, absgrad=True, records=rec)
+    assert rec["consumed"]
+    again = S.render_backward(*args, screen=True, absgrad=True, records=rec)
+    want = S.render_backward(*args, screen=True, absgrad=True)
+    for a, b, c in zip(got, want, again):
+        assert rel_l2(a.cpu(), b.cpu()) <= 1e-4
+        assert torch.equal(b, c) or rel_l2(c.cpu(), b.cpu()) <= 1e-5
