@@ -88,7 +88,7 @@ SIGNATURES: dict[str, tuple] = {
     "splat_aaa_bin": (_I, [_I, _L, _P, _P, _P, _P, _P, _P, _I, _I, _P, _Z, _P, _P, _P]),
     "splat_aaa_emit": (_I, [_I, _L, _P, _P, _P, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
     "splat_aaa_render": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
-                              _I, _P, _P, _P, _P]),
+                              _I, _P, _P, _P, _I, _I, _P, _P, _P, _P]),
     "splat_aaa_record_bytes": (_Z, [_I, _I, _I]),
     "splat_aaa_metadata": (_I, [_I, _P, _F, _F, _F, _F, _P, _P, _P, _P, _P, _P, _P, _P]),
     "splat_aaa_render_backward": (_I, [_I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P,

@@ -21,7 +21,7 @@ from torch import Tensor
 
 from ..cameras import validate_camera_options
 from ..inputs import batch_item, normalize_inputs, spherical_harmonics
-from ..statistics import StatisticsRequest
+from ..statistics import StatisticsRequest, prepare_statistics
 from ..training import prepare_training_metadata
 from . import stages
 from .autograd import RasterizeView
@@ -117,10 +117,12 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
         validate_settings(settings)
     config = default_settings() if settings is None else settings.copy()
     stages.require_supported(config)
-    if statistics:
-        raise NotImplementedError("contribution statistics are not implemented for aaa.rasterize "
-                                  "on the B200 path")
     cameras = prepare_cameras(layout.viewmats, layout.Ks, width, height, near_plane, far_plane)
+    prepared_stats, statistics_outputs = (
+        prepare_statistics(statistics, batch_dims=layout.batch_dims,
+                           batch_count=layout.batch_count, cameras=layout.cameras, n=layout.n,
+                           width=width, height=height, device=layout.device)
+        if statistics else ([], {}))
     colors = layout.colors
     ones = torch.ones(layout.n, 1, device=layout.device, dtype=torch.float32)
     frames, states = [], []
@@ -174,7 +176,8 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
             stages.AaaView(view.width, view.height, view.tanfovx, view.tanfovy, view.principal,
                            view.viewmatrix.detach(), view.projmatrix.detach(),
                            view.campos.detach()),
-            config, st, bins[i], bg, filters, training.absolute_targets[i], grad_enabled)
+            config, st, bins[i], bg, filters, training.absolute_targets[i], grad_enabled,
+            prepared_stats[i] if statistics else None)
         hwc = image.permute(1, 2, 0)
         if layout.n == 0:
             hwc = hwc + bg
@@ -187,7 +190,8 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
         meta["render_extra_signals"] = torch.stack(extras).reshape(
             shape + (layout.extras.channels,))
     return RasterizationResult(torch.stack(outputs).reshape(shape + (channels,)),
-                               torch.stack(alphas).reshape(shape + (1,)), meta)
+                               torch.stack(alphas).reshape(shape + (1,)), meta,
+                               statistics_outputs)
 
 
 __all__ = ["rasterize", "RasterizationResult", "ExtendedSettings", "default_settings"]

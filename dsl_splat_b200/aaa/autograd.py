@@ -23,7 +23,8 @@ class RasterizeView(torch.autograd.Function):
     @staticmethod
     def forward(ctx: Any, means, quats, scales, opacities, features, means2d, viewmatrix,
                 projmatrix, campos, view: stages.AaaView, settings, state: stages.AaaState,
-                bins: dict, background, filters, absgrad_target, grad_enabled: bool):
+                bins: dict, background, filters, absgrad_target, grad_enabled: bool,
+                statistics=None):
         cull = bool(settings.culling_settings.hierarchical_4x4_culling)
         features = features.contiguous()
         needs_backward = grad_enabled and any(ctx.needs_input_grad[:9])
@@ -31,7 +32,8 @@ class RasterizeView(torch.autograd.Function):
         # the backward reads each pixel's samples instead of replaying queues
         image, final_t, contrib, records = stages.render(
             state, bins, features, background, view.width, view.height, cull,
-            record_capacity=stages.RECORD_CAPACITY if needs_backward else 0)
+            record_capacity=stages.RECORD_CAPACITY if needs_backward else 0,
+            statistics=statistics)
         if means.shape[0] == 0:
             image.zero_()
         ctx.mark_non_differentiable(final_t, contrib)
@@ -50,7 +52,7 @@ class RasterizeView(torch.autograd.Function):
     @staticmethod
     @once_differentiable
     def backward(ctx: Any, grad_image, grad_t, grad_contrib):
-        none = (None,) * 17
+        none = (None,) * 18
         if grad_image is None:
             return none
         means, quats, scales, opacities, features, image, final_t, background = ctx.saved_tensors
@@ -76,7 +78,7 @@ class RasterizeView(torch.autograd.Function):
                 g_opac.reshape_as(opacities) if needs[3] else None,
                 g_col if needs[4] else None, g_scr if needs[5] and g_scr is not None else None,
                 g_view if needs[6] else None, g_proj if needs[7] else None,
-                g_campos if needs[8] else None) + (None,) * 8
+                g_campos if needs[8] else None) + (None,) * 9
 
 
 __all__ = ["RasterizeView"]

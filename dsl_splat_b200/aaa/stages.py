@@ -231,10 +231,12 @@ RECORD_CAPACITY = 192
 
 
 def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, width: int,
-           height: int, cull: bool, record_capacity: int = 0):
+           height: int, cull: bool, record_capacity: int = 0, statistics=None):
     """aaa/render_hierarchical_warp.py:694-801: color (C,H,W), final_T and
     contributors (H,W); with record_capacity > 0 also the blend records
-    (a dict the backward takes), else None."""
+    (a dict the backward takes), else None.  statistics: a
+    PreparedStatistics whose counts / sums receive the view's contribution
+    statistics (render_statistics, :608-653)."""
     dev = features.device
     C = features.shape[1]
     image = torch.empty((C, height, width), device=dev, dtype=torch.float32)
@@ -255,6 +257,9 @@ def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, wi
                        overflow=torch.empty(tiles, device=dev, dtype=torch.int32))
     rec = records or {}
     pin = Args()
+    stats = statistics
+    stat_count = len(stats.key) if stats is not None else 0
+    stat_mask = sum(1 << r for r, k in enumerate(stats.key) if k == 1) if stat_count else 0
     with core._timed("aaa_render_forward", dev):
         check(lib.splat_aaa_render(features.shape[0], width, height, C, int(cull),
                                    ptr(bins["ranges"]), ptr(bins["point_list"]),
@@ -262,7 +267,10 @@ def render(state: AaaState, bins: dict, features: Tensor, background: Tensor, wi
                                    pin(background), ptr(bins.get("tile_order")), ptr(image),
                                    ptr(final_t), ptr(contrib), rec.get("capacity", 0),
                                    ptr(rec.get("entries")), ptr(rec.get("counts")),
-                                   ptr(rec.get("overflow")),
+                                   ptr(rec.get("overflow")), stat_count, stat_mask,
+                                   pin(stats.pixel_values) if stat_count else None,
+                                   ptr(stats.counts) if stat_count else None,
+                                   ptr(stats.sums) if stat_count else None,
                                    nv.stream(dev)), "aaa_render")
     return image, final_t, contrib, records
 

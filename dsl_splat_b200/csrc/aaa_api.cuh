@@ -91,9 +91,12 @@ int launch_hier(const HierParams& p, int tiles, bool backward, bool screen, bool
     q.only_flagged = p.tile_overflow;
     q.records = nullptr;
   }
-  if (!backward)
-    aaa_hier_kernel<CHP, false, false, false><<<blocks, kHierThreads, 0, counted(s)>>>(q);
-  else if (!screen)
+  if (!backward) {
+    if (q.stat_count)
+      aaa_hier_kernel<CHP, false, false, false, true><<<blocks, kHierThreads, 0, counted(s)>>>(q);
+    else
+      aaa_hier_kernel<CHP, false, false, false><<<blocks, kHierThreads, 0, counted(s)>>>(q);
+  } else if (!screen)
     aaa_hier_kernel<CHP, true, false, false><<<blocks, kHierThreads, 0, counted(s)>>>(q);
   else if (!absgrad)
     aaa_hier_kernel<CHP, true, true, false><<<blocks, kHierThreads, 0, counted(s)>>>(q);
@@ -334,7 +337,9 @@ int splat_aaa_render(int n, int width, int height, int channels, int cull, const
                      const int* points, const float* transforms, const float* opacity,
                      const float* colors, const float* bg, const int* tile_order, float* image,
                      float* final_t, int* contributors, int record_capacity, float* records,
-                     int* record_counts, int* tile_overflow, void* stream) {
+                     int* record_counts, int* tile_overflow, int stat_count, int stat_sum_mask,
+                     const float* stat_pixels, int* stat_counts, float* stat_sums,
+                     void* stream) {
   int r = check_hier_inputs(width, height, channels, ranges, points, transforms, opacity, colors, bg);
   if (r != kOk) return r;
   if (!image || !final_t || !contributors) return fail(kInvalidArgument, "null AAA blend output");
@@ -348,6 +353,10 @@ int splat_aaa_render(int n, int width, int height, int channels, int cull, const
       cudaMemsetAsync(tile_overflow, 0, sizeof(int) * tiles, as_stream(stream)) != cudaSuccess)
     return check_launch("aaa_render records");
   if (n < 0) return fail(kInvalidArgument, "n < 0");
+  if (stat_count < 0 || stat_count > 30 ||
+      (stat_count && (!stat_pixels || (!stat_counts && stat_sum_mask != (1 << stat_count) - 1) ||
+                      (!stat_sums && stat_sum_mask != 0))))
+    return fail(kInvalidArgument, "bad AAA statistics arguments");
   HierParams p{};
   p.n = n;
   p.width = width;
@@ -361,6 +370,11 @@ int splat_aaa_render(int n, int width, int height, int channels, int cull, const
   p.colors = colors;
   p.bg = bg;
   p.tile_order = tile_order;
+  p.stat_count = stat_count;
+  p.stat_sum_mask = stat_sum_mask;
+  p.stat_pixels = stat_pixels;
+  p.stat_counts = stat_counts;
+  p.stat_sums = stat_sums;
   p.image = image;
   p.final_t = final_t;
   p.contributors = contributors;

@@ -49,6 +49,13 @@ struct HierParams {
   int* record_counts;       // (T*256): count, or -1 when the capacity overflowed
   int* tile_overflow;       // (T): 1 when a pixel of the tile overflowed
   const int* only_flagged;  // replay: run only the tiles whose flag is set
+  // forward contribution statistics (statistics.py:47-73), or stat_count 0:
+  // request r is a weighted sum when bit r of stat_sum_mask is set, else a
+  // masked count; rows of n
+  int stat_count, stat_sum_mask;
+  const float* stat_pixels;  // (stat_count, H*W)
+  int* stat_counts;
+  float* stat_sums;
 };
 
 // The record backward of a recorded blend (aaa_backward.cu): every tile not

@@ -231,7 +231,25 @@ SPLAT_DEV void accumulate_ray_gradient(const HierParams& p, int id, float x, flo
   }
 }
 
-template <int CHP, bool BWD, bool SCREEN, bool ABS>
+// statistics.py:57-73 observe: a blended sample with weight w = alpha * T
+// adds 1 (masked count) or map * w (weighted sum) to its Gaussian wherever
+// the pixel's map value is nonzero (render_hierarchical_warp.py:160-163)
+SPLAT_DEV void observe(const HierParams& p, int id, int pixel, float w) {
+  const long long P = static_cast<long long>(p.width) * p.height;
+  int count_row = 0, sum_row = 0;
+  for (int r = 0; r < p.stat_count; ++r) {
+    const float v = p.stat_pixels[r * P + pixel];
+    if ((p.stat_sum_mask >> r) & 1) {
+      if (v != 0.0f) atomicAdd(p.stat_sums + static_cast<long long>(sum_row) * p.n + id, v * w);
+      ++sum_row;
+    } else {
+      if (v != 0.0f) atomicAdd(p.stat_counts + static_cast<long long>(count_row) * p.n + id, 1);
+      ++count_row;
+    }
+  }
+}
+
+template <int CHP, bool BWD, bool SCREEN, bool ABS, bool STATS = false>
 struct HierWarp {
   const HierParams& p;
   WarpQueues& q;
@@ -272,6 +290,7 @@ struct HierWarp {
 #pragma unroll
       for (int c = 0; c < CHP; ++c)
         if (c < C) px.color[c] = px.color[c] + (id >= 0 ? rgb[c] : 0.0f) * alpha * px.T;
+      if (STATS && id >= 0) observe(p, id, y * p.width + x, alpha * px.T);
       if (p.records) {
         if (px.records < p.record_capacity) {
           const long long at = ((static_cast<long long>(tile) * p.record_capacity + px.records) << 8) + local;
@@ -656,7 +675,7 @@ constexpr int kHierBlocksPerTile = 256 / kHierThreads;
 // Register budget: the forward at 16 blocks (32 warps, 64 registers) per SM
 // -- measured 5% faster than 12 blocks at 80 registers despite its spills --
 // the replay (run for overflowed tiles only) at 8.
-template <int CHP, bool BWD, bool SCREEN, bool ABS>
+template <int CHP, bool BWD, bool SCREEN, bool ABS, bool STATS = false>
 __global__ void __launch_bounds__(kHierThreads, BWD ? 8 : 16) aaa_hier_kernel(HierParams p) {
   __shared__ WarpQueues queues[kHierWarps];
   const int slot = blockIdx.x / kHierBlocksPerTile;
@@ -683,7 +702,7 @@ __global__ void __launch_bounds__(kHierThreads, BWD ? 8 : 16) aaa_hier_kernel(Hi
     }
     __syncwarp();
   }
-  HierWarp<CHP, BWD, SCREEN, ABS> w(p, queues[threadIdx.x >> 5]);
+  HierWarp<CHP, BWD, SCREEN, ABS, STATS> w(p, queues[threadIdx.x >> 5]);
   w.run(tile, local);
 }
 

@@ -495,12 +495,21 @@ int splat_aaa_emit(int n, long long pairs, const int* offsets, const float* cent
  * (HIER 64/8/4 blend, 4x4 culling when cull): image (C,H,W) planar
  * = blended features + T * bg, final_t and contributors (H,W).  n Gaussians
  * (ids outside [0, n) are never read); colors (n,C) row-major, C = 1..64;
- * tile_order (T) a block schedule (splat_tile_order) or NULL. */
+ * tile_order (T) a block schedule (splat_tile_order) or NULL.  Contribution
+ * statistics (render_hierarchical_warp.py:608-653 render_statistics with the
+ * observer of statistics.py:47-73): stat_count requests (0 disables, at most
+ * 30) over the (stat_count, H*W) maps stat_pixels; every blended sample, of
+ * weight alpha*T, whose pixel value v is nonzero adds 1 to its Gaussian's row
+ * of stat_counts (a masked count) or v*alpha*T to its row of stat_sums (a
+ * weighted sum: bit r of stat_sum_mask), rows of n in request order per
+ * kind. */
 int splat_aaa_render(int n, int width, int height, int channels, int cull, const int* ranges,
                      const int* points, const float* transforms, const float* opacity,
                      const float* colors, const float* bg, const int* tile_order, float* image,
                      float* final_t, int* contributors, int record_capacity, float* records,
-                     int* record_counts, int* tile_overflow, void* stream);
+                     int* record_counts, int* tile_overflow, int stat_count, int stat_sum_mask,
+                     const float* stat_pixels, int* stat_counts, float* stat_sums,
+                     void* stream);
 
 /* Bytes of the optional blend records of splat_aaa_render for a capacity
  * (records: T*256*capacity entries of two floats, 8-byte aligned;

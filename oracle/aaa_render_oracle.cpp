@@ -234,7 +234,34 @@ struct Scene {
   const float* final_t;     // (H, W)
   const float* pixel_grad;  // (C, H, W)
   Grads grads;
+  // forward contribution statistics (statistics.py:47-73), or stat_count 0
+  int stat_count, stat_sum_mask;
+  const float* stat_pixels;  // (stat_count, H*W)
+  int* stat_counts;          // (masked counts, n)
+  double* stat_sums;         // (weighted sums, n)
+  int n;
 };
+
+// statistics.py:57-73 observe: a blended sample with weight w = alpha * T
+// adds 1 (masked count) or map * w (weighted sum) to its Gaussian wherever
+// the pixel's map value is nonzero
+void observe(const Scene& s, int id, int pixel, float w) {
+  const long long P = static_cast<long long>(s.width) * s.height;
+  int count_row = 0, sum_row = 0;
+  for (int r = 0; r < s.stat_count; ++r) {
+    const float v = s.stat_pixels[r * P + pixel];
+    if ((s.stat_sum_mask >> r) & 1) {
+      if (v != 0.0f) atomic_add(s.stat_sums + static_cast<long long>(sum_row) * s.n + id, v * w);
+      ++sum_row;
+    } else {
+      if (v != 0.0f) {
+#pragma omp atomic
+        s.stat_counts[static_cast<long long>(count_row) * s.n + id] += 1;
+      }
+      ++count_row;
+    }
+  }
+}
 
 struct Pixel {
   bool active;
@@ -338,6 +365,7 @@ void WarpReplay::blend(int l) {
   const float* rgb = id >= 0 ? s_.colors + static_cast<long long>(id) * C : nullptr;
   if (!backward_) {
     for (int c = 0; c < C; ++c) p.color[c] = p.color[c] + (rgb ? rgb[c] : 0.0f) * alpha * p.transmittance;
+    if (s_.stat_count && id >= 0) observe(s_, id, p.y * s_.width + p.x, alpha * p.transmittance);
   } else {
     float alpha_gradient = 0.0f;
     const float weight = alpha * p.transmittance;
@@ -642,16 +670,27 @@ void WarpReplay::write_forward(float* image, float* final_t, int* contributors) 
 
 extern "C" {
 
-// aaa/render_hierarchical_warp.py:599-691 render for one view: image
-// (C, H, W) planar, final transmittance and evaluated-sample counts (H, W).
-// transforms (n, 4, 4) mathematical rows; colors (n, C); bg (C); ranges
-// (T, 2); points the sorted ids.  Returns 0, or -1 if C is unsupported.
+// aaa/render_hierarchical_warp.py:599-691 render (and render_statistics,
+// :608-653) for one view: image (C, H, W) planar, final transmittance and
+// evaluated-sample counts (H, W).  transforms (n, 4, 4) mathematical rows;
+// colors (n, C); bg (C); ranges (T, 2); points the sorted ids.  With
+// stat_count > 0 every blended sample is observed: request r (a
+// (stat_count, H*W) map) is a weighted sum into stat_sums when bit r of
+// stat_sum_mask is set, else a masked count into stat_counts (rows of n).
+// Returns 0, or -1 if C is unsupported.
 int oracle_aaa_render(int width, int height, int channels, const int* ranges, const int* points,
                       const float* transforms, const float* opacity, const float* colors,
                       const float* bg, int cull, float* image, float* final_t,
-                      int* contributors) {
+                      int* contributors, int n, int stat_count, int stat_sum_mask,
+                      const float* stat_pixels, int* stat_counts, double* stat_sums) {
   if (channels < 1 || channels > kMaxChannels) return -1;
   Scene s{};
+  s.n = n;
+  s.stat_count = stat_count;
+  s.stat_sum_mask = stat_sum_mask;
+  s.stat_pixels = stat_pixels;
+  s.stat_counts = stat_counts;
+  s.stat_sums = stat_sums;
   s.width = width;
   s.height = height;
   s.channels = channels;

@@ -115,7 +115,7 @@ def lib():
         L.oracle_aaa_camera_backward.restype = None
         L.oracle_aaa_render.argtypes = [
             _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _int, _f32p, _f32p,
-            _i32p]
+            _i32p, _int, _int, _int, _f32p, _i32p, _f64p]
         L.oracle_aaa_render.restype = _int
         L.oracle_aaa_render_backward.argtypes = [
             _int, _int, _int, _i32p, _i32p, _f32p, _f32p, _f32p, _f32p, _int, _f32p, _f32p,
@@ -584,20 +584,31 @@ def aaa_sort(keys, values, tiles_total):
     return skeys, svals, ranges
 
 
-def aaa_render(width, height, ranges, points, transforms, opacity, colors, bg, cull=True):
+def aaa_render(width, height, ranges, points, transforms, opacity, colors, bg, cull=True,
+               stat_maps=None, stat_kinds=()):
     """aaa/render_hierarchical_warp.py:599-691 (aaa_render_oracle.cpp): the
     HIER 64/8/4 blend.  Returns image (C, H, W), final_t (H, W) and the
-    evaluated-sample counts (H, W)."""
+    evaluated-sample counts (H, W); with stat_maps ((R, H, W), kinds 0 =
+    masked count, 1 = weighted sum) also the statistics: counts (Rc, n)
+    int32 and float64 sums (Rs, n) (statistics.py:47-73)."""
     colors = _c(colors)
-    C = colors.shape[1]
+    n, C = colors.shape
     image = np.zeros((C, height, width), np.float32)
     final_t = np.zeros((height, width), np.float32)
     contrib = np.zeros((height, width), np.int32)
+    kinds = tuple(stat_kinds)
+    maps = (np.zeros((1, 1), np.float32) if stat_maps is None
+            else _c(np.asarray(stat_maps, np.float32).reshape(len(kinds), -1)))
+    counts = np.zeros((max(1, kinds.count(0)), n), np.int32)
+    sums = np.zeros((max(1, kinds.count(1)), n), np.float64)
+    mask = sum(1 << r for r, k in enumerate(kinds) if k == 1)
     assert lib().oracle_aaa_render(
         int(width), int(height), C, _c(ranges, np.int32), _c(points, np.int32),
         _c(transforms), _c(opacity), colors, _c(bg), int(bool(cull)), image, final_t,
-        contrib) == 0
-    return image, final_t, contrib
+        contrib, n, len(kinds) if stat_maps is not None else 0, mask, maps, counts, sums) == 0
+    if stat_maps is None:
+        return image, final_t, contrib
+    return image, final_t, contrib, counts[: kinds.count(0)], sums[: kinds.count(1)]
 
 
 def aaa_render_backward(width, height, ranges, points, transforms, opacity, colors, bg, image,

@@ -593,7 +593,8 @@ def aaa_scenes():
     ]
 
 
-def aaa_render_case(name, scene: dict, channels: int, cull: bool, seed: int) -> dict:
+def aaa_render_case(name, scene: dict, channels: int, cull: bool, seed: int,
+                    statistics: bool = False) -> dict:
     """The AAA HIER 64/8/4 blend and its replay backward, the reference's own
     Warp kernels, on one view of the load-balanced path:
       aaa/preprocess3d.py:17-245 + aaa/cooperative_culling.py:152-192 +
@@ -605,7 +606,10 @@ def aaa_render_case(name, scene: dict, channels: int, cull: bool, seed: int) -> 
                                               statistics on).
     Features are seeded U[0,1] with a constant last channel (aaa/api.py:
     67-71 appends ones), the background seeded U[0,1] (0 for the constant
-    channel), the upstream image gradient seeded N(0,1)."""
+    channel), the upstream image gradient seeded N(0,1).  With statistics the
+    forward is the reference's render_statistics kernel (:608-653, the
+    observer of statistics.py:47-73 in blend_step) with a masked count over
+    the upper half and a weighted sum of seeded U[0,1] pixel weights."""
     flags = dict(ewa=True, new_aabb=True, near_clipping=False, tile_culling=True,
                  complete=False, cooperative=True)
     pre = aaa_case("coop", scene, flags, False, False)
@@ -636,10 +640,23 @@ def aaa_render_case(name, scene: dict, channels: int, cull: bool, seed: int) -> 
     transforms = pre["transforms"].astype(np.float32)
     opacity = pre["opacity"].astype(np.float32)
     t0 = time.time()
-    kernel = warp_render._make_kernel(cull, channels)
-    ws.launch(kernel, 256 * T, [W, H, A(ranges.reshape(-1)), A(ids), A(transforms, wp.mat44),
-                                A(opacity), A(feats, ftype), A(bg), A(image), A(final_t),
-                                A(contrib)], block=256)
+    stats = {}
+    args = [W, H, A(ranges.reshape(-1)), A(ids), A(transforms, wp.mat44), A(opacity),
+            A(feats, ftype), A(bg), A(image), A(final_t), A(contrib)]
+    if statistics:
+        mask = np.zeros((H, W), np.float32)
+        mask[: H // 2] = 1.0
+        weights = gen.uniform(0.0, 1.0, (H, W)).astype(np.float32)
+        pixel_values = np.stack([mask.ravel(), weights.ravel()])  # request 0 count, 1 sum
+        counts = np.zeros((1, n), np.int32)
+        sums = np.zeros((1, n), np.float32)
+        kernel = warp_render._make_kernel(cull, channels, (0, 1))
+        args += [A(pixel_values), A(counts), A(sums)]
+        stats = dict(stat_mask=mask, stat_weights=weights, stat_counts=counts[0],
+                     stat_sums=sums[0])
+    else:
+        kernel = warp_render._make_kernel(cull, channels)
+    ws.launch(kernel, 256 * T, args, block=256)
     t1 = time.time()
     up = gen.standard_normal(channels * H * W).astype(np.float32)
     g_tr = np.zeros(n * 16, np.float32)
@@ -661,7 +678,7 @@ def aaa_render_case(name, scene: dict, channels: int, cull: bool, seed: int) -> 
                 contributors=contrib.reshape(H, W), upstream=up.reshape(channels, H, W),
                 grad_transforms=g_tr.reshape(n, 16), grad_opacity=g_op,
                 grad_features=g_col.reshape(n, channels), grad_screen=g_scr.reshape(n, 2),
-                grad_screen_abs=g_abs.reshape(n, 2))
+                grad_screen_abs=g_abs.reshape(n, 2), **stats)
 
 
 def aaa_render_scenes():
@@ -683,8 +700,8 @@ def aaa_render_scenes():
                  viewmat=look_at(torch.tensor([0.2, -0.1, -1.0]),
                                  torch.tensor([0.0, 0.0, 4.0])).numpy(),
                  K=intrinsics(40.0, 38.0, 21.5, 17.5).numpy())
-    return [("sparse_c4", base, 4, True, 11), ("dense_c7", dense, 7, True, 12),
-            ("dense_nocull_c4", dense, 4, False, 13)]
+    return [("sparse_c4", base, 4, True, 11, False), ("dense_c7", dense, 7, True, 12, True),
+            ("dense_nocull_c4", dense, 4, False, 13, False)]
 
 
 def tile_mode_case(ref, name, scene: dict) -> dict:
@@ -845,8 +862,8 @@ def main():
             data = aaa_case(name, scene, flags, use_sh, with_filter)
             np.savez_compressed(os.path.join(HERE, f"aaa_{name}.npz"), **data)
     if not only or "--aaa-render-only" in only:
-        for name, scene, channels, cull, seed in aaa_render_scenes():
-            data = aaa_render_case(name, scene, channels, cull, seed)
+        for name, scene, channels, cull, seed, statistics in aaa_render_scenes():
+            data = aaa_render_case(name, scene, channels, cull, seed, statistics)
             np.savez_compressed(os.path.join(HERE, f"aaa_render_{name}.npz"), **data)
     if only and "--tile-modes-only" not in only:
         return

@@ -248,6 +248,27 @@ def test_hier_blend_matches_reference_kernel(render_golden):
         np.testing.assert_array_equal(image.cpu().numpy(), g["image"])
 
 
+def test_hier_statistics_match_reference_kernel(render_golden):
+    """The statistics variant of the blend (render_statistics): the image is
+    unchanged, the masked count bit for bit, the weighted sum within 1e-5
+    relative L2 (float32 atomics in a different order)."""
+    from dsl_splat_b200.statistics import PreparedStatistics
+    g = render_golden
+    if "stat_counts" not in g:
+        pytest.skip("this golden has no statistics requests")
+    W, H = int(g["width"]), int(g["height"])
+    st, bins = _render_inputs(g)
+    n = len(g["opacity"])
+    maps = _t(np.stack([g["stat_mask"].ravel(), g["stat_weights"].ravel()]))
+    stats = PreparedStatistics((0, 1), maps, torch.zeros((1, n), device=_dev(), dtype=torch.int32),
+                               torch.zeros((1, n), device=_dev()))
+    image, _, _, _ = S.render(st, bins, _t(g["features"]), _t(g["background"]), W, H,
+                              bool(g["cull"]), statistics=stats)
+    np.testing.assert_array_equal(image.cpu().numpy(), g["image"])
+    np.testing.assert_array_equal(stats.counts[0].cpu().numpy(), g["stat_counts"])
+    assert rel_l2(stats.sums[0].cpu(), g["stat_sums"]) <= 1e-5
+
+
 def test_hier_replay_matches_reference_kernel(render_golden):
     g = render_golden
     W, H = int(g["width"]), int(g["height"])
@@ -506,3 +527,47 @@ def test_recorded_backward_dense_tile_takes_the_per_sample_path():
     for a, b, c in zip(got, want, again):
         assert rel_l2(a.cpu(), b.cpu()) <= 1e-4
         assert torch.equal(b, c) or rel_l2(c.cpu(), b.cpu()) <= 1e-5
+
+
+def test_rasterize_statistics_against_oracle():
+    """aaa.rasterize with a masked count and a weighted sum over two cameras
+    (statistics.py's requests, owned (C, N) outputs) against the oracle's
+    observer on each view: counts bit for bit, sums within 1e-5."""
+    from dsl_splat_b200.scenes import make_scene
+    from dsl_splat_b200.statistics import MaskedContributionCount, WeightedContributionSum
+    dev = _dev()
+    sc = make_scene(1, n=6000, width=160, height=96)
+    gen = torch.Generator().manual_seed(41)
+    colors = torch.rand(sc.means.shape[0], 3, generator=gen)
+    H, W = sc.height, sc.width
+    mask = torch.rand(H, W, generator=gen) > 0.5
+    weights = torch.rand(2, H, W, generator=gen)
+    vms = torch.cat([sc.viewmats[:1], sc.viewmats[:1].clone()])  # (2, 4, 4)
+    vms[1, 0, 3] += 0.05
+    Ks = torch.cat([sc.Ks[:1], sc.Ks[:1]])
+    args = [getattr(sc, k).to(dev) for k in ("means", "quats", "scales", "opacities")]
+    res = aaa.rasterize(*args, vms.to(dev), Ks.to(dev), W, H, features=colors.to(dev),
+                        statistics=(MaskedContributionCount("hits", mask.to(dev)),
+                                    WeightedContributionSum("weight", weights.to(dev))))
+    assert set(res.statistics) == {"hits", "weight"}
+    assert res.statistics["hits"].shape == (2, len(colors))
+    qn = F.normalize(sc.quats.to(dev), dim=-1).cpu().numpy()  # CUDA F.normalize bits
+    cams = aaa.cameras.prepare_cameras(vms.to(dev)[None], Ks.to(dev)[None], W, H, 0.01, 1e10)
+    features = np.concatenate([colors.numpy(), np.ones((len(colors), 1))], 1).astype(np.float32)
+    for c in range(2):
+        view = cams.view(0, c)
+        vargs = (view.viewmatrix.cpu().numpy(), view.projmatrix.cpu().numpy(),
+                 view.campos.cpu().numpy())
+        pre = O.aaa_preprocess(sc.means.numpy(), qn, sc.scales.numpy(), sc.opacities.numpy(),
+                               *vargs, W, H, (view.tanfovx, view.tanfovy), view.principal)
+        final = O.aaa_cull_remainder(pre, W, H)
+        _, keys, values = O.aaa_duplicate(pre, final["radii"], final["tiles"], W, H)
+        T = ((W + 15) // 16) * ((H + 15) // 16)
+        _, ids, ranges = O.aaa_sort(keys, values, T)
+        maps = np.stack([mask.numpy().astype(np.float32), weights[c].numpy()])
+        _, _, _, counts, sums = O.aaa_render(W, H, ranges, ids, pre["transforms"],
+                                             pre["opacity"], features, np.zeros(4, np.float32),
+                                             stat_maps=maps, stat_kinds=(0, 1))
+        np.testing.assert_array_equal(res.statistics["hits"][c].cpu().numpy(), counts[0])
+        assert counts[0].any()
+        assert rel_l2(res.statistics["weight"][c].cpu(), sums[0]) <= 1e-5
