@@ -388,8 +388,15 @@ def scan_counts(counts: Tensor) -> tuple[Tensor, int]:
 _PAIR_CAPACITY: dict[tuple, int] = {}
 
 
+# the emission's pair limit (splat_bin_emit returns kTooLarge at 2^30 pairs)
+_MAX_PAIR_CAPACITY = (1 << 30) - 1
+
+
 def _capacity_for(pairs: int) -> int:
-    return pairs + pairs // 8 + 4096
+    """The early emission's id capacity for the next call: the last count
+    plus 12.5 %, clamped to the emission limit (a count above it is emitted
+    again exactly after the host read)."""
+    return min(pairs + pairs // 8 + 4096, _MAX_PAIR_CAPACITY)
 
 
 class BinPlan:

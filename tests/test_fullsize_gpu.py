@@ -6,6 +6,10 @@ The CUDA path against the CPU oracle on the benchmark scenes themselves:
   workload): every stage, then gs3d.rasterize end to end;
 * config 2 -- 3M Gaussians, SH3, 1296x840: one full view stage by stage,
   then the sum over three of its eight orbit views through gs3d.rasterize;
+* config 3 -- AAA-Gaussians, 2M Gaussians, SH3, 1920x1080, absgrad:
+  aaa.rasterize forward and backward against the oracle's composition
+  (SH colours, preprocessing, remainder cull, emission and sort, HIER blend,
+  replay, both adjoints, SH backward);
 * config 4 -- RaDe-GS, 1M Gaussians, SH3 + 32 extra channels, 1600x1200:
   projection, bins, blend and blend backward, and the projection VJP on a
   fixed band of Gaussian rows against the float64 autograd oracle.
@@ -183,3 +187,61 @@ def test_config4_full_view():
     for got, want_g, name in zip(grads[:4], ref_g[:4], ("means", "quats", "scales", "opacities")):
         g_band = got.cpu().numpy()[band]
         assert rel_l2(g_band[bvis], np.asarray(want_g)[bvis]) <= GRAD_TOL, name
+
+
+def test_config3_full_aaa():
+    import torch.nn.functional as F
+
+    from dsl_splat_b200 import aaa
+    dev = _dev()
+    sc = make_scene(3)
+    W, H = sc.width, sc.height
+    leaves = {k: getattr(sc, k).to(dev).requires_grad_(True)
+              for k in ("means", "quats", "scales", "opacities", "sh_coeffs")}
+    res = aaa.rasterize(leaves["means"], leaves["quats"], leaves["scales"], leaves["opacities"],
+                        sc.viewmats.to(dev), sc.Ks.to(dev), W, H,
+                        sh_coeffs=leaves["sh_coeffs"], absgrad=True)
+    torch.autograd.backward([res.features, res.alpha],
+                            [sc.grad_image.to(dev), sc.grad_alpha.to(dev)])
+    # the oracle's composition of the same view
+    view = aaa.cameras.prepare_cameras(sc.viewmats[None].to(dev), sc.Ks[None].to(dev), W, H,
+                                       0.01, 1e10).view(0, 0)
+    vargs = (view.viewmatrix.cpu().numpy(), view.projmatrix.cpu().numpy(),
+             view.campos.cpu().numpy())
+    tanfov = (view.tanfovx, view.tanfovy)
+    means, scales, opac = sc.means.numpy(), sc.scales.numpy(), sc.opacities.numpy()
+    qn = F.normalize(sc.quats.to(dev), dim=-1).cpu().numpy()  # CUDA F.normalize bits
+    pre = O.aaa_preprocess(means, qn, scales, opac, *vargs, W, H, tanfov, view.principal)
+    final = O.aaa_cull_remainder(pre, W, H)
+    radii = final["radii"]
+    np.testing.assert_array_equal((res.radii[0] > 0).any(-1).cpu().numpy(), radii > 0)
+    np.testing.assert_array_equal(res.meta["tiles_per_gauss"][0].cpu().numpy(), final["tiles"])
+    dirs = means - vargs[2]
+    colors, active = O.sh_forward(sc.sh_coeffs.numpy(), dirs, 3)  # aaa/api.py: before culling
+    feats = np.concatenate([colors, np.ones((len(means), 1), np.float32)], 1)
+    _, keys, values = O.aaa_duplicate(pre, radii, final["tiles"], W, H)
+    T = ((W + 15) // 16) * ((H + 15) // 16)
+    _, ids, ranges = O.aaa_sort(keys, values, T)
+    bg = np.zeros(4, np.float32)
+    image, final_t, _ = O.aaa_render(W, H, ranges, ids, pre["transforms"], pre["opacity"],
+                                     feats, bg)
+    got = torch.cat([res.features, res.alpha], -1)[0].detach().cpu().numpy()
+    np.testing.assert_array_equal(np.moveaxis(got, -1, 0), image)
+    up = np.concatenate([sc.grad_image[0].numpy(), sc.grad_alpha[0].numpy()], -1)
+    g = O.aaa_render_backward(W, H, ranges, ids, pre["transforms"], pre["opacity"], feats, bg,
+                              image, final_t, np.moveaxis(up, -1, 0).copy(), screen=True,
+                              absgrad=True)
+    assert rel_l2(res.means2d.grad[0].cpu(), g["screen"]) <= GRAD_TOL
+    assert rel_l2(res.means2d.absgrad[0].cpu(), g["screen_abs"]) <= GRAD_TOL
+    up_t, up_o = g["transforms"].astype(np.float32), g["opacity"].astype(np.float32)
+    adj = O.aaa_preprocess_backward(means, qn, scales, opac, radii, *vargs, W, H,
+                                    np.float32(W / (2.0 * tanfov[0])), up_t, up_o)
+    g_sh, g_dirs = O.sh_backward(sc.sh_coeffs.numpy(), dirs, 3, None, active,
+                                 g["colors"][:, :3].astype(np.float32))
+    assert rel_l2(leaves["sh_coeffs"].grad.cpu(), g_sh) <= GRAD_TOL
+    assert rel_l2(leaves["means"].grad.cpu(), adj["means"] + g_dirs) <= GRAD_TOL
+    assert rel_l2(leaves["scales"].grad.cpu(), adj["scales"]) <= GRAD_TOL
+    assert rel_l2(leaves["opacities"].grad.cpu(), adj["opacity"]) <= GRAD_TOL
+    _, vjp = torch.func.vjp(lambda x: F.normalize(x, dim=-1), sc.quats.double())
+    gq = vjp(torch.from_numpy(adj["quats"].astype(np.float64)))[0].numpy()
+    assert rel_l2(leaves["quats"].grad.cpu(), gq) <= GRAD_TOL
