@@ -157,7 +157,12 @@ class ClockSampler:
                 ["nvidia-smi", f"--id={self.ident}", f"--query-gpu={self.QUERY}",
                  "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
-            time.sleep(0.3)  # let the first sample land inside the timed region
+            # the timed region starts once the sampler has written its first
+            # row (nvidia-smi can take longer to start than a short region)
+            deadline = time.time() + 5.0
+            while time.time() < deadline and os.path.getsize(self.file.name) == 0:
+                time.sleep(0.02)
+            self.start_rows = self._count_rows()
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
@@ -171,11 +176,21 @@ class ClockSampler:
                 self.proc.kill()
         return False
 
+    def _count_rows(self) -> int:
+        with open(self.file.name) as f:
+            return sum(1 for line in f if line.strip())
+
     def summary(self):
         self.file.flush()
         self.file.seek(0)
         rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
         os.unlink(self.file.name)
+        # the rows written during the timed region (the ones before it only
+        # showed that the sampler had started), unless the region was shorter
+        # than one sampling interval
+        start = getattr(self, "start_rows", 0)
+        if len(rows) > start:
+            rows = rows[start:]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
@@ -655,7 +670,11 @@ def main():
         line = {"metric": metric_for(args.config), "value": value, "unit": UNIT,
                 "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "higher_is_better": True,
+                # config 2 splits a fixed batch of cameras over the ranks; the
+                # single-view configs give every rank its own view
+                "scaling": "strong" if s.meta.get("cameras", 1) > 1 else "weak",
+                "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded, BASELINE config distributions)",
                 "config": dict(describe(s, world), **(
                     {"gradient_allreduce": (
