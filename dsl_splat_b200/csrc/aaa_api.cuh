@@ -41,10 +41,18 @@ struct AaaBinLayout {
 
 size_t round256(size_t v) { return (v + 255) & ~static_cast<size_t>(255); }
 
+// the pair sort's onesweep shape (threads per block, keys per thread): at
+// config 3's 10.4M pairs 8 keys per thread measured 696 us for the five
+// passes against 795 us with 16 (512 threads: 714 / 963 us with 8 / 16).
+// A per-tile shared-memory sort by depth key after two tile passes measured
+// slower (730 us: the tiles' random gathers and ranking rounds).
+constexpr int kAaaSortThreads = 256, kAaaSortItems = 8;
+constexpr int kAaaSortTile = kAaaSortThreads * kAaaSortItems;
+
 AaaBinLayout aaa_bin_layout(long long pairs) {
   AaaBinLayout L{};
   const size_t m = static_cast<size_t>(pairs > 0 ? pairs : 1);
-  L.sort_tiles = blocks_for(static_cast<long long>(m), kSortTile);
+  L.sort_tiles = blocks_for(static_cast<long long>(m), kAaaSortTile);
   size_t at = 0;
   auto take = [&](size_t bytes) {
     const size_t here = at;
@@ -304,19 +312,24 @@ int splat_aaa_bin(int n, long long pairs, const int* offsets, const float* cente
   auto offs = [&](int pass) { return u32(L.offs) + pass * kRadix; };
   uint32_t *keys_a = u32(L.keys_a), *vals_a = u32(L.vals_a), *keys_b = u32(L.keys_b),
            *vals_b = u32(L.vals_b);
-  onesweep_kernel<splat::aaa::DepthKeyLoader, true><<<blocks, kSortBlock, 0, counted(s)>>>(
+  onesweep_kernel<splat::aaa::DepthKeyLoader, true, kAaaSortThreads, kAaaSortItems>
+      <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
       splat::aaa::DepthKeyLoader{depth_in}, m, 0, offs(0), status(0), counter(0), keys_a, vals_a);
-  onesweep_kernel<KeyValueLoader, true><<<blocks, kSortBlock, 0, counted(s)>>>(
+  onesweep_kernel<KeyValueLoader, true, kAaaSortThreads, kAaaSortItems>
+      <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
       KeyValueLoader{keys_a, vals_a}, m, 8, offs(1), status(1), counter(1), keys_b, vals_b);
-  onesweep_kernel<KeyValueLoader, false><<<blocks, kSortBlock, 0, counted(s)>>>(
+  onesweep_kernel<KeyValueLoader, false, kAaaSortThreads, kAaaSortItems>
+      <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
       KeyValueLoader{keys_b, vals_b}, m, 16, offs(2), status(2), counter(2), keys_a, vals_a);
-  onesweep_kernel<splat::aaa::TileGatherLoader, true><<<blocks, kSortBlock, 0, counted(s)>>>(
+  onesweep_kernel<splat::aaa::TileGatherLoader, true, kAaaSortThreads, kAaaSortItems>
+      <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
       splat::aaa::TileGatherLoader{tiles_in, vals_a}, m, 0, offs(3), status(3), counter(3), keys_b,
       vals_b);
   const uint32_t* sorted_tiles = keys_b;
   const uint32_t* sorted_pairs = vals_b;
   if (tile_passes > 1) {
-    onesweep_kernel<KeyValueLoader, true><<<blocks, kSortBlock, 0, counted(s)>>>(
+    onesweep_kernel<KeyValueLoader, true, kAaaSortThreads, kAaaSortItems>
+      <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
         KeyValueLoader{keys_b, vals_b}, m, 8, offs(4), status(4), counter(4), keys_a, vals_a);
     sorted_tiles = keys_a;
     sorted_pairs = vals_a;
