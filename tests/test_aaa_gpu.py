@@ -571,3 +571,34 @@ def test_rasterize_statistics_against_oracle():
         np.testing.assert_array_equal(res.statistics["hits"][c].cpu().numpy(), counts[0])
         assert counts[0].any()
         assert rel_l2(res.statistics["weight"][c].cpu(), sums[0]) <= 1e-5
+
+
+@pytest.mark.parametrize("channels", [2, 9, 33])
+def test_recorded_backward_wide_features(channels):
+    """The record backward's per-channel paths (fewer than four channels,
+    and 16- / 64-channel instantiations): gradients equal the replay's on a
+    dense view."""
+    from dsl_splat_b200.scenes import make_scene
+    dev = _dev()
+    sc = make_scene(1, n=12000, width=192, height=128)
+    cams = aaa.cameras.prepare_cameras(sc.viewmats[None].to(dev), sc.Ks[None].to(dev),
+                                       sc.width, sc.height, 0.01, 1e10)
+    q = F.normalize(sc.quats.to(dev), dim=-1)
+    st = S.preprocess(cams.view(0, 0), aaa.default_settings(), sc.means.to(dev), q,
+                      sc.scales.to(dev), sc.opacities.to(dev))
+    bins, _ = S.bin_and_sort_many([st], sc.width, sc.height)
+    gen = torch.Generator().manual_seed(channels)
+    feats = torch.rand(len(q), channels, generator=gen).to(dev)
+    bg = torch.rand(channels, generator=gen).to(dev)
+    W, H = sc.width, sc.height
+    image, final_t, _, rec = S.render(st, bins[0], feats, bg, W, H, True, record_capacity=192)
+    plain, plain_t, _, _ = S.render(st, bins[0], feats, bg, W, H, True)
+    assert torch.equal(image, plain) and torch.equal(final_t, plain_t)
+    assert int(rec["overflow"].sum()) < len(rec["overflow"])
+    up = torch.randn(channels, H, W, generator=gen).to(dev)
+    args = (st, bins[0], feats, bg, image, final_t, up, W, H, True)
+    got = S.render_backward(*args, screen=True, absgrad=True, records=rec)
+    want = S.render_backward(*args, screen=True, absgrad=True)
+    for a, b in zip(got, want):
+        assert b.abs().sum() > 0
+        assert rel_l2(a.cpu(), b.cpu()) <= 1e-4
