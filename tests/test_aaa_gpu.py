@@ -602,3 +602,51 @@ def test_recorded_backward_wide_features(channels):
     for a, b in zip(got, want):
         assert b.abs().sum() > 0
         assert rel_l2(a.cpu(), b.cpu()) <= 1e-4
+
+
+def test_stage_ops_compose_like_rasterize():
+    """aaa.ops (aaa/ops.py:320-464): prepare_gaussians -> bin_and_sort ->
+    rasterize_to_pixels gives aaa.rasterize's images and statistics bit for
+    bit and its gradients (Gaussians, features, pose) within 1e-4."""
+    from dsl_splat_b200.cameras import PinholeCamera
+    from dsl_splat_b200.scenes import make_scene
+    from dsl_splat_b200.statistics import MaskedContributionCount
+    dev = _dev()
+    sc = make_scene(1, n=8000, width=256, height=160)
+    W, H = sc.width, sc.height
+    gen = torch.Generator().manual_seed(53)
+    colors = torch.rand(len(sc.means), 3, generator=gen).to(dev)
+    bg = torch.tensor([0.1, 0.5, 0.9], device=dev)
+    mask = (torch.rand(H, W, generator=gen) > 0.3).to(dev)
+    gF = torch.randn(H, W, 3, generator=gen).to(dev)
+    gA = torch.randn(H, W, 1, generator=gen).to(dev)
+
+    def leaves():
+        out = {k: getattr(sc, k).to(dev).requires_grad_(True)
+               for k in ("means", "quats", "scales", "opacities")}
+        out["features"] = colors.clone().requires_grad_(True)
+        out["viewmat"] = sc.viewmats[0].to(dev).requires_grad_(True)
+        return out
+
+    a = leaves()
+    camera = PinholeCamera(a["viewmat"], sc.Ks[0].to(dev), W, H)
+    geo = aaa.ops.prepare_gaussians(a["means"], a["quats"], a["scales"], a["opacities"], camera)
+    tiles = aaa.ops.bin_and_sort(geo)
+    px = aaa.ops.rasterize_to_pixels(geo, tiles, a["features"], bg,
+                                     statistics=(MaskedContributionCount("hits", mask),))
+    ((px.features * gF).sum() + (px.alpha * gA).sum()).backward()
+
+    b = leaves()
+    res = aaa.rasterize(b["means"], b["quats"], b["scales"], b["opacities"], b["viewmat"][None],
+                        sc.Ks[:1].to(dev), W, H, features=b["features"], backgrounds=bg[None],
+                        statistics=(MaskedContributionCount("hits", mask),))
+    ((res.features[0] * gF).sum() + (res.alpha[0] * gA).sum()).backward()
+    assert torch.equal(px.features, res.features[0]) and torch.equal(px.alpha, res.alpha[0])
+    assert torch.equal(px.statistics["hits"], res.statistics["hits"][0])
+    np.testing.assert_array_equal(geo.radii.cpu().numpy() > 0,
+                                  (res.radii[0] > 0).any(-1).cpu().numpy())
+    for name in ("means", "quats", "scales", "opacities", "features", "viewmat"):
+        assert a[name].grad is not None and a[name].grad.abs().sum() > 0, name
+        assert rel_l2(a[name].grad.cpu(), b[name].grad.cpu()) <= 1e-4, name
+    with pytest.raises(ValueError):
+        aaa.ops.rasterize_to_pixels(geo, aaa.ops.bin_and_sort(geo), a["features"][:, :2][:-1])
