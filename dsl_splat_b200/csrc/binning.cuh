@@ -108,6 +108,44 @@ SPLAT_DEV typename S::Word lookback(const typename S::Word* status, int64_t tile
   return excl;
 }
 
+// The same walk by a whole warp (all 32 lanes call; every lane returns the
+// prefix): lane l reads the status of tile t - l, so one round covers 32
+// predecessors, nearest first up to the first inclusive or unpublished one.
+// Positions before tile 0 read as inclusive zero.
+template <class S>
+SPLAT_DEV typename S::Word warp_lookback(const typename S::Word* status, int64_t tile,
+                                         size_t stride, uint32_t spin_limit = kSpinLimit) {
+  using Word = typename S::Word;
+  const int lane = threadIdx.x & 31;
+  Word excl = 0;
+  uint32_t spins = 0;
+  int64_t t = tile - 1;
+  while (t >= 0) {
+    const int64_t mine = t - lane;
+    const Word w = mine >= 0 ? S::load(status + mine * stride) : S::kInclusive;
+    const Word flag = w & ~S::kMask;
+    const uint32_t incl = __ballot_sync(0xffffffffu, flag == S::kInclusive);
+    const uint32_t stop_mask = incl | __ballot_sync(0xffffffffu, flag == 0);
+    const int stop = stop_mask ? __ffs(stop_mask) - 1 : 32;
+    const bool done = stop < 32 && ((incl >> stop) & 1u);
+    const int consumed = done ? stop + 1 : stop;  // lanes summed this round
+    Word v = lane < consumed ? (w & S::kMask) : Word(0);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    excl += v;
+    if (done) break;
+    if (stop < 32) {
+      if (++spins > spin_limit) {
+        if (lane == 0) record_device_error(kDeviceTimeout);
+        break;
+      }
+      __nanosleep(32);
+    }
+    t -= consumed;
+  }
+  return excl;
+}
+
 // One thread walks the look-back of tile 1 over `status` (two words the
 // caller zeroed, i.e. never published) with a short spin limit: the wait
 // runs out, kDeviceTimeout is recorded and the thread returns.  This is how
@@ -330,8 +368,18 @@ __global__ void __launch_bounds__(THREADS)
   constexpr int kWarps = THREADS / 32;
   constexpr uint32_t kTile = static_cast<uint32_t>(THREADS) * ITEMS;
   static_assert(THREADS >= kRadix && THREADS % 32 == 0, "one thread per digit");
+  // Staged output: the tile's keys and values are first placed in digit
+  // order in shared memory, then written out by consecutive threads, so a
+  // digit's run in the output is written with contiguous stores (direct
+  // stores put every lane of a warp in a different 32-byte sector).  Taken
+  // when the two staging arrays fit beside the loader's shared state.
+  constexpr bool kStage = 8 * kTile + sizeof(typename Loader::Shared) <= 40 * 1024;
+  constexpr uint32_t kStaged = kStage ? kTile : 1u;
   __shared__ uint32_t s_hist[kWarps][kRadix];
   __shared__ uint32_t s_base[kRadix];
+  __shared__ uint32_t s_start[kStage ? kRadix : 1];
+  __shared__ uint32_t s_key[kStaged], s_val[kStaged];
+  __shared__ uint32_t s_warp[32];
   __shared__ uint32_t s_tile;
   __shared__ typename Loader::Shared s_ld;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -345,12 +393,20 @@ __global__ void __launch_bounds__(THREADS)
 
   uint32_t keys[ITEMS], vals[ITEMS], rank[ITEMS];
   const uint32_t lt = lanemask_lt();
+  // every load of the thread is issued before the ranking (whose warp
+  // barriers would otherwise wait out one load latency per item)
+#pragma unroll
+  for (int r = 0; r < ITEMS; ++r) {
+    const uint32_t idx = base + warp * (32 * ITEMS) + r * 32 + lane;
+    keys[r] = 0u;
+    vals[r] = 0u;
+    if (idx < end) ld.load(idx, s_ld, keys[r], vals[r]);
+  }
 #pragma unroll
   for (int r = 0; r < ITEMS; ++r) {
     const uint32_t idx = base + warp * (32 * ITEMS) + r * 32 + lane;
     const bool valid = idx < end;
-    uint32_t key = 0u, val = 0u;
-    if (valid) ld.load(idx, s_ld, key, val);
+    const uint32_t key = keys[r];
     const uint32_t d = valid ? ((key >> shift) & 255u) : 256u;
     const uint32_t peers = __match_any_sync(0xffffffffu, d);
     uint32_t before = 0u;
@@ -358,45 +414,80 @@ __global__ void __launch_bounds__(THREADS)
     __syncwarp();
     if (valid && (peers & lt) == 0u) s_hist[warp][d] = before + __popc(peers);
     __syncwarp();
-    keys[r] = key;
-    vals[r] = val;
     rank[r] = valid ? before + __popc(peers & lt) : 0xFFFFFFFFu;
   }
   __syncthreads();
 
+  // per digit: the warps' exclusive offsets, the tile's count, published
+  // as this tile's aggregate (tile 0: inclusive) before anything else
+  uint32_t total = 0u;
+  uint32_t* mine = status + static_cast<size_t>(tile) * kRadix + threadIdx.x;
   if (threadIdx.x < kRadix) {
     const int d = threadIdx.x;
-    uint32_t total = 0u;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) {
       const uint32_t c = s_hist[w][d];
       s_hist[w][d] = total;
       total += c;
     }
+    st_relaxed(mine, (tile == 0 ? kFlagInclusive : kFlagAggregate) | total);
+  }
+  if constexpr (kStage) {
+    // digit-ordered positions inside the tile, filled while predecessors
+    // publish
+    const uint32_t start = block_exclusive_scan(threadIdx.x < kRadix ? total : 0u, s_warp, nullptr);
+    if (threadIdx.x < kRadix) s_start[threadIdx.x] = start;
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+      if (rank[r] == 0xFFFFFFFFu) continue;
+      const uint32_t d = (keys[r] >> shift) & 255u;
+      const uint32_t local = s_start[d] + s_hist[warp][d] + rank[r];
+      s_key[local] = keys[r];
+      s_val[local] = vals[r];
+    }
+  }
+  if (threadIdx.x < kRadix) {
+    const int d = threadIdx.x;
     uint32_t excl = 0u;
-    uint32_t* mine = status + static_cast<size_t>(tile) * kRadix + d;
-    if (tile == 0) {
-      st_relaxed(mine, kFlagInclusive | total);
-    } else {
-      st_relaxed(mine, kFlagAggregate | total);
+    if (tile != 0) {
       excl = lookback<Status32, 8>(status + d, static_cast<int64_t>(tile), kRadix);
       st_relaxed(mine, kFlagInclusive | (excl + total));
     }
-    s_base[d] = digit_offsets[d] + excl;
+    // output position of the digit's first key, less its tile-local start
+    // when staged
+    s_base[d] = digit_offsets[d] + excl - (kStage ? s_start[d] : 0u);
   }
   __syncthreads();
 
+  if constexpr (kStage) {
+    const uint32_t count = end > base ? end - base : 0u;
 #pragma unroll
-  for (int r = 0; r < ITEMS; ++r) {
-    if (rank[r] == 0xFFFFFFFFu) continue;
-    const uint32_t d = (keys[r] >> shift) & 255u;
-    const uint32_t pos = s_base[d] + s_hist[warp][d] + rank[r];
-    if (pos >= n) {  // only reachable with inconsistent histograms
-      record_device_error(kInconsistentInput);
-      continue;
+    for (int r = 0; r < ITEMS; ++r) {
+      const uint32_t i = r * THREADS + threadIdx.x;
+      if (i >= count) break;
+      const uint32_t key = s_key[i];
+      const uint32_t pos = s_base[(key >> shift) & 255u] + i;
+      if (pos >= n) {  // only reachable with inconsistent histograms
+        record_device_error(kInconsistentInput);
+        continue;
+      }
+      if (WRITE_KEYS) keys_out[pos] = key;
+      vals_out[pos] = s_val[i];
     }
-    if (WRITE_KEYS) keys_out[pos] = keys[r];
-    vals_out[pos] = vals[r];
+  } else {
+#pragma unroll
+    for (int r = 0; r < ITEMS; ++r) {
+      if (rank[r] == 0xFFFFFFFFu) continue;
+      const uint32_t d = (keys[r] >> shift) & 255u;
+      const uint32_t pos = s_base[d] + s_hist[warp][d] + rank[r];
+      if (pos >= n) {  // only reachable with inconsistent histograms
+        record_device_error(kInconsistentInput);
+        continue;
+      }
+      if (WRITE_KEYS) keys_out[pos] = keys[r];
+      vals_out[pos] = vals[r];
+    }
   }
 }
 
@@ -589,17 +680,17 @@ __global__ void __launch_bounds__(kSortBlock)
   }
   uint32_t tile_total;
   uint32_t run = block_exclusive_scan(sum, s_warp, &tile_total);
-  if (threadIdx.x == 0) {
+  if (threadIdx.x < 32) {
     unsigned long long* mine = status + tile;
     unsigned long long excl = 0ull;
     if (tile == 0) {
-      st_relaxed64(mine, Status64::kInclusive | tile_total);
+      if (threadIdx.x == 0) st_relaxed64(mine, Status64::kInclusive | tile_total);
     } else {
-      st_relaxed64(mine, Status64::kAggregate | tile_total);
-      excl = lookback<Status64, 16>(status, static_cast<int64_t>(tile), 1);
-      st_relaxed64(mine, Status64::kInclusive | (excl + tile_total));
+      if (threadIdx.x == 0) st_relaxed64(mine, Status64::kAggregate | tile_total);
+      excl = warp_lookback<Status64>(status, static_cast<int64_t>(tile), 1);
+      if (threadIdx.x == 0) st_relaxed64(mine, Status64::kInclusive | (excl + tile_total));
     }
-    s_excl = static_cast<uint32_t>(excl);
+    if (threadIdx.x == 0) s_excl = static_cast<uint32_t>(excl);
   }
   __syncthreads();
   run += s_excl;
@@ -687,13 +778,12 @@ __global__ void __launch_bounds__(256)
 // (tiles + kChunkGaussianCost per Gaussian, from a prefix scan in depth
 // order).  cnt[k][t] = pairs of chunk k in tile t; an exclusive prefix over
 // k plus the tile's range start gives every chunk its first write position
-// per tile, so all chunks scatter independently.  Inside a chunk, waves of
-// 32 Gaussians are placed in order: a Gaussian's rank within tile t is the
-// number of earlier wave members whose rectangle covers t, read from
-// per-column and per-row 64-bit coverage masks (waves of 64 Gaussians).  The result is the depth
-// order within every tile, i.e. the reference's stable sort of 64-bit keys.
+// per tile, so all chunks scatter independently.  Inside a chunk the
+// Gaussians are placed in depth order (tile_scatter_kernel).  The result is
+// the depth order within every tile, i.e. the reference's stable sort of
+// 64-bit keys.
 
-constexpr uint32_t kChunkGaussianCost = 8;  // per-Gaussian wave overhead, in pairs
+constexpr uint32_t kChunkGaussianCost = 8;  // per-Gaussian scatter overhead, in pairs
 
 SPLAT_DEV void unpack_rect(uint2 r, uint32_t& x0, uint32_t& y0, uint32_t& x1, uint32_t& y1) {
   x0 = r.x & 0xFFFFu;
@@ -839,223 +929,107 @@ __global__ void __launch_bounds__(1024)
   if (threadIdx.x == 0) *total = s_carry;
 }
 
-// Wave metadata (double-buffered): member ids, rectangles, exclusive pair
-// prefix (pref[kWave] = pairs of the wave) and 1/width.
-constexpr int kWave = 64;
+// Scatter of chunk k = blockIdx.x: 8 warps, warp w places the chunk's pairs
+// in tile rows y with y % 8 == w (interleaved rows keep the warps' loads
+// even), so no two warps touch one tile.  Dynamic shared memory: next[T],
+// the next write position of every tile.  A warp walks the chunk's members
+// 32 at a time in depth order; the pairs of those members in its rows
+// (row-major inside each member's rectangle) are laid out over the lanes by
+// a warp prefix scan, 32 per step.  Pairs of one step that share a tile
+// come from distinct members in lane (= depth) order: each takes next[t]
+// plus the number of lower peer lanes, and the highest peer advances
+// next[t] by the peer count.
+constexpr int kScatterWarps = 8;
 
-struct ScatterWave {
-  uint32_t g[kWave];
-  uint2 rect[kWave];
-  uint32_t pref[kWave + 1];
-  uint32_t lines[kWave + 1];  // exclusive prefix of width + height (mask tasks)
-  float inv_w[kWave];
-};
-
-SPLAT_DEV float inverse_width(uint2 r) {
-  const uint32_t width = (r.y & 0xFFFFu) - (r.x & 0xFFFFu);
-  return rect_area(r) ? 1.0f / static_cast<float>(width) : 0.0f;
-}
-
-// Warp 0 publishes a wave's metadata; lane l holds members l and 32 + l.
-SPLAT_DEV uint32_t rect_lines(uint2 r) {
-  uint32_t x0, y0, x1, y1;
-  unpack_rect(r, x0, y0, x1, y1);
-  return (x1 > x0 && y1 > y0) ? (x1 - x0) + (y1 - y0) : 0u;
-}
-
-SPLAT_DEV void publish_wave(ScatterWave& w, int lane, uint32_t g0, uint2 r0, uint32_t g1,
-                            uint2 r1) {
-  uint32_t a = rect_area(r0), b = rect_area(r1);
-  uint32_t la = rect_lines(r0), lb = rect_lines(r1);
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t ya = __shfl_up_sync(0xffffffffu, a, o);
-    const uint32_t yb = __shfl_up_sync(0xffffffffu, b, o);
-    const uint32_t yla = __shfl_up_sync(0xffffffffu, la, o);
-    const uint32_t ylb = __shfl_up_sync(0xffffffffu, lb, o);
-    if (lane >= o) {
-      a += ya;
-      b += yb;
-      la += yla;
-      lb += ylb;
-    }
-  }
-  b += __shfl_sync(0xffffffffu, a, 31);
-  lb += __shfl_sync(0xffffffffu, la, 31);
-  w.g[lane] = g0;
-  w.g[32 + lane] = g1;
-  w.rect[lane] = r0;
-  w.rect[32 + lane] = r1;
-  w.pref[lane + 1] = a;
-  w.pref[33 + lane] = b;
-  w.lines[lane + 1] = la;
-  w.lines[33 + lane] = lb;
-  if (lane == 0) {
-    w.pref[0] = 0u;
-    w.lines[0] = 0u;
-  }
-  w.inv_w[lane] = inverse_width(r0);
-  w.inv_w[32 + lane] = inverse_width(r1);
-}
-
-// Pair p of a wave: its member (largest j with pref[j] <= p), the tile it
-// covers (row-major order inside the member's rectangle) and the coverage
-// mask of that tile.
-struct WavePair {
-  int member;
-  uint32_t tile;
-  unsigned long long cover;
-};
-
-SPLAT_DEV WavePair wave_pair(const ScatterWave& w, uint32_t p, int gx,
-                             const unsigned long long* col, const unsigned long long* rowm) {
-  int j = 0;
-#pragma unroll
-  for (int step = kWave / 2; step > 0; step >>= 1)
-    if (w.pref[j + step] <= p) j += step;
-  uint32_t x0, y0, x1, y1;
-  unpack_rect(w.rect[j], x0, y0, x1, y1);
-  const uint32_t width = x1 - x0, local = p - w.pref[j];
-  // local < 2^24: the float quotient is within one of the integer one
-  uint32_t q = static_cast<uint32_t>(static_cast<float>(local) * w.inv_w[j]);
-  if (q * width > local)
-    --q;
-  else if ((q + 1) * width <= local)
-    ++q;
-  const uint32_t tx = x0 + (local - q * width), ty = y0 + q;
-  WavePair r;
-  r.member = j;
-  r.tile = ty * static_cast<uint32_t>(gx) + tx;
-  r.cover = col[tx] & rowm[ty];
-  return r;
-}
-
-SPLAT_DEV unsigned long long members_below(int j) { return (1ull << j) - 1ull; }
-
-// Scatter of chunk k = blockIdx.x (256 threads).  Dynamic shared memory:
-// next[T] write positions, then two buffers of gx column masks and gy row
-// masks (64-bit; the buffer of the next wave is cleared while this one is
-// read).
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32 * kScatterWarps)
     tile_scatter_kernel(const uint32_t* __restrict__ order, const uint32_t* __restrict__ bounds,
                         const uint2* __restrict__ sorted_rects, int gx, int gy,
                         const uint32_t* __restrict__ prefix, const uint32_t* __restrict__ starts,
                         uint32_t m, const uint32_t* __restrict__ pair_total,
                         uint32_t* __restrict__ ids) {
-  constexpr int kKept = 4;  // pairs per thread whose tile update stays in registers
   // ids holds m entries; m may be a capacity above or below the true pair
   // count: positions past m are skipped (the caller re-emits when m was too
   // small) and only positions past the true count are an error
   const uint32_t total = __ldg(pair_total);
-  extern __shared__ __align__(16) uint32_t s_dyn[];
-  __shared__ ScatterWave s_wave[2];
+  extern __shared__ __align__(16) uint32_t s_next[];  // [T]
   const int T = gx * gy;
-  const int mask_words = gx + gy;
-  unsigned long long* s_masks = reinterpret_cast<unsigned long long*>(s_dyn);  // [2][gx + gy]
-  uint32_t* s_next = s_dyn + 4 * mask_words;                                    // [T]
   const uint32_t* base = prefix + static_cast<size_t>(blockIdx.x) * T;
 #pragma unroll 4
   for (int t = threadIdx.x; t < T; t += blockDim.x) s_next[t] = starts[t] + base[t];
-  for (int c = threadIdx.x; c < 2 * mask_words; c += blockDim.x) s_masks[c] = 0ull;
+  __syncthreads();
   const uint32_t begin = bounds[blockIdx.x], end = bounds[blockIdx.x + 1];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // warp 0 loads members two waves ahead and publishes one wave ahead
-  uint32_t ahead_g0 = 0u, ahead_g1 = 0u;
-  uint2 ahead_r0 = make_uint2(0u, 0u), ahead_r1 = make_uint2(0u, 0u);
-  auto load = [&](uint32_t i, uint32_t& g, uint2& r) {
-    g = 0u;
-    r = make_uint2(0u, 0u);
-    if (i < end) {
-      g = order[i];
-      r = sorted_rects[i];
-    }
-  };
-  // coverage masks of wave w: task q is column or row (q - lines[j]) of
-  // member j; each sets bit j with a 32-bit atomic on the half of the 64-bit
-  // word that holds it
-  auto build_masks = [&](const ScatterWave& wave, unsigned long long* col) {
-    unsigned long long* rowm = col + gx;
-    for (uint32_t q = threadIdx.x; q < wave.lines[kWave]; q += blockDim.x) {
-      int j = 0;
-#pragma unroll
-      for (int step = kWave / 2; step > 0; step >>= 1)
-        if (wave.lines[j + step] <= q) j += step;
-      uint32_t x0, y0, x1, y1;
-      unpack_rect(wave.rect[j], x0, y0, x1, y1);
-      const uint32_t local = q - wave.lines[j];
-      unsigned long long* word = local < x1 - x0 ? col + x0 + local : rowm + y0 + (local - (x1 - x0));
-      atomicOr(reinterpret_cast<uint32_t*>(word) + (j >> 5), 1u << (j & 31));
-    }
-  };
-  if (warp == 0) {
-    uint32_t g0, g1;
-    uint2 r0, r1;
-    load(begin + lane, g0, r0);
-    load(begin + 32 + lane, g1, r1);
-    publish_wave(s_wave[0], lane, g0, r0, g1, r1);
-    load(begin + kWave + lane, ahead_g0, ahead_r0);
-    load(begin + kWave + 32 + lane, ahead_g1, ahead_r1);
+  const uint32_t lane = threadIdx.x & 31, band = threadIdx.x >> 5;
+  const uint32_t lt = lanemask_lt();
+  // member loads run one window ahead
+  uint32_t next_g = 0u;
+  uint2 next_r = make_uint2(0u, 0u);
+  if (begin + lane < end) {
+    next_g = __ldg(order + begin + lane);
+    next_r = __ldg(sorted_rects + begin + lane);
   }
-  __syncthreads();
-  build_masks(s_wave[0], s_masks);
-  __syncthreads();
-  // Two barriers per wave w (buffers by parity):
-  //   phase B: pairs of w (read wave[b], masks[b], next); clear masks[b^1]
-  //            and publish wave w+1 into wave[b^1] (both last read in
-  //            phase C of w-1)
-  //   phase C: advance next by w (read wave[b], masks[b]); build masks[b^1]
-  //            of wave w+1
-  int buf = 0;
-  for (uint32_t w0 = begin; w0 < end; w0 += kWave, buf ^= 1) {
-    const ScatterWave& wave = s_wave[buf];
-    unsigned long long* col = s_masks + buf * mask_words;
-    unsigned long long* rowm = col + gx;
-    const uint32_t P = wave.pref[kWave];
-    uint32_t kept_tile[kKept], kept_add[kKept];
+  for (uint32_t m0 = begin; m0 < end; m0 += 32) {
+    const uint32_t g = next_g;
+    const uint2 r = next_r;
+    const uint32_t ahead = m0 + 32 + lane;
+    next_g = 0u;
+    next_r = make_uint2(0u, 0u);
+    if (ahead < end) {
+      next_g = __ldg(order + ahead);
+      next_r = __ldg(sorted_rects + ahead);
+    }
+    // an empty rectangle (also the padding lanes past end) has no pairs
+    uint32_t x0, y0, x1, y1, width = 0u, count = 0u;
+    unpack_rect(r, x0, y0, x1, y1);
+    // first row of the band at or below y0, and the band's rows in [y0, y1)
+    const uint32_t fy = y0 + ((band - y0) & (kScatterWarps - 1));
+    if (x1 > x0 && fy < y1) {
+      width = x1 - x0;
+      count = ((y1 - 1u - fy) / kScatterWarps + 1u) * width;
+    }
+    uint32_t incl = count;
 #pragma unroll
-    for (int it = 0; it < kKept; ++it) {
-      kept_add[it] = 0u;
-      kept_tile[it] = 0u;
-      const uint32_t p = threadIdx.x + it * blockDim.x;
-      if (p < P) {
-        const WavePair q = wave_pair(wave, p, gx, col, rowm);
-        const unsigned long long below = q.cover & members_below(q.member);
-        const uint32_t pos = s_next[q.tile] + __popcll(below);
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= static_cast<uint32_t>(o)) incl += v;
+    }
+    const uint32_t P = __shfl_sync(0xffffffffu, incl, 31);
+    const uint32_t excl = incl - count;
+    const float inv_w = width ? 1.0f / static_cast<float>(width) : 0.0f;
+    for (uint32_t o = 0; o < P; o += 32) {
+      const uint32_t p = o + lane;
+      // member j: the number of lanes whose inclusive prefix is <= p
+      uint32_t j = 0u;
+#pragma unroll
+      for (uint32_t step = 16; step > 0; step >>= 1)
+        if (__shfl_sync(0xffffffffu, incl, j + step - 1u) <= p) j += step;
+      const uint32_t local = p - __shfl_sync(0xffffffffu, excl, j);
+      const uint32_t w = __shfl_sync(0xffffffffu, width, j);
+      const float inv = __shfl_sync(0xffffffffu, inv_w, j);
+      const uint32_t mx0 = __shfl_sync(0xffffffffu, x0, j);
+      const uint32_t mfy = __shfl_sync(0xffffffffu, fy, j);
+      const uint32_t mg = __shfl_sync(0xffffffffu, g, j);
+      // local < 2^24: the float quotient is within one of the integer one
+      uint32_t q = static_cast<uint32_t>(static_cast<float>(local) * inv);
+      if (q * w > local)
+        --q;
+      else if ((q + 1u) * w <= local)
+        ++q;
+      const bool active = p < P;
+      const uint32_t tile = active ? (mfy + kScatterWarps * q) * static_cast<uint32_t>(gx) +
+                                         mx0 + (local - q * w)
+                                   : 0xFFFFFFFFu;
+      const uint32_t peers = __match_any_sync(0xffffffffu, tile);
+      if (active) {
+        const uint32_t pos = s_next[tile] + __popc(peers & lt);
         if (pos < m)
-          ids[pos] = wave.g[q.member];
+          ids[pos] = mg;
         else if (pos >= total)
           record_device_error(kInconsistentInput);
-        kept_tile[it] = q.tile;
-        kept_add[it] = below == 0ull ? __popcll(q.cover) : 0u;  // first covering member
       }
+      __syncwarp();
+      if (active && (peers >> lane) == 1u) s_next[tile] += __popc(peers);
+      __syncwarp();
     }
-    for (uint32_t p = threadIdx.x + kKept * blockDim.x; p < P; p += blockDim.x) {
-      const WavePair q = wave_pair(wave, p, gx, col, rowm);
-      const uint32_t pos = s_next[q.tile] + __popcll(q.cover & members_below(q.member));
-      if (pos < m)
-        ids[pos] = wave.g[q.member];
-      else if (pos >= total)
-        record_device_error(kInconsistentInput);
-    }
-    unsigned long long* other = s_masks + (buf ^ 1) * mask_words;
-    for (int c = threadIdx.x; c < mask_words; c += blockDim.x) other[c] = 0ull;
-    if (warp == 0) {
-      publish_wave(s_wave[buf ^ 1], lane, ahead_g0, ahead_r0, ahead_g1, ahead_r1);
-      load(w0 + 2 * kWave + lane, ahead_g0, ahead_r0);
-      load(w0 + 2 * kWave + 32 + lane, ahead_g1, ahead_r1);
-    }
-    __syncthreads();
-    // advance each covered tile by the wave's count (its first covering
-    // member does it)
-#pragma unroll
-    for (int it = 0; it < kKept; ++it)
-      if (kept_add[it]) s_next[kept_tile[it]] += kept_add[it];
-    for (uint32_t p = threadIdx.x + kKept * blockDim.x; p < P; p += blockDim.x) {
-      const WavePair q = wave_pair(wave, p, gx, col, rowm);
-      if ((q.cover & members_below(q.member)) == 0ull) s_next[q.tile] += __popcll(q.cover);
-    }
-    build_masks(s_wave[buf ^ 1], other);
-    __syncthreads();
   }
 }
 

@@ -92,7 +92,7 @@ ChunkPlan chunk_plan(long long n, int gx, int gy, int tile_mode) {
   if (tile_mode == kTileAccutile) return c;
   const size_t T = static_cast<size_t>(gx) * gy;
   c.smem_counts = 4 * static_cast<size_t>(gx + 1) * (gy + 1);
-  c.smem_scatter = 4 * T + 16 * static_cast<size_t>(gx + gy);
+  c.smem_scatter = 4 * T;
   if (c.smem_counts > kChunkSmemLimit || c.smem_scatter > kChunkSmemLimit) return c;
   // the uint32 work prefix (tiles + kChunkGaussianCost per Gaussian) must not wrap
   if (n > (1LL << 27)) return c;
@@ -985,7 +985,7 @@ int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
     if (plan.smem_scatter > 48 * 1024)
       cudaFuncSetAttribute(tile_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(plan.smem_scatter));
-    tile_scatter_kernel<<<plan.chunks, 256, plan.smem_scatter, counted(s)>>>(
+    tile_scatter_kernel<<<plan.chunks, 32 * kScatterWarps, plan.smem_scatter, counted(s)>>>(
         at<uint32_t>(ws, L.vals_a), at<uint32_t>(ws, L.chunk_bounds),
         at<uint2>(ws, L.sorted_rects), gx, gy, at<uint32_t>(ws, L.chunk_counts),
         at<uint32_t>(ws, L.tile_starts), static_cast<uint32_t>(pairs),
