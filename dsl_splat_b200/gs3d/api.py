@@ -71,6 +71,19 @@ def _check_sh(sh_coeffs, sh_degree, features):
     return sh_degree
 
 
+_ZERO_BACKGROUNDS: dict = {}
+
+
+def _zero_background(device: torch.device, channels: int) -> Tensor:
+    """A zero background vector, made once per device and size (the kernels
+    only read it)."""
+    key = (device, channels)
+    bg = _ZERO_BACKGROUNDS.get(key)
+    if bg is None:
+        bg = _ZERO_BACKGROUNDS[key] = torch.zeros(channels, device=device)
+    return bg
+
+
 def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, viewmats: Tensor,
               Ks: Tensor, width: int, height: int, *, features: Tensor | None = None,
               sh_coeffs: Tensor | None = None, sh_degree: int | None = None,
@@ -173,8 +186,10 @@ def rasterize(means: Tensor, quats: Tensor, scales: Tensor, opacities: Tensor, v
     backgrounds = []
     for (b, c, ctr, con, colors, extras, bg, _state) in frames:
         total = channels + (0 if extras is None else extras.shape[-1]) + 1
-        packed_bg = ctr.new_zeros(total)
-        if bg is not None:
+        if bg is None:
+            packed_bg = _zero_background(ctr.device, total)
+        else:
+            packed_bg = ctr.new_zeros(total)
             packed_bg[:channels] = bg
         backgrounds.append(packed_bg)
     if not packed:

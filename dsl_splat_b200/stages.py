@@ -411,7 +411,8 @@ class BinPlan:
         self.state = state
         gx, gy = (width + 15) // 16, (height + 15) // 16
         self.ranges = torch.empty((gx * gy, 2), dtype=torch.int32, device=dev)
-        self.pairs_dev = torch.zeros(1, dtype=torch.int64, device=dev)
+        # written by splat_bin_prepare (the total, or 0 without Gaussians)
+        self.pairs_dev = torch.empty(1, dtype=torch.int64, device=dev)
         self.workspace = torch.empty(lib.splat_bin_workspace_bytes(n, width, height, self.mode),
                                      dtype=torch.uint8, device=dev)
         self.pin = Args()  # the projected rows stay referenced until emit
@@ -639,8 +640,12 @@ def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
     else:
         pix_stride, ch_stride = stored, 1
     centers = centers_out if centers_out is not None else torch.zeros_like(state.centers)
-    conics = torch.zeros_like(state.conics)
-    ga = torch.zeros_like(a) if need_a else None
+    # the conic and first feature gradients share one zero fill (conics first:
+    # their rows stay 16-byte aligned)
+    n_rows = len(state.conics)
+    flat = state.conics.new_zeros(n_rows * 4 + (a.numel() if need_a else 0))
+    conics = flat[:n_rows * 4].view(state.conics.shape)
+    ga = flat[n_rows * 4:].view(a.shape) if need_a else None
     gb = torch.zeros_like(b) if (b is not None and need_b) else None
     if absgrad:
         absolute = absolute_out if absolute_out is not None else torch.zeros_like(state.centers)

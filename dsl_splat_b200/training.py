@@ -68,7 +68,9 @@ class ScreenGradientTarget:
         if self.gaussian_ids is not None or self.fresh is None:
             return None
         if self.leaf.grad is None:
-            self.leaf.grad = torch.zeros_like(self.leaf)
+            # zeros allocated beside absgrad's by the forward when it made both
+            spare = self.fresh.pop("spare", None)
+            self.leaf.grad = spare if spare is not None else torch.zeros_like(self.leaf)
             self.fresh["grad"] = self.leaf.grad
             self.fresh["views"] = set(range(self.fresh["count"]))
         if self.leaf.grad is not self.fresh.get("grad") or self.index not in self.fresh["views"]:
@@ -83,7 +85,8 @@ class ScreenGradientTarget:
     @torch.no_grad()
     def add(self, gradient: Tensor) -> None:
         if self.leaf.grad is None:
-            self.leaf.grad = torch.zeros_like(self.leaf)
+            spare = self.fresh.pop("spare", None) if self.fresh is not None else None
+            self.leaf.grad = spare if spare is not None else torch.zeros_like(self.leaf)
         if self.gaussian_ids is None:
             views = self.fresh["count"] if self.fresh is not None else -1
             self.leaf.grad.view(views, *gradient.shape)[self.index].add_(gradient)
@@ -150,7 +153,15 @@ def prepare_training_metadata(dense: dict[str, Tensor], layout: Inputs, *, packe
     else:
         dense_screen = screen.reshape(layout.batch_count, layout.cameras, layout.n, 2)
     if absgrad:
-        absolute = torch.zeros_like(screen)
+        if packed:
+            absolute = torch.zeros_like(screen)
+        else:
+            # dense: absgrad and the first gradient of the means2d leaf come
+            # from one zero fill (the leaf's gradient half is handed out by
+            # the first direct_buffer() call of this call's views)
+            pair = screen.new_zeros((2,) + tuple(screen.shape))
+            absolute = pair[1]
+            fresh["spare"] = pair[0]
         setattr(screen, "absgrad", absolute)
         if packed:
             begin = 0
