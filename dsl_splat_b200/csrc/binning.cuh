@@ -227,8 +227,21 @@ __global__ void __launch_bounds__(256)
       vals[i] = static_cast<uint32_t>(i);
       rects[i] = rect;
     }
+    // the two low digits of visible rows are spread over all 256 values
+    // (lanes rarely collide); culled rows (all digits 255) are counted once
+    // per warp, and the two high digits, which take few values, are
+    // aggregated per warp
+    const bool culled = valid && key == kCulledKey;
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < 2; ++p)
+      if (valid && !culled) atomicAdd(&s_hist[p * kRadix + ((key >> (8 * p)) & 255u)], 1u);
+    const uint32_t culled_lanes = __popc(__ballot_sync(0xffffffffu, culled));
+    if ((threadIdx.x & 31) == 0 && culled_lanes) {
+      atomicAdd(&s_hist[0 * kRadix + 255], culled_lanes);
+      atomicAdd(&s_hist[1 * kRadix + 255], culled_lanes);
+    }
+#pragma unroll
+    for (int p = 2; p < 4; ++p) {
       const uint32_t d = valid ? ((key >> (8 * p)) & 255u) : 256u;
       const uint32_t peers = __match_any_sync(0xffffffffu, d);
       if (valid && (peers & lt) == 0u) atomicAdd(&s_hist[p * kRadix + d], __popc(peers));
@@ -892,38 +905,59 @@ __global__ void __launch_bounds__(1024)
 
 // One block: ranges from per-tile totals (empty tiles get [0, 0), as
 // identify_ranges leaves them), the first position of every tile, and the
-// pair total.
+// pair total.  Each round stages kPer * 1024 totals in shared memory with
+// coalesced loads, scans them (thread t owns kPer consecutive tiles), and
+// writes the results back through shared memory with coalesced stores (a
+// single block storing thread-major runs would touch a new 32-byte sector
+// with every lane).
 __global__ void __launch_bounds__(1024)
     tile_ranges_kernel(const uint32_t* __restrict__ totals, int T, int* __restrict__ ranges,
                        uint32_t* __restrict__ starts, uint32_t* __restrict__ total) {
   constexpr int kPer = 8;
+  constexpr int kRound = 1024 * kPer;
+  // row t of s_v at t + t / 32: thread-major reads of kPer words stay off
+  // one bank
+  __shared__ uint32_t s_v[kRound + kRound / 32];
   __shared__ uint32_t s_warp[32];
   __shared__ uint32_t s_carry;
+  auto slot = [](int k) { return k + (k >> 5); };
   if (threadIdx.x == 0) s_carry = 0u;
-  __syncthreads();
-  for (int base = 0; base < T; base += 1024 * kPer) {
+  for (int base = 0; base < T; base += kRound) {
+    const int count = min(kRound, T - base);
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int k = r * 1024 + threadIdx.x;
+      s_v[slot(k)] = k < count ? totals[base + k] : 0u;
+    }
+    __syncthreads();
     uint32_t v[kPer];
     uint32_t sum = 0u;
 #pragma unroll
     for (int r = 0; r < kPer; ++r) {
-      const int t = base + threadIdx.x * kPer + r;
-      v[r] = t < T ? totals[t] : 0u;
+      v[r] = s_v[slot(threadIdx.x * kPer + r)];
       sum += v[r];
     }
-    uint32_t chunk_total;
-    uint32_t run = block_exclusive_scan(sum, s_warp, &chunk_total) + s_carry;
+    uint32_t round_total;
+    uint32_t run = block_exclusive_scan(sum, s_warp, &round_total) + s_carry;
 #pragma unroll
     for (int r = 0; r < kPer; ++r) {
-      const int t = base + threadIdx.x * kPer + r;
-      if (t < T) {
-        ranges[2 * t] = v[r] ? static_cast<int>(run) : 0;
-        ranges[2 * t + 1] = v[r] ? static_cast<int>(run + v[r]) : 0;
-        starts[t] = run;
-      }
+      s_v[slot(threadIdx.x * kPer + r)] = run;  // exclusive start of the tile
       run += v[r];
     }
     __syncthreads();
-    if (threadIdx.x == 0) s_carry += chunk_total;
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int k = r * 1024 + threadIdx.x;
+      if (k < count) {
+        const uint32_t first = s_v[slot(k)];
+        const uint32_t n = totals[base + k];
+        starts[base + k] = first;
+        reinterpret_cast<int2*>(ranges)[base + k] =
+            n ? make_int2(static_cast<int>(first), static_cast<int>(first + n)) : make_int2(0, 0);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_carry += round_total;
     __syncthreads();
   }
   if (threadIdx.x == 0) *total = s_carry;

@@ -103,23 +103,47 @@ SPLAT_DEV int block_tile(const RenderParams& p) {
 
 // Tiles by descending pair count (ranges), for RenderParams::tile_order: a
 // counting sort of the counts scaled into 256 buckets (order inside a bucket
-// is arbitrary).  One block of 1024 threads.
+// is arbitrary).  One block of 1024 threads; each thread reads its tiles'
+// counts once (kPer per round, all loads in flight together) and keeps them
+// for the histogram and the placement.
 __global__ void __launch_bounds__(1024)
     tile_order_kernel(const int* __restrict__ ranges, int T, int* __restrict__ order) {
+  constexpr int kPer = 8;
   __shared__ int s_bucket[256];
   __shared__ int s_max;
   if (threadIdx.x == 0) s_max = 0;
   for (int b = threadIdx.x; b < 256; b += blockDim.x) s_bucket[b] = 0;
   __syncthreads();
+  const int2* span = reinterpret_cast<const int2*>(ranges);
   int local = 0;
-  for (int t = threadIdx.x; t < T; t += blockDim.x)
-    local = max(local, ranges[2 * t + 1] - ranges[2 * t]);
+  for (int base = 0; base < T; base += kPer * 1024) {
+    int count[kPer];
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int t = base + r * 1024 + threadIdx.x;
+      const int2 v = t < T ? span[t] : make_int2(0, 0);
+      count[r] = v.y - v.x;
+    }
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) local = max(local, count[r]);
+  }
   local = __reduce_max_sync(0xffffffffu, local);
   if ((threadIdx.x & 31) == 0) atomicMax(&s_max, local);
   __syncthreads();
   const int shift = max(0, 32 - __clz(s_max) - 8);  // the largest count maps below 256
-  for (int t = threadIdx.x; t < T; t += blockDim.x)
-    atomicAdd(&s_bucket[255 - ((ranges[2 * t + 1] - ranges[2 * t]) >> shift)], 1);
+  for (int base = 0; base < T; base += kPer * 1024) {
+    int count[kPer];
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int t = base + r * 1024 + threadIdx.x;
+      const int2 v = t < T ? span[t] : make_int2(0, 0);
+      count[r] = v.y - v.x;
+    }
+#pragma unroll
+    for (int r = 0; r < kPer; ++r)
+      if (base + r * 1024 + static_cast<int>(threadIdx.x) < T)
+        atomicAdd(&s_bucket[255 - (count[r] >> shift)], 1);
+  }
   __syncthreads();
   if (threadIdx.x < 32) {  // exclusive scan of the 256 buckets by one warp
     int v[8], sum = 0;
@@ -142,8 +166,20 @@ __global__ void __launch_bounds__(1024)
     }
   }
   __syncthreads();
-  for (int t = threadIdx.x; t < T; t += blockDim.x)
-    order[atomicAdd(&s_bucket[255 - ((ranges[2 * t + 1] - ranges[2 * t]) >> shift)], 1)] = t;
+  for (int base = 0; base < T; base += kPer * 1024) {
+    int count[kPer];
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int t = base + r * 1024 + threadIdx.x;
+      const int2 v = t < T ? span[t] : make_int2(0, 0);
+      count[r] = v.y - v.x;
+    }
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int t = base + r * 1024 + threadIdx.x;
+      if (t < T) order[atomicAdd(&s_bucket[255 - (count[r] >> shift)], 1)] = t;
+    }
+  }
 }
 
 // All CHP channels of staged slot j (padding channels are zero).

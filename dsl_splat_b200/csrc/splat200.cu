@@ -869,8 +869,8 @@ int splat_bin_prepare(int n, const float* centers, const float* conics, const in
   const BinLayout L = bin_layout(n, width, height, tile_mode);
   if (!workspace || workspace_bytes < L.bytes) return fail(kWorkspaceTooSmall, "bin workspace too small");
   if (!ranges || !pairs) return fail(kInvalidArgument, "null ranges/pairs");
-  if (!aligned(centers, 8) || !aligned(workspace, 256))
-    return fail(kInvalidArgument, "centers need 8-byte, workspace 256-byte alignment");
+  if (!aligned(centers, 8) || !aligned(ranges, 8) || !aligned(workspace, 256))
+    return fail(kInvalidArgument, "centers and ranges need 8-byte, workspace 256-byte alignment");
   cudaStream_t s = as_stream(stream);
   char* ws = static_cast<char*>(workspace);
   if (cudaMemsetAsync(ws + L.zero_begin, 0, L.zero_end - L.zero_begin, s) != cudaSuccess)
@@ -1065,6 +1065,7 @@ int splat_tile_order(const int* ranges, int tiles, int* order, void* stream) {
   if (tiles < 0) return fail(kInvalidArgument, "bad tile count");
   if (tiles == 0) return kOk;
   if (!ranges || !order) return fail(kInvalidArgument, "null ranges or order");
+  if (!aligned(ranges, 8)) return fail(kInvalidArgument, "ranges need 8-byte alignment");
   tile_order_kernel<<<1, 1024, 0, counted(as_stream(stream))>>>(ranges, tiles, order);
   return check_launch("tile_order");
 }

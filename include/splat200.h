@@ -225,8 +225,8 @@ int splat_scan_counts_static(int n, const int* counts, int* offsets, long long* 
  * required for modes 1 and 2; tiles must be the projection's counts for the
  * same mode):
  *   splat_bin_prepare: depth-key sort, pair offsets, per-tile ranges (T,2)
- *     (zeros for empty tiles, as identify_ranges leaves them) and the pair
- *     count M into *pairs (device int64).
+ *     (zeros for empty tiles, as identify_ranges leaves them; 8-byte
+ *     aligned) and the pair count M into *pairs (device int64).
  *   splat_bin_emit: generates and sorts the M (tile, Gaussian) pairs into
  *     ids (M) -- the reference's point_list: per tile, Gaussians ordered by
  *     (float bits of depth, index), identical to the stable 64-bit key sort
@@ -249,8 +249,9 @@ int splat_bin_emit(int n, long long pairs, int width, int height, int tile_mode,
                    int* ids, void* stream);
 
 /* Scheduling order for the blend kernels: the T tiles by descending pair
- * count (ranges[t][1] - ranges[t][0]), written to order (T).  No reference
- * counterpart (the reference launches tiles in index order). */
+ * count (ranges[t][1] - ranges[t][0]), written to order (T).  ranges needs
+ * 8-byte alignment.  No reference counterpart (the reference launches tiles
+ * in index order). */
 int splat_tile_order(const int* ranges, int tiles, int* order, void* stream);
 
 /* gs3d/render.py:359-406 render -> evaluate :41-125.  Blended channels are
