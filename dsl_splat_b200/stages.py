@@ -613,14 +613,18 @@ def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
                     height: int, *, planar: bool = False, absgrad: bool = False,
                     constant_tail: int = 0, need_a: bool = True, need_b: bool = True,
                     gradient_alpha: Tensor | None = None, separate_alpha: bool = False,
-                    absolute_out: Tensor | None = None, centers_out: Tensor | None = None):
+                    absolute_out: Tensor | None = None, centers_out: Tensor | None = None,
+                    separate_buffers: bool = False):
     """gs3d/render.py:409-463: grads of centers, conics, feat_a, feat_b, abs.
 
     separate_alpha: gradient holds the channels before the constant one
     (H, W, C'-1) and gradient_alpha (H, W, 1) the constant channel's; either
     may be None (zero).  absolute_out: a zeroed contiguous (n, 2) buffer that
     receives the |d centers| sums in place of a new one; centers_out: a zeroed
-    contiguous (n, 2) buffer that receives the centre gradient likewise."""
+    contiguous (n, 2) buffer that receives the centre gradient likewise.
+    separate_buffers: the conic and feature gradients get allocations of
+    their own (outputs of a Torch custom op must not alias one another);
+    otherwise they are views of one zero fill."""
     pin = Args()
     a, b, ca, cb = _features(feat_a, feat_b)
     channels = ca + cb + int(append_one)
@@ -642,10 +646,14 @@ def render_backward(state: ProjectedFootprint, bins: dict, feat_a: Tensor,
     centers = centers_out if centers_out is not None else torch.zeros_like(state.centers)
     # the conic and first feature gradients share one zero fill (conics first:
     # their rows stay 16-byte aligned)
-    n_rows = len(state.conics)
-    flat = state.conics.new_zeros(n_rows * 4 + (a.numel() if need_a else 0))
-    conics = flat[:n_rows * 4].view(state.conics.shape)
-    ga = flat[n_rows * 4:].view(a.shape) if need_a else None
+    if separate_buffers:
+        conics = torch.zeros_like(state.conics)
+        ga = torch.zeros_like(a) if need_a else None
+    else:
+        n_rows = len(state.conics)
+        flat = state.conics.new_zeros(n_rows * 4 + (a.numel() if need_a else 0))
+        conics = flat[:n_rows * 4].view(state.conics.shape)
+        ga = flat[n_rows * 4:].view(a.shape) if need_a else None
     gb = torch.zeros_like(b) if (b is not None and need_b) else None
     if absgrad:
         absolute = absolute_out if absolute_out is not None else torch.zeros_like(state.centers)

@@ -303,7 +303,8 @@ def render_backward(centers: Tensor, conics: Tensor, ranges: Tensor, point_list:
     gc, gq, gf, _, gabs = stages.render_backward(
         stages.ProjectedFootprint(centers, conics), dict(ranges=ranges, point_list=point_list),
         features, None, True, background, transmittance, contributors, grad_image, width,
-        height, absgrad=True, constant_tail=1, gradient_alpha=grad_alpha, separate_alpha=True)
+        height, absgrad=True, constant_tail=1, gradient_alpha=grad_alpha, separate_alpha=True,
+        separate_buffers=True)
     return gc, gq, gf, gabs
 
 
