@@ -128,7 +128,7 @@ SPLAT_DEV typename S::Word warp_lookback(const typename S::Word* status, int64_t
     const uint32_t stop_mask = incl | __ballot_sync(0xffffffffu, flag == 0);
     const int stop = stop_mask ? __ffs(stop_mask) - 1 : 32;
     const bool done = stop < 32 && ((incl >> stop) & 1u);
-    const int consumed = done ? stop + 1 : stop;  // lanes summed this round
+    const int consumed = done ? stop + 1 : stop;  // lanes summed in this step of the walk
     Word v = lane < consumed ? (w & S::kMask) : Word(0);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
