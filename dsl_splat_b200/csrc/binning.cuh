@@ -965,8 +965,9 @@ __global__ void __launch_bounds__(1024)
 
 // Scatter of chunk k = blockIdx.x: 8 warps, warp w places the chunk's pairs
 // in tile rows y with y % 8 == w (interleaved rows keep the warps' loads
-// even), so no two warps touch one tile.  Dynamic shared memory: next[T],
-// the next write position of every tile.  A warp walks the chunk's members
+// even), so no two warps touch one tile and the block needs no barrier (a
+// warp fills next[] for its own rows).  Dynamic shared memory: next[T], the
+// next write position of every tile.  A warp walks the chunk's members
 // 32 at a time in depth order; the pairs of those members in its rows
 // (row-major inside each member's rectangle) are laid out over the lanes by
 // a warp prefix scan, 32 per step.  Pairs of one step that share a tile
@@ -988,12 +989,24 @@ __global__ void __launch_bounds__(32 * kScatterWarps)
   extern __shared__ __align__(16) uint32_t s_next[];  // [T]
   const int T = gx * gy;
   const uint32_t* base = prefix + static_cast<size_t>(blockIdx.x) * T;
-#pragma unroll 4
-  for (int t = threadIdx.x; t < T; t += blockDim.x) s_next[t] = starts[t] + base[t];
-  __syncthreads();
   const uint32_t begin = bounds[blockIdx.x], end = bounds[blockIdx.x + 1];
   const uint32_t lane = threadIdx.x & 31, band = threadIdx.x >> 5;
+  // each warp fills next[] for its own rows only (no block barrier: a warp
+  // starts placing pairs as soon as its rows are ready)
+  for (int y = static_cast<int>(band); y < gy; y += kScatterWarps) {
+#pragma unroll 4
+    for (int x = static_cast<int>(lane); x < gx; x += 32) {
+      const int t = y * gx + x;
+      s_next[t] = starts[t] + base[t];
+    }
+  }
+  __syncwarp();
   const uint32_t lt = lanemask_lt();
+  // per warp, the window's Gaussians as (id, x0 | first row << 16, width,
+  // 1/width bits): one shared-memory load per pair instead of a shuffle per
+  // field
+  __shared__ uint4 s_member[kScatterWarps][32];
+  uint4* member = s_member[band];
   // member loads run one window ahead
   uint32_t next_g = 0u;
   uint2 next_r = make_uint2(0u, 0u);
@@ -1027,21 +1040,31 @@ __global__ void __launch_bounds__(32 * kScatterWarps)
       if (lane >= static_cast<uint32_t>(o)) incl += v;
     }
     const uint32_t P = __shfl_sync(0xffffffffu, incl, 31);
-    const uint32_t excl = incl - count;
+    if (P == 0u) continue;  // warp-uniform
     const float inv_w = width ? 1.0f / static_cast<float>(width) : 0.0f;
+    __syncwarp();  // the previous window's readers are done with member[]
+    member[lane] = make_uint4(g, x0 | (fy << 16), width, __float_as_uint(inv_w));
+    __syncwarp();
     for (uint32_t o = 0; o < P; o += 32) {
       const uint32_t p = o + lane;
-      // member j: the number of lanes whose inclusive prefix is <= p
-      uint32_t j = 0u;
+      // member j: the number of lanes whose inclusive prefix is <= p; before:
+      // the largest such prefix (the index of the member's first pair)
+      uint32_t j = 0u, before = 0u;
 #pragma unroll
-      for (uint32_t step = 16; step > 0; step >>= 1)
-        if (__shfl_sync(0xffffffffu, incl, j + step - 1u) <= p) j += step;
-      const uint32_t local = p - __shfl_sync(0xffffffffu, excl, j);
-      const uint32_t w = __shfl_sync(0xffffffffu, width, j);
-      const float inv = __shfl_sync(0xffffffffu, inv_w, j);
-      const uint32_t mx0 = __shfl_sync(0xffffffffu, x0, j);
-      const uint32_t mfy = __shfl_sync(0xffffffffu, fy, j);
-      const uint32_t mg = __shfl_sync(0xffffffffu, g, j);
+      for (uint32_t step = 16; step > 0; step >>= 1) {
+        const uint32_t v = __shfl_sync(0xffffffffu, incl, j + step - 1u);
+        if (v <= p) {
+          j += step;
+          before = v;
+        }
+      }
+      const uint4 d = member[j];
+      const uint32_t local = p - before;
+      const uint32_t w = d.z;
+      const float inv = __uint_as_float(d.w);
+      const uint32_t mx0 = d.y & 0xFFFFu;
+      const uint32_t mfy = d.y >> 16;
+      const uint32_t mg = d.x;
       // local < 2^24: the float quotient is within one of the integer one
       uint32_t q = static_cast<uint32_t>(static_cast<float>(local) * inv);
       if (q * w > local)
