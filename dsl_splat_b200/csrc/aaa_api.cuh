@@ -34,7 +34,7 @@ int aaa_check_frame(const SplatAaaFrame* f) {
 
 // bytes of the AAA binning workspace for `pairs` pairs (layout below)
 struct AaaBinLayout {
-  size_t tiles_in, depth_in, ids_in, keys_a, vals_a, keys_b, vals_b, hist, offs, status, counters,
+  size_t tiles_in, depth_in, ids_in, keys_a, vals_a, keys_b, vals_b, hist, status, counters,
       bytes;
   unsigned sort_tiles;
 };
@@ -67,7 +67,6 @@ AaaBinLayout aaa_bin_layout(long long pairs) {
   L.keys_b = take(4 * m);
   L.vals_b = take(4 * m);
   L.hist = take(4 * 5 * kRadix);
-  L.offs = take(4 * 5 * kRadix);
   L.status = take(4ull * 5 * L.sort_tiles * kRadix);
   L.counters = take(4 * 8);
   L.bytes = at;
@@ -296,7 +295,6 @@ int splat_aaa_bin(int n, long long pairs, const int* offsets, const float* cente
   if (r != kOk) return r;
   const int tile_bits = bit_length(T);
   const int tile_passes = tile_bits > 8 ? 2 : 1;
-  const int passes = 3 + tile_passes;
   if (cudaMemsetAsync(ws + L.hist, 0, 4 * 5 * kRadix, s) != cudaSuccess ||
       cudaMemsetAsync(ws + L.status, 0, L.counters + 4 * 8 - L.status, s) != cudaSuccess)
     return check_launch("aaa_bin memset");
@@ -305,30 +303,30 @@ int splat_aaa_bin(int n, long long pairs, const int* offsets, const float* cente
   splat::aaa::aaa_key_histograms_kernel<<<hist_blocks, 256, 0, counted(s)>>>(
       pairs, tiles_in, depth_in, tile_passes, u32(L.hist));
   // hist rows: depth bytes 0-2, tile bytes 0-1 (the pass order)
-  digit_offsets_kernel<<<1, kRadix, 0, counted(s)>>>(u32(L.hist), passes, u32(L.offs));
   const unsigned blocks = L.sort_tiles;
   auto status = [&](int pass) { return u32(L.status) + static_cast<size_t>(pass) * blocks * kRadix; };
   auto counter = [&](int pass) { return u32(L.counters) + pass; };
-  auto offs = [&](int pass) { return u32(L.offs) + pass * kRadix; };
+  // each pass's blocks form the exclusive prefix of its histogram row
+  auto offs = [&](int pass) { return u32(L.hist) + pass * kRadix; };
   uint32_t *keys_a = u32(L.keys_a), *vals_a = u32(L.vals_a), *keys_b = u32(L.keys_b),
            *vals_b = u32(L.vals_b);
-  onesweep_kernel<splat::aaa::DepthKeyLoader, true, kAaaSortThreads, kAaaSortItems>
+  onesweep_kernel<splat::aaa::DepthKeyLoader, true, kAaaSortThreads, kAaaSortItems, true>
       <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
       splat::aaa::DepthKeyLoader{depth_in}, m, 0, offs(0), status(0), counter(0), keys_a, vals_a);
-  onesweep_kernel<KeyValueLoader, true, kAaaSortThreads, kAaaSortItems>
+  onesweep_kernel<KeyValueLoader, true, kAaaSortThreads, kAaaSortItems, true>
       <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
       KeyValueLoader{keys_a, vals_a}, m, 8, offs(1), status(1), counter(1), keys_b, vals_b);
-  onesweep_kernel<KeyValueLoader, false, kAaaSortThreads, kAaaSortItems>
+  onesweep_kernel<KeyValueLoader, false, kAaaSortThreads, kAaaSortItems, true>
       <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
       KeyValueLoader{keys_b, vals_b}, m, 16, offs(2), status(2), counter(2), keys_a, vals_a);
-  onesweep_kernel<splat::aaa::TileGatherLoader, true, kAaaSortThreads, kAaaSortItems>
+  onesweep_kernel<splat::aaa::TileGatherLoader, true, kAaaSortThreads, kAaaSortItems, true>
       <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
       splat::aaa::TileGatherLoader{tiles_in, vals_a}, m, 0, offs(3), status(3), counter(3), keys_b,
       vals_b);
   const uint32_t* sorted_tiles = keys_b;
   const uint32_t* sorted_pairs = vals_b;
   if (tile_passes > 1) {
-    onesweep_kernel<KeyValueLoader, true, kAaaSortThreads, kAaaSortItems>
+    onesweep_kernel<KeyValueLoader, true, kAaaSortThreads, kAaaSortItems, true>
       <<<blocks, kAaaSortThreads, 0, counted(s)>>>(
         KeyValueLoader{keys_b, vals_b}, m, 8, offs(4), status(4), counter(4), keys_a, vals_a);
     sorted_tiles = keys_a;

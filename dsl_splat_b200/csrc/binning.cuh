@@ -373,7 +373,10 @@ struct EmitLoader {
 // larger blocks shorten the look-back chain at the cost of fewer blocks.
 // ITEMS keys per thread: fewer make more, shorter tiles (more blocks in
 // flight and a shorter ranking loop per block, a longer look-back chain).
-template <class Loader, bool WRITE_KEYS, int THREADS = kSortBlock, int ITEMS = kSortItems>
+// SCAN_HIST: digit_offsets holds this pass's 256-bin key histogram, whose
+// exclusive prefix every block forms itself (no separate offsets launch).
+template <class Loader, bool WRITE_KEYS, int THREADS = kSortBlock, int ITEMS = kSortItems,
+          bool SCAN_HIST = false>
 __global__ void __launch_bounds__(THREADS)
     onesweep_kernel(Loader ld, uint32_t n, int shift, const uint32_t* __restrict__ digit_offsets,
                     uint32_t* __restrict__ status, uint32_t* __restrict__ counter,
@@ -406,6 +409,10 @@ __global__ void __launch_bounds__(THREADS)
 
   uint32_t keys[ITEMS], vals[ITEMS], rank[ITEMS];
   const uint32_t lt = lanemask_lt();
+  uint32_t digit_first = 0u;  // SCAN_HIST: output position of this thread's digit
+  if constexpr (SCAN_HIST)
+    digit_first = block_exclusive_scan(
+        threadIdx.x < kRadix ? __ldg(digit_offsets + threadIdx.x) : 0u, s_warp, nullptr);
   // every load of the thread is issued before the ranking (whose warp
   // barriers would otherwise wait out one load latency per item)
 #pragma unroll
@@ -469,7 +476,7 @@ __global__ void __launch_bounds__(THREADS)
     }
     // output position of the digit's first key, less its tile-local start
     // when staged
-    s_base[d] = digit_offsets[d] + excl - (kStage ? s_start[d] : 0u);
+    s_base[d] = (SCAN_HIST ? digit_first : digit_offsets[d]) + excl - (kStage ? s_start[d] : 0u);
   }
   __syncthreads();
 

@@ -117,7 +117,7 @@ struct BinLayout {
   size_t zero_begin;  // everything from here to zero_end is cleared per call
   size_t depth_hist, diff, depth_status, counters, totals, work_status;
   size_t zero_end;
-  size_t depth_digits, tile_digits;
+  size_t tile_digits;
   size_t chunk_counts, tile_totals, tile_starts, chunk_bounds, sorted_rects;  // chunked path
   size_t bytes;
 };
@@ -156,7 +156,6 @@ BinLayout bin_layout(long long n, int width, int height, int tile_mode) {
   L.totals = take(8 * 4);
   L.work_status = take(plan.use ? 8 * sort_tiles : 0);  // work scan look-back
   L.zero_end = o;
-  L.depth_digits = take(4 * 4 * kRadix);
   L.tile_digits = take(plan.use ? 0 : 4 * 3 * kRadix);
   L.chunk_counts = take(plan.use ? 4 * static_cast<size_t>(plan.chunks) * T : 0);
   L.tile_totals = take(plan.use ? 4 * T : 0);
@@ -894,7 +893,6 @@ int splat_bin_prepare(int n, const float* centers, const float* conics, const in
   uint32_t* status = at<uint32_t>(ws, L.depth_status);
   uint32_t* counters = at<uint32_t>(ws, L.counters);
   uint32_t* totals = at<uint32_t>(ws, L.totals);
-  uint32_t* depth_digits = at<uint32_t>(ws, L.depth_digits);
   uint32_t* tile_digits = at<uint32_t>(ws, L.tile_digits);
   const unsigned sort_tiles = blocks_for(n, kSortTile);
   // depth passes: 256-thread onesweep blocks of kDepthItems keys per thread
@@ -909,14 +907,13 @@ int splat_bin_prepare(int n, const float* centers, const float* conics, const in
   bin_prepare_kernel<<<prep_grid, 256, 0, counted(s)>>>(n, centers, conics, radii, tiles, depths,
                                                         gx, gy, tile_mode, keys_a, vals_a, rects,
                                                         diff, hist, total64);
-  digit_offsets_kernel<<<1, kRadix, 0, counted(s)>>>(hist, 4, depth_digits);
   // four stable passes over the 32-bit depth keys: a -> b -> a -> b -> a
   for (int pass = 0; pass < 4; ++pass) {
     const bool even = (pass % 2) == 0;
     KeyValueLoader ld{even ? keys_a : keys_b, even ? vals_a : vals_b};
-    onesweep_kernel<KeyValueLoader, true, kDepthThreads, kDepthItems>
+    onesweep_kernel<KeyValueLoader, true, kDepthThreads, kDepthItems, true>
         <<<dtiles, kDepthThreads, 0, counted(s)>>>(
-            ld, static_cast<uint32_t>(n), 8 * pass, depth_digits + pass * kRadix,
+            ld, static_cast<uint32_t>(n), 8 * pass, hist + pass * kRadix,
             status + static_cast<size_t>(pass) * dtiles * kRadix, counters + pass,
             even ? keys_b : keys_a, even ? vals_b : vals_a);
   }
