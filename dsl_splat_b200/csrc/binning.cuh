@@ -282,16 +282,6 @@ SPLAT_DEV uint32_t block_exclusive_scan(uint32_t v, uint32_t* s_warp, uint32_t* 
   return before;
 }
 
-// Exclusive scans of `passes` 256-bin histograms (one block of 256 threads).
-__global__ void digit_offsets_kernel(const uint32_t* __restrict__ hist, int passes,
-                                     uint32_t* __restrict__ offsets) {
-  __shared__ uint32_t s_warp[32];
-  for (int p = 0; p < passes; ++p) {
-    const uint32_t v = hist[p * kRadix + threadIdx.x];
-    offsets[p * kRadix + threadIdx.x] = block_exclusive_scan(v, s_warp, nullptr);
-  }
-}
-
 // ---- generic onesweep pass ---------------------------------------------
 
 struct KeyValueLoader {
